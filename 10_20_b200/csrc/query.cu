@@ -1,0 +1,344 @@
+// Per-row query metadata, fine page tables, shared sink/tail staging and the
+// non-fused mask / mapping kernels for sm_100a.
+//
+// Reference behaviour (sglang/srt/layers/attention/v1_deepseek/kernels.py):
+//   query_lengths :224-245, output_ids :323-376, mask_fine :444-472,
+//   reduce_centers :475-486, fine_table_shared :488-514,
+//   stage_tail_shared :518-564, query_metadata :568-591, expand_logical :594-600;
+//   the fixed-budget take rule of bench_v1_dynamic_budget_metadata.py:5-27.
+// All index arithmetic is 64-bit (the pools exceed 2 GiB).
+#include "common.cuh"
+
+namespace v1x {
+namespace {
+
+__device__ __forceinline__ int64_t take_rule(int64_t pages, int64_t topk, int64_t num, int64_t den,
+                                             const int32_t* budget) {
+  if (budget) return min(pages, static_cast<int64_t>(*budget));
+  return min(pages, max((pages * num + den - 1) / den, (topk + 63) / 64));
+}
+
+__global__ void __launch_bounds__(128) query_metadata_kernel(
+    const int32_t* __restrict__ lens, const int32_t* __restrict__ nt, int32_t* __restrict__ fine_lens,
+    int32_t* __restrict__ takes, int32_t* __restrict__ dg_lens, int32_t* __restrict__ center_lens,
+    int32_t* __restrict__ tail_rows, int64_t np, int64_t topk, int64_t num, int64_t den, int64_t sink_cfg,
+    int64_t window, const int32_t* __restrict__ budget) {
+  const int64_t row = blockIdx.x;
+  const int n = lens[row];
+  const int64_t pages = static_cast<int64_t>(max(n - 1, 0) / 1024) * 16;
+  const int64_t take = take_rule(pages, topk, num, den, budget);
+  const RowBounds rb = row_bounds(n, static_cast<int>(sink_cfg), static_cast<int>(window));
+  const int64_t fine = take * 64 + rb.sink + n - rb.tail;
+  // share the staging copy with row 0 only if the length and every page id the
+  // sink/tail copy touches are identical (:583-591)
+  const int i = threadIdx.x;
+  const int64_t page = i == 0 ? 0 : rb.tail / 64 + i - 1;
+  const bool valid = (n > 0) && ((i == 0) || (page < (static_cast<int64_t>(n) + 63) / 64)) && (page < np);
+  const int mine = valid ? nt[row * np + page] : -1;
+  const int first = valid ? nt[page] : -1;
+  const int differs = __syncthreads_or(mine != first);
+  if (i == 0) {
+    const bool share = (n == lens[0]) && !differs;
+    fine_lens[row] = static_cast<int32_t>(fine);
+    takes[row] = static_cast<int32_t>(take);
+    dg_lens[row] = static_cast<int32_t>(max(fine, int64_t(1)));
+    center_lens[row] = static_cast<int32_t>(max(pages * 8, int64_t(1)));
+    tail_rows[row] = share ? 0 : static_cast<int32_t>(row);
+  }
+}
+
+__global__ void query_lengths_kernel(const int32_t* __restrict__ lens, int32_t* __restrict__ fine_lens,
+                                     int32_t* __restrict__ takes, int64_t topk, int64_t num,
+                                     int64_t den, int64_t sink_cfg, int64_t window, int64_t batch) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (row >= batch) return;
+  const int n = lens[row];
+  const int64_t pages = static_cast<int64_t>(max(n - 1, 0) / 1024) * 16;
+  const int64_t take = take_rule(pages, topk, num, den, nullptr);
+  const RowBounds rb = row_bounds(n, static_cast<int>(sink_cfg), static_cast<int>(window));
+  fine_lens[row] = static_cast<int32_t>(take * 64 + rb.sink + n - rb.tail);
+  takes[row] = static_cast<int32_t>(take);
+}
+
+__global__ void fine_table_shared_kernel(const int32_t* __restrict__ rt, const void* selected,
+                                         int sel64, const int32_t* __restrict__ takes,
+                                         int32_t* __restrict__ ft, const int32_t* __restrict__ tail_rows,
+                                         int64_t cap, int64_t maxp, int64_t take_stride, int64_t fp,
+                                         int64_t scratch) {
+  const int64_t row = blockIdx.x;
+  const int take = takes[row];
+  const int64_t pad_base = cap + static_cast<int64_t>(tail_rows[row]) * scratch;
+  for (int64_t j = threadIdx.x; j < fp; j += blockDim.x) {
+    int64_t page;
+    if (j < take) {
+      const int64_t rank = load_index(selected, sel64, row * take_stride + j);
+      page = rt[row * maxp + rank];
+    } else {
+      page = pad_base + min(max(j - take, int64_t(0)), scratch - 1);
+    }
+    ft[row * fp + j] = static_cast<int32_t>(page);
+  }
+}
+
+struct StageArgs {
+  const uint8_t* native;
+  const float* nscale;
+  const int32_t* nt;
+  const int32_t* lens;
+  uint8_t* fine;
+  float* fscale;
+  const int32_t* tail_rows;
+  int64_t cap, np, scratch, sink, window, rows_bound, group;
+};
+
+// One program (g, p): for each owner row of group g in ascending order, stage
+// candidate slots [p*64, p*64+64) of that row's sink+tail list (:535-564).
+__global__ void __launch_bounds__(256) stage_tail_shared_kernel(const __grid_constant__ StageArgs a) {
+  const int64_t g = blockIdx.x;
+  const int p = blockIdx.y;
+  for (int64_t k = 0; k < a.group; ++k) {
+    const int64_t row = g * a.group + k;
+    if (a.rows_bound > 0 && row >= a.rows_bound) break;
+    if (a.tail_rows[row] != row) continue;
+    const int n = a.lens[row];
+    const RowBounds rb = row_bounds(n, static_cast<int>(a.sink), static_cast<int>(a.window));
+    const int count = rb.sink + n - rb.tail;
+    if (!(p * 64 < count || p == 0)) continue;
+    const int64_t dst = a.cap + row * a.scratch + p;
+    for (int c = threadIdx.x; c < 64 * 8; c += blockDim.x) {
+      const int tok = c >> 3, part = c & 7;
+      const int i = p * 64 + tok;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (i < count) {
+        const int logical = i < rb.sink ? i : rb.tail + i - rb.sink;
+        const int64_t page = a.nt[row * a.np + logical / 64];
+        v = reinterpret_cast<const uint4*>(a.native + page * kPageBytes + (logical % 64) * 128)[part];
+      }
+      reinterpret_cast<uint4*>(a.fine + dst * kPageBytes + tok * 128)[part] = v;
+    }
+    if (threadIdx.x < 64) {
+      const int tok = threadIdx.x;
+      const int i = p * 64 + tok;
+      float s = 0.0f;
+      if (i < count) {
+        const int logical = i < rb.sink ? i : rb.tail + i - rb.sink;
+        const int64_t page = a.nt[row * a.np + logical / 64];
+        s = a.nscale[page * kPageWords + kScaleWord + logical % 64];
+      }
+      a.fscale[dst * kPageWords + kScaleWord + tok] = s;
+    }
+  }
+}
+
+__global__ void mask_fine_kernel(float* __restrict__ scores, const void* selected, int sel64,
+                                 const int32_t* __restrict__ rt, const int32_t* __restrict__ members,
+                                 const int32_t* __restrict__ lens, const int32_t* __restrict__ takes,
+                                 int64_t maxp, int64_t take_stride, int64_t stride, int64_t width,
+                                 int64_t sink_cfg, int64_t window) {
+  const int64_t row = blockIdx.x;
+  const int64_t j = static_cast<int64_t>(blockIdx.y) * blockDim.x + threadIdx.x;
+  if (j >= width) return;
+  const int n = lens[row];
+  const int take = takes[row];
+  const RowBounds rb = row_bounds(n, static_cast<int>(sink_cfg), static_cast<int>(window));
+  const int64_t count = static_cast<int64_t>(take) * 64 + rb.sink + n - rb.tail;
+  const bool fine = j < static_cast<int64_t>(take) * 64;
+  bool good = j < count;
+  if (fine && good) {
+    const int64_t rank = load_index(selected, sel64, row * take_stride + j / 64);
+    const int64_t page = rt[row * maxp + rank];
+    const int logical = members[page * 64 + j % 64];
+    good = logical >= rb.sink && logical < rb.tail;
+  }
+  if (!good) scores[row * stride + j] = -CUDART_INF_F;
+}
+
+__global__ void reduce_centers_kernel(const float* __restrict__ logits, const int32_t* __restrict__ lens,
+                                      float* __restrict__ out, int64_t maxp, int64_t cols, int64_t stride) {
+  const int64_t row = blockIdx.x;
+  const int64_t p = static_cast<int64_t>(blockIdx.y) * blockDim.x + threadIdx.x;
+  if (p >= cols) return;
+  const int64_t pages = static_cast<int64_t>(max(lens[row] - 1, 0) / 1024) * 16;
+  float best = -CUDART_INF_F;
+  if (p < pages) {
+    const float* s = logits + row * stride + p * 8;
+#pragma unroll
+    for (int g = 0; g < 8; ++g) best = fmaxf(best, s[g]);
+  }
+  out[row * maxp + p] = best;
+}
+
+struct OutputIdsArgs {
+  const int32_t* raw;
+  const float* scores;
+  const int32_t* members;
+  const int32_t* rt;
+  const int32_t* nt;
+  const void* selected;
+  int sel64;
+  const int32_t* lens;
+  const int32_t* takes;
+  int32_t* out;
+  int32_t* logical;
+  const int32_t* ft;
+  int64_t maxp, np, take_stride, width, topk, sink, window;
+  int map_physical, direct_fine;
+  int64_t fp;
+};
+
+__global__ void output_ids_kernel(const __grid_constant__ OutputIdsArgs a) {
+  const int64_t row = blockIdx.x;
+  const int64_t j = static_cast<int64_t>(blockIdx.y) * blockDim.x + threadIdx.x;
+  if (j >= a.topk) return;
+  const int raw = a.raw[row * a.topk + j];
+  const int take = a.takes[row];
+  const int n = a.lens[row];
+  const RowBounds rb = row_bounds(n, static_cast<int>(a.sink), static_cast<int>(a.window));
+  bool valid = raw >= 0 && raw < a.width;
+  int logical = -1;
+  if (valid) {
+    if (raw < take * 64) {
+      int64_t page;
+      if (a.direct_fine) {
+        page = a.ft[row * a.fp + raw / 64];
+      } else {
+        const int64_t rank = load_index(a.selected, a.sel64, row * a.take_stride + raw / 64);
+        page = a.rt[row * a.maxp + rank];
+      }
+      logical = a.members[page * 64 + raw % 64];
+    } else {
+      const int off = raw - take * 64;
+      logical = off < rb.sink ? off : rb.tail + off - rb.sink;
+    }
+    valid = a.scores[row * a.width + raw] != -CUDART_INF_F && logical >= 0 && logical < n;
+  }
+  if (a.map_physical)
+    a.out[row * a.topk + j] = valid ? a.nt[row * a.np + logical / 64] * 64 + logical % 64 : -1;
+  a.logical[row * a.topk + j] = valid ? logical : -1;
+}
+
+__global__ void expand_logical_kernel(const int32_t* __restrict__ logical, int32_t* __restrict__ out,
+                                      int64_t topk, int64_t stride) {
+  const int64_t row = blockIdx.x;
+  for (int64_t j = threadIdx.x; j < stride; j += blockDim.x) {
+    int32_t v = -1;
+    if (j < topk * 4) {
+      const int32_t lg = logical[row * topk + j / 4];
+      if (lg >= 0) v = lg * 4 + static_cast<int32_t>(j % 4);
+    }
+    out[row * stride + j] = v;
+  }
+}
+
+}  // namespace
+}  // namespace v1x
+
+using namespace v1x;
+
+extern "C" int v1x_query_metadata(const int32_t* lens, const int32_t* nt, int32_t* fine_lens,
+                                  int32_t* takes, int32_t* dg_lens, int32_t* center_lens,
+                                  int32_t* tail_rows, int64_t np, int64_t topk, int64_t num,
+                                  int64_t den, int64_t sink, int64_t window, const int32_t* budget,
+                                  int64_t batch, void* stream) {
+  clear_error();
+  V1X_CHECK_ARG(batch >= 0 && np > 0 && den > 0 && num >= 0, "query_metadata: bad geometry");
+  if (batch == 0) return V1X_OK;
+  query_metadata_kernel<<<static_cast<unsigned>(batch), 128, 0, as_stream(stream)>>>(
+      lens, nt, fine_lens, takes, dg_lens, center_lens, tail_rows, np, topk, num, den, sink, window,
+      budget);
+  return launch_status("v1x_query_metadata");
+}
+
+extern "C" int v1x_query_lengths(const int32_t* lens, int32_t* fine_lens, int32_t* takes,
+                                 int64_t topk, int64_t num, int64_t den, int64_t sink,
+                                 int64_t window, int64_t batch, void* stream) {
+  clear_error();
+  V1X_CHECK_ARG(batch >= 0 && den > 0 && num >= 0, "query_lengths: bad geometry");
+  if (batch == 0) return V1X_OK;
+  query_lengths_kernel<<<static_cast<unsigned>((batch + 127) / 128), 128, 0, as_stream(stream)>>>(
+      lens, fine_lens, takes, topk, num, den, sink, window, batch);
+  return launch_status("v1x_query_lengths");
+}
+
+extern "C" int v1x_fine_table_shared(const int32_t* rt, const void* selected, int selected_is_i64,
+                                     const int32_t* takes, int32_t* ft, const int32_t* tail_rows,
+                                     int64_t cap, int64_t maxp, int64_t take, int64_t fp,
+                                     int64_t scratch, int64_t batch, void* stream) {
+  clear_error();
+  V1X_CHECK_ARG(batch >= 0 && fp >= 0 && scratch >= 1, "fine_table_shared: bad geometry");
+  if (batch == 0 || fp == 0) return V1X_OK;
+  fine_table_shared_kernel<<<static_cast<unsigned>(batch), 128, 0, as_stream(stream)>>>(
+      rt, selected, selected_is_i64, takes, ft, tail_rows, cap, maxp, take, fp, scratch);
+  return launch_status("v1x_fine_table_shared");
+}
+
+extern "C" int v1x_stage_tail_shared(const uint8_t* native_bytes, const float* native_scales,
+                                     const int32_t* nt, const int32_t* lens, uint8_t* fine_bytes,
+                                     float* fine_scales, const int32_t* tail_rows, int64_t cap,
+                                     int64_t np, int64_t scratch, int64_t sink, int64_t window,
+                                     int64_t rows_bound, int64_t group, int64_t grid_groups,
+                                     int64_t grid_pages, void* stream) {
+  clear_error();
+  V1X_CHECK_ARG(group >= 1 && grid_groups >= 0 && grid_pages >= 0 && grid_pages < 65536,
+                "stage_tail_shared: bad grid");
+  V1X_CHECK_ARG(((reinterpret_cast<uintptr_t>(native_bytes) | reinterpret_cast<uintptr_t>(fine_bytes)) & 15) == 0,
+                "stage_tail_shared: page pools must be 16-byte aligned");
+  if (grid_groups == 0 || grid_pages == 0) return V1X_OK;
+  StageArgs a{native_bytes, native_scales, nt, lens, fine_bytes, fine_scales, tail_rows, cap, np,
+              scratch, sink, window, rows_bound, group};
+  stage_tail_shared_kernel<<<dim3(static_cast<unsigned>(grid_groups), static_cast<unsigned>(grid_pages)),
+                             256, 0, as_stream(stream)>>>(a);
+  return launch_status("v1x_stage_tail_shared");
+}
+
+extern "C" int v1x_mask_fine(float* scores, const void* selected, int selected_is_i64,
+                             const int32_t* rt, const int32_t* members, const int32_t* lens,
+                             const int32_t* takes, int64_t maxp, int64_t take, int64_t stride,
+                             int64_t width, int64_t sink, int64_t window, int64_t batch,
+                             void* stream) {
+  clear_error();
+  V1X_CHECK_ARG(batch >= 0 && width >= 0, "mask_fine: bad geometry");
+  if (batch == 0 || width == 0) return V1X_OK;
+  mask_fine_kernel<<<dim3(static_cast<unsigned>(batch), static_cast<unsigned>((width + 255) / 256)), 256, 0,
+                     as_stream(stream)>>>(scores, selected, selected_is_i64, rt, members, lens, takes,
+                                          maxp, take, stride, width, sink, window);
+  return launch_status("v1x_mask_fine");
+}
+
+extern "C" int v1x_reduce_centers(const float* logits, const int32_t* lens, float* out,
+                                  int64_t maxp, int64_t pcount, int64_t stride, int64_t batch,
+                                  void* stream) {
+  clear_error();
+  V1X_CHECK_ARG(batch >= 0 && maxp >= 0 && pcount >= 0, "reduce_centers: bad geometry");
+  const int64_t cols = pcount < maxp ? pcount : maxp;
+  if (batch == 0 || cols == 0) return V1X_OK;
+  reduce_centers_kernel<<<dim3(static_cast<unsigned>(batch), static_cast<unsigned>((cols + 127) / 128)), 128,
+                          0, as_stream(stream)>>>(logits, lens, out, maxp, cols, stride);
+  return launch_status("v1x_reduce_centers");
+}
+
+extern "C" int v1x_output_ids(const int32_t* raw, const float* scores, const int32_t* members,
+                              const int32_t* rt, const int32_t* nt, const void* selected,
+                              int selected_is_i64, const int32_t* lens, const int32_t* takes,
+                              int32_t* out, int32_t* logical, const int32_t* ft, int64_t maxp,
+                              int64_t np, int64_t take, int64_t width, int64_t topk, int64_t sink,
+                              int64_t window, int map_physical, int direct_fine, int64_t fp,
+                              int64_t batch, void* stream) {
+  clear_error();
+  V1X_CHECK_ARG(batch >= 0 && topk >= 0, "output_ids: bad geometry");
+  if (batch == 0 || topk == 0) return V1X_OK;
+  OutputIdsArgs a{raw, scores, members, rt, nt, selected, selected_is_i64, lens, takes, out, logical,
+                  ft, maxp, np, take, width, topk, sink, window, map_physical, direct_fine, fp};
+  output_ids_kernel<<<dim3(static_cast<unsigned>(batch), static_cast<unsigned>((topk + 255) / 256)), 256, 0,
+                      as_stream(stream)>>>(a);
+  return launch_status("v1x_output_ids");
+}
+
+extern "C" int v1x_expand_logical(const int32_t* logical, int32_t* out, int64_t topk, int64_t stride,
+                                  int64_t batch, void* stream) {
+  clear_error();
+  V1X_CHECK_ARG(batch >= 0 && topk >= 0 && stride >= 0, "expand_logical: bad geometry");
+  if (batch == 0 || stride == 0) return V1X_OK;
+  expand_logical_kernel<<<static_cast<unsigned>(batch), 256, 0, as_stream(stream)>>>(logical, out, topk, stride);
+  return launch_status("v1x_expand_logical");
+}

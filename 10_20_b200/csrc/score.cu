@@ -1,0 +1,116 @@
+// FP8 paged scoring for sm_100a: out[b, j] = sum_h w[b,h] * relu(q[b,h,:] . k_j) * s_j.
+//
+// Reference contract: DeepGEMM fp8_paged_mqa_logits as called at
+// sglang/srt/layers/attention/v1_deepseek/runtime.py:434-444 (centres) and
+// :538-548 (fine candidates); the formula is the reference's own restatement in
+// kernels.py:310-313 (fine) / :210-213 (coarse), pinned against DeepGEMM at
+// experiments/fine_pool_shared_20261021/test_and_bench.py:37-41.
+//
+// This file holds the SIMT path: one thread per key, 16-byte loads of the
+// key's 128 FP8 bytes, exact e4m3 -> fp32 conversion, and a FIXED fp32
+// evaluation order (per head d = 0..127 with fma -- every e4m3 x e4m3 product
+// is exact in fp32 -- then acc += w_h * relu with separately rounded multiply
+// and add, then * scale) so the result is bit-identical to the CPU oracle.
+// It is the path for few heads (the single-head config is 2 FLOP/byte).
+#include <cuda_fp8.h>
+
+#include "common.cuh"
+
+namespace v1x {
+namespace {
+
+constexpr int kScoreThreads = 128;
+constexpr int kSimtMaxHeads = 64;
+
+struct ScoreArgs {
+  const uint8_t* q;
+  const float* w;
+  const uint8_t* pool;
+  const int32_t* lens;
+  const int32_t* table;
+  int64_t table_stride;
+  float* out;
+  int64_t out_stride, max_len;
+  int heads, relu;
+};
+
+__device__ __forceinline__ float2 e4m3x2_to_float2(uint16_t v) {
+  const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(v), __NV_E4M3);
+  return __half22float2(*reinterpret_cast<const __half2*>(&h));
+}
+
+__global__ void __launch_bounds__(kScoreThreads) score_simt_kernel(const __grid_constant__ ScoreArgs a) {
+  __shared__ __align__(16) float qs[kSimtMaxHeads * 128];
+  __shared__ float ws[kSimtMaxHeads];
+  const int64_t b = blockIdx.x;
+  const int H = a.heads;
+  for (int i = threadIdx.x; i < H * 64; i += blockDim.x) {
+    const uint16_t two = reinterpret_cast<const uint16_t*>(a.q + b * H * 128)[i];
+    const float2 f = e4m3x2_to_float2(two);
+    qs[2 * i] = f.x;
+    qs[2 * i + 1] = f.y;
+  }
+  for (int h = threadIdx.x; h < H; h += blockDim.x) ws[h] = a.w[b * H + h];
+  __syncthreads();
+  const int64_t j = static_cast<int64_t>(blockIdx.y) * blockDim.x + threadIdx.x;
+  if (j >= a.max_len) return;
+  const int n = a.lens[b];
+  float result = -CUDART_INF_F;
+  if (j < n) {
+    const int64_t page = a.table[b * a.table_stride + j / 64];
+    const uint8_t* kp = a.pool + page * kPageBytes + (j % 64) * 128;
+    uint4 kw[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) kw[c] = reinterpret_cast<const uint4*>(kp)[c];
+    const float scale = reinterpret_cast<const float*>(a.pool + page * kPageBytes)[kScaleWord + j % 64];
+    float acc = 0.0f;
+    for (int h = 0; h < H; ++h) {
+      const float4* qh = reinterpret_cast<const float4*>(qs + h * 128);
+      float dot = 0.0f;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint32_t w4[4] = {kw[c].x, kw[c].y, kw[c].z, kw[c].w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float2 lo = e4m3x2_to_float2(static_cast<uint16_t>(w4[u] & 0xFFFFu));
+          const float2 hi = e4m3x2_to_float2(static_cast<uint16_t>(w4[u] >> 16));
+          const float4 qq = qh[c * 4 + u];
+          dot = __fmaf_rn(qq.x, lo.x, dot);
+          dot = __fmaf_rn(qq.y, lo.y, dot);
+          dot = __fmaf_rn(qq.z, hi.x, dot);
+          dot = __fmaf_rn(qq.w, hi.y, dot);
+        }
+      }
+      const float r = a.relu ? (dot > 0.0f ? dot : 0.0f) : dot;
+      acc = __fadd_rn(acc, __fmul_rn(ws[h], r));
+    }
+    result = __fmul_rn(acc, scale);
+  }
+  a.out[b * a.out_stride + j] = result;
+}
+
+}  // namespace
+}  // namespace v1x
+
+extern "C" int v1x_score_fp8(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages,
+                             const int32_t* lens, const int32_t* table, int64_t table_stride,
+                             float* out, int64_t out_stride, int64_t max_len, int64_t heads,
+                             int relu, int64_t batch, void* stream) {
+  using namespace v1x;
+  clear_error();
+  V1X_CHECK_ARG(heads >= 1 && heads <= 256, "score_fp8: heads must be in [1, 256]");
+  V1X_CHECK_ARG(batch >= 0 && max_len >= 0 && out_stride >= max_len && pool_pages > 0,
+                "score_fp8: bad geometry");
+  V1X_CHECK_ARG((reinterpret_cast<uintptr_t>(pool) & 15) == 0, "score_fp8: pool must be 16-byte aligned");
+  V1X_CHECK_ARG(table_stride * 64 >= 0, "score_fp8: bad table stride");
+  if (batch == 0 || max_len == 0) return V1X_OK;
+  if (heads > kSimtMaxHeads) {
+    set_error("score_fp8: heads > %d not implemented", kSimtMaxHeads);
+    return V1X_ERR_UNSUPPORTED;
+  }
+  ScoreArgs a{q, w, pool, lens, table, table_stride, out, out_stride, max_len,
+              static_cast<int>(heads), relu};
+  const dim3 grid(static_cast<unsigned>(batch), static_cast<unsigned>((max_len + kScoreThreads - 1) / kScoreThreads));
+  score_simt_kernel<<<grid, kScoreThreads, 0, as_stream(stream)>>>(a);
+  return launch_status("v1x_score_fp8");
+}

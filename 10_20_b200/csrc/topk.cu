@@ -1,0 +1,302 @@
+// fused.topk for sm_100a: in-place boundary mask + exact Top-T radix select +
+// raw -> logical -> physical mapping (+ optional x4 expansion), one CTA per row.
+//
+// Reference behaviour: sglang/kernels/jit/csrc/deepseek_v4/v1_query.cuh:62-153
+// (kernel) and :181-220 (host checks).  Selection semantics: the T largest of
+// scores[row, :fine_lens[row]] ordered by (value desc, index asc) -- exact ties at
+// the boundary go to the lower index, where the reference falls back to
+// shared-memory atomic order (topk_impl.cuh:400-401).  Outputs are written in
+// ascending raw-index order (the reference leaves the order unspecified).
+//
+// Design: the row's candidate scores are staged once in shared memory as
+// order-preserving uint32 keys; four 8-bit radix passes (warp-aggregated
+// histogram atomics) find the exact T-th key and how many of its ties to keep;
+// two block scans then place every selected candidate at its output slot in
+// index order, and the selecting thread performs the mapping epilogue itself.
+#include "common.cuh"
+
+namespace v1x {
+namespace {
+
+constexpr int kTopkThreads = 512;
+constexpr int kTopkMaxSmemKeys = 48 * 1024;  // 192 KB of staged keys per CTA
+constexpr uint32_t kNegInfKey = 0x007FFFFFu;  // order_key(-inf)
+
+struct TopkArgs {
+  float* scores;
+  int64_t score_stride, cols;
+  const int32_t* fine_lens;
+  const int32_t* members;
+  int64_t member_rows;
+  const int32_t* rt;
+  const int32_t* nt;
+  int64_t pages;
+  const void* selected;
+  int sel64;
+  int64_t take_stride;
+  const int32_t* lens;
+  const int32_t* takes;
+  int32_t* physical;
+  int32_t* logical;
+  int32_t* raw;
+  int topk, window, mask;
+  int32_t* expanded;
+  int64_t expansion_stride;
+  int physical_output, bucket_from_rank;
+  const int32_t* fine_table;
+  int64_t fine_table_cols;
+  int direct_fine;
+};
+
+struct RowCtx {
+  int64_t row;
+  int n, take, sink, tail, L;
+  const float* s;
+};
+
+// Mapping epilogue for one output slot (VQ:121-148).
+__device__ __forceinline__ void emit_slot(const TopkArgs& a, const RowCtx& c, int slot, int raw,
+                                          bool finite) {
+  int logical = -1, physical = -1;
+  if (raw >= 0 && raw < c.L && finite) {
+    int lg = -1;
+    bool ok = true;
+    if (raw < c.take * 64) {
+      int64_t page = -1;
+      const int r = raw >> 6;
+      if (a.direct_fine) {
+        if (r < a.fine_table_cols) page = a.fine_table[c.row * a.fine_table_cols + r];
+      } else if (r < a.take_stride) {
+        const int64_t rank = load_index(a.selected, a.sel64, c.row * a.take_stride + r);
+        if (rank >= 0 && rank < a.pages) page = a.rt[c.row * a.pages + rank];
+      }
+      ok = page >= 0 && page < a.member_rows;
+      if (ok) lg = a.members[page * 64 + (raw & 63)];
+    } else {
+      const int off = raw - c.take * 64;
+      lg = off < c.sink ? off : c.tail + off - c.sink;
+    }
+    if (ok && lg >= 0 && lg < c.n) {
+      logical = lg;
+      if (a.physical_output) {
+        const int64_t p = lg >> 6;
+        physical = p < a.pages ? a.nt[c.row * a.pages + p] * 64 + (lg & 63) : -1;
+      }
+    }
+  }
+  const int64_t dst = c.row * a.topk + slot;
+  a.logical[dst] = logical;
+  if (a.physical_output) {
+    a.physical[dst] = physical;
+    a.raw[dst] = raw;
+  }
+  if (a.expansion_stride) {
+    const int b = logical * 4;
+    reinterpret_cast<int4*>(a.expanded + c.row * a.expansion_stride)[slot] =
+        logical < 0 ? make_int4(-1, -1, -1, -1) : make_int4(b, b + 1, b + 2, b + 3);
+  }
+}
+
+// In-place -inf mask of boundary-bucket members (VQ:71-107): one warp per
+// selected page rank r < take; interior buckets are skipped after one lookup.
+__device__ void apply_mask(const TopkArgs& a, const RowCtx& c, float* srow) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int r = warp; r < c.take; r += nw) {
+    int64_t rank = -1;
+    int bucket = 0;
+    if (lane == 0) {
+      if (r < a.take_stride) rank = load_index(a.selected, a.sel64, c.row * a.take_stride + r);
+      if (rank >= 0 && rank < a.pages) {
+        if (a.bucket_from_rank) {
+          bucket = static_cast<int>(rank / 16) * 1024;
+        } else {
+          const int64_t page = a.rt[c.row * a.pages + rank];
+          bucket = (page >= 0 && page < a.member_rows) ? (a.members[page * 64] / 1024) * 1024 : 0;
+        }
+      }
+    }
+    rank = __shfl_sync(0xffffffffu, rank, 0);
+    bucket = __shfl_sync(0xffffffffu, bucket, 0);
+    if (rank < 0 || rank >= a.pages) continue;
+    if (bucket < c.sink || bucket + 1024 > c.tail) {
+      const int64_t page = a.rt[c.row * a.pages + rank];
+      if (page < 0 || page >= a.member_rows) continue;
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int off = lane + i * 32;
+        const int lg = a.members[page * 64 + off];
+        const int64_t col = static_cast<int64_t>(r) * 64 + off;
+        if ((lg < c.sink || lg >= c.tail) && col < a.cols) srow[col] = -CUDART_INF_F;
+      }
+    }
+  }
+}
+
+struct TopkSmem {
+  int hist[256];
+  int warp_tot[kTopkThreads / 32 + 1];
+  int digit, need;
+};
+
+template <bool kStaged>
+__device__ __forceinline__ uint32_t key_at(const uint32_t* keys, const float* srow, int i) {
+  if constexpr (kStaged) return keys[i];
+  else return order_key(srow[i]);
+}
+
+template <bool kStaged>
+__global__ void __launch_bounds__(kTopkThreads) topk_kernel(const __grid_constant__ TopkArgs a) {
+  extern __shared__ __align__(16) uint32_t keys[];
+  __shared__ TopkSmem sm;
+  const int tid = threadIdx.x, nt = blockDim.x;
+  const int lane = tid & 31, warp = tid >> 5;
+  RowCtx c;
+  c.row = blockIdx.x;
+  c.n = a.lens[c.row];
+  c.take = a.takes[c.row];
+  const RowBounds rb = row_bounds(c.n, 64, a.window);
+  c.sink = rb.sink;
+  c.tail = rb.tail;
+  c.L = static_cast<int>(min(static_cast<int64_t>(max(a.fine_lens[c.row], 0)), a.cols));
+  float* srow = a.scores + c.row * a.score_stride;
+  c.s = srow;
+
+  if (a.mask) {
+    apply_mask(a, c, srow);
+    __syncthreads();
+  }
+
+  if (c.L <= a.topk) {
+    for (int t = tid; t < a.topk; t += nt) {
+      const int raw = t < c.L ? t : -1;
+      const bool fin = raw >= 0 && srow[raw] != -CUDART_INF_F;
+      emit_slot(a, c, t, raw, fin);
+    }
+  } else {
+    if constexpr (kStaged) {
+      const bool vec = (reinterpret_cast<uintptr_t>(srow) & 15) == 0;
+      const int nv = vec ? c.L >> 2 : 0;
+      for (int v = tid; v < nv; v += nt) {
+        const float4 x = reinterpret_cast<const float4*>(srow)[v];
+        reinterpret_cast<uint4*>(keys)[v] =
+            make_uint4(order_key(x.x), order_key(x.y), order_key(x.z), order_key(x.w));
+      }
+      for (int i = nv * 4 + tid; i < c.L; i += nt) keys[i] = order_key(srow[i]);
+    }
+    // ---- exact radix select of the T-th largest key --------------------------
+    uint32_t prefix = 0, known = 0;
+    int need = a.topk;
+    for (int pass = 0; pass < 4; ++pass) {
+      const int shift = 24 - 8 * pass;
+      for (int b = tid; b < 256; b += nt) sm.hist[b] = 0;
+      __syncthreads();
+      const int iters = (c.L + nt - 1) / nt;
+      for (int j = 0; j < iters; ++j) {
+        const int i = j * nt + tid;
+        int bin = -1;
+        if (i < c.L) {
+          const uint32_t k = key_at<kStaged>(keys, srow, i);
+          if ((k & known) == prefix) bin = (k >> shift) & 255;
+        }
+        const unsigned act = __activemask();
+        const unsigned same = __match_any_sync(act, bin);
+        if (bin >= 0 && lane == __ffs(same) - 1) atomicAdd(&sm.hist[bin], __popc(same));
+      }
+      __syncthreads();
+      if (warp == 0) {
+        int cnt[8], s = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          cnt[j] = sm.hist[255 - (lane * 8 + j)];
+          s += cnt[j];
+        }
+        int cum = warp_inclusive_scan(s) - s;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (cum < need && cum + cnt[j] >= need) {
+            sm.digit = 255 - (lane * 8 + j);
+            sm.need = need - cum;
+          }
+          cum += cnt[j];
+        }
+      }
+      __syncthreads();
+      prefix |= static_cast<uint32_t>(sm.digit) << shift;
+      known |= 255u << shift;
+      need = sm.need;
+      __syncthreads();
+    }
+    const uint32_t thr = prefix;
+    // ---- place selected candidates in ascending index order -------------------
+    const int chunk = (c.L + nt - 1) / nt;
+    const int beg = min(tid * chunk, c.L), end = min(beg + chunk, c.L);
+    int eq = 0, gt = 0;
+    for (int i = beg; i < end; ++i) {
+      const uint32_t k = key_at<kStaged>(keys, srow, i);
+      eq += k == thr;
+      gt += k > thr;
+    }
+    int tot;
+    const int eq_before = block_exclusive_scan(eq, sm.warp_tot, &tot);
+    const int take_eq = min(max(need - eq_before, 0), eq);
+    int pos = block_exclusive_scan(gt + take_eq, sm.warp_tot, &tot);
+    int eq_seen = eq_before;
+    for (int i = beg; i < end; ++i) {
+      const uint32_t k = key_at<kStaged>(keys, srow, i);
+      bool sel = k > thr;
+      if (k == thr) {
+        sel = eq_seen < need;
+        ++eq_seen;
+      }
+      if (sel && pos < a.topk) emit_slot(a, c, pos++, i, k != kNegInfKey);
+    }
+  }
+  if (a.expansion_stride) {
+    for (int64_t j = static_cast<int64_t>(a.topk) * 4 + tid; j < a.expansion_stride; j += nt)
+      a.expanded[c.row * a.expansion_stride + j] = -1;
+  }
+}
+
+}  // namespace
+}  // namespace v1x
+
+extern "C" int v1x_topk(float* scores, int64_t score_stride, int64_t cols, const int32_t* fine_lens,
+                        const int32_t* members, int64_t member_rows, const int32_t* rt,
+                        const int32_t* nt, int64_t pages, const void* selected, int selected_is_i64,
+                        int64_t take_stride, const int32_t* lens, const int32_t* takes,
+                        int32_t* physical, int32_t* logical, int32_t* raw, int64_t topk,
+                        int64_t window, int mask, int32_t* expanded, int64_t expansion_stride,
+                        int physical_output, int bucket_from_rank, const int32_t* fine_table,
+                        int64_t fine_table_cols, int direct_fine, int64_t batch, void* stream) {
+  using namespace v1x;
+  clear_error();
+  V1X_CHECK_ARG(batch >= 0, "topk: negative batch");
+  V1X_CHECK_ARG(topk > 0 && topk <= 2048, "Unsupported fused V1 TopK: topk=%lld", (long long)topk);
+  V1X_CHECK_ARG(window >= 0 && window <= 4096, "Unsupported fused V1 TopK: window=%lld",
+                (long long)window);
+  V1X_CHECK_ARG(expansion_stride == 0 || expansion_stride == topk * 4 + 64,
+                "Invalid expansion buffer");
+  V1X_CHECK_ARG(!direct_fine || fine_table_cols >= take_stride, "Invalid direct fine table");
+  V1X_CHECK_ARG(score_stride >= cols && cols >= 0, "topk: score stride < cols");
+  V1X_CHECK_ARG(pages > 0 && take_stride >= 0 && member_rows > 0, "topk: bad table shapes");
+  if (batch == 0) return V1X_OK;
+  TopkArgs a{scores, score_stride, cols, fine_lens, members, member_rows, rt, nt, pages, selected,
+             selected_is_i64, take_stride, lens, takes, physical, logical, raw,
+             static_cast<int>(topk), static_cast<int>(window), mask, expanded, expansion_stride,
+             physical_output, bucket_from_rank, fine_table, fine_table_cols, direct_fine};
+  cudaStream_t s = as_stream(stream);
+  if (cols <= kTopkMaxSmemKeys) {
+    const size_t smem = static_cast<size_t>(cols > 0 ? cols : 1) * 4;
+    if (smem > 48 * 1024) {
+      static DeviceOnce once;
+      if (once.first()) {
+        cudaFuncSetAttribute(topk_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kTopkMaxSmemKeys * 4);
+      }
+    }
+    topk_kernel<true><<<static_cast<unsigned>(batch), kTopkThreads, smem, s>>>(a);
+  } else {
+    topk_kernel<false><<<static_cast<unsigned>(batch), kTopkThreads, 0, s>>>(a);
+  }
+  return launch_status("v1x_topk");
+}

@@ -1,0 +1,60 @@
+"""FP8 paged index scoring with the DeepGEMM ``fp8_paged_mqa_logits`` contract.
+
+The reference calls DeepGEMM (an external, unvendored dependency) at
+sglang/srt/layers/attention/v1_deepseek/runtime.py:434-444 (centre logits) and
+:538-548 (fine logits); its formula is restated by the reference at
+kernels.py:310-313 and pinned against DeepGEMM at
+experiments/fine_pool_shared_20261021/test_and_bench.py:37-41:
+
+    logits[b, j] = sum_h w[b, h] * relu(q[b, h, :] . k_j) * scale_j,  j < len[b]
+
+This module mirrors the DeepGEMM call surface used there (next_n = 1) and runs
+libv1x.so's sm_100a kernel.  The schedule argument is accepted for signature
+compatibility and ignored: the kernel needs no host-built schedule.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import ptr, require
+
+
+def get_paged_mqa_logits_metadata(context_lens: torch.Tensor, block_size: int, num_sms: int):
+    """Signature-compatible schedule stub: an int32 [num_sms + 1, 2] zero tensor."""
+    require(block_size == 64, "only 64-token pages are supported")
+    return torch.zeros((num_sms + 1, 2), dtype=torch.int32, device=context_lens.device)
+
+
+def fp8_paged_mqa_logits(q, kv_cache, weights, context_lens, block_table, schedule_meta,
+                         max_context_len: int, clean_logits: bool = True, relu: bool = True,
+                         out: torch.Tensor | None = None):
+    """Logits [B, max_context_len] (float32); columns >= context_lens[b] are -inf.
+
+    q: e4m3 [B, H, 128] or [B, 1, H, 128]; kv_cache: packed uint8 [pages, 8448] or
+    [pages, 64, 1, 132]; weights: float32 [B, H]; context_lens: int32 [B] or [B, 1];
+    block_table: int32 [B, max_blocks].
+    """
+    if q.dim() == 4:
+        require(q.shape[1] == 1, "only next_n == 1 is supported")
+        q = q[:, 0]
+    require(q.dim() == 3 and q.shape[2] == 128, "q: [B, H, 128]")
+    require(q.dtype in (torch.float8_e4m3fn, torch.uint8), "q: float8_e4m3fn")
+    require(q.is_contiguous(), "q must be contiguous")
+    B, H = q.shape[0], q.shape[1]
+    require(kv_cache.dtype == torch.uint8 and kv_cache.is_contiguous() and kv_cache.numel() % 8448 == 0,
+            "kv_cache: contiguous packed uint8 pages of 8448 bytes")
+    require(weights.shape == (B, H) and weights.dtype == torch.float32 and weights.is_contiguous(),
+            "weights: float32 [B, H]")
+    lens = context_lens.reshape(-1)
+    require(lens.numel() == B and lens.dtype == torch.int32, "context_lens: int32 [B]")
+    require(block_table.dim() == 2 and block_table.shape[0] == B and block_table.dtype == torch.int32
+            and block_table.stride(1) == 1, "block_table: int32 [B, max_blocks]")
+    if out is None:
+        out = torch.empty((B, max_context_len), dtype=torch.float32, device=q.device)
+    require(out.dtype == torch.float32 and out.stride(1) == 1 and out.shape[1] >= max_context_len,
+            "out: float32 [B, >= max_context_len]")
+    _lib.call("v1x_score_fp8", ptr(q), ptr(weights), ptr(kv_cache), kv_cache.numel() // 8448, ptr(lens),
+              ptr(block_table), block_table.stride(0), ptr(out), out.stride(0), int(max_context_len), H,
+              int(bool(relu)), B, _lib.stream_of(q), device=q.device)
+    return out

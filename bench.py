@@ -1,0 +1,340 @@
+"""Benchmark of the V1 query-side selection path on B200 (one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload decode|single]
+
+Workloads (synthetic, seeded; shapes of the benchmark configurations):
+  decode  128 requests per GPU, context ~U[32K, 128K] tokens, 64 index heads,
+          FP8 e4m3 keys with per-token scales, fixed page budget take=40,
+          window 64, route -> FP8 score -> Top-2048 -> gather of the 576-dim
+          bf16 MLA latent (single output: K and V are the same latent).
+  single  1024 single-head queries over 64 built pages + 65-token tail
+          (2688 candidates), route -> score -> Top-2048 (no gather).
+A step is one pass of the whole selection path over one batch.  Requests are
+independent, so N GPUs run N independent batches (weak scaling, no collective
+on the data path); `value` is the whole-job queries/s = N*B*K / max-over-ranks
+device time.  Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+METRIC = "indexed queries/sec (route+FP8 score+Top2048+gather); HBM GB/s as % of peak"
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def workload_cfg(name):
+    if name == "decode":
+        return dict(B=128, H=64, P=2048, take=40, window=64, topk=2048, lo=32768, hi=131072, latent=576)
+    if name == "single":
+        return dict(B=1024, H=1, P=128, take=40, window=64, topk=2048, lo=4097, hi=4097, latent=0)
+    raise SystemExit(f"unknown workload {name}")
+
+
+def make_case(synth, cfg, seed, device, rows=None):
+    B = cfg["B"] if rows is None else rows
+    if cfg["lo"] == cfg["hi"]:
+        lens = [cfg["lo"]] * B
+    else:
+        lens = synth.decode_lens(cfg["B"], cfg["lo"], cfg["hi"], seed)[:B]
+    return synth.make_query_case(B, cfg["H"], lens, P=cfg["P"], take=cfg["take"], window=cfg["window"],
+                                 topk=cfg["topk"], seed=seed, device=device, latent_dim=cfg["latent"])
+
+
+class Clocks:
+    """Sample SM clocks / throttle reasons with nvidia-smi during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_port_rate(cfg, seed, rows, budget_s=20.0):
+    """Queries/s of the oracle port on a bounded CPU sample (all host cores for BLAS)."""
+    import oracle.port as port
+
+    synth = importlib.import_module("10_20_b200.synth")
+    torch.set_num_threads(os.cpu_count() or 1)
+    case = make_case(synth, cfg, seed, "cpu", rows=rows)
+    c = port.to_numpy_case(case)
+    port.run_rows(c, rows=[0])            # warm-up (page-in, BLAS init)
+    done, t0 = 0, time.perf_counter()
+    while True:
+        port.run_rows(c, rows=[done % rows])
+        done += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or done >= 4 * rows:
+            break
+    return done / el, dict(rows=done, seconds=round(el, 3), sample_requests=rows,
+                           lens=[int(x) for x in c["lens"]])
+
+
+def run_reference(args, cfg):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    rows = 4 if args.workload == "decode" else 32
+    vals = []
+    for _ in range(args.warmup):
+        cpu_port_rate(cfg, 1000, rows, budget_s=2.0)
+    meta = None
+    for _ in range(args.steps):
+        v, meta = cpu_port_rate(cfg, 1000, rows, budget_s=max(5.0, 60.0 / max(args.steps, 1)))
+        vals.append(v)
+    value = statistics.median(vals)
+    cores = os.cpu_count()
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp8-e4m3 keys, f32 scores, bf16 latent", "data": "synthetic",
+            "config": {"workload": args.workload, **{k: v for k, v in cfg.items()}},
+            "cpu_baseline": {"value": value, "unit": "queries/s", "cores": cores, "kind": "port",
+                             "sample": f"{meta['rows']} queries of a {rows}-request sample "
+                                       f"(oracle port, numpy/BLAS), per step"},
+            "e2e": {"value": value, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "single"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    cfg = workload_cfg(args.workload)
+    if args.impl == "reference":
+        return run_reference(args, cfg)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+
+    pkg = importlib.import_module("10_20_b200")
+    pkg.load()
+    synth = importlib.import_module("10_20_b200.synth")
+    pipeline = importlib.import_module("10_20_b200.pipeline")
+
+    seed = 1000 + rank
+    case = make_case(synth, cfg, seed, device)
+    step = pipeline.SelectionStep(case, gather=cfg["latent"] > 0)
+    acct = step.algorithmic_bytes()
+    # two graphs: selection (6 kernels + metadata) and gather, so the dominant
+    # kernel is timed with events on its own stream position
+    sel_graph = torch.cuda.CUDAGraph()
+    gat_graph = torch.cuda.CUDAGraph() if step.gather else None
+    s = torch.cuda.Stream(device=device)
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(2):
+            step.run()
+    s.synchronize()
+    gather_on = step.gather
+    step.gather = False
+    with torch.cuda.graph(sel_graph, stream=s):
+        step.run()
+    if gather_on:
+        step.gather = True
+        lat = case.latent
+        from importlib import import_module
+        gmod = import_module("10_20_b200.gather")
+        with torch.cuda.graph(gat_graph, stream=s):
+            gmod._gather_impl((1,), lat, None, None, step.physical, step.kv, None, case.B, case.topk, 0,
+                              *lat.stride(), 0, 0, 0, step.physical.stride(0))
+    s.synchronize()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    launches_per_step = 7 + (1 if gather_on else 0)
+
+    def one_step(evs):
+        flush.fill_(1)                      # evict L2 between timed iterations
+        evs[0].record()
+        sel_graph.replay()
+        evs[1].record()
+        if gat_graph is not None:
+            gat_graph.replay()
+        evs[2].record()
+
+    for _ in range(max(args.warmup, 3)):
+        one_step([torch.cuda.Event(enable_timing=True) for _ in range(3)])
+    torch.cuda.synchronize()
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            one_step(events[i])
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+    if dist:
+        dist.barrier()
+    step_ms = [e[0].elapsed_time(e[2]) for e in events]
+    gather_ms = [e[1].elapsed_time(e[2]) for e in events]
+    sel_ms = [e[0].elapsed_time(e[1]) for e in events]
+    total_ms = sum(step_ms)
+    t = torch.tensor([total_ms], dtype=torch.float64, device=device)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = float(t.item())
+    queries = case.B * args.steps * world
+    value = queries / (total_ms / 1e3)
+
+    # end-to-end through the public step: pinned H2D of the step's inputs,
+    # the step, D2H of the selected slot ids
+    pin_q = case.q8.view(torch.uint8).cpu().pin_memory()
+    pin_w = case.w.cpu().pin_memory()
+    pin_l = case.lens.cpu().pin_memory()
+    pin_nt = case.native_table.cpu().pin_memory()
+    out_host = torch.empty(step.physical.shape, dtype=torch.int32).pin_memory()
+    h2d = pin_q.numel() + pin_w.numel() * 4 + pin_l.numel() * 4 + pin_nt.numel() * 4
+    d2h = out_host.numel() * 4
+
+    def e2e_step():
+        case.q8.view(torch.uint8).copy_(pin_q, non_blocking=True)
+        case.w.copy_(pin_w, non_blocking=True)
+        case.lens.copy_(pin_l, non_blocking=True)
+        case.native_table.copy_(pin_nt, non_blocking=True)
+        sel_graph.replay()
+        if gat_graph is not None:
+            gat_graph.replay()
+        out_host.copy_(step.physical, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ea.record()
+    for _ in range(args.steps):
+        flush.fill_(1)
+        e2e_step()
+    eb.record()
+    torch.cuda.synchronize()
+    e2e_ms = ea.elapsed_time(eb)
+    te = torch.tensor([e2e_ms], dtype=torch.float64, device=device)
+    if dist:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = queries / (float(te.item()) / 1e3)
+
+    if rank == 0:
+        hbm, kind = peaks()
+        if gather_on:
+            dom_bytes, dom_ms, dom = acct["gather"], statistics.mean(gather_ms), "gather_vec_kernel"
+        else:
+            dom_bytes, dom_ms, dom = acct["total"], statistics.mean(sel_ms), "selection graph"
+        achieved = dom_bytes / (dom_ms / 1e3) / 1e9
+        line = {
+            "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp8-e4m3 keys, f32 scores, bf16 latent",
+            "data": "synthetic",
+            "config": {"workload": args.workload, "requests_per_gpu": case.B, "heads": case.H,
+                       "page_budget": case.take, "topk": case.topk, "window": case.window,
+                       "context": [cfg["lo"], cfg["hi"]], "latent_dim": cfg["latent"],
+                       "parallelism": f"requests sharded, {world} independent batches",
+                       "l2": "flushed (256 MB write) between timed steps",
+                       "algorithmic_bytes_per_step": acct["total"]},
+            "step_hbm_gbs": acct["total"] / (total_ms / args.steps / 1e3) / 1e9,
+            "step_frac_of_peak": acct["total"] / (total_ms / args.steps / 1e3) / 1e9 / hbm,
+            "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "peak_kind": kind, "traffic": None},
+            "stage_ms": {"selection": statistics.mean(sel_ms), "gather": statistics.mean(gather_ms)},
+            "e2e": {"value": e2e_value, "unit": "queries/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk.summary(),
+            "wall_s": wall,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            rows = 4 if args.workload == "decode" else 32
+            v, meta = cpu_port_rate(cfg, 1000, rows, budget_s=15.0)
+            line["cpu_baseline"] = {"value": v, "unit": "queries/s", "cores": os.cpu_count(), "kind": "port",
+                                    "sample": f"{meta['rows']} queries from a {rows}-request sample of the "
+                                              f"same workload, oracle port (numpy + BLAS), "
+                                              f"{meta['seconds']} s"}
+        print(json.dumps(line), flush=True)
+    if dist:
+        del sel_graph, gat_graph
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

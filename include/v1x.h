@@ -1,0 +1,234 @@
+/*
+ * v1x.h -- C ABI of the B200 (sm_100a) kernels for the SGLang V1 sparse-attention
+ * query-side selection path.
+ *
+ * Conventions shared by every entry point:
+ *   - All tensor arguments are raw DEVICE pointers of the dtype named in the
+ *     comment; sizes and strides are in ELEMENTS unless the name says bytes.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Every call only
+ *     enqueues work on that stream: no allocation, no host<->device copy, no
+ *     synchronisation, so every call can be captured in a CUDA graph.
+ *   - Return value: V1X_OK (0) or a negative V1X_ERR_* code; on error nothing was
+ *     launched and v1x_last_error() returns a message (per calling thread).
+ *   - Kernels never trap.  Conditions the reference turns into device asserts are
+ *     reported through a caller-owned int32 device status word (see
+ *     v1x_allocate), leaving the guarded state untouched.
+ *   - Packed page: 8448 bytes = 64 tokens x 128 FP8 e4m3 bytes, then 64 fp32
+ *     scales (reference: sglang/srt/layers/attention/v1_deepseek/kernels.py:1-3).
+ *
+ * Reference paths below are relative to the reference checkout:
+ *   DS = sglang/srt/layers/attention/v1_deepseek
+ *   NA = sglang/srt/layers/attention/v1_native
+ *   VQ = sglang/kernels/jit/csrc/deepseek_v4/v1_query.cuh
+ */
+#ifndef V1X_H
+#define V1X_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define V1X_API __attribute__((visibility("default")))
+#else
+#define V1X_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define V1X_OK 0
+#define V1X_ERR_INVALID (-1)     /* argument / shape / dtype check failed      */
+#define V1X_ERR_CUDA (-2)        /* CUDA runtime error while launching         */
+#define V1X_ERR_UNSUPPORTED (-3) /* valid request outside what is implemented  */
+
+/* device status word values (written by kernels, read by the host) */
+#define V1X_STATUS_OK 0
+#define V1X_STATUS_ARENA_EXHAUSTED 1 /* allocate: free stack smaller than needed */
+
+/* Library identity: returns 0x010000 * major + 0x100 * minor + patch. */
+V1X_API int v1x_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+V1X_API const char* v1x_last_error(void);
+
+/* ------------------------------------------------------------------------ */
+/* fused.route -- replaces V1QueryKernel::route (VQ:155-180, kernel VQ:7-49).
+ * scores  f32 [batch, score_cols] with row stride score_stride (% 4 == 0)
+ * lens, takes, tail_rows  i32 [batch]
+ * selected  i32 or i64 [batch, take_stride] (selected_is_i64 selects)
+ * rt  i32 [batch, pages];  ft  i32 [batch, fine_pages]
+ * Checks as the reference: 64 <= pages <= 4096, score_cols >= 8*pages,
+ * take_stride <= pages, score_stride % 4 == 0, capacity > 0,
+ * fine_pages >= take_stride. */
+V1X_API int v1x_route(const float* scores, int64_t score_stride, int64_t score_cols,
+              const int32_t* lens, const int32_t* takes, void* selected, int selected_is_i64,
+              int64_t take_stride, int64_t pages, const int32_t* rt, int32_t* ft,
+              int64_t fine_pages, const int32_t* tail_rows, int64_t capacity, int fill_table,
+              int64_t batch, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* fused.topk -- replaces V1QueryKernel::topk (VQ:181-220, kernel VQ:62-153).
+ * scores f32 [batch, cols] row stride score_stride (% 4 == 0); mutated in place
+ *   when mask != 0 (boundary-bucket members outside [sink, tail) -> -inf).
+ * fine_lens, lens, takes i32 [batch]; members i32 [member_rows, 64];
+ * rt, nt i32 [batch, pages]; selected i32/i64 [batch, take_stride];
+ * physical, logical, raw i32 [batch, topk]; expanded i32 [batch,
+ * expansion_stride] with expansion_stride 0 or 4*topk+64; fine_table i32
+ * [batch, fine_table_cols] (read when direct_fine).
+ * Selection: the topk largest scores of scores[row, :fine_lens[row]] ordered
+ * by (value desc, index asc); outputs in ascending raw-index order.
+ * Checks: 0 < topk <= 2048, 0 <= window <= 4096, expansion stride, and
+ * fine_table_cols >= take_stride when direct_fine.  Unlike the reference, any
+ * batch >= 1 is accepted (the reference requires batch > 512). */
+V1X_API int v1x_topk(float* scores, int64_t score_stride, int64_t cols, const int32_t* fine_lens,
+             const int32_t* members, int64_t member_rows, const int32_t* rt, const int32_t* nt,
+             int64_t pages, const void* selected, int selected_is_i64, int64_t take_stride,
+             const int32_t* lens, const int32_t* takes, int32_t* physical, int32_t* logical,
+             int32_t* raw, int64_t topk, int64_t window, int mask, int32_t* expanded,
+             int64_t expansion_stride, int physical_output, int bucket_from_rank,
+             const int32_t* fine_table, int64_t fine_table_cols, int direct_fine, int64_t batch,
+             void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* _sort -- replaces the Triton kernel NA/fused_grouping.py:64-76.
+ * P (i32), S (f32), O (i32) are [heads, 4096]; segment (g, h) is the N
+ * entries at h*4096 + g*N.  flag i32 scalar: the call is a no-op unless
+ * *flag < 0 (read on the device).  N is a power of two in [2, 4096] and
+ * groups*N <= 4096.  Output: stable sort by score desc, ties by position,
+ * +0 == -0. */
+V1X_API int v1x_sort_segments(const int32_t* P, int32_t* O, const float* S, const int32_t* flag,
+                      int64_t N, int64_t groups, int64_t heads, void* stream);
+
+/* Extension (no reference counterpart): per-segment group offsets for integer
+ * keys in [0, key_range) stored as float scores: offsets[seg, j] = number of
+ * records of the segment whose key > key_range-1-j, j in [0, key_range].
+ * offsets i32 [heads*groups, key_range+1]; key_range <= 12288. */
+V1X_API int v1x_group_offsets(const float* S, int32_t* offsets, int64_t N, int64_t groups,
+                      int64_t heads, int64_t key_range, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Page lifecycle -- replace DS/kernels.py:57-179.  meta i32[3] =
+ * {bucket start, lease, active}; every op is a no-op when meta[2] == 0
+ * (release has no meta, as in the reference). */
+
+/* DS/kernels.py:57-69. tmp u8 [n_pages, 8448], map i32 [n_pages, 64] -> hash i64 [n_pages, 2] */
+V1X_API int v1x_fingerprint(const uint8_t* tmp, const int32_t* map, const int32_t* meta, int64_t* hash,
+                    int64_t n_pages, void* stream);
+
+/* DS/kernels.py:72-113. For each tmp page: the lowest live (refs > 0) arena page
+ * whose two hashes, 8448 bytes and 64 members are equal, else -1.
+ * fine u8 [cap, 8448], members i32 [cap, 64], hashes i64 [cap, 2], refs i32 [cap],
+ * match i32 [n_pages]. */
+V1X_API int v1x_match_pages(const uint8_t* tmp, const int32_t* map, const int64_t* hash,
+                    const int32_t* meta, const uint8_t* fine, const int32_t* members,
+                    const int64_t* hashes, const int32_t* refs, int32_t* match, int64_t cap,
+                    int64_t n_pages, void* stream);
+
+/* DS/kernels.py:116-131. 16 lanes. free i32 [cap], count i32 scalar, refs i32
+ * [cap], tables i32 [leases, 16], new_flags u8 (torch.bool) [16].  If the free
+ * stack holds fewer pages than needed, *status = V1X_STATUS_ARENA_EXHAUSTED and
+ * nothing else is written (the reference traps).  status may be NULL. */
+V1X_API int v1x_allocate(const int32_t* meta, const int32_t* match, int32_t* free_stack,
+                 int32_t* count, int32_t* refs, int32_t* tables, uint8_t* new_flags,
+                 int32_t* status, void* stream);
+
+/* DS/kernels.py:134-167. tmp u8 [16, 8448]; tc_bytes u8 / tc_scales f32 = the
+ * bucket's 2 centre pages (byte and float views); fine u8 [cap, 8448];
+ * centers u8 / center_scales f32 = centre pool views; members i32; hashes i64. */
+V1X_API int v1x_publish(const uint8_t* tmp, const uint8_t* tc_bytes, const float* tc_scales,
+                const int32_t* map, const int64_t* hash, const int32_t* meta,
+                const int32_t* tables, const uint8_t* new_flags, uint8_t* fine,
+                uint8_t* centers, float* center_scales, int32_t* members, int64_t* hashes,
+                void* stream);
+
+/* DS/kernels.py:170-179. table i32 [16] (one lease's row). */
+V1X_API int v1x_release(const int32_t* table, int32_t* refs, int32_t* free_stack, int32_t* count,
+                void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Per-row query metadata and staging. */
+
+/* DS/kernels.py:568-591 (budget == NULL) or bench_v1_dynamic_budget_metadata.py:5-27
+ * (budget = i32 device scalar, take = min(pages, *budget)). lens i32 [batch];
+ * nt i32 [batch, np] (row stride np); outputs i32 [batch]. */
+V1X_API int v1x_query_metadata(const int32_t* lens, const int32_t* nt, int32_t* fine_lens,
+                       int32_t* takes, int32_t* dg_lens, int32_t* center_lens,
+                       int32_t* tail_rows, int64_t np, int64_t topk, int64_t num, int64_t den,
+                       int64_t sink, int64_t window, const int32_t* budget, int64_t batch,
+                       void* stream);
+
+/* DS/kernels.py:224-245. */
+V1X_API int v1x_query_lengths(const int32_t* lens, int32_t* fine_lens, int32_t* takes, int64_t topk,
+                      int64_t num, int64_t den, int64_t sink, int64_t window, int64_t batch,
+                      void* stream);
+
+/* DS/kernels.py:488-514. rt i32 (row stride maxp), selected i32/i64 (row stride
+ * take), ft i32 [batch, fp]. */
+V1X_API int v1x_fine_table_shared(const int32_t* rt, const void* selected, int selected_is_i64,
+                          const int32_t* takes, int32_t* ft, const int32_t* tail_rows,
+                          int64_t cap, int64_t maxp, int64_t take, int64_t fp, int64_t scratch,
+                          int64_t batch, void* stream);
+
+/* DS/kernels.py:518-564. native_bytes u8 / native_scales f32 and fine_bytes /
+ * fine_scales are byte and float views of packed pools; nt row stride np.
+ * Programs (g, p) for g < grid_groups, p < grid_pages; rows g*group + [0, group)
+ * bounded by rows_bound when rows_bound > 0. */
+V1X_API int v1x_stage_tail_shared(const uint8_t* native_bytes, const float* native_scales,
+                          const int32_t* nt, const int32_t* lens, uint8_t* fine_bytes,
+                          float* fine_scales, const int32_t* tail_rows, int64_t cap,
+                          int64_t np, int64_t scratch, int64_t sink, int64_t window,
+                          int64_t rows_bound, int64_t group, int64_t grid_groups,
+                          int64_t grid_pages, void* stream);
+
+/* DS/kernels.py:444-472 (non-fused mask). scores row stride `stride`, WIDTH cols. */
+V1X_API int v1x_mask_fine(float* scores, const void* selected, int selected_is_i64, const int32_t* rt,
+                  const int32_t* members, const int32_t* lens, const int32_t* takes,
+                  int64_t maxp, int64_t take, int64_t stride, int64_t width, int64_t sink,
+                  int64_t window, int64_t batch, void* stream);
+
+/* DS/kernels.py:475-486. logits row stride `stride`; out f32 [batch, maxp];
+ * pages p < min(maxp, pcount) are written (pcount = programs x 32 in the reference). */
+V1X_API int v1x_reduce_centers(const float* logits, const int32_t* lens, float* out, int64_t maxp,
+                       int64_t pcount, int64_t stride, int64_t batch, void* stream);
+
+/* DS/kernels.py:323-376 (non-fused mapping). raw/out/logical i32 [batch, topk];
+ * scores row stride width. */
+V1X_API int v1x_output_ids(const int32_t* raw, const float* scores, const int32_t* members,
+                   const int32_t* rt, const int32_t* nt, const void* selected,
+                   int selected_is_i64, const int32_t* lens, const int32_t* takes, int32_t* out,
+                   int32_t* logical, const int32_t* ft, int64_t maxp, int64_t np, int64_t take,
+                   int64_t width, int64_t topk, int64_t sink, int64_t window, int map_physical,
+                   int direct_fine, int64_t fp, int64_t batch, void* stream);
+
+/* DS/kernels.py:594-600. logical i32 [batch, topk] -> out i32 [batch, stride]. */
+V1X_API int v1x_expand_logical(const int32_t* logical, int32_t* out, int64_t topk, int64_t stride,
+                       int64_t batch, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* FP8 paged scoring -- the DeepGEMM fp8_paged_mqa_logits contract the reference
+ * calls at DS/runtime.py:434-444 and :538-548 (next_n = 1), with the formula of
+ * DS/kernels.py:310-313: out[b, j] = sum_h w[b,h] * relu(q[b,h,:] . k_j) * s_j for
+ * j < lens[b], -inf for lens[b] <= j < max_len.
+ * q u8 (e4m3) [batch, heads, 128]; w f32 [batch, heads]; pool u8 [pool_pages, 8448];
+ * table i32 [batch, table_stride]; out f32 [batch, out_stride]. heads in [1, 256].
+ * relu = 0 gives the signed variant. */
+V1X_API int v1x_score_fp8(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages,
+                  const int32_t* lens, const int32_t* table, int64_t table_stride, float* out,
+                  int64_t out_stride, int64_t max_len, int64_t heads, int relu, int64_t batch,
+                  void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* _gather_slots -- replaces NA/kernels.py:62-77 (GatherWorkspace.gather, :102-111).
+ * For t < rows*top: id = ids[(t/top)*ids_stride + t%top]; if id >= 0 the slot
+ * p = req ? req[id] : id and kg[t, :] = k[p*ks0 + head*ks1 + d*ks2] (d < dim), same
+ * for v; else zero rows.  Element size elem_bytes in {1, 2, 4}; kg/vg contiguous
+ * [rows*top, dim]; v/vg may both be NULL (single-output gather). */
+V1X_API int v1x_gather_slots(const void* k, const void* v, const int32_t* req, const int32_t* ids,
+                     void* kg, void* vg, int64_t rows, int64_t top, int64_t head, int64_t ks0,
+                     int64_t ks1, int64_t ks2, int64_t vs0, int64_t vs1, int64_t vs2,
+                     int64_t ids_stride, int64_t dim, int64_t elem_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* V1X_H */

@@ -625,8 +625,9 @@ def score_row(q_u8, w, keys, scales, relu=True, exact=True):
     DeepGEMM at experiments/fine_pool_shared_20261021/test_and_bench.py:37-41.
     exact=True fixes the fp32 evaluation order the SIMT CUDA scorer uses:
     per head, d = 0..127 accumulated in fp32 (every e4m3 x e4m3 product is
-    exact in fp32); then heads 0..H-1 accumulated as acc += w[h] * relu(dot)
-    with separately rounded multiply and add; then one multiply by the scale.
+    exact in fp32); relu(x) = x if x > 0 else +0; then heads 0..H-1
+    accumulated as acc += w[h] * relu(dot) with separately rounded multiply
+    and add; then one multiply by the scale.
     exact=False uses a float64 BLAS product (for large cases / timing).
     """
     q = e4m3_to_f32(np.asarray(q_u8, np.uint8)).reshape(-1, 128)
@@ -641,7 +642,7 @@ def score_row(q_u8, w, keys, scales, relu=True, exact=True):
     for d in range(128):
         dot = dot + q[:, d:d + 1] * keys[None, :, d]
     if relu:
-        dot = np.maximum(dot, np.float32(0))
+        dot = np.where(dot > 0, dot, np.float32(0)).astype(np.float32)
     acc = np.zeros(keys.shape[0], np.float32)
     for h in range(H):
         acc = acc + (w[h] * dot[h]).astype(np.float32)

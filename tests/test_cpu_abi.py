@@ -1,0 +1,56 @@
+"""CPU: the C-ABI library loads, exports every declared entry point, and the
+Python shims refuse to run without CUDA tensors (there is no CPU path)."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def declared_symbols():
+    text = (ROOT / "include" / "v1x.h").read_text()
+    return sorted(set(re.findall(r"V1X_API\s+[\w\s\*]*?\b(v1x_\w+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    syms = declared_symbols()
+    assert len(syms) >= 20
+    assert "v1x_route" in syms and "v1x_topk" in syms and "v1x_gather_slots" in syms
+
+
+def test_library_exports_every_declared_symbol(v1x):
+    lib = ctypes.CDLL(v1x.library_path())
+    for s in declared_symbols():
+        assert hasattr(lib, s), f"missing export {s}"
+    assert lib.v1x_version() == 0x000100
+
+
+def test_ctypes_table_covers_header(v1x):
+    from importlib import import_module
+    _lib = import_module("10_20_b200._lib")
+    assert sorted(_lib.SIGNATURES) == declared_symbols()
+
+
+def test_shims_reject_cpu_tensors(v1x):
+    from importlib import import_module
+    qf = import_module("10_20_b200.query_fused")
+    B, P = 4, 64
+    scores = torch.zeros((B, P * 8))
+    i32 = lambda *s: torch.zeros(s, dtype=torch.int32)
+    with pytest.raises(ValueError):
+        qf.module().route(scores, i32(B), i32(B), i32(B, 8), P, i32(B, P), i32(B, 76), i32(B), 1, True)
+    gather = import_module("10_20_b200.gather")
+    ws = gather.GatherWorkspace(2, "cpu", torch.bfloat16)
+    with pytest.raises(ValueError):
+        ws.gather(torch.zeros((8, 1, 128), dtype=torch.bfloat16), None, None,
+                  torch.zeros((2, 2048), dtype=torch.int32), 0)
+
+
+def test_triton_style_launcher_requires_grid(v1x):
+    from importlib import import_module
+    K = import_module("10_20_b200.kernels")
+    with pytest.raises(TypeError):
+        K.release(None, None, None, None)

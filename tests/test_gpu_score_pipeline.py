@@ -1,0 +1,134 @@
+"""GPU parity: FP8 paged scoring (DeepGEMM fp8_paged_mqa_logits contract) and
+the composed selection step vs the oracle.
+
+Tolerances: the few-head SIMT scorer follows the oracle's fixed fp32 order and
+must match it exactly; the tensor-core scorer (many heads) must be within
+rtol = 1e-2 of the fp64 reference math (the north-star score tolerance), with
+an absolute floor of 1e-3 x the row's largest |score|.  Selection parity is
+bit-exact given the device scores.
+"""
+import importlib
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+S = importlib.import_module("10_20_b200.scoring")
+synth = importlib.import_module("10_20_b200.synth")
+pipeline = importlib.import_module("10_20_b200.pipeline")
+
+RTOL = 1e-2
+
+
+def dev(x):
+    return torch.as_tensor(np.ascontiguousarray(x)).cuda()
+
+
+def close(got, exp):
+    fin = np.isfinite(exp)
+    assert np.array_equal(np.isfinite(got), fin)
+    for r in range(exp.shape[0]):
+        e, g = exp[r][fin[r]], got[r][fin[r]]
+        if e.size == 0:
+            continue
+        atol = 1e-3 * np.abs(e).max()
+        assert np.all(np.abs(g - e) <= atol + RTOL * np.abs(e)), r
+
+
+def test_score_golden_formula(golden, cuda_dev):
+    """Centre logits: the reference coarse kernel's page maxima (H=16)."""
+    g = golden("scores")
+    B, H, MAXP = 2, 16, 64
+    lens = torch.as_tensor([(int(n) - 1) // 1024 * 128 for n in g["lens"]], dtype=torch.int32).cuda()
+    out = S.fp8_paged_mqa_logits(dev(g["q"]).view(torch.float8_e4m3fn), dev(g["centers"]), dev(g["w"]),
+                                 lens, dev(g["ctable"]), None, MAXP * 8)
+    pm = out.view(B, MAXP, 8).amax(-1).cpu().numpy()
+    np.testing.assert_allclose(pm, g["coarse"], rtol=2e-5, atol=2e-5)
+
+
+@pytest.mark.parametrize("H", [1, 2, 16, 32, 64])
+def test_score_exact_vs_oracle(H, cuda_dev):
+    rng = np.random.default_rng(H)
+    B, NP = 3, 40
+    pool = np.zeros((NP, 8448), np.uint8)
+    kb = torch.randn((NP, 64, 128), generator=torch.Generator().manual_seed(H)).to(torch.float8_e4m3fn)
+    pool[:, :8192] = kb.view(torch.uint8).reshape(NP, 8192).numpy()
+    pool.view(np.float32)[:, 2048:] = rng.random((NP, 64)).astype(np.float32) + 0.1
+    q = torch.randn((B, H, 128), generator=torch.Generator().manual_seed(7 + H)).to(torch.float8_e4m3fn)
+    q8 = q.view(torch.uint8).numpy()
+    w = rng.random((B, H)).astype(np.float32)
+    table = np.stack([rng.permutation(NP)[:20] for _ in range(B)]).astype(np.int32)
+    lens = np.array([1280, 1, 700], np.int32)
+    out = S.fp8_paged_mqa_logits(q.cuda(), dev(pool), dev(w), dev(lens), dev(table), None, 1300).cpu().numpy()
+    exp = O.score_paged(q8, w, pool, table, lens, 1300, exact=True)
+    if H <= 64:
+        assert np.array_equal(out, exp), np.abs(out - exp).max()
+    close(out, O.score_paged(q8, w, pool, table, lens, 1300, exact=False))
+
+
+def _small_case(B=24, H=64, seed=5, latent=576):
+    lens = synth.decode_lens(B, 2048, 20000, seed)
+    lens[0] = 4097
+    lens[1] = 3073
+    return synth.make_query_case(B, H, lens, P=512, take=12, window=64, topk=2048, seed=seed,
+                                 device="cuda", latent_dim=latent)
+
+
+def test_selection_step_end_to_end(cuda_dev):
+    """Every stage of the step vs the oracle: metadata exact, centre/fine scores
+    within tolerance, route/top-k/gather bit-exact given the device scores."""
+    case = _small_case()
+    step = pipeline.SelectionStep(case, gather=True)
+    step.run()
+    torch.cuda.synchronize()
+    c = case
+    lens = c.lens.cpu().numpy()
+    nt = c.native_table.cpu().numpy()
+    fl, tk, dg, cl, tr = O.query_metadata(lens, nt, c.P, 2048, 1, 2, 64, c.window, budget=c.take)
+    assert np.array_equal(step.fine_lens.cpu().numpy(), fl)
+    assert np.array_equal(step.takes.cpu().numpy(), tk)
+    assert np.array_equal(step.tail_rows.cpu().numpy(), tr)
+    q8 = c.q8.view(torch.uint8).cpu().numpy()
+    w = c.w.cpu().numpy()
+    centers = c.centers.cpu().numpy()
+    ctab = c.center_table.cpu().numpy()
+    clog = step.center_logits.cpu().numpy()
+    close(clog, O.score_paged(q8, w, centers, ctab, cl, c.P * 8, exact=False))
+    rt = c.reordered_table.cpu().numpy()
+    sel, ft = O.route(clog, lens, tk, c.take, c.P, rt, np.zeros((c.B, step.width // 64), np.int32), tr,
+                      c.capacity, False)
+    assert np.array_equal(step.selected.cpu().numpy(), sel)
+    ft = O.fine_table_shared(rt, sel, tk, (c.B, step.width // 64), tr, c.capacity, c.P, c.take, 68)
+    assert np.array_equal(step.fine_table.cpu().numpy(), ft)
+    fine_pool = c.fine.cpu().numpy()
+    fine_exp = O.score_paged(q8, w, fine_pool, ft, dg, step.width, exact=False)
+    got_scores = step.scores.cpu().numpy()   # masked in place by the top-k
+    members = c.members.cpu().numpy()
+    unmasked = got_scores.copy()
+    e = O.topk(got_scores, fl, members, rt, nt, sel, lens, tk, c.window, True, 2048,
+               fine_table=ft, direct_fine=False)
+    assert np.array_equal(e["scores"], got_scores)          # mask is idempotent
+    assert np.array_equal(step.raw.cpu().numpy(), e["raw"])
+    assert np.array_equal(step.logical.cpu().numpy(), e["logical"])
+    assert np.array_equal(step.physical.cpu().numpy(), e["physical"])
+    fin = np.isfinite(unmasked)
+    close(np.where(fin, unmasked, -np.inf), np.where(fin, fine_exp, -np.inf))
+    lat = c.latent.view(torch.int16).cpu().numpy()
+    kg, _ = O.gather_slots(lat, None, None, step.physical.cpu().numpy(), c.B, 2048, 0)
+    assert np.array_equal(step.kv.view(torch.int16).reshape(-1, lat.shape[-1]).cpu().numpy(), kg)
+
+
+def test_selection_step_graph_replay(cuda_dev):
+    case = _small_case(B=8, seed=9, latent=0)
+    step = pipeline.SelectionStep(case, gather=False)
+    step.run()
+    ref = step.physical.clone()
+    step.capture()
+    step.physical.fill_(-3)
+    step.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(step.physical, ref)
