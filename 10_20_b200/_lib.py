@@ -20,6 +20,7 @@ V1X_ERR_INVALID = -1
 V1X_ERR_CUDA = -2
 V1X_ERR_UNSUPPORTED = -3
 V1X_STATUS_ARENA_EXHAUSTED = 1
+V1X_STATUS_TIMEOUT = 2
 
 P = ctypes.c_void_p
 I64 = ctypes.c_int64
@@ -48,7 +49,7 @@ SIGNATURES = {
     "v1x_output_ids": [P, P, P, P, P, P, I32, P, P, P, P, P, I64, I64, I64, I64, I64, I64, I64, I32,
                        I32, I64, I64, P],
     "v1x_expand_logical": [P, P, I64, I64, I64, P],
-    "v1x_score_fp8": [P, P, P, I64, P, P, I64, P, I64, I64, I64, I32, I64, P],
+    "v1x_score_fp8": [P, P, P, I64, P, P, I64, P, I64, I64, I64, I32, I32, I32, P, I64, P],
     "v1x_gather_slots": [P, P, P, P, P, P, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64,
                          P],
 }

@@ -31,7 +31,7 @@ struct ScoreArgs {
   int64_t table_stride;
   float* out;
   int64_t out_stride, max_len;
-  int heads, relu;
+  int heads, relu, clean;
 };
 
 __device__ __forceinline__ float2 e4m3x2_to_float2(uint16_t v) {
@@ -55,6 +55,7 @@ __global__ void __launch_bounds__(kScoreThreads) score_simt_kernel(const __grid_
   const int64_t j = static_cast<int64_t>(blockIdx.y) * blockDim.x + threadIdx.x;
   if (j >= a.max_len) return;
   const int n = a.lens[b];
+  if (j >= n && !a.clean) return;
   float result = -CUDART_INF_F;
   if (j < n) {
     const int64_t page = a.table[b * a.table_stride + j / 64];
@@ -90,26 +91,35 @@ __global__ void __launch_bounds__(kScoreThreads) score_simt_kernel(const __grid_
 }
 
 }  // namespace
+
+int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages, const int32_t* lens,
+                 const int32_t* table, int64_t table_stride, float* out, int64_t out_stride, int64_t max_len,
+                 int64_t heads, int relu, int clean, int64_t batch, int32_t* status, cudaStream_t stream);
 }  // namespace v1x
 
 extern "C" int v1x_score_fp8(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages,
                              const int32_t* lens, const int32_t* table, int64_t table_stride,
                              float* out, int64_t out_stride, int64_t max_len, int64_t heads,
-                             int relu, int64_t batch, void* stream) {
+                             int relu, int clean, int impl, int32_t* status, int64_t batch,
+                             void* stream) {
   using namespace v1x;
   clear_error();
   V1X_CHECK_ARG(heads >= 1 && heads <= 256, "score_fp8: heads must be in [1, 256]");
   V1X_CHECK_ARG(batch >= 0 && max_len >= 0 && out_stride >= max_len && pool_pages > 0,
                 "score_fp8: bad geometry");
   V1X_CHECK_ARG((reinterpret_cast<uintptr_t>(pool) & 15) == 0, "score_fp8: pool must be 16-byte aligned");
-  V1X_CHECK_ARG(table_stride * 64 >= 0, "score_fp8: bad table stride");
+  V1X_CHECK_ARG(table_stride >= 0 && impl >= 0 && impl <= 2, "score_fp8: bad table stride / impl");
   if (batch == 0 || max_len == 0) return V1X_OK;
+  const bool tc = impl == 2 || (impl == 0 && heads % 32 == 0);
+  if (tc)
+    return score_fp8_tc(q, w, pool, pool_pages, lens, table, table_stride, out, out_stride, max_len, heads,
+                        relu, clean, batch, status, as_stream(stream));
   if (heads > kSimtMaxHeads) {
-    set_error("score_fp8: heads > %d not implemented", kSimtMaxHeads);
+    set_error("score_fp8: the SIMT path takes heads <= %d", kSimtMaxHeads);
     return V1X_ERR_UNSUPPORTED;
   }
   ScoreArgs a{q, w, pool, lens, table, table_stride, out, out_stride, max_len,
-              static_cast<int>(heads), relu};
+              static_cast<int>(heads), relu, clean};
   const dim3 grid(static_cast<unsigned>(batch), static_cast<unsigned>((max_len + kScoreThreads - 1) / kScoreThreads));
   score_simt_kernel<<<grid, kScoreThreads, 0, as_stream(stream)>>>(a);
   return launch_status("v1x_score_fp8");

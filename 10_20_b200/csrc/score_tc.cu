@@ -1,0 +1,326 @@
+// Tensor-core FP8 paged scoring for sm_100a (tcgen05, TMA, TMEM).
+//
+//   out[b, j] = sum_h w[b,h] * relu(q[b,h,:] . k_j) * scale_j      (j < len[b])
+//
+// Same contract as the SIMT path in score.cu (DeepGEMM fp8_paged_mqa_logits as
+// called at sglang/srt/layers/attention/v1_deepseek/runtime.py:434-444 and
+// :538-548; formula of kernels.py:310-313).  With many index heads the score is
+// a dense contraction -- 64 heads x 128 dims per key is ~124 FLOP per key byte --
+// so it runs on the 5th-generation tensor cores:
+//
+//   tile = 128 keys (two 64-token pages) of one row; D[128 x H] = K[128 x 128] .
+//   Q[H x 128]^T with tcgen05.mma kind::f8f6f4 (E4M3 x E4M3 -> F32), four K=32
+//   steps, accumulator in TMEM (two accumulators, ping-pong).
+//
+// Warp roles in a persistent CTA (192 threads):
+//   warp 0    TMA producer: per tile, two 8 KB page boxes (3-D tensor map over
+//             the packed pool, 128-byte swizzle) + the row's 64x128 q box.
+//   warp 1    TMEM owner + single-thread MMA issuer; commits release the smem
+//             stage and publish the accumulator.
+//   warps 2-5 epilogue: tcgen05.ld of the accumulator (one key per thread),
+//             ReLU, weighted head sum, per-key scale, coalesced store.
+// Tiles (row, 128-key block) are enumerated from a per-row prefix computed in
+// shared memory from the device lengths and dealt round-robin to the CTAs.
+// Every mbarrier wait is bounded (2 s); on timeout the CTA records
+// V1X_STATUS_TIMEOUT, drains what it issued and frees its TMEM before exiting.
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "sm100.cuh"
+
+namespace v1x {
+namespace {
+
+using namespace sm100;
+
+constexpr int kTcThreads = 192;
+constexpr int kTcStages = 4;
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+constexpr int kMaxTcRows = 8192;
+
+struct TcArgs {
+  const int32_t* lens;
+  const int32_t* table;
+  int64_t table_stride;
+  const float* w;
+  const uint8_t* pool;
+  float* out;
+  int64_t out_stride, max_len;
+  int B, H, relu, clean;
+  uint32_t tmem_cols;
+  int32_t* status;
+};
+
+struct TcShared {
+  uint64_t full[kTcStages], empty[kTcStages], tfull[2], tempty[2];
+  uint32_t tmem_base;
+  int abort;
+  int zero;  // always 0: lets drain waits ignore the abort flag
+  int warp_tot[kTcThreads / 32 + 1];
+  int total;
+};
+
+__device__ __forceinline__ int locate_row(const int* prefix, int B, int T) {
+  int lo = 0, hi = B;  // prefix[lo] <= T < prefix[hi]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (prefix[mid] <= T) lo = mid;
+    else hi = mid;
+  }
+  return lo;
+}
+
+__device__ __forceinline__ void raise_abort(TcShared& sh, int32_t* status) {
+  *reinterpret_cast<volatile int*>(&sh.abort) = 1;
+  if (status) atomicExch(status, V1X_STATUS_TIMEOUT);
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    score_tc_kernel(const __grid_constant__ CUtensorMap pool_map, const __grid_constant__ CUtensorMap q_map,
+                    const __grid_constant__ TcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t b_bytes = static_cast<uint32_t>(a.H) * 128;
+  const uint32_t stage_bytes = 16384 + b_bytes;
+  TcShared& sh = *reinterpret_cast<TcShared*>(base + kTcStages * stage_bytes);
+  int* prefix = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(&sh) + sizeof(TcShared));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  // ---- per-row tile prefix ----------------------------------------------------
+  {
+    const int chunk = (a.B + kTcThreads - 1) / kTcThreads;
+    const int beg = min(tid * chunk, a.B), end = min(beg + chunk, a.B);
+    int local = 0;
+    for (int b = beg; b < end; ++b) {
+      const int64_t eff = min(static_cast<int64_t>(a.lens[b]), a.max_len);
+      local += eff > 0 ? static_cast<int>((eff + 127) / 128) : 0;
+    }
+    int tot;
+    int run = block_exclusive_scan(local, sh.warp_tot, &tot);
+    for (int b = beg; b < end; ++b) {
+      prefix[b] = run;
+      const int64_t eff = min(static_cast<int64_t>(a.lens[b]), a.max_len);
+      run += eff > 0 ? static_cast<int>((eff + 127) / 128) : 0;
+    }
+    if (tid == 0) {
+      prefix[a.B] = tot;
+      sh.total = tot;
+      sh.abort = 0;
+      sh.zero = 0;
+      for (int s = 0; s < kTcStages; ++s) {
+        mbar_init(&sh.full[s], 1);
+        mbar_init(&sh.empty[s], 1);
+      }
+      for (int c = 0; c < 2; ++c) {
+        mbar_init(&sh.tfull[c], 1);
+        mbar_init(&sh.tempty[c], 128);
+      }
+      fence_mbar_init();
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(&sh.tmem_base, a.tmem_cols);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&pool_map);
+    tma_prefetch_desc(&q_map);
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh.tmem_base;
+  const int total = sh.total;
+  const int G = gridDim.x;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int it = 0;
+      for (int T = blockIdx.x; T < total; T += G, ++it) {
+        const int s = it % kTcStages;
+        const uint32_t ph = (it / kTcStages) & 1;
+        if (!mbar_wait(&sh.empty[s], ph ^ 1, &sh.abort, kWaitLimitNs)) { raise_abort(sh, a.status); break; }
+        const int b = locate_row(prefix, a.B, T);
+        const int t = T - prefix[b];
+        const int64_t eff = min(static_cast<int64_t>(a.lens[b]), a.max_len);
+        const int p0 = a.table[b * a.table_stride + 2 * t];
+        const int p1 = (static_cast<int64_t>(2 * t + 1) * 64 < eff) ? a.table[b * a.table_stride + 2 * t + 1] : p0;
+        uint8_t* st = base + s * stage_bytes;
+        mbar_arrive_expect_tx(&sh.full[s], stage_bytes);
+        tma_load_3d(st, &pool_map, &sh.full[s], 0, 0, p0);
+        tma_load_3d(st + 8192, &pool_map, &sh.full[s], 0, 0, p1);
+        tma_load_2d(st + 16384, &q_map, &sh.full[s], 0, b * a.H);
+      }
+      if (*reinterpret_cast<volatile int*>(&sh.abort)) {  // drain the loads this thread issued
+        const int issued = it;
+        for (int k = max(0, issued - kTcStages); k < issued; ++k)
+          mbar_wait(&sh.full[k % kTcStages], (k / kTcStages) & 1, &sh.zero, kWaitLimitNs);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idesc = idesc_e4m3_f32(128, a.H);
+      int it = 0;
+      for (int T = blockIdx.x; T < total; T += G, ++it) {
+        const int s = it % kTcStages;
+        const uint32_t ph = (it / kTcStages) & 1;
+        const int acc = it & 1;
+        const uint32_t aph = (it >> 1) & 1;
+        if (!mbar_wait(&sh.tempty[acc], aph ^ 1, &sh.abort, kWaitLimitNs)) { raise_abort(sh, a.status); break; }
+        if (!mbar_wait(&sh.full[s], ph, &sh.abort, kWaitLimitNs)) { raise_abort(sh, a.status); break; }
+        tc_fence_after();
+        const uint32_t sa = smem_u32(base + s * stage_bytes);
+        const uint32_t sb = sa + 16384;
+        const uint32_t d = tmem + static_cast<uint32_t>(acc * a.H);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          umma_f8(d, umma_desc_sw128(sa + 32 * k), umma_desc_sw128(sb + 32 * k), idesc, k > 0 ? 1u : 0u);
+        umma_commit(&sh.empty[s]);
+        umma_commit(&sh.tfull[acc]);
+      }
+      if (*reinterpret_cast<volatile int*>(&sh.abort) && it > 0) {  // let issued MMAs retire
+        const int k = it - 1;
+        mbar_wait(&sh.tfull[k & 1], (k >> 1) & 1, &sh.zero, kWaitLimitNs);
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int q4 = warp & 3;
+    const int i = q4 * 32 + lane;
+    const float* poolf = reinterpret_cast<const float*>(a.pool);
+    int it = 0;
+    for (int T = blockIdx.x; T < total; T += G, ++it) {
+      const int acc = it & 1;
+      const uint32_t aph = (it >> 1) & 1;
+      const int b = locate_row(prefix, a.B, T);
+      const int t = T - prefix[b];
+      const int64_t eff = min(static_cast<int64_t>(a.lens[b]), a.max_len);
+      const int64_t key = static_cast<int64_t>(t) * 128 + i;
+      float scale = 0.0f;
+      if (key < eff) {
+        const int64_t page = a.table[b * a.table_stride + (key >> 6)];
+        scale = __ldg(poolf + page * kPageWords + kScaleWord + (key & 63));
+      }
+      if (!mbar_wait(&sh.tfull[acc], aph, &sh.abort, kWaitLimitNs)) { raise_abort(sh, a.status); break; }
+      tc_fence_after();
+      float sum = 0.0f;
+      const float* wr = a.w + static_cast<int64_t>(b) * a.H;
+      for (int c0 = 0; c0 < a.H; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem + (static_cast<uint32_t>(q4 * 32) << 16) + static_cast<uint32_t>(acc * a.H + c0), r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          const float4 w4 = __ldg(reinterpret_cast<const float4*>(wr + c0 + j));
+          float v0 = __uint_as_float(r[j]), v1 = __uint_as_float(r[j + 1]);
+          float v2 = __uint_as_float(r[j + 2]), v3 = __uint_as_float(r[j + 3]);
+          if (a.relu) {
+            v0 = fmaxf(v0, 0.0f); v1 = fmaxf(v1, 0.0f); v2 = fmaxf(v2, 0.0f); v3 = fmaxf(v3, 0.0f);
+          }
+          sum = fmaf(w4.x, v0, sum);
+          sum = fmaf(w4.y, v1, sum);
+          sum = fmaf(w4.z, v2, sum);
+          sum = fmaf(w4.w, v3, sum);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&sh.tempty[acc]);
+      if (key < a.max_len && (key < eff || a.clean))
+        a.out[b * a.out_stride + key] = key < eff ? sum * scale : -CUDART_INF_F;
+    }
+    if (a.clean) {
+      const int e = tid - 64;
+      for (int b = blockIdx.x; b < a.B; b += G) {
+        const int64_t eff = min(static_cast<int64_t>(a.lens[b]), a.max_len);
+        const int64_t start = eff > 0 ? (eff + 127) / 128 * 128 : 0;
+        for (int64_t j = start + e; j < a.max_len; j += 128) a.out[b * a.out_stride + j] = -CUDART_INF_F;
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, a.tmem_cols);
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+}  // namespace
+
+// Launch the tensor-core scorer; returns V1X_ERR_UNSUPPORTED if the shape is not covered.
+int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages, const int32_t* lens,
+                 const int32_t* table, int64_t table_stride, float* out, int64_t out_stride, int64_t max_len,
+                 int64_t heads, int relu, int clean, int64_t batch, int32_t* status, cudaStream_t stream) {
+  if (heads % 32 != 0 || heads > 256 || batch > kMaxTcRows || pool_pages >= (int64_t(1) << 31)) {
+    set_error("score_fp8 (tensor core): heads must be a multiple of 32 <= 256 and batch <= %d", kMaxTcRows);
+    return V1X_ERR_UNSUPPORTED;
+  }
+  if ((reinterpret_cast<uintptr_t>(q) & 15) != 0) {
+    set_error("score_fp8 (tensor core): q must be 16-byte aligned");
+    return V1X_ERR_INVALID;
+  }
+  auto enc = encode_fn();
+  if (!enc) {
+    set_error("score_fp8: cuTensorMapEncodeTiled unavailable");
+    return V1X_ERR_CUDA;
+  }
+  CUtensorMap pool_map, q_map;
+  {
+    cuuint64_t dims[3] = {128, 64, static_cast<cuuint64_t>(pool_pages)};
+    cuuint64_t strides[2] = {128, static_cast<cuuint64_t>(kPageBytes)};
+    cuuint32_t box[3] = {128, 64, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    CUresult r = enc(&pool_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(pool), dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+      set_error("score_fp8: pool tensor map encode failed (%d)", static_cast<int>(r));
+      return V1X_ERR_CUDA;
+    }
+  }
+  {
+    cuuint64_t dims[2] = {128, static_cast<cuuint64_t>(batch * heads)};
+    cuuint64_t strides[1] = {128};
+    cuuint32_t box[2] = {128, static_cast<cuuint32_t>(heads)};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = enc(&q_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(q), dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+      set_error("score_fp8: q tensor map encode failed (%d)", static_cast<int>(r));
+      return V1X_ERR_CUDA;
+    }
+  }
+  uint32_t cols = 32;
+  while (cols < static_cast<uint32_t>(2 * heads)) cols <<= 1;
+  TcArgs args{lens, table, table_stride, w, pool, out, out_stride, max_len, static_cast<int>(batch),
+              static_cast<int>(heads), relu, clean, cols, status};
+  const size_t smem = 1024 + kTcStages * (16384 + heads * 128) + sizeof(TcShared) + (batch + 1) * 4 + 16;
+  static DeviceOnce once;
+  if (once.first())
+    cudaFuncSetAttribute(score_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  if (smem > 227 * 1024) {
+    set_error("score_fp8 (tensor core): shared memory %zu too large", smem);
+    return V1X_ERR_UNSUPPORTED;
+  }
+  const int64_t max_tiles = batch * ((max_len + 127) / 128);
+  int64_t grid = static_cast<int64_t>(num_sms()) * (cols <= 256 ? 2 : 1);
+  if (grid > max_tiles) grid = max_tiles > 0 ? max_tiles : 1;
+  score_tc_kernel<<<static_cast<unsigned>(grid), kTcThreads, smem, stream>>>(pool_map, q_map, args);
+  return launch_status("v1x_score_fp8 (tensor core)");
+}
+
+}  // namespace v1x

@@ -26,14 +26,19 @@ def get_paged_mqa_logits_metadata(context_lens: torch.Tensor, block_size: int, n
     return torch.zeros((num_sms + 1, 2), dtype=torch.int32, device=context_lens.device)
 
 
+IMPLS = {"auto": 0, "simt": 1, "tensor_core": 2}
+
+
 def fp8_paged_mqa_logits(q, kv_cache, weights, context_lens, block_table, schedule_meta,
                          max_context_len: int, clean_logits: bool = True, relu: bool = True,
-                         out: torch.Tensor | None = None):
+                         out: torch.Tensor | None = None, impl: str = "auto"):
     """Logits [B, max_context_len] (float32); columns >= context_lens[b] are -inf.
 
     q: e4m3 [B, H, 128] or [B, 1, H, 128]; kv_cache: packed uint8 [pages, 8448] or
     [pages, 64, 1, 132]; weights: float32 [B, H]; context_lens: int32 [B] or [B, 1];
-    block_table: int32 [B, max_blocks].
+    block_table: int32 [B, max_blocks].  impl: "auto" (tensor cores when H is a
+    multiple of 32), "simt" (fixed fp32 evaluation order, H <= 64) or "tensor_core".
+    clean_logits=False leaves columns >= context_lens[b] untouched.
     """
     if q.dim() == 4:
         require(q.shape[1] == 1, "only next_n == 1 is supported")
@@ -54,7 +59,9 @@ def fp8_paged_mqa_logits(q, kv_cache, weights, context_lens, block_table, schedu
         out = torch.empty((B, max_context_len), dtype=torch.float32, device=q.device)
     require(out.dtype == torch.float32 and out.stride(1) == 1 and out.shape[1] >= max_context_len,
             "out: float32 [B, >= max_context_len]")
+    from .kernels import status_word
     _lib.call("v1x_score_fp8", ptr(q), ptr(weights), ptr(kv_cache), kv_cache.numel() // 8448, ptr(lens),
               ptr(block_table), block_table.stride(0), ptr(out), out.stride(0), int(max_context_len), H,
-              int(bool(relu)), B, _lib.stream_of(q), device=q.device)
+              int(bool(relu)), int(bool(clean_logits)), IMPLS[impl], ptr(status_word(q.device)), B,
+              _lib.stream_of(q), device=q.device)
     return out

@@ -22,7 +22,6 @@ import importlib
 import json
 import os
 import statistics
-import subprocess
 import sys
 import time
 from pathlib import Path
@@ -63,55 +62,63 @@ def make_case(synth, cfg, seed, device, rows=None):
 
 
 class Clocks:
-    """Sample SM clocks / throttle reasons with nvidia-smi during the timed region."""
+    """Sample SM clocks and clock-event (throttle) reasons through NVML in a
+    background thread every ~2 ms while the timed region runs."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown"}
 
-    def __init__(self, index):
-        self.index = index
-        self.proc = None
+    def __init__(self, device: torch.device):
+        self.device = device
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = None
+
+    def _handle(self, nv):
+        try:
+            p = torch.cuda.get_device_properties(self.device)
+            bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+            return nv.nvmlDeviceGetHandleByPciBusId_v2(bus)
+        except Exception:
+            return nv.nvmlDeviceGetHandleByIndex(self.device.index or 0)
 
     def __enter__(self):
+        import threading
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
-                 "-i", str(self.index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+            import pynvml as nv
+            nv.nvmlInit()
+            h = self._handle(nv)
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        except Exception:
+            return self
+        self._stop = threading.Event()
+
+        def loop():
+            while True:
+                try:
+                    self.samples.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
+                    r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    for bit, name in self.REASONS.items():
+                        if r & bit:
+                            self.reasons.add(name)
+                except Exception:
+                    pass
+                if self._stop.wait(0.002):
+                    break
+
+        self._thr = threading.Thread(target=loop, daemon=True)
+        self._thr.start()
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [l for l in out.splitlines() if l.strip()]
+        if self._stop is not None:
+            self._stop.set()
+            self._thr.join(timeout=2)
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for l in getattr(self, "lines", []):
-            f = [x.strip() for x in l.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
 def cpu_port_rate(cfg, seed, rows, budget_s=20.0):
@@ -128,7 +135,7 @@ def cpu_port_rate(cfg, seed, rows, budget_s=20.0):
         port.run_rows(c, rows=[done % rows])
         done += 1
         el = time.perf_counter() - t0
-        if el >= budget_s or done >= 4 * rows:
+        if el >= budget_s or done >= 64 * rows:
             break
     return done / el, dict(rows=done, seconds=round(el, 3), sample_requests=rows,
                            lens=[int(x) for x in c["lens"]])
@@ -163,13 +170,17 @@ def run_reference(args, cfg):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--requests", type=int, default=0,
+                    help="override the per-GPU batch (small cases for profiling; not a bench config)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="decode", choices=["decode", "single"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     cfg = workload_cfg(args.workload)
+    if args.requests:
+        cfg["B"] = args.requests
     if args.impl == "reference":
         return run_reference(args, cfg)
 
@@ -235,7 +246,7 @@ def main():
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
-    with Clocks(local) as clk:
+    with Clocks(device) as clk:
         t0 = time.perf_counter()
         for i in range(args.steps):
             one_step(events[i])

@@ -44,6 +44,7 @@ extern "C" {
 /* device status word values (written by kernels, read by the host) */
 #define V1X_STATUS_OK 0
 #define V1X_STATUS_ARENA_EXHAUSTED 1 /* allocate: free stack smaller than needed */
+#define V1X_STATUS_TIMEOUT 2         /* a bounded device-side wait gave up          */
 
 /* Library identity: returns 0x010000 * major + 0x100 * minor + patch. */
 V1X_API int v1x_version(void);
@@ -208,14 +209,17 @@ V1X_API int v1x_expand_logical(const int32_t* logical, int32_t* out, int64_t top
 /* FP8 paged scoring -- the DeepGEMM fp8_paged_mqa_logits contract the reference
  * calls at DS/runtime.py:434-444 and :538-548 (next_n = 1), with the formula of
  * DS/kernels.py:310-313: out[b, j] = sum_h w[b,h] * relu(q[b,h,:] . k_j) * s_j for
- * j < lens[b], -inf for lens[b] <= j < max_len.
+ * j < lens[b]; when clean != 0 also -inf for lens[b] <= j < max_len.
  * q u8 (e4m3) [batch, heads, 128]; w f32 [batch, heads]; pool u8 [pool_pages, 8448];
  * table i32 [batch, table_stride]; out f32 [batch, out_stride]. heads in [1, 256].
- * relu = 0 gives the signed variant. */
+ * relu = 0 gives the signed variant.  impl: 0 = automatic (tensor cores when heads
+ * is a multiple of 32, else the SIMT path), 1 = SIMT (fixed fp32 order, heads <=
+ * 64), 2 = tensor cores.  status: optional i32 device word receiving
+ * V1X_STATUS_TIMEOUT if a bounded device wait gave up. */
 V1X_API int v1x_score_fp8(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages,
                   const int32_t* lens, const int32_t* table, int64_t table_stride, float* out,
-                  int64_t out_stride, int64_t max_len, int64_t heads, int relu, int64_t batch,
-                  void* stream);
+                  int64_t out_stride, int64_t max_len, int64_t heads, int relu, int clean,
+                  int impl, int32_t* status, int64_t batch, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* _gather_slots -- replaces NA/kernels.py:62-77 (GatherWorkspace.gather, :102-111).

@@ -51,7 +51,7 @@ def test_score_golden_formula(golden, cuda_dev):
 
 
 @pytest.mark.parametrize("H", [1, 2, 16, 32, 64])
-def test_score_exact_vs_oracle(H, cuda_dev):
+def test_score_simt_exact_vs_oracle(H, cuda_dev):
     rng = np.random.default_rng(H)
     B, NP = 3, 40
     pool = np.zeros((NP, 8448), np.uint8)
@@ -63,11 +63,55 @@ def test_score_exact_vs_oracle(H, cuda_dev):
     w = rng.random((B, H)).astype(np.float32)
     table = np.stack([rng.permutation(NP)[:20] for _ in range(B)]).astype(np.int32)
     lens = np.array([1280, 1, 700], np.int32)
-    out = S.fp8_paged_mqa_logits(q.cuda(), dev(pool), dev(w), dev(lens), dev(table), None, 1300).cpu().numpy()
+    out = S.fp8_paged_mqa_logits(q.cuda(), dev(pool), dev(w), dev(lens), dev(table), None, 1300,
+                                 impl="simt").cpu().numpy()
     exp = O.score_paged(q8, w, pool, table, lens, 1300, exact=True)
-    if H <= 64:
-        assert np.array_equal(out, exp), np.abs(out - exp).max()
+    assert np.array_equal(out, exp), np.abs(out - exp).max()
     close(out, O.score_paged(q8, w, pool, table, lens, 1300, exact=False))
+
+
+@pytest.mark.parametrize("H", [32, 64, 128, 256])
+@pytest.mark.parametrize("relu", [True, False])
+def test_score_tensor_core_vs_oracle(H, relu, cuda_dev):
+    """tcgen05 scorer: ragged rows (empty, one key, partial tiles, longer than
+    max_len), many rows over many CTAs, non-multiple-of-128 max_len."""
+    rng = np.random.default_rng(H + relu)
+    B, NP = 70, 300
+    pool = np.zeros((NP, 8448), np.uint8)
+    kb = torch.randn((NP, 64, 128), generator=torch.Generator().manual_seed(H)).to(torch.float8_e4m3fn)
+    pool[:, :8192] = kb.view(torch.uint8).reshape(NP, 8192).numpy()
+    pool.view(np.float32)[:, 2048:] = rng.random((NP, 64)).astype(np.float32) + 0.1
+    q = torch.randn((B, H, 128), generator=torch.Generator().manual_seed(9 + H)).to(torch.float8_e4m3fn)
+    q8 = q.view(torch.uint8).numpy()
+    w = rng.random((B, H)).astype(np.float32)
+    table = np.stack([rng.permutation(NP)[:40] for _ in range(B)]).astype(np.int32)
+    lens = rng.integers(0, 2600, size=B).astype(np.int32)
+    lens[:6] = [0, 1, 127, 128, 129, 2560]
+    max_len = 2500
+    out = torch.full((B, 2600), 7.0, device="cuda")
+    S.fp8_paged_mqa_logits(q.cuda(), dev(pool), dev(w), dev(lens), dev(table), None, max_len,
+                           relu=relu, out=out, impl="tensor_core")
+    got = out.cpu().numpy()
+    exp = O.score_paged(q8, w, pool, table, np.minimum(lens, max_len), max_len, relu=relu, exact=False)
+    if relu:
+        close(got[:, :max_len], exp)
+    else:   # signed scores: absolute tolerance relative to the row scale
+        fin = np.isfinite(exp)
+        assert np.array_equal(np.isfinite(got[:, :max_len]), fin)
+        for r in range(B):
+            if fin[r].any():
+                e = exp[r][fin[r]]
+                assert np.abs(got[r, :max_len][fin[r]] - e).max() <= 1e-2 * np.abs(e).max()
+    assert (got[:, max_len:] == 7.0).all()          # columns past max_len untouched
+    # clean_logits=False leaves the padding alone
+    out.fill_(7.0)
+    S.fp8_paged_mqa_logits(q.cuda(), dev(pool), dev(w), dev(lens), dev(table), None, max_len,
+                           relu=relu, out=out, impl="tensor_core", clean_logits=False)
+    got2 = out.cpu().numpy()
+    for r in range(B):
+        n = min(int(lens[r]), max_len)
+        assert (got2[r, n:] == 7.0).all()
+        assert np.array_equal(got2[r, :n], got[r, :n])
 
 
 def _small_case(B=24, H=64, seed=5, latent=576):
