@@ -91,42 +91,61 @@ struct StageArgs {
   int64_t cap, np, scratch, sink, window, rows_bound, group;
 };
 
-// One program (g, p): for each owner row of group g in ascending order, stage
-// candidate slots [p*64, p*64+64) of that row's sink+tail list (:535-564).
-__global__ void __launch_bounds__(256) stage_tail_shared_kernel(const __grid_constant__ StageArgs a) {
-  const int64_t g = blockIdx.x;
-  const int p = blockIdx.y;
-  for (int64_t k = 0; k < a.group; ++k) {
-    const int64_t row = g * a.group + k;
-    if (a.rows_bound > 0 && row >= a.rows_bound) break;
-    if (a.tail_rows[row] != row) continue;
-    const int n = a.lens[row];
-    const RowBounds rb = row_bounds(n, static_cast<int>(a.sink), static_cast<int>(a.window));
-    const int count = rb.sink + n - rb.tail;
-    if (!(p * 64 < count || p == 0)) continue;
-    const int64_t dst = a.cap + row * a.scratch + p;
-    for (int c = threadIdx.x; c < 64 * 8; c += blockDim.x) {
-      const int tok = c >> 3, part = c & 7;
-      const int i = p * 64 + tok;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (i < count) {
-        const int logical = i < rb.sink ? i : rb.tail + i - rb.sink;
-        const int64_t page = a.nt[row * a.np + logical / 64];
-        v = reinterpret_cast<const uint4*>(a.native + page * kPageBytes + (logical % 64) * 128)[part];
+// Staging of each owner row's sink + tail candidates (:535-564).  The
+// reference runs programs (group, page) that loop over the group's owner rows;
+// rows write disjoint staging pages, so the order is free: here one CTA takes
+// one row and kStagePages consecutive staging pages, copies every needed 16-byte
+// chunk with several loads in flight, and zero-fills masked slots exactly as the
+// reference does (pages p with p*64 < count, plus page 0).
+constexpr int kStagePages = 4;
+
+__global__ void __launch_bounds__(256) stage_tail_shared_kernel(const __grid_constant__ StageArgs a,
+                                                                int64_t grid_pages) {
+  const int64_t row = blockIdx.x;
+  if (a.rows_bound > 0 && row >= a.rows_bound) return;
+  if (a.tail_rows[row] != row) return;
+  const int n = a.lens[row];
+  const RowBounds rb = row_bounds(n, static_cast<int>(a.sink), static_cast<int>(a.window));
+  const int count = rb.sink + n - rb.tail;
+  const int64_t need = min(grid_pages, static_cast<int64_t>(max((count + 63) / 64, 1)));
+  const int p0 = blockIdx.y * kStagePages;
+  const int p1 = static_cast<int>(min(need, static_cast<int64_t>(p0 + kStagePages)));
+  if (p0 >= p1) return;
+  const int chunks = (p1 - p0) * 512;
+  constexpr int U = 4;
+  for (int c0 = threadIdx.x; c0 < chunks; c0 += blockDim.x * U) {
+    uint4 v[U];
+    int64_t dst[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int c = c0 + u * blockDim.x;
+      v[u] = make_uint4(0, 0, 0, 0);
+      dst[u] = -1;
+      if (c < chunks) {
+        const int p = p0 + c / 512, tok = (c % 512) >> 3, part = c & 7;
+        const int i = p * 64 + tok;
+        if (i < count) {
+          const int logical = i < rb.sink ? i : rb.tail + i - rb.sink;
+          const int64_t page = a.nt[row * a.np + logical / 64];
+          v[u] = reinterpret_cast<const uint4*>(a.native + page * kPageBytes + (logical % 64) * 128)[part];
+        }
+        dst[u] = (a.cap + row * a.scratch + p) * kPageBytes + tok * 128 + part * 16;
       }
-      reinterpret_cast<uint4*>(a.fine + dst * kPageBytes + tok * 128)[part] = v;
     }
-    if (threadIdx.x < 64) {
-      const int tok = threadIdx.x;
-      const int i = p * 64 + tok;
-      float s = 0.0f;
-      if (i < count) {
-        const int logical = i < rb.sink ? i : rb.tail + i - rb.sink;
-        const int64_t page = a.nt[row * a.np + logical / 64];
-        s = a.nscale[page * kPageWords + kScaleWord + logical % 64];
-      }
-      a.fscale[dst * kPageWords + kScaleWord + tok] = s;
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (dst[u] >= 0) *reinterpret_cast<uint4*>(a.fine + dst[u]) = v[u];
+  }
+  for (int e = threadIdx.x; e < (p1 - p0) * 64; e += blockDim.x) {
+    const int p = p0 + e / 64, tok = e % 64;
+    const int i = p * 64 + tok;
+    float s = 0.0f;
+    if (i < count) {
+      const int logical = i < rb.sink ? i : rb.tail + i - rb.sink;
+      const int64_t page = a.nt[row * a.np + logical / 64];
+      s = a.nscale[page * kPageWords + kScaleWord + logical % 64];
     }
+    a.fscale[(a.cap + row * a.scratch + p) * kPageWords + kScaleWord + tok] = s;
   }
 }
 
@@ -286,8 +305,11 @@ extern "C" int v1x_stage_tail_shared(const uint8_t* native_bytes, const float* n
   if (grid_groups == 0 || grid_pages == 0) return V1X_OK;
   StageArgs a{native_bytes, native_scales, nt, lens, fine_bytes, fine_scales, tail_rows, cap, np,
               scratch, sink, window, rows_bound, group};
-  stage_tail_shared_kernel<<<dim3(static_cast<unsigned>(grid_groups), static_cast<unsigned>(grid_pages)),
-                             256, 0, as_stream(stream)>>>(a);
+  int64_t rows = grid_groups * group;
+  if (rows_bound > 0 && rows > rows_bound) rows = rows_bound;
+  if (rows <= 0) return V1X_OK;
+  const dim3 grid(static_cast<unsigned>(rows), static_cast<unsigned>((grid_pages + kStagePages - 1) / kStagePages));
+  stage_tail_shared_kernel<<<grid, 256, 0, as_stream(stream)>>>(a, grid_pages);
   return launch_status("v1x_stage_tail_shared");
 }
 

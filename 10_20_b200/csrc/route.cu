@@ -48,6 +48,8 @@ __device__ __forceinline__ void store_sel(const RouteArgs& a, int64_t i, int64_t
   else static_cast<int32_t*>(a.selected)[i] = static_cast<int32_t>(v);
 }
 
+// kPages: `scores` already holds one value per page (the max of its 8 centres).
+template <bool kPages>
 __global__ void __launch_bounds__(kRouteThreads) route_kernel(const __grid_constant__ RouteArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   RouteSmem& sm = *reinterpret_cast<RouteSmem*>(smem_raw);
@@ -69,13 +71,15 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const __grid_const
     return;
   }
   // ---- page keys in blocked-rank order (VQ:26-41) ----------------------------
-  const int act = static_cast<int>(min(static_cast<int64_t>(active), a.score_cols / 8));
+  const int act = static_cast<int>(min(static_cast<int64_t>(active), kPages ? a.score_cols : a.score_cols / 8));
   const float* srow = a.scores + row * a.score_stride;
   const bool vec = (reinterpret_cast<uintptr_t>(srow) & 15) == 0;
   for (int r = tid; r < a.n_items; r += nt) {
     const int p = r / a.base + (r % a.base) * 128;
     float best = -CUDART_INF_F;
-    if (p < act) {
+    if (kPages) {
+      if (p < act) best = srow[p];
+    } else if (p < act) {
       const float* s = srow + static_cast<int64_t>(p) * 8;
       if (vec) {
         const float4 x = reinterpret_cast<const float4*>(s)[0];
@@ -174,6 +178,36 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const __grid_const
 }  // namespace
 }  // namespace v1x
 
+namespace v1x {
+namespace {
+int route_launch(bool pages_in, const float* scores, int64_t score_stride, int64_t score_cols,
+                 const int32_t* lens, const int32_t* takes, void* selected, int selected_is_i64,
+                 int64_t take_stride, int64_t pages, const int32_t* rt, int32_t* ft, int64_t fine_pages,
+                 const int32_t* tail_rows, int64_t capacity, int fill_table, int64_t batch, void* stream) {
+  int threads, items;
+  if (pages <= 128) { threads = 64; items = 2; }
+  else if (pages <= 256) { threads = 64; items = 4; }
+  else if (pages <= 512) { threads = 64; items = 8; }
+  else if (pages <= 1024) { threads = 128; items = 8; }
+  else if (pages <= 2048) { threads = 128; items = 16; }
+  else { threads = 128; items = 32; }
+  const int n_items = threads * items;
+  RouteArgs a{scores, score_stride, score_cols, lens, takes, selected, selected_is_i64,
+              take_stride, static_cast<int>(pages), rt, ft, fine_pages, tail_rows, capacity,
+              fill_table, n_items, n_items / 128};
+  const size_t smem = sizeof(RouteSmem);
+  static DeviceOnce once;
+  if (once.first()) {
+    cudaFuncSetAttribute(route_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(route_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  }
+  if (pages_in) route_kernel<true><<<static_cast<unsigned>(batch), kRouteThreads, smem, as_stream(stream)>>>(a);
+  else route_kernel<false><<<static_cast<unsigned>(batch), kRouteThreads, smem, as_stream(stream)>>>(a);
+  return launch_status(pages_in ? "v1x_route_pages" : "v1x_route");
+}
+}  // namespace
+}  // namespace v1x
+
 extern "C" int v1x_route(const float* scores, int64_t score_stride, int64_t score_cols,
                          const int32_t* lens, const int32_t* takes, void* selected,
                          int selected_is_i64, int64_t take_stride, int64_t pages,
@@ -189,21 +223,22 @@ extern "C" int v1x_route(const float* scores, int64_t score_stride, int64_t scor
   V1X_CHECK_ARG(batch >= 0 && take_stride >= 0 && score_stride >= score_cols,
                 "route: bad batch / strides");
   if (batch == 0) return V1X_OK;
-  int threads, items;
-  if (pages <= 128) { threads = 64; items = 2; }
-  else if (pages <= 256) { threads = 64; items = 4; }
-  else if (pages <= 512) { threads = 64; items = 8; }
-  else if (pages <= 1024) { threads = 128; items = 8; }
-  else if (pages <= 2048) { threads = 128; items = 16; }
-  else { threads = 128; items = 32; }
-  const int n_items = threads * items;
-  RouteArgs a{scores, score_stride, score_cols, lens, takes, selected, selected_is_i64,
-              take_stride, static_cast<int>(pages), rt, ft, fine_pages, tail_rows, capacity,
-              fill_table, n_items, n_items / 128};
-  const size_t smem = sizeof(RouteSmem);
-  static DeviceOnce once;
-  if (once.first())
-    cudaFuncSetAttribute(route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  route_kernel<<<static_cast<unsigned>(batch), kRouteThreads, smem, as_stream(stream)>>>(a);
-  return launch_status("v1x_route");
+  return route_launch(false, scores, score_stride, score_cols, lens, takes, selected, selected_is_i64,
+                      take_stride, pages, rt, ft, fine_pages, tail_rows, capacity, fill_table, batch, stream);
+}
+
+extern "C" int v1x_route_pages(const float* page_scores, int64_t page_stride, const int32_t* lens,
+                               const int32_t* takes, void* selected, int selected_is_i64,
+                               int64_t take_stride, int64_t pages, const int32_t* rt, int32_t* ft,
+                               int64_t fine_pages, const int32_t* tail_rows, int64_t capacity,
+                               int fill_table, int64_t batch, void* stream) {
+  using namespace v1x;
+  clear_error();
+  V1X_CHECK_ARG(capacity > 0 && fine_pages >= take_stride, "Invalid fine page table");
+  V1X_CHECK_ARG(pages >= 64 && pages <= 4096 && page_stride >= pages && take_stride <= pages,
+                "Invalid V1 route capacity");
+  V1X_CHECK_ARG(batch >= 0 && take_stride >= 0, "route: bad batch / strides");
+  if (batch == 0) return V1X_OK;
+  return route_launch(true, page_scores, page_stride, page_stride, lens, takes, selected, selected_is_i64,
+                      take_stride, pages, rt, ft, fine_pages, tail_rows, capacity, fill_table, batch, stream);
 }

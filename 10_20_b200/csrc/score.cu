@@ -31,6 +31,8 @@ struct ScoreArgs {
   int64_t table_stride;
   float* out;
   int64_t out_stride, max_len;
+  float* page_max;
+  int64_t page_stride;
   int heads, relu, clean;
 };
 
@@ -53,11 +55,9 @@ __global__ void __launch_bounds__(kScoreThreads) score_simt_kernel(const __grid_
   for (int h = threadIdx.x; h < H; h += blockDim.x) ws[h] = a.w[b * H + h];
   __syncthreads();
   const int64_t j = static_cast<int64_t>(blockIdx.y) * blockDim.x + threadIdx.x;
-  if (j >= a.max_len) return;
   const int n = a.lens[b];
-  if (j >= n && !a.clean) return;
   float result = -CUDART_INF_F;
-  if (j < n) {
+  if (j < n && j < a.max_len) {
     const int64_t page = a.table[b * a.table_stride + j / 64];
     const uint8_t* kp = a.pool + page * kPageBytes + (j % 64) * 128;
     uint4 kw[8];
@@ -87,6 +87,14 @@ __global__ void __launch_bounds__(kScoreThreads) score_simt_kernel(const __grid_
     }
     result = __fmul_rn(acc, scale);
   }
+  if (a.page_max) {  // max over each group of 8 consecutive keys (lanes 8k..8k+7)
+    float m = result;
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+    if ((threadIdx.x & 7) == 0 && j < a.max_len) a.page_max[b * a.page_stride + j / 8] = m;
+  }
+  if (j >= a.max_len || !a.out || (j >= n && !a.clean)) return;
   a.out[b * a.out_stride + j] = result;
 }
 
@@ -94,31 +102,34 @@ __global__ void __launch_bounds__(kScoreThreads) score_simt_kernel(const __grid_
 
 int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages, const int32_t* lens,
                  const int32_t* table, int64_t table_stride, float* out, int64_t out_stride, int64_t max_len,
-                 int64_t heads, int relu, int clean, int64_t batch, int32_t* status, cudaStream_t stream);
+                 float* page_max, int64_t page_stride, int64_t heads, int relu, int clean, int64_t batch,
+                 int32_t* status, cudaStream_t stream);
 }  // namespace v1x
 
 extern "C" int v1x_score_fp8(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages,
                              const int32_t* lens, const int32_t* table, int64_t table_stride,
-                             float* out, int64_t out_stride, int64_t max_len, int64_t heads,
-                             int relu, int clean, int impl, int32_t* status, int64_t batch,
-                             void* stream) {
+                             float* out, int64_t out_stride, int64_t max_len, float* page_max,
+                             int64_t page_stride, int64_t heads, int relu, int clean, int impl,
+                             int32_t* status, int64_t batch, void* stream) {
   using namespace v1x;
   clear_error();
   V1X_CHECK_ARG(heads >= 1 && heads <= 256, "score_fp8: heads must be in [1, 256]");
-  V1X_CHECK_ARG(batch >= 0 && max_len >= 0 && out_stride >= max_len && pool_pages > 0,
-                "score_fp8: bad geometry");
+  V1X_CHECK_ARG(batch >= 0 && max_len >= 0 && pool_pages > 0, "score_fp8: bad geometry");
+  V1X_CHECK_ARG(!out || out_stride >= max_len, "score_fp8: out row stride < max_len");
+  V1X_CHECK_ARG(!page_max || page_stride * 8 >= max_len, "score_fp8: page_max row stride < max_len / 8");
+  V1X_CHECK_ARG(out || page_max, "score_fp8: no output requested");
   V1X_CHECK_ARG((reinterpret_cast<uintptr_t>(pool) & 15) == 0, "score_fp8: pool must be 16-byte aligned");
   V1X_CHECK_ARG(table_stride >= 0 && impl >= 0 && impl <= 2, "score_fp8: bad table stride / impl");
   if (batch == 0 || max_len == 0) return V1X_OK;
   const bool tc = impl == 2 || (impl == 0 && heads % 32 == 0);
   if (tc)
-    return score_fp8_tc(q, w, pool, pool_pages, lens, table, table_stride, out, out_stride, max_len, heads,
-                        relu, clean, batch, status, as_stream(stream));
+    return score_fp8_tc(q, w, pool, pool_pages, lens, table, table_stride, out, out_stride, max_len, page_max,
+                        page_stride, heads, relu, clean, batch, status, as_stream(stream));
   if (heads > kSimtMaxHeads) {
     set_error("score_fp8: the SIMT path takes heads <= %d", kSimtMaxHeads);
     return V1X_ERR_UNSUPPORTED;
   }
-  ScoreArgs a{q, w, pool, lens, table, table_stride, out, out_stride, max_len,
+  ScoreArgs a{q, w, pool, lens, table, table_stride, out, out_stride, max_len, page_max, page_stride,
               static_cast<int>(heads), relu, clean};
   const dim3 grid(static_cast<unsigned>(batch), static_cast<unsigned>((max_len + kScoreThreads - 1) / kScoreThreads));
   score_simt_kernel<<<grid, kScoreThreads, 0, as_stream(stream)>>>(a);

@@ -34,7 +34,9 @@ namespace {
 using namespace sm100;
 
 constexpr int kTcThreads = 192;
-constexpr int kTcStages = 4;
+constexpr int kTcStages = 4;     // key/q smem stages
+constexpr int kScaleSlots = 8;   // per-tile key scales (2 x 256 B), consumed by the epilogue
+constexpr int kMaxAcc = 4;       // TMEM accumulators
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 constexpr int kMaxTcRows = 8192;
 
@@ -43,16 +45,19 @@ struct TcArgs {
   const int32_t* table;
   int64_t table_stride;
   const float* w;
-  const uint8_t* pool;
   float* out;
   int64_t out_stride, max_len;
-  int B, H, relu, clean;
+  float* page_max;
+  int64_t page_stride;
+  int B, H, relu, clean, nacc;
   uint32_t tmem_cols;
   int32_t* status;
 };
 
 struct TcShared {
-  uint64_t full[kTcStages], empty[kTcStages], tfull[2], tempty[2];
+  uint64_t full[kTcStages], empty[kTcStages];
+  uint64_t sfull[kScaleSlots], sempty[kScaleSlots];
+  uint64_t tfull[kMaxAcc], tempty[kMaxAcc];
   uint32_t tmem_base;
   int abort;
   int zero;  // always 0: lets drain waits ignore the abort flag
@@ -75,16 +80,21 @@ __device__ __forceinline__ void raise_abort(TcShared& sh, int32_t* status) {
   if (status) atomicExch(status, V1X_STATUS_TIMEOUT);
 }
 
+__device__ __forceinline__ int64_t row_eff(const TcArgs& a, int b) {
+  return min(static_cast<int64_t>(a.lens[b]), a.max_len);
+}
+
 __global__ void __launch_bounds__(kTcThreads, 1)
     score_tc_kernel(const __grid_constant__ CUtensorMap pool_map, const __grid_constant__ CUtensorMap q_map,
-                    const __grid_constant__ TcArgs a) {
+                    const __grid_constant__ CUtensorMap scale_map, const __grid_constant__ TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const uint32_t b_bytes = static_cast<uint32_t>(a.H) * 128;
-  const uint32_t stage_bytes = 16384 + b_bytes;
-  TcShared& sh = *reinterpret_cast<TcShared*>(base + kTcStages * stage_bytes);
+  const uint32_t stage_bytes = 16384 + static_cast<uint32_t>(a.H) * 128;
+  float* scales = reinterpret_cast<float*>(base + kTcStages * stage_bytes);   // [kScaleSlots][128]
+  TcShared& sh = *reinterpret_cast<TcShared*>(reinterpret_cast<uint8_t*>(scales) + kScaleSlots * 512);
   int* prefix = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(&sh) + sizeof(TcShared));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nacc = a.nacc;
 
   // ---- per-row tile prefix ----------------------------------------------------
   {
@@ -92,14 +102,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int beg = min(tid * chunk, a.B), end = min(beg + chunk, a.B);
     int local = 0;
     for (int b = beg; b < end; ++b) {
-      const int64_t eff = min(static_cast<int64_t>(a.lens[b]), a.max_len);
+      const int64_t eff = row_eff(a, b);
       local += eff > 0 ? static_cast<int>((eff + 127) / 128) : 0;
     }
     int tot;
     int run = block_exclusive_scan(local, sh.warp_tot, &tot);
     for (int b = beg; b < end; ++b) {
       prefix[b] = run;
-      const int64_t eff = min(static_cast<int64_t>(a.lens[b]), a.max_len);
+      const int64_t eff = row_eff(a, b);
       run += eff > 0 ? static_cast<int>((eff + 127) / 128) : 0;
     }
     if (tid == 0) {
@@ -111,7 +121,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         mbar_init(&sh.full[s], 1);
         mbar_init(&sh.empty[s], 1);
       }
-      for (int c = 0; c < 2; ++c) {
+      for (int r = 0; r < kScaleSlots; ++r) {
+        mbar_init(&sh.sfull[r], 1);
+        mbar_init(&sh.sempty[r], 128);
+      }
+      for (int c = 0; c < kMaxAcc; ++c) {
         mbar_init(&sh.tfull[c], 1);
         mbar_init(&sh.tempty[c], 128);
       }
@@ -126,6 +140,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&pool_map);
     tma_prefetch_desc(&q_map);
+    tma_prefetch_desc(&scale_map);
   }
   __syncthreads();
   tc_fence_after();
@@ -134,29 +149,59 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int G = gridDim.x;
 
   if (warp == 0) {
-    // ---------------- TMA producer ----------------
-    if (lane == 0) {
-      int it = 0;
-      for (int T = blockIdx.x; T < total; T += G, ++it) {
-        const int s = it % kTcStages;
-        const uint32_t ph = (it / kTcStages) & 1;
-        if (!mbar_wait(&sh.empty[s], ph ^ 1, &sh.abort, kWaitLimitNs)) { raise_abort(sh, a.status); break; }
-        const int b = locate_row(prefix, a.B, T);
-        const int t = T - prefix[b];
-        const int64_t eff = min(static_cast<int64_t>(a.lens[b]), a.max_len);
-        const int p0 = a.table[b * a.table_stride + 2 * t];
-        const int p1 = (static_cast<int64_t>(2 * t + 1) * 64 < eff) ? a.table[b * a.table_stride + 2 * t + 1] : p0;
-        uint8_t* st = base + s * stage_bytes;
-        mbar_arrive_expect_tx(&sh.full[s], stage_bytes);
-        tma_load_3d(st, &pool_map, &sh.full[s], 0, 0, p0);
-        tma_load_3d(st + 8192, &pool_map, &sh.full[s], 0, 0, p1);
-        tma_load_2d(st + 16384, &q_map, &sh.full[s], 0, b * a.H);
+    // ---------------- TMA producer (whole warp resolves page ids 32 tiles at a time) ----------------
+    int it = 0, issued_keys = 0, issued_scales = 0;
+    bool stop = false;
+    for (int c = 0; !stop; c += 32) {
+      const int Tl = blockIdx.x + (c + lane) * G;
+      const bool valid = Tl < total;
+      int bl = 0, p0l = 0, p1l = 0;
+      if (valid) {
+        bl = locate_row(prefix, a.B, Tl);
+        const int t = Tl - prefix[bl];
+        const int64_t eff = row_eff(a, bl);
+        p0l = a.table[bl * a.table_stride + 2 * t];
+        p1l = (static_cast<int64_t>(2 * t + 1) * 64 < eff) ? a.table[bl * a.table_stride + 2 * t + 1] : p0l;
       }
-      if (*reinterpret_cast<volatile int*>(&sh.abort)) {  // drain the loads this thread issued
-        const int issued = it;
-        for (int k = max(0, issued - kTcStages); k < issued; ++k)
-          mbar_wait(&sh.full[k % kTcStages], (k / kTcStages) & 1, &sh.zero, kWaitLimitNs);
+      const int n = __popc(__ballot_sync(0xffffffffu, valid));
+      for (int j = 0; j < n; ++j, ++it) {
+        const int b = __shfl_sync(0xffffffffu, bl, j);
+        const int p0 = __shfl_sync(0xffffffffu, p0l, j);
+        const int p1 = __shfl_sync(0xffffffffu, p1l, j);
+        int ok = 1;
+        if (lane == 0) {
+          const int s = it % kTcStages;
+          ok = mbar_wait(&sh.empty[s], ((it / kTcStages) & 1) ^ 1, &sh.abort, kWaitLimitNs);
+          if (ok) {
+            uint8_t* st = base + s * stage_bytes;
+            mbar_arrive_expect_tx(&sh.full[s], stage_bytes);
+            tma_load_3d(st, &pool_map, &sh.full[s], 0, 0, p0);
+            tma_load_3d(st + 8192, &pool_map, &sh.full[s], 0, 0, p1);
+            tma_load_2d(st + 16384, &q_map, &sh.full[s], 0, b * a.H);
+            ++issued_keys;
+            const int r = it % kScaleSlots;
+            ok = mbar_wait(&sh.sempty[r], ((it / kScaleSlots) & 1) ^ 1, &sh.abort, kWaitLimitNs);
+            if (ok) {
+              mbar_arrive_expect_tx(&sh.sfull[r], 512);
+              tma_load_2d(scales + r * 128, &scale_map, &sh.sfull[r], 0, p0);
+              tma_load_2d(scales + r * 128 + 64, &scale_map, &sh.sfull[r], 0, p1);
+              ++issued_scales;
+            }
+          }
+          if (!ok) raise_abort(sh, a.status);
+        }
+        if (!__shfl_sync(0xffffffffu, ok, 0)) {
+          stop = true;
+          break;
+        }
       }
+      if (n < 32) break;
+    }
+    if (lane == 0 && *reinterpret_cast<volatile int*>(&sh.abort)) {  // drain what this thread issued
+      for (int k = max(0, issued_keys - kTcStages); k < issued_keys; ++k)
+        mbar_wait(&sh.full[k % kTcStages], (k / kTcStages) & 1, &sh.zero, kWaitLimitNs);
+      for (int k = max(0, issued_scales - kScaleSlots); k < issued_scales; ++k)
+        mbar_wait(&sh.sfull[k % kScaleSlots], (k / kScaleSlots) & 1, &sh.zero, kWaitLimitNs);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -165,11 +210,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       int it = 0;
       for (int T = blockIdx.x; T < total; T += G, ++it) {
         const int s = it % kTcStages;
-        const uint32_t ph = (it / kTcStages) & 1;
-        const int acc = it & 1;
-        const uint32_t aph = (it >> 1) & 1;
-        if (!mbar_wait(&sh.tempty[acc], aph ^ 1, &sh.abort, kWaitLimitNs)) { raise_abort(sh, a.status); break; }
-        if (!mbar_wait(&sh.full[s], ph, &sh.abort, kWaitLimitNs)) { raise_abort(sh, a.status); break; }
+        const int acc = it % nacc;
+        if (!mbar_wait(&sh.tempty[acc], ((it / nacc) & 1) ^ 1, &sh.abort, kWaitLimitNs)) { raise_abort(sh, a.status); break; }
+        if (!mbar_wait(&sh.full[s], (it / kTcStages) & 1, &sh.abort, kWaitLimitNs)) { raise_abort(sh, a.status); break; }
         tc_fence_after();
         const uint32_t sa = smem_u32(base + s * stage_bytes);
         const uint32_t sb = sa + 16384;
@@ -182,40 +225,34 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       if (*reinterpret_cast<volatile int*>(&sh.abort) && it > 0) {  // let issued MMAs retire
         const int k = it - 1;
-        mbar_wait(&sh.tfull[k & 1], (k >> 1) & 1, &sh.zero, kWaitLimitNs);
+        mbar_wait(&sh.tfull[k % nacc], (k / nacc) & 1, &sh.zero, kWaitLimitNs);
       }
     }
   } else {
-    // ---------------- epilogue (warps 2..5) ----------------
+    // ---------------- epilogue (warps 2..5): one key per thread ----------------
     const int q4 = warp & 3;
     const int i = q4 * 32 + lane;
-    const float* poolf = reinterpret_cast<const float*>(a.pool);
     int it = 0;
     for (int T = blockIdx.x; T < total; T += G, ++it) {
-      const int acc = it & 1;
-      const uint32_t aph = (it >> 1) & 1;
+      const int acc = it % nacc;
+      const int r = it % kScaleSlots;
       const int b = locate_row(prefix, a.B, T);
       const int t = T - prefix[b];
-      const int64_t eff = min(static_cast<int64_t>(a.lens[b]), a.max_len);
+      const int64_t eff = row_eff(a, b);
       const int64_t key = static_cast<int64_t>(t) * 128 + i;
-      float scale = 0.0f;
-      if (key < eff) {
-        const int64_t page = a.table[b * a.table_stride + (key >> 6)];
-        scale = __ldg(poolf + page * kPageWords + kScaleWord + (key & 63));
-      }
-      if (!mbar_wait(&sh.tfull[acc], aph, &sh.abort, kWaitLimitNs)) { raise_abort(sh, a.status); break; }
+      if (!mbar_wait(&sh.tfull[acc], (it / nacc) & 1, &sh.abort, kWaitLimitNs)) { raise_abort(sh, a.status); break; }
       tc_fence_after();
       float sum = 0.0f;
       const float* wr = a.w + static_cast<int64_t>(b) * a.H;
       for (int c0 = 0; c0 < a.H; c0 += 32) {
-        uint32_t r[32];
-        tmem_ld32(tmem + (static_cast<uint32_t>(q4 * 32) << 16) + static_cast<uint32_t>(acc * a.H + c0), r);
+        uint32_t v[32];
+        tmem_ld32(tmem + (static_cast<uint32_t>(q4 * 32) << 16) + static_cast<uint32_t>(acc * a.H + c0), v);
         tmem_ld_wait();
 #pragma unroll
         for (int j = 0; j < 32; j += 4) {
           const float4 w4 = __ldg(reinterpret_cast<const float4*>(wr + c0 + j));
-          float v0 = __uint_as_float(r[j]), v1 = __uint_as_float(r[j + 1]);
-          float v2 = __uint_as_float(r[j + 2]), v3 = __uint_as_float(r[j + 3]);
+          float v0 = __uint_as_float(v[j]), v1 = __uint_as_float(v[j + 1]);
+          float v2 = __uint_as_float(v[j + 2]), v3 = __uint_as_float(v[j + 3]);
           if (a.relu) {
             v0 = fmaxf(v0, 0.0f); v1 = fmaxf(v1, 0.0f); v2 = fmaxf(v2, 0.0f); v3 = fmaxf(v3, 0.0f);
           }
@@ -227,13 +264,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(&sh.tempty[acc]);
-      if (key < a.max_len && (key < eff || a.clean))
-        a.out[b * a.out_stride + key] = key < eff ? sum * scale : -CUDART_INF_F;
+      if (!mbar_wait(&sh.sfull[r], (it / kScaleSlots) & 1, &sh.abort, kWaitLimitNs)) { raise_abort(sh, a.status); break; }
+      const float scale = scales[r * 128 + i];
+      mbar_arrive(&sh.sempty[r]);
+      const float score = key < eff ? sum * scale : -CUDART_INF_F;
+      if (a.out && key < a.max_len && (key < eff || a.clean)) a.out[b * a.out_stride + key] = score;
+      if (a.page_max) {
+        float m = score;
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+        if ((lane & 7) == 0 && key < a.max_len) a.page_max[b * a.page_stride + (key >> 3)] = m;
+      }
     }
-    if (a.clean) {
+    if (a.clean && a.out) {
       const int e = tid - 64;
       for (int b = blockIdx.x; b < a.B; b += G) {
-        const int64_t eff = min(static_cast<int64_t>(a.lens[b]), a.max_len);
+        const int64_t eff = row_eff(a, b);
         const int64_t start = eff > 0 ? (eff + 127) / 128 * 128 : 0;
         for (int64_t j = start + e; j < a.max_len; j += 128) a.out[b * a.out_stride + j] = -CUDART_INF_F;
       }
@@ -263,7 +310,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 // Launch the tensor-core scorer; returns V1X_ERR_UNSUPPORTED if the shape is not covered.
 int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages, const int32_t* lens,
                  const int32_t* table, int64_t table_stride, float* out, int64_t out_stride, int64_t max_len,
-                 int64_t heads, int relu, int clean, int64_t batch, int32_t* status, cudaStream_t stream) {
+                 float* page_max, int64_t page_stride, int64_t heads, int relu, int clean, int64_t batch,
+                 int32_t* status, cudaStream_t stream) {
   if (heads % 32 != 0 || heads > 256 || batch > kMaxTcRows || pool_pages >= (int64_t(1) << 31)) {
     set_error("score_fp8 (tensor core): heads must be a multiple of 32 <= 256 and batch <= %d", kMaxTcRows);
     return V1X_ERR_UNSUPPORTED;
@@ -277,7 +325,7 @@ int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t 
     set_error("score_fp8: cuTensorMapEncodeTiled unavailable");
     return V1X_ERR_CUDA;
   }
-  CUtensorMap pool_map, q_map;
+  CUtensorMap pool_map, q_map, scale_map;
   {
     cuuint64_t dims[3] = {128, 64, static_cast<cuuint64_t>(pool_pages)};
     cuuint64_t strides[2] = {128, static_cast<cuuint64_t>(kPageBytes)};
@@ -304,11 +352,27 @@ int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t 
       return V1X_ERR_CUDA;
     }
   }
+  {
+    // the 64 fp32 scales of each page: 256 contiguous bytes at page + 8192
+    cuuint64_t dims[2] = {64, static_cast<cuuint64_t>(pool_pages)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(kPageBytes)};
+    cuuint32_t box[2] = {64, 1};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = enc(&scale_map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<uint8_t*>(pool) + kKeyBytes, dims,
+                     strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                     CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+      set_error("score_fp8: scale tensor map encode failed (%d)", static_cast<int>(r));
+      return V1X_ERR_CUDA;
+    }
+  }
+  const int nacc = 4 * heads <= 256 ? 4 : 2;
   uint32_t cols = 32;
-  while (cols < static_cast<uint32_t>(2 * heads)) cols <<= 1;
-  TcArgs args{lens, table, table_stride, w, pool, out, out_stride, max_len, static_cast<int>(batch),
-              static_cast<int>(heads), relu, clean, cols, status};
-  const size_t smem = 1024 + kTcStages * (16384 + heads * 128) + sizeof(TcShared) + (batch + 1) * 4 + 16;
+  while (cols < static_cast<uint32_t>(nacc * heads)) cols <<= 1;
+  TcArgs args{lens, table, table_stride, w, out, out_stride, max_len, page_max, page_stride,
+              static_cast<int>(batch), static_cast<int>(heads), relu, clean, nacc, cols, status};
+  const size_t smem = 1024 + kTcStages * (16384 + heads * 128) + kScaleSlots * 512 + sizeof(TcShared) +
+                      (batch + 1) * 4 + 16;
   static DeviceOnce once;
   if (once.first())
     cudaFuncSetAttribute(score_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
@@ -317,9 +381,10 @@ int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t 
     return V1X_ERR_UNSUPPORTED;
   }
   const int64_t max_tiles = batch * ((max_len + 127) / 128);
-  int64_t grid = static_cast<int64_t>(num_sms()) * (cols <= 256 ? 2 : 1);
+  const int per_sm = (cols <= 256 && smem <= 113 * 1024) ? 2 : 1;
+  int64_t grid = static_cast<int64_t>(num_sms()) * per_sm;
   if (grid > max_tiles) grid = max_tiles > 0 ? max_tiles : 1;
-  score_tc_kernel<<<static_cast<unsigned>(grid), kTcThreads, smem, stream>>>(pool_map, q_map, args);
+  score_tc_kernel<<<static_cast<unsigned>(grid), kTcThreads, smem, stream>>>(pool_map, q_map, scale_map, args);
   return launch_status("v1x_score_fp8 (tensor core)");
 }
 

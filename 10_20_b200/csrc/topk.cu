@@ -13,6 +13,8 @@
 // histogram atomics) find the exact T-th key and how many of its ties to keep;
 // two block scans then place every selected candidate at its output slot in
 // index order, and the selecting thread performs the mapping epilogue itself.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace v1x {
@@ -51,25 +53,40 @@ struct TopkArgs {
 struct RowCtx {
   int64_t row;
   int n, take, sink, tail, L;
-  const float* s;
 };
 
+constexpr int kPageCache = 256;   // page ids of the first 256 selected ranks, cached in smem
+
+struct TopkSmem {
+  int hist[256];
+  int warp_tot[kTopkThreads / 32 + 1];
+  int digit, need;
+  int pgc[kPageCache];
+};
+
+// Page holding raw candidate r*64+x (r < take): the fine table's entry (direct)
+// or the reordered page of the r-th selected rank (VQ:124-132).
+__device__ __forceinline__ int64_t page_of_rank(const TopkArgs& a, const RowCtx& c, int r) {
+  int64_t page = -1;
+  if (a.direct_fine) {
+    if (r < a.fine_table_cols) page = a.fine_table[c.row * a.fine_table_cols + r];
+  } else if (r < a.take_stride) {
+    const int64_t rank = load_index(a.selected, a.sel64, c.row * a.take_stride + r);
+    if (rank >= 0 && rank < a.pages) page = a.rt[c.row * a.pages + rank];
+  }
+  return page;
+}
+
 // Mapping epilogue for one output slot (VQ:121-148).
-__device__ __forceinline__ void emit_slot(const TopkArgs& a, const RowCtx& c, int slot, int raw,
-                                          bool finite) {
+__device__ __forceinline__ void emit_slot(const TopkArgs& a, const RowCtx& c, const TopkSmem& sm, int slot,
+                                          int raw, bool finite) {
   int logical = -1, physical = -1;
   if (raw >= 0 && raw < c.L && finite) {
     int lg = -1;
     bool ok = true;
     if (raw < c.take * 64) {
-      int64_t page = -1;
       const int r = raw >> 6;
-      if (a.direct_fine) {
-        if (r < a.fine_table_cols) page = a.fine_table[c.row * a.fine_table_cols + r];
-      } else if (r < a.take_stride) {
-        const int64_t rank = load_index(a.selected, a.sel64, c.row * a.take_stride + r);
-        if (rank >= 0 && rank < a.pages) page = a.rt[c.row * a.pages + rank];
-      }
+      const int64_t page = r < kPageCache ? sm.pgc[r] : page_of_rank(a, c, r);
       ok = page >= 0 && page < a.member_rows;
       if (ok) lg = a.members[page * 64 + (raw & 63)];
     } else {
@@ -97,46 +114,51 @@ __device__ __forceinline__ void emit_slot(const TopkArgs& a, const RowCtx& c, in
   }
 }
 
-// In-place -inf mask of boundary-bucket members (VQ:71-107): one warp per
-// selected page rank r < take; interior buckets are skipped after one lookup.
-__device__ void apply_mask(const TopkArgs& a, const RowCtx& c, float* srow) {
+// One warp per selected rank r < take: cache the rank's page for the epilogue
+// and, when masking, -inf the members of boundary buckets that fall outside
+// [sink, tail) (VQ:71-107) -- in global memory (the reference mutates `scores`)
+// and in the smem bitmap that the staged keys are built from.
+__device__ void ranks_and_mask(const TopkArgs& a, const RowCtx& c, float* srow, TopkSmem& sm, uint32_t* bitmap) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   for (int r = warp; r < c.take; r += nw) {
-    int64_t rank = -1;
+    int64_t rank = -1, rpage = -1, epage = -1;
     int bucket = 0;
     if (lane == 0) {
       if (r < a.take_stride) rank = load_index(a.selected, a.sel64, c.row * a.take_stride + r);
-      if (rank >= 0 && rank < a.pages) {
-        if (a.bucket_from_rank) {
-          bucket = static_cast<int>(rank / 16) * 1024;
-        } else {
-          const int64_t page = a.rt[c.row * a.pages + rank];
-          bucket = (page >= 0 && page < a.member_rows) ? (a.members[page * 64] / 1024) * 1024 : 0;
-        }
+      if (rank >= 0 && rank < a.pages) rpage = a.rt[c.row * a.pages + rank];
+      epage = a.direct_fine ? (r < a.fine_table_cols ? a.fine_table[c.row * a.fine_table_cols + r] : -1) : rpage;
+      if (r < kPageCache) sm.pgc[r] = static_cast<int>(epage);
+      if (a.mask && rank >= 0 && rank < a.pages) {
+        if (a.bucket_from_rank) bucket = static_cast<int>(rank / 16) * 1024;
+        else bucket = (rpage >= 0 && rpage < a.member_rows) ? (a.members[rpage * 64] / 1024) * 1024 : 0;
       }
     }
+    if (!a.mask) continue;
     rank = __shfl_sync(0xffffffffu, rank, 0);
+    rpage = __shfl_sync(0xffffffffu, rpage, 0);
     bucket = __shfl_sync(0xffffffffu, bucket, 0);
-    if (rank < 0 || rank >= a.pages) continue;
+    if (rank < 0 || rank >= a.pages || rpage < 0 || rpage >= a.member_rows) continue;
     if (bucket < c.sink || bucket + 1024 > c.tail) {
-      const int64_t page = a.rt[c.row * a.pages + rank];
-      if (page < 0 || page >= a.member_rows) continue;
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
         const int off = lane + i * 32;
-        const int lg = a.members[page * 64 + off];
+        const int lg = a.members[rpage * 64 + off];
         const int64_t col = static_cast<int64_t>(r) * 64 + off;
-        if ((lg < c.sink || lg >= c.tail) && col < a.cols) srow[col] = -CUDART_INF_F;
+        const bool bad = (lg < c.sink || lg >= c.tail) && col < a.cols;
+        if (bad) {
+          srow[col] = -CUDART_INF_F;
+          if (bitmap) atomicOr(&bitmap[col >> 5], 1u << (col & 31));
+        }
       }
     }
   }
 }
 
-struct TopkSmem {
-  int hist[256];
-  int warp_tot[kTopkThreads / 32 + 1];
-  int digit, need;
-};
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
+               "l"(gsrc)
+               : "memory");
+}
 
 template <bool kStaged>
 __device__ __forceinline__ uint32_t key_at(const uint32_t* keys, const float* srow, int i) {
@@ -159,29 +181,38 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(const __grid_constan
   c.tail = rb.tail;
   c.L = static_cast<int>(min(static_cast<int64_t>(max(a.fine_lens[c.row], 0)), a.cols));
   float* srow = a.scores + c.row * a.score_stride;
-  c.s = srow;
+  const bool select = c.L > a.topk;
+  // staged path: bitmap of masked columns after the keys (words for take*64 columns)
+  const int bm_words = kStaged ? static_cast<int>((min(static_cast<int64_t>(max(c.take, 0)) * 64, a.cols) + 31) / 32) : 0;
+  uint32_t* bitmap = kStaged && select && a.mask ? keys + ((a.cols + 3) & ~int64_t(3)) : nullptr;
+  const bool vec = (reinterpret_cast<uintptr_t>(srow) & 15) == 0;
+  const int nv = (kStaged && select && vec) ? c.L >> 2 : 0;
+  // 1. start the asynchronous copy of the row's scores into shared memory
+  for (int v = tid; v < nv; v += nt) cp_async16(keys + 4 * v, srow + 4 * v);
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  if (bitmap)
+    for (int w = tid; w < bm_words; w += nt) bitmap[w] = 0u;
+  __syncthreads();
+  // 2. page ids of the selected ranks + boundary mask, overlapping the copy
+  ranks_and_mask(a, c, srow, sm, bitmap);
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncthreads();
 
-  if (a.mask) {
-    apply_mask(a, c, srow);
-    __syncthreads();
-  }
-
-  if (c.L <= a.topk) {
+  if (!select) {
     for (int t = tid; t < a.topk; t += nt) {
       const int raw = t < c.L ? t : -1;
       const bool fin = raw >= 0 && srow[raw] != -CUDART_INF_F;
-      emit_slot(a, c, t, raw, fin);
+      emit_slot(a, c, sm, t, raw, fin);
     }
   } else {
     if constexpr (kStaged) {
-      const bool vec = (reinterpret_cast<uintptr_t>(srow) & 15) == 0;
-      const int nv = vec ? c.L >> 2 : 0;
-      for (int v = tid; v < nv; v += nt) {
-        const float4 x = reinterpret_cast<const float4*>(srow)[v];
-        reinterpret_cast<uint4*>(keys)[v] =
-            make_uint4(order_key(x.x), order_key(x.y), order_key(x.z), order_key(x.w));
+      // 3. floats -> order keys in place, masked columns -> -inf
+      for (int i = tid; i < c.L; i += nt) {
+        const float x = i < nv * 4 ? __uint_as_float(keys[i]) : srow[i];
+        const bool masked = bitmap && i < bm_words * 32 && ((bitmap[i >> 5] >> (i & 31)) & 1u);
+        keys[i] = masked ? kNegInfKey : order_key(x);
       }
-      for (int i = nv * 4 + tid; i < c.L; i += nt) keys[i] = order_key(srow[i]);
+      __syncthreads();
     }
     // ---- exact radix select of the T-th largest key --------------------------
     uint32_t prefix = 0, known = 0;
@@ -198,8 +229,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(const __grid_constan
           const uint32_t k = key_at<kStaged>(keys, srow, i);
           if ((k & known) == prefix) bin = (k >> shift) & 255;
         }
-        const unsigned act = __activemask();
-        const unsigned same = __match_any_sync(act, bin);
+        const unsigned same = __match_any_sync(0xffffffffu, bin);
         if (bin >= 0 && lane == __ffs(same) - 1) atomicAdd(&sm.hist[bin], __popc(same));
       }
       __syncthreads();
@@ -248,7 +278,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(const __grid_constan
         sel = eq_seen < need;
         ++eq_seen;
       }
-      if (sel && pos < a.topk) emit_slot(a, c, pos++, i, k != kNegInfKey);
+      if (sel && pos < a.topk) emit_slot(a, c, sm, pos++, i, k != kNegInfKey);
     }
   }
   if (a.expansion_stride) {
@@ -285,13 +315,15 @@ extern "C" int v1x_topk(float* scores, int64_t score_stride, int64_t cols, const
              static_cast<int>(topk), static_cast<int>(window), mask, expanded, expansion_stride,
              physical_output, bucket_from_rank, fine_table, fine_table_cols, direct_fine};
   cudaStream_t s = as_stream(stream);
+  V1X_CHECK_ARG(take_stride <= 65536, "topk: take stride too large");
   if (cols <= kTopkMaxSmemKeys) {
-    const size_t smem = static_cast<size_t>(cols > 0 ? cols : 1) * 4;
+    const int64_t bm = (std::min<int64_t>(take_stride * 64, cols) + 31) / 32;
+    const size_t smem = static_cast<size_t>(((cols + 3) & ~int64_t(3)) + bm + 1) * 4;
     if (smem > 48 * 1024) {
       static DeviceOnce once;
       if (once.first()) {
         cudaFuncSetAttribute(topk_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kTopkMaxSmemKeys * 4);
+                             kTopkMaxSmemKeys * 4 + 8192 * 4 + 16);
       }
     }
     topk_kernel<true><<<static_cast<unsigned>(batch), kTopkThreads, smem, s>>>(a);

@@ -27,7 +27,8 @@ from .gather import _gather_impl
 
 
 class SelectionStep:
-    def __init__(self, case, gather: bool = True, gather_v: bool = False):
+    def __init__(self, case, gather: bool = True, gather_v: bool = False, fused_route_pages: bool = True,
+                 keep_logits: bool = False):
         c = self.case = case
         d = c.lens.device
         B = c.B
@@ -38,6 +39,7 @@ class SelectionStep:
         self.center_lens = torch.zeros(B, dtype=torch.int32, device=d)
         self.tail_rows = torch.zeros(B, dtype=torch.int32, device=d)
         self.center_logits = torch.empty((B, c.P * 8), dtype=torch.float32, device=d)
+        self.page_scores = torch.empty((B, c.P), dtype=torch.float32, device=d)
         self.selected = torch.empty((B, c.take), dtype=torch.int32, device=d)
         self.width = c.width
         self.fine_table = torch.zeros((B, self.width // 64), dtype=torch.int32, device=d)
@@ -55,6 +57,11 @@ class SelectionStep:
         self.fused = query_fused.module()
         self.meta = K.BudgetMetadata(self.budget)
         self.graph = None
+        # fused_route_pages: page maxima from the scoring epilogue + route_pages with
+        # the fine-table write (the reference's query_route_table_fusion); equal
+        # outputs to route(center_logits) + fine_table_shared.
+        self.fused_route_pages = fused_route_pages
+        self.keep_logits = keep_logits or not fused_route_pages
 
     # -- the step ------------------------------------------------------------
     def run(self):
@@ -62,18 +69,29 @@ class SelectionStep:
         B = c.B
         self.meta[(B,)](c.lens, c.native_table, self.fine_lens, self.takes, self.dg_lens,
                         self.center_lens, self.tail_rows, c.P, c.topk, 1, 2, 64, c.window)
-        scoring.fp8_paged_mqa_logits(c.q8, c.centers, c.w, self.center_lens, c.center_table, None,
-                                     c.P * 8, out=self.center_logits)
-        self.fused.route(self.center_logits, c.lens, self.takes, self.selected, c.P,
-                         c.reordered_table, self.fine_table, self.tail_rows, c.capacity, False)
-        K.fine_table_shared[(B,)](c.reordered_table, self.selected, self.takes, c.lens, self.fine_table,
-                                  self.tail_rows, c.capacity, c.P, c.take, self.width // 64, 68)
+        if self.fused_route_pages:
+            # centre scoring emits each page's max-of-8 directly; route reads P floats
+            # per row and writes the fine page table itself (fill_table)
+            scoring.fp8_paged_mqa_logits(c.q8, c.centers, c.w, self.center_lens, c.center_table, None,
+                                         c.P * 8, page_max=self.page_scores, logits=self.keep_logits,
+                                         out=self.center_logits if self.keep_logits else None,
+                                         clean_logits=False)
+            self.fused.route_pages(self.page_scores, c.lens, self.takes, self.selected, c.P,
+                                   c.reordered_table, self.fine_table, self.tail_rows, c.capacity, True)
+        else:
+            scoring.fp8_paged_mqa_logits(c.q8, c.centers, c.w, self.center_lens, c.center_table, None,
+                                         c.P * 8, out=self.center_logits)
+            self.fused.route(self.center_logits, c.lens, self.takes, self.selected, c.P,
+                             c.reordered_table, self.fine_table, self.tail_rows, c.capacity, False)
+            K.fine_table_shared[(B,)](c.reordered_table, self.selected, self.takes, c.lens,
+                                      self.fine_table, self.tail_rows, c.capacity, c.P, c.take,
+                                      self.width // 64, 68)
         K.stage_tail_shared[(-(-B // 32) if B > 512 else B, 68)](
             c.native, c.native.view(torch.float32), c.native_table, c.lens, c.fine,
             c.fine.view(torch.float32), self.tail_rows, c.capacity, c.P, 68, 64, c.window,
             ROWS=B, GROUP=32 if B > 512 else 1)
         scoring.fp8_paged_mqa_logits(c.q8, c.fine, c.w, self.dg_lens, self.fine_table, None,
-                                     self.width, out=self.scores)
+                                     self.width, out=self.scores, clean_logits=False)
         self.fused.topk(self.scores, self.fine_lens, c.members, c.reordered_table, c.native_table,
                         self.selected, c.lens, self.takes, self.physical, self.logical, self.raw,
                         c.window, True, self.no_expansion, True, True, self.fine_table, False)

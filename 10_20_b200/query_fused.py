@@ -65,6 +65,24 @@ class V1QueryModule:
                   int(bool(fill_table)), B, _lib.stream_of(scores), device=scores.device)
 
     @staticmethod
+    def route_pages(page_scores, lens, takes, selected, pages, rt, ft, tail_rows, capacity, fill_table):
+        """Extension: fused.route over per-page scores (max of each page's 8 centres)."""
+        B = page_scores.shape[0] if page_scores.dim() == 2 else -1
+        _check_2d(page_scores, "page_scores", B, torch.float32, row_stride_ok=True)
+        _check_1d(lens, "lens", B)
+        _check_1d(takes, "takes", B)
+        sel64 = _selected(selected, B)
+        _check_2d(rt, "rt", B, torch.int32, cols=int(pages))
+        _check_2d(ft, "ft", B, torch.int32)
+        _check_1d(tail_rows, "tail_rows", B)
+        require(page_scores.shape[1] >= int(pages), "page_scores: need >= pages columns")
+        _lib.same_device(page_scores, lens, takes, selected, rt, ft, tail_rows)
+        _lib.call("v1x_route_pages", ptr(page_scores), page_scores.stride(0) if B > 1 else page_scores.shape[1],
+                  ptr(lens), ptr(takes), ptr(selected), sel64, selected.shape[1], int(pages), ptr(rt), ptr(ft),
+                  ft.shape[1], ptr(tail_rows), int(capacity), int(bool(fill_table)), B,
+                  _lib.stream_of(page_scores), device=page_scores.device)
+
+    @staticmethod
     def topk(scores, fine_lens, members, rt, nt, selected, lens, takes, physical, logical, raw,
              window, mask, expanded, physical_output, bucket_from_rank, fine_table, direct_fine):
         """fused.topk (VQ:181-220): mask + Top-T + raw->logical->physical (+ x4 expansion)."""

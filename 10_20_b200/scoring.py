@@ -31,7 +31,8 @@ IMPLS = {"auto": 0, "simt": 1, "tensor_core": 2}
 
 def fp8_paged_mqa_logits(q, kv_cache, weights, context_lens, block_table, schedule_meta,
                          max_context_len: int, clean_logits: bool = True, relu: bool = True,
-                         out: torch.Tensor | None = None, impl: str = "auto"):
+                         out: torch.Tensor | None = None, impl: str = "auto",
+                         page_max: torch.Tensor | None = None, logits: bool = True):
     """Logits [B, max_context_len] (float32); columns >= context_lens[b] are -inf.
 
     q: e4m3 [B, H, 128] or [B, 1, H, 128]; kv_cache: packed uint8 [pages, 8448] or
@@ -39,6 +40,9 @@ def fp8_paged_mqa_logits(q, kv_cache, weights, context_lens, block_table, schedu
     block_table: int32 [B, max_blocks].  impl: "auto" (tensor cores when H is a
     multiple of 32), "simt" (fixed fp32 evaluation order, H <= 64) or "tensor_core".
     clean_logits=False leaves columns >= context_lens[b] untouched.
+    page_max (extension): float32 [B, >= ceil(max_context_len / 8)] receiving the max of
+    every 8 consecutive logits (fused.route's page score); logits=False skips the
+    logits output (then `page_max` is required and the call returns it).
     """
     if q.dim() == 4:
         require(q.shape[1] == 1, "only next_n == 1 is supported")
@@ -55,13 +59,21 @@ def fp8_paged_mqa_logits(q, kv_cache, weights, context_lens, block_table, schedu
     require(lens.numel() == B and lens.dtype == torch.int32, "context_lens: int32 [B]")
     require(block_table.dim() == 2 and block_table.shape[0] == B and block_table.dtype == torch.int32
             and block_table.stride(1) == 1, "block_table: int32 [B, max_blocks]")
-    if out is None:
-        out = torch.empty((B, max_context_len), dtype=torch.float32, device=q.device)
-    require(out.dtype == torch.float32 and out.stride(1) == 1 and out.shape[1] >= max_context_len,
-            "out: float32 [B, >= max_context_len]")
+    if logits:
+        if out is None:
+            out = torch.empty((B, max_context_len), dtype=torch.float32, device=q.device)
+        require(out.dtype == torch.float32 and out.stride(1) == 1 and out.shape[1] >= max_context_len,
+                "out: float32 [B, >= max_context_len]")
+    else:
+        require(page_max is not None, "logits=False needs page_max")
+        out = None
+    if page_max is not None:
+        require(page_max.dtype == torch.float32 and page_max.stride(1) == 1 and page_max.shape[0] == B
+                and page_max.shape[1] * 8 >= max_context_len, "page_max: float32 [B, >= max_len/8]")
     from .kernels import status_word
     _lib.call("v1x_score_fp8", ptr(q), ptr(weights), ptr(kv_cache), kv_cache.numel() // 8448, ptr(lens),
-              ptr(block_table), block_table.stride(0), ptr(out), out.stride(0), int(max_context_len), H,
+              ptr(block_table), block_table.stride(0), ptr(out), out.stride(0) if out is not None else 0,
+              int(max_context_len), ptr(page_max), page_max.stride(0) if page_max is not None else 0, H,
               int(bool(relu)), int(bool(clean_logits)), IMPLS[impl], ptr(status_word(q.device)), B,
               _lib.stream_of(q), device=q.device)
-    return out
+    return out if logits else page_max

@@ -67,6 +67,16 @@ V1X_API int v1x_route(const float* scores, int64_t score_stride, int64_t score_c
               int64_t fine_pages, const int32_t* tail_rows, int64_t capacity, int fill_table,
               int64_t batch, void* stream);
 
+/* Extension (no reference counterpart): fused.route taking per-page scores
+ * (the maxima of each page's 8 centre logits, e.g. v1x_score_fp8's page_max)
+ * instead of centre logits.  page_scores f32 [batch, >= pages] with row stride
+ * page_stride.  Selection, fine-table fill and checks are those of v1x_route. */
+V1X_API int v1x_route_pages(const float* page_scores, int64_t page_stride, const int32_t* lens,
+              const int32_t* takes, void* selected, int selected_is_i64, int64_t take_stride,
+              int64_t pages, const int32_t* rt, int32_t* ft, int64_t fine_pages,
+              const int32_t* tail_rows, int64_t capacity, int fill_table, int64_t batch,
+              void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* fused.topk -- replaces V1QueryKernel::topk (VQ:181-220, kernel VQ:62-153).
  * scores f32 [batch, cols] row stride score_stride (% 4 == 0); mutated in place
@@ -211,15 +221,19 @@ V1X_API int v1x_expand_logical(const int32_t* logical, int32_t* out, int64_t top
  * DS/kernels.py:310-313: out[b, j] = sum_h w[b,h] * relu(q[b,h,:] . k_j) * s_j for
  * j < lens[b]; when clean != 0 also -inf for lens[b] <= j < max_len.
  * q u8 (e4m3) [batch, heads, 128]; w f32 [batch, heads]; pool u8 [pool_pages, 8448];
- * table i32 [batch, table_stride]; out f32 [batch, out_stride]. heads in [1, 256].
- * relu = 0 gives the signed variant.  impl: 0 = automatic (tensor cores when heads
- * is a multiple of 32, else the SIMT path), 1 = SIMT (fixed fp32 order, heads <=
- * 64), 2 = tensor cores.  status: optional i32 device word receiving
- * V1X_STATUS_TIMEOUT if a bounded device wait gave up. */
+ * table i32 [batch, table_stride]; out f32 [batch, out_stride] (may be NULL).
+ * page_max (extension, may be NULL): f32 [batch, page_stride], entry p = max over
+ * keys 8p..8p+7 (-inf for keys >= lens[b]) -- the per-page centre maximum that
+ * fused.route computes (VQ:26-41), produced in the scoring epilogue.
+ * heads in [1, 256]; relu = 0 gives the signed variant.  impl: 0 = automatic
+ * (tensor cores when heads is a multiple of 32, else SIMT), 1 = SIMT (fixed fp32
+ * evaluation order, heads <= 64), 2 = tensor cores.  status: optional i32 device
+ * word receiving V1X_STATUS_TIMEOUT if a bounded device wait gave up. */
 V1X_API int v1x_score_fp8(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages,
                   const int32_t* lens, const int32_t* table, int64_t table_stride, float* out,
-                  int64_t out_stride, int64_t max_len, int64_t heads, int relu, int clean,
-                  int impl, int32_t* status, int64_t batch, void* stream);
+                  int64_t out_stride, int64_t max_len, float* page_max, int64_t page_stride,
+                  int64_t heads, int relu, int clean, int impl, int32_t* status, int64_t batch,
+                  void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* _gather_slots -- replaces NA/kernels.py:62-77 (GatherWorkspace.gather, :102-111).

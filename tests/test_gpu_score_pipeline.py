@@ -126,7 +126,7 @@ def test_selection_step_end_to_end(cuda_dev):
     """Every stage of the step vs the oracle: metadata exact, centre/fine scores
     within tolerance, route/top-k/gather bit-exact given the device scores."""
     case = _small_case()
-    step = pipeline.SelectionStep(case, gather=True)
+    step = pipeline.SelectionStep(case, gather=True, keep_logits=True)
     step.run()
     torch.cuda.synchronize()
     c = case
@@ -151,16 +151,22 @@ def test_selection_step_end_to_end(cuda_dev):
     fine_pool = c.fine.cpu().numpy()
     fine_exp = O.score_paged(q8, w, fine_pool, ft, dg, step.width, exact=False)
     got_scores = step.scores.cpu().numpy()   # masked in place by the top-k
+    cols = np.arange(got_scores.shape[1])[None, :]
+    got_scores = np.where(cols < fl[:, None], got_scores, -np.inf).astype(np.float32)  # past fine_lens: unwritten
     members = c.members.cpu().numpy()
-    unmasked = got_scores.copy()
     e = O.topk(got_scores, fl, members, rt, nt, sel, lens, tk, c.window, True, 2048,
                fine_table=ft, direct_fine=False)
     assert np.array_equal(e["scores"], got_scores)          # mask is idempotent
     assert np.array_equal(step.raw.cpu().numpy(), e["raw"])
     assert np.array_equal(step.logical.cpu().numpy(), e["logical"])
     assert np.array_equal(step.physical.cpu().numpy(), e["physical"])
-    fin = np.isfinite(unmasked)
-    close(np.where(fin, unmasked, -np.inf), np.where(fin, fine_exp, -np.inf))
+    fin = np.isfinite(got_scores)
+    close(np.where(fin, got_scores, -np.inf), np.where(fin, fine_exp, -np.inf))
+    # page maxima from the scoring epilogue == max of the centre logits of each page
+    pm = step.page_scores.cpu().numpy()
+    for r in range(c.B):
+        np_ = int(cl[r]) // 8
+        assert np.array_equal(pm[r, :np_], clog[r, :np_ * 8].reshape(np_, 8).max(1))
     lat = c.latent.view(torch.int16).cpu().numpy()
     kg, _ = O.gather_slots(lat, None, None, step.physical.cpu().numpy(), c.B, 2048, 0)
     assert np.array_equal(step.kv.view(torch.int16).reshape(-1, lat.shape[-1]).cpu().numpy(), kg)
@@ -176,3 +182,37 @@ def test_selection_step_graph_replay(cuda_dev):
     step.replay()
     torch.cuda.synchronize()
     assert torch.equal(step.physical, ref)
+
+
+@pytest.mark.parametrize("impl,H", [("simt", 1), ("simt", 16), ("tensor_core", 64)])
+def test_page_max_and_route_pages(impl, H, cuda_dev):
+    """Scoring page maxima + route_pages == route over the centre logits (bit-exact)."""
+    rng = np.random.default_rng(H)
+    B, P, NP = 33, 256, 400
+    pool = np.zeros((NP, 8448), np.uint8)
+    kb = torch.randn((NP, 64, 128), generator=torch.Generator().manual_seed(1)).to(torch.float8_e4m3fn)
+    pool[:, :8192] = kb.view(torch.uint8).reshape(NP, 8192).numpy()
+    pool.view(np.float32)[:, 2048:] = rng.random((NP, 64)).astype(np.float32) + 0.1
+    q = torch.randn((B, H, 128), generator=torch.Generator().manual_seed(2)).to(torch.float8_e4m3fn).cuda()
+    w = dev(rng.random((B, H)).astype(np.float32))
+    ctable = dev(rng.integers(0, NP, size=(B, P // 8)).astype(np.int32))
+    lens = rng.integers(1, P * 64, size=B).astype(np.int32)
+    lens[:3] = [1, 1025, P * 64]
+    clen = dev(np.maximum((np.maximum(lens - 1, 0) // 1024) * 128, 1).astype(np.int32))
+    logits = torch.empty((B, P * 8), device="cuda")
+    pm = torch.full((B, P), 5.0, device="cuda")
+    S.fp8_paged_mqa_logits(q, dev(pool), w, clen, ctable, None, P * 8, out=logits, page_max=pm, impl=impl)
+    lg = logits.cpu().numpy()
+    pmn = pm.cpu().numpy()
+    assert np.array_equal(pmn, lg.reshape(B, P, 8).max(2))
+    qf = importlib.import_module("10_20_b200.query_fused")
+    takes = dev(rng.integers(0, 40, size=B).astype(np.int32))
+    rt = dev(rng.integers(0, 10000, size=(B, P)).astype(np.int32))
+    trows = dev(rng.integers(0, B, size=B).astype(np.int32))
+    sel_a = torch.empty((B, 40), dtype=torch.int32, device="cuda")
+    sel_b = torch.empty_like(sel_a)
+    ft_a = torch.full((B, 40 + 68), -3, dtype=torch.int32, device="cuda")
+    ft_b = ft_a.clone()
+    qf.module().route(logits, dev(lens), takes, sel_a, P, rt, ft_a, trows, 77, True)
+    qf.module().route_pages(pm, dev(lens), takes, sel_b, P, rt, ft_b, trows, 77, True)
+    assert torch.equal(sel_a, sel_b) and torch.equal(ft_a, ft_b)
