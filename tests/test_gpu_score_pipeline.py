@@ -141,6 +141,8 @@ def test_selection_step_end_to_end(cuda_dev):
     centers = c.centers.cpu().numpy()
     ctab = c.center_table.cpu().numpy()
     clog = step.center_logits.cpu().numpy()
+    ccols = np.arange(clog.shape[1])[None, :]
+    clog = np.where(ccols < cl[:, None], clog, -np.inf).astype(np.float32)  # unwritten past center_lens
     close(clog, O.score_paged(q8, w, centers, ctab, cl, c.P * 8, exact=False))
     rt = c.reordered_table.cpu().numpy()
     sel, ft = O.route(clog, lens, tk, c.take, c.P, rt, np.zeros((c.B, step.width // 64), np.int32), tr,
