@@ -277,13 +277,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if ((lane & 7) == 0 && key < a.max_len) a.page_max[b * a.page_stride + (key >> 3)] = m;
       }
     }
-    if (a.clean && a.out) {
-      const int e = tid - 64;
-      for (int b = blockIdx.x; b < a.B; b += G) {
-        const int64_t eff = row_eff(a, b);
-        const int64_t start = eff > 0 ? (eff + 127) / 128 * 128 : 0;
+    // columns past the last tile: -inf logits (clean) and -inf page maxima (always)
+    const int e = tid - 64;
+    for (int b = blockIdx.x; b < a.B; b += G) {
+      const int64_t eff = row_eff(a, b);
+      const int64_t start = eff > 0 ? (eff + 127) / 128 * 128 : 0;
+      if (a.clean && a.out)
         for (int64_t j = start + e; j < a.max_len; j += 128) a.out[b * a.out_stride + j] = -CUDART_INF_F;
-      }
+      if (a.page_max)
+        for (int64_t g = start / 8 + e; g < (a.max_len + 7) / 8; g += 128)
+          a.page_max[b * a.page_stride + g] = -CUDART_INF_F;
     }
   }
   __syncthreads();

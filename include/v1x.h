@@ -222,9 +222,10 @@ V1X_API int v1x_expand_logical(const int32_t* logical, int32_t* out, int64_t top
  * j < lens[b]; when clean != 0 also -inf for lens[b] <= j < max_len.
  * q u8 (e4m3) [batch, heads, 128]; w f32 [batch, heads]; pool u8 [pool_pages, 8448];
  * table i32 [batch, table_stride]; out f32 [batch, out_stride] (may be NULL).
- * page_max (extension, may be NULL): f32 [batch, page_stride], entry p = max over
- * keys 8p..8p+7 (-inf for keys >= lens[b]) -- the per-page centre maximum that
- * fused.route computes (VQ:26-41), produced in the scoring epilogue.
+ * page_max (extension, may be NULL): f32 [batch, page_stride], entries
+ * p < ceil(max_len/8) = max over keys 8p..8p+7 (-inf for keys >= lens[b]) -- the
+ * per-page centre maximum that fused.route computes (VQ:26-41), produced in the
+ * scoring epilogue.
  * heads in [1, 256]; relu = 0 gives the signed variant.  impl: 0 = automatic
  * (tensor cores when heads is a multiple of 32, else SIMT), 1 = SIMT (fixed fp32
  * evaluation order, heads <= 64), 2 = tensor cores.  status: optional i32 device
