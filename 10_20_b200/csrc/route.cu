@@ -71,25 +71,53 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const __grid_const
     return;
   }
   // ---- page keys in blocked-rank order (VQ:26-41) ----------------------------
+  // All loads of a thread are issued before any is consumed (a loop that stores
+  // each load's result before the next load would serialise the latencies).
   const int act = static_cast<int>(min(static_cast<int64_t>(active), kPages ? a.score_cols : a.score_cols / 8));
   const float* srow = a.scores + row * a.score_stride;
-  const bool vec = (reinterpret_cast<uintptr_t>(srow) & 15) == 0;
-  for (int r = tid; r < a.n_items; r += nt) {
-    const int p = r / a.base + (r % a.base) * 128;
-    float best = -CUDART_INF_F;
-    if (kPages) {
-      if (p < act) best = srow[p];
-    } else if (p < act) {
-      const float* s = srow + static_cast<int64_t>(p) * 8;
-      if (vec) {
-        const float4 x = reinterpret_cast<const float4*>(s)[0];
-        const float4 y = reinterpret_cast<const float4*>(s)[1];
-        best = fmaxf(fmaxf(fmaxf(x.x, x.y), fmaxf(x.z, x.w)), fmaxf(fmaxf(y.x, y.y), fmaxf(y.z, y.w)));
-      } else {
-        best = fmaxf(fmaxf(fmaxf(s[0], s[1]), fmaxf(s[2], s[3])), fmaxf(fmaxf(s[4], s[5]), fmaxf(s[6], s[7])));
+  if (kPages) {
+    // stage the row's page scores in smem (reusing the sort list), coalesced
+    float* ps = reinterpret_cast<float*>(sm.list);
+    const bool vec = (reinterpret_cast<uintptr_t>(srow) & 15) == 0;
+    const int nv = vec ? act >> 2 : 0;
+    for (int v = tid; v < nv; v += nt) reinterpret_cast<float4*>(ps)[v] = reinterpret_cast<const float4*>(srow)[v];
+    for (int p = nv * 4 + tid; p < act; p += nt) ps[p] = srow[p];
+    __syncthreads();
+    for (int r = tid; r < a.n_items; r += nt) {
+      const int p = r / a.base + (r % a.base) * 128;
+      sm.keys[r] = order_key(p < act ? ps[p] : -CUDART_INF_F);
+    }
+  } else {
+    const bool vec = (reinterpret_cast<uintptr_t>(srow) & 15) == 0;
+    constexpr int kBatch = 4;
+    for (int r0 = tid; r0 < a.n_items; r0 += nt * kBatch) {
+      float4 x[kBatch], y[kBatch];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int r = r0 + u * nt;
+        const int p = r / a.base + (r % a.base) * 128;
+        x[u] = y[u] = make_float4(-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F);
+        if (r < a.n_items && p < act) {
+          const float* sp = srow + static_cast<int64_t>(p) * 8;
+          if (vec) {
+            x[u] = reinterpret_cast<const float4*>(sp)[0];
+            y[u] = reinterpret_cast<const float4*>(sp)[1];
+          } else {
+            x[u] = make_float4(sp[0], sp[1], sp[2], sp[3]);
+            y[u] = make_float4(sp[4], sp[5], sp[6], sp[7]);
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int r = r0 + u * nt;
+        if (r < a.n_items) {
+          const float best = fmaxf(fmaxf(fmaxf(x[u].x, x[u].y), fmaxf(x[u].z, x[u].w)),
+                                   fmaxf(fmaxf(y[u].x, y[u].y), fmaxf(y[u].z, y[u].w)));
+          sm.keys[r] = order_key(best);
+        }
       }
     }
-    sm.keys[r] = order_key(best);
   }
   // number of ranks the output needs: selected (take_stride) and ft (take)
   const int want = static_cast<int>(min(static_cast<int64_t>(a.n_items),

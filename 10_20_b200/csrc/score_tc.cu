@@ -86,12 +86,15 @@ __device__ __forceinline__ int64_t row_eff(const TcArgs& a, int b) {
 
 __global__ void __launch_bounds__(kTcThreads, 1)
     score_tc_kernel(const __grid_constant__ CUtensorMap pool_map, const __grid_constant__ CUtensorMap q_map,
-                    const __grid_constant__ CUtensorMap scale_map, const __grid_constant__ TcArgs a) {
+                    const __grid_constant__ CUtensorMap scale_map, const __grid_constant__ CUtensorMap w_map,
+                    const __grid_constant__ TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t stage_bytes = 16384 + static_cast<uint32_t>(a.H) * 128;
-  float* scales = reinterpret_cast<float*>(base + kTcStages * stage_bytes);   // [kScaleSlots][128]
-  TcShared& sh = *reinterpret_cast<TcShared*>(reinterpret_cast<uint8_t*>(scales) + kScaleSlots * 512);
+  // epilogue ring: per tile the 128 key scales and the row's H head weights
+  const uint32_t slot_bytes = 512 + static_cast<uint32_t>(a.H) * 4;
+  uint8_t* ering = base + kTcStages * stage_bytes;
+  TcShared& sh = *reinterpret_cast<TcShared*>(ering + kScaleSlots * slot_bytes);
   int* prefix = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(&sh) + sizeof(TcShared));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nacc = a.nacc;
@@ -141,6 +144,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tma_prefetch_desc(&pool_map);
     tma_prefetch_desc(&q_map);
     tma_prefetch_desc(&scale_map);
+    tma_prefetch_desc(&w_map);
   }
   __syncthreads();
   tc_fence_after();
@@ -182,9 +186,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const int r = it % kScaleSlots;
             ok = mbar_wait(&sh.sempty[r], ((it / kScaleSlots) & 1) ^ 1, &sh.abort, kWaitLimitNs);
             if (ok) {
-              mbar_arrive_expect_tx(&sh.sfull[r], 512);
-              tma_load_2d(scales + r * 128, &scale_map, &sh.sfull[r], 0, p0);
-              tma_load_2d(scales + r * 128 + 64, &scale_map, &sh.sfull[r], 0, p1);
+              uint8_t* slot = ering + r * slot_bytes;
+              mbar_arrive_expect_tx(&sh.sfull[r], slot_bytes);
+              tma_load_2d(slot, &scale_map, &sh.sfull[r], 0, p0);
+              tma_load_2d(slot + 256, &scale_map, &sh.sfull[r], 0, p1);
+              tma_load_2d(slot + 512, &w_map, &sh.sfull[r], 0, b);
               ++issued_scales;
             }
           }
@@ -240,17 +246,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int t = T - prefix[b];
       const int64_t eff = row_eff(a, b);
       const int64_t key = static_cast<int64_t>(t) * 128 + i;
+      if (!mbar_wait(&sh.sfull[r], (it / kScaleSlots) & 1, &sh.abort, kWaitLimitNs)) { raise_abort(sh, a.status); break; }
+      const float* slot = reinterpret_cast<const float*>(ering + r * slot_bytes);
+      const float scale = slot[i];
+      const float* wr = slot + 128;
       if (!mbar_wait(&sh.tfull[acc], (it / nacc) & 1, &sh.abort, kWaitLimitNs)) { raise_abort(sh, a.status); break; }
       tc_fence_after();
       float sum = 0.0f;
-      const float* wr = a.w + static_cast<int64_t>(b) * a.H;
       for (int c0 = 0; c0 < a.H; c0 += 32) {
         uint32_t v[32];
         tmem_ld32(tmem + (static_cast<uint32_t>(q4 * 32) << 16) + static_cast<uint32_t>(acc * a.H + c0), v);
         tmem_ld_wait();
 #pragma unroll
         for (int j = 0; j < 32; j += 4) {
-          const float4 w4 = __ldg(reinterpret_cast<const float4*>(wr + c0 + j));
+          const float4 w4 = *reinterpret_cast<const float4*>(wr + c0 + j);
           float v0 = __uint_as_float(v[j]), v1 = __uint_as_float(v[j + 1]);
           float v2 = __uint_as_float(v[j + 2]), v3 = __uint_as_float(v[j + 3]);
           if (a.relu) {
@@ -264,8 +273,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(&sh.tempty[acc]);
-      if (!mbar_wait(&sh.sfull[r], (it / kScaleSlots) & 1, &sh.abort, kWaitLimitNs)) { raise_abort(sh, a.status); break; }
-      const float scale = scales[r * 128 + i];
       mbar_arrive(&sh.sempty[r]);
       const float score = key < eff ? sum * scale : -CUDART_INF_F;
       if (a.out && key < a.max_len && (key < eff || a.clean)) a.out[b * a.out_stride + key] = score;
@@ -319,8 +326,8 @@ int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t 
     set_error("score_fp8 (tensor core): heads must be a multiple of 32 <= 256 and batch <= %d", kMaxTcRows);
     return V1X_ERR_UNSUPPORTED;
   }
-  if ((reinterpret_cast<uintptr_t>(q) & 15) != 0) {
-    set_error("score_fp8 (tensor core): q must be 16-byte aligned");
+  if (((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(w)) & 15) != 0) {
+    set_error("score_fp8 (tensor core): q and w must be 16-byte aligned");
     return V1X_ERR_INVALID;
   }
   auto enc = encode_fn();
@@ -369,13 +376,27 @@ int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t 
       return V1X_ERR_CUDA;
     }
   }
+  CUtensorMap w_map;
+  {
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(heads), static_cast<cuuint64_t>(batch)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(heads * 4)};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(heads), 1};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = enc(&w_map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(w), dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+      set_error("score_fp8: weight tensor map encode failed (%d)", static_cast<int>(r));
+      return V1X_ERR_CUDA;
+    }
+  }
   const int nacc = 4 * heads <= 256 ? 4 : 2;
   uint32_t cols = 32;
   while (cols < static_cast<uint32_t>(nacc * heads)) cols <<= 1;
   TcArgs args{lens, table, table_stride, w, out, out_stride, max_len, page_max, page_stride,
               static_cast<int>(batch), static_cast<int>(heads), relu, clean, nacc, cols, status};
-  const size_t smem = 1024 + kTcStages * (16384 + heads * 128) + kScaleSlots * 512 + sizeof(TcShared) +
-                      (batch + 1) * 4 + 16;
+  const size_t smem = 1024 + kTcStages * (16384 + heads * 128) + kScaleSlots * (512 + heads * 4) +
+                      sizeof(TcShared) + (batch + 1) * 4 + 16;
   static DeviceOnce once;
   if (once.first())
     cudaFuncSetAttribute(score_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
@@ -387,7 +408,8 @@ int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t 
   const int per_sm = (cols <= 256 && smem <= 113 * 1024) ? 2 : 1;
   int64_t grid = static_cast<int64_t>(num_sms()) * per_sm;
   if (grid > max_tiles) grid = max_tiles > 0 ? max_tiles : 1;
-  score_tc_kernel<<<static_cast<unsigned>(grid), kTcThreads, smem, stream>>>(pool_map, q_map, scale_map, args);
+  score_tc_kernel<<<static_cast<unsigned>(grid), kTcThreads, smem, stream>>>(pool_map, q_map, scale_map, w_map,
+                                                                              args);
   return launch_status("v1x_score_fp8 (tensor core)");
 }
 

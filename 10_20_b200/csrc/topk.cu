@@ -56,12 +56,16 @@ struct RowCtx {
 };
 
 constexpr int kPageCache = 256;   // page ids of the first 256 selected ranks, cached in smem
+constexpr int kMaxTopk = 2048;
 
 struct TopkSmem {
   int hist[256];
   int warp_tot[kTopkThreads / 32 + 1];
   int digit, need;
+  int nbnd;
   int pgc[kPageCache];
+  int2 bnd[kPageCache];            // (rank index, reordered page) of boundary buckets
+  int rawbuf[kMaxTopk];            // selected raw candidate ids in output order
 };
 
 // Page holding raw candidate r*64+x (r < take): the fine table's entry (direct)
@@ -77,79 +81,110 @@ __device__ __forceinline__ int64_t page_of_rank(const TopkArgs& a, const RowCtx&
   return page;
 }
 
-// Mapping epilogue for one output slot (VQ:121-148).
-__device__ __forceinline__ void emit_slot(const TopkArgs& a, const RowCtx& c, const TopkSmem& sm, int slot,
-                                          int raw, bool finite) {
-  int logical = -1, physical = -1;
-  if (raw >= 0 && raw < c.L && finite) {
-    int lg = -1;
-    bool ok = true;
-    if (raw < c.take * 64) {
-      const int r = raw >> 6;
-      const int64_t page = r < kPageCache ? sm.pgc[r] : page_of_rank(a, c, r);
-      ok = page >= 0 && page < a.member_rows;
-      if (ok) lg = a.members[page * 64 + (raw & 63)];
-    } else {
-      const int off = raw - c.take * 64;
-      lg = off < c.sink ? off : c.tail + off - c.sink;
+// Members of the boundary bucket page `page` outside [sink, tail) -> -inf, in
+// global memory and in the staged-key bitmap (VQ:94-103).
+__device__ __forceinline__ void mask_page(const TopkArgs& a, const RowCtx& c, float* srow, uint32_t* bitmap,
+                                          int r, int64_t page, int lane_lo, int lane_step) {
+  for (int off = lane_lo; off < 64; off += lane_step) {
+    const int lg = a.members[page * 64 + off];
+    const int64_t col = static_cast<int64_t>(r) * 64 + off;
+    if ((lg < c.sink || lg >= c.tail) && col < a.cols) {
+      srow[col] = -CUDART_INF_F;
+      if (bitmap) atomicOr(&bitmap[col >> 5], 1u << (col & 31));
     }
-    if (ok && lg >= 0 && lg < c.n) {
-      logical = lg;
-      if (a.physical_output) {
-        const int64_t p = lg >> 6;
-        physical = p < a.pages ? a.nt[c.row * a.pages + p] * 64 + (lg & 63) : -1;
-      }
-    }
-  }
-  const int64_t dst = c.row * a.topk + slot;
-  a.logical[dst] = logical;
-  if (a.physical_output) {
-    a.physical[dst] = physical;
-    a.raw[dst] = raw;
-  }
-  if (a.expansion_stride) {
-    const int b = logical * 4;
-    reinterpret_cast<int4*>(a.expanded + c.row * a.expansion_stride)[slot] =
-        logical < 0 ? make_int4(-1, -1, -1, -1) : make_int4(b, b + 1, b + 2, b + 3);
   }
 }
 
-// One warp per selected rank r < take: cache the rank's page for the epilogue
-// and, when masking, -inf the members of boundary buckets that fall outside
-// [sink, tail) (VQ:71-107) -- in global memory (the reference mutates `scores`)
-// and in the smem bitmap that the staged keys are built from.
+// Selected ranks: every thread resolves its own ranks (selected -> reordered
+// page, and the bucket identity) so the loads of all ranks are in flight at
+// once; pages are cached for the epilogue and boundary buckets are queued.
+// Then one warp per boundary page masks its members (VQ:71-107).
 __device__ void ranks_and_mask(const TopkArgs& a, const RowCtx& c, float* srow, TopkSmem& sm, uint32_t* bitmap) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  for (int r = warp; r < c.take; r += nw) {
-    int64_t rank = -1, rpage = -1, epage = -1;
-    int bucket = 0;
-    if (lane == 0) {
-      if (r < a.take_stride) rank = load_index(a.selected, a.sel64, c.row * a.take_stride + r);
-      if (rank >= 0 && rank < a.pages) rpage = a.rt[c.row * a.pages + rank];
-      epage = a.direct_fine ? (r < a.fine_table_cols ? a.fine_table[c.row * a.fine_table_cols + r] : -1) : rpage;
-      if (r < kPageCache) sm.pgc[r] = static_cast<int>(epage);
-      if (a.mask && rank >= 0 && rank < a.pages) {
-        if (a.bucket_from_rank) bucket = static_cast<int>(rank / 16) * 1024;
-        else bucket = (rpage >= 0 && rpage < a.member_rows) ? (a.members[rpage * 64] / 1024) * 1024 : 0;
-      }
-    }
-    if (!a.mask) continue;
-    rank = __shfl_sync(0xffffffffu, rank, 0);
-    rpage = __shfl_sync(0xffffffffu, rpage, 0);
-    bucket = __shfl_sync(0xffffffffu, bucket, 0);
-    if (rank < 0 || rank >= a.pages || rpage < 0 || rpage >= a.member_rows) continue;
+  const int tid = threadIdx.x, nt = blockDim.x;
+  const int lane = tid & 31, warp = tid >> 5, nw = nt >> 5;
+  for (int r = tid; r < c.take; r += nt) {
+    int64_t rank = -1, rpage = -1;
+    if (r < a.take_stride) rank = load_index(a.selected, a.sel64, c.row * a.take_stride + r);
+    const bool rank_ok = rank >= 0 && rank < a.pages;
+    if (rank_ok) rpage = a.rt[c.row * a.pages + rank];
+    const int64_t epage =
+        a.direct_fine ? (r < a.fine_table_cols ? a.fine_table[c.row * a.fine_table_cols + r] : -1) : rpage;
+    if (r < kPageCache) sm.pgc[r] = static_cast<int>(epage);
+    if (!a.mask || !rank_ok || rpage < 0 || rpage >= a.member_rows) continue;
+    const int bucket = a.bucket_from_rank ? static_cast<int>(rank / 16) * 1024 : (a.members[rpage * 64] / 1024) * 1024;
     if (bucket < c.sink || bucket + 1024 > c.tail) {
+      const int k = atomicAdd(&sm.nbnd, 1);
+      if (k < kPageCache) sm.bnd[k] = make_int2(r, static_cast<int>(rpage));
+      else mask_page(a, c, srow, bitmap, r, rpage, 0, 1);   // queue full: this thread masks it
+    }
+  }
+  __syncthreads();
+  const int nb = min(sm.nbnd, kPageCache);
+  for (int k = warp; k < nb; k += nw) mask_page(a, c, srow, bitmap, sm.bnd[k].x, sm.bnd[k].y, lane, 32);
+}
+
+// Mapping epilogue for output slots tid, tid+nt, ... (VQ:121-148).  Each
+// thread issues the loads of all its slots before consuming any of them.
+template <bool kStaged>
+__device__ void emit_all(const TopkArgs& a, const RowCtx& c, const TopkSmem& sm, const uint32_t* keys,
+                         const float* srow) {
+  constexpr int kPer = (kMaxTopk + kTopkThreads - 1) / kTopkThreads;
+  const int tid = threadIdx.x, nt = blockDim.x;
+  int raw[kPer], lg[kPer];
+  bool live[kPer];
 #pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const int off = lane + i * 32;
-        const int lg = a.members[rpage * 64 + off];
-        const int64_t col = static_cast<int64_t>(r) * 64 + off;
-        const bool bad = (lg < c.sink || lg >= c.tail) && col < a.cols;
-        if (bad) {
-          srow[col] = -CUDART_INF_F;
-          if (bitmap) atomicOr(&bitmap[col >> 5], 1u << (col & 31));
-        }
-      }
+  for (int k = 0; k < kPer; ++k) {
+    const int t = tid + k * nt;
+    raw[k] = t < a.topk ? sm.rawbuf[t] : -1;
+    live[k] = false;
+    if (raw[k] >= 0 && raw[k] < c.L) {
+      if constexpr (kStaged) live[k] = keys[raw[k]] != kNegInfKey;
+      else live[k] = srow[raw[k]] != -CUDART_INF_F;
+    }
+  }
+  // raw -> logical (members load for reordered candidates)
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    lg[k] = -1;
+    if (!live[k]) continue;
+    const int x = raw[k];
+    if (x < c.take * 64) {
+      const int r = x >> 6;
+      const int64_t page = r < kPageCache ? sm.pgc[r] : page_of_rank(a, c, r);
+      if (page >= 0 && page < a.member_rows) lg[k] = a.members[page * 64 + (x & 63)];
+    } else {
+      const int off = x - c.take * 64;
+      lg[k] = off < c.sink ? off : c.tail + off - c.sink;
+    }
+  }
+  // logical -> physical (current native table) and stores
+  int ph[kPer];
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    ph[k] = -1;
+    if (!(lg[k] >= 0 && lg[k] < c.n)) {
+      lg[k] = -1;
+      continue;
+    }
+    if (a.physical_output) {
+      const int64_t p = lg[k] >> 6;
+      ph[k] = p < a.pages ? a.nt[c.row * a.pages + p] * 64 + (lg[k] & 63) : -1;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const int t = tid + k * nt;
+    if (t >= a.topk) continue;
+    const int64_t dst = c.row * a.topk + t;
+    a.logical[dst] = lg[k];
+    if (a.physical_output) {
+      a.physical[dst] = ph[k];
+      a.raw[dst] = raw[k];
+    }
+    if (a.expansion_stride) {
+      const int b = lg[k] * 4;
+      reinterpret_cast<int4*>(a.expanded + c.row * a.expansion_stride)[t] =
+          lg[k] < 0 ? make_int4(-1, -1, -1, -1) : make_int4(b, b + 1, b + 2, b + 3);
     }
   }
 }
@@ -192,6 +227,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(const __grid_constan
   asm volatile("cp.async.commit_group;" ::: "memory");
   if (bitmap)
     for (int w = tid; w < bm_words; w += nt) bitmap[w] = 0u;
+  if (tid == 0) sm.nbnd = 0;
   __syncthreads();
   // 2. page ids of the selected ranks + boundary mask, overlapping the copy
   ranks_and_mask(a, c, srow, sm, bitmap);
@@ -199,11 +235,9 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(const __grid_constan
   __syncthreads();
 
   if (!select) {
-    for (int t = tid; t < a.topk; t += nt) {
-      const int raw = t < c.L ? t : -1;
-      const bool fin = raw >= 0 && srow[raw] != -CUDART_INF_F;
-      emit_slot(a, c, sm, t, raw, fin);
-    }
+    for (int t = tid; t < a.topk; t += nt) sm.rawbuf[t] = t < c.L ? t : -1;
+    __syncthreads();
+    emit_all<false>(a, c, sm, keys, srow);
   } else {
     if constexpr (kStaged) {
       // 3. floats -> order keys in place, masked columns -> -inf
@@ -278,8 +312,10 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(const __grid_constan
         sel = eq_seen < need;
         ++eq_seen;
       }
-      if (sel && pos < a.topk) emit_slot(a, c, sm, pos++, i, k != kNegInfKey);
+      if (sel && pos < a.topk) sm.rawbuf[pos++] = i;
     }
+    __syncthreads();
+    emit_all<kStaged>(a, c, sm, keys, srow);
   }
   if (a.expansion_stride) {
     for (int64_t j = static_cast<int64_t>(a.topk) * 4 + tid; j < a.expansion_stride; j += nt)

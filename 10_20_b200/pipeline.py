@@ -62,6 +62,9 @@ class SelectionStep:
         # outputs to route(center_logits) + fine_table_shared.
         self.fused_route_pages = fused_route_pages
         self.keep_logits = keep_logits or not fused_route_pages
+        # the sink/tail staging depends only on the metadata: it runs on a side
+        # stream, concurrently with centre scoring and routing
+        self.side = torch.cuda.Stream(device=d)
 
     # -- the step ------------------------------------------------------------
     def run(self):
@@ -69,6 +72,13 @@ class SelectionStep:
         B = c.B
         self.meta[(B,)](c.lens, c.native_table, self.fine_lens, self.takes, self.dg_lens,
                         self.center_lens, self.tail_rows, c.P, c.topk, 1, 2, 64, c.window)
+        main = torch.cuda.current_stream(c.lens.device)
+        self.side.wait_stream(main)
+        with torch.cuda.stream(self.side):
+            K.stage_tail_shared[(-(-B // 32) if B > 512 else B, 68)](
+                c.native, c.native.view(torch.float32), c.native_table, c.lens, c.fine,
+                c.fine.view(torch.float32), self.tail_rows, c.capacity, c.P, 68, 64, c.window,
+                ROWS=B, GROUP=32 if B > 512 else 1)
         if self.fused_route_pages:
             # centre scoring emits each page's max-of-8 directly; route reads P floats
             # per row and writes the fine page table itself (fill_table)
@@ -86,10 +96,7 @@ class SelectionStep:
             K.fine_table_shared[(B,)](c.reordered_table, self.selected, self.takes, c.lens,
                                       self.fine_table, self.tail_rows, c.capacity, c.P, c.take,
                                       self.width // 64, 68)
-        K.stage_tail_shared[(-(-B // 32) if B > 512 else B, 68)](
-            c.native, c.native.view(torch.float32), c.native_table, c.lens, c.fine,
-            c.fine.view(torch.float32), self.tail_rows, c.capacity, c.P, 68, 64, c.window,
-            ROWS=B, GROUP=32 if B > 512 else 1)
+        main.wait_stream(self.side)
         scoring.fp8_paged_mqa_logits(c.q8, c.fine, c.w, self.dg_lens, self.fine_table, None,
                                      self.width, out=self.scores, clean_logits=False)
         self.fused.topk(self.scores, self.fine_lens, c.members, c.reordered_table, c.native_table,
