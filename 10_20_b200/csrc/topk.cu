@@ -359,7 +359,7 @@ extern "C" int v1x_topk(float* scores, int64_t score_stride, int64_t cols, const
       static DeviceOnce once;
       if (once.first()) {
         cudaFuncSetAttribute(topk_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kTopkMaxSmemKeys * 4 + 8192 * 4 + 16);
+                             kTopkMaxSmemKeys * 4 + kTopkMaxSmemKeys / 8 + 64);
       }
     }
     topk_kernel<true><<<static_cast<unsigned>(batch), kTopkThreads, smem, s>>>(a);
