@@ -121,7 +121,7 @@ extern "C" int v1x_score_fp8(const uint8_t* q, const float* w, const uint8_t* po
   V1X_CHECK_ARG((reinterpret_cast<uintptr_t>(pool) & 15) == 0, "score_fp8: pool must be 16-byte aligned");
   V1X_CHECK_ARG(table_stride >= 0 && impl >= 0 && impl <= 2, "score_fp8: bad table stride / impl");
   if (batch == 0 || max_len == 0) return V1X_OK;
-  const bool tc = impl == 2 || (impl == 0 && heads % 32 == 0);
+  const bool tc = impl == 2 || (impl == 0 && heads % 32 == 0 && heads <= 128);
   if (tc)
     return score_fp8_tc(q, w, pool, pool_pages, lens, table, table_stride, out, out_stride, max_len, page_max,
                         page_stride, heads, relu, clean, batch, status, as_stream(stream));

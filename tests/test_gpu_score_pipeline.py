@@ -70,7 +70,17 @@ def test_score_simt_exact_vs_oracle(H, cuda_dev):
     close(out, O.score_paged(q8, w, pool, table, lens, 1300, exact=False))
 
 
-@pytest.mark.parametrize("H", [32, 64, 128, 256])
+def test_score_tensor_core_rejects_unsupported_heads(cuda_dev):
+    q = torch.zeros((2, 256, 128), dtype=torch.float8_e4m3fn, device="cuda")
+    pool = torch.zeros((4, 8448), dtype=torch.uint8, device="cuda")
+    with pytest.raises(Exception):
+        S.fp8_paged_mqa_logits(q, pool, torch.zeros((2, 256), device="cuda"),
+                               torch.ones(2, dtype=torch.int32, device="cuda"),
+                               torch.zeros((2, 1), dtype=torch.int32, device="cuda"), None, 64,
+                               impl="tensor_core")
+
+
+@pytest.mark.parametrize("H", [32, 64, 96, 128])
 @pytest.mark.parametrize("relu", [True, False])
 def test_score_tensor_core_vs_oracle(H, relu, cuda_dev):
     """tcgen05 scorer: ragged rows (empty, one key, partial tiles, longer than
