@@ -10,20 +10,27 @@
 //
 //   tile = 128 keys (two 64-token pages) of one row; D[128 x H] = K[128 x 128] .
 //   Q[H x 128]^T with tcgen05.mma kind::f8f6f4 (E4M3 x E4M3 -> F32), four K=32
-//   steps, accumulator in TMEM (two accumulators, ping-pong).
+//   steps, accumulator in TMEM (four accumulators in flight).
 //
-// Warp roles in a persistent CTA (192 threads):
-//   warp 0    TMA producer: per tile, two 8 KB page boxes (3-D tensor map over
-//             the packed pool, 128-byte swizzle) + the row's 64x128 q box.
-//   warp 1    TMEM owner + single-thread MMA issuer; commits release the smem
-//             stage and publish the accumulator.
-//   warps 2-5 epilogue: tcgen05.ld of the accumulator (one key per thread),
-//             ReLU, weighted head sum, per-key scale, coalesced store.
-// Tiles (row, 128-key block) are enumerated from a per-row prefix computed in
-// shared memory from the device lengths and dealt round-robin to the CTAs.
-// Every mbarrier wait is bounded (2 s); on timeout the CTA records
-// V1X_STATUS_TIMEOUT, drains what it issued and frees its TMEM before exiting.
+// Warp roles in a persistent CTA (352 threads, two CTAs per SM):
+//   warps 0-1  TMA producers (alternate tiles): two 8 KB page boxes (3-D tensor
+//              map over the packed pool, 128-byte swizzle) and the two pages'
+//              256-byte scale vectors.  Several issuing warps are needed: one
+//              warp sustains only ~4 TMA operations per microsecond.
+//   warp 2     TMEM owner + single-thread MMA issuer; loads the row's q tile
+//              (H x 128) when the row changes; commits release the smem stage
+//              and publish the accumulator.
+//   warps 3-10 two epilogue groups (alternate tiles): tcgen05.ld of the
+//              accumulator (one key per thread), ReLU, weighted head sum with
+//              the head weights staged in smem, per-key scale, coalesced store.
+// Each CTA owns a contiguous range of tiles (row, 128-key block), computed from
+// a per-row tile prefix over the device lengths, so q and the head weights
+// change only at row boundaries.  Every mbarrier wait is bounded (2 s); on
+// timeout the CTA records V1X_STATUS_TIMEOUT, lets what it issued retire and
+// frees its TMEM before exiting.
 #include <cudaTypedefs.h>
+
+#include <algorithm>
 
 #include "common.cuh"
 #include "sm100.cuh"
@@ -33,11 +40,14 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kTcThreads = 320;   // warp 0 TMA, warp 1 MMA, warps 2-5 / 6-9 two epilogue groups
+constexpr int kProducers = 2;                      // TMA issuing warps
+constexpr int kMmaWarp = kProducers;
+constexpr int kEpiWarp0 = kProducers + 1;          // first epilogue warp
+constexpr int kTcThreads = 32 * (kProducers + 1 + 8);
 constexpr int kTcStages = 4;      // key smem stages (2 pages each)
 constexpr int kScaleSlots = 8;    // per-tile key scales (2 x 256 B), consumed by the epilogues
 constexpr int kQSlots = 2;        // per-row q tiles
-constexpr int kMaxAcc = 4;        // TMEM accumulators (epilogue group = acc & 1)
+constexpr int kMaxAcc = 4;        // TMEM accumulators (epilogue group = accumulator & 1)
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 constexpr int kMaxTcRows = 8192;
 
@@ -50,7 +60,7 @@ struct TcArgs {
   int64_t out_stride, max_len;
   float* page_max;
   int64_t page_stride;
-  int B, H, relu, clean;
+  int B, H, relu, clean, w_rows;
   uint32_t tmem_cols;
   int32_t* status;
 };
@@ -108,22 +118,26 @@ struct TileCursor {
       t = 0;
     }
   }
+  __device__ void advance(const int* prefix, int k) {
+    for (int i = 0; i < k; ++i) next(prefix);
+  }
 };
 
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(kTcThreads, 2)
     score_tc_kernel(const __grid_constant__ CUtensorMap pool_map, const __grid_constant__ CUtensorMap q_map,
                     const __grid_constant__ CUtensorMap scale_map, const __grid_constant__ TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t q_bytes = static_cast<uint32_t>(a.H) * 128;
-  uint8_t* stages = base;                                    // kTcStages x 16 KB (A operand)
-  uint8_t* qring = stages + kTcStages * 16384;               // kQSlots x H*128 (B operand)
-  float* sring = reinterpret_cast<float*>(qring + kQSlots * q_bytes);   // kScaleSlots x 128
-  TcShared& sh = *reinterpret_cast<TcShared*>(sring + kScaleSlots * 128);
+  uint8_t* stages = base;                                               // kTcStages x 16 KB (A operand)
+  uint8_t* qring = stages + kTcStages * 16384;                          // kQSlots x H*128 (B operand)
+  float* sring = reinterpret_cast<float*>(qring + kQSlots * q_bytes);   // kScaleSlots x 128 scales
+  float* wsm = sring + kScaleSlots * 128;                               // head weights of this CTA's rows
+  TcShared& sh = *reinterpret_cast<TcShared*>(wsm + a.w_rows * a.H);
   int* prefix = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(&sh) + sizeof(TcShared));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
-  // ---- per-row tile prefix and this CTA's contiguous tile range ---------------
+  // ---- per-row tile prefix and barrier set-up -----------------------------------
   {
     const int chunk = (a.B + kTcThreads - 1) / kTcThreads;
     const int beg = min(tid * chunk, a.B), end = min(beg + chunk, a.B);
@@ -160,7 +174,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       fence_mbar_init();
     }
   }
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     tmem_alloc(&sh.tmem_base, a.tmem_cols);
     tmem_relinquish();
     tc_fence_before();
@@ -176,92 +190,84 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int T0 = min(static_cast<int>(blockIdx.x) * sh.per, sh.total);
   const int T1 = min(T0 + sh.per, sh.total);
   const int ntiles = T1 - T0;
+  // head weights of the rows this CTA's tiles belong to, staged once
+  const int b_first = ntiles > 0 ? locate_row(prefix, a.B, T0) : 0;
+  const int b_last = ntiles > 0 ? locate_row(prefix, a.B, T1 - 1) : -1;
+  const bool w_staged = b_last - b_first + 1 <= a.w_rows;
+  if (w_staged)
+    for (int e = tid; e < (b_last - b_first + 1) * a.H; e += kTcThreads)
+      wsm[e] = a.w[static_cast<int64_t>(b_first) * a.H + e];
+  __syncthreads();
 
-  if (warp == 0) {
-    // ---------------- TMA producer: lanes resolve 32 tiles' pages at once; lanes 0-3 issue ----------------
-    int issued_keys = 0, issued_scales = 0, q_rows = 0, cur_b = -1;
-    bool stop = false;
-    for (int c = 0; c < ntiles && !stop; c += 32) {
-      int bl = 0, p0l = 0, p1l = 0;
-      if (c + lane < ntiles) {
-        const int T = T0 + c + lane;
-        bl = locate_row(prefix, a.B, T);
-        const int t = T - prefix[bl];
-        const int64_t eff = row_eff(a, bl);
-        p0l = a.table[bl * a.table_stride + 2 * t];
-        p1l = (static_cast<int64_t>(2 * t + 1) * 64 < eff) ? a.table[bl * a.table_stride + 2 * t + 1] : p0l;
+  if (warp < kProducers) {
+    // ---------------- TMA producers: warp p issues tiles p, p + kProducers, ... ----------------
+    if (lane == 0) {
+      int last_it = -1;
+      TileCursor cur;
+      if (warp < ntiles) {
+        cur.start(prefix, a.B, T0);
+        cur.advance(prefix, warp);
       }
-      const int n = min(32, ntiles - c);
-      for (int j = 0; j < n; ++j) {
-        const int it = c + j;
-        const int b = __shfl_sync(0xffffffffu, bl, j);
-        const int p0 = __shfl_sync(0xffffffffu, p0l, j);
-        const int p1 = __shfl_sync(0xffffffffu, p1l, j);
+      for (int it = warp; it < ntiles; it += kProducers) {
+        const int b = cur.b, t = cur.t;
+        const int64_t eff = row_eff(a, b);
+        const int p0 = a.table[b * a.table_stride + 2 * t];
+        const int p1 = (static_cast<int64_t>(2 * t + 1) * 64 < eff) ? a.table[b * a.table_stride + 2 * t + 1] : p0;
         const int s = it % kTcStages, r = it % kScaleSlots;
-        int ok = 1;
-        if (lane == 0) {
-          if (b != cur_b) {  // new row: its q tile into the next q slot
-            const int qs = q_rows % kQSlots;
-            ok = mbar_wait(&sh.qempty[qs], ((q_rows / kQSlots) & 1) ^ 1, &sh.abort, kWaitLimitNs);
-            if (ok) {
-              mbar_arrive_expect_tx(&sh.qfull[qs], q_bytes);
-              tma_load_2d(qring + qs * q_bytes, &q_map, &sh.qfull[qs], 0, b * a.H);
-            }
-          }
-          ok = ok && mbar_wait(&sh.empty[s], ((it / kTcStages) & 1) ^ 1, &sh.abort, kWaitLimitNs);
-          ok = ok && mbar_wait(&sh.sempty[r], ((it / kScaleSlots) & 1) ^ 1, &sh.abort, kWaitLimitNs);
-          if (ok) {
-            mbar_arrive_expect_tx(&sh.full[s], 16384);
-            mbar_arrive_expect_tx(&sh.sfull[r], 512);
-          } else {
-            raise_abort(sh, a.status);
-          }
-        }
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) {
-          stop = true;
+        if (!mbar_wait(&sh.empty[s], ((it / kTcStages) & 1) ^ 1, &sh.abort, kWaitLimitNs) ||
+            !mbar_wait(&sh.sempty[r], ((it / kScaleSlots) & 1) ^ 1, &sh.abort, kWaitLimitNs)) {
+          raise_abort(sh, a.status);
           break;
         }
-        if (b != cur_b) {
-          cur_b = b;
-          ++q_rows;
+        mbar_arrive_expect_tx(&sh.full[s], 16384);
+        mbar_arrive_expect_tx(&sh.sfull[r], 512);
+        tma_load_3d(stages + s * 16384, &pool_map, &sh.full[s], 0, 0, p0);
+        tma_load_3d(stages + s * 16384 + 8192, &pool_map, &sh.full[s], 0, 0, p1);
+        tma_load_2d(sring + r * 128, &scale_map, &sh.sfull[r], 0, p0);
+        tma_load_2d(sring + r * 128 + 64, &scale_map, &sh.sfull[r], 0, p1);
+        last_it = it;
+        cur.advance(prefix, kProducers);
+      }
+      if (*reinterpret_cast<volatile int*>(&sh.abort)) {  // let this warp's recent loads land
+        for (int k = 0, it = last_it; k < 4 && it >= 0; ++k, it -= kProducers) {
+          mbar_wait(&sh.full[it % kTcStages], (it / kTcStages) & 1, &sh.zero, kWaitLimitNs);
+          mbar_wait(&sh.sfull[it % kScaleSlots], (it / kScaleSlots) & 1, &sh.zero, kWaitLimitNs);
         }
-        // four TMA issues in parallel, one per lane
-        if (lane == 0) tma_load_3d(stages + s * 16384, &pool_map, &sh.full[s], 0, 0, p0);
-        else if (lane == 1) tma_load_3d(stages + s * 16384 + 8192, &pool_map, &sh.full[s], 0, 0, p1);
-        else if (lane == 2) tma_load_2d(sring + r * 128, &scale_map, &sh.sfull[r], 0, p0);
-        else if (lane == 3) tma_load_2d(sring + r * 128 + 64, &scale_map, &sh.sfull[r], 0, p1);
-        ++issued_keys;
-        ++issued_scales;
-        __syncwarp();
       }
     }
-    if (lane == 0 && *reinterpret_cast<volatile int*>(&sh.abort)) {  // drain what was issued
-      for (int k = max(0, issued_keys - kTcStages); k < issued_keys; ++k)
-        mbar_wait(&sh.full[k % kTcStages], (k / kTcStages) & 1, &sh.zero, kWaitLimitNs);
-      for (int k = max(0, issued_scales - kScaleSlots); k < issued_scales; ++k)
-        mbar_wait(&sh.sfull[k % kScaleSlots], (k / kScaleSlots) & 1, &sh.zero, kWaitLimitNs);
-      for (int k = max(0, q_rows - kQSlots); k < q_rows; ++k)
-        mbar_wait(&sh.qfull[k % kQSlots], (k / kQSlots) & 1, &sh.zero, kWaitLimitNs);
-    }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
+  } else if (warp == kMmaWarp) {
+    // ---------------- MMA issuer (also loads q at row changes) ----------------
     if (lane == 0 && ntiles > 0) {
       const uint32_t idesc = idesc_e4m3_f32(128, a.H);
       TileCursor cur;
       cur.start(prefix, a.B, T0);
       int q_rows = 0, cur_b = -1, it = 0;
+      bool q_pending = false;
       for (; it < ntiles; ++it) {
         const int s = it % kTcStages, acc = it % kMaxAcc;
         if (cur.b != cur_b) {
           if (cur_b >= 0) umma_commit(&sh.qempty[(q_rows - 1) % kQSlots]);  // previous row's q is free
           const int qs = q_rows % kQSlots;
-          if (!mbar_wait(&sh.qfull[qs], (q_rows / kQSlots) & 1, &sh.abort, kWaitLimitNs)) { raise_abort(sh, a.status); break; }
+          if (!mbar_wait(&sh.qempty[qs], ((q_rows / kQSlots) & 1) ^ 1, &sh.abort, kWaitLimitNs)) {
+            raise_abort(sh, a.status);
+            break;
+          }
+          mbar_arrive_expect_tx(&sh.qfull[qs], q_bytes);
+          tma_load_2d(qring + qs * q_bytes, &q_map, &sh.qfull[qs], 0, cur.b * a.H);
+          q_pending = true;
+          if (!mbar_wait(&sh.qfull[qs], (q_rows / kQSlots) & 1, &sh.abort, kWaitLimitNs)) {
+            raise_abort(sh, a.status);
+            break;
+          }
+          q_pending = false;
           cur_b = cur.b;
           ++q_rows;
         }
-        if (!mbar_wait(&sh.tempty[acc], ((it / kMaxAcc) & 1) ^ 1, &sh.abort, kWaitLimitNs)) { raise_abort(sh, a.status); break; }
-        if (!mbar_wait(&sh.full[s], (it / kTcStages) & 1, &sh.abort, kWaitLimitNs)) { raise_abort(sh, a.status); break; }
+        if (!mbar_wait(&sh.tempty[acc], ((it / kMaxAcc) & 1) ^ 1, &sh.abort, kWaitLimitNs) ||
+            !mbar_wait(&sh.full[s], (it / kTcStages) & 1, &sh.abort, kWaitLimitNs)) {
+          raise_abort(sh, a.status);
+          break;
+        }
         tc_fence_after();
         const uint32_t sa = smem_u32(stages + s * 16384);
         const uint32_t sb = smem_u32(qring + ((q_rows - 1) % kQSlots) * q_bytes);
@@ -273,53 +279,55 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         umma_commit(&sh.tfull[acc]);
         cur.next(prefix);
       }
-      if (*reinterpret_cast<volatile int*>(&sh.abort) && it > 0) {  // let issued MMAs retire
-        const int k = it - 1;
-        mbar_wait(&sh.tfull[k % kMaxAcc], (k / kMaxAcc) & 1, &sh.zero, kWaitLimitNs);
+      if (*reinterpret_cast<volatile int*>(&sh.abort)) {  // let issued copies and MMAs retire
+        if (q_pending) mbar_wait(&sh.qfull[q_rows % kQSlots], (q_rows / kQSlots) & 1, &sh.zero, kWaitLimitNs);
+        if (it > 0) mbar_wait(&sh.tfull[(it - 1) % kMaxAcc], ((it - 1) / kMaxAcc) & 1, &sh.zero, kWaitLimitNs);
       }
     }
   } else {
-    // ---------------- epilogue: group g = 0 (warps 2-5) / 1 (warps 6-9), alternate tiles ----------------
-    const int g = (warp - 2) >> 2;
-    const int q4 = warp & 3;
-    const int i = q4 * 32 + lane;                 // row of the 128-key tile == TMEM lane
+    // ---------------- epilogue: group g = 0 (warps 3-6) / 1 (warps 7-10), alternate tiles ----------------
+    const int g = (warp - kEpiWarp0) >> 2;
+    const int q4 = warp & 3;                      // TMEM lane quarter this warp may access
+    const int i = q4 * 32 + lane;                 // key of the 128-key tile == TMEM lane
     TileCursor cur;
     if (ntiles > g) {
       cur.start(prefix, a.B, T0);
-      if (g) cur.next(prefix);
+      cur.advance(prefix, g);
     }
     for (int it = g; it < ntiles; it += 2) {
       const int acc = it % kMaxAcc, r = it % kScaleSlots;
       const int b = cur.b;
       const int64_t eff = row_eff(a, b);
       const int64_t key = static_cast<int64_t>(cur.t) * 128 + i;
-      const float* wg = a.w + static_cast<int64_t>(b) * a.H;   // L1-resident: a CTA's tiles share rows
-      if (!mbar_wait(&sh.sfull[r], (it / kScaleSlots) & 1, &sh.abort, kWaitLimitNs)) { raise_abort(sh, a.status); break; }
+      const float* wr = w_staged ? wsm + (b - b_first) * a.H : a.w + static_cast<int64_t>(b) * a.H;
+      if (!mbar_wait(&sh.sfull[r], (it / kScaleSlots) & 1, &sh.abort, kWaitLimitNs) ||
+          !mbar_wait(&sh.tfull[acc], (it / kMaxAcc) & 1, &sh.abort, kWaitLimitNs)) {
+        raise_abort(sh, a.status);
+        break;
+      }
       const float scale = sring[r * 128 + i];
-      if (!mbar_wait(&sh.tfull[acc], (it / kMaxAcc) & 1, &sh.abort, kWaitLimitNs)) { raise_abort(sh, a.status); break; }
       tc_fence_after();
       float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
-      for (int c0 = 0; c0 < a.H; c0 += 64) {
-        uint32_t v[64];
-        const uint32_t ta = tmem + (static_cast<uint32_t>(q4 * 32) << 16) + static_cast<uint32_t>(acc * a.H + c0);
-        tmem_ld32(ta, *reinterpret_cast<uint32_t(*)[32]>(v));
-        if (c0 + 32 < a.H) tmem_ld32(ta + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+      const uint32_t ta = tmem + (static_cast<uint32_t>(q4 * 32) << 16) + static_cast<uint32_t>(acc * a.H);
+      for (int c0 = 0; c0 < a.H; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(ta + c0, v);
         tmem_ld_wait();
-        const int ncol = min(64, a.H - c0);
 #pragma unroll
-        for (int j = 0; j < 64; j += 4) {
-          if (j < ncol) {
-            const float4 w4 = __ldg(reinterpret_cast<const float4*>(wg + c0 + j));
-            float v0 = __uint_as_float(v[j]), v1 = __uint_as_float(v[j + 1]);
-            float v2 = __uint_as_float(v[j + 2]), v3 = __uint_as_float(v[j + 3]);
-            if (a.relu) {
-              v0 = fmaxf(v0, 0.0f); v1 = fmaxf(v1, 0.0f); v2 = fmaxf(v2, 0.0f); v3 = fmaxf(v3, 0.0f);
-            }
-            s0 = fmaf(w4.x, v0, s0);
-            s1 = fmaf(w4.y, v1, s1);
-            s2 = fmaf(w4.z, v2, s2);
-            s3 = fmaf(w4.w, v3, s3);
+        for (int j = 0; j < 32; j += 4) {
+          const float4 w4 = *reinterpret_cast<const float4*>(wr + c0 + j);
+          float v0 = __uint_as_float(v[j]), v1 = __uint_as_float(v[j + 1]);
+          float v2 = __uint_as_float(v[j + 2]), v3 = __uint_as_float(v[j + 3]);
+          if (a.relu) {
+            v0 = fmaxf(v0, 0.0f);
+            v1 = fmaxf(v1, 0.0f);
+            v2 = fmaxf(v2, 0.0f);
+            v3 = fmaxf(v3, 0.0f);
           }
+          s0 = fmaf(w4.x, v0, s0);
+          s1 = fmaf(w4.y, v1, s1);
+          s2 = fmaf(w4.z, v2, s2);
+          s3 = fmaf(w4.w, v3, s3);
         }
       }
       tc_fence_before();
@@ -335,11 +343,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
         if ((lane & 7) == 0 && key < a.max_len) a.page_max[b * a.page_stride + (key >> 3)] = m;
       }
-      cur.next(prefix);
-      cur.next(prefix);
+      cur.advance(prefix, 2);
     }
     // columns past the last tile: -inf logits (clean) and -inf page maxima (always)
-    const int e = tid - 64;   // 0..255 across both groups
+    const int e = tid - 32 * kEpiWarp0;   // 0..255 across both groups
     for (int b = blockIdx.x; b < a.B; b += gridDim.x) {
       const int64_t eff = row_eff(a, b);
       const int64_t start = eff > 0 ? (eff + 127) / 128 * 128 : 0;
@@ -351,7 +358,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   }
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, a.tmem_cols);
   }
@@ -367,6 +374,21 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
       fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
   }
   return fn;
+}
+
+int encode(PFN_cuTensorMapEncodeTiled_v12000 enc, CUtensorMap* m, CUtensorMapDataType type, int rank, const void* ptr,
+           const cuuint64_t* dims, const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle swz,
+           const char* what) {
+  const cuuint32_t es[3] = {1, 1, 1};
+  const CUresult r = enc(m, type, rank, const_cast<void*>(ptr), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         swz, swz == CU_TENSOR_MAP_SWIZZLE_NONE ? CU_TENSOR_MAP_L2_PROMOTION_NONE
+                                                                : CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("score_fp8: %s tensor map encode failed (%d)", what, static_cast<int>(r));
+    return V1X_ERR_CUDA;
+  }
+  return V1X_OK;
 }
 
 }  // namespace
@@ -391,67 +413,60 @@ int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t 
   }
   CUtensorMap pool_map, q_map, scale_map;
   {
-    cuuint64_t dims[3] = {128, 64, static_cast<cuuint64_t>(pool_pages)};
-    cuuint64_t strides[2] = {128, static_cast<cuuint64_t>(kPageBytes)};
-    cuuint32_t box[3] = {128, 64, 1};
-    cuuint32_t es[3] = {1, 1, 1};
-    CUresult r = enc(&pool_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(pool), dims, strides, box, es,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) {
-      set_error("score_fp8: pool tensor map encode failed (%d)", static_cast<int>(r));
-      return V1X_ERR_CUDA;
-    }
+    // keys: {128 bytes, 64 tokens, pages}, one page per box, 128-byte swizzle
+    const cuuint64_t dims[3] = {128, 64, static_cast<cuuint64_t>(pool_pages)};
+    const cuuint64_t strides[2] = {128, static_cast<cuuint64_t>(kPageBytes)};
+    const cuuint32_t box[3] = {128, 64, 1};
+    if (int rc = encode(enc, &pool_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, pool, dims, strides, box,
+                        CU_TENSOR_MAP_SWIZZLE_128B, "pool"))
+      return rc;
   }
   {
-    cuuint64_t dims[2] = {128, static_cast<cuuint64_t>(batch * heads)};
-    cuuint64_t strides[1] = {128};
-    cuuint32_t box[2] = {128, static_cast<cuuint32_t>(heads)};
-    cuuint32_t es[2] = {1, 1};
-    CUresult r = enc(&q_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(q), dims, strides, box, es,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) {
-      set_error("score_fp8: q tensor map encode failed (%d)", static_cast<int>(r));
-      return V1X_ERR_CUDA;
-    }
+    // q: {128 bytes, batch*heads rows}, one row's H heads per box
+    const cuuint64_t dims[2] = {128, static_cast<cuuint64_t>(batch * heads)};
+    const cuuint64_t strides[1] = {128};
+    const cuuint32_t box[2] = {128, static_cast<cuuint32_t>(heads)};
+    if (int rc = encode(enc, &q_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, q, dims, strides, box,
+                        CU_TENSOR_MAP_SWIZZLE_128B, "q"))
+      return rc;
   }
   {
     // the 64 fp32 scales of each page: 256 contiguous bytes at page + 8192
-    cuuint64_t dims[2] = {64, static_cast<cuuint64_t>(pool_pages)};
-    cuuint64_t strides[1] = {static_cast<cuuint64_t>(kPageBytes)};
-    cuuint32_t box[2] = {64, 1};
-    cuuint32_t es[2] = {1, 1};
-    CUresult r = enc(&scale_map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<uint8_t*>(pool) + kKeyBytes, dims,
-                     strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                     CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) {
-      set_error("score_fp8: scale tensor map encode failed (%d)", static_cast<int>(r));
-      return V1X_ERR_CUDA;
-    }
+    const cuuint64_t dims[2] = {64, static_cast<cuuint64_t>(pool_pages)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kPageBytes)};
+    const cuuint32_t box[2] = {64, 1};
+    if (int rc = encode(enc, &scale_map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, pool + kKeyBytes, dims, strides, box,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, "scale"))
+      return rc;
   }
-  const int nacc = kMaxAcc;
   uint32_t cols = 32;
-  while (cols < static_cast<uint32_t>(nacc * heads)) cols <<= 1;
-  if (cols > 512) {
-    set_error("score_fp8 (tensor core): heads > 128 not supported");
-    return V1X_ERR_UNSUPPORTED;
+  while (cols < static_cast<uint32_t>(kMaxAcc * heads)) cols <<= 1;
+  const int64_t max_tiles = batch * ((max_len + 127) / 128);
+  const int64_t sms = num_sms();
+  // head-weight rows staged per CTA: a range of ceil(total/grid) tiles touches at
+  // most that many rows plus one (a range that also spans rows without tiles
+  // falls back to global reads inside the kernel)
+  auto plan = [&](int64_t grid, int64_t& w_rows) {
+    w_rows = std::min<int64_t>(batch, (std::max<int64_t>(max_tiles, 1) + grid - 1) / grid + 1);
+    return static_cast<size_t>(1024 + kTcStages * 16384 + kQSlots * heads * 128 + kScaleSlots * 512 +
+                               w_rows * heads * 4 + sizeof(TcShared) + (batch + 1) * 4 + 16);
+  };
+  int64_t grid = std::min<int64_t>(sms * 2, std::max<int64_t>(max_tiles, 1)), w_rows = 0;
+  size_t smem = plan(grid, w_rows);
+  if (cols > 256 || smem > 113 * 1024) {  // two CTAs per SM need <= 256 TMEM columns and <= 113 KB each
+    grid = std::min<int64_t>(sms, std::max<int64_t>(max_tiles, 1));
+    smem = plan(grid, w_rows);
   }
-  TcArgs args{lens, table, table_stride, w, out, out_stride, max_len, page_max, page_stride,
-              static_cast<int>(batch), static_cast<int>(heads), relu, clean, cols, status};
-  const size_t smem = 1024 + kTcStages * 16384 + kQSlots * heads * 128 + kScaleSlots * 512 + sizeof(TcShared) +
-                      (batch + 1) * 4 + 16;
-  static DeviceOnce once;
-  if (once.first())
-    cudaFuncSetAttribute(score_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   if (smem > 227 * 1024) {
     set_error("score_fp8 (tensor core): shared memory %zu too large", smem);
     return V1X_ERR_UNSUPPORTED;
   }
-  const int64_t max_tiles = batch * ((max_len + 127) / 128);
-  const int per_sm = (cols <= 256 && smem <= 113 * 1024) ? 2 : 1;  // TMEM and smem both allow two
-  int64_t grid = static_cast<int64_t>(num_sms()) * per_sm;
-  if (grid > max_tiles) grid = max_tiles > 0 ? max_tiles : 1;
+  TcArgs args{lens, table, table_stride, w, out, out_stride, max_len, page_max, page_stride,
+              static_cast<int>(batch), static_cast<int>(heads), relu, clean, static_cast<int>(w_rows), cols,
+              status};
+  static DeviceOnce once;
+  if (once.first())
+    cudaFuncSetAttribute(score_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   score_tc_kernel<<<static_cast<unsigned>(grid), kTcThreads, smem, stream>>>(pool_map, q_map, scale_map, args);
   return launch_status("v1x_score_fp8 (tensor core)");
 }
