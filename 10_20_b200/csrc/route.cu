@@ -7,15 +7,19 @@
 // (descending, stable); a slot's stable position is its blocked rank
 //   rank(p) = (p % 128) * BASE + p / 128,  BASE = THREADS*ITEMS / 128,
 // and CUB folds -0.0 onto +0.0.  Here the same total order -- key desc, blocked
-// rank asc -- is produced by an exact radix select of the K-th key followed by a
-// bitonic sort of only the K selected (key, rank) pairs.
+// rank asc -- is produced by an exact search for the K-th key (select.cuh)
+// followed by ordering only the winners.
 #include "common.cuh"
+#include "select.cuh"
 
 namespace v1x {
 namespace {
 
 constexpr int kRouteThreads = 256;
+constexpr int kRouteWarps = kRouteThreads / 32;
 constexpr int kRouteMaxItems = 4096;
+constexpr int kRoutePer = kRouteMaxItems / kRouteThreads;  // page keys per thread
+constexpr int kRankDirect = 256;  // winner lists up to this size are ordered by counting
 
 struct RouteArgs {
   const float* scores;
@@ -33,14 +37,17 @@ struct RouteArgs {
   int64_t capacity;
   int fill_table;
   int n_items, base;  // padded slot count (THREADS*ITEMS) and BASE
+  int stage_rt;       // the row's rt entries are copied to shared memory up front
 };
 
 struct RouteSmem {
-  uint32_t keys[kRouteMaxItems];
-  unsigned long long list[kRouteMaxItems];
-  int hist[256];
-  int warp_tot[kRouteThreads / 32 + 1];
-  int digit, need;
+  unsigned long long list[kRouteMaxItems];  // winners as (key << 32) | ~rank
+  int rt[kRouteMaxItems];                   // the row's reordered-page table (stage_rt)
+  int hist[kBins];
+  int4 red[2 * kRouteWarps];
+  int warp_tot[kRouteWarps + 1];
+  int4 res;
+  int count;
 };
 
 __device__ __forceinline__ void store_sel(const RouteArgs& a, int64_t i, int64_t v) {
@@ -48,12 +55,30 @@ __device__ __forceinline__ void store_sel(const RouteArgs& a, int64_t i, int64_t
   else static_cast<int32_t*>(a.selected)[i] = static_cast<int32_t>(v);
 }
 
+__device__ __forceinline__ void cp_async4(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
+               "l"(gsrc)
+               : "memory");
+}
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
+               "l"(gsrc)
+               : "memory");
+}
+
 // kPages: `scores` already holds one value per page (the max of its 8 centres).
+//
+// Thread t owns pages p = t + j*256 (coalesced loads); the tie order of a page
+// is its blocked rank, computed from p.  The want-th largest key comes from the
+// bitwise search; the winners (keys above it and all keys equal to it) are then
+// ordered by (key desc, rank asc) by counting, or by a bitonic sort when ties
+// make the list long.
 template <bool kPages>
-__global__ void __launch_bounds__(kRouteThreads) route_kernel(const __grid_constant__ RouteArgs a) {
+__global__ void __launch_bounds__(kRouteThreads, 1) route_kernel(const __grid_constant__ RouteArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   RouteSmem& sm = *reinterpret_cast<RouteSmem*>(smem_raw);
-  const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x, nt = kRouteThreads;
   const int64_t row = blockIdx.x;
   const int n = a.lens[row];
   const int take = a.takes[row];
@@ -70,136 +95,110 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const __grid_const
     }
     return;
   }
-  // ---- page keys in blocked-rank order (VQ:26-41) ----------------------------
-  // All loads of a thread are issued before any is consumed (a loop that stores
-  // each load's result before the next load would serialise the latencies).
-  const int act = static_cast<int>(min(static_cast<int64_t>(active), kPages ? a.score_cols : a.score_cols / 8));
-  const float* srow = a.scores + row * a.score_stride;
-  if (kPages) {
-    // stage the row's page scores in smem (reusing the sort list), coalesced
-    float* ps = reinterpret_cast<float*>(sm.list);
-    const bool vec = (reinterpret_cast<uintptr_t>(srow) & 15) == 0;
-    const int nv = vec ? act >> 2 : 0;
-    for (int v = tid; v < nv; v += nt) reinterpret_cast<float4*>(ps)[v] = reinterpret_cast<const float4*>(srow)[v];
-    for (int p = nv * 4 + tid; p < act; p += nt) ps[p] = srow[p];
-    __syncthreads();
-    for (int r = tid; r < a.n_items; r += nt) {
-      const int p = r / a.base + (r % a.base) * 128;
-      sm.keys[r] = order_key(p < act ? ps[p] : -CUDART_INF_F);
-    }
-  } else {
-    const bool vec = (reinterpret_cast<uintptr_t>(srow) & 15) == 0;
-    constexpr int kBatch = 4;
-    for (int r0 = tid; r0 < a.n_items; r0 += nt * kBatch) {
-      float4 x[kBatch], y[kBatch];
-#pragma unroll
-      for (int u = 0; u < kBatch; ++u) {
-        const int r = r0 + u * nt;
-        const int p = r / a.base + (r % a.base) * 128;
-        x[u] = y[u] = make_float4(-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F);
-        if (r < a.n_items && p < act) {
-          const float* sp = srow + static_cast<int64_t>(p) * 8;
-          if (vec) {
-            x[u] = reinterpret_cast<const float4*>(sp)[0];
-            y[u] = reinterpret_cast<const float4*>(sp)[1];
-          } else {
-            x[u] = make_float4(sp[0], sp[1], sp[2], sp[3]);
-            y[u] = make_float4(sp[4], sp[5], sp[6], sp[7]);
-          }
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < kBatch; ++u) {
-        const int r = r0 + u * nt;
-        if (r < a.n_items) {
-          const float best = fmaxf(fmaxf(fmaxf(x[u].x, x[u].y), fmaxf(x[u].z, x[u].w)),
-                                   fmaxf(fmaxf(y[u].x, y[u].y), fmaxf(y[u].z, y[u].w)));
-          sm.keys[r] = order_key(best);
-        }
-      }
-    }
-  }
   // number of ranks the output needs: selected (take_stride) and ft (take)
   const int want = static_cast<int>(min(static_cast<int64_t>(a.n_items),
       max(a.take_stride, a.fill_table ? min(static_cast<int64_t>(take), a.fine_pages) : int64_t(0))));
-  // ---- radix select of the want-th largest key ---------------------------------
-  uint32_t prefix = 0, known = 0;
-  int need = want;
-  for (int pass = 0; pass < 4 && want > 0; ++pass) {
-    const int shift = 24 - 8 * pass;
-    for (int b = tid; b < 256; b += nt) sm.hist[b] = 0;
-    __syncthreads();
-    const int iters = (a.n_items + nt - 1) / nt;
-    for (int j = 0; j < iters; ++j) {
-      const int r = j * nt + tid;
-      int bin = -1;
-      if (r < a.n_items) {
-        const uint32_t k = sm.keys[r];
-        if ((k & known) == prefix) bin = (k >> shift) & 255;
-      }
-      const unsigned same = __match_any_sync(0xffffffffu, bin);
-      if (bin >= 0 && lane == __ffs(same) - 1) atomicAdd(&sm.hist[bin], __popc(same));
+  if (want <= 0) return;
+  const int32_t* rtrow = a.rt + row * a.pages;
+  if (a.stage_rt) {  // overlaps the selection below
+    if ((reinterpret_cast<uintptr_t>(rtrow) & 15) == 0 && (a.pages & 3) == 0) {
+      for (int v = tid; v < (a.pages >> 2); v += nt) cp_async16(sm.rt + 4 * v, rtrow + 4 * v);
+    } else {
+      for (int v = tid; v < a.pages; v += nt) cp_async4(sm.rt + v, rtrow + v);
     }
-    __syncthreads();
-    if (warp == 0) {
-      int cnt[8], s = 0;
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  if (tid == 0) sm.count = 0;
+  // ---- page keys (VQ:26-41): p < act -> key of the page's max centre, else -inf
+  const int act = static_cast<int>(min(static_cast<int64_t>(active), kPages ? a.score_cols : a.score_cols / 8));
+  const float* srow = a.scores + row * a.score_stride;
+  uint32_t kr[kRoutePer];
+  float x[kRoutePer];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        cnt[j] = sm.hist[255 - (lane * 8 + j)];
-        s += cnt[j];
-      }
-      int cum = warp_inclusive_scan(s) - s;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if (cum < need && cum + cnt[j] >= need) {
-          sm.digit = 255 - (lane * 8 + j);
-          sm.need = need - cum;
+  for (int j = 0; j < kRoutePer; ++j) {
+    const int p = tid + j * nt;
+    x[j] = -CUDART_INF_F;
+    if (p < act) {
+      if (kPages) {
+        x[j] = srow[p];
+      } else {
+        const float* sp = srow + static_cast<int64_t>(p) * 8;
+        float4 u, w;
+        if ((reinterpret_cast<uintptr_t>(srow) & 15) == 0) {
+          u = reinterpret_cast<const float4*>(sp)[0];
+          w = reinterpret_cast<const float4*>(sp)[1];
+        } else {
+          u = make_float4(sp[0], sp[1], sp[2], sp[3]);
+          w = make_float4(sp[4], sp[5], sp[6], sp[7]);
         }
-        cum += cnt[j];
+        x[j] = fmaxf(fmaxf(fmaxf(u.x, u.y), fmaxf(u.z, u.w)), fmaxf(fmaxf(w.x, w.y), fmaxf(w.z, w.w)));
       }
     }
-    __syncthreads();
-    prefix |= static_cast<uint32_t>(sm.digit) << shift;
-    known |= 255u << shift;
-    need = sm.need;
-    __syncthreads();
   }
-  const uint32_t thr = prefix;
-  // ---- gather the `want` winners (ties: lowest blocked rank) --------------------
-  const int chunk = (a.n_items + nt - 1) / nt;
-  const int beg = min(tid * chunk, a.n_items), end = min(beg + chunk, a.n_items);
-  int eq = 0, gt = 0;
-  for (int r = beg; r < end; ++r) {
-    eq += sm.keys[r] == thr;
-    gt += sm.keys[r] > thr;
-  }
-  int tot;
-  const int eq_before = block_exclusive_scan(eq, sm.warp_tot, &tot);
-  const int take_eq = min(max(need - eq_before, 0), eq);
-  int pos = block_exclusive_scan(gt + take_eq, sm.warp_tot, &tot);
-  int eq_seen = eq_before;
-  for (int r = beg; r < end; ++r) {
-    const uint32_t k = sm.keys[r];
-    bool sel = k > thr;
-    if (k == thr) {
-      sel = eq_seen < need;
-      ++eq_seen;
-    }
-    if (sel && pos < want)
-      sm.list[pos++] = (static_cast<unsigned long long>(k) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(r));
-  }
-  // pad to a power of two with the smallest composite, then sort descending
-  int m = 1;
-  while (m < want) m <<= 1;
-  for (int i = want + tid; i < m; i += nt) sm.list[i] = 0ull;
+  const int nv = a.n_items > tid ? (a.n_items - tid + nt - 1) / nt : 0;  // pages of this thread
+#pragma unroll
+  for (int j = 0; j < kRoutePer; ++j) kr[j] = order_key(x[j]);
+  // ---- winners: a 12-bit histogram finds the bin of the want-th key; every key
+  // in that bin or above is a winner candidate.  When ties make that list long,
+  // the exact want-th key from the bitwise search bounds it instead.
+  zero_hist<kRouteThreads>(sm.hist);
   __syncthreads();
-  bitonic_sort_desc(sm.list, m);
-  for (int i = tid; i < want; i += nt) {
-    const int r = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(sm.list[i] & 0xFFFFFFFFull));
+#pragma unroll
+  for (int j = 0; j < kRoutePer; ++j)
+    if (j < nv) atomicAdd(&sm.hist[bin_of(kr[j])], 1);
+  __syncthreads();
+  const TopBin tb = find_top_bin<kRouteThreads>(want, sm.hist, sm.warp_tot, &sm.res);
+  uint32_t lo = static_cast<uint32_t>(tb.bin) << (32 - kBinBits);
+  if (tb.above + tb.in > kRankDirect) {
+    int gt = 0;
+    lo = block_kth_largest<kRouteWarps>(
+        want,
+        [&](uint32_t c1, uint32_t c2, uint32_t c3, int& n1, int& n2, int& n3) {
+          n1 = n2 = n3 = 0;
+#pragma unroll
+          for (int j = 0; j < kRoutePer; ++j) {
+            if (j < nv) {
+              n1 += kr[j] >= c1;
+              n2 += kr[j] >= c2;
+              n3 += kr[j] >= c3;
+            }
+          }
+        },
+        sm.red, &gt);
+  }
+#pragma unroll
+  for (int j = 0; j < kRoutePer; ++j) {
+    if (j < nv && kr[j] >= lo) {
+      const int p = tid + j * nt;
+      const uint32_t rank = static_cast<uint32_t>((p & 127) * a.base + (p >> 7));
+      const int e = atomicAdd(&sm.count, 1);
+      sm.list[e] = (static_cast<unsigned long long>(kr[j]) << 32) | (0xFFFFFFFFu - rank);
+    }
+  }
+  if (a.stage_rt) asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncthreads();
+  const int m = sm.count;
+  auto emit = [&](int pos, unsigned long long comp) {
+    const int r = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(comp & 0xFFFFFFFFull));
     const int p = r / a.base + (r % a.base) * 128;
-    if (i < a.take_stride) store_sel(a, row * a.take_stride + i, p);
-    if (a.fill_table && i < take && i < a.fine_pages)
-      a.ft[row * a.fine_pages + i] = p < a.pages ? a.rt[row * a.pages + p] : -1;
+    if (pos < a.take_stride) store_sel(a, row * a.take_stride + pos, p);
+    if (a.fill_table && pos < take && pos < a.fine_pages)
+      a.ft[row * a.fine_pages + pos] = p < a.pages ? (a.stage_rt ? sm.rt[p] : rtrow[p]) : -1;
+  };
+  if (m <= kRankDirect) {
+    // composites are unique: a winner's position is the number of larger ones
+    for (int e = tid; e < m; e += nt) {
+      const unsigned long long c = sm.list[e];
+      int pos = 0;
+      for (int f = 0; f < m; ++f) pos += sm.list[f] > c;
+      if (pos < want) emit(pos, c);
+    }
+  } else {
+    int mp = 1;
+    while (mp < m) mp <<= 1;
+    for (int i = m + tid; i < mp; i += nt) sm.list[i] = 0ull;
+    bitonic_sort_desc(sm.list, mp);
+    for (int i = tid; i < want; i += nt) emit(i, sm.list[i]);
   }
 }
 
@@ -222,7 +221,8 @@ int route_launch(bool pages_in, const float* scores, int64_t score_stride, int64
   const int n_items = threads * items;
   RouteArgs a{scores, score_stride, score_cols, lens, takes, selected, selected_is_i64,
               take_stride, static_cast<int>(pages), rt, ft, fine_pages, tail_rows, capacity,
-              fill_table, n_items, n_items / 128};
+              fill_table, n_items, n_items / 128,
+              fill_table && pages <= kRouteMaxItems ? 1 : 0};
   const size_t smem = sizeof(RouteSmem);
   static DeviceOnce once;
   if (once.first()) {

@@ -1,4 +1,4 @@
-// fused.topk for sm_100a: in-place boundary mask + exact Top-T radix select +
+// fused.topk for sm_100a: in-place boundary mask + exact Top-T selection +
 // raw -> logical -> physical mapping (+ optional x4 expansion), one CTA per row.
 //
 // Reference behaviour: sglang/kernels/jit/csrc/deepseek_v4/v1_query.cuh:62-153
@@ -8,21 +8,39 @@
 // shared-memory atomic order (topk_impl.cuh:400-401).  Outputs are written in
 // ascending raw-index order (the reference leaves the order unspecified).
 //
-// Design: the row's candidate scores are staged once in shared memory as
-// order-preserving uint32 keys; four 8-bit radix passes (warp-aggregated
-// histogram atomics) find the exact T-th key and how many of its ties to keep;
-// two block scans then place every selected candidate at its output slot in
-// index order, and the selecting thread performs the mapping epilogue itself.
+// Design (one CTA of 512 threads per row):
+//   1. cp.async copies of the row's scores, its native-table row and the 64
+//      members of every selected rank's page into shared memory, overlapping
+//      the dependent selected -> rt loads that find those pages;
+//   2. one pass turns the scores into order-preserving keys and applies the
+//      boundary-bucket mask (global -inf write + key) from the staged members;
+//   3. the exact T-th key comes from the bitwise search of select.cuh;
+//   4. warp ballots + one scan over (slice, warp) counts give every selected
+//      candidate its output slot in index order, and the selecting thread maps
+//      raw -> logical -> physical from shared memory and stores the outputs.
+// Rows whose scores do not fit in shared memory read them from global memory
+// at every step (same results, slower).
 #include <algorithm>
 
 #include "common.cuh"
+#include "select.cuh"
 
 namespace v1x {
 namespace {
 
 constexpr int kTopkThreads = 512;
+constexpr int kTopkWarps = kTopkThreads / 32;
 constexpr int kTopkMaxSmemKeys = 48 * 1024;  // 192 KB of staged keys per CTA
 constexpr uint32_t kNegInfKey = 0x007FFFFFu;  // order_key(-inf)
+constexpr int kRankCache = kTopkMaxSmemKeys / 64;  // ranks whose page ids live in smem
+constexpr int kStageTake = 128;    // ranks whose 64 members are staged (32 KB)
+constexpr int kStageNt = 4096;     // native-table entries staged (16 KB)
+constexpr int kRegKeys = 16;       // keys per thread kept in registers (cols <= 8192)
+constexpr int kMaxSlices = kTopkMaxSmemKeys / kTopkThreads;
+constexpr int kMaskQueue = 256;
+constexpr int kMaxBin = 2048;      // threshold-bin keys resolved exactly (else bitwise search)
+constexpr int kSmallBin = 96;      // bins up to this size are ranked pairwise directly
+constexpr int kMaxBin2 = 256;      // second-level bin size limit
 
 struct TopkArgs {
   float* scores;
@@ -48,6 +66,8 @@ struct TopkArgs {
   const int32_t* fine_table;
   int64_t fine_table_cols;
   int direct_fine;
+  // shared-memory staging plan (staged modes): word offsets in the dynamic area
+  int stage_take, stage_nt, memb_off, ntab_off;
 };
 
 struct RowCtx {
@@ -55,18 +75,41 @@ struct RowCtx {
   int n, take, sink, tail, L;
 };
 
-constexpr int kPageCache = 256;   // page ids of the first 256 selected ranks, cached in smem
-constexpr int kMaxTopk = 2048;
-
 struct TopkSmem {
-  int hist[256];
-  int warp_tot[kTopkThreads / 32 + 1];
-  int digit, need;
-  int nbnd;
-  int pgc[kPageCache];
-  int2 bnd[kPageCache];            // (rank index, reordered page) of boundary buckets
-  int rawbuf[kMaxTopk];            // selected raw candidate ids in output order
+  int pgc[kRankCache];              // page of rank r used for the mapping
+  int rpg[kRankCache];              // reordered page of rank r used for the mask
+  uint8_t bflag[kRankCache];        // rank r < take is a boundary bucket
+  union {
+    struct {
+      int hist[kBins];              // coarse histogram (selection step 1)
+      int2 bnd[kMaskQueue];         // boundary queue of the unstaged mode
+    } h;
+    struct {
+      int2 cand[kMaxBin];           // keys + indices of the threshold bin
+      int2 cnt[kMaxSlices * kTopkWarps];  // per (slice, warp) counts, then their scan
+    } c;
+  } u;
+  uint32_t selbit[kTopkMaxSmemKeys / 32];  // threshold-bin keys that are selected
+  int hist2[256];                   // second level over the threshold bin
+  int2 cand2[kMaxBin2];
+  int warp_tot[kTopkWarps + 1];
+  int4 red[2 * kTopkWarps];
+  int4 res, res2;
+  int2 carry;
+  int nbnd, ncand, ncand2;
 };
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
+               "l"(gsrc)
+               : "memory");
+}
+
+__device__ __forceinline__ void cp_async4(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
+               "l"(gsrc)
+               : "memory");
+}
 
 // Page holding raw candidate r*64+x (r < take): the fine table's entry (direct)
 // or the reordered page of the r-th selected rank (VQ:124-132).
@@ -81,134 +124,35 @@ __device__ __forceinline__ int64_t page_of_rank(const TopkArgs& a, const RowCtx&
   return page;
 }
 
-// Members of the boundary bucket page `page` outside [sink, tail) -> -inf, in
-// global memory and in the staged-key bitmap (VQ:94-103).
-__device__ __forceinline__ void mask_page(const TopkArgs& a, const RowCtx& c, float* srow, uint32_t* bitmap,
-                                          int r, int64_t page, int lane_lo, int lane_step) {
+// Members of the boundary bucket page `page` outside [sink, tail) -> -inf in
+// global memory (VQ:94-103); unstaged mode only.
+__device__ __forceinline__ void mask_page(const TopkArgs& a, const RowCtx& c, float* srow, int r, int64_t page,
+                                          int lane_lo, int lane_step) {
   for (int off = lane_lo; off < 64; off += lane_step) {
     const int lg = a.members[page * 64 + off];
     const int64_t col = static_cast<int64_t>(r) * 64 + off;
-    if ((lg < c.sink || lg >= c.tail) && col < a.cols) {
-      srow[col] = -CUDART_INF_F;
-      if (bitmap) atomicOr(&bitmap[col >> 5], 1u << (col & 31));
-    }
+    if ((lg < c.sink || lg >= c.tail) && col < a.cols) srow[col] = -CUDART_INF_F;
   }
 }
 
-// Selected ranks: every thread resolves its own ranks (selected -> reordered
-// page, and the bucket identity) so the loads of all ranks are in flight at
-// once; pages are cached for the epilogue and boundary buckets are queued.
-// Then one warp per boundary page masks its members (VQ:71-107).
-__device__ void ranks_and_mask(const TopkArgs& a, const RowCtx& c, float* srow, TopkSmem& sm, uint32_t* bitmap) {
-  const int tid = threadIdx.x, nt = blockDim.x;
-  const int lane = tid & 31, warp = tid >> 5, nw = nt >> 5;
-  for (int r = tid; r < c.take; r += nt) {
-    int64_t rank = -1, rpage = -1;
-    if (r < a.take_stride) rank = load_index(a.selected, a.sel64, c.row * a.take_stride + r);
-    const bool rank_ok = rank >= 0 && rank < a.pages;
-    if (rank_ok) rpage = a.rt[c.row * a.pages + rank];
-    const int64_t epage =
-        a.direct_fine ? (r < a.fine_table_cols ? a.fine_table[c.row * a.fine_table_cols + r] : -1) : rpage;
-    if (r < kPageCache) sm.pgc[r] = static_cast<int>(epage);
-    if (!a.mask || !rank_ok || rpage < 0 || rpage >= a.member_rows) continue;
-    const int bucket = a.bucket_from_rank ? static_cast<int>(rank / 16) * 1024 : (a.members[rpage * 64] / 1024) * 1024;
-    if (bucket < c.sink || bucket + 1024 > c.tail) {
-      const int k = atomicAdd(&sm.nbnd, 1);
-      if (k < kPageCache) sm.bnd[k] = make_int2(r, static_cast<int>(rpage));
-      else mask_page(a, c, srow, bitmap, r, rpage, 0, 1);   // queue full: this thread masks it
-    }
-  }
-  __syncthreads();
-  const int nb = min(sm.nbnd, kPageCache);
-  for (int k = warp; k < nb; k += nw) mask_page(a, c, srow, bitmap, sm.bnd[k].x, sm.bnd[k].y, lane, 32);
-}
-
-// Mapping epilogue for output slots tid, tid+nt, ... (VQ:121-148).  Each
-// thread issues the loads of all its slots before consuming any of them.
-template <bool kStaged>
-__device__ void emit_all(const TopkArgs& a, const RowCtx& c, const TopkSmem& sm, const uint32_t* keys,
-                         const float* srow) {
-  constexpr int kPer = (kMaxTopk + kTopkThreads - 1) / kTopkThreads;
-  const int tid = threadIdx.x, nt = blockDim.x;
-  int raw[kPer], lg[kPer];
-  bool live[kPer];
-#pragma unroll
-  for (int k = 0; k < kPer; ++k) {
-    const int t = tid + k * nt;
-    raw[k] = t < a.topk ? sm.rawbuf[t] : -1;
-    live[k] = false;
-    if (raw[k] >= 0 && raw[k] < c.L) {
-      if constexpr (kStaged) live[k] = keys[raw[k]] != kNegInfKey;
-      else live[k] = srow[raw[k]] != -CUDART_INF_F;
-    }
-  }
-  // raw -> logical (members load for reordered candidates)
-#pragma unroll
-  for (int k = 0; k < kPer; ++k) {
-    lg[k] = -1;
-    if (!live[k]) continue;
-    const int x = raw[k];
-    if (x < c.take * 64) {
-      const int r = x >> 6;
-      const int64_t page = r < kPageCache ? sm.pgc[r] : page_of_rank(a, c, r);
-      if (page >= 0 && page < a.member_rows) lg[k] = a.members[page * 64 + (x & 63)];
-    } else {
-      const int off = x - c.take * 64;
-      lg[k] = off < c.sink ? off : c.tail + off - c.sink;
-    }
-  }
-  // logical -> physical (current native table) and stores
-  int ph[kPer];
-#pragma unroll
-  for (int k = 0; k < kPer; ++k) {
-    ph[k] = -1;
-    if (!(lg[k] >= 0 && lg[k] < c.n)) {
-      lg[k] = -1;
-      continue;
-    }
-    if (a.physical_output) {
-      const int64_t p = lg[k] >> 6;
-      ph[k] = p < a.pages ? a.nt[c.row * a.pages + p] * 64 + (lg[k] & 63) : -1;
-    }
-  }
-#pragma unroll
-  for (int k = 0; k < kPer; ++k) {
-    const int t = tid + k * nt;
-    if (t >= a.topk) continue;
-    const int64_t dst = c.row * a.topk + t;
-    a.logical[dst] = lg[k];
-    if (a.physical_output) {
-      a.physical[dst] = ph[k];
-      a.raw[dst] = raw[k];
-    }
-    if (a.expansion_stride) {
-      const int b = lg[k] * 4;
-      reinterpret_cast<int4*>(a.expanded + c.row * a.expansion_stride)[t] =
-          lg[k] < 0 ? make_int4(-1, -1, -1, -1) : make_int4(b, b + 1, b + 2, b + 3);
-    }
-  }
-}
-
-__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
-               "l"(gsrc)
-               : "memory");
-}
-
-template <bool kStaged>
-__device__ __forceinline__ uint32_t key_at(const uint32_t* keys, const float* srow, int i) {
-  if constexpr (kStaged) return keys[i];
-  else return order_key(srow[i]);
-}
-
-template <bool kStaged>
-__global__ void __launch_bounds__(kTopkThreads) topk_kernel(const __grid_constant__ TopkArgs a) {
-  extern __shared__ __align__(16) uint32_t keys[];
+// kMode 0: keys read from global memory at every use (rows too long for smem);
+// 1: keys staged in shared memory; 2: staged and also held in registers
+// (cols <= kRegKeys * 512).
+template <int kMode>
+__global__ void __launch_bounds__(kTopkThreads, 1) topk_kernel(const __grid_constant__ TopkArgs a) {
+  constexpr bool kStaged = kMode > 0;
+  extern __shared__ __align__(16) uint32_t dyn[];
   __shared__ TopkSmem sm;
-  const int tid = threadIdx.x, nt = blockDim.x;
+  uint32_t* keys = dyn;
+  int* memb = reinterpret_cast<int*>(dyn) + a.memb_off;
+  int* ntab = reinterpret_cast<int*>(dyn) + a.ntab_off;
+  const int tid = threadIdx.x, nt = kTopkThreads;
   const int lane = tid & 31, warp = tid >> 5;
   RowCtx c;
   c.row = blockIdx.x;
+  // the first selected rank of this thread is loaded before the row sizes are
+  // known (selected rows always hold take_stride entries): one latency less
+  const int64_t rank0 = tid < a.take_stride ? load_index(a.selected, a.sel64, c.row * a.take_stride + tid) : -1;
   c.n = a.lens[c.row];
   c.take = a.takes[c.row];
   const RowBounds rb = row_bounds(c.n, 64, a.window);
@@ -217,105 +161,349 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(const __grid_constan
   c.L = static_cast<int>(min(static_cast<int64_t>(max(a.fine_lens[c.row], 0)), a.cols));
   float* srow = a.scores + c.row * a.score_stride;
   const bool select = c.L > a.topk;
-  // staged path: bitmap of masked columns after the keys (words for take*64 columns)
-  const int bm_words = kStaged ? static_cast<int>((min(static_cast<int64_t>(max(c.take, 0)) * 64, a.cols) + 31) / 32) : 0;
-  uint32_t* bitmap = kStaged && select && a.mask ? keys + ((a.cols + 3) & ~int64_t(3)) : nullptr;
-  const bool vec = (reinterpret_cast<uintptr_t>(srow) & 15) == 0;
-  const int nv = (kStaged && select && vec) ? c.L >> 2 : 0;
-  // 1. start the asynchronous copy of the row's scores into shared memory
-  for (int v = tid; v < nv; v += nt) cp_async16(keys + 4 * v, srow + 4 * v);
+  const int S = kStaged ? min(max(c.take, 0), a.stage_take) : 0;  // ranks with staged members
+  const int Sn = kStaged ? static_cast<int>(min(min(a.pages, static_cast<int64_t>(a.stage_nt)),
+                                                (static_cast<int64_t>(max(c.n, 0)) + 63) / 64))
+                         : 0;
+  const int32_t* ntrow = a.nt + c.row * a.pages;
+
+  // ---- 1. asynchronous copies into shared memory --------------------------------
+  const int nv4 = (kStaged && (reinterpret_cast<uintptr_t>(srow) & 15) == 0) ? c.L >> 2 : 0;
+  if (kStaged) {
+    for (int v = tid; v < nv4; v += nt) cp_async16(keys + 4 * v, srow + 4 * v);
+    if ((reinterpret_cast<uintptr_t>(ntrow) & 15) == 0) {
+      for (int v = tid; v < (Sn >> 2); v += nt) cp_async16(ntab + 4 * v, ntrow + 4 * v);
+      for (int v = (Sn & ~3) + tid; v < Sn; v += nt) cp_async4(ntab + v, ntrow + v);
+    } else {
+      for (int v = tid; v < Sn; v += nt) cp_async4(ntab + v, ntrow + v);
+    }
+  } else {
+    if (tid == 0) sm.nbnd = 0;
+    __syncthreads();
+  }
+  // selected ranks -> pages; members of staged ranks; boundary flags
+  for (int r = tid; r < c.take; r += nt) {
+    int64_t rank = -1, rpage = -1;
+    if (r < a.take_stride) rank = r == tid ? rank0 : load_index(a.selected, a.sel64, c.row * a.take_stride + r);
+    const bool rank_ok = rank >= 0 && rank < a.pages;
+    if (rank_ok) rpage = a.rt[c.row * a.pages + rank];
+    const int64_t epage =
+        a.direct_fine ? (r < a.fine_table_cols ? a.fine_table[c.row * a.fine_table_cols + r] : -1) : rpage;
+    if (r < kRankCache) {
+      sm.pgc[r] = static_cast<int>(epage);
+      sm.rpg[r] = static_cast<int>(rpage);
+    }
+    if (r < S && epage >= 0 && epage < a.member_rows) {
+      const int32_t* src = a.members + epage * 64;
+#pragma unroll
+      for (int q = 0; q < 16; ++q) cp_async16(memb + r * 64 + 4 * q, src + 4 * q);
+    }
+    bool boundary = false;
+    if (a.mask && rank_ok && rpage >= 0 && rpage < a.member_rows) {
+      const int bucket =
+          a.bucket_from_rank ? static_cast<int>(rank / 16) * 1024 : (a.members[rpage * 64] / 1024) * 1024;
+      boundary = bucket < c.sink || bucket + 1024 > c.tail;
+    }
+    if (kStaged) {
+      // ranks >= kRankCache only own columns >= cols: nothing to mask there
+      if (r < kRankCache) sm.bflag[r] = boundary ? 1 : 0;
+    } else if (boundary) {
+      const int k = atomicAdd(&sm.nbnd, 1);
+      if (k < kMaskQueue) sm.u.h.bnd[k] = make_int2(r, static_cast<int>(rpage));
+      else mask_page(a, c, srow, r, rpage, 0, 1);
+    }
+  }
   asm volatile("cp.async.commit_group;" ::: "memory");
-  if (bitmap)
-    for (int w = tid; w < bm_words; w += nt) bitmap[w] = 0u;
-  if (tid == 0) sm.nbnd = 0;
-  __syncthreads();
-  // 2. page ids of the selected ranks + boundary mask, overlapping the copy
-  ranks_and_mask(a, c, srow, sm, bitmap);
   asm volatile("cp.async.wait_all;" ::: "memory");
   __syncthreads();
 
-  if (!select) {
-    for (int t = tid; t < a.topk; t += nt) sm.rawbuf[t] = t < c.L ? t : -1;
-    __syncthreads();
-    emit_all<false>(a, c, sm, keys, srow);
+  // ---- 2. mask + keys -------------------------------------------------------------
+  if (kStaged) {
+    const int mcols = a.mask ? static_cast<int>(min(static_cast<int64_t>(max(c.take, 0)) * 64, a.cols)) : 0;
+    const int hi = max(c.L, mcols);
+    for (int i = tid; i < hi; i += nt) {
+      bool masked = false;
+      if (i < mcols) {
+        const int r = i >> 6;
+        if (sm.bflag[r]) {
+          // the staged members are those of the mapping page; they are the mask
+          // page's too unless a direct fine table points elsewhere
+          const int lg = (r < S && sm.rpg[r] == sm.pgc[r]) ? memb[i]
+                                                           : a.members[static_cast<int64_t>(sm.rpg[r]) * 64 + (i & 63)];
+          masked = lg < c.sink || lg >= c.tail;
+          if (masked) srow[i] = -CUDART_INF_F;
+        }
+      }
+      if (i < c.L) keys[i] = masked ? kNegInfKey : order_key(i < nv4 * 4 ? __uint_as_float(keys[i]) : srow[i]);
+    }
   } else {
-    if constexpr (kStaged) {
-      // 3. floats -> order keys in place, masked columns -> -inf
-      for (int i = tid; i < c.L; i += nt) {
-        const float x = i < nv * 4 ? __uint_as_float(keys[i]) : srow[i];
-        const bool masked = bitmap && i < bm_words * 32 && ((bitmap[i >> 5] >> (i & 31)) & 1u);
-        keys[i] = masked ? kNegInfKey : order_key(x);
+    const int nb = min(sm.nbnd, kMaskQueue);
+    for (int k = warp; k < nb; k += kTopkWarps) mask_page(a, c, srow, sm.u.h.bnd[k].x, sm.u.h.bnd[k].y, lane, 32);
+  }
+  __syncthreads();
+
+  // ---- mapping epilogue for one output slot (VQ:121-148) ----------------------------
+  auto emit = [&](int pos, int raw) {
+    bool live = false;
+    if (raw >= 0 && raw < c.L) live = kStaged ? keys[raw] != kNegInfKey : srow[raw] != -CUDART_INF_F;
+    int lg = -1;
+    if (live) {
+      if (raw < c.take * 64) {
+        const int r = raw >> 6;
+        const int64_t page = r < kRankCache ? sm.pgc[r] : page_of_rank(a, c, r);
+        if (page >= 0 && page < a.member_rows) lg = r < S ? memb[raw] : a.members[page * 64 + (raw & 63)];
+      } else {
+        const int off = raw - c.take * 64;
+        lg = off < c.sink ? off : c.tail + off - c.sink;
       }
-      __syncthreads();
     }
-    // ---- exact radix select of the T-th largest key --------------------------
-    uint32_t prefix = 0, known = 0;
-    int need = a.topk;
-    for (int pass = 0; pass < 4; ++pass) {
-      const int shift = 24 - 8 * pass;
-      for (int b = tid; b < 256; b += nt) sm.hist[b] = 0;
-      __syncthreads();
-      const int iters = (c.L + nt - 1) / nt;
-      for (int j = 0; j < iters; ++j) {
+    if (!(lg >= 0 && lg < c.n)) lg = -1;
+    const int64_t dst = c.row * a.topk + pos;
+    a.logical[dst] = lg;
+    if (a.physical_output) {
+      int ph = -1;
+      if (lg >= 0) {
+        const int p = lg >> 6;
+        if (p < a.pages) ph = (p < Sn ? ntab[p] : ntrow[p]) * 64 + (lg & 63);
+      }
+      a.physical[dst] = ph;
+      a.raw[dst] = raw;
+    }
+    if (a.expansion_stride) {
+      const int b = lg * 4;
+      reinterpret_cast<int4*>(a.expanded + c.row * a.expansion_stride)[pos] =
+          lg < 0 ? make_int4(-1, -1, -1, -1) : make_int4(b, b + 1, b + 2, b + 3);
+    }
+  };
+
+  if (!select) {
+    for (int t = tid; t < a.topk; t += nt) emit(t, t < c.L ? t : -1);
+  } else {
+    // ---- 3. selection ---------------------------------------------------------------
+    const int nsl = (c.L + nt - 1) / nt;  // slices of nt consecutive candidates
+    uint32_t kr[kMode == 2 ? kRegKeys : 1];
+    if constexpr (kMode == 2) {
+#pragma unroll
+      for (int j = 0; j < kRegKeys; ++j) {
         const int i = j * nt + tid;
-        int bin = -1;
-        if (i < c.L) {
-          const uint32_t k = key_at<kStaged>(keys, srow, i);
-          if ((k & known) == prefix) bin = (k >> shift) & 255;
-        }
-        const unsigned same = __match_any_sync(0xffffffffu, bin);
-        if (bin >= 0 && lane == __ffs(same) - 1) atomicAdd(&sm.hist[bin], __popc(same));
+        kr[j] = i < c.L ? keys[i] : 0u;
+      }
+    }
+    auto key_of = [&](int j) -> uint32_t {  // this thread's key of slice j (i < L)
+      const int i = j * nt + tid;
+      if constexpr (kMode == 0) return order_key(srow[i]);
+      else return keys[i];
+    };
+    // staged modes: one 12-bit histogram pass finds the bin of the T-th key; the
+    // bin's keys are ranked exactly by (key desc, index asc) and the selected ones
+    // flagged.  Rows whose bin holds more than kMaxBin keys (mass ties) and the
+    // unstaged mode take the bitwise search instead.
+    bool by_bin = false;
+    TopBin tb{0, 0, 0};
+    if constexpr (kStaged) {
+      int* hist = sm.u.h.hist;
+      zero_hist<kTopkThreads>(hist);
+      for (int w = tid; w < (c.L + 31) / 32; w += nt) sm.selbit[w] = 0u;
+      if (tid < 256) sm.hist2[tid] = 0;
+      if (tid == 0) {
+        sm.ncand = 0;
+        sm.ncand2 = 0;
       }
       __syncthreads();
-      if (warp == 0) {
-        int cnt[8], s = 0;
+      if constexpr (kMode == 2) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          cnt[j] = sm.hist[255 - (lane * 8 + j)];
-          s += cnt[j];
+        for (int j = 0; j < kRegKeys; ++j)
+          if (j * nt + tid < c.L) atomicAdd(&hist[bin_of(kr[j])], 1);
+      } else {
+        for (int i = tid; i < c.L; i += nt) atomicAdd(&hist[bin_of(keys[i])], 1);
+      }
+      __syncthreads();
+      tb = find_top_bin<kTopkThreads>(a.topk, hist, sm.warp_tot, &sm.res);
+      by_bin = tb.in <= kMaxBin;
+      if (by_bin) {
+        // the histogram is dead: the candidate list reuses its storage
+        int2* cand = sm.u.c.cand;
+        const uint32_t ltm = lanemask_lt();
+        auto append = [&](int j, uint32_t k) {
+          const bool m = j * nt + tid < c.L && bin_of(k) == tb.bin;
+          const unsigned bal = __ballot_sync(0xffffffffu, m);
+          if (bal == 0u) return;
+          int base = 0;
+          if (lane == 0) base = atomicAdd(&sm.ncand, __popc(bal));
+          base = __shfl_sync(0xffffffffu, base, 0);
+          if (m) cand[base + __popc(bal & ltm)] = make_int2(static_cast<int>(k), j * nt + tid);
+        };
+        if constexpr (kMode == 2) {
+#pragma unroll
+          for (int j = 0; j < kRegKeys; ++j)
+            if (j < nsl) append(j, kr[j]);
+        } else {
+          for (int j = 0; j < nsl; ++j) append(j, j * nt + tid < c.L ? key_of(j) : 0u);
         }
-        int cum = warp_inclusive_scan(s) - s;
+        __syncthreads();
+        int need_bin = a.topk - tb.above;
+        const int2* rk = cand;
+        int nres = tb.in;
+        if (tb.in > kSmallBin) {
+          // second level: the next 8 key bits of the bin's keys
+          for (int q = tid; q < tb.in; q += nt) atomicAdd(&sm.hist2[(cand[q].x >> (24 - kBinBits)) & 255], 1);
+          __syncthreads();
+          if (warp == 0) {
+            const int hi = 256 - lane * 8;  // lane owns sub-bins [hi - 8, hi), descending
+            int cc[8], s = 0;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          if (cum < need && cum + cnt[j] >= need) {
-            sm.digit = 255 - (lane * 8 + j);
-            sm.need = need - cum;
+            for (int j = 0; j < 8; ++j) {
+              cc[j] = sm.hist2[hi - 8 + j];
+              s += cc[j];
+            }
+            int cum = warp_inclusive_scan(s) - s;
+            if (cum < need_bin && cum + s >= need_bin) {
+#pragma unroll
+              for (int j = 7; j >= 0; --j) {
+                if (cum < need_bin && cum + cc[j] >= need_bin) sm.res2 = make_int4(hi - 8 + j, cum, cc[j], 0);
+                cum += cc[j];
+              }
+            }
           }
-          cum += cnt[j];
+          __syncthreads();
+          const int4 r2 = sm.res2;
+          by_bin = r2.z <= kMaxBin2;
+          if (by_bin) {
+            for (int q = tid; q < tb.in; q += nt) {
+              const int2 me = cand[q];
+              const int sub = (me.x >> (24 - kBinBits)) & 255;
+              if (sub > r2.x) atomicOr(&sm.selbit[me.y >> 5], 1u << (me.y & 31));
+              else if (sub == r2.x) sm.cand2[atomicAdd(&sm.ncand2, 1)] = me;
+            }
+            __syncthreads();
+            need_bin -= r2.y;
+            rk = sm.cand2;
+            nres = r2.z;
+          }
+        }
+        if (by_bin) {
+          // exact rank among the remaining keys by (key desc, index asc)
+          for (int q = tid; q < nres; q += nt) {
+            const int2 me = rk[q];
+            const uint32_t k = static_cast<uint32_t>(me.x);
+            int r = 0;
+            for (int f = 0; f < nres; ++f) {
+              const int2 o = rk[f];
+              const uint32_t ko = static_cast<uint32_t>(o.x);
+              r += (ko > k) | ((ko == k) & (o.y < me.y));
+            }
+            if (r < need_bin) atomicOr(&sm.selbit[me.y >> 5], 1u << (me.y & 31));
+          }
+          __syncthreads();
         }
       }
-      __syncthreads();
-      prefix |= static_cast<uint32_t>(sm.digit) << shift;
-      known |= 255u << shift;
-      need = sm.need;
-      __syncthreads();
     }
-    const uint32_t thr = prefix;
-    // ---- place selected candidates in ascending index order -------------------
-    const int chunk = (c.L + nt - 1) / nt;
-    const int beg = min(tid * chunk, c.L), end = min(beg + chunk, c.L);
-    int eq = 0, gt = 0;
-    for (int i = beg; i < end; ++i) {
-      const uint32_t k = key_at<kStaged>(keys, srow, i);
-      eq += k == thr;
-      gt += k > thr;
+    uint32_t thr = 0;
+    int need = 0;
+    if (!by_bin) {
+      int gt = 0;
+      thr = block_kth_largest<kTopkWarps>(
+          a.topk,
+          [&](uint32_t c1, uint32_t c2, uint32_t c3, int& n1, int& n2, int& n3) {
+            n1 = n2 = n3 = 0;
+            if constexpr (kMode == 2) {
+#pragma unroll
+              for (int j = 0; j < kRegKeys; ++j) {
+                if (j * nt + tid < c.L) {
+                  n1 += kr[j] >= c1;
+                  n2 += kr[j] >= c2;
+                  n3 += kr[j] >= c3;
+                }
+              }
+            } else {
+              for (int i = tid; i < c.L; i += nt) {
+                const uint32_t k = kMode == 1 ? keys[i] : order_key(srow[i]);
+                n1 += k >= c1;
+                n2 += k >= c2;
+                n3 += k >= c3;
+              }
+            }
+          },
+          sm.red, &gt);
+      need = a.topk - gt;  // ties of thr that are selected (lowest indices)
     }
-    int tot;
-    const int eq_before = block_exclusive_scan(eq, sm.warp_tot, &tot);
-    const int take_eq = min(max(need - eq_before, 0), eq);
-    int pos = block_exclusive_scan(gt + take_eq, sm.warp_tot, &tot);
-    int eq_seen = eq_before;
-    for (int i = beg; i < end; ++i) {
-      const uint32_t k = key_at<kStaged>(keys, srow, i);
-      bool sel = k > thr;
-      if (k == thr) {
-        sel = eq_seen < need;
-        ++eq_seen;
+    // class of candidate i with key k: 1 = selected outright, 2 = tie of thr
+    // (selected while fewer than `need` ties precede it), 0 = not selected
+    auto klass = [&](int i, uint32_t k) -> int {
+      if (i >= c.L) return 0;
+      if (by_bin) {
+        const int b = bin_of(k);
+        return (b > tb.bin || (b == tb.bin && ((sm.selbit[i >> 5] >> (i & 31)) & 1u))) ? 1 : 0;
       }
-      if (sel && pos < a.topk) sm.rawbuf[pos++] = i;
+      return k > thr ? 1 : (k == thr ? 2 : 0);
+    };
+    // ---- 4. output slot of every selected candidate, in index order ----------------
+    // (selected, tie) counts per (slice, warp) -> exclusive scan -> slot =
+    // selected before it + min(ties before it, need).  Chunks of kMaxSlices
+    // slices (more than one only in the unstaged mode) carry their totals.
+    const uint32_t lt = lanemask_lt();
+    int2* cnt = sm.u.c.cnt;
+    auto count_slice = [&](int j, int jc, uint32_t k) {
+      const int kl = klass(j * nt + tid, k);
+      const unsigned gb = __ballot_sync(0xffffffffu, kl == 1);
+      const unsigned eb = __ballot_sync(0xffffffffu, kl == 2);
+      if (lane == 0) cnt[jc * kTopkWarps + warp] = make_int2(__popc(gb), __popc(eb));
+    };
+    auto place_slice = [&](int j, int jc, uint32_t k) {
+      const int i = j * nt + tid;
+      const int kl = klass(i, k);
+      const unsigned gb = __ballot_sync(0xffffffffu, kl == 1);
+      const unsigned eb = __ballot_sync(0xffffffffu, kl == 2);
+      const int2 base = cnt[jc * kTopkWarps + warp];
+      const int gt_lt = base.x + __popc(gb & lt);
+      const int eq_lt = base.y + __popc(eb & lt);
+      if (kl == 1 || (kl == 2 && eq_lt < need)) emit(gt_lt + min(eq_lt, need), i);
+    };
+    auto scan_counts = [&](int E, int2 carry) {
+      if (warp == 0) {
+        const int ch = (E + 31) / 32;
+        const int beg = min(lane * ch, E), end = min(beg + ch, E);
+        int sg = 0, se = 0;
+        for (int q = beg; q < end; ++q) {
+          sg += cnt[q].x;
+          se += cnt[q].y;
+        }
+        const int ig = warp_inclusive_scan(sg), ie = warp_inclusive_scan(se);
+        int rg = carry.x + ig - sg, re = carry.y + ie - se;
+        for (int q = beg; q < end; ++q) {
+          const int2 v = cnt[q];
+          cnt[q] = make_int2(rg, re);
+          rg += v.x;
+          re += v.y;
+        }
+        if (lane == 31) sm.carry = make_int2(carry.x + ig, carry.y + ie);
+      }
+    };
+    if constexpr (kMode == 2) {
+      // rolled loops over the staged keys: the unrolled mapping epilogue would be
+      // kRegKeys copies of a long code path
+#pragma unroll 1
+      for (int j = 0; j < nsl; ++j) count_slice(j, j, j * nt + tid < c.L ? keys[j * nt + tid] : 0u);
+      __syncthreads();
+      scan_counts(nsl * kTopkWarps, make_int2(0, 0));
+      __syncthreads();
+#pragma unroll 1
+      for (int j = 0; j < nsl; ++j) place_slice(j, j, j * nt + tid < c.L ? keys[j * nt + tid] : 0u);
+    } else {
+      int2 carry = make_int2(0, 0);
+      for (int j0 = 0; j0 < nsl; j0 += kMaxSlices) {
+        const int jn = min(nsl - j0, kMaxSlices);
+        for (int jc = 0; jc < jn; ++jc)
+          count_slice(j0 + jc, jc, (j0 + jc) * nt + tid < c.L ? key_of(j0 + jc) : 0u);
+        __syncthreads();
+        scan_counts(jn * kTopkWarps, carry);
+        __syncthreads();
+        for (int jc = 0; jc < jn; ++jc)
+          place_slice(j0 + jc, jc, (j0 + jc) * nt + tid < c.L ? key_of(j0 + jc) : 0u);
+        carry = sm.carry;
+        __syncthreads();
+      }
     }
-    __syncthreads();
-    emit_all<kStaged>(a, c, sm, keys, srow);
   }
   if (a.expansion_stride) {
     for (int64_t j = static_cast<int64_t>(a.topk) * 4 + tid; j < a.expansion_stride; j += nt)
@@ -349,22 +537,37 @@ extern "C" int v1x_topk(float* scores, int64_t score_stride, int64_t cols, const
   TopkArgs a{scores, score_stride, cols, fine_lens, members, member_rows, rt, nt, pages, selected,
              selected_is_i64, take_stride, lens, takes, physical, logical, raw,
              static_cast<int>(topk), static_cast<int>(window), mask, expanded, expansion_stride,
-             physical_output, bucket_from_rank, fine_table, fine_table_cols, direct_fine};
+             physical_output, bucket_from_rank, fine_table, fine_table_cols, direct_fine,
+             0, 0, 0, 0};
   cudaStream_t s = as_stream(stream);
   V1X_CHECK_ARG(take_stride <= 65536, "topk: take stride too large");
-  if (cols <= kTopkMaxSmemKeys) {
-    const int64_t bm = (std::min<int64_t>(take_stride * 64, cols) + 31) / 32;
-    const size_t smem = static_cast<size_t>(((cols + 3) & ~int64_t(3)) + bm + 1) * 4;
-    if (smem > 48 * 1024) {
-      static DeviceOnce once;
-      if (once.first()) {
-        cudaFuncSetAttribute(topk_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kTopkMaxSmemKeys * 4 + kTopkMaxSmemKeys / 8 + 64);
-      }
+  // dynamic shared memory of the staged modes: keys | staged members | staged
+  // native-table row; rows whose keys alone do not fit take the unstaged mode
+  const int64_t limit = 227 * 1024 - static_cast<int64_t>(sizeof(TopkSmem)) - 1024;
+  const int64_t cols_pad = (cols + 3) & ~int64_t(3);
+  if (cols <= kTopkMaxSmemKeys && cols_pad * 4 <= limit) {
+    const int64_t rank_bound = direct_fine ? fine_table_cols : take_stride;
+    int64_t stake = (reinterpret_cast<uintptr_t>(members) & 15) == 0 ? std::min<int64_t>(rank_bound, kStageTake) : 0;
+    int64_t snt = std::min<int64_t>(pages, kStageNt);
+    auto bytes = [&] { return (cols_pad + stake * 64 + snt) * 4; };
+    if (bytes() > limit) snt = 0;
+    if (bytes() > limit) stake = 0;
+    a.stage_take = static_cast<int>(stake);
+    a.stage_nt = static_cast<int>(snt);
+    a.memb_off = static_cast<int>(cols_pad);
+    a.ntab_off = static_cast<int>(cols_pad + stake * 64);
+    static DeviceOnce once;
+    if (once.first()) {
+      cudaFuncSetAttribute(topk_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(limit));
+      cudaFuncSetAttribute(topk_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(limit));
     }
-    topk_kernel<true><<<static_cast<unsigned>(batch), kTopkThreads, smem, s>>>(a);
+    if (cols <= kRegKeys * kTopkThreads)
+      topk_kernel<2><<<static_cast<unsigned>(batch), kTopkThreads, static_cast<size_t>(bytes()), s>>>(a);
+    else
+      topk_kernel<1><<<static_cast<unsigned>(batch), kTopkThreads, static_cast<size_t>(bytes()), s>>>(a);
   } else {
-    topk_kernel<false><<<static_cast<unsigned>(batch), kTopkThreads, 0, s>>>(a);
+    a.stage_take = a.stage_nt = a.memb_off = a.ntab_off = 0;
+    topk_kernel<0><<<static_cast<unsigned>(batch), kTopkThreads, 0, s>>>(a);
   }
   return launch_status("v1x_topk");
 }

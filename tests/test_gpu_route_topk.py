@@ -152,7 +152,8 @@ def _topk_case(rng, B, L, T, take, P=96, cap=64, tie="float"):
     return members, rt, nt, selected, lens, takes, scores, fl, ft
 
 
-@pytest.mark.parametrize("L,T", [(2688, 2048), (3648, 2048), (700, 512), (9000, 2048), (20000, 1024)])
+@pytest.mark.parametrize("L,T", [(2688, 2048), (3648, 2048), (700, 512), (6912, 2048), (9000, 2048),
+                                 (20000, 1024), (46000, 2048)])
 @pytest.mark.parametrize("tie", ["float", "zeros", "coarse"])
 def test_topk_random(L, T, tie, cuda_dev):
     rng = np.random.default_rng(L + T + len(tie))
