@@ -41,6 +41,36 @@ struct DeviceOnce {
   }
 };
 
+// ---- programmatic dependent launch -------------------------------------------
+// The query-path kernels are launched with programmatic stream serialization: a
+// kernel may start (and run its set-up) while the kernel before it on the stream
+// finishes.  Each such kernel reads, before pdl_wait(), only caller inputs that no
+// kernel of this library writes (lengths, page tables, members, q, w, pools) and
+// writes nothing; everything else comes after pdl_wait(), which returns once the
+// preceding grid has completed and its writes are visible.  pdl_trigger() is
+// called only after pdl_wait(), so when a kernel starts, every kernel two or
+// more launches back has completed.  Kernels of other libraries never trigger
+// early, so a kernel that follows one of them starts after it completes.  Both
+// instructions are no-ops in a plain launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // ---- device helpers ---------------------------------------------------------
 constexpr int kPageBytes = 8448;
 constexpr int kKeyBytes = 8192;
@@ -58,6 +88,14 @@ __device__ __forceinline__ uint32_t order_key(float x) {
 
 __device__ __forceinline__ int64_t load_index(const void* p, int is64, int64_t i) {
   return is64 ? static_cast<const int64_t*>(p)[i] : static_cast<int64_t>(static_cast<const int32_t*>(p)[i]);
+}
+
+// Scoring lengths: kind 0 = the lengths as given; kind 1 = the centre count of
+// a token length n, max(8 * built pages, 1) with built pages = (n-1)//1024*16
+// (center_lens of DS/kernels.py:589).
+__device__ __forceinline__ int64_t score_len(int n, int kind) {
+  if (kind == 1) return max(static_cast<int64_t>(max(n - 1, 0) / 1024) * 16 * 8, int64_t(1));
+  return n;
 }
 
 // Row bounds shared by every stage (DS/kernels.py:242-243, VQ:69-70).

@@ -37,6 +37,8 @@ constexpr int kUnroll = 4;
 
 template <bool kHasV>
 __global__ void __launch_bounds__(256) gather_vec_kernel(const __grid_constant__ GatherArgs a) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t cpr = a.dim * a.elem / 16;  // 16-byte chunks per row
   const int64_t total = a.rows * a.top * cpr;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -72,6 +74,8 @@ __global__ void __launch_bounds__(256) gather_vec_kernel(const __grid_constant__
 
 template <typename T>
 __global__ void gather_scalar_kernel(const __grid_constant__ GatherArgs a) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t total = a.rows * a.top * a.dim;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   const T* k = reinterpret_cast<const T*>(a.k);
@@ -120,15 +124,15 @@ extern "C" int v1x_gather_slots(const void* k, const void* v, const int32_t* req
     const int64_t total = rows * top * dim * elem_bytes / 16;
     int64_t blocks = (total + 256 * kUnroll - 1) / (256 * kUnroll);
     blocks = blocks < sms * 16 ? blocks : sms * 16;
-    if (hv) gather_vec_kernel<true><<<static_cast<unsigned>(blocks), 256, 0, s>>>(a);
-    else gather_vec_kernel<false><<<static_cast<unsigned>(blocks), 256, 0, s>>>(a);
+    if (hv) launch_pdl(gather_vec_kernel<true>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, a);
+    else launch_pdl(gather_vec_kernel<false>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, a);
   } else {
     const int64_t total = rows * top * dim;
     int64_t blocks = (total + 255) / 256;
     blocks = blocks < sms * 32 ? blocks : sms * 32;
-    if (elem_bytes == 1) gather_scalar_kernel<uint8_t><<<static_cast<unsigned>(blocks), 256, 0, s>>>(a);
-    else if (elem_bytes == 2) gather_scalar_kernel<uint16_t><<<static_cast<unsigned>(blocks), 256, 0, s>>>(a);
-    else gather_scalar_kernel<uint32_t><<<static_cast<unsigned>(blocks), 256, 0, s>>>(a);
+    if (elem_bytes == 1) launch_pdl(gather_scalar_kernel<uint8_t>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, a);
+    else if (elem_bytes == 2) launch_pdl(gather_scalar_kernel<uint16_t>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, a);
+    else launch_pdl(gather_scalar_kernel<uint32_t>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, a);
   }
   return launch_status("v1x_gather_slots");
 }

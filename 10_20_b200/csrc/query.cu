@@ -37,6 +37,8 @@ __global__ void __launch_bounds__(128) query_metadata_kernel(
   const int mine = valid ? nt[row * np + page] : -1;
   const int first = valid ? nt[page] : -1;
   const int differs = __syncthreads_or(mine != first);
+  pdl_wait();  // everything above reads caller inputs only
+  pdl_trigger();
   if (i == 0) {
     const bool share = (n == lens[0]) && !differs;
     fine_lens[row] = static_cast<int32_t>(fine);
@@ -102,6 +104,8 @@ constexpr int kStagePages = 4;
 __global__ void __launch_bounds__(256) stage_tail_shared_kernel(const __grid_constant__ StageArgs a,
                                                                 int64_t grid_pages) {
   const int64_t row = blockIdx.x;
+  pdl_wait();
+  pdl_trigger();
   if (a.rows_bound > 0 && row >= a.rows_bound) return;
   if (a.tail_rows[row] != row) return;
   const int n = a.lens[row];
@@ -262,8 +266,8 @@ extern "C" int v1x_query_metadata(const int32_t* lens, const int32_t* nt, int32_
   clear_error();
   V1X_CHECK_ARG(batch >= 0 && np > 0 && den > 0 && num >= 0, "query_metadata: bad geometry");
   if (batch == 0) return V1X_OK;
-  query_metadata_kernel<<<static_cast<unsigned>(batch), 128, 0, as_stream(stream)>>>(
-      lens, nt, fine_lens, takes, dg_lens, center_lens, tail_rows, np, topk, num, den, sink, window,
+  launch_pdl(query_metadata_kernel, dim3(static_cast<unsigned>(batch)), dim3(128), 0, as_stream(stream),
+             lens, nt, fine_lens, takes, dg_lens, center_lens, tail_rows, np, topk, num, den, sink, window,
       budget);
   return launch_status("v1x_query_metadata");
 }
@@ -309,7 +313,7 @@ extern "C" int v1x_stage_tail_shared(const uint8_t* native_bytes, const float* n
   if (rows_bound > 0 && rows > rows_bound) rows = rows_bound;
   if (rows <= 0) return V1X_OK;
   const dim3 grid(static_cast<unsigned>(rows), static_cast<unsigned>((grid_pages + kStagePages - 1) / kStagePages));
-  stage_tail_shared_kernel<<<grid, 256, 0, as_stream(stream)>>>(a, grid_pages);
+  launch_pdl(stage_tail_shared_kernel, grid, dim3(256), 0, as_stream(stream), a, grid_pages);
   return launch_status("v1x_stage_tail_shared");
 }
 

@@ -81,32 +81,36 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_kernel(const __grid_co
   const int tid = threadIdx.x, nt = kRouteThreads;
   const int64_t row = blockIdx.x;
   const int n = a.lens[row];
-  const int take = a.takes[row];
   const int active = max(n - 1, 0) / 1024 * 16;
-  if (a.fill_table) {
-    const int64_t base = a.capacity + static_cast<int64_t>(a.tail_rows[row]) * 68;
-    for (int64_t j = max(take, 0) + tid; j < a.fine_pages; j += nt)
-      a.ft[row * a.fine_pages + j] = static_cast<int32_t>(base + min(j - take, int64_t(67)));
-  }
-  if (take >= active) {
-    for (int64_t i = tid; i < a.take_stride; i += nt) {
-      store_sel(a, row * a.take_stride + i, i);
-      if (a.fill_table && i < take) a.ft[row * a.fine_pages + i] = a.rt[row * a.pages + i];
-    }
-    return;
-  }
-  // number of ranks the output needs: selected (take_stride) and ft (take)
-  const int want = static_cast<int>(min(static_cast<int64_t>(a.n_items),
-      max(a.take_stride, a.fill_table ? min(static_cast<int64_t>(take), a.fine_pages) : int64_t(0))));
-  if (want <= 0) return;
   const int32_t* rtrow = a.rt + row * a.pages;
-  if (a.stage_rt) {  // overlaps the selection below
+  if (a.stage_rt) {  // caller input: copied while the previous kernel finishes
     if ((reinterpret_cast<uintptr_t>(rtrow) & 15) == 0 && (a.pages & 3) == 0) {
       for (int v = tid; v < (a.pages >> 2); v += nt) cp_async16(sm.rt + 4 * v, rtrow + 4 * v);
     } else {
       for (int v = tid; v < a.pages; v += nt) cp_async4(sm.rt + v, rtrow + v);
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  pdl_wait();
+  pdl_trigger();
+  const int take = a.takes[row];
+  if (a.fill_table) {
+    const int64_t base = a.capacity + static_cast<int64_t>(a.tail_rows[row]) * 68;
+    for (int64_t j = max(take, 0) + tid; j < a.fine_pages; j += nt)
+      a.ft[row * a.fine_pages + j] = static_cast<int32_t>(base + min(j - take, int64_t(67)));
+  }
+  // number of ranks the output needs: selected (take_stride) and ft (take)
+  const int want = static_cast<int>(min(static_cast<int64_t>(a.n_items),
+      max(a.take_stride, a.fill_table ? min(static_cast<int64_t>(take), a.fine_pages) : int64_t(0))));
+  if (take >= active || want <= 0) {
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    if (take >= active) {
+      for (int64_t i = tid; i < a.take_stride; i += nt) {
+        store_sel(a, row * a.take_stride + i, i);
+        if (a.fill_table && i < take) a.ft[row * a.fine_pages + i] = a.rt[row * a.pages + i];
+      }
+    }
+    return;
   }
   if (tid == 0) sm.count = 0;
   // ---- page keys (VQ:26-41): p < act -> key of the page's max centre, else -inf
@@ -229,8 +233,8 @@ int route_launch(bool pages_in, const float* scores, int64_t score_stride, int64
     cudaFuncSetAttribute(route_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     cudaFuncSetAttribute(route_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   }
-  if (pages_in) route_kernel<true><<<static_cast<unsigned>(batch), kRouteThreads, smem, as_stream(stream)>>>(a);
-  else route_kernel<false><<<static_cast<unsigned>(batch), kRouteThreads, smem, as_stream(stream)>>>(a);
+  if (pages_in) launch_pdl(route_kernel<true>, dim3(static_cast<unsigned>(batch)), dim3(kRouteThreads), smem, as_stream(stream), a);
+  else launch_pdl(route_kernel<false>, dim3(static_cast<unsigned>(batch)), dim3(kRouteThreads), smem, as_stream(stream), a);
   return launch_status(pages_in ? "v1x_route_pages" : "v1x_route");
 }
 }  // namespace

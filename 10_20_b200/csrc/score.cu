@@ -34,6 +34,7 @@ struct ScoreArgs {
   float* page_max;
   int64_t page_stride;
   int heads, relu, clean;
+  int lens_kind;
 };
 
 __device__ __forceinline__ float2 e4m3x2_to_float2(uint16_t v) {
@@ -53,9 +54,11 @@ __global__ void __launch_bounds__(kScoreThreads) score_simt_kernel(const __grid_
     qs[2 * i + 1] = f.y;
   }
   for (int h = threadIdx.x; h < H; h += blockDim.x) ws[h] = a.w[b * H + h];
+  pdl_wait();
+  pdl_trigger();
   __syncthreads();
   const int64_t j = static_cast<int64_t>(blockIdx.y) * blockDim.x + threadIdx.x;
-  const int n = a.lens[b];
+  const int64_t n = score_len(a.lens[b], a.lens_kind);
   float result = -CUDART_INF_F;
   if (j < n && j < a.max_len) {
     const int64_t page = a.table[b * a.table_stride + j / 64];
@@ -102,16 +105,14 @@ __global__ void __launch_bounds__(kScoreThreads) score_simt_kernel(const __grid_
 
 int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages, const int32_t* lens,
                  const int32_t* table, int64_t table_stride, float* out, int64_t out_stride, int64_t max_len,
-                 float* page_max, int64_t page_stride, int64_t heads, int relu, int clean, int64_t batch,
-                 int32_t* status, cudaStream_t stream);
-}  // namespace v1x
+                 float* page_max, int64_t page_stride, int64_t heads, int relu, int clean, int lens_kind,
+                 int64_t batch, int32_t* status, cudaStream_t stream);
 
-extern "C" int v1x_score_fp8(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages,
-                             const int32_t* lens, const int32_t* table, int64_t table_stride,
-                             float* out, int64_t out_stride, int64_t max_len, float* page_max,
-                             int64_t page_stride, int64_t heads, int relu, int clean, int impl,
-                             int32_t* status, int64_t batch, void* stream) {
-  using namespace v1x;
+namespace {
+int score_dispatch(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages, const int32_t* lens,
+                   const int32_t* table, int64_t table_stride, float* out, int64_t out_stride, int64_t max_len,
+                   float* page_max, int64_t page_stride, int64_t heads, int relu, int clean, int impl,
+                   int lens_kind, int32_t* status, int64_t batch, void* stream) {
   clear_error();
   V1X_CHECK_ARG(heads >= 1 && heads <= 256, "score_fp8: heads must be in [1, 256]");
   V1X_CHECK_ARG(batch >= 0 && max_len >= 0 && pool_pages > 0, "score_fp8: bad geometry");
@@ -120,18 +121,39 @@ extern "C" int v1x_score_fp8(const uint8_t* q, const float* w, const uint8_t* po
   V1X_CHECK_ARG(out || page_max, "score_fp8: no output requested");
   V1X_CHECK_ARG((reinterpret_cast<uintptr_t>(pool) & 15) == 0, "score_fp8: pool must be 16-byte aligned");
   V1X_CHECK_ARG(table_stride >= 0 && impl >= 0 && impl <= 2, "score_fp8: bad table stride / impl");
+  V1X_CHECK_ARG(lens_kind == 0 || lens_kind == 1, "score_fp8: lens_kind must be 0 or 1");
   if (batch == 0 || max_len == 0) return V1X_OK;
   const bool tc = impl == 2 || (impl == 0 && heads % 32 == 0 && heads <= 128);
   if (tc)
     return score_fp8_tc(q, w, pool, pool_pages, lens, table, table_stride, out, out_stride, max_len, page_max,
-                        page_stride, heads, relu, clean, batch, status, as_stream(stream));
+                        page_stride, heads, relu, clean, lens_kind, batch, status, as_stream(stream));
   if (heads > kSimtMaxHeads) {
     set_error("score_fp8: the SIMT path takes heads <= %d", kSimtMaxHeads);
     return V1X_ERR_UNSUPPORTED;
   }
   ScoreArgs a{q, w, pool, lens, table, table_stride, out, out_stride, max_len, page_max, page_stride,
-              static_cast<int>(heads), relu, clean};
+              static_cast<int>(heads), relu, clean, lens_kind};
   const dim3 grid(static_cast<unsigned>(batch), static_cast<unsigned>((max_len + kScoreThreads - 1) / kScoreThreads));
-  score_simt_kernel<<<grid, kScoreThreads, 0, as_stream(stream)>>>(a);
+  launch_pdl(score_simt_kernel, grid, dim3(kScoreThreads), 0, as_stream(stream), a);
   return launch_status("v1x_score_fp8");
+}
+}  // namespace
+}  // namespace v1x
+
+extern "C" int v1x_score_fp8(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages,
+                             const int32_t* lens, const int32_t* table, int64_t table_stride,
+                             float* out, int64_t out_stride, int64_t max_len, float* page_max,
+                             int64_t page_stride, int64_t heads, int relu, int clean, int impl,
+                             int32_t* status, int64_t batch, void* stream) {
+  return v1x::score_dispatch(q, w, pool, pool_pages, lens, table, table_stride, out, out_stride, max_len, page_max,
+                             page_stride, heads, relu, clean, impl, 0, status, batch, stream);
+}
+
+extern "C" int v1x_score_fp8_ex(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages,
+                                const int32_t* lens, const int32_t* table, int64_t table_stride,
+                                float* out, int64_t out_stride, int64_t max_len, float* page_max,
+                                int64_t page_stride, int64_t heads, int relu, int clean, int impl,
+                                int lens_kind, int32_t* status, int64_t batch, void* stream) {
+  return v1x::score_dispatch(q, w, pool, pool_pages, lens, table, table_stride, out, out_stride, max_len, page_max,
+                             page_stride, heads, relu, clean, impl, lens_kind, status, batch, stream);
 }

@@ -50,6 +50,7 @@ constexpr int kQSlots = 2;        // per-row q tiles
 constexpr int kMaxAcc = 4;        // TMEM accumulators (epilogue group = accumulator & 1)
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 constexpr int kMaxTcRows = 8192;
+constexpr int64_t kMaxWRows = 8;  // head-weight rows staged in shared memory per CTA
 
 struct TcArgs {
   const int32_t* lens;
@@ -60,7 +61,7 @@ struct TcArgs {
   int64_t out_stride, max_len;
   float* page_max;
   int64_t page_stride;
-  int B, H, relu, clean, w_rows;
+  int B, H, relu, clean, w_rows, lens_kind;
   uint32_t tmem_cols;
   int32_t* status;
 };
@@ -93,7 +94,7 @@ __device__ __forceinline__ void raise_abort(TcShared& sh, int32_t* status) {
 }
 
 __device__ __forceinline__ int64_t row_eff(const TcArgs& a, int b) {
-  return min(static_cast<int64_t>(a.lens[b]), a.max_len);
+  return min(score_len(a.lens[b], a.lens_kind), a.max_len);
 }
 
 __device__ __forceinline__ int tiles_of(const TcArgs& a, int b) {
@@ -137,7 +138,41 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   int* prefix = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(&sh) + sizeof(TcShared));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
-  // ---- per-row tile prefix and barrier set-up -----------------------------------
+  // ---- set-up that reads nothing another kernel writes (overlaps the previous
+  // kernel under programmatic launch), then the per-row tile prefix --------------
+  if (tid == 0) {
+    sh.abort = 0;
+    sh.zero = 0;
+    for (int s = 0; s < kTcStages; ++s) {
+      mbar_init(&sh.full[s], 1);
+      mbar_init(&sh.empty[s], 1);
+    }
+    for (int r = 0; r < kScaleSlots; ++r) {
+      mbar_init(&sh.sfull[r], 1);
+      mbar_init(&sh.sempty[r], 128);
+    }
+    for (int r = 0; r < kQSlots; ++r) {
+      mbar_init(&sh.qfull[r], 1);
+      mbar_init(&sh.qempty[r], 1);
+    }
+    for (int c = 0; c < kMaxAcc; ++c) {
+      mbar_init(&sh.tfull[c], 1);
+      mbar_init(&sh.tempty[c], 128);
+    }
+    fence_mbar_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(&sh.tmem_base, a.tmem_cols);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&pool_map);
+    tma_prefetch_desc(&q_map);
+    tma_prefetch_desc(&scale_map);
+  }
+  pdl_wait();
+  pdl_trigger();
   {
     const int chunk = (a.B + kTcThreads - 1) / kTcThreads;
     const int beg = min(tid * chunk, a.B), end = min(beg + chunk, a.B);
@@ -153,36 +188,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       prefix[a.B] = tot;
       sh.total = tot;
       sh.per = (tot + gridDim.x - 1) / gridDim.x;
-      sh.abort = 0;
-      sh.zero = 0;
-      for (int s = 0; s < kTcStages; ++s) {
-        mbar_init(&sh.full[s], 1);
-        mbar_init(&sh.empty[s], 1);
-      }
-      for (int r = 0; r < kScaleSlots; ++r) {
-        mbar_init(&sh.sfull[r], 1);
-        mbar_init(&sh.sempty[r], 128);
-      }
-      for (int r = 0; r < kQSlots; ++r) {
-        mbar_init(&sh.qfull[r], 1);
-        mbar_init(&sh.qempty[r], 1);
-      }
-      for (int c = 0; c < kMaxAcc; ++c) {
-        mbar_init(&sh.tfull[c], 1);
-        mbar_init(&sh.tempty[c], 128);
-      }
-      fence_mbar_init();
     }
-  }
-  if (warp == kMmaWarp) {
-    tmem_alloc(&sh.tmem_base, a.tmem_cols);
-    tmem_relinquish();
-    tc_fence_before();
-  }
-  if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&pool_map);
-    tma_prefetch_desc(&q_map);
-    tma_prefetch_desc(&scale_map);
   }
   __syncthreads();
   tc_fence_after();
@@ -194,10 +200,6 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   const int b_first = ntiles > 0 ? locate_row(prefix, a.B, T0) : 0;
   const int b_last = ntiles > 0 ? locate_row(prefix, a.B, T1 - 1) : -1;
   const bool w_staged = b_last - b_first + 1 <= a.w_rows;
-  if (w_staged)
-    for (int e = tid; e < (b_last - b_first + 1) * a.H; e += kTcThreads)
-      wsm[e] = a.w[static_cast<int64_t>(b_first) * a.H + e];
-  __syncthreads();
 
   if (warp < kProducers) {
     // ---------------- TMA producers: warp p issues tiles p, p + kProducers, ... ----------------
@@ -289,6 +291,11 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     const int g = (warp - kEpiWarp0) >> 2;
     const int q4 = warp & 3;                      // TMEM lane quarter this warp may access
     const int i = q4 * 32 + lane;                 // key of the 128-key tile == TMEM lane
+    // the epilogue warps alone stage the head weights (off the producers' path)
+    if (w_staged)
+      for (int e = tid - 32 * kEpiWarp0; e < (b_last - b_first + 1) * a.H; e += kTcThreads - 32 * kEpiWarp0)
+        wsm[e] = a.w[static_cast<int64_t>(b_first) * a.H + e];
+    asm volatile("bar.sync 1, %0;" ::"r"(kTcThreads - 32 * kEpiWarp0) : "memory");
     TileCursor cur;
     if (ntiles > g) {
       cur.start(prefix, a.B, T0);
@@ -396,8 +403,8 @@ int encode(PFN_cuTensorMapEncodeTiled_v12000 enc, CUtensorMap* m, CUtensorMapDat
 // Launch the tensor-core scorer; returns V1X_ERR_UNSUPPORTED if the shape is not covered.
 int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages, const int32_t* lens,
                  const int32_t* table, int64_t table_stride, float* out, int64_t out_stride, int64_t max_len,
-                 float* page_max, int64_t page_stride, int64_t heads, int relu, int clean, int64_t batch,
-                 int32_t* status, cudaStream_t stream) {
+                 float* page_max, int64_t page_stride, int64_t heads, int relu, int clean, int lens_kind,
+                 int64_t batch, int32_t* status, cudaStream_t stream) {
   if (heads % 32 != 0 || heads > 128 || batch > kMaxTcRows || pool_pages >= (int64_t(1) << 31)) {
     set_error("score_fp8 (tensor core): heads must be a multiple of 32 <= 128 and batch <= %d", kMaxTcRows);
     return V1X_ERR_UNSUPPORTED;
@@ -444,10 +451,10 @@ int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t 
   const int64_t max_tiles = batch * ((max_len + 127) / 128);
   const int64_t sms = num_sms();
   // head-weight rows staged per CTA: a range of ceil(total/grid) tiles touches at
-  // most that many rows plus one (a range that also spans rows without tiles
-  // falls back to global reads inside the kernel)
+  // most that many rows plus one; at most kMaxWRows are staged (a CTA whose range
+  // spans more rows reads the weights from global memory)
   auto plan = [&](int64_t grid, int64_t& w_rows) {
-    w_rows = std::min<int64_t>(batch, (std::max<int64_t>(max_tiles, 1) + grid - 1) / grid + 1);
+    w_rows = std::min<int64_t>({batch, (std::max<int64_t>(max_tiles, 1) + grid - 1) / grid + 1, kMaxWRows});
     return static_cast<size_t>(1024 + kTcStages * 16384 + kQSlots * heads * 128 + kScaleSlots * 512 +
                                w_rows * heads * 4 + sizeof(TcShared) + (batch + 1) * 4 + 16);
   };
@@ -462,12 +469,13 @@ int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t 
     return V1X_ERR_UNSUPPORTED;
   }
   TcArgs args{lens, table, table_stride, w, out, out_stride, max_len, page_max, page_stride,
-              static_cast<int>(batch), static_cast<int>(heads), relu, clean, static_cast<int>(w_rows), cols,
-              status};
+              static_cast<int>(batch), static_cast<int>(heads), relu, clean, static_cast<int>(w_rows), lens_kind,
+              cols, status};
   static DeviceOnce once;
   if (once.first())
     cudaFuncSetAttribute(score_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-  score_tc_kernel<<<static_cast<unsigned>(grid), kTcThreads, smem, stream>>>(pool_map, q_map, scale_map, args);
+  launch_pdl(score_tc_kernel, dim3(static_cast<unsigned>(grid)), dim3(kTcThreads), smem, stream, pool_map, q_map,
+             scale_map, args);
   return launch_status("v1x_score_fp8 (tensor core)");
 }
 

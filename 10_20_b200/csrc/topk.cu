@@ -150,10 +150,23 @@ __global__ void __launch_bounds__(kTopkThreads, 1) topk_kernel(const __grid_cons
   const int lane = tid & 31, warp = tid >> 5;
   RowCtx c;
   c.row = blockIdx.x;
-  // the first selected rank of this thread is loaded before the row sizes are
-  // known (selected rows always hold take_stride entries): one latency less
-  const int64_t rank0 = tid < a.take_stride ? load_index(a.selected, a.sel64, c.row * a.take_stride + tid) : -1;
+  // caller inputs first (lengths, native table): they overlap the previous kernel
   c.n = a.lens[c.row];
+  const int Sn = kStaged ? static_cast<int>(min(min(a.pages, static_cast<int64_t>(a.stage_nt)),
+                                                (static_cast<int64_t>(max(c.n, 0)) + 63) / 64))
+                         : 0;
+  const int32_t* ntrow = a.nt + c.row * a.pages;
+  if (kStaged) {
+    if ((reinterpret_cast<uintptr_t>(ntrow) & 15) == 0) {
+      for (int v = tid; v < (Sn >> 2); v += nt) cp_async16(ntab + 4 * v, ntrow + 4 * v);
+      for (int v = (Sn & ~3) + tid; v < Sn; v += nt) cp_async4(ntab + v, ntrow + v);
+    } else {
+      for (int v = tid; v < Sn; v += nt) cp_async4(ntab + v, ntrow + v);
+    }
+  }
+  pdl_wait();
+  pdl_trigger();
+  const int64_t rank0 = tid < a.take_stride ? load_index(a.selected, a.sel64, c.row * a.take_stride + tid) : -1;
   c.take = a.takes[c.row];
   const RowBounds rb = row_bounds(c.n, 64, a.window);
   c.sink = rb.sink;
@@ -162,21 +175,11 @@ __global__ void __launch_bounds__(kTopkThreads, 1) topk_kernel(const __grid_cons
   float* srow = a.scores + c.row * a.score_stride;
   const bool select = c.L > a.topk;
   const int S = kStaged ? min(max(c.take, 0), a.stage_take) : 0;  // ranks with staged members
-  const int Sn = kStaged ? static_cast<int>(min(min(a.pages, static_cast<int64_t>(a.stage_nt)),
-                                                (static_cast<int64_t>(max(c.n, 0)) + 63) / 64))
-                         : 0;
-  const int32_t* ntrow = a.nt + c.row * a.pages;
 
   // ---- 1. asynchronous copies into shared memory --------------------------------
   const int nv4 = (kStaged && (reinterpret_cast<uintptr_t>(srow) & 15) == 0) ? c.L >> 2 : 0;
   if (kStaged) {
     for (int v = tid; v < nv4; v += nt) cp_async16(keys + 4 * v, srow + 4 * v);
-    if ((reinterpret_cast<uintptr_t>(ntrow) & 15) == 0) {
-      for (int v = tid; v < (Sn >> 2); v += nt) cp_async16(ntab + 4 * v, ntrow + 4 * v);
-      for (int v = (Sn & ~3) + tid; v < Sn; v += nt) cp_async4(ntab + v, ntrow + v);
-    } else {
-      for (int v = tid; v < Sn; v += nt) cp_async4(ntab + v, ntrow + v);
-    }
   } else {
     if (tid == 0) sm.nbnd = 0;
     __syncthreads();
@@ -562,12 +565,12 @@ extern "C" int v1x_topk(float* scores, int64_t score_stride, int64_t cols, const
       cudaFuncSetAttribute(topk_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(limit));
     }
     if (cols <= kRegKeys * kTopkThreads)
-      topk_kernel<2><<<static_cast<unsigned>(batch), kTopkThreads, static_cast<size_t>(bytes()), s>>>(a);
+      launch_pdl(topk_kernel<2>, dim3(static_cast<unsigned>(batch)), dim3(kTopkThreads), static_cast<size_t>(bytes()), s, a);
     else
-      topk_kernel<1><<<static_cast<unsigned>(batch), kTopkThreads, static_cast<size_t>(bytes()), s>>>(a);
+      launch_pdl(topk_kernel<1>, dim3(static_cast<unsigned>(batch)), dim3(kTopkThreads), static_cast<size_t>(bytes()), s, a);
   } else {
     a.stage_take = a.stage_nt = a.memb_off = a.ntab_off = 0;
-    topk_kernel<0><<<static_cast<unsigned>(batch), kTopkThreads, 0, s>>>(a);
+    launch_pdl(topk_kernel<0>, dim3(static_cast<unsigned>(batch)), dim3(kTopkThreads), 0, s, a);
   }
   return launch_status("v1x_topk");
 }

@@ -5,7 +5,9 @@ query sequence (sglang/srt/layers/attention/v1_deepseek/runtime.py:417-636,
 DeepGEMM ReLU path with fused route and fused topk) on libv1x.so kernels:
 
   1. query metadata with the fixed page budget  (BudgetMetadata)        :364-368
+     (side stream, with step 4's staging)
   2. FP8 centre logits of every built page's 8 centres                  :434-444
+     (centre counts derived from the token lengths in the scorer)
   3. fused.route: page max-of-8 + stable top pages                      :446-448
   4. fine_table_shared + stage_tail_shared                              :478-509
   5. FP8 fine logits over the fine page table                           :538-548
@@ -70,11 +72,14 @@ class SelectionStep:
     def run(self):
         c = self.case
         B = c.B
-        self.meta[(B,)](c.lens, c.native_table, self.fine_lens, self.takes, self.dg_lens,
-                        self.center_lens, self.tail_rows, c.P, c.topk, 1, 2, 64, c.window)
         main = torch.cuda.current_stream(c.lens.device)
+        # metadata and the sink/tail staging run on a side stream, concurrently
+        # with centre scoring, which derives each row's centre count from the
+        # token length itself (lens_kind="centres")
         self.side.wait_stream(main)
         with torch.cuda.stream(self.side):
+            self.meta[(B,)](c.lens, c.native_table, self.fine_lens, self.takes, self.dg_lens,
+                            self.center_lens, self.tail_rows, c.P, c.topk, 1, 2, 64, c.window)
             K.stage_tail_shared[(-(-B // 32) if B > 512 else B, 68)](
                 c.native, c.native.view(torch.float32), c.native_table, c.lens, c.fine,
                 c.fine.view(torch.float32), self.tail_rows, c.capacity, c.P, 68, 64, c.window,
@@ -82,21 +87,22 @@ class SelectionStep:
         if self.fused_route_pages:
             # centre scoring emits each page's max-of-8 directly; route reads P floats
             # per row and writes the fine page table itself (fill_table)
-            scoring.fp8_paged_mqa_logits(c.q8, c.centers, c.w, self.center_lens, c.center_table, None,
+            scoring.fp8_paged_mqa_logits(c.q8, c.centers, c.w, c.lens, c.center_table, None,
                                          c.P * 8, page_max=self.page_scores, logits=self.keep_logits,
                                          out=self.center_logits if self.keep_logits else None,
-                                         clean_logits=False)
+                                         clean_logits=False, lens_kind="centres")
+            main.wait_stream(self.side)
             self.fused.route_pages(self.page_scores, c.lens, self.takes, self.selected, c.P,
                                    c.reordered_table, self.fine_table, self.tail_rows, c.capacity, True)
         else:
-            scoring.fp8_paged_mqa_logits(c.q8, c.centers, c.w, self.center_lens, c.center_table, None,
-                                         c.P * 8, out=self.center_logits)
+            scoring.fp8_paged_mqa_logits(c.q8, c.centers, c.w, c.lens, c.center_table, None,
+                                         c.P * 8, out=self.center_logits, lens_kind="centres")
+            main.wait_stream(self.side)
             self.fused.route(self.center_logits, c.lens, self.takes, self.selected, c.P,
                              c.reordered_table, self.fine_table, self.tail_rows, c.capacity, False)
             K.fine_table_shared[(B,)](c.reordered_table, self.selected, self.takes, c.lens,
                                       self.fine_table, self.tail_rows, c.capacity, c.P, c.take,
                                       self.width // 64, 68)
-        main.wait_stream(self.side)
         scoring.fp8_paged_mqa_logits(c.q8, c.fine, c.w, self.dg_lens, self.fine_table, None,
                                      self.width, out=self.scores, clean_logits=False)
         self.fused.topk(self.scores, self.fine_lens, c.members, c.reordered_table, c.native_table,

@@ -27,12 +27,14 @@ def get_paged_mqa_logits_metadata(context_lens: torch.Tensor, block_size: int, n
 
 
 IMPLS = {"auto": 0, "simt": 1, "tensor_core": 2}
+LENS_KINDS = {"tokens": 0, "centres": 1}
 
 
 def fp8_paged_mqa_logits(q, kv_cache, weights, context_lens, block_table, schedule_meta,
                          max_context_len: int, clean_logits: bool = True, relu: bool = True,
                          out: torch.Tensor | None = None, impl: str = "auto",
-                         page_max: torch.Tensor | None = None, logits: bool = True):
+                         page_max: torch.Tensor | None = None, logits: bool = True,
+                         lens_kind: str = "tokens"):
     """Logits [B, max_context_len] (float32); columns >= context_lens[b] are -inf.
 
     q: e4m3 [B, H, 128] or [B, 1, H, 128]; kv_cache: packed uint8 [pages, 8448] or
@@ -43,6 +45,10 @@ def fp8_paged_mqa_logits(q, kv_cache, weights, context_lens, block_table, schedu
     page_max (extension): float32 [B, >= ceil(max_context_len / 8)] receiving the max of
     every 8 consecutive logits (fused.route's page score); logits=False skips the
     logits output (then `page_max` is required and the call returns it).
+    lens_kind (extension): "tokens" scores context_lens[b] keys; "centres" scores
+    the centre count of a token length n, max(8 * ((n-1)//1024*16), 1) -- the
+    center_lens the query metadata derives (DS/kernels.py:589) -- so centre scoring
+    can take the raw token lengths and need not wait for the metadata kernel.
     """
     if q.dim() == 4:
         require(q.shape[1] == 1, "only next_n == 1 is supported")
@@ -70,10 +76,12 @@ def fp8_paged_mqa_logits(q, kv_cache, weights, context_lens, block_table, schedu
     if page_max is not None:
         require(page_max.dtype == torch.float32 and page_max.stride(1) == 1 and page_max.shape[0] == B
                 and page_max.shape[1] * 8 >= max_context_len, "page_max: float32 [B, >= max_len/8]")
+    require(lens_kind in LENS_KINDS, "lens_kind: 'tokens' or 'centres'")
     from .kernels import status_word
-    _lib.call("v1x_score_fp8", ptr(q), ptr(weights), ptr(kv_cache), kv_cache.numel() // 8448, ptr(lens),
+    _lib.call("v1x_score_fp8_ex", ptr(q), ptr(weights), ptr(kv_cache), kv_cache.numel() // 8448, ptr(lens),
               ptr(block_table), block_table.stride(0), ptr(out), out.stride(0) if out is not None else 0,
               int(max_context_len), ptr(page_max), page_max.stride(0) if page_max is not None else 0, H,
-              int(bool(relu)), int(bool(clean_logits)), IMPLS[impl], ptr(status_word(q.device)), B,
+              int(bool(relu)), int(bool(clean_logits)), IMPLS[impl], LENS_KINDS[lens_kind],
+              ptr(status_word(q.device)), B,
               _lib.stream_of(q), device=q.device)
     return out if logits else page_max

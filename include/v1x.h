@@ -3,6 +3,11 @@
  * query-side selection path.
  *
  * Conventions shared by every entry point:
+ *   - Kernels of the query path (metadata, staging, scoring, route, topk,
+ *     gather) are launched with programmatic stream serialization: a kernel
+ *     may start its set-up while the previous kernel on the stream finishes,
+ *     reading only caller inputs that no kernel of this library writes before
+ *     it waits for that kernel's completion.
  *   - All tensor arguments are raw DEVICE pointers of the dtype named in the
  *     comment; sizes and strides are in ELEMENTS unless the name says bytes.
  *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Every call only
@@ -236,6 +241,17 @@ V1X_API int v1x_score_fp8(const uint8_t* q, const float* w, const uint8_t* pool,
                   int64_t out_stride, int64_t max_len, float* page_max, int64_t page_stride,
                   int64_t heads, int relu, int clean, int impl, int32_t* status, int64_t batch,
                   void* stream);
+
+/* Extension (no reference counterpart): v1x_score_fp8 with the scored length of
+ * row b derived from lens[b] by lens_kind: 0 = lens[b] (v1x_score_fp8 itself);
+ * 1 = the centre count of a token length n, max(8 * ((n-1)/1024*16), 1) -- the
+ * center_lens of DS/kernels.py:589 -- so centre scoring can run on the raw token
+ * lengths concurrently with the query-metadata kernel. */
+V1X_API int v1x_score_fp8_ex(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages,
+                  const int32_t* lens, const int32_t* table, int64_t table_stride, float* out,
+                  int64_t out_stride, int64_t max_len, float* page_max, int64_t page_stride,
+                  int64_t heads, int relu, int clean, int impl, int lens_kind, int32_t* status,
+                  int64_t batch, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* _gather_slots -- replaces NA/kernels.py:62-77 (GatherWorkspace.gather, :102-111).

@@ -217,6 +217,12 @@ def test_page_max_and_route_pages(impl, H, cuda_dev):
     lg = logits.cpu().numpy()
     pmn = pm.cpu().numpy()
     assert np.array_equal(pmn, lg.reshape(B, P, 8).max(2))
+    # lens_kind="centres" on the token lengths == the derived centre lengths
+    logits2 = torch.empty_like(logits)
+    pm2 = torch.full_like(pm, 5.0)
+    S.fp8_paged_mqa_logits(q, dev(pool), w, dev(lens), ctable, None, P * 8, out=logits2, page_max=pm2,
+                           impl=impl, lens_kind="centres")
+    assert torch.equal(logits, logits2) and torch.equal(pm, pm2)
     qf = importlib.import_module("10_20_b200.query_fused")
     takes = dev(rng.integers(0, 40, size=B).astype(np.int32))
     rt = dev(rng.integers(0, 10000, size=(B, P)).astype(np.int32))
