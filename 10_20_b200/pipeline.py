@@ -26,11 +26,23 @@ import torch
 from . import kernels as K
 from . import query_fused, scoring
 from .gather import _gather_impl
+from .sharding import row_bytes
 
 
 class SelectionStep:
+    """One query step over a batch of rows (see the module docstring).
+
+    chunks > 1 splits the rows into that many consecutive chunks and pipelines
+    them: centre scoring runs chunk after chunk on one stream, and as soon as a
+    chunk's centres are scored its route -> fine scoring -> top-k chain runs on
+    its own stream while the next chunk's centres are scored; its gather then
+    runs on a low-priority stream.  The latency-bound kernels (route, top-k)
+    thereby overlap bandwidth-bound ones.  Outputs are identical for any chunk
+    count: rows are independent.
+    """
+
     def __init__(self, case, gather: bool = True, gather_v: bool = False, fused_route_pages: bool = True,
-                 keep_logits: bool = False):
+                 keep_logits: bool = False, chunks: int = 1):
         c = self.case = case
         d = c.lens.device
         B = c.B
@@ -64,18 +76,64 @@ class SelectionStep:
         # outputs to route(center_logits) + fine_table_shared.
         self.fused_route_pages = fused_route_pages
         self.keep_logits = keep_logits or not fused_route_pages
-        # the sink/tail staging depends only on the metadata: it runs on a side
-        # stream, concurrently with centre scoring and routing
-        self.side = torch.cuda.Stream(device=d)
+        chunks = max(1, min(int(chunks), B))
+        self.bounds = [(B * k // chunks, B * (k + 1) // chunks) for k in range(chunks)]
+        # metadata + sink/tail staging depend only on the lengths and tables: a side
+        # stream runs them concurrently with centre scoring
+        # selection streams at high priority, the bandwidth-bound gather at the default
+        self.side = torch.cuda.Stream(device=d, priority=-1)
+        self.centre_stream = torch.cuda.Stream(device=d, priority=-1)
+        self.chain = [torch.cuda.Stream(device=d, priority=-1) for _ in self.bounds]
+        self.gather_stream = torch.cuda.Stream(device=d, priority=0)
+        self.ev_centre = [torch.cuda.Event() for _ in self.bounds]
+        self.ev_topk = [torch.cuda.Event() for _ in self.bounds]
 
     # -- the step ------------------------------------------------------------
+    def _centres(self, rs):
+        c = self.case
+        if self.fused_route_pages:
+            # centre scoring emits each page's max-of-8 directly; route reads P floats
+            # per row and writes the fine page table itself (fill_table)
+            scoring.fp8_paged_mqa_logits(c.q8[rs], c.centers, c.w[rs], c.lens[rs], c.center_table[rs], None,
+                                         c.P * 8, page_max=self.page_scores[rs], logits=self.keep_logits,
+                                         out=self.center_logits[rs] if self.keep_logits else None,
+                                         clean_logits=False, lens_kind="centres")
+        else:
+            scoring.fp8_paged_mqa_logits(c.q8[rs], c.centers, c.w[rs], c.lens[rs], c.center_table[rs], None,
+                                         c.P * 8, out=self.center_logits[rs], lens_kind="centres")
+
+    def _route_fine_topk(self, rs):
+        c = self.case
+        n = rs.stop - rs.start
+        if self.fused_route_pages:
+            self.fused.route_pages(self.page_scores[rs], c.lens[rs], self.takes[rs], self.selected[rs], c.P,
+                                   c.reordered_table[rs], self.fine_table[rs], self.tail_rows[rs], c.capacity,
+                                   True)
+        else:
+            self.fused.route(self.center_logits[rs], c.lens[rs], self.takes[rs], self.selected[rs], c.P,
+                             c.reordered_table[rs], self.fine_table[rs], self.tail_rows[rs], c.capacity, False)
+            K.fine_table_shared[(n,)](c.reordered_table[rs], self.selected[rs], self.takes[rs], c.lens[rs],
+                                      self.fine_table[rs], self.tail_rows[rs], c.capacity, c.P, c.take,
+                                      self.width // 64, 68)
+        scoring.fp8_paged_mqa_logits(c.q8[rs], c.fine, c.w[rs], self.dg_lens[rs], self.fine_table[rs], None,
+                                     self.width, out=self.scores[rs], clean_logits=False)
+        self.fused.topk(self.scores[rs], self.fine_lens[rs], c.members, c.reordered_table[rs],
+                        c.native_table[rs], self.selected[rs], c.lens[rs], self.takes[rs], self.physical[rs],
+                        self.logical[rs], self.raw[rs], c.window, True, self.no_expansion[rs], True, True,
+                        self.fine_table[rs], False)
+
+    def _gather(self, rs):
+        c = self.case
+        lat = c.latent
+        n = rs.stop - rs.start
+        _gather_impl((1,), lat, lat if self.gather_v else None, None, self.physical[rs], self.kv[rs],
+                     self.kv2[rs] if self.gather_v else None, n, c.topk, 0, *lat.stride(),
+                     *(lat.stride() if self.gather_v else (0, 0, 0)), self.physical.stride(0))
+
     def run(self):
         c = self.case
         B = c.B
         main = torch.cuda.current_stream(c.lens.device)
-        # metadata and the sink/tail staging run on a side stream, concurrently
-        # with centre scoring, which derives each row's centre count from the
-        # token length itself (lens_kind="centres")
         self.side.wait_stream(main)
         with torch.cuda.stream(self.side):
             self.meta[(B,)](c.lens, c.native_table, self.fine_lens, self.takes, self.dg_lens,
@@ -84,35 +142,30 @@ class SelectionStep:
                 c.native, c.native.view(torch.float32), c.native_table, c.lens, c.fine,
                 c.fine.view(torch.float32), self.tail_rows, c.capacity, c.P, 68, 64, c.window,
                 ROWS=B, GROUP=32 if B > 512 else 1)
-        if self.fused_route_pages:
-            # centre scoring emits each page's max-of-8 directly; route reads P floats
-            # per row and writes the fine page table itself (fill_table)
-            scoring.fp8_paged_mqa_logits(c.q8, c.centers, c.w, c.lens, c.center_table, None,
-                                         c.P * 8, page_max=self.page_scores, logits=self.keep_logits,
-                                         out=self.center_logits if self.keep_logits else None,
-                                         clean_logits=False, lens_kind="centres")
-            main.wait_stream(self.side)
-            self.fused.route_pages(self.page_scores, c.lens, self.takes, self.selected, c.P,
-                                   c.reordered_table, self.fine_table, self.tail_rows, c.capacity, True)
-        else:
-            scoring.fp8_paged_mqa_logits(c.q8, c.centers, c.w, c.lens, c.center_table, None,
-                                         c.P * 8, out=self.center_logits, lens_kind="centres")
-            main.wait_stream(self.side)
-            self.fused.route(self.center_logits, c.lens, self.takes, self.selected, c.P,
-                             c.reordered_table, self.fine_table, self.tail_rows, c.capacity, False)
-            K.fine_table_shared[(B,)](c.reordered_table, self.selected, self.takes, c.lens,
-                                      self.fine_table, self.tail_rows, c.capacity, c.P, c.take,
-                                      self.width // 64, 68)
-        scoring.fp8_paged_mqa_logits(c.q8, c.fine, c.w, self.dg_lens, self.fine_table, None,
-                                     self.width, out=self.scores, clean_logits=False)
-        self.fused.topk(self.scores, self.fine_lens, c.members, c.reordered_table, c.native_table,
-                        self.selected, c.lens, self.takes, self.physical, self.logical, self.raw,
-                        c.window, True, self.no_expansion, True, True, self.fine_table, False)
+        self.centre_stream.wait_stream(main)
         if self.gather:
-            lat = c.latent
-            _gather_impl((1,), lat, lat if self.gather_v else None, None, self.physical, self.kv,
-                         self.kv2, B, c.topk, 0, *lat.stride(),
-                         *(lat.stride() if self.gather_v else (0, 0, 0)), self.physical.stride(0))
+            self.gather_stream.wait_stream(main)
+        for k, (r0, r1) in enumerate(self.bounds):
+            rs = slice(r0, r1)
+            with torch.cuda.stream(self.centre_stream):
+                self._centres(rs)
+                self.ev_centre[k].record(self.centre_stream)
+            s = self.chain[k]
+            s.wait_event(self.ev_centre[k])
+            s.wait_stream(self.side)
+            with torch.cuda.stream(s):
+                self._route_fine_topk(rs)
+                self.ev_topk[k].record(s)
+            if self.gather:
+                self.gather_stream.wait_event(self.ev_topk[k])
+                with torch.cuda.stream(self.gather_stream):
+                    self._gather(rs)
+        main.wait_stream(self.side)
+        main.wait_stream(self.centre_stream)
+        for s in self.chain:
+            main.wait_stream(s)
+        if self.gather:
+            main.wait_stream(self.gather_stream)
 
     def capture(self, warmup: int = 2):
         s = torch.cuda.Stream(device=self.case.lens.device)
@@ -135,24 +188,12 @@ class SelectionStep:
 
     # -- accounting ----------------------------------------------------------
     def algorithmic_bytes(self) -> dict:
-        """Compulsory bytes of one step, each input byte once, each output once."""
+        """Compulsory bytes of one step, each input byte once, each output once
+        (the per-request sum of `sharding.row_bytes`)."""
         c = self.case
-        lens = c.lens.tolist()
-        B, H = c.B, c.H
-        pages = [max(n - 1, 0) // 1024 * 16 for n in lens]
-        take = [min(p, c.take) for p in pages]
-        sink = [min(64, n) for n in lens]
-        tail = [max(s, min(max(n - 1, 0) // 1024 * 1024, max(s, n - c.window))) for n, s in zip(lens, sink)]
-        count = [s + n - t for n, s, t in zip(lens, sink, tail)]
-        fine = [tk * 64 + cnt for tk, cnt in zip(take, count)]
-        q = B * H * (128 + 4)
-        centres = sum(p * 8 for p in pages) * 132
-        staging = sum(count) * 132 * 2
-        fine_b = sum(fine) * 132 + sum(tk * 64 * 4 for tk in take)
-        out = B * c.topk * 4 * 3
-        gather = 0
-        if self.gather:
-            row = c.latent.shape[-1] * c.latent.element_size()
-            gather = B * c.topk * row * (2 + (1 if self.gather_v else 0))
-        return dict(q=q, centres=centres, staging=staging, fine=fine_b, topk_out=out, gather=gather,
-                    total=q + centres + staging + fine_b + out + gather)
+        row = c.latent.shape[-1] * c.latent.element_size() if self.gather else 0
+        total = {}
+        for n in c.lens.tolist():
+            for k, v in row_bytes(n, c.H, c.take, c.window, c.topk, row, 2 if self.gather_v else 1).items():
+                total[k] = total.get(k, 0) + v
+        return total
