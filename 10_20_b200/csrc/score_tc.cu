@@ -171,8 +171,13 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     tma_prefetch_desc(&q_map);
     tma_prefetch_desc(&scale_map);
   }
-  pdl_wait();
-  pdl_trigger();
+  // Token-length centre counts (lens_kind 1) and everything the producers and the
+  // MMA read are caller inputs: only the epilogue, which writes, waits for the
+  // previous kernel.  Lengths of kind 0 may come from the previous kernel.
+  if (a.lens_kind == 0) {
+    pdl_wait();
+    pdl_trigger();
+  }
   {
     const int chunk = (a.B + kTcThreads - 1) / kTcThreads;
     const int beg = min(tid * chunk, a.B), end = min(beg + chunk, a.B);
@@ -291,6 +296,10 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     const int g = (warp - kEpiWarp0) >> 2;
     const int q4 = warp & 3;                      // TMEM lane quarter this warp may access
     const int i = q4 * 32 + lane;                 // key of the 128-key tile == TMEM lane
+    if (a.lens_kind != 0) {
+      pdl_wait();
+      pdl_trigger();
+    }
     // the epilogue warps alone stage the head weights (off the producers' path)
     if (w_staged)
       for (int e = tid - 32 * kEpiWarp0; e < (b_last - b_first + 1) * a.H; e += kTcThreads - 32 * kEpiWarp0)

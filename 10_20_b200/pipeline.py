@@ -5,7 +5,7 @@ query sequence (sglang/srt/layers/attention/v1_deepseek/runtime.py:417-636,
 DeepGEMM ReLU path with fused route and fused topk) on libv1x.so kernels:
 
   1. query metadata with the fixed page budget  (BudgetMetadata)        :364-368
-     (side stream, with step 4's staging)
+     and the sink/tail staging of step 4
   2. FP8 centre logits of every built page's 8 centres                  :434-444
      (centre counts derived from the token lengths in the scorer)
   3. fused.route: page max-of-8 + stable top pages                      :446-448
@@ -32,17 +32,14 @@ from .sharding import row_bytes
 class SelectionStep:
     """One query step over a batch of rows (see the module docstring).
 
-    chunks > 1 splits the rows into that many consecutive chunks and pipelines
-    them: centre scoring runs chunk after chunk on one stream, and as soon as a
-    chunk's centres are scored its route -> fine scoring -> top-k chain runs on
-    its own stream while the next chunk's centres are scored; its gather then
-    runs on a low-priority stream.  The latency-bound kernels (route, top-k)
-    thereby overlap bandwidth-bound ones.  Outputs are identical for any chunk
-    count: rows are independent.
+    All kernels run in order on the caller's current stream.  Each is launched
+    with programmatic stream serialization, so it starts while its predecessor
+    drains; the centre scorer reads only caller inputs before its epilogue, so
+    it streams centre pages while metadata and staging are still running.
     """
 
     def __init__(self, case, gather: bool = True, gather_v: bool = False, fused_route_pages: bool = True,
-                 keep_logits: bool = False, chunks: int = 1):
+                 keep_logits: bool = False):
         c = self.case = case
         d = c.lens.device
         B = c.B
@@ -76,17 +73,6 @@ class SelectionStep:
         # outputs to route(center_logits) + fine_table_shared.
         self.fused_route_pages = fused_route_pages
         self.keep_logits = keep_logits or not fused_route_pages
-        chunks = max(1, min(int(chunks), B))
-        self.bounds = [(B * k // chunks, B * (k + 1) // chunks) for k in range(chunks)]
-        # metadata + sink/tail staging depend only on the lengths and tables: a side
-        # stream runs them concurrently with centre scoring
-        # selection streams at high priority, the bandwidth-bound gather at the default
-        self.side = torch.cuda.Stream(device=d, priority=-1)
-        self.centre_stream = torch.cuda.Stream(device=d, priority=-1)
-        self.chain = [torch.cuda.Stream(device=d, priority=-1) for _ in self.bounds]
-        self.gather_stream = torch.cuda.Stream(device=d, priority=0)
-        self.ev_centre = [torch.cuda.Event() for _ in self.bounds]
-        self.ev_topk = [torch.cuda.Event() for _ in self.bounds]
 
     # -- the step ------------------------------------------------------------
     def _centres(self, rs):
@@ -102,7 +88,7 @@ class SelectionStep:
             scoring.fp8_paged_mqa_logits(c.q8[rs], c.centers, c.w[rs], c.lens[rs], c.center_table[rs], None,
                                          c.P * 8, out=self.center_logits[rs], lens_kind="centres")
 
-    def _route_fine_topk(self, rs):
+    def _route(self, rs):
         c = self.case
         n = rs.stop - rs.start
         if self.fused_route_pages:
@@ -115,6 +101,9 @@ class SelectionStep:
             K.fine_table_shared[(n,)](c.reordered_table[rs], self.selected[rs], self.takes[rs], c.lens[rs],
                                       self.fine_table[rs], self.tail_rows[rs], c.capacity, c.P, c.take,
                                       self.width // 64, 68)
+
+    def _fine_topk(self, rs):
+        c = self.case
         scoring.fp8_paged_mqa_logits(c.q8[rs], c.fine, c.w[rs], self.dg_lens[rs], self.fine_table[rs], None,
                                      self.width, out=self.scores[rs], clean_logits=False)
         self.fused.topk(self.scores[rs], self.fine_lens[rs], c.members, c.reordered_table[rs],
@@ -133,39 +122,18 @@ class SelectionStep:
     def run(self):
         c = self.case
         B = c.B
-        main = torch.cuda.current_stream(c.lens.device)
-        self.side.wait_stream(main)
-        with torch.cuda.stream(self.side):
-            self.meta[(B,)](c.lens, c.native_table, self.fine_lens, self.takes, self.dg_lens,
-                            self.center_lens, self.tail_rows, c.P, c.topk, 1, 2, 64, c.window)
-            K.stage_tail_shared[(-(-B // 32) if B > 512 else B, 68)](
-                c.native, c.native.view(torch.float32), c.native_table, c.lens, c.fine,
-                c.fine.view(torch.float32), self.tail_rows, c.capacity, c.P, 68, 64, c.window,
-                ROWS=B, GROUP=32 if B > 512 else 1)
-        self.centre_stream.wait_stream(main)
+        rs = slice(0, B)
+        self.meta[(B,)](c.lens, c.native_table, self.fine_lens, self.takes, self.dg_lens,
+                        self.center_lens, self.tail_rows, c.P, c.topk, 1, 2, 64, c.window)
+        K.stage_tail_shared[(-(-B // 32) if B > 512 else B, 68)](
+            c.native, c.native.view(torch.float32), c.native_table, c.lens, c.fine,
+            c.fine.view(torch.float32), self.tail_rows, c.capacity, c.P, 68, 64, c.window,
+            ROWS=B, GROUP=32 if B > 512 else 1)
+        self._centres(rs)
+        self._route(rs)
+        self._fine_topk(rs)
         if self.gather:
-            self.gather_stream.wait_stream(main)
-        for k, (r0, r1) in enumerate(self.bounds):
-            rs = slice(r0, r1)
-            with torch.cuda.stream(self.centre_stream):
-                self._centres(rs)
-                self.ev_centre[k].record(self.centre_stream)
-            s = self.chain[k]
-            s.wait_event(self.ev_centre[k])
-            s.wait_stream(self.side)
-            with torch.cuda.stream(s):
-                self._route_fine_topk(rs)
-                self.ev_topk[k].record(s)
-            if self.gather:
-                self.gather_stream.wait_event(self.ev_topk[k])
-                with torch.cuda.stream(self.gather_stream):
-                    self._gather(rs)
-        main.wait_stream(self.side)
-        main.wait_stream(self.centre_stream)
-        for s in self.chain:
-            main.wait_stream(s)
-        if self.gather:
-            main.wait_stream(self.gather_stream)
+            self._gather(rs)
 
     def capture(self, warmup: int = 2):
         s = torch.cuda.Stream(device=self.case.lens.device)

@@ -179,8 +179,6 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="decode", choices=["decode", "single"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--chunks", type=int, default=4,
-                    help="row chunks pipelined inside the step (selection of chunk k+1 overlaps chunk k)")
     args = ap.parse_args()
     cfg = workload_cfg(args.workload)
     if args.requests:
@@ -220,7 +218,7 @@ def main():
             lens = lens_all
     seed = 1000 + rank
     case = make_case(synth, cfg, seed, device, lens=lens)
-    step = pipeline.SelectionStep(case, gather=cfg["latent"] > 0, chunks=args.chunks)
+    step = pipeline.SelectionStep(case, gather=cfg["latent"] > 0)
     acct = step.algorithmic_bytes()
     gather_on = step.gather
     s = torch.cuda.Stream(device=device)
@@ -254,8 +252,7 @@ def main():
                                                       case.topk, 0, *lat.stride(), 0, 0, 0,
                                                       step.physical.stride(0)))
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
-    chunks = len(step.bounds)
-    launches_per_step = 2 + chunks * (4 + (1 if gather_on else 0))
+    launches_per_step = 6 + (1 if gather_on else 0)
 
     def timed(graph, n):
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
@@ -348,7 +345,6 @@ def main():
                        "context": [cfg["lo"], cfg["hi"]], "latent_dim": cfg["latent"],
                        "parallelism": f"requests sharded by bytes (longest first), {world} ranks x "
                                       f"{case.B} requests, no data-path collective",
-                       "row_chunks": chunks,
                        "l2": "flushed (256 MB write) between timed steps; e2e: working set 0.86 GB > L2",
                        "algorithmic_bytes_per_step": acct["total"]},
             "step_hbm_gbs": acct["total"] / (total_ms / args.steps / 1e3) / 1e9,
