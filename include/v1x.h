@@ -264,6 +264,15 @@ V1X_API int v1x_gather_slots(const void* k, const void* v, const int32_t* req, c
                      int64_t ks1, int64_t ks2, int64_t vs0, int64_t vs1, int64_t vs2,
                      int64_t ids_stride, int64_t dim, int64_t elem_bytes, void* stream);
 
+/* ------------------------------------------------------------------------ */
+/* Extension (no reference counterpart): failure-detection self test.  Launches
+ * one kernel that waits, with the same bounded mbarrier wait the pipelined
+ * kernels use, on a barrier nothing arrives at; after limit_ns (plus at most
+ * ~64 ms of polling granularity) it writes V1X_STATUS_TIMEOUT to *status and,
+ * if elapsed_ns is not NULL, the measured wait (u64 ns).  The context remains
+ * usable.  0 < limit_ns <= 10 s. */
+V1X_API int v1x_selftest_wait_timeout(int64_t limit_ns, int32_t* status, uint64_t* elapsed_ns, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
