@@ -27,6 +27,20 @@ int launch_status(const char* what) {
   return V1X_OK;
 }
 
+int greatest_priority() {
+  static int cached[64] = {};
+  static bool have[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  if (!have[dev]) {
+    int least = 0, greatest = 0;
+    if (cudaDeviceGetStreamPriorityRange(&least, &greatest) != cudaSuccess) greatest = 0;
+    cached[dev] = greatest;
+    have[dev] = true;
+  }
+  return cached[dev];
+}
+
 int num_sms() {
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) {

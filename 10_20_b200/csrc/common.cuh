@@ -55,20 +55,35 @@ struct DeviceOnce {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// Scheduling priority of a launch: the latency-bound selection kernels are
+// launched at the device's greatest priority so that, when another batch's
+// bandwidth-bound gather runs beside them, their CTAs are placed first as SM
+// slots free up; the gather keeps the default (lowest) priority.
+enum class LaunchPriority { kHigh, kDefault };
+int greatest_priority();
+
 template <typename... KArgs, typename... Args>
-inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
-                       Args... args) {
+inline void launch_pdl_prio(LaunchPriority prio, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                            cudaStream_t stream, Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributePriority;
+  attr[1].val.priority = prio == LaunchPriority::kHigh ? greatest_priority() : 0;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args... args) {
+  launch_pdl_prio(LaunchPriority::kHigh, kernel, grid, block, smem, stream, args...);
 }
 
 // ---- device helpers ---------------------------------------------------------

@@ -6,11 +6,13 @@
 // K[REQ[ids[q, j]], HEAD, :] (and V), or zeros when the id is negative.  The
 // reference fixes D = 128; any D is accepted here (D = 576 for the MLA latent).
 //
-// Design: a pure HBM copy.  The vector path moves 16-byte chunks: consecutive
-// threads own consecutive chunks of the flat output (fully coalesced stores,
-// row-contiguous loads), each thread keeps 4 chunk loads (8 with V) in flight
-// before storing, loads bypass L1 and stores are marked evict-first so the
-// streamed output does not flush the slot index out of L2.
+// Design: a pure HBM copy.  Rows of 72 or 16 16-byte chunks (the 576-wide
+// latent, 128-wide heads) take gather_rows_kernel (a warp per group of rows,
+// chunk counts known at compile time); other 16-byte-aligned rows take the
+// general vector path (consecutive threads own consecutive chunks of the flat
+// output, 4 loads in flight per thread); anything else the scalar path.  Loads
+// bypass L1 and stores are marked evict-first so the streamed output does not
+// flush the slot index out of L2.
 #include "common.cuh"
 
 namespace v1x {
@@ -72,6 +74,60 @@ __global__ void __launch_bounds__(256) gather_vec_kernel(const __grid_constant__
   }
 }
 
+// Rows of a compile-time number of 16-byte chunks (kCpr: 72 for the 576-wide
+// bf16 latent, 16 for 128-wide bf16 heads): a warp copies kR consecutive output
+// rows at a time.  The row -> slot lookups are done once per row by kR lanes and
+// broadcast with shuffles, the (row, chunk) split of a lane's flat index is a
+// division by a constant, and every lane keeps kPer 16-byte loads in flight
+// (kCpr * kR is a multiple of 32, so no lane idles).  Per chunk this is a handful
+// of instructions -- the general path above spends a 64-bit division per chunk,
+// which at ~37M chunks per decode step is as long as the copy itself.
+template <int kCpr, int kR, bool kHasV>
+__global__ void __launch_bounds__(256) gather_rows_kernel(const __grid_constant__ GatherArgs a) {
+  static_assert((kCpr * kR) % 32 == 0, "a row group must fill the warp's lanes");
+  constexpr int kPer = kCpr * kR / 32;
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int64_t nrows = a.rows * a.top;
+  const int64_t ngroups = (nrows + kR - 1) / kR;
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  const unsigned char* kbase = a.k + a.head * a.ks1 * a.elem;
+  const unsigned char* vbase = kHasV ? a.v + a.head * a.vs1 * a.elem : nullptr;
+  const int64_t krow = a.ks0 * a.elem, vrow = kHasV ? a.vs0 * a.elem : 0;
+  for (int64_t g = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); g < ngroups;
+       g += nwarps) {
+    const int64_t t0 = g * kR;
+    int64_t my_slot = -1;
+    if (lane < kR && t0 + lane < nrows) my_slot = slot_of(a, t0 + lane);
+    uint4 kv[kPer], vv[kPer];
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int f = lane + 32 * i;
+      const int r = f / kCpr, c = f - r * kCpr;
+      const int64_t s = __shfl_sync(0xffffffffu, my_slot, r);
+      kv[i] = make_uint4(0, 0, 0, 0);
+      if (kHasV) vv[i] = make_uint4(0, 0, 0, 0);
+      if (s >= 0) {
+        kv[i] = __ldcs(reinterpret_cast<const uint4*>(kbase + s * krow) + c);
+        if (kHasV) vv[i] = __ldcs(reinterpret_cast<const uint4*>(vbase + s * vrow) + c);
+      }
+    }
+    // output rows are contiguous: the group's chunks are one coalesced span
+    uint4* ko = reinterpret_cast<uint4*>(a.kg) + t0 * kCpr;
+    uint4* vo = kHasV ? reinterpret_cast<uint4*>(a.vg) + t0 * kCpr : nullptr;
+    const int64_t limit = (nrows - t0) * kCpr;  // chunks left in the output
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int f = lane + 32 * i;
+      if (f < limit) {
+        __stcs(ko + f, kv[i]);
+        if (kHasV) __stcs(vo + f, vv[i]);
+      }
+    }
+  }
+}
+
 template <typename T>
 __global__ void gather_scalar_kernel(const __grid_constant__ GatherArgs a) {
   pdl_wait();
@@ -120,19 +176,32 @@ extern "C" int v1x_gather_slots(const void* k, const void* v, const int32_t* req
   if (hv) vec = vec && vs2 == 1 && (vs0 * elem_bytes) % 16 == 0 && (vs1 * elem_bytes) % 16 == 0 && al16(v) && al16(vg);
   cudaStream_t s = as_stream(stream);
   const int64_t sms = num_sms();
-  if (vec) {
+  const int64_t cpr = vec ? dim * elem_bytes / 16 : 0;
+  if (vec && (cpr == 72 || cpr == 16)) {
+    const int64_t groups = (rows * top + (cpr == 72 ? 4 : 8) - 1) / (cpr == 72 ? 4 : 8);
+    int64_t blocks = (groups + 7) / 8;
+    blocks = blocks < sms * 16 ? blocks : sms * 16;
+    const dim3 grid(static_cast<unsigned>(blocks)), block(256);
+    if (cpr == 72) {
+      if (hv) launch_pdl_prio(LaunchPriority::kDefault, gather_rows_kernel<72, 4, true>, grid, block, 0, s, a);
+      else launch_pdl_prio(LaunchPriority::kDefault, gather_rows_kernel<72, 4, false>, grid, block, 0, s, a);
+    } else {
+      if (hv) launch_pdl_prio(LaunchPriority::kDefault, gather_rows_kernel<16, 8, true>, grid, block, 0, s, a);
+      else launch_pdl_prio(LaunchPriority::kDefault, gather_rows_kernel<16, 8, false>, grid, block, 0, s, a);
+    }
+  } else if (vec) {
     const int64_t total = rows * top * dim * elem_bytes / 16;
     int64_t blocks = (total + 256 * kUnroll - 1) / (256 * kUnroll);
     blocks = blocks < sms * 16 ? blocks : sms * 16;
-    if (hv) launch_pdl(gather_vec_kernel<true>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, a);
-    else launch_pdl(gather_vec_kernel<false>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, a);
+    if (hv) launch_pdl_prio(LaunchPriority::kDefault, gather_vec_kernel<true>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, a);
+    else launch_pdl_prio(LaunchPriority::kDefault, gather_vec_kernel<false>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, a);
   } else {
     const int64_t total = rows * top * dim;
     int64_t blocks = (total + 255) / 256;
     blocks = blocks < sms * 32 ? blocks : sms * 32;
-    if (elem_bytes == 1) launch_pdl(gather_scalar_kernel<uint8_t>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, a);
-    else if (elem_bytes == 2) launch_pdl(gather_scalar_kernel<uint16_t>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, a);
-    else launch_pdl(gather_scalar_kernel<uint32_t>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, a);
+    if (elem_bytes == 1) launch_pdl_prio(LaunchPriority::kDefault, gather_scalar_kernel<uint8_t>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, a);
+    else if (elem_bytes == 2) launch_pdl_prio(LaunchPriority::kDefault, gather_scalar_kernel<uint16_t>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, a);
+    else launch_pdl_prio(LaunchPriority::kDefault, gather_scalar_kernel<uint32_t>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, a);
   }
   return launch_status("v1x_gather_slots");
 }
