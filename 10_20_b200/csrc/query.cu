@@ -18,35 +18,62 @@ __device__ __forceinline__ int64_t take_rule(int64_t pages, int64_t topk, int64_
   return min(pages, max((pages * num + den - 1) / den, (topk + 63) / 64));
 }
 
-__global__ void __launch_bounds__(128) query_metadata_kernel(
-    const int32_t* __restrict__ lens, const int32_t* __restrict__ nt, int32_t* __restrict__ fine_lens,
-    int32_t* __restrict__ takes, int32_t* __restrict__ dg_lens, int32_t* __restrict__ center_lens,
-    int32_t* __restrict__ tail_rows, int64_t np, int64_t topk, int64_t num, int64_t den, int64_t sink_cfg,
-    int64_t window, const int32_t* __restrict__ budget) {
-  const int64_t row = blockIdx.x;
-  const int n = lens[row];
-  const int64_t pages = static_cast<int64_t>(max(n - 1, 0) / 1024) * 16;
-  const int64_t take = take_rule(pages, topk, num, den, budget);
-  const RowBounds rb = row_bounds(n, static_cast<int>(sink_cfg), static_cast<int>(window));
-  const int64_t fine = take * 64 + rb.sink + n - rb.tail;
+struct MetaArgs {
+  const int32_t* lens;
+  const int32_t* nt;
+  int32_t* fine_lens;
+  int32_t* takes;
+  int32_t* dg_lens;
+  int32_t* center_lens;
+  int32_t* tail_rows;
+  int64_t np, topk, num, den, sink_cfg, window;
+  const int32_t* budget;
+};
+
+struct RowMeta {
+  int n;
+  RowBounds rb;
+  int64_t pages, take, fine;
+  bool owner;  // tail_rows[row] == row: the row stages its own sink/tail pages
+};
+
+// Per-row metadata (:568-591) computed by one CTA (threads 0..127 take part in
+// the page-id comparison).  Reads caller inputs only.
+__device__ __forceinline__ RowMeta row_meta(const MetaArgs& a, int64_t row) {
+  RowMeta m;
+  m.n = a.lens[row];
+  m.pages = static_cast<int64_t>(max(m.n - 1, 0) / 1024) * 16;
+  m.take = take_rule(m.pages, a.topk, a.num, a.den, a.budget);
+  m.rb = row_bounds(m.n, static_cast<int>(a.sink_cfg), static_cast<int>(a.window));
+  m.fine = m.take * 64 + m.rb.sink + m.n - m.rb.tail;
   // share the staging copy with row 0 only if the length and every page id the
   // sink/tail copy touches are identical (:583-591)
   const int i = threadIdx.x;
-  const int64_t page = i == 0 ? 0 : rb.tail / 64 + i - 1;
-  const bool valid = (n > 0) && ((i == 0) || (page < (static_cast<int64_t>(n) + 63) / 64)) && (page < np);
-  const int mine = valid ? nt[row * np + page] : -1;
-  const int first = valid ? nt[page] : -1;
+  const int64_t page = i == 0 ? 0 : m.rb.tail / 64 + i - 1;
+  const bool valid = i < 128 && (m.n > 0) && ((i == 0) || (page < (static_cast<int64_t>(m.n) + 63) / 64)) &&
+                     (page < a.np);
+  const int mine = valid ? a.nt[row * a.np + page] : -1;
+  const int first = valid ? a.nt[page] : -1;
   const int differs = __syncthreads_or(mine != first);
+  const bool share = (m.n == a.lens[0]) && !differs;
+  m.owner = !share || row == 0;
+  return m;
+}
+
+__device__ __forceinline__ void write_meta(const MetaArgs& a, int64_t row, const RowMeta& m) {
+  a.fine_lens[row] = static_cast<int32_t>(m.fine);
+  a.takes[row] = static_cast<int32_t>(m.take);
+  a.dg_lens[row] = static_cast<int32_t>(max(m.fine, int64_t(1)));
+  a.center_lens[row] = static_cast<int32_t>(max(m.pages * 8, int64_t(1)));
+  a.tail_rows[row] = m.owner ? static_cast<int32_t>(row) : 0;
+}
+
+__global__ void __launch_bounds__(128) query_metadata_kernel(const __grid_constant__ MetaArgs a) {
+  const int64_t row = blockIdx.x;
+  const RowMeta m = row_meta(a, row);
   pdl_wait();  // everything above reads caller inputs only
   pdl_trigger();
-  if (i == 0) {
-    const bool share = (n == lens[0]) && !differs;
-    fine_lens[row] = static_cast<int32_t>(fine);
-    takes[row] = static_cast<int32_t>(take);
-    dg_lens[row] = static_cast<int32_t>(max(fine, int64_t(1)));
-    center_lens[row] = static_cast<int32_t>(max(pages * 8, int64_t(1)));
-    tail_rows[row] = share ? 0 : static_cast<int32_t>(row);
-  }
+  if (threadIdx.x == 0) write_meta(a, row, m);
 }
 
 __global__ void query_lengths_kernel(const int32_t* __restrict__ lens, int32_t* __restrict__ fine_lens,
@@ -101,20 +128,9 @@ struct StageArgs {
 // reference does (pages p with p*64 < count, plus page 0).
 constexpr int kStagePages = 4;
 
-__global__ void __launch_bounds__(256) stage_tail_shared_kernel(const __grid_constant__ StageArgs a,
-                                                                int64_t grid_pages) {
-  const int64_t row = blockIdx.x;
-  pdl_wait();
-  pdl_trigger();
-  if (a.rows_bound > 0 && row >= a.rows_bound) return;
-  if (a.tail_rows[row] != row) return;
-  const int n = a.lens[row];
-  const RowBounds rb = row_bounds(n, static_cast<int>(a.sink), static_cast<int>(a.window));
-  const int count = rb.sink + n - rb.tail;
-  const int64_t need = min(grid_pages, static_cast<int64_t>(max((count + 63) / 64, 1)));
-  const int p0 = blockIdx.y * kStagePages;
-  const int p1 = static_cast<int>(min(need, static_cast<int64_t>(p0 + kStagePages)));
-  if (p0 >= p1) return;
+// Copies staging pages [p0, p1) of an owner row (any block size).
+__device__ __forceinline__ void stage_pages(const StageArgs& a, int64_t row, const RowBounds& rb, int count, int p0,
+                                            int p1) {
   const int chunks = (p1 - p0) * 512;
   constexpr int U = 4;
   for (int c0 = threadIdx.x; c0 < chunks; c0 += blockDim.x * U) {
@@ -151,6 +167,46 @@ __global__ void __launch_bounds__(256) stage_tail_shared_kernel(const __grid_con
     }
     a.fscale[(a.cap + row * a.scratch + p) * kPageWords + kScaleWord + tok] = s;
   }
+}
+
+__global__ void __launch_bounds__(256) stage_tail_shared_kernel(const __grid_constant__ StageArgs a,
+                                                                int64_t grid_pages) {
+  const int64_t row = blockIdx.x;
+  pdl_wait();
+  pdl_trigger();
+  if (a.rows_bound > 0 && row >= a.rows_bound) return;
+  if (a.tail_rows[row] != row) return;
+  const int n = a.lens[row];
+  const RowBounds rb = row_bounds(n, static_cast<int>(a.sink), static_cast<int>(a.window));
+  const int count = rb.sink + n - rb.tail;
+  const int64_t need = min(grid_pages, static_cast<int64_t>(max((count + 63) / 64, 1)));
+  const int p0 = blockIdx.y * kStagePages;
+  const int p1 = static_cast<int>(min(need, static_cast<int64_t>(p0 + kStagePages)));
+  if (p0 >= p1) return;
+  stage_pages(a, row, rb, count, p0, p1);
+}
+
+// Metadata + sink/tail staging in one launch: CTA (row, g) derives the row's
+// metadata itself (row 0's page ids decide the shared-tail owner), CTAs with
+// g == 0 write it, and an owner row's CTAs stage pages [4g, 4g + 4).  Equal to
+// query_metadata followed by stage_tail_shared (every owner row stages its own
+// pages; the reference's row grouping only changes which program copies them).
+// Light CTAs (128 threads, no shared memory), so the centre scorer launched
+// next can be resident beside them.
+__global__ void __launch_bounds__(128) query_prepare_kernel(const __grid_constant__ MetaArgs m,
+                                                            const __grid_constant__ StageArgs s) {
+  const int64_t row = blockIdx.x;
+  const RowMeta r = row_meta(m, row);
+  pdl_wait();
+  pdl_trigger();
+  if (blockIdx.y == 0 && threadIdx.x == 0) write_meta(m, row, r);
+  if (!r.owner) return;
+  const int count = r.rb.sink + r.n - r.rb.tail;
+  const int64_t need = min(s.scratch, static_cast<int64_t>(max((count + 63) / 64, 1)));
+  const int p0 = blockIdx.y * kStagePages;
+  const int p1 = static_cast<int>(min(need, static_cast<int64_t>(p0 + kStagePages)));
+  if (p0 >= p1) return;
+  stage_pages(s, row, r.rb, count, p0, p1);
 }
 
 __global__ void mask_fine_kernel(float* __restrict__ scores, const void* selected, int sel64,
@@ -266,10 +322,31 @@ extern "C" int v1x_query_metadata(const int32_t* lens, const int32_t* nt, int32_
   clear_error();
   V1X_CHECK_ARG(batch >= 0 && np > 0 && den > 0 && num >= 0, "query_metadata: bad geometry");
   if (batch == 0) return V1X_OK;
-  launch_pdl(query_metadata_kernel, dim3(static_cast<unsigned>(batch)), dim3(128), 0, as_stream(stream),
-             lens, nt, fine_lens, takes, dg_lens, center_lens, tail_rows, np, topk, num, den, sink, window,
-      budget);
+  const MetaArgs a{lens, nt, fine_lens, takes, dg_lens, center_lens, tail_rows, np, topk, num, den, sink, window,
+                   budget};
+  launch_pdl(query_metadata_kernel, dim3(static_cast<unsigned>(batch)), dim3(128), 0, as_stream(stream), a);
   return launch_status("v1x_query_metadata");
+}
+
+extern "C" int v1x_query_prepare(const int32_t* lens, const int32_t* nt, int32_t* fine_lens, int32_t* takes,
+                                 int32_t* dg_lens, int32_t* center_lens, int32_t* tail_rows, int64_t np,
+                                 int64_t topk, int64_t num, int64_t den, int64_t sink, int64_t window,
+                                 const int32_t* budget, const uint8_t* native_bytes, const float* native_scales,
+                                 uint8_t* fine_bytes, float* fine_scales, int64_t cap, int64_t scratch,
+                                 int64_t batch, void* stream) {
+  clear_error();
+  V1X_CHECK_ARG(batch >= 0 && np > 0 && den > 0 && num >= 0, "query_prepare: bad geometry");
+  V1X_CHECK_ARG(scratch >= 1 && scratch < 65536 * kStagePages && cap >= 0, "query_prepare: bad staging geometry");
+  V1X_CHECK_ARG(((reinterpret_cast<uintptr_t>(native_bytes) | reinterpret_cast<uintptr_t>(fine_bytes)) & 15) == 0,
+                "query_prepare: page pools must be 16-byte aligned");
+  if (batch == 0) return V1X_OK;
+  const MetaArgs m{lens, nt, fine_lens, takes, dg_lens, center_lens, tail_rows, np, topk, num, den, sink, window,
+                   budget};
+  const StageArgs s{native_bytes, native_scales, nt, lens, fine_bytes, fine_scales, tail_rows, cap, np,
+                    scratch, sink, window, batch, 1};
+  const dim3 grid(static_cast<unsigned>(batch), static_cast<unsigned>((scratch + kStagePages - 1) / kStagePages));
+  launch_pdl(query_prepare_kernel, grid, dim3(128), 0, as_stream(stream), m, s);
+  return launch_status("v1x_query_prepare");
 }
 
 extern "C" int v1x_query_lengths(const int32_t* lens, int32_t* fine_lens, int32_t* takes,

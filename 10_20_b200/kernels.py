@@ -215,6 +215,18 @@ def stage_tail_shared(grid, NATIVE, NS, NT, LENS, K, KS, TAIL_ROWS, CAP, NP, SCR
               int(GROUP), int(g[0]), int(g[1]), _s(NT), device=NT.device)
 
 
+def query_prepare(LENS, NT, FLENS, TAKES, DG_LENS, CENTER_LENS, TAIL_ROWS, NP, TOPK, NUM, DEN, SINK, WINDOW,
+                  NATIVE, NS, K, KS, CAP, SCRATCH, budget=None):
+    """Extension: query_metadata + stage_tail_shared in one launch (one program per
+    row and group of 4 staging pages).  Same arguments and outputs as the two
+    reference ops; `budget` as in BudgetMetadata."""
+    require(NS.dtype == torch.float32 and KS.dtype == torch.float32, "NS/KS must be float32 views")
+    _lib.call("v1x_query_prepare", ptr(LENS), ptr(NT), ptr(FLENS), ptr(TAKES), ptr(DG_LENS), ptr(CENTER_LENS),
+              ptr(TAIL_ROWS), int(NP), int(TOPK), int(NUM), int(DEN), int(SINK), int(WINDOW),
+              ptr(budget) if budget is not None else None, ptr(NATIVE), ptr(NS), ptr(K), ptr(KS), int(CAP),
+              int(SCRATCH), LENS.shape[0], _s(LENS), device=LENS.device)
+
+
 @_op
 def mask_fine(grid, SCORES, SELECTED, RT, MEMBERS, LENS, TAKES, MAXP, TAKE, STRIDE, WIDTH, SINK,
               WINDOW):

@@ -123,12 +123,10 @@ class SelectionStep:
         c = self.case
         B = c.B
         rs = slice(0, B)
-        self.meta[(B,)](c.lens, c.native_table, self.fine_lens, self.takes, self.dg_lens,
-                        self.center_lens, self.tail_rows, c.P, c.topk, 1, 2, 64, c.window)
-        K.stage_tail_shared[(-(-B // 32) if B > 512 else B, 68)](
-            c.native, c.native.view(torch.float32), c.native_table, c.lens, c.fine,
-            c.fine.view(torch.float32), self.tail_rows, c.capacity, c.P, 68, 64, c.window,
-            ROWS=B, GROUP=32 if B > 512 else 1)
+        # query metadata with the fixed page budget + sink/tail staging, one launch
+        K.query_prepare(c.lens, c.native_table, self.fine_lens, self.takes, self.dg_lens, self.center_lens,
+                        self.tail_rows, c.P, c.topk, 1, 2, 64, c.window, c.native, c.native.view(torch.float32),
+                        c.fine, c.fine.view(torch.float32), c.capacity, 68, budget=self.budget)
         self._centres(rs)
         self._route(rs)
         self._fine_topk(rs)

@@ -173,6 +173,17 @@ V1X_API int v1x_query_metadata(const int32_t* lens, const int32_t* nt, int32_t* 
                        int64_t sink, int64_t window, const int32_t* budget, int64_t batch,
                        void* stream);
 
+/* Extension (no reference counterpart): v1x_query_metadata followed by
+ * v1x_stage_tail_shared (grid form rows_bound = group-of-1 = batch, grid_pages =
+ * scratch) in one launch.  Outputs are identical to the two calls; the reference
+ * runs them as two kernels (DS/runtime.py:364-368, :492-509). */
+V1X_API int v1x_query_prepare(const int32_t* lens, const int32_t* nt, int32_t* fine_lens, int32_t* takes,
+                      int32_t* dg_lens, int32_t* center_lens, int32_t* tail_rows, int64_t np,
+                      int64_t topk, int64_t num, int64_t den, int64_t sink, int64_t window,
+                      const int32_t* budget, const uint8_t* native_bytes, const float* native_scales,
+                      uint8_t* fine_bytes, float* fine_scales, int64_t cap, int64_t scratch,
+                      int64_t batch, void* stream);
+
 /* DS/kernels.py:224-245. */
 V1X_API int v1x_query_lengths(const int32_t* lens, int32_t* fine_lens, int32_t* takes, int64_t topk,
                       int64_t num, int64_t den, int64_t sink, int64_t window, int64_t batch,

@@ -162,3 +162,34 @@ def test_gather_latent_random(D, strided, cuda_dev):
         e, _ = O.gather_slots(kp.contiguous().view(torch.int16).cpu().numpy(), None, None,
                               idc.cpu().numpy(), rows, top, 1)
         assert np.array_equal(out.view(torch.int16).reshape(-1, D).cpu().numpy(), e)
+
+
+def test_query_prepare_equals_metadata_then_staging(cuda_dev):
+    """The fused metadata + staging launch == query_metadata + stage_tail_shared."""
+    synth = importlib.import_module("10_20_b200.synth")
+    rng = np.random.default_rng(17)
+    B, P = 9, 256
+    lens = rng.integers(100, P * 64, size=B).tolist()
+    lens[1] = lens[0]
+    lens[2], lens[3] = 0, 40
+    case = synth.make_query_case(B, 4, lens, P=P, take=8, window=64, topk=512, seed=3, device="cuda")
+    case.native_table[1] = case.native_table[0]      # row 1 shares row 0's tail pages
+    budget = torch.tensor([8], dtype=torch.int32, device="cuda")
+    outs = []
+    for fused in (False, True):
+        meta = [torch.full((B,), -7, dtype=torch.int32, device="cuda") for _ in range(5)]
+        fine = case.fine.clone()
+        fine[case.capacity:] = 255
+        if fused:
+            K.query_prepare(case.lens, case.native_table, *meta, P, 512, 1, 2, 64, 64, case.native,
+                            case.native.view(torch.float32), fine, fine.view(torch.float32), case.capacity, 68,
+                            budget=budget)
+        else:
+            K.BudgetMetadata(budget)[(B,)](case.lens, case.native_table, *meta, P, 512, 1, 2, 64, 64)
+            K.stage_tail_shared[(B, 68)](case.native, case.native.view(torch.float32), case.native_table,
+                                         case.lens, fine, fine.view(torch.float32), meta[4], case.capacity,
+                                         P, 68, 64, 64, ROWS=B, GROUP=1)
+        outs.append((torch.stack(meta).cpu().numpy(), fine[case.capacity:].cpu().numpy()))
+    assert np.array_equal(outs[0][0], outs[1][0])
+    assert outs[0][0][4][1] == 0                       # the shared row points at row 0
+    assert np.array_equal(outs[0][1], outs[1][1])
