@@ -10,10 +10,10 @@ Workloads (synthetic, seeded; shapes of the benchmark configurations):
           bf16 MLA latent (single output: K and V are the same latent).
   single  1024 single-head queries over 64 built pages + 65-token tail
           (2688 candidates), route -> score -> Top-2048 (no gather).
-A step is one pass of the whole selection path over one batch.  Two
-independent batches (separate pools, same context lengths) are in flight on two
-streams, alternating, so the gather of one batch overlaps the selection of the
-next (`--inflight 1` runs one batch at a time).  Requests are independent, so N
+A step is one pass of the whole selection path over one batch.  Three
+independent batches (separate pools, same context lengths) are in flight on three
+streams, in turn, so the gather of one batch overlaps the selection of the next
+(`--inflight 1` runs one batch at a time).  Requests are independent, so N
 GPUs run N shares of the job's requests (weak scaling, no collective on the data
 path); `value` is the whole-job queries/s = N*B*K / max-over-ranks device time of
 the K timed steps.  Rank 0 prints one JSON line.
@@ -182,7 +182,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="decode", choices=["decode", "single"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--inflight", type=int, default=2,
+    ap.add_argument("--inflight", type=int, default=3,
                     help="independent batches in flight (the gather of one overlaps the selection of the next)")
     args = ap.parse_args()
     cfg = workload_cfg(args.workload)
