@@ -1,0 +1,160 @@
+"""Host driver of the V1 page arena: the request-level page lifecycle.
+
+Mirrors the page part of the reference's ``Indexer``
+(sglang/srt/layers/attention/v1_deepseek/runtime.py):
+
+  State            :681-690   a request's reordered page table, centre table,
+                              leases and indexed length
+  arena tensors    :718-745   fine pool, centre pool, members, refcounts, free
+                              stack + count, hashes, lease tables, centre pages,
+                              host stack of free leases
+  _release         :771-780   release every lease of a request (kernel + host)
+  _prepare         :806-825   index each newly complete 1K bucket of a request
+  Build.compute    :230-270   per bucket: fingerprint -> match_pages ->
+                              allocate -> publish
+
+One bucket is 1024 tokens = 16 pages of 64.  The reference builds a bucket's
+reordered pages, members and centres from the native cache (``assemble`` and
+the grouping sort, the index build, which is outside this path); here the
+caller supplies them through ``bucket_source(owner, bucket) -> (tmp, mapping,
+centers)``: tmp uint8 [16, 8448] packed pages, mapping int32 [16, 64] logical
+token positions, centers uint8 [2, 8448] the bucket's 128 packed centres.
+
+With ``graphs=True`` (the reference's ``Config.graphs``) the four kernels of a
+bucket run as one captured CUDA graph over fixed input buffers, as the
+reference's ``Build`` execution does; the bucket's inputs are copied into
+those buffers first.  Every launch is asynchronous: an exhausted arena is
+recorded in the device status word (the reference traps) and raised by
+``check()``.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from . import kernels as K
+
+PAGE_BYTES = 8448
+
+
+class State:
+    """A request's index state (reference State, DS/runtime.py:681-690)."""
+
+    def __init__(self, pages: int, device):
+        self.table = torch.zeros(pages, dtype=torch.int32, device=device)
+        self.center_table = torch.zeros(pages // 8, dtype=torch.int32, device=device)
+        self.leases: list[int] = []
+        self.length = 0
+
+
+class PageArena:
+    def __init__(self, capacity: int, pages: int, device, max_requests: int | None = None,
+                 graphs: bool = False):
+        """capacity: arena pages; pages: per-request page-table capacity
+        (Config.pages, max_context / 64); max_requests: live request limit."""
+        if capacity <= 0 or capacity % 16 or pages <= 0 or pages % 16:
+            raise ValueError("capacity and pages must be positive multiples of 16")
+        d = self.device = torch.device(device)
+        self.capacity, self.pages = capacity, pages
+        self.max_requests = max_requests if max_requests is not None else max(capacity // pages, 1)
+        self.max_leases = capacity // 16
+        self.fine = torch.zeros((capacity, PAGE_BYTES), dtype=torch.uint8, device=d)
+        self.centers = torch.zeros((-(-capacity // 8), PAGE_BYTES), dtype=torch.uint8, device=d)
+        self.members = torch.full((capacity, 64), -1, dtype=torch.int32, device=d)
+        self.refs = torch.zeros(capacity, dtype=torch.int32, device=d)
+        self.free = torch.arange(capacity, dtype=torch.int32, device=d)
+        self.free_count = torch.full((), capacity, dtype=torch.int32, device=d)
+        self.hashes = torch.zeros((capacity, 2), dtype=torch.int64, device=d)
+        self.tables = torch.full((self.max_leases, 16), -1, dtype=torch.int32, device=d)
+        self.center_pages = torch.arange(self.max_leases * 2, dtype=torch.int32, device=d).view(-1, 2)
+        self.free_leases = list(range(self.max_leases - 1, -1, -1))
+        self.states: dict = {}
+        # per-bucket work buffers (the reference's Build tensors)
+        self.tmp = torch.zeros((16, PAGE_BYTES), dtype=torch.uint8, device=d)
+        self.mapping = torch.zeros((16, 64), dtype=torch.int32, device=d)
+        self.bucket_centers = torch.zeros((2, PAGE_BYTES), dtype=torch.uint8, device=d)
+        self.hash = torch.zeros((16, 2), dtype=torch.int64, device=d)
+        self.matches = torch.zeros(16, dtype=torch.int32, device=d)
+        self.new = torch.zeros(16, dtype=torch.bool, device=d)
+        self.meta = torch.zeros(3, dtype=torch.int32, device=d)
+        self.status = torch.zeros(1, dtype=torch.int32, device=d)
+        self.graphs = graphs
+        self._graph = None
+
+    # -- one bucket ------------------------------------------------------------
+    def _kernels(self, tmp, mapping, centers):
+        K.fingerprint[(16,)](tmp, mapping, self.meta, self.hash)
+        K.match_pages[(16,)](tmp, mapping, self.hash, self.meta, self.fine, self.members, self.hashes,
+                             self.refs, self.matches, self.capacity)
+        K.allocate[(1,)](self.meta, self.matches, self.free, self.free_count, self.refs, self.tables, self.new,
+                         status=self.status, check=False)
+        K.publish[(16,)](tmp, centers, centers.view(torch.float32), mapping, self.hash, self.meta, self.tables,
+                         self.new, self.fine, self.centers, self.centers.view(torch.float32), self.members,
+                         self.hashes)
+
+    def _bucket(self, tmp, mapping, centers, start: int, lease: int):
+        self.meta.copy_(torch.tensor([start, lease, 1], dtype=torch.int32), non_blocking=True)
+        if not self.graphs:
+            self._kernels(tmp, mapping, centers)
+            return
+        self.tmp.copy_(tmp, non_blocking=True)
+        self.mapping.copy_(mapping, non_blocking=True)
+        self.bucket_centers.copy_(centers, non_blocking=True)
+        if self._graph is None:
+            # capture on a side stream once the first bucket's inputs are in place;
+            # the first bucket itself runs eagerly (capture does not execute)
+            self._kernels(self.tmp, self.mapping, self.bucket_centers)
+            s = torch.cuda.Stream(device=self.device)
+            s.wait_stream(torch.cuda.current_stream(self.device))
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                self._kernels(self.tmp, self.mapping, self.bucket_centers)
+            torch.cuda.current_stream(self.device).wait_stream(s)
+            self._graph = g
+            return
+        self._graph.replay()
+
+    # -- requests ---------------------------------------------------------------
+    def prepare(self, owner, length: int, bucket_source):
+        """Index every newly complete bucket of `owner` up to `length` tokens
+        (reference Indexer._prepare, DS/runtime.py:806-825)."""
+        if not 0 <= length <= self.pages * 64:
+            raise ValueError("Index context capacity exceeded")
+        state = self.states.get(owner)
+        if state is not None and length < state.length:
+            self.release(owner)
+            state = None
+        if state is None:
+            if len(self.states) >= self.max_requests:
+                raise ValueError("V1 request capacity exceeded")
+            state = self.states[owner] = State(self.pages, self.device)
+        complete = length // 1024
+        for bucket in range(len(state.leases), complete):
+            if not self.free_leases:
+                raise RuntimeError("V1 bucket records exhausted")
+            lease = self.free_leases.pop()
+            tmp, mapping, centers = bucket_source(owner, bucket)
+            self._bucket(tmp, mapping, centers, bucket * 1024, lease)
+            state.leases.append(lease)
+            state.table[bucket * 16:(bucket + 1) * 16].copy_(self.tables[lease])
+            state.center_table[bucket * 2:(bucket + 1) * 2].copy_(self.center_pages[lease])
+        state.length = length
+        return state
+
+    def release(self, owner):
+        """Drop every lease of `owner` (reference Indexer._release, :771-780)."""
+        state = self.states.pop(owner, None)
+        if state:
+            for lease in state.leases:
+                K.release[(1,)](self.tables[lease], self.refs, self.free, self.free_count)
+                self.free_leases.append(lease)
+
+    def check(self):
+        """Raise ArenaExhausted if an allocation found too few free pages (the
+        reference's device_assert); the arena is unchanged by that bucket."""
+        code = int(self.status.item())
+        if code:
+            self.status.zero_()
+            if code == _lib.V1X_STATUS_ARENA_EXHAUSTED:
+                raise K.ArenaExhausted("V1 DeepSeek page arena exhausted")
+            raise RuntimeError(f"v1x device status {code}")

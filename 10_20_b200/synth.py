@@ -163,3 +163,81 @@ def make_query_case(B: int, H: int, lens, P: int, take: int, window: int = 64, t
 def decode_lens(B: int, lo: int, hi: int, seed: int):
     g = torch.Generator().manual_seed(seed)
     return torch.randint(lo, hi + 1, (B,), generator=g).tolist()
+
+
+# ---------------------------------------------------------------------------
+# page-lifecycle schedules
+# ---------------------------------------------------------------------------
+
+class LifecycleWorkload:
+    """A seeded request schedule for the page arena.
+
+    Requests grow bucket by bucket over `rounds`; each new request shares, with
+    probability `share`, a prefix of another request's bucket chain (identical
+    pages and members at identical logical offsets, so match_pages finds them),
+    and about a quarter of the live requests complete (release) after every
+    round.  Bucket contents are indexed by a content id; `contents(device)`
+    materialises them: tmp uint8 [U, 16, 8448] (random packed pages), mapping
+    int32 [U, 16, 64] (the bucket's 1024 logical positions, shuffled) and
+    centers uint8 [U, 2, 8448].  `ops` is a list of rounds, each a list of
+    ("prepare", owner, length) and ("release", owner) in canonical order."""
+
+    def __init__(self, requests: int, max_buckets: int, rounds: int, seed: int, max_leases: int,
+                 share: float = 0.5, grow: int = 8):
+        g = torch.Generator().manual_seed(seed)
+        rnd = lambda n: int(torch.randint(0, n, (1,), generator=g).item())
+        self.chains: dict[int, list[int]] = {}
+        self.bucket_of: list[int] = []            # content id -> its bucket index
+        prepared: dict[int, int] = {}
+        live: list[int] = []
+        next_owner = 0
+        self.ops = []
+        for _ in range(rounds):
+            ops = []
+            while len(live) < requests:
+                owner = next_owner
+                next_owner += 1
+                n = 1 + rnd(max_buckets)
+                chain = []
+                if self.chains and rnd(1000) < share * 1000:
+                    other = self.chains[list(self.chains)[rnd(len(self.chains))]]
+                    k = 1 + rnd(min(len(other), n))
+                    chain = other[:k]
+                while len(chain) < n:
+                    self.bucket_of.append(len(chain))
+                    chain.append(len(self.bucket_of) - 1)
+                self.chains[owner] = chain
+                prepared[owner] = 0
+                live.append(owner)
+            used = sum(prepared[o] for o in live)
+            for owner in live:
+                add = min(1 + rnd(grow), len(self.chains[owner]) - prepared[owner])
+                add = min(add, max_leases - used)
+                if add <= 0:
+                    continue
+                prepared[owner] += add
+                used += add
+                ops.append(("prepare", owner, prepared[owner] * 1024 + rnd(1024)))
+            done = [o for o in live if rnd(4) == 0]
+            for owner in done:
+                ops.append(("release", owner))
+                live.remove(owner)
+                prepared.pop(owner)
+            self.ops.append(ops)
+        self.n_contents = len(self.bucket_of)
+
+    def contents(self, device):
+        U = self.n_contents
+        gen = torch.Generator(device=device).manual_seed(7)
+        tmp = torch.randint(0, 256, (U, 16, PAGE), generator=gen, device=device, dtype=torch.uint8)
+        centers = torch.randint(0, 256, (U, 2, PAGE), generator=gen, device=device, dtype=torch.uint8)
+        perm = torch.argsort(torch.rand((U, 1024), generator=gen, device=device), dim=1).to(torch.int32)
+        base = torch.as_tensor(self.bucket_of, dtype=torch.int32, device=device)[:, None] * 1024
+        mapping = (base + perm).reshape(U, 16, 64).contiguous()
+        return tmp, mapping, centers
+
+    def source(self, contents):
+        """bucket_source(owner, bucket) for PageArena / ArenaPort over materialised contents."""
+        tmp, mapping, centers = contents
+        return lambda owner, bucket: (tmp[self.chains[owner][bucket]], mapping[self.chains[owner][bucket]],
+                                      centers[self.chains[owner][bucket]])

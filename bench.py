@@ -172,6 +172,324 @@ def run_reference(args, cfg):
     return 0
 
 
+# ---------------------------------------------------------------------------
+# Component workloads (the other rows of the path, each on its own config):
+# one JSON line each with the kernel roofline and the oracle timed on the host.
+# ---------------------------------------------------------------------------
+
+def _dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    return world, rank, device, dist
+
+
+def _timed_replays(graph, steps, warmup, dist, device):
+    """Back-to-back replays (every component workload moves far more than L2
+    per step); device time of the K timed replays, max over ranks."""
+    for _ in range(max(warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(device) as clk:
+        a.record()
+        for _ in range(steps):
+            graph.replay()
+        b.record()
+        torch.cuda.synchronize()
+    ms = a.elapsed_time(b)
+    tt = torch.tensor([ms], dtype=torch.float64, device=device)
+    if dist:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    return float(tt.item()), clk.summary()
+
+
+def _capture(fn, device):
+    s = torch.cuda.Stream(device=device)
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()
+        fn()
+    s.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        fn()
+    s.synchronize()
+    return g
+
+
+def _cpu_rate(fn, units_per_call, budget_s=10.0):
+    fn()
+    done, t0 = 0, time.perf_counter()
+    while True:
+        fn()
+        done += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    return units_per_call * done / el, done, el
+
+
+def _component_line(args, world, metric, unit, value, steps, ms, clocks, cfg, bytes_per_step, kernel,
+                    launches, cpu, parity):
+    hbm, kind = peaks()
+    achieved = bytes_per_step / (ms / steps / 1e3) / 1e9
+    line = {"metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": ms / steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "data": "synthetic", "config": cfg,
+            "roofline": {"bound": "hbm", "kernel": kernel, "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "peak_kind": kind, "traffic": None},
+            "gpu_launches": launches * steps, "clocks": clocks, "parity_spot_check": parity}
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    return line
+
+
+def run_sort_workload(args, world, rank, device, dist):
+    """d2: _sort over 256 instances of 16 x 4096 records keyed by group ids with
+    ~30% duplicate runs, plus the per-segment group offsets (extension)."""
+    import numpy as np
+    fg = importlib.import_module("10_20_b200.fused_grouping")
+    lib = importlib.import_module("10_20_b200._lib")
+    inst = 256
+    heads = 16 * inst
+    rng = np.random.default_rng(11 + rank)
+    keys = rng.integers(0, 4096, size=(heads, 4096))
+    run = rng.random((heads, 4096)) < 0.3
+    run[:, 0] = False
+    idx = np.where(run, 0, np.arange(4096)[None, :])
+    idx = np.maximum.accumulate(idx, axis=1)           # forward-fill the runs
+    keys = np.take_along_axis(keys, idx, axis=1)
+    S = torch.as_tensor(keys.astype(np.float32), device=device)
+    P = torch.arange(heads * 4096, dtype=torch.int32, device=device).reshape(heads, 4096)
+    out = torch.empty_like(P)
+    flag = torch.tensor(-1, dtype=torch.int32, device=device)
+    offs = torch.empty((heads, 4097), dtype=torch.int32, device=device)
+    stream = lambda: torch.cuda.current_stream(device).cuda_stream
+
+    def step():
+        fg._sort[(1, heads)](P, out, S, flag, 4096)
+        lib.call("v1x_group_offsets", S.data_ptr(), offs.data_ptr(), 4096, 1, heads, 4096, stream(),
+                 device=device)
+
+    g = _capture(step, device)
+    ms, clk = _timed_replays(g, args.steps, args.warmup, dist, device)
+    records = heads * 4096
+    value = records * args.steps * world / (ms / 1e3)
+    bytes_per_step = records * 12 + heads * 4097 * 4
+    oracle = importlib.import_module("oracle.v1x_oracle")
+    torch.cuda.synchronize()
+    k16 = keys[:16].astype(np.float32)
+    exp = oracle.sort_segments(np.arange(16 * 4096, dtype=np.int32), k16, -1, 4096, 1, 16).reshape(16, 4096)
+    parity = bool(np.array_equal(out[:16].cpu().numpy(), exp))
+    eo = [oracle.group_offsets(keys[h][exp[h] - h * 4096], 4096) for h in range(16)]
+    parity = parity and bool(np.array_equal(offs[:16].cpu().numpy(), np.stack(eo)))
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        Pn = np.arange(16 * 4096, dtype=np.int32)
+        rate, n, el = _cpu_rate(lambda: oracle.sort_segments(Pn, k16, -1, 4096, 1, 16), 16 * 4096)
+        cpu = {"value": rate, "unit": "records/s", "cores": 1, "kind": "port",
+               "sample": f"{n} calls of one 16 x 4096 instance, oracle sort_segments (numpy lexsort), {el:.1f} s"}
+    return _component_line(args, world, "stable-grouped records/s (_sort + group offsets)", "records/s", value,
+                           args.steps, ms, clk,
+                           {"workload": "sort", "instances_per_gpu": inst, "records_per_instance": 65536,
+                            "segments": "16 x 4096 per instance", "keys": "group ids U[0,4096), ~30% duplicate runs",
+                            "bytes_per_step": bytes_per_step}, bytes_per_step, "sort_kernel + group_offsets_kernel",
+                           2, cpu, parity)
+
+
+def run_gather_workload(args, world, rank, device, dist):
+    """d4: _gather_slots of 1024 x 2048 selected slots of the 576-wide bf16 latent
+    through GatherWorkspace, K and V from the same latent pool, 2M-token pool under
+    a shuffled page table (REQ maps logical -> physical slots)."""
+    import numpy as np
+    gmod = importlib.import_module("10_20_b200.gather")
+    rows, top, D, tokens = 1024, 2048, 576, 1 << 21
+    gen = torch.Generator(device=device).manual_seed(21 + rank)
+    table = torch.randperm(tokens // 64, generator=gen, device=device).to(torch.int32)
+    logical = torch.arange(tokens, device=device, dtype=torch.int32)
+    req = (table[logical // 64] * 64 + logical % 64).to(torch.int32)
+    ids = torch.randint(0, tokens, (rows, top), generator=gen, device=device, dtype=torch.int32)
+    ids[torch.rand((rows, top), generator=gen, device=device) < 0.01] = -1
+    lat = torch.randn((tokens, 1, D), generator=gen, device=device, dtype=torch.bfloat16)
+    ws = gmod.GatherWorkspace(rows, str(device), torch.bfloat16, dim=D, top=top)
+    g_kv = _capture(lambda: ws.gather(lat, lat, req, ids, 0), device)
+    ms, clk = _timed_replays(g_kv, args.steps, args.warmup, dist, device)
+    g_k = _capture(lambda: ws.gather(lat, None, req, ids, 0), device)
+    ms1, _ = _timed_replays(g_k, args.steps, args.warmup, None, device)
+    slots = rows * top
+    row = D * 2
+    bytes_kv = slots * row * 3          # rows read once, K and V written
+    bytes_k = slots * row * 2
+    value = slots * args.steps * world / (ms / 1e3)
+    oracle = importlib.import_module("oracle.v1x_oracle")
+    torch.cuda.synchronize()
+    # spot check against the oracle on 8 rows: the slots they touch, copied to a
+    # compact host pool, with the id -> slot map rewritten to index it
+    sample = 8
+    ids_s = ids[:sample].cpu().numpy()
+    req_n = req.cpu().numpy()
+    used = np.unique(ids_s[ids_s >= 0])
+    slots_used = req_n[used]
+    pool = lat.view(torch.int16).reshape(tokens, D)[torch.as_tensor(slots_used, device=device).long()].cpu().numpy()
+    req_small = np.zeros(tokens, np.int32)
+    req_small[used] = np.arange(used.size, dtype=np.int32)
+    exp_k, exp_v = oracle.gather_slots(pool[:, None, :], pool[:, None, :], req_small, ids_s, sample, top, 0)
+    kk = ws.k[:sample].view(torch.int16).reshape(-1, D).cpu().numpy()
+    vv = ws.v[:sample].view(torch.int16).reshape(-1, D).cpu().numpy()
+    parity = bool(np.array_equal(kk, exp_k) and np.array_equal(vv, exp_v))
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        host_tokens = 1 << 18                            # a 256K-token sample pool on the host
+        lat_n = lat.view(torch.int16).reshape(tokens, D)[:host_tokens].cpu().numpy()
+        req_h = np.random.default_rng(3).integers(0, host_tokens, size=tokens).astype(np.int32)
+        ids_h = np.random.default_rng(4).integers(0, tokens, size=(16, top)).astype(np.int32)
+        rate, n, el = _cpu_rate(lambda: (lat_n[req_h[ids_h.reshape(-1)]], lat_n[req_h[ids_h.reshape(-1)]]),
+                                16 * top, budget_s=8.0)
+        cpu = {"value": rate, "unit": "slots/s", "cores": 1, "kind": "port",
+               "sample": f"{n} K+V gathers of 16 x 2048 slots from a 256K-token host pool (numpy indexing), "
+                         f"{el:.1f} s"}
+    hbm, _ = peaks()
+    line = _component_line(args, world, "gathered slots/s (_gather_slots, K+V)", "slots/s", value, args.steps, ms,
+                           clk, {"workload": "gather", "rows": rows, "top": top, "dim": D, "dtype": "bf16",
+                                 "pool_tokens": tokens, "bytes_per_step_kv": bytes_kv,
+                                 "bytes_per_step_k_only": bytes_k}, bytes_kv, "gather_rows_kernel<72,4,true>", 1,
+                           cpu, parity)
+    line["single_output"] = {"ms_per_step": ms1 / args.steps,
+                             "achieved_gbs": bytes_k / (ms1 / args.steps / 1e3) / 1e9,
+                             "frac": bytes_k / (ms1 / args.steps / 1e3) / 1e9 / hbm}
+    return line
+
+
+def run_pages_workload(args, world, rank, device, dist):
+    """d3: the page lifecycle on a 131,072-page arena: 256 live requests whose
+    bucket chains (1-64 buckets) grow by up to 8 buckets per round, half of them
+    sharing a prefix of another request's chain, a quarter completing (released)
+    after every round; 8 rounds, the first untimed.  Per bucket: fingerprint ->
+    match_pages -> allocate -> publish as one captured graph (the reference's
+    Build execution)."""
+    import numpy as np
+    synth = importlib.import_module("10_20_b200.synth")
+    lifecycle = importlib.import_module("10_20_b200.lifecycle")
+    cap, pages, requests = 131072, 2048, 256
+    wl = synth.LifecycleWorkload(requests, 64, 8, 31 + rank, cap // 16, share=0.5, grow=8)
+    contents = wl.contents(device)
+    arena = lifecycle.PageArena(cap, pages, device, max_requests=requests, graphs=True)
+    src = wl.source(contents)
+
+    def run_round(ops):
+        nb = 0
+        for op in ops:
+            if op[0] == "prepare":
+                before = len(arena.states[op[1]].leases) if op[1] in arena.states else 0
+                arena.prepare(op[1], op[2], src)
+                nb += len(arena.states[op[1]].leases) - before
+            else:
+                arena.release(op[1])
+        return nb
+
+    run_round(wl.ops[0])
+    arena.check()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(device) as clk:
+        t0 = time.perf_counter()
+        a.record()
+        buckets = sum(run_round(ops) for ops in wl.ops[1:])
+        b.record()
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+    arena.check()
+    ms = a.elapsed_time(b)
+    tt = torch.tensor([ms], dtype=torch.float64, device=device)
+    if dist:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    ms = float(tt.item())
+    value = buckets * world / (ms / 1e3)
+    # algorithmic bytes per bucket (the O(CAP) hash scan excluded): fingerprint
+    # reads 16 pages + members, publish writes them (fresh pages) and moves the
+    # bucket's 2 centre pages, release touches 16 refcounts
+    per_bucket = 16 * (8448 + 256) + 16 * (8448 + 256 + 16) + 4 * 8448 + 64
+    # parity spot check: a small arena through the driver and the CPU port
+    port = importlib.import_module("oracle.port")
+    small = synth.LifecycleWorkload(12, 6, 3, 5, 4096 // 16, share=0.6, grow=3)
+    sc = small.contents(device)
+    ga = lifecycle.PageArena(4096, 128, device, max_requests=16, graphs=True)
+    ca = port.ArenaPort(4096, 128, max_requests=16)
+    sg, scpu = small.source(sc), small.source(tuple(x.cpu().numpy() for x in sc))
+    for ops in small.ops:
+        for op in ops:
+            if op[0] == "prepare":
+                ga.prepare(op[1], op[2], sg)
+                ca.prepare(op[1], op[2], scpu)
+            else:
+                ga.release(op[1])
+                ca.release(op[1])
+    ga.check()
+    parity = all(np.array_equal(getattr(ga, n).cpu().numpy(), getattr(ca, n))
+                 for n in ("refs", "free", "tables", "members", "hashes", "fine", "centers"))
+    parity = parity and int(ga.free_count.item()) == ca.count
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        # the CPU port on the same 131,072-page arena, first buckets of round 0
+        host = tuple(x.cpu().numpy() for x in contents)
+        carena = port.ArenaPort(cap, pages, max_requests=requests)
+        hsrc = wl.source(host)
+        done, t0 = 0, time.perf_counter()
+        for op in wl.ops[0]:
+            if op[0] != "prepare":
+                continue
+            before = len(carena.states[op[1]]["leases"]) if op[1] in carena.states else 0
+            carena.prepare(op[1], op[2], hsrc)
+            done += len(carena.states[op[1]]["leases"]) - before
+            if time.perf_counter() - t0 > 10.0:
+                break
+        el = time.perf_counter() - t0
+        cpu = {"value": done / el, "unit": "buckets/s", "cores": 1, "kind": "port",
+               "sample": f"{done} buckets of round 0 on the same 131,072-page arena, oracle port (numpy), "
+                         f"{el:.1f} s"}
+    line = _component_line(args, world, "indexed buckets/s (page lifecycle: fingerprint, match, allocate, "
+                           "publish; releases)", "buckets/s", value, 1, ms, clk,
+                           {"workload": "pages", "capacity_pages": cap, "requests": requests,
+                            "rounds_timed": len(wl.ops) - 1, "buckets_timed": buckets, "share": 0.5,
+                            "bytes_per_bucket": per_bucket}, per_bucket * buckets, "match_scan_kernel + publish",
+                           6, cpu, parity)
+    line["steps"] = len(wl.ops) - 1
+    line["ms_per_bucket"] = ms / max(buckets, 1)
+    line["wall_s"] = wall
+    line["gpu_launches"] = 6 * buckets
+    return line
+
+
+def run_component(args):
+    world, rank, device, dist = _dist_setup()
+    importlib.import_module("10_20_b200").load()
+    if args.workload == "sort":
+        line = run_sort_workload(args, world, rank, device, dist)
+    elif args.workload == "gather":
+        line = run_gather_workload(args, world, rank, device, dist)
+    else:
+        line = run_pages_workload(args, world, rank, device, dist)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -180,11 +498,15 @@ def main():
     ap.add_argument("--requests", type=int, default=0,
                     help="override the per-GPU batch (small cases for profiling; not a bench config)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "single"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "single", "sort", "gather", "pages"],
+                    help="decode (the headline), single (1024 single-head queries), sort (_sort, 256 x 65,536 "
+                         "records), gather (_gather_slots, 1024 x 2048 slots of 576 bf16), pages (page lifecycle)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--inflight", type=int, default=3,
                     help="independent batches in flight (the gather of one overlaps the selection of the next)")
     args = ap.parse_args()
+    if args.workload in ("sort", "gather", "pages"):
+        return run_component(args)
     cfg = workload_cfg(args.workload)
     if args.requests:
         cfg["B"] = args.requests
@@ -369,7 +691,7 @@ def main():
     if rank == 0:
         hbm, kind = peaks()
         if gather_on:
-            dom_bytes, dom_ms, dom = acct["gather"], statistics.mean(gather_ms), "gather_vec_kernel"
+            dom_bytes, dom_ms, dom = acct["gather"], statistics.mean(gather_ms), "gather_rows_kernel"
         else:
             dom_bytes, dom_ms, dom = acct["total"], statistics.mean(sel_ms), "selection graph"
         achieved = dom_bytes / (dom_ms / 1e3) / 1e9

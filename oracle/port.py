@@ -64,3 +64,66 @@ def run_rows(c, rows=None):
             kv, _ = O.gather_slots(c["latent"], None, None, e["physical"], 1, T, 0)
         out.append(dict(selected=sel[0], physical=e["physical"][0], kv=kv))
     return out
+
+
+# --------------------------------------------------------------------------
+# page lifecycle driver (DS/runtime.py:681-825, Build.compute page part :230-270)
+# --------------------------------------------------------------------------
+
+class ArenaPort:
+    """numpy restatement of the request-level page lifecycle that
+    10_20_b200/lifecycle.PageArena drives on the GPU: per request a page table,
+    centre table and lease list; per newly complete bucket fingerprint ->
+    match_pages -> allocate -> publish; release returns every lease."""
+
+    def __init__(self, capacity, pages, max_requests=None):
+        self.capacity, self.pages = capacity, pages
+        self.max_requests = max_requests if max_requests is not None else max(capacity // pages, 1)
+        self.max_leases = capacity // 16
+        self.fine = np.zeros((capacity, O.PAGE_BYTES), np.uint8)
+        self.centers = np.zeros((-(-capacity // 8), O.PAGE_BYTES), np.uint8)
+        self.members = np.full((capacity, 64), -1, np.int32)
+        self.refs = np.zeros(capacity, np.int32)
+        self.free = np.arange(capacity, dtype=np.int32)
+        self.count = capacity
+        self.hashes = np.zeros((capacity, 2), np.int64)
+        self.tables = np.full((self.max_leases, 16), -1, np.int32)
+        self.center_pages = np.arange(self.max_leases * 2, dtype=np.int32).reshape(-1, 2)
+        self.free_leases = list(range(self.max_leases - 1, -1, -1))
+        self.states = {}
+
+    def _bucket(self, tmp, mapping, centers, start, lease):
+        meta = np.array([start, lease, 1], np.int32)
+        h = O.fingerprint(tmp, mapping)
+        match = O.match_pages(tmp, mapping, h, self.fine, self.members, self.hashes, self.refs, self.capacity)
+        self.count, new = O.allocate(meta, match, self.free, self.count, self.refs, self.tables)
+        O.publish(tmp, centers, mapping, h, meta, self.tables, new, self.fine, self.centers, self.members,
+                  self.hashes)
+
+    def prepare(self, owner, length, bucket_source):
+        st = self.states.get(owner)
+        if st is not None and length < st["length"]:
+            self.release(owner)
+            st = None
+        if st is None:
+            if len(self.states) >= self.max_requests:
+                raise ValueError("V1 request capacity exceeded")
+            st = self.states[owner] = dict(table=np.zeros(self.pages, np.int32),
+                                           center_table=np.zeros(self.pages // 8, np.int32), leases=[],
+                                           length=0)
+        for bucket in range(len(st["leases"]), length // 1024):
+            lease = self.free_leases.pop()
+            tmp, mapping, centers = bucket_source(owner, bucket)
+            self._bucket(tmp, mapping, centers, bucket * 1024, lease)
+            st["leases"].append(lease)
+            st["table"][bucket * 16:(bucket + 1) * 16] = self.tables[lease]
+            st["center_table"][bucket * 2:(bucket + 1) * 2] = self.center_pages[lease]
+        st["length"] = length
+        return st
+
+    def release(self, owner):
+        st = self.states.pop(owner, None)
+        if st:
+            for lease in st["leases"]:
+                self.count = O.release(self.tables[lease], self.refs, self.free, self.count)
+                self.free_leases.append(lease)
