@@ -4,8 +4,17 @@
 // Segment (g, h) is S[h*4096 + g*N + i], i < N.  A score equal to zero becomes
 // +0 (:69); the key (ordered(score) << 32) | (0xFFFFFFFF - i) is sorted descending
 // (:70-74) -- score desc, position asc -- and O[... + i] = P[... + pos_i].  All
-// keys are unique, so any correct sort of them is bit-identical: one CTA sorts
-// one segment with a shared-memory bitonic network.
+// keys are unique, so any correct sort of them is bit-identical.
+//
+// One CTA sorts one segment.  Segments of 32..4096 records use a stable block
+// radix sort (CUB's header-only BlockRadixSort compiled into this kernel) of the
+// 32-bit ordered scores carrying their positions: descending, and stable, so
+// equal scores keep ascending positions -- the reference's composite key order.
+// A shared-memory bitonic network of all log2(N)*(log2(N)+1)/2 stages moves 32 B
+// of shared memory per compare-exchange and was bound by shared-memory bandwidth
+// (3% of HBM on 256 x 65,536 records); it remains for segments below 32 records.
+#include <cub/block/block_radix_sort.cuh>
+
 #include "common.cuh"
 
 namespace v1x {
@@ -30,6 +39,61 @@ __global__ void __launch_bounds__(1024) sort_kernel(const int32_t* __restrict__ 
   for (int i = threadIdx.x; i < N; i += blockDim.x) {
     const int pos = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(list[i] & 0xFFFFFFFFull));
     O[base + i] = P[base + pos];
+  }
+}
+
+__device__ __forceinline__ uint32_t ordered_score(float s) {
+  if (s == 0.0f) s = 0.0f;  // -0 -> +0 (:69)
+  const uint32_t b = __float_as_uint(s);
+  return b ^ ((b & 0x80000000u) ? 0xFFFFFFFFu : 0x80000000u);
+}
+
+// kThreads x kItems == N.  Thread t loads and stores records t*kItems + [0, kItems)
+// (contiguous per thread), the blocked arrangement BlockRadixSort works in.  S and
+// O must be 16-byte aligned when kItems % 4 == 0 (the host checks).
+template <int kThreads, int kItems>
+__global__ void __launch_bounds__(kThreads) sort_radix_kernel(const int32_t* __restrict__ P,
+                                                              int32_t* __restrict__ O,
+                                                              const float* __restrict__ S,
+                                                              const int32_t* __restrict__ flag) {
+  using Sorter = cub::BlockRadixSort<uint32_t, kThreads, kItems, int>;
+  __shared__ typename Sorter::TempStorage temp;
+  if (*flag >= 0) return;
+  constexpr int N = kThreads * kItems;
+  const int64_t base = static_cast<int64_t>(blockIdx.y) * 4096 + static_cast<int64_t>(blockIdx.x) * N;
+  const int i0 = threadIdx.x * kItems;
+  uint32_t key[kItems];
+  int pos[kItems];
+  float s[kItems];
+  if constexpr (kItems % 4 == 0) {   // 16-byte loads: segments start at multiples of N records
+#pragma unroll
+    for (int k = 0; k < kItems; k += 4) {
+      const float4 v = *reinterpret_cast<const float4*>(S + base + i0 + k);
+      s[k] = v.x;
+      s[k + 1] = v.y;
+      s[k + 2] = v.z;
+      s[k + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) s[k] = S[base + i0 + k];
+  }
+#pragma unroll
+  for (int k = 0; k < kItems; ++k) {
+    key[k] = ordered_score(s[k]);
+    pos[k] = i0 + k;
+  }
+  Sorter(temp).SortDescending(key, pos);
+  int o[kItems];
+#pragma unroll
+  for (int k = 0; k < kItems; ++k) o[k] = P[base + pos[k]];
+  if constexpr (kItems % 4 == 0) {
+#pragma unroll
+    for (int k = 0; k < kItems; k += 4)
+      *reinterpret_cast<int4*>(O + base + i0 + k) = make_int4(o[k], o[k + 1], o[k + 2], o[k + 3]);
+  } else {
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) O[base + i0 + k] = o[k];
   }
 }
 
@@ -74,13 +138,23 @@ extern "C" int v1x_sort_segments(const int32_t* P, int32_t* O, const float* S, c
   V1X_CHECK_ARG(N >= 2 && N <= 4096 && (N & (N - 1)) == 0, "_sort: N must be a power of two in [2, 4096]");
   V1X_CHECK_ARG(groups >= 0 && heads >= 0 && groups * N <= 4096, "_sort: groups*N exceeds 4096");
   if (groups == 0 || heads == 0) return V1X_OK;
-  const int threads = static_cast<int>(N / 2 < 1024 ? (N / 2 < 32 ? 32 : N / 2) : 1024);
-  const size_t smem = static_cast<size_t>(N) * 8;
-  static DeviceOnce once;
-  if (once.first())
-    cudaFuncSetAttribute(sort_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 4096 * 8);
-  sort_kernel<<<dim3(static_cast<unsigned>(groups), static_cast<unsigned>(heads)), threads, smem,
-                as_stream(stream)>>>(P, O, S, flag, static_cast<int>(N));
+  const dim3 grid(static_cast<unsigned>(groups), static_cast<unsigned>(heads));
+  cudaStream_t s = as_stream(stream);
+  const bool al = ((reinterpret_cast<uintptr_t>(S) | reinterpret_cast<uintptr_t>(O)) & 15) == 0;
+  switch (al ? N : 0) {
+    case 4096: sort_radix_kernel<512, 8><<<grid, 512, 0, s>>>(P, O, S, flag); break;
+    case 2048: sort_radix_kernel<256, 8><<<grid, 256, 0, s>>>(P, O, S, flag); break;
+    case 1024: sort_radix_kernel<128, 8><<<grid, 128, 0, s>>>(P, O, S, flag); break;
+    case 512: sort_radix_kernel<64, 8><<<grid, 64, 0, s>>>(P, O, S, flag); break;
+    case 256: sort_radix_kernel<32, 8><<<grid, 32, 0, s>>>(P, O, S, flag); break;
+    case 128: sort_radix_kernel<32, 4><<<grid, 32, 0, s>>>(P, O, S, flag); break;
+    case 64: sort_radix_kernel<32, 2><<<grid, 32, 0, s>>>(P, O, S, flag); break;
+    case 32: sort_radix_kernel<32, 1><<<grid, 32, 0, s>>>(P, O, S, flag); break;
+    default: {  // below 32 records, or unaligned scores / output
+      const int threads = static_cast<int>(N / 2 < 1024 ? (N / 2 < 32 ? 32 : N / 2) : 1024);
+      sort_kernel<<<grid, threads, static_cast<size_t>(N) * 8, s>>>(P, O, S, flag, static_cast<int>(N));
+    }
+  }
   return launch_status("v1x_sort_segments");
 }
 

@@ -462,7 +462,7 @@ def run_pages_workload(args, world, rank, device, dist):
                "sample": f"{done} buckets of round 0 on the same 131,072-page arena, oracle port (numpy), "
                          f"{el:.1f} s"}
     line = _component_line(args, world, "indexed buckets/s (page lifecycle: fingerprint, match, allocate, "
-                           "publish; releases)", "buckets/s", value, 1, ms, clk,
+                           "publish; releases)", "buckets/s", value, 1, ms, clk.summary(),
                            {"workload": "pages", "capacity_pages": cap, "requests": requests,
                             "rounds_timed": len(wl.ops) - 1, "buckets_timed": buckets, "share": 0.5,
                             "bytes_per_bucket": per_bucket}, per_bucket * buckets, "match_scan_kernel + publish",

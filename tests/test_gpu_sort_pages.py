@@ -39,7 +39,7 @@ def test_sort_golden(golden, cuda_dev):
     assert np.array_equal(o.cpu().numpy(), g["o4096"])
 
 
-@pytest.mark.parametrize("N", [2, 16, 32, 64, 128, 1024, 4096])
+@pytest.mark.parametrize("N", [2, 16, 32, 64, 128, 256, 512, 1024, 2048, 4096])
 def test_sort_random_sizes(N, cuda_dev):
     rng = np.random.default_rng(N)
     heads = 16
@@ -47,6 +47,7 @@ def test_sort_random_sizes(N, cuda_dev):
     S[S == 0] = np.where(rng.random(int((S == 0).sum())) < 0.5, 0.0, -0.0)
     S.reshape(-1)[::101] = np.inf
     S.reshape(-1)[::103] = -np.inf
+    S.reshape(-1)[::107] = np.nan
     P = rng.permutation(heads * 4096).astype(np.int32).reshape(heads, 4096)
     flag = torch.tensor(-1, dtype=torch.int32, device="cuda")
     o = torch.full((heads, 4096), -7, dtype=torch.int32, device="cuda")
