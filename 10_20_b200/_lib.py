@@ -35,6 +35,7 @@ SIGNATURES = {
                  I64, I32, I32, P, I64, I32, I64, P],
     "v1x_sort_segments": [P, P, P, P, I64, I64, I64, P],
     "v1x_group_offsets": [P, P, I64, I64, I64, I64, P],
+    "v1x_sort_segments_grouped": [P, P, P, P, P, I64, I64, I64, I64, P],
     "v1x_fingerprint": [P, P, P, P, I64, P],
     "v1x_match_pages": [P, P, P, P, P, P, P, P, P, I64, I64, P],
     "v1x_allocate": [P, P, P, P, P, P, P, P, P],

@@ -48,22 +48,42 @@ __device__ __forceinline__ uint32_t ordered_score(float s) {
   return b ^ ((b & 0x80000000u) ? 0xFFFFFFFFu : 0x80000000u);
 }
 
+struct LastValid {  // scan operator: the most recent valid (>= 0) value
+  __device__ __forceinline__ int operator()(int a, int b) const { return b >= 0 ? b : a; }
+};
+
 // kThreads x kItems == N.  Thread t loads and stores records t*kItems + [0, kItems)
 // (contiguous per thread), the blocked arrangement BlockRadixSort works in.  S and
 // O must be 16-byte aligned when kItems % 4 == 0 (the host checks).
-template <int kThreads, int kItems>
+//
+// Only the key bits that differ within the segment are sorted: bits equal in every
+// key cannot change the order, and score keys usually share their high bits (group
+// ids 0..4095 as floats differ in ~19 of 32), which saves radix passes.
+//
+// kOffsets: also write the segment's descending group offsets (v1x_group_offsets
+// semantics) from the sorted keys: offs[j] = number of records whose score is an
+// integer key in [0, key_range) greater than key_range-1-j.  In sorted order the
+// valid keys appear descending; a record whose key v starts a run writes offs[j]
+// for every threshold between v and the previous valid key, with the count of
+// valid records before it -- every entry is written exactly once, no atomics.
+template <int kThreads, int kItems, bool kOffsets>
 __global__ void __launch_bounds__(kThreads) sort_radix_kernel(const int32_t* __restrict__ P,
                                                               int32_t* __restrict__ O,
                                                               const float* __restrict__ S,
-                                                              const int32_t* __restrict__ flag) {
+                                                              const int32_t* __restrict__ flag,
+                                                              int32_t* __restrict__ offs, int groups,
+                                                              int key_range) {
   using Sorter = cub::BlockRadixSort<uint32_t, kThreads, kItems, int>;
-  __shared__ typename Sorter::TempStorage temp;
+  using Scan = cub::BlockScan<int, kThreads>;
+  __shared__ union {
+    typename Sorter::TempStorage sort;
+    typename Scan::TempStorage scan;
+  } temp;
+  __shared__ uint32_t red_and[kThreads / 32], red_or[kThreads / 32];
   if (*flag >= 0) return;
   constexpr int N = kThreads * kItems;
   const int64_t base = static_cast<int64_t>(blockIdx.y) * 4096 + static_cast<int64_t>(blockIdx.x) * N;
   const int i0 = threadIdx.x * kItems;
-  uint32_t key[kItems];
-  int pos[kItems];
   float s[kItems];
   if constexpr (kItems % 4 == 0) {   // 16-byte loads: segments start at multiples of N records
 #pragma unroll
@@ -78,12 +98,33 @@ __global__ void __launch_bounds__(kThreads) sort_radix_kernel(const int32_t* __r
 #pragma unroll
     for (int k = 0; k < kItems; ++k) s[k] = S[base + i0 + k];
   }
+  uint32_t key[kItems];
+  int pos[kItems];
+  uint32_t kand = 0xFFFFFFFFu, kor = 0u;
 #pragma unroll
   for (int k = 0; k < kItems; ++k) {
     key[k] = ordered_score(s[k]);
     pos[k] = i0 + k;
+    kand &= key[k];
+    kor |= key[k];
   }
-  Sorter(temp).SortDescending(key, pos);
+  kand = __reduce_and_sync(0xffffffffu, kand);
+  kor = __reduce_or_sync(0xffffffffu, kor);
+  if ((threadIdx.x & 31) == 0) {
+    red_and[threadIdx.x >> 5] = kand;
+    red_or[threadIdx.x >> 5] = kor;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int w = 0; w < kThreads / 32; ++w) {
+    kand &= red_and[w];
+    kor |= red_or[w];
+  }
+  const uint32_t diff = kand ^ kor;   // bits that differ between some keys
+  if (diff != 0u) {                   // all keys equal: the stable order is the identity
+    const int begin = __ffs(diff) - 1, end = 32 - __clz(diff);
+    Sorter(temp.sort).SortDescending(key, pos, begin, end);
+  }
   int o[kItems];
 #pragma unroll
   for (int k = 0; k < kItems; ++k) o[k] = P[base + pos[k]];
@@ -94,6 +135,40 @@ __global__ void __launch_bounds__(kThreads) sort_radix_kernel(const int32_t* __r
   } else {
 #pragma unroll
     for (int k = 0; k < kItems; ++k) O[base + i0 + k] = o[k];
+  }
+  if constexpr (kOffsets) {
+    // sorted keys back to scores; -1 marks records outside the integer key range
+    int v[kItems];
+    int nvalid = 0, last = -1;
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) {
+      const uint32_t b = (key[k] & 0x80000000u) ? (key[k] ^ 0x80000000u) : ~key[k];
+      const float x = __uint_as_float(b);
+      const int ki = static_cast<int>(x);
+      v[k] = (x >= 0.0f && ki < key_range && static_cast<float>(ki) == x) ? ki : -1;
+      nvalid += v[k] >= 0;
+      if (v[k] >= 0) last = v[k];
+    }
+    __syncthreads();  // the sort's shared storage is reused by the scans
+    int before, prev, total;
+    Scan(temp.scan).ExclusiveSum(nvalid, before, total);
+    __syncthreads();
+    Scan(temp.scan).ExclusiveScan(last, prev, -1, LastValid());
+    int32_t* out = offs + (static_cast<int64_t>(blockIdx.y) * groups + blockIdx.x) * (key_range + 1);
+    int cnt = before;
+    int hi = prev >= 0 ? prev : key_range;  // previous valid key (key_range: none yet)
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) {
+      if (v[k] < 0) continue;
+      if (v[k] != hi)   // first record of key v[k]: thresholds u in [v, hi) see cnt keys above
+        for (int u = v[k]; u < hi; ++u) out[key_range - 1 - u] = cnt;
+      hi = v[k];
+      ++cnt;
+    }
+    if (threadIdx.x == kThreads - 1) {   // thresholds below the smallest valid key: all of them
+      const int lo = total > 0 ? hi : key_range;
+      for (int u = -1; u < lo; ++u) out[key_range - 1 - u] = total;
+    }
   }
 }
 
@@ -142,14 +217,14 @@ extern "C" int v1x_sort_segments(const int32_t* P, int32_t* O, const float* S, c
   cudaStream_t s = as_stream(stream);
   const bool al = ((reinterpret_cast<uintptr_t>(S) | reinterpret_cast<uintptr_t>(O)) & 15) == 0;
   switch (al ? N : 0) {
-    case 4096: sort_radix_kernel<512, 8><<<grid, 512, 0, s>>>(P, O, S, flag); break;
-    case 2048: sort_radix_kernel<256, 8><<<grid, 256, 0, s>>>(P, O, S, flag); break;
-    case 1024: sort_radix_kernel<128, 8><<<grid, 128, 0, s>>>(P, O, S, flag); break;
-    case 512: sort_radix_kernel<64, 8><<<grid, 64, 0, s>>>(P, O, S, flag); break;
-    case 256: sort_radix_kernel<32, 8><<<grid, 32, 0, s>>>(P, O, S, flag); break;
-    case 128: sort_radix_kernel<32, 4><<<grid, 32, 0, s>>>(P, O, S, flag); break;
-    case 64: sort_radix_kernel<32, 2><<<grid, 32, 0, s>>>(P, O, S, flag); break;
-    case 32: sort_radix_kernel<32, 1><<<grid, 32, 0, s>>>(P, O, S, flag); break;
+    case 4096: sort_radix_kernel<512, 8, false><<<grid, 512, 0, s>>>(P, O, S, flag, nullptr, 0, 0); break;
+    case 2048: sort_radix_kernel<256, 8, false><<<grid, 256, 0, s>>>(P, O, S, flag, nullptr, 0, 0); break;
+    case 1024: sort_radix_kernel<128, 8, false><<<grid, 128, 0, s>>>(P, O, S, flag, nullptr, 0, 0); break;
+    case 512: sort_radix_kernel<64, 8, false><<<grid, 64, 0, s>>>(P, O, S, flag, nullptr, 0, 0); break;
+    case 256: sort_radix_kernel<32, 8, false><<<grid, 32, 0, s>>>(P, O, S, flag, nullptr, 0, 0); break;
+    case 128: sort_radix_kernel<32, 4, false><<<grid, 32, 0, s>>>(P, O, S, flag, nullptr, 0, 0); break;
+    case 64: sort_radix_kernel<32, 2, false><<<grid, 32, 0, s>>>(P, O, S, flag, nullptr, 0, 0); break;
+    case 32: sort_radix_kernel<32, 1, false><<<grid, 32, 0, s>>>(P, O, S, flag, nullptr, 0, 0); break;
     default: {  // below 32 records, or unaligned scores / output
       const int threads = static_cast<int>(N / 2 < 1024 ? (N / 2 < 32 ? 32 : N / 2) : 1024);
       sort_kernel<<<grid, threads, static_cast<size_t>(N) * 8, s>>>(P, O, S, flag, static_cast<int>(N));
@@ -170,4 +245,29 @@ extern "C" int v1x_group_offsets(const float* S, int32_t* offsets, int64_t N, in
                          static_cast<size_t>(key_range) * 4, as_stream(stream)>>>(
       S, offsets, static_cast<int>(N), static_cast<int>(groups), static_cast<int>(key_range));
   return launch_status("v1x_group_offsets");
+}
+
+extern "C" int v1x_sort_segments_grouped(const int32_t* P, int32_t* O, const float* S, const int32_t* flag,
+                                         int32_t* offsets, int64_t N, int64_t groups, int64_t heads,
+                                         int64_t key_range, void* stream) {
+  using namespace v1x;
+  clear_error();
+  V1X_CHECK_ARG(N == 4096 || N == 2048 || N == 1024 || N == 512 || N == 256,
+                "sort_segments_grouped: N must be a power of two in [256, 4096]");
+  V1X_CHECK_ARG(groups >= 0 && heads >= 0 && groups * N <= 4096, "sort_segments_grouped: groups*N exceeds 4096");
+  V1X_CHECK_ARG(key_range >= 1 && key_range <= (1 << 20), "sort_segments_grouped: key_range in [1, 2^20]");
+  V1X_CHECK_ARG(((reinterpret_cast<uintptr_t>(S) | reinterpret_cast<uintptr_t>(O)) & 15) == 0,
+                "sort_segments_grouped: S and O must be 16-byte aligned");
+  if (groups == 0 || heads == 0) return V1X_OK;
+  const dim3 grid(static_cast<unsigned>(groups), static_cast<unsigned>(heads));
+  cudaStream_t s = as_stream(stream);
+  const int g = static_cast<int>(groups), kr = static_cast<int>(key_range);
+  switch (N) {
+    case 4096: sort_radix_kernel<512, 8, true><<<grid, 512, 0, s>>>(P, O, S, flag, offsets, g, kr); break;
+    case 2048: sort_radix_kernel<256, 8, true><<<grid, 256, 0, s>>>(P, O, S, flag, offsets, g, kr); break;
+    case 1024: sort_radix_kernel<128, 8, true><<<grid, 128, 0, s>>>(P, O, S, flag, offsets, g, kr); break;
+    case 512: sort_radix_kernel<64, 8, true><<<grid, 64, 0, s>>>(P, O, S, flag, offsets, g, kr); break;
+    default: sort_radix_kernel<32, 8, true><<<grid, 32, 0, s>>>(P, O, S, flag, offsets, g, kr); break;
+  }
+  return launch_status("v1x_sort_segments_grouped");
 }

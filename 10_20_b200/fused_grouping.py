@@ -39,3 +39,18 @@ def group_offsets(S: torch.Tensor, N: int, heads: int, key_range: int) -> torch.
     _lib.call("v1x_group_offsets", ptr(S), ptr(out), int(N), groups, int(heads), int(key_range),
               _lib.stream_of(S), device=S.device)
     return out
+
+
+def sort_grouped(P: torch.Tensor, O: torch.Tensor, S: torch.Tensor, FLAG: torch.Tensor, N: int, heads: int,
+                 key_range: int, offsets: torch.Tensor | None = None) -> torch.Tensor:
+    """Extension: ``_sort`` and ``group_offsets`` in one launch (N in 256..4096):
+    writes the permutation to O and returns the offsets [heads * 4096/N,
+    key_range + 1], equal to the two separate ops."""
+    require(P.dtype == torch.int32 and O.dtype == torch.int32 and S.dtype == torch.float32,
+            "sort_grouped: P/O int32, S float32")
+    groups = 4096 // N
+    if offsets is None:
+        offsets = torch.empty((heads * groups, key_range + 1), dtype=torch.int32, device=S.device)
+    _lib.call("v1x_sort_segments_grouped", ptr(P), ptr(O), ptr(S), ptr(FLAG), ptr(offsets), int(N), groups,
+              int(heads), int(key_range), _lib.stream_of(S), device=S.device)
+    return offsets

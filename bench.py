@@ -277,10 +277,8 @@ def run_sort_workload(args, world, rank, device, dist):
     offs = torch.empty((heads, 4097), dtype=torch.int32, device=device)
     stream = lambda: torch.cuda.current_stream(device).cuda_stream
 
-    def step():
-        fg._sort[(1, heads)](P, out, S, flag, 4096)
-        lib.call("v1x_group_offsets", S.data_ptr(), offs.data_ptr(), 4096, 1, heads, 4096, stream(),
-                 device=device)
+    def step():   # the stable permutation and the group offsets, one launch
+        fg.sort_grouped(P, out, S, flag, 4096, heads, 4096, offsets=offs)
 
     g = _capture(step, device)
     ms, clk = _timed_replays(g, args.steps, args.warmup, dist, device)
@@ -304,8 +302,8 @@ def run_sort_workload(args, world, rank, device, dist):
                            args.steps, ms, clk,
                            {"workload": "sort", "instances_per_gpu": inst, "records_per_instance": 65536,
                             "segments": "16 x 4096 per instance", "keys": "group ids U[0,4096), ~30% duplicate runs",
-                            "bytes_per_step": bytes_per_step}, bytes_per_step, "sort_kernel + group_offsets_kernel",
-                           2, cpu, parity)
+                            "bytes_per_step": bytes_per_step}, bytes_per_step, "sort_radix_kernel<512,8,offsets>",
+                           1, cpu, parity)
 
 
 def run_gather_workload(args, world, rank, device, dist):

@@ -77,6 +77,34 @@ def test_sort_baseline_records_and_offsets(cuda_dev):
         assert np.array_equal(offs[h], O.group_offsets(sk, 4096))
 
 
+@pytest.mark.parametrize("N", [256, 1024, 4096])
+@pytest.mark.parametrize("kind", ["groups", "mixed"])
+def test_sort_grouped_equals_sort_then_offsets(N, kind, cuda_dev):
+    """The fused sort + offsets launch == _sort followed by group_offsets."""
+    rng = np.random.default_rng(N + len(kind))
+    heads, K = 8, 3000
+    if kind == "groups":
+        S = rng.integers(0, K, size=(heads, 4096)).astype(np.float32)
+        S[:, 1::3] = S[:, 0::3][:, : S[:, 1::3].shape[1]]          # duplicate runs
+        S[0] = 7.0                                                  # one segment of equal keys
+    else:   # non-integers, negatives, out-of-range keys, +-0, inf and NaN mixed in
+        S = rng.integers(-50, K + 50, size=(heads, 4096)).astype(np.float32)
+        S[:, ::5] += 0.5
+        S.reshape(-1)[::97] = -0.0
+        S.reshape(-1)[::89] = np.inf
+        S.reshape(-1)[::83] = np.nan
+    P = rng.permutation(heads * 4096).astype(np.int32).reshape(heads, 4096)
+    flag = torch.tensor(-1, dtype=torch.int32, device="cuda")
+    o1 = torch.empty((heads, 4096), dtype=torch.int32, device="cuda")
+    o2 = torch.empty_like(o1)
+    FG._sort[(4096 // N, heads)](dev(P), o1, dev(S), flag, N)
+    offs1 = FG.group_offsets(dev(S), N, heads, K)
+    offs2 = FG.sort_grouped(dev(P), o2, dev(S), flag, N, heads, K)
+    assert torch.equal(o1, o2)
+    assert torch.equal(offs1, offs2)
+    assert np.array_equal(o1.cpu().numpy().reshape(-1), O.sort_segments(P, S, -1, N, 4096 // N, heads))
+
+
 def _state(cap, free=None):
     return dict(fine=torch.zeros((cap, 8448), dtype=torch.uint8, device="cuda"),
                 members=torch.full((cap, 64), -1, dtype=torch.int32, device="cuda"),
