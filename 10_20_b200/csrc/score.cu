@@ -57,48 +57,64 @@ __global__ void __launch_bounds__(kScoreThreads) score_simt_kernel(const __grid_
   pdl_wait();
   pdl_trigger();
   __syncthreads();
-  const int64_t j = static_cast<int64_t>(blockIdx.y) * blockDim.x + threadIdx.x;
+  // Grid-stride over the row's blocks of 128 keys: the query is staged once per
+  // CTA, and the next block's key bytes are loaded while the current block is
+  // evaluated (two keys' loads in flight per thread).
   const int64_t n = score_len(a.lens[b], a.lens_kind);
-  float result = -CUDART_INF_F;
-  if (j < n && j < a.max_len) {
-    const int64_t page = a.table[b * a.table_stride + j / 64];
-    const uint8_t* kp = a.pool + page * kPageBytes + (j % 64) * 128;
-    uint4 kw[8];
+  const int64_t lim = min(n, a.max_len);   // keys j < lim are scored
+  const int64_t step = static_cast<int64_t>(gridDim.y) * blockDim.x;
+  auto load_key = [&](int64_t j, uint4 (&kw)[8], float& scale) {
+    if (j < lim) {
+      const int64_t page = a.table[b * a.table_stride + j / 64];
+      const uint8_t* kp = a.pool + page * kPageBytes + (j % 64) * 128;
 #pragma unroll
-    for (int c = 0; c < 8; ++c) kw[c] = reinterpret_cast<const uint4*>(kp)[c];
-    const float scale = reinterpret_cast<const float*>(a.pool + page * kPageBytes)[kScaleWord + j % 64];
-    float acc = 0.0f;
-    for (int h = 0; h < H; ++h) {
-      const float4* qh = reinterpret_cast<const float4*>(qs + h * 128);
-      float dot = 0.0f;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint32_t w4[4] = {kw[c].x, kw[c].y, kw[c].z, kw[c].w};
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float2 lo = e4m3x2_to_float2(static_cast<uint16_t>(w4[u] & 0xFFFFu));
-          const float2 hi = e4m3x2_to_float2(static_cast<uint16_t>(w4[u] >> 16));
-          const float4 qq = qh[c * 4 + u];
-          dot = __fmaf_rn(qq.x, lo.x, dot);
-          dot = __fmaf_rn(qq.y, lo.y, dot);
-          dot = __fmaf_rn(qq.z, hi.x, dot);
-          dot = __fmaf_rn(qq.w, hi.y, dot);
-        }
-      }
-      const float r = a.relu ? (dot > 0.0f ? dot : 0.0f) : dot;
-      acc = __fadd_rn(acc, __fmul_rn(ws[h], r));
+      for (int c = 0; c < 8; ++c) kw[c] = reinterpret_cast<const uint4*>(kp)[c];
+      scale = reinterpret_cast<const float*>(a.pool + page * kPageBytes)[kScaleWord + j % 64];
     }
-    result = __fmul_rn(acc, scale);
+  };
+  uint4 cur[8], nxt[8];
+  float cur_scale = 0.0f, nxt_scale = 0.0f;
+  int64_t j = static_cast<int64_t>(blockIdx.y) * blockDim.x + threadIdx.x;
+  load_key(j, cur, cur_scale);
+  for (; j - threadIdx.x < a.max_len; j += step) {
+    load_key(j + step, nxt, nxt_scale);
+    float result = -CUDART_INF_F;
+    if (j < lim) {
+      float acc = 0.0f;
+      for (int h = 0; h < H; ++h) {
+        const float4* qh = reinterpret_cast<const float4*>(qs + h * 128);
+        float dot = 0.0f;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint32_t w4[4] = {cur[c].x, cur[c].y, cur[c].z, cur[c].w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float2 lo = e4m3x2_to_float2(static_cast<uint16_t>(w4[u] & 0xFFFFu));
+            const float2 hi = e4m3x2_to_float2(static_cast<uint16_t>(w4[u] >> 16));
+            const float4 qq = qh[c * 4 + u];
+            dot = __fmaf_rn(qq.x, lo.x, dot);
+            dot = __fmaf_rn(qq.y, lo.y, dot);
+            dot = __fmaf_rn(qq.z, hi.x, dot);
+            dot = __fmaf_rn(qq.w, hi.y, dot);
+          }
+        }
+        const float r = a.relu ? (dot > 0.0f ? dot : 0.0f) : dot;
+        acc = __fadd_rn(acc, __fmul_rn(ws[h], r));
+      }
+      result = __fmul_rn(acc, cur_scale);
+    }
+    if (a.page_max) {  // max over each group of 8 consecutive keys (lanes 8k..8k+7)
+      float m = result;
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+      if ((threadIdx.x & 7) == 0 && j < a.max_len) a.page_max[b * a.page_stride + j / 8] = m;
+    }
+    if (j < a.max_len && a.out && (j < n || a.clean)) a.out[b * a.out_stride + j] = result;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) cur[c] = nxt[c];
+    cur_scale = nxt_scale;
   }
-  if (a.page_max) {  // max over each group of 8 consecutive keys (lanes 8k..8k+7)
-    float m = result;
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
-    if ((threadIdx.x & 7) == 0 && j < a.max_len) a.page_max[b * a.page_stride + j / 8] = m;
-  }
-  if (j >= a.max_len || !a.out || (j >= n && !a.clean)) return;
-  a.out[b * a.out_stride + j] = result;
 }
 
 }  // namespace
@@ -133,7 +149,8 @@ int score_dispatch(const uint8_t* q, const float* w, const uint8_t* pool, int64_
   }
   ScoreArgs a{q, w, pool, lens, table, table_stride, out, out_stride, max_len, page_max, page_stride,
               static_cast<int>(heads), relu, clean, lens_kind};
-  const dim3 grid(static_cast<unsigned>(batch), static_cast<unsigned>((max_len + kScoreThreads - 1) / kScoreThreads));
+  const int64_t blocks = (max_len + kScoreThreads - 1) / kScoreThreads;
+  const dim3 grid(static_cast<unsigned>(batch), static_cast<unsigned>(blocks < 8 ? blocks : 8));
   launch_pdl(score_simt_kernel, grid, dim3(kScoreThreads), 0, as_stream(stream), a);
   return launch_status("v1x_score_fp8");
 }
