@@ -41,49 +41,40 @@ struct DeviceOnce {
   }
 };
 
-// ---- programmatic dependent launch -------------------------------------------
-// The query-path kernels are launched with programmatic stream serialization: a
-// kernel may start (and run its set-up) while the kernel before it on the stream
-// finishes.  Each such kernel reads, before pdl_wait(), only caller inputs that no
-// kernel of this library writes (lengths, page tables, members, q, w, pools) and
-// writes nothing; everything else comes after pdl_wait(), which returns once the
-// preceding grid has completed and its writes are visible.  pdl_trigger() is
-// called only after pdl_wait(), so when a kernel starts, every kernel two or
-// more launches back has completed.  Kernels of other libraries never trigger
-// early, so a kernel that follows one of them starts after it completes.  Both
-// instructions are no-ops in a plain launch.
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-
+// ---- launches ------------------------------------------------------------------
 // Scheduling priority of a launch: the latency-bound selection kernels are
 // launched at the device's greatest priority so that, when another batch's
 // bandwidth-bound gather runs beside them, their CTAs are placed first as SM
 // slots free up; the gather keeps the default (lowest) priority.
+//
+// Programmatic dependent launch (a kernel starting while its predecessor drains)
+// was measured and is not used: it saved ~4 us per step with one batch at a
+// time, but with independent batches in flight the early-launched CTAs sat
+// resident waiting for their predecessor and held the SM slots the other
+// batch's gather needed (159 vs 167 us per step without it).
 enum class LaunchPriority { kHigh, kDefault };
 int greatest_priority();
 
 template <typename... KArgs, typename... Args>
-inline void launch_pdl_prio(LaunchPriority prio, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
-                            cudaStream_t stream, Args... args) {
+inline void launch_kernel_prio(LaunchPriority prio, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                               cudaStream_t stream, Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  attr[1].id = cudaLaunchAttributePriority;
-  attr[1].val.priority = prio == LaunchPriority::kHigh ? greatest_priority() : 0;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributePriority;
+  attr[0].val.priority = prio == LaunchPriority::kHigh ? greatest_priority() : 0;
   cfg.attrs = attr;
-  cfg.numAttrs = 2;
+  cfg.numAttrs = 1;
   cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
 template <typename... KArgs, typename... Args>
-inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
-                       Args... args) {
-  launch_pdl_prio(LaunchPriority::kHigh, kernel, grid, block, smem, stream, args...);
+inline void launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                          Args... args) {
+  launch_kernel_prio(LaunchPriority::kHigh, kernel, grid, block, smem, stream, args...);
 }
 
 // ---- device helpers ---------------------------------------------------------

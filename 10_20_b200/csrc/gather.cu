@@ -39,8 +39,6 @@ constexpr int kUnroll = 4;
 
 template <bool kHasV>
 __global__ void __launch_bounds__(256) gather_vec_kernel(const __grid_constant__ GatherArgs a) {
-  pdl_wait();
-  pdl_trigger();
   const int64_t cpr = a.dim * a.elem / 16;  // 16-byte chunks per row
   const int64_t total = a.rows * a.top * cpr;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -86,8 +84,6 @@ template <int kCpr, int kR, bool kHasV>
 __global__ void __launch_bounds__(256) gather_rows_kernel(const __grid_constant__ GatherArgs a) {
   static_assert((kCpr * kR) % 32 == 0, "a row group must fill the warp's lanes");
   constexpr int kPer = kCpr * kR / 32;
-  pdl_wait();
-  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int64_t nrows = a.rows * a.top;
   const int64_t ngroups = (nrows + kR - 1) / kR;
@@ -130,8 +126,6 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const __grid_constant_
 
 template <typename T>
 __global__ void gather_scalar_kernel(const __grid_constant__ GatherArgs a) {
-  pdl_wait();
-  pdl_trigger();
   const int64_t total = a.rows * a.top * a.dim;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   const T* k = reinterpret_cast<const T*>(a.k);
@@ -183,25 +177,25 @@ extern "C" int v1x_gather_slots(const void* k, const void* v, const int32_t* req
     blocks = blocks < sms * 16 ? blocks : sms * 16;
     const dim3 grid(static_cast<unsigned>(blocks)), block(256);
     if (cpr == 72) {
-      if (hv) launch_pdl_prio(LaunchPriority::kDefault, gather_rows_kernel<72, 4, true>, grid, block, 0, s, a);
-      else launch_pdl_prio(LaunchPriority::kDefault, gather_rows_kernel<72, 4, false>, grid, block, 0, s, a);
+      if (hv) launch_kernel_prio(LaunchPriority::kDefault, gather_rows_kernel<72, 4, true>, grid, block, 0, s, a);
+      else launch_kernel_prio(LaunchPriority::kDefault, gather_rows_kernel<72, 4, false>, grid, block, 0, s, a);
     } else {
-      if (hv) launch_pdl_prio(LaunchPriority::kDefault, gather_rows_kernel<16, 8, true>, grid, block, 0, s, a);
-      else launch_pdl_prio(LaunchPriority::kDefault, gather_rows_kernel<16, 8, false>, grid, block, 0, s, a);
+      if (hv) launch_kernel_prio(LaunchPriority::kDefault, gather_rows_kernel<16, 8, true>, grid, block, 0, s, a);
+      else launch_kernel_prio(LaunchPriority::kDefault, gather_rows_kernel<16, 8, false>, grid, block, 0, s, a);
     }
   } else if (vec) {
     const int64_t total = rows * top * dim * elem_bytes / 16;
     int64_t blocks = (total + 256 * kUnroll - 1) / (256 * kUnroll);
     blocks = blocks < sms * 16 ? blocks : sms * 16;
-    if (hv) launch_pdl_prio(LaunchPriority::kDefault, gather_vec_kernel<true>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, a);
-    else launch_pdl_prio(LaunchPriority::kDefault, gather_vec_kernel<false>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, a);
+    if (hv) launch_kernel_prio(LaunchPriority::kDefault, gather_vec_kernel<true>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, a);
+    else launch_kernel_prio(LaunchPriority::kDefault, gather_vec_kernel<false>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, a);
   } else {
     const int64_t total = rows * top * dim;
     int64_t blocks = (total + 255) / 256;
     blocks = blocks < sms * 32 ? blocks : sms * 32;
-    if (elem_bytes == 1) launch_pdl_prio(LaunchPriority::kDefault, gather_scalar_kernel<uint8_t>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, a);
-    else if (elem_bytes == 2) launch_pdl_prio(LaunchPriority::kDefault, gather_scalar_kernel<uint16_t>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, a);
-    else launch_pdl_prio(LaunchPriority::kDefault, gather_scalar_kernel<uint32_t>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, a);
+    if (elem_bytes == 1) launch_kernel_prio(LaunchPriority::kDefault, gather_scalar_kernel<uint8_t>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, a);
+    else if (elem_bytes == 2) launch_kernel_prio(LaunchPriority::kDefault, gather_scalar_kernel<uint16_t>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, a);
+    else launch_kernel_prio(LaunchPriority::kDefault, gather_scalar_kernel<uint32_t>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, a);
   }
   return launch_status("v1x_gather_slots");
 }

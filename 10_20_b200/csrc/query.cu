@@ -38,7 +38,7 @@ struct RowMeta {
 };
 
 // Per-row metadata (:568-591) computed by one CTA (threads 0..127 take part in
-// the page-id comparison).  Reads caller inputs only.
+// the page-id comparison).
 __device__ __forceinline__ RowMeta row_meta(const MetaArgs& a, int64_t row) {
   RowMeta m;
   m.n = a.lens[row];
@@ -71,8 +71,6 @@ __device__ __forceinline__ void write_meta(const MetaArgs& a, int64_t row, const
 __global__ void __launch_bounds__(128) query_metadata_kernel(const __grid_constant__ MetaArgs a) {
   const int64_t row = blockIdx.x;
   const RowMeta m = row_meta(a, row);
-  pdl_wait();  // everything above reads caller inputs only
-  pdl_trigger();
   if (threadIdx.x == 0) write_meta(a, row, m);
 }
 
@@ -172,8 +170,6 @@ __device__ __forceinline__ void stage_pages(const StageArgs& a, int64_t row, con
 __global__ void __launch_bounds__(256) stage_tail_shared_kernel(const __grid_constant__ StageArgs a,
                                                                 int64_t grid_pages) {
   const int64_t row = blockIdx.x;
-  pdl_wait();
-  pdl_trigger();
   if (a.rows_bound > 0 && row >= a.rows_bound) return;
   if (a.tail_rows[row] != row) return;
   const int n = a.lens[row];
@@ -197,8 +193,6 @@ __global__ void __launch_bounds__(128) query_prepare_kernel(const __grid_constan
                                                             const __grid_constant__ StageArgs s) {
   const int64_t row = blockIdx.x;
   const RowMeta r = row_meta(m, row);
-  pdl_wait();
-  pdl_trigger();
   if (blockIdx.y == 0 && threadIdx.x == 0) write_meta(m, row, r);
   if (!r.owner) return;
   const int count = r.rb.sink + r.n - r.rb.tail;
@@ -324,7 +318,7 @@ extern "C" int v1x_query_metadata(const int32_t* lens, const int32_t* nt, int32_
   if (batch == 0) return V1X_OK;
   const MetaArgs a{lens, nt, fine_lens, takes, dg_lens, center_lens, tail_rows, np, topk, num, den, sink, window,
                    budget};
-  launch_pdl(query_metadata_kernel, dim3(static_cast<unsigned>(batch)), dim3(128), 0, as_stream(stream), a);
+  launch_kernel(query_metadata_kernel, dim3(static_cast<unsigned>(batch)), dim3(128), 0, as_stream(stream), a);
   return launch_status("v1x_query_metadata");
 }
 
@@ -345,7 +339,7 @@ extern "C" int v1x_query_prepare(const int32_t* lens, const int32_t* nt, int32_t
   const StageArgs s{native_bytes, native_scales, nt, lens, fine_bytes, fine_scales, tail_rows, cap, np,
                     scratch, sink, window, batch, 1};
   const dim3 grid(static_cast<unsigned>(batch), static_cast<unsigned>((scratch + kStagePages - 1) / kStagePages));
-  launch_pdl(query_prepare_kernel, grid, dim3(128), 0, as_stream(stream), m, s);
+  launch_kernel(query_prepare_kernel, grid, dim3(128), 0, as_stream(stream), m, s);
   return launch_status("v1x_query_prepare");
 }
 
@@ -390,7 +384,7 @@ extern "C" int v1x_stage_tail_shared(const uint8_t* native_bytes, const float* n
   if (rows_bound > 0 && rows > rows_bound) rows = rows_bound;
   if (rows <= 0) return V1X_OK;
   const dim3 grid(static_cast<unsigned>(rows), static_cast<unsigned>((grid_pages + kStagePages - 1) / kStagePages));
-  launch_pdl(stage_tail_shared_kernel, grid, dim3(256), 0, as_stream(stream), a, grid_pages);
+  launch_kernel(stage_tail_shared_kernel, grid, dim3(256), 0, as_stream(stream), a, grid_pages);
   return launch_status("v1x_stage_tail_shared");
 }
 

@@ -83,7 +83,7 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_kernel(const __grid_co
   const int n = a.lens[row];
   const int active = max(n - 1, 0) / 1024 * 16;
   const int32_t* rtrow = a.rt + row * a.pages;
-  if (a.stage_rt) {  // caller input: copied while the previous kernel finishes
+  if (a.stage_rt) {  // the row's reordered-page table, copied while the keys are selected
     if ((reinterpret_cast<uintptr_t>(rtrow) & 15) == 0 && (a.pages & 3) == 0) {
       for (int v = tid; v < (a.pages >> 2); v += nt) cp_async16(sm.rt + 4 * v, rtrow + 4 * v);
     } else {
@@ -91,8 +91,6 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_kernel(const __grid_co
     }
   }
   asm volatile("cp.async.commit_group;" ::: "memory");
-  pdl_wait();
-  pdl_trigger();
   const int take = a.takes[row];
   if (a.fill_table) {
     const int64_t base = a.capacity + static_cast<int64_t>(a.tail_rows[row]) * 68;
@@ -233,8 +231,8 @@ int route_launch(bool pages_in, const float* scores, int64_t score_stride, int64
     cudaFuncSetAttribute(route_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     cudaFuncSetAttribute(route_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   }
-  if (pages_in) launch_pdl(route_kernel<true>, dim3(static_cast<unsigned>(batch)), dim3(kRouteThreads), smem, as_stream(stream), a);
-  else launch_pdl(route_kernel<false>, dim3(static_cast<unsigned>(batch)), dim3(kRouteThreads), smem, as_stream(stream), a);
+  if (pages_in) launch_kernel(route_kernel<true>, dim3(static_cast<unsigned>(batch)), dim3(kRouteThreads), smem, as_stream(stream), a);
+  else launch_kernel(route_kernel<false>, dim3(static_cast<unsigned>(batch)), dim3(kRouteThreads), smem, as_stream(stream), a);
   return launch_status(pages_in ? "v1x_route_pages" : "v1x_route");
 }
 }  // namespace

@@ -54,8 +54,6 @@ __global__ void __launch_bounds__(kScoreThreads) score_simt_kernel(const __grid_
     qs[2 * i + 1] = f.y;
   }
   for (int h = threadIdx.x; h < H; h += blockDim.x) ws[h] = a.w[b * H + h];
-  pdl_wait();
-  pdl_trigger();
   __syncthreads();
   // Grid-stride over the row's blocks of 128 keys: the query is staged once per
   // CTA, and the next block's key bytes are loaded while the current block is
@@ -151,7 +149,7 @@ int score_dispatch(const uint8_t* q, const float* w, const uint8_t* pool, int64_
               static_cast<int>(heads), relu, clean, lens_kind};
   const int64_t blocks = (max_len + kScoreThreads - 1) / kScoreThreads;
   const dim3 grid(static_cast<unsigned>(batch), static_cast<unsigned>(blocks < 8 ? blocks : 8));
-  launch_pdl(score_simt_kernel, grid, dim3(kScoreThreads), 0, as_stream(stream), a);
+  launch_kernel(score_simt_kernel, grid, dim3(kScoreThreads), 0, as_stream(stream), a);
   return launch_status("v1x_score_fp8");
 }
 }  // namespace

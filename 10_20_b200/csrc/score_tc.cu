@@ -138,8 +138,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   int* prefix = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(&sh) + sizeof(TcShared));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
-  // ---- set-up that reads nothing another kernel writes (overlaps the previous
-  // kernel under programmatic launch), then the per-row tile prefix --------------
+  // ---- barriers, TMEM, tensor-map prefetch, then the per-row tile prefix ---------
   if (tid == 0) {
     sh.abort = 0;
     sh.zero = 0;
@@ -170,13 +169,6 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     tma_prefetch_desc(&pool_map);
     tma_prefetch_desc(&q_map);
     tma_prefetch_desc(&scale_map);
-  }
-  // Token-length centre counts (lens_kind 1) and everything the producers and the
-  // MMA read are caller inputs: only the epilogue, which writes, waits for the
-  // previous kernel.  Lengths of kind 0 may come from the previous kernel.
-  if (a.lens_kind == 0) {
-    pdl_wait();
-    pdl_trigger();
   }
   {
     const int chunk = (a.B + kTcThreads - 1) / kTcThreads;
@@ -296,10 +288,6 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     const int g = (warp - kEpiWarp0) >> 2;
     const int q4 = warp & 3;                      // TMEM lane quarter this warp may access
     const int i = q4 * 32 + lane;                 // key of the 128-key tile == TMEM lane
-    if (a.lens_kind != 0) {
-      pdl_wait();
-      pdl_trigger();
-    }
     // the epilogue warps alone stage the head weights (off the producers' path)
     if (w_staged)
       for (int e = tid - 32 * kEpiWarp0; e < (b_last - b_first + 1) * a.H; e += kTcThreads - 32 * kEpiWarp0)
@@ -483,7 +471,7 @@ int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t 
   static DeviceOnce once;
   if (once.first())
     cudaFuncSetAttribute(score_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-  launch_pdl(score_tc_kernel, dim3(static_cast<unsigned>(grid)), dim3(kTcThreads), smem, stream, pool_map, q_map,
+  launch_kernel(score_tc_kernel, dim3(static_cast<unsigned>(grid)), dim3(kTcThreads), smem, stream, pool_map, q_map,
              scale_map, args);
   return launch_status("v1x_score_fp8 (tensor core)");
 }

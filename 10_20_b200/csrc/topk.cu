@@ -150,7 +150,7 @@ __global__ void __launch_bounds__(kTopkThreads, 1) topk_kernel(const __grid_cons
   const int lane = tid & 31, warp = tid >> 5;
   RowCtx c;
   c.row = blockIdx.x;
-  // caller inputs first (lengths, native table): they overlap the previous kernel
+  // lengths and the native-table row (its copy overlaps the selection below)
   c.n = a.lens[c.row];
   const int Sn = kStaged ? static_cast<int>(min(min(a.pages, static_cast<int64_t>(a.stage_nt)),
                                                 (static_cast<int64_t>(max(c.n, 0)) + 63) / 64))
@@ -164,8 +164,6 @@ __global__ void __launch_bounds__(kTopkThreads, 1) topk_kernel(const __grid_cons
       for (int v = tid; v < Sn; v += nt) cp_async4(ntab + v, ntrow + v);
     }
   }
-  pdl_wait();
-  pdl_trigger();
   const int64_t rank0 = tid < a.take_stride ? load_index(a.selected, a.sel64, c.row * a.take_stride + tid) : -1;
   c.take = a.takes[c.row];
   const RowBounds rb = row_bounds(c.n, 64, a.window);
@@ -565,12 +563,12 @@ extern "C" int v1x_topk(float* scores, int64_t score_stride, int64_t cols, const
       cudaFuncSetAttribute(topk_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(limit));
     }
     if (cols <= kRegKeys * kTopkThreads)
-      launch_pdl(topk_kernel<2>, dim3(static_cast<unsigned>(batch)), dim3(kTopkThreads), static_cast<size_t>(bytes()), s, a);
+      launch_kernel(topk_kernel<2>, dim3(static_cast<unsigned>(batch)), dim3(kTopkThreads), static_cast<size_t>(bytes()), s, a);
     else
-      launch_pdl(topk_kernel<1>, dim3(static_cast<unsigned>(batch)), dim3(kTopkThreads), static_cast<size_t>(bytes()), s, a);
+      launch_kernel(topk_kernel<1>, dim3(static_cast<unsigned>(batch)), dim3(kTopkThreads), static_cast<size_t>(bytes()), s, a);
   } else {
     a.stage_take = a.stage_nt = a.memb_off = a.ntab_off = 0;
-    launch_pdl(topk_kernel<0>, dim3(static_cast<unsigned>(batch)), dim3(kTopkThreads), 0, s, a);
+    launch_kernel(topk_kernel<0>, dim3(static_cast<unsigned>(batch)), dim3(kTopkThreads), 0, s, a);
   }
   return launch_status("v1x_topk");
 }

@@ -32,10 +32,10 @@ from .sharding import row_bytes
 class SelectionStep:
     """One query step over a batch of rows (see the module docstring).
 
-    All kernels run in order on the caller's current stream.  Each is launched
-    with programmatic stream serialization, so it starts while its predecessor
-    drains; the centre scorer reads only caller inputs before its epilogue, so
-    it streams centre pages while metadata and staging are still running.
+    All kernels run in order on the caller's current stream, the latency-bound
+    selection kernels at high launch priority and the gather at the default, so
+    that independent batches stepped on separate streams overlap: one batch's
+    gather fills the GPU while the next batch is selected.
     """
 
     def __init__(self, case, gather: bool = True, gather_v: bool = False, fused_route_pages: bool = True,

@@ -491,7 +491,8 @@ def run_component(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--steps", type=int, default=2000,
+                    help="timed steps (the default times ~0.3 s, enough for the NVML clock samples)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--requests", type=int, default=0,
                     help="override the per-GPU batch (small cases for profiling; not a bench config)")

@@ -3,11 +3,11 @@
  * query-side selection path.
  *
  * Conventions shared by every entry point:
- *   - Kernels of the query path (metadata, staging, scoring, route, topk,
- *     gather) are launched with programmatic stream serialization: a kernel
- *     may start its set-up while the previous kernel on the stream finishes,
- *     reading only caller inputs that no kernel of this library writes before
- *     it waits for that kernel's completion.
+ *   - Kernels of the query path (metadata, staging, scoring, route, topk) are
+ *     launched at the device's greatest stream priority, the gather at the
+ *     default priority, so that independent batches on separate streams
+ *     overlap (one batch's gather fills the SMs the next batch's selection
+ *     leaves free).
  *   - All tensor arguments are raw DEVICE pointers of the dtype named in the
  *     comment; sizes and strides are in ELEMENTS unless the name says bytes.
  *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Every call only
