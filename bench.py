@@ -147,26 +147,38 @@ def cpu_port_rate(cfg, seed, rows, budget_s=20.0):
 
 
 def run_reference(args, cfg):
+    """The reference arm: the CPU port of the path on the host cores.  One step
+    = one query row of a 4-request (decode) / 32-request (single) sample of the
+    workload; the arm stops after ~60 s of timed steps and reports the rate over
+    the steps it timed."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
+    import oracle.port as port
+
+    synth = importlib.import_module("10_20_b200.synth")
+    torch.set_num_threads(os.cpu_count() or 1)
     rows = 4 if args.workload == "decode" else 32
-    vals = []
-    for _ in range(args.warmup):
-        cpu_port_rate(cfg, 1000, rows, budget_s=2.0)
-    meta = None
-    for _ in range(args.steps):
-        v, meta = cpu_port_rate(cfg, 1000, rows, budget_s=max(5.0, 60.0 / max(args.steps, 1)))
-        vals.append(v)
-    value = statistics.median(vals)
+    case = make_case(synth, cfg, 1000, "cpu", rows=rows)
+    c = port.to_numpy_case(case)
+    for k in range(max(args.warmup, 1)):
+        port.run_rows(c, rows=[k % rows])
+    done, t0 = 0, time.perf_counter()
+    for k in range(args.steps):
+        port.run_rows(c, rows=[k % rows])
+        done += 1
+        if time.perf_counter() - t0 > 60.0:
+            break
+    el = time.perf_counter() - t0
+    value = done / el
     cores = os.cpu_count()
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "fp8-e4m3 keys, f32 scores, bf16 latent", "data": "synthetic",
             "config": {"workload": args.workload, **{k: v for k, v in cfg.items()}},
             "cpu_baseline": {"value": value, "unit": "queries/s", "cores": cores, "kind": "port",
-                             "sample": f"{meta['rows']} queries of a {rows}-request sample "
-                                       f"(oracle port, numpy/BLAS), per step"},
+                             "sample": f"{done} of {args.steps} steps timed ({el:.1f} s), one query row of a "
+                                       f"{rows}-request sample per step, oracle port (numpy + BLAS)"},
             "e2e": {"value": value, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
