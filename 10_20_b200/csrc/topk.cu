@@ -135,11 +135,14 @@ __device__ __forceinline__ void mask_page(const TopkArgs& a, const RowCtx& c, fl
   }
 }
 
+// Two CTAs per SM (register cap 64, a few spilled registers): with many rows
+// (1024 single-head queries) the second resident CTA hides the first's latency
+// chains, and with few rows it leaves room for an overlapping batch's gather.
 // kMode 0: keys read from global memory at every use (rows too long for smem);
 // 1: keys staged in shared memory; 2: staged and also held in registers
 // (cols <= kRegKeys * 512).
 template <int kMode>
-__global__ void __launch_bounds__(kTopkThreads, 1) topk_kernel(const __grid_constant__ TopkArgs a) {
+__global__ void __launch_bounds__(kTopkThreads, 2) topk_kernel(const __grid_constant__ TopkArgs a) {
   constexpr bool kStaged = kMode > 0;
   extern __shared__ __align__(16) uint32_t dyn[];
   __shared__ TopkSmem sm;
