@@ -1,0 +1,221 @@
+"""Drop-in for the reference's ``Indexer`` library API
+(sglang/srt/layers/attention/v1_deepseek/runtime.py:693-937): one layer's native
+cache + V1 page arena, ``prepare`` / ``query`` / ``release_request`` / ``clear``
+/ ``close``, calls serialised by a lock.
+
+``query`` mirrors :828-907: input validation, the per-owner ``prepare`` to each
+request's largest visible length, then per chunk of at most ``q_buckets[-1]``
+rows a per-bucket ``Query`` (:281-678) that stages the rows into capture-stable
+buffers (zeroing the padding rows, copying each owner's page tables), runs the
+selection step (optionally as a captured CUDA graph) and returns clones of the
+physical slot ids -- or of the x4 expanded logical positions when
+``Config.expand_output`` -- plus the logical ids when ``return_logical``.
+
+One deliberate difference: building a bucket's reordered pages, members and
+centres from the native cache is the index build, outside this path.  The
+caller supplies it as ``bucket_source(owner, bucket) -> (tmp, mapping,
+centers)`` (see lifecycle.PageArena); ``prepare`` otherwise keeps the
+reference's signature and checks.
+"""
+from __future__ import annotations
+
+import threading
+
+import torch
+
+from .config import Config
+from .lifecycle import PageArena
+from .pipeline import SelectionStep
+from .synth import QueryCase
+
+
+class _Query:
+    """Capture-stable buffers of one query bucket of `rows` rows (:281-313, :643-678)."""
+
+    def __init__(self, owner: "Indexer", rows: int):
+        c, d = owner.config, owner.device
+        self.owner, self.rows = owner, rows
+        a = owner.arena
+        self.case = QueryCase(
+            B=rows, H=c.heads, P=c.pages, take=c.take, window=c.window, topk=c.topk,
+            lens=torch.zeros(rows, dtype=torch.int32, device=d),
+            q8=torch.zeros((rows, c.heads, 128), dtype=torch.float8_e4m3fn, device=d),
+            w=torch.zeros((rows, c.heads), dtype=torch.float32, device=d),
+            native=owner.native, fine=a.fine, centers=a.centers, members=a.members,
+            native_table=torch.zeros((rows, c.pages), dtype=torch.int32, device=d),
+            reordered_table=torch.zeros((rows, c.pages), dtype=torch.int32, device=d),
+            center_table=torch.zeros((rows, c.pages // 8), dtype=torch.int32, device=d),
+            capacity=a.capacity)
+        ratio = c.ratio
+        self.step = SelectionStep(self.case, gather=False, ratio=(ratio.numerator, ratio.denominator),
+                                  expand=c.expand_output)
+        self.graph = None
+        self.graphs = c.graphs
+
+    def _execute(self):
+        if not self.graphs:
+            self.step.run()
+            return
+        if self.graph is None:
+            self.step.run()     # the first call runs eagerly, then the step is captured
+            s = torch.cuda.Stream(device=self.owner.device)
+            s.wait_stream(torch.cuda.current_stream(self.owner.device))
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                self.step.run()
+            torch.cuda.current_stream(self.owner.device).wait_stream(s)
+            self.graph = g
+            return
+        self.graph.replay()
+
+    def run(self, q, w, native_tables, lengths, states, return_logical=False):
+        c = self.case
+        n = len(q)
+        c.q8[:n].copy_(q)
+        c.w[:n].copy_(w)
+        c.lens[:n].copy_(lengths)
+        c.native_table[:n, : native_tables.shape[1]].copy_(native_tables)
+        if native_tables.shape[1] < c.native_table.shape[1]:
+            c.native_table[:n, native_tables.shape[1]:].zero_()
+        if n < self.rows:
+            for t in (c.q8.view(torch.uint8), c.w, c.lens, c.native_table, c.reordered_table, c.center_table):
+                t[n:].zero_()
+        row = 0
+        while row < n:
+            end = row + 1
+            while end < n and states[end] is states[row]:
+                end += 1
+            c.reordered_table[row:end].copy_(states[row].table[None].expand(end - row, -1))
+            c.center_table[row:end].copy_(states[row].center_table[None].expand(end - row, -1))
+            row = end
+        self._execute()
+        out = self.step.expanded if self.owner.config.expand_output else self.step.physical
+        result = out[:n].clone()
+        if return_logical:
+            result = (result, self.step.logical[:n].clone())
+        return result
+
+
+class Indexer:
+    """One layer's native cache + V1 arena (reference Indexer, :693-937)."""
+
+    def __init__(self, native_cache, config: Config = Config(), bucket_source=None):
+        if (
+            native_cache.dtype != torch.uint8
+            or not native_cache.is_cuda
+            or not native_cache.is_contiguous()
+            or native_cache.ndim not in (2, 4)
+            or native_cache.numel() % 8448
+            or (native_cache.ndim == 2 and native_cache.shape[1] != 8448)
+            or (native_cache.ndim == 4 and native_cache.shape[1:] != (64, 1, 132))
+        ):
+            raise ValueError("Expected native contiguous FP8 page64 packed byte cache")
+        if config.reservation > config.budget_bytes:
+            raise ValueError(f"V1 reservation {config.reservation} exceeds budget {config.budget_bytes}")
+        self.config = config
+        self.native = native_cache.view(-1, 8448)
+        self.device = native_cache.device
+        self.capacity = config.pages * config.max_requests
+        self.arena = PageArena(self.capacity, config.pages, self.device, max_requests=config.max_requests,
+                               graphs=config.graphs, staging_rows=config.q_buckets[-1])
+        self.bucket_source = bucket_source
+        self.queries: dict[int, _Query] = {}
+        self.lock = threading.RLock()
+        self.closed = False
+
+    @property
+    def states(self):
+        return self.arena.states
+
+    def _begin(self):
+        if self.closed:
+            raise RuntimeError("Indexer is closed")
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("V1 index subgraphs must execute outside full-model capture")
+
+    def _source(self, owner, bucket):
+        if self.bucket_source is None:
+            raise RuntimeError("no bucket_source: building bucket indices is outside this path")
+        return self.bucket_source(owner, bucket)
+
+    def _prepare(self, owner, native_table, length):
+        if not 0 <= length <= self.config.max_context:
+            raise ValueError("Index context capacity exceeded")
+        if (native_table.dtype != torch.int32 or native_table.device != self.device or native_table.ndim != 1
+                or native_table.numel() < -(-length // 64) or not native_table.is_contiguous()):
+            raise ValueError("Invalid compact native page table")
+        return self.arena.prepare(owner, length, self._source)
+
+    @torch.inference_mode()
+    def prepare(self, owner, native_table, length):
+        with self.lock:
+            self._begin()
+            return self._prepare(owner, native_table, length)
+
+    @torch.inference_mode()
+    def query(self, q, weights, native_tables, lengths, owners, lengths_cpu, return_logical=False):
+        n = len(q)
+        c = self.config
+        if (
+            q.shape != (n, c.heads, 128) or q.dtype != torch.float8_e4m3fn or not q.is_contiguous()
+            or weights.shape != (n, c.heads) or weights.dtype != torch.float32 or not weights.is_contiguous()
+            or native_tables.ndim != 2 or native_tables.shape[0] != n or native_tables.shape[1] > c.pages
+            or native_tables.dtype != torch.int32 or not native_tables.is_contiguous()
+            or lengths.numel() != n or lengths.dtype != torch.int32 or not lengths.is_contiguous()
+            or len(owners) != n or len(lengths_cpu) != n
+            or any(t.device != self.device for t in (q, weights, native_tables, lengths))
+        ):
+            raise ValueError("Unsupported V1 FP8/page64 query inputs")
+        cpu = [int(x) for x in lengths_cpu]
+        if any(x < 0 or x > c.max_context or (x + 63) // 64 > native_tables.shape[1] for x in cpu):
+            raise ValueError("Query lengths exceed page-table/context capacity")
+        with self.lock:
+            self._begin()
+            if not n:
+                empty = torch.empty((0, c.topk * 4 + 64 if c.expand_output else c.topk), device=self.device,
+                                    dtype=torch.int32)
+                return (empty, torch.empty((0, c.topk), device=self.device, dtype=torch.int32)) \
+                    if return_logical else empty
+            # build each request to its largest visible length before querying
+            max_rows = {}
+            for i, key in enumerate(owners):
+                if key not in max_rows or cpu[i] > cpu[max_rows[key]]:
+                    max_rows[key] = i
+            for key, i in max_rows.items():
+                self._prepare(key, native_tables[i], cpu[i])
+            self.arena.check()
+            outputs = []
+            for start in range(0, n, c.q_buckets[-1]):
+                end = min(n, start + c.q_buckets[-1])
+                rows = next(r for r in c.q_buckets if r >= end - start)
+                if rows not in self.queries:
+                    self.queries[rows] = _Query(self, rows)
+                outputs.append(self.queries[rows].run(q[start:end], weights[start:end], native_tables[start:end],
+                                                      lengths.reshape(-1)[start:end],
+                                                      [self.states[x] for x in owners[start:end]],
+                                                      return_logical))
+            if len(outputs) == 1:
+                return outputs[0]
+            if return_logical:
+                return tuple(torch.cat([x[i] for x in outputs]) for i in (0, 1))
+            return torch.cat(outputs)
+
+    @torch.inference_mode()
+    def release_request(self, owner):
+        with self.lock:
+            self._begin()
+            self.arena.release(owner)
+
+    @torch.inference_mode()
+    def clear(self):
+        with self.lock:
+            if self.closed:
+                return
+            for key in list(self.states):
+                self.arena.release(key)
+            torch.cuda.synchronize(self.device)
+            self.queries.clear()
+
+    def close(self):
+        self.clear()
+        self.closed = True

@@ -49,16 +49,18 @@ class State:
 
 class PageArena:
     def __init__(self, capacity: int, pages: int, device, max_requests: int | None = None,
-                 graphs: bool = False):
+                 graphs: bool = False, staging_rows: int = 0):
         """capacity: arena pages; pages: per-request page-table capacity
-        (Config.pages, max_context / 64); max_requests: live request limit."""
+        (Config.pages, max_context / 64); max_requests: live request limit;
+        staging_rows: query rows whose 68 sink/tail staging pages follow the arena
+        in the fine pool (the reference's q_buckets[-1] * 68, :729)."""
         if capacity <= 0 or capacity % 16 or pages <= 0 or pages % 16:
             raise ValueError("capacity and pages must be positive multiples of 16")
         d = self.device = torch.device(device)
         self.capacity, self.pages = capacity, pages
         self.max_requests = max_requests if max_requests is not None else max(capacity // pages, 1)
         self.max_leases = capacity // 16
-        self.fine = torch.zeros((capacity, PAGE_BYTES), dtype=torch.uint8, device=d)
+        self.fine = torch.zeros((capacity + staging_rows * 68, PAGE_BYTES), dtype=torch.uint8, device=d)
         self.centers = torch.zeros((-(-capacity // 8), PAGE_BYTES), dtype=torch.uint8, device=d)
         self.members = torch.full((capacity, 64), -1, dtype=torch.int32, device=d)
         self.refs = torch.zeros(capacity, dtype=torch.int32, device=d)

@@ -39,11 +39,16 @@ class SelectionStep:
     """
 
     def __init__(self, case, gather: bool = True, gather_v: bool = False, fused_route_pages: bool = True,
-                 keep_logits: bool = False):
+                 keep_logits: bool = False, ratio=None, expand: bool = False):
+        """ratio=None: the fixed page budget take = min(pages, case.take) (the
+        reference's BudgetMetadata); ratio=(num, den): the reference's default take
+        rule min(pages, max(ceil(pages*num/den), ceil(topk/64))).  expand: also
+        write the x4 expanded logical positions ([B, 4*topk+64], -1 padded)."""
         c = self.case = case
         d = c.lens.device
         B = c.B
-        self.budget = torch.tensor([c.take], dtype=torch.int32, device=d)
+        self.ratio = (1, 2) if ratio is None else (int(ratio[0]), int(ratio[1]))
+        self.budget = torch.tensor([c.take], dtype=torch.int32, device=d) if ratio is None else None
         self.fine_lens = torch.zeros(B, dtype=torch.int32, device=d)
         self.takes = torch.zeros(B, dtype=torch.int32, device=d)
         self.dg_lens = torch.zeros(B, dtype=torch.int32, device=d)
@@ -59,6 +64,8 @@ class SelectionStep:
         self.logical = torch.empty_like(self.physical)
         self.raw = torch.empty_like(self.physical)
         self.no_expansion = torch.empty_strided((B, 0), (0, 1), device=d, dtype=torch.int32)
+        self.expanded = (torch.empty((B, c.topk * 4 + 64), dtype=torch.int32, device=d) if expand
+                         else self.no_expansion)
         self.gather = gather and c.latent is not None
         self.gather_v = gather_v
         if self.gather:
@@ -66,7 +73,6 @@ class SelectionStep:
             self.kv = torch.empty((B, c.topk, 1, D), dtype=c.latent.dtype, device=d)
             self.kv2 = torch.empty_like(self.kv) if gather_v else None
         self.fused = query_fused.module()
-        self.meta = K.BudgetMetadata(self.budget)
         self.graph = None
         # fused_route_pages: page maxima from the scoring epilogue + route_pages with
         # the fine-table write (the reference's query_route_table_fusion); equal
@@ -108,7 +114,7 @@ class SelectionStep:
                                      self.width, out=self.scores[rs], clean_logits=False)
         self.fused.topk(self.scores[rs], self.fine_lens[rs], c.members, c.reordered_table[rs],
                         c.native_table[rs], self.selected[rs], c.lens[rs], self.takes[rs], self.physical[rs],
-                        self.logical[rs], self.raw[rs], c.window, True, self.no_expansion[rs], True, True,
+                        self.logical[rs], self.raw[rs], c.window, True, self.expanded[rs], True, True,
                         self.fine_table[rs], False)
 
     def _gather(self, rs):
@@ -125,8 +131,9 @@ class SelectionStep:
         rs = slice(0, B)
         # query metadata with the fixed page budget + sink/tail staging, one launch
         K.query_prepare(c.lens, c.native_table, self.fine_lens, self.takes, self.dg_lens, self.center_lens,
-                        self.tail_rows, c.P, c.topk, 1, 2, 64, c.window, c.native, c.native.view(torch.float32),
-                        c.fine, c.fine.view(torch.float32), c.capacity, 68, budget=self.budget)
+                        self.tail_rows, c.P, c.topk, self.ratio[0], self.ratio[1], 64, c.window, c.native,
+                        c.native.view(torch.float32), c.fine, c.fine.view(torch.float32), c.capacity, 68,
+                        budget=self.budget)
         self._centres(rs)
         self._route(rs)
         self._fine_topk(rs)
