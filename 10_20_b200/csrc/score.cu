@@ -42,11 +42,16 @@ __device__ __forceinline__ float2 e4m3x2_to_float2(uint16_t v) {
   return __half22float2(*reinterpret_cast<const __half2*>(&h));
 }
 
-__global__ void __launch_bounds__(kScoreThreads) score_simt_kernel(const __grid_constant__ ScoreArgs a) {
-  __shared__ __align__(16) float qs[kSimtMaxHeads * 128];
-  __shared__ float ws[kSimtMaxHeads];
+// kHeads: 1 compiles the single-head case (a 512-byte query in shared memory and
+// a register budget for eight resident CTAs per SM); 0 takes the head count from
+// the arguments (up to kSimtMaxHeads).  The arithmetic per key is the same.
+template <int kHeads>
+__global__ void __launch_bounds__(kScoreThreads, kHeads == 1 ? 8 : 1)
+    score_simt_kernel(const __grid_constant__ ScoreArgs a) {
+  __shared__ __align__(16) float qs[(kHeads ? kHeads : kSimtMaxHeads) * 128];
+  __shared__ float ws[kHeads ? kHeads : kSimtMaxHeads];
   const int64_t b = blockIdx.x;
-  const int H = a.heads;
+  const int H = kHeads ? kHeads : a.heads;
   for (int i = threadIdx.x; i < H * 64; i += blockDim.x) {
     const uint16_t two = reinterpret_cast<const uint16_t*>(a.q + b * H * 128)[i];
     const float2 f = e4m3x2_to_float2(two);
@@ -149,7 +154,8 @@ int score_dispatch(const uint8_t* q, const float* w, const uint8_t* pool, int64_
               static_cast<int>(heads), relu, clean, lens_kind};
   const int64_t blocks = (max_len + kScoreThreads - 1) / kScoreThreads;
   const dim3 grid(static_cast<unsigned>(batch), static_cast<unsigned>(blocks < 8 ? blocks : 8));
-  launch_kernel(score_simt_kernel, grid, dim3(kScoreThreads), 0, as_stream(stream), a);
+  if (heads == 1) launch_kernel(score_simt_kernel<1>, grid, dim3(kScoreThreads), 0, as_stream(stream), a);
+  else launch_kernel(score_simt_kernel<0>, grid, dim3(kScoreThreads), 0, as_stream(stream), a);
   return launch_status("v1x_score_fp8");
 }
 }  // namespace
