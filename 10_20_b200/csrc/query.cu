@@ -7,6 +7,8 @@
 //   stage_tail_shared :518-564, query_metadata :568-591, expand_logical :594-600;
 //   the fixed-budget take rule of bench_v1_dynamic_budget_metadata.py:5-27.
 // All index arithmetic is 64-bit (the pools exceed 2 GiB).
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace v1x {
@@ -197,10 +199,10 @@ __global__ void __launch_bounds__(128) query_prepare_kernel(const __grid_constan
   if (!r.owner) return;
   const int count = r.rb.sink + r.n - r.rb.tail;
   const int64_t need = min(s.scratch, static_cast<int64_t>(max((count + 63) / 64, 1)));
-  const int p0 = blockIdx.y * kStagePages;
-  const int p1 = static_cast<int>(min(need, static_cast<int64_t>(p0 + kStagePages)));
-  if (p0 >= p1) return;
-  stage_pages(s, row, r.rb, count, p0, p1);
+  for (int p0 = blockIdx.y * kStagePages; p0 < need; p0 += gridDim.y * kStagePages) {
+    const int p1 = static_cast<int>(min(need, static_cast<int64_t>(p0 + kStagePages)));
+    stage_pages(s, row, r.rb, count, p0, p1);
+  }
 }
 
 __global__ void mask_fine_kernel(float* __restrict__ scores, const void* selected, int sel64,
@@ -338,7 +340,11 @@ extern "C" int v1x_query_prepare(const int32_t* lens, const int32_t* nt, int32_t
                    budget};
   const StageArgs s{native_bytes, native_scales, nt, lens, fine_bytes, fine_scales, tail_rows, cap, np,
                     scratch, sink, window, batch, 1};
-  const dim3 grid(static_cast<unsigned>(batch), static_cast<unsigned>((scratch + kStagePages - 1) / kStagePages));
+  // CTA (row, g) stages page groups g, g + gridDim.y, ...: enough CTAs in total to
+  // fill the GPU (about 2560), but not one per group when rows are many
+  const int64_t groups = (scratch + kStagePages - 1) / kStagePages;
+  const int64_t gy = std::min<int64_t>(groups, std::max<int64_t>(1, (2560 + batch - 1) / batch));
+  const dim3 grid(static_cast<unsigned>(batch), static_cast<unsigned>(gy));
   launch_kernel(query_prepare_kernel, grid, dim3(128), 0, as_stream(stream), m, s);
   return launch_status("v1x_query_prepare");
 }
