@@ -97,6 +97,7 @@ struct TopkSmem {
   int4 res, res2;
   int2 carry;
   int nbnd, ncand, ncand2;
+  uint32_t kmin, kmax, kmin2, kmax2;  // key range of the threshold bin / sub-bin
 };
 
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
@@ -302,7 +303,9 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_kernel(const __grid_cons
     // bin's keys are ranked exactly by (key desc, index asc) and the selected ones
     // flagged.  Rows whose bin holds more than kMaxBin keys (mass ties) and the
     // unstaged mode take the bitwise search instead.
-    bool by_bin = false;
+    bool by_bin = false, have_tie = false;
+    uint32_t tie_thr = 0;
+    int tie_need = 0;
     TopBin tb{0, 0, 0};
     if constexpr (kStaged) {
       int* hist = sm.u.h.hist;
@@ -312,6 +315,8 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_kernel(const __grid_cons
       if (tid == 0) {
         sm.ncand = 0;
         sm.ncand2 = 0;
+        sm.kmin = sm.kmin2 = 0xFFFFFFFFu;
+        sm.kmax = sm.kmax2 = 0u;
       }
       __syncthreads();
       if constexpr (kMode == 2) {
@@ -323,19 +328,28 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_kernel(const __grid_cons
       }
       __syncthreads();
       tb = find_top_bin<kTopkThreads>(a.topk, hist, sm.warp_tot, &sm.res);
-      by_bin = tb.in <= kMaxBin;
-      if (by_bin) {
-        // the histogram is dead: the candidate list reuses its storage
-        int2* cand = sm.u.c.cand;
+      // the histogram is dead: the candidate list reuses its storage.  The bin's
+      // key range is tracked while compacting it: a bin of one repeated value
+      // (ReLU zeros of single-head scores, for instance) needs no ranking -- its
+      // ties are taken by lowest index.
+      int2* cand = sm.u.c.cand;
+      const bool keep = tb.in <= kMaxBin;
+      {
         const uint32_t ltm = lanemask_lt();
         auto append = [&](int j, uint32_t k) {
           const bool m = j * nt + tid < c.L && bin_of(k) == tb.bin;
           const unsigned bal = __ballot_sync(0xffffffffu, m);
           if (bal == 0u) return;
+          const uint32_t lo = __reduce_min_sync(0xffffffffu, m ? k : 0xFFFFFFFFu);
+          const uint32_t hi = __reduce_max_sync(0xffffffffu, m ? k : 0u);
           int base = 0;
-          if (lane == 0) base = atomicAdd(&sm.ncand, __popc(bal));
+          if (lane == 0) {
+            atomicMin(&sm.kmin, lo);
+            atomicMax(&sm.kmax, hi);
+            if (keep) base = atomicAdd(&sm.ncand, __popc(bal));
+          }
           base = __shfl_sync(0xffffffffu, base, 0);
-          if (m) cand[base + __popc(bal & ltm)] = make_int2(static_cast<int>(k), j * nt + tid);
+          if (keep && m) cand[base + __popc(bal & ltm)] = make_int2(static_cast<int>(k), j * nt + tid);
         };
         if constexpr (kMode == 2) {
 #pragma unroll
@@ -344,7 +358,14 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_kernel(const __grid_cons
         } else {
           for (int j = 0; j < nsl; ++j) append(j, j * nt + tid < c.L ? key_of(j) : 0u);
         }
-        __syncthreads();
+      }
+      __syncthreads();
+      if (sm.kmin == sm.kmax) {
+        tie_thr = sm.kmin;
+        tie_need = a.topk - tb.above;
+        have_tie = true;
+      } else if (keep) {
+        by_bin = true;
         int need_bin = a.topk - tb.above;
         const int2* rk = cand;
         int nres = tb.in;
@@ -371,8 +392,7 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_kernel(const __grid_cons
           }
           __syncthreads();
           const int4 r2 = sm.res2;
-          by_bin = r2.z <= kMaxBin2;
-          if (by_bin) {
+          if (r2.z <= kMaxBin2) {
             for (int q = tid; q < tb.in; q += nt) {
               const int2 me = cand[q];
               const int sub = (me.x >> (24 - kBinBits)) & 255;
@@ -383,6 +403,30 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_kernel(const __grid_cons
             need_bin -= r2.y;
             rk = sm.cand2;
             nres = r2.z;
+          } else {
+            // a crowded sub-bin: one repeated value takes the tie path, anything
+            // else the bitwise search
+            by_bin = false;
+            uint32_t lo = 0xFFFFFFFFu, hi = 0u;
+            for (int q = tid; q < tb.in; q += nt) {
+              const uint32_t k = static_cast<uint32_t>(cand[q].x);
+              if (((k >> (24 - kBinBits)) & 255) == static_cast<uint32_t>(r2.x)) {
+                lo = min(lo, k);
+                hi = max(hi, k);
+              }
+            }
+            lo = __reduce_min_sync(0xffffffffu, lo);
+            hi = __reduce_max_sync(0xffffffffu, hi);
+            if (lane == 0) {
+              atomicMin(&sm.kmin2, lo);
+              atomicMax(&sm.kmax2, hi);
+            }
+            __syncthreads();
+            if (sm.kmin2 == sm.kmax2) {
+              tie_thr = sm.kmin2;
+              tie_need = need_bin - r2.y;
+              have_tie = true;
+            }
           }
         }
         if (by_bin) {
@@ -402,9 +446,9 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_kernel(const __grid_cons
         }
       }
     }
-    uint32_t thr = 0;
-    int need = 0;
-    if (!by_bin) {
+    uint32_t thr = tie_thr;
+    int need = tie_need;
+    if (!by_bin && !have_tie) {
       int gt = 0;
       thr = block_kth_largest<kTopkWarps>(
           a.topk,
