@@ -6,12 +6,15 @@
 // kernels.py:310-313 (fine) / :210-213 (coarse), pinned against DeepGEMM at
 // experiments/fine_pool_shared_20261021/test_and_bench.py:37-41.
 //
-// This file holds the SIMT path: one thread per key, 16-byte loads of the
-// key's 128 FP8 bytes, exact e4m3 -> fp32 conversion, and a FIXED fp32
-// evaluation order (per head d = 0..127 with fma -- every e4m3 x e4m3 product
-// is exact in fp32 -- then acc += w_h * relu with separately rounded multiply
-// and add, then * scale) so the result is bit-identical to the CPU oracle.
-// It is the path for few heads (the single-head config is 2 FLOP/byte).
+// This file holds the SIMT path for few heads (the single-head config is 2
+// FLOP/byte).  Eight lanes share a key, each holding 16 of its 128 FP8 bytes, so
+// one warp load covers four consecutive keys (512 contiguous bytes) and the row's
+// query sits in registers (one head) or shared memory.  Exact e4m3 -> fp32
+// conversion and a FIXED fp32 evaluation order make the result bit-identical to
+// the CPU oracle: per head, each lane accumulates its 16 products with fma from
+// 0 (every e4m3 x e4m3 product is exact in fp32), the eight partial sums combine
+// as ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7)), then acc += w_h * relu with separately
+// rounded multiply and add, then one multiply by the key's scale.
 #include <cuda_fp8.h>
 
 #include "common.cuh"
@@ -42,81 +45,141 @@ __device__ __forceinline__ float2 e4m3x2_to_float2(uint16_t v) {
   return __half22float2(*reinterpret_cast<const __half2*>(&h));
 }
 
-// kHeads: 1 compiles the single-head case (a 512-byte query in shared memory and
-// a register budget for eight resident CTAs per SM); 0 takes the head count from
-// the arguments (up to kSimtMaxHeads).  The arithmetic per key is the same.
+// Keys per warp iteration: kKeyLoads loads of four keys each.
+constexpr int kKeyLoads = 8;
+constexpr int kWarpKeys = 4 * kKeyLoads;
+
+// kHeads: 1 compiles the single-head case (the lane's 16 query values in
+// registers, 128 registers per thread for four resident CTAs per SM); 0 takes the
+// head count from the arguments (up to kSimtMaxHeads) with the query in shared
+// memory.  The arithmetic per key is the same.
 template <int kHeads>
-__global__ void __launch_bounds__(kScoreThreads, kHeads == 1 ? 8 : 1)
+__global__ void __launch_bounds__(kScoreThreads, kHeads == 1 ? 4 : 1)
     score_simt_kernel(const __grid_constant__ ScoreArgs a) {
-  __shared__ __align__(16) float qs[(kHeads ? kHeads : kSimtMaxHeads) * 128];
-  __shared__ float ws[kHeads ? kHeads : kSimtMaxHeads];
+  __shared__ __align__(16) float qs[kHeads == 1 ? 4 : kSimtMaxHeads * 128];
+  __shared__ float ws[kHeads == 1 ? 1 : kSimtMaxHeads];
   const int64_t b = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int grp = lane >> 3, part = lane & 7;  // key of the load, 16-byte part of it
   const int H = kHeads ? kHeads : a.heads;
-  for (int i = threadIdx.x; i < H * 64; i += blockDim.x) {
-    const uint16_t two = reinterpret_cast<const uint16_t*>(a.q + b * H * 128)[i];
-    const float2 f = e4m3x2_to_float2(two);
-    qs[2 * i] = f.x;
-    qs[2 * i + 1] = f.y;
-  }
-  for (int h = threadIdx.x; h < H; h += blockDim.x) ws[h] = a.w[b * H + h];
-  __syncthreads();
-  // Grid-stride over the row's blocks of 128 keys: the query is staged once per
-  // CTA, and the next block's key bytes are loaded while the current block is
-  // evaluated (two keys' loads in flight per thread).
-  const int64_t n = score_len(a.lens[b], a.lens_kind);
-  const int64_t lim = min(n, a.max_len);   // keys j < lim are scored
-  const int64_t step = static_cast<int64_t>(gridDim.y) * blockDim.x;
-  auto load_key = [&](int64_t j, uint4 (&kw)[8], float& scale) {
-    if (j < lim) {
-      const int64_t page = a.table[b * a.table_stride + j / 64];
-      const uint8_t* kp = a.pool + page * kPageBytes + (j % 64) * 128;
+  float qr[kHeads == 1 ? 16 : 1];
+  float w0 = 0.0f;
+  if constexpr (kHeads == 1) {
+    const uint4 qw = reinterpret_cast<const uint4*>(a.q + b * 128)[part];
+    const uint32_t q4[4] = {qw.x, qw.y, qw.z, qw.w};
 #pragma unroll
-      for (int c = 0; c < 8; ++c) kw[c] = reinterpret_cast<const uint4*>(kp)[c];
-      scale = reinterpret_cast<const float*>(a.pool + page * kPageBytes)[kScaleWord + j % 64];
+    for (int u = 0; u < 4; ++u) {
+      const float2 lo = e4m3x2_to_float2(static_cast<uint16_t>(q4[u] & 0xFFFFu));
+      const float2 hi = e4m3x2_to_float2(static_cast<uint16_t>(q4[u] >> 16));
+      qr[4 * u] = lo.x;
+      qr[4 * u + 1] = lo.y;
+      qr[4 * u + 2] = hi.x;
+      qr[4 * u + 3] = hi.y;
+    }
+    w0 = a.w[b];
+  } else {
+    for (int i = threadIdx.x; i < H * 64; i += blockDim.x) {
+      const uint16_t two = reinterpret_cast<const uint16_t*>(a.q + b * H * 128)[i];
+      const float2 f = e4m3x2_to_float2(two);
+      qs[2 * i] = f.x;
+      qs[2 * i + 1] = f.y;
+    }
+    for (int h = threadIdx.x; h < H; h += blockDim.x) ws[h] = a.w[b * H + h];
+    __syncthreads();
+  }
+  // A warp takes blocks of kWarpKeys keys (inside one page), striding over the
+  // row; the next block's bytes are loaded while the current one is evaluated.
+  const int64_t n = score_len(a.lens[b], a.lens_kind);
+  const int64_t lim = min(n, a.max_len);  // keys j < lim are scored
+  const int64_t live = (lim + kWarpKeys - 1) / kWarpKeys;  // blocks holding a scored key
+  const int64_t wstep = static_cast<int64_t>(gridDim.y) * (kScoreThreads / 32);
+  auto load = [&](int64_t blk, uint4 (&kw)[kKeyLoads], float& scale) {
+    const int64_t k0 = blk * kWarpKeys;
+    if (blk < live) {
+      const int64_t page = a.table[b * a.table_stride + k0 / 64];
+      const uint8_t* base = a.pool + page * kPageBytes;
+#pragma unroll
+      for (int u = 0; u < kKeyLoads; ++u) {
+        const int64_t key = k0 + u * 4 + grp;
+        kw[u] = key < lim ? reinterpret_cast<const uint4*>(base + (key % 64) * 128)[part] : make_uint4(0, 0, 0, 0);
+      }
+      const int64_t ks = k0 + lane;  // lane i holds the scale of the block's key i
+      scale = ks < lim ? reinterpret_cast<const float*>(base)[kScaleWord + ks % 64] : 0.0f;
     }
   };
-  uint4 cur[8], nxt[8];
+  uint4 cur[kKeyLoads], nxt[kKeyLoads];
   float cur_scale = 0.0f, nxt_scale = 0.0f;
-  int64_t j = static_cast<int64_t>(blockIdx.y) * blockDim.x + threadIdx.x;
-  load_key(j, cur, cur_scale);
-  for (; j - threadIdx.x < a.max_len; j += step) {
-    load_key(j + step, nxt, nxt_scale);
-    float result = -CUDART_INF_F;
-    if (j < lim) {
+  int64_t blk = static_cast<int64_t>(blockIdx.y) * (kScoreThreads / 32) + warp;
+  load(blk, cur, cur_scale);
+  for (; blk < live; blk += wstep) {
+    load(blk + wstep, nxt, nxt_scale);
+    const int64_t k0 = blk * kWarpKeys;
+    float res[kKeyLoads];
+#pragma unroll
+    for (int u = 0; u < kKeyLoads; ++u) {
+      const uint32_t k4[4] = {cur[u].x, cur[u].y, cur[u].z, cur[u].w};
+      float kf[16];
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        const float2 lo = e4m3x2_to_float2(static_cast<uint16_t>(k4[v] & 0xFFFFu));
+        const float2 hi = e4m3x2_to_float2(static_cast<uint16_t>(k4[v] >> 16));
+        kf[4 * v] = lo.x;
+        kf[4 * v + 1] = lo.y;
+        kf[4 * v + 2] = hi.x;
+        kf[4 * v + 3] = hi.y;
+      }
       float acc = 0.0f;
       for (int h = 0; h < H; ++h) {
-        const float4* qh = reinterpret_cast<const float4*>(qs + h * 128);
-        float dot = 0.0f;
+        float p = 0.0f;
+        if constexpr (kHeads == 1) {
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const uint32_t w4[4] = {cur[c].x, cur[c].y, cur[c].z, cur[c].w};
+          for (int d = 0; d < 16; ++d) p = __fmaf_rn(qr[d], kf[d], p);
+        } else {
+          const float4* qh = reinterpret_cast<const float4*>(qs + h * 128 + part * 16);
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const float2 lo = e4m3x2_to_float2(static_cast<uint16_t>(w4[u] & 0xFFFFu));
-            const float2 hi = e4m3x2_to_float2(static_cast<uint16_t>(w4[u] >> 16));
-            const float4 qq = qh[c * 4 + u];
-            dot = __fmaf_rn(qq.x, lo.x, dot);
-            dot = __fmaf_rn(qq.y, lo.y, dot);
-            dot = __fmaf_rn(qq.z, hi.x, dot);
-            dot = __fmaf_rn(qq.w, hi.y, dot);
+          for (int v = 0; v < 4; ++v) {
+            const float4 qq = qh[v];
+            p = __fmaf_rn(qq.x, kf[4 * v], p);
+            p = __fmaf_rn(qq.y, kf[4 * v + 1], p);
+            p = __fmaf_rn(qq.z, kf[4 * v + 2], p);
+            p = __fmaf_rn(qq.w, kf[4 * v + 3], p);
           }
         }
-        const float r = a.relu ? (dot > 0.0f ? dot : 0.0f) : dot;
-        acc = __fadd_rn(acc, __fmul_rn(ws[h], r));
+        p = __fadd_rn(p, __shfl_xor_sync(0xffffffffu, p, 1));
+        p = __fadd_rn(p, __shfl_xor_sync(0xffffffffu, p, 2));
+        p = __fadd_rn(p, __shfl_xor_sync(0xffffffffu, p, 4));
+        const float r = a.relu ? (p > 0.0f ? p : 0.0f) : p;
+        acc = __fadd_rn(acc, __fmul_rn(kHeads == 1 ? w0 : ws[h], r));
       }
-      result = __fmul_rn(acc, cur_scale);
+      const float scale = __shfl_sync(0xffffffffu, cur_scale, u * 4 + grp);
+      const int64_t key = k0 + u * 4 + grp;
+      res[u] = key < lim ? __fmul_rn(acc, scale) : -CUDART_INF_F;
+      if (part == u && a.out && key < a.max_len && (key < n || a.clean)) a.out[b * a.out_stride + key] = res[u];
     }
-    if (a.page_max) {  // max over each group of 8 consecutive keys (lanes 8k..8k+7)
-      float m = result;
-      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
-      if ((threadIdx.x & 7) == 0 && j < a.max_len) a.page_max[b * a.page_stride + j / 8] = m;
-    }
-    if (j < a.max_len && a.out && (j < n || a.clean)) a.out[b * a.out_stride + j] = result;
+    if (a.page_max) {  // max over each group of 8 consecutive keys: loads u, u+1 of the four key lanes
 #pragma unroll
-    for (int c = 0; c < 8; ++c) cur[c] = nxt[c];
+      for (int u = 0; u < kKeyLoads; u += 2) {
+        float m = fmaxf(res[u], res[u + 1]);
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
+        const int64_t first = k0 + u * 4;
+        if (lane == 0 && first < a.max_len) a.page_max[b * a.page_stride + first / 8] = m;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kKeyLoads; ++u) cur[u] = nxt[u];
     cur_scale = nxt_scale;
+  }
+  // blocks past the row's length: -inf logits (clean) and page maxima only
+  if ((a.out && a.clean) || a.page_max) {
+    const int64_t nblk = (a.max_len + kWarpKeys - 1) / kWarpKeys;
+    for (; blk < nblk; blk += wstep) {
+      const int64_t key = blk * kWarpKeys + lane;
+      if (a.out && a.clean && key < a.max_len) a.out[b * a.out_stride + key] = -CUDART_INF_F;
+      const int64_t first = blk * kWarpKeys + lane * 8;
+      if (a.page_max && lane < kWarpKeys / 8 && first < a.max_len)
+        a.page_max[b * a.page_stride + first / 8] = -CUDART_INF_F;
+    }
   }
 }
 
@@ -152,7 +215,7 @@ int score_dispatch(const uint8_t* q, const float* w, const uint8_t* pool, int64_
   }
   ScoreArgs a{q, w, pool, lens, table, table_stride, out, out_stride, max_len, page_max, page_stride,
               static_cast<int>(heads), relu, clean, lens_kind};
-  const int64_t blocks = (max_len + kScoreThreads - 1) / kScoreThreads;
+  const int64_t blocks = (max_len + kScoreThreads - 1) / kScoreThreads;  // 128 keys per CTA iteration
   const dim3 grid(static_cast<unsigned>(batch), static_cast<unsigned>(blocks < 8 ? blocks : 8));
   if (heads == 1) launch_kernel(score_simt_kernel<1>, grid, dim3(kScoreThreads), 0, as_stream(stream), a);
   else launch_kernel(score_simt_kernel<0>, grid, dim3(kScoreThreads), 0, as_stream(stream), a);

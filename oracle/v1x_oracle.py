@@ -624,10 +624,11 @@ def score_row(q_u8, w, keys, scales, relu=True, exact=True):
     Formula: DS/kernels.py:310-313 (fine), :210-213 (coarse), pinned against
     DeepGEMM at experiments/fine_pool_shared_20261021/test_and_bench.py:37-41.
     exact=True fixes the fp32 evaluation order the SIMT CUDA scorer uses:
-    per head, d = 0..127 accumulated in fp32 (every e4m3 x e4m3 product is
-    exact in fp32); relu(x) = x if x > 0 else +0; then heads 0..H-1
-    accumulated as acc += w[h] * relu(dot) with separately rounded multiply
-    and add; then one multiply by the scale.
+    per head, eight partial sums p_g over dims 16g..16g+15, each accumulated
+    in fp32 from 0 in dim order (every e4m3 x e4m3 product is exact in fp32),
+    combined as ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7)); relu(x) = x if x > 0
+    else +0; then heads 0..H-1 accumulated as acc += w[h] * relu(dot) with
+    separately rounded multiply and add; then one multiply by the scale.
     exact=False uses a float64 BLAS product (for large cases / timing).
     """
     q = e4m3_to_f32(np.asarray(q_u8, np.uint8)).reshape(-1, 128)
@@ -638,9 +639,14 @@ def score_row(q_u8, w, keys, scales, relu=True, exact=True):
         if relu:
             d = np.maximum(d, 0)
         return ((d @ w.astype(np.float64)) * scales).astype(np.float32)
-    dot = np.zeros((H, keys.shape[0]), np.float32)
-    for d in range(128):
-        dot = dot + q[:, d:d + 1] * keys[None, :, d]
+    qp = q.reshape(H, 1, 8, 16)
+    kp = np.asarray(keys, np.float32).reshape(1, -1, 8, 16)
+    p = np.zeros((H, keys.shape[0], 8), np.float32)
+    for d in range(16):
+        p = p + qp[..., d] * kp[..., d]
+    p = p[..., 0::2] + p[..., 1::2]
+    p = p[..., 0::2] + p[..., 1::2]
+    dot = p[..., 0] + p[..., 1]
     if relu:
         dot = np.where(dot > 0, dot, np.float32(0)).astype(np.float32)
     acc = np.zeros(keys.shape[0], np.float32)
