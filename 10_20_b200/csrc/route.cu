@@ -18,7 +18,7 @@ namespace {
 constexpr int kRouteThreads = 256;
 constexpr int kRouteWarps = kRouteThreads / 32;
 constexpr int kRouteMaxItems = 4096;
-constexpr int kRoutePer = kRouteMaxItems / kRouteThreads;  // page keys per thread
+constexpr int kRouteSmallItems = 512;  // tables up to this many padded slots take 2 keys per thread
 constexpr int kRankDirect = 256;  // winner lists up to this size are ordered by counting
 
 struct RouteArgs {
@@ -40,15 +40,17 @@ struct RouteArgs {
   int stage_rt;       // the row's rt entries are copied to shared memory up front
 };
 
+// Shared memory: this fixed head, then (dynamic, sized by the launch) the winner
+// list of n_items composites (key << 32) | ~rank and, with stage_rt, the row's
+// reordered-page table.
 struct RouteSmem {
-  unsigned long long list[kRouteMaxItems];  // winners as (key << 32) | ~rank
-  int rt[kRouteMaxItems];                   // the row's reordered-page table (stage_rt)
   int hist[kBins];
   int4 red[2 * kRouteWarps];
   int warp_tot[kRouteWarps + 1];
   int4 res;
   int count;
 };
+constexpr size_t kRouteListOff = (sizeof(RouteSmem) + 15) & ~size_t(15);
 
 __device__ __forceinline__ void store_sel(const RouteArgs& a, int64_t i, int64_t v) {
   if (a.sel64) static_cast<int64_t*>(a.selected)[i] = v;
@@ -68,16 +70,20 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
 }
 
 // kPages: `scores` already holds one value per page (the max of its 8 centres).
+// kPer: page keys per thread (n_items <= kPer * kRouteThreads); small tables
+// take kPer = 2, which fits four CTAs per SM.
 //
 // Thread t owns pages p = t + j*256 (coalesced loads); the tie order of a page
 // is its blocked rank, computed from p.  The want-th largest key comes from the
 // bitwise search; the winners (keys above it and all keys equal to it) are then
 // ordered by (key desc, rank asc) by counting, or by a bitonic sort when ties
 // make the list long.
-template <bool kPages>
-__global__ void __launch_bounds__(kRouteThreads, 1) route_kernel(const __grid_constant__ RouteArgs a) {
+template <bool kPages, int kPer>
+__global__ void __launch_bounds__(kRouteThreads, kPer <= 2 ? 4 : 1) route_kernel(const __grid_constant__ RouteArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   RouteSmem& sm = *reinterpret_cast<RouteSmem*>(smem_raw);
+  unsigned long long* list = reinterpret_cast<unsigned long long*>(smem_raw + kRouteListOff);
+  int* srt = reinterpret_cast<int*>(list + a.n_items);
   const int tid = threadIdx.x, nt = kRouteThreads;
   const int64_t row = blockIdx.x;
   const int n = a.lens[row];
@@ -85,9 +91,9 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_kernel(const __grid_co
   const int32_t* rtrow = a.rt + row * a.pages;
   if (a.stage_rt) {  // the row's reordered-page table, copied while the keys are selected
     if ((reinterpret_cast<uintptr_t>(rtrow) & 15) == 0 && (a.pages & 3) == 0) {
-      for (int v = tid; v < (a.pages >> 2); v += nt) cp_async16(sm.rt + 4 * v, rtrow + 4 * v);
+      for (int v = tid; v < (a.pages >> 2); v += nt) cp_async16(srt + 4 * v, rtrow + 4 * v);
     } else {
-      for (int v = tid; v < a.pages; v += nt) cp_async4(sm.rt + v, rtrow + v);
+      for (int v = tid; v < a.pages; v += nt) cp_async4(srt + v, rtrow + v);
     }
   }
   asm volatile("cp.async.commit_group;" ::: "memory");
@@ -114,10 +120,10 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_kernel(const __grid_co
   // ---- page keys (VQ:26-41): p < act -> key of the page's max centre, else -inf
   const int act = static_cast<int>(min(static_cast<int64_t>(active), kPages ? a.score_cols : a.score_cols / 8));
   const float* srow = a.scores + row * a.score_stride;
-  uint32_t kr[kRoutePer];
-  float x[kRoutePer];
+  uint32_t kr[kPer];
+  float x[kPer];
 #pragma unroll
-  for (int j = 0; j < kRoutePer; ++j) {
+  for (int j = 0; j < kPer; ++j) {
     const int p = tid + j * nt;
     x[j] = -CUDART_INF_F;
     if (p < act) {
@@ -139,14 +145,14 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_kernel(const __grid_co
   }
   const int nv = a.n_items > tid ? (a.n_items - tid + nt - 1) / nt : 0;  // pages of this thread
 #pragma unroll
-  for (int j = 0; j < kRoutePer; ++j) kr[j] = order_key(x[j]);
+  for (int j = 0; j < kPer; ++j) kr[j] = order_key(x[j]);
   // ---- winners: a 12-bit histogram finds the bin of the want-th key; every key
   // in that bin or above is a winner candidate.  When ties make that list long,
   // the exact want-th key from the bitwise search bounds it instead.
   zero_hist<kRouteThreads>(sm.hist);
   __syncthreads();
 #pragma unroll
-  for (int j = 0; j < kRoutePer; ++j)
+  for (int j = 0; j < kPer; ++j)
     if (j < nv) atomicAdd(&sm.hist[bin_of(kr[j])], 1);
   __syncthreads();
   const TopBin tb = find_top_bin<kRouteThreads>(want, sm.hist, sm.warp_tot, &sm.res);
@@ -158,7 +164,7 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_kernel(const __grid_co
         [&](uint32_t c1, uint32_t c2, uint32_t c3, int& n1, int& n2, int& n3) {
           n1 = n2 = n3 = 0;
 #pragma unroll
-          for (int j = 0; j < kRoutePer; ++j) {
+          for (int j = 0; j < kPer; ++j) {
             if (j < nv) {
               n1 += kr[j] >= c1;
               n2 += kr[j] >= c2;
@@ -169,12 +175,12 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_kernel(const __grid_co
         sm.red, &gt);
   }
 #pragma unroll
-  for (int j = 0; j < kRoutePer; ++j) {
+  for (int j = 0; j < kPer; ++j) {
     if (j < nv && kr[j] >= lo) {
       const int p = tid + j * nt;
       const uint32_t rank = static_cast<uint32_t>((p & 127) * a.base + (p >> 7));
       const int e = atomicAdd(&sm.count, 1);
-      sm.list[e] = (static_cast<unsigned long long>(kr[j]) << 32) | (0xFFFFFFFFu - rank);
+      list[e] = (static_cast<unsigned long long>(kr[j]) << 32) | (0xFFFFFFFFu - rank);
     }
   }
   if (a.stage_rt) asm volatile("cp.async.wait_all;" ::: "memory");
@@ -185,22 +191,22 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_kernel(const __grid_co
     const int p = r / a.base + (r % a.base) * 128;
     if (pos < a.take_stride) store_sel(a, row * a.take_stride + pos, p);
     if (a.fill_table && pos < take && pos < a.fine_pages)
-      a.ft[row * a.fine_pages + pos] = p < a.pages ? (a.stage_rt ? sm.rt[p] : rtrow[p]) : -1;
+      a.ft[row * a.fine_pages + pos] = p < a.pages ? (a.stage_rt ? srt[p] : rtrow[p]) : -1;
   };
   if (m <= kRankDirect) {
     // composites are unique: a winner's position is the number of larger ones
     for (int e = tid; e < m; e += nt) {
-      const unsigned long long c = sm.list[e];
+      const unsigned long long c = list[e];
       int pos = 0;
-      for (int f = 0; f < m; ++f) pos += sm.list[f] > c;
+      for (int f = 0; f < m; ++f) pos += list[f] > c;
       if (pos < want) emit(pos, c);
     }
   } else {
     int mp = 1;
     while (mp < m) mp <<= 1;
-    for (int i = m + tid; i < mp; i += nt) sm.list[i] = 0ull;
-    bitonic_sort_desc(sm.list, mp);
-    for (int i = tid; i < want; i += nt) emit(i, sm.list[i]);
+    for (int i = m + tid; i < mp; i += nt) list[i] = 0ull;
+    bitonic_sort_desc(list, mp);
+    for (int i = tid; i < want; i += nt) emit(i, list[i]);
   }
 }
 
@@ -225,14 +231,24 @@ int route_launch(bool pages_in, const float* scores, int64_t score_stride, int64
               take_stride, static_cast<int>(pages), rt, ft, fine_pages, tail_rows, capacity,
               fill_table, n_items, n_items / 128,
               fill_table && pages <= kRouteMaxItems ? 1 : 0};
-  const size_t smem = sizeof(RouteSmem);
+  const size_t smem = kRouteListOff + static_cast<size_t>(n_items) * 8 + (a.stage_rt ? static_cast<size_t>(pages) * 4 : 0);
   static DeviceOnce once;
   if (once.first()) {
-    cudaFuncSetAttribute(route_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    cudaFuncSetAttribute(route_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const int most = static_cast<int>(kRouteListOff + kRouteMaxItems * 12);
+    cudaFuncSetAttribute(route_kernel<false, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
+    cudaFuncSetAttribute(route_kernel<true, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
+    cudaFuncSetAttribute(route_kernel<false, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
+    cudaFuncSetAttribute(route_kernel<true, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
   }
-  if (pages_in) launch_kernel(route_kernel<true>, dim3(static_cast<unsigned>(batch)), dim3(kRouteThreads), smem, as_stream(stream), a);
-  else launch_kernel(route_kernel<false>, dim3(static_cast<unsigned>(batch)), dim3(kRouteThreads), smem, as_stream(stream), a);
+  const dim3 grid(static_cast<unsigned>(batch)), block(kRouteThreads);
+  static_assert(kRouteSmallItems <= 2 * kRouteThreads && kRouteMaxItems <= 16 * kRouteThreads, "route slots per thread");
+  if (n_items <= kRouteSmallItems) {
+    if (pages_in) launch_kernel(route_kernel<true, 2>, grid, block, smem, as_stream(stream), a);
+    else launch_kernel(route_kernel<false, 2>, grid, block, smem, as_stream(stream), a);
+  } else {
+    if (pages_in) launch_kernel(route_kernel<true, 16>, grid, block, smem, as_stream(stream), a);
+    else launch_kernel(route_kernel<false, 16>, grid, block, smem, as_stream(stream), a);
+  }
   return launch_status(pages_in ? "v1x_route_pages" : "v1x_route");
 }
 }  // namespace
