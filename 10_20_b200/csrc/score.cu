@@ -17,6 +17,8 @@
 // rounded multiply and add, then one multiply by the key's scale.
 #include <cuda_fp8.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace v1x {
@@ -215,8 +217,13 @@ int score_dispatch(const uint8_t* q, const float* w, const uint8_t* pool, int64_
   }
   ScoreArgs a{q, w, pool, lens, table, table_stride, out, out_stride, max_len, page_max, page_stride,
               static_cast<int>(heads), relu, clean, lens_kind};
+  // CTAs per row: about one wave of resident CTAs over the batch (four per SM),
+  // at most one per 128 keys and 8 per row.  Fewer CTAs per row give each warp
+  // several blocks, so its next block's loads overlap the current evaluation.
   const int64_t blocks = (max_len + kScoreThreads - 1) / kScoreThreads;  // 128 keys per CTA iteration
-  const dim3 grid(static_cast<unsigned>(batch), static_cast<unsigned>(blocks < 8 ? blocks : 8));
+  const int64_t wave = static_cast<int64_t>(num_sms()) * 4;
+  const int64_t per_row = std::max<int64_t>(1, std::min<int64_t>({(wave + batch - 1) / batch, blocks, 8}));
+  const dim3 grid(static_cast<unsigned>(batch), static_cast<unsigned>(per_row));
   if (heads == 1) launch_kernel(score_simt_kernel<1>, grid, dim3(kScoreThreads), 0, as_stream(stream), a);
   else launch_kernel(score_simt_kernel<0>, grid, dim3(kScoreThreads), 0, as_stream(stream), a);
   return launch_status("v1x_score_fp8");
