@@ -21,6 +21,7 @@ V1X_ERR_CUDA = -2
 V1X_ERR_UNSUPPORTED = -3
 V1X_STATUS_ARENA_EXHAUSTED = 1
 V1X_STATUS_TIMEOUT = 2
+V1X_STATUS_BAD_PAGE = 3
 
 P = ctypes.c_void_p
 I64 = ctypes.c_int64
@@ -57,7 +58,16 @@ SIGNATURES = {
     "v1x_route_pages": [P, I64, P, P, P, I32, I64, I64, P, P, I64, P, I64, I32, I64, P],
     "v1x_gather_slots": [P, P, P, P, P, P, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64,
                          P],
+    "v1x_build_workspace_bytes": [I64],
+    "v1x_build_buckets": [P, I64, P, P, P, P, P, P, P, P, I64, P],
+    "v1x_initialize": [P, I64, P, P, P, P, P, P, P],
+    "v1x_group_init": [P, I32, P, P, P, P, I64, I64, I64, I64, P],
+    "v1x_group_dots": [P, P, P, P, P, I64, I64, I32, I64, I64, P],
+    "v1x_group_anchor": [P, P, P, P, I64, I32, I64, I64, P],
+    "v1x_assemble": [P, I64, P, P, P, P, P, P, P],
 }
+# entry points whose return type is not int
+RESTYPES = {"v1x_last_error": ctypes.c_char_p, "v1x_build_workspace_bytes": ctypes.c_int64}
 
 _lock = threading.Lock()
 _lib = None
@@ -79,7 +89,7 @@ def lib() -> ctypes.CDLL:
                 for name, args in SIGNATURES.items():
                     fn = getattr(h, name)
                     fn.argtypes = args
-                    fn.restype = ctypes.c_char_p if name == "v1x_last_error" else ctypes.c_int
+                    fn.restype = RESTYPES.get(name, ctypes.c_int)
                 _lib = h
     return _lib
 

@@ -11,11 +11,12 @@ selection step (optionally as a captured CUDA graph) and returns clones of the
 physical slot ids -- or of the x4 expanded logical positions when
 ``Config.expand_output`` -- plus the logical ids when ``return_logical``.
 
-One deliberate difference: building a bucket's reordered pages, members and
-centres from the native cache is the index build, outside this path.  The
-caller supplies it as ``bucket_source(owner, bucket) -> (tmp, mapping,
-centers)`` (see lifecycle.PageArena); ``prepare`` otherwise keeps the
-reference's signature and checks.
+``prepare`` builds every new bucket from the native cache through the
+request's native page table (Build.compute, :170-270): the index build of
+index_build.py for all new buckets of the call in one launch, then per bucket
+fingerprint / match / allocate / publish.  The optional ``bucket_source(owner,
+bucket) -> (tmp, mapping, centers)`` replaces the index build with supplied
+bucket contents (see lifecycle.PageArena).
 """
 from __future__ import annotations
 
@@ -24,6 +25,7 @@ import threading
 import torch
 
 from .config import Config
+from .index_build import BucketBuilder
 from .lifecycle import PageArena
 from .pipeline import SelectionStep
 from .synth import QueryCase
@@ -119,6 +121,7 @@ class Indexer:
         self.arena = PageArena(self.capacity, config.pages, self.device, max_requests=config.max_requests,
                                graphs=config.graphs, staging_rows=config.q_buckets[-1])
         self.bucket_source = bucket_source
+        self.builder = BucketBuilder(self.device, max(config.pages // 16, 1)) if bucket_source is None else None
         self.queries: dict[int, _Query] = {}
         self.lock = threading.RLock()
         self.closed = False
@@ -134,8 +137,6 @@ class Indexer:
             raise RuntimeError("V1 index subgraphs must execute outside full-model capture")
 
     def _source(self, owner, bucket):
-        if self.bucket_source is None:
-            raise RuntimeError("no bucket_source: building bucket indices is outside this path")
         return self.bucket_source(owner, bucket)
 
     def _prepare(self, owner, native_table, length):
@@ -144,7 +145,20 @@ class Indexer:
         if (native_table.dtype != torch.int32 or native_table.device != self.device or native_table.ndim != 1
                 or native_table.numel() < -(-length // 64) or not native_table.is_contiguous()):
             raise ValueError("Invalid compact native page table")
-        return self.arena.prepare(owner, length, self._source)
+        if self.bucket_source is not None:
+            return self.arena.prepare(owner, length, self._source)
+        built = {}
+
+        def batch(_owner, buckets):
+            # consecutive new buckets: their native pages are one slice of the table
+            b0, n = buckets[0], len(buckets)
+            source = native_table[b0 * 16:(b0 + n) * 16].view(n, 16)
+            tmp, centers, mapping, _ = self.builder.build(self.native, source, [b * 1024 for b in buckets],
+                                                          self.arena.status)
+            for i, b in enumerate(buckets):
+                built[b] = (tmp[i], mapping[i], centers[i])
+
+        return self.arena.prepare(owner, length, lambda _o, b: built[b], batch=batch)
 
     @torch.inference_mode()
     def prepare(self, owner, native_table, length):

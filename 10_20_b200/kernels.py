@@ -7,7 +7,7 @@ ignored.  Every launch goes to a hand-written sm_100a kernel in libv1x.so on
 the current CUDA stream.
 
 Ops (reference sglang/srt/layers/attention/v1_deepseek/kernels.py):
-  fingerprint :57-69, match_pages :72-113, allocate :116-131, publish :134-167,
+  initialize :9-29, assemble :32-54, fingerprint :57-69, match_pages :72-113, allocate :116-131, publish :134-167,
   release :170-179, query_lengths :224-245, output_ids :323-376,
   mask_fine :444-472, reduce_centers :475-486, fine_table_shared :488-514,
   stage_tail_shared :518-564, query_metadata :568-591, expand_logical :594-600;
@@ -94,6 +94,39 @@ def _s(t):
 def _sel64(sel):
     require(sel.dtype in (torch.int32, torch.int64), "SELECTED: int32 or int64 required")
     return 1 if sel.dtype == torch.int64 else 0
+
+
+# ---------------------------------------------------------------------------
+# index build of one bucket (the fused many-bucket form is index_build.py)
+# ---------------------------------------------------------------------------
+
+def _native_pages(K):
+    require(K.dtype in (torch.uint8, torch.float8_e4m3fn) and K.is_contiguous() and K.numel() % 8448 == 0,
+            "K: contiguous packed native pool (uint8 / float8 view, 8448 bytes per page)")
+    return K.numel() // 8448
+
+
+@_op
+def initialize(grid, K, KS, TABLE, META, UNIT, PERM, FLAG):
+    """Dequantise + normalise the bucket's 1024 keys (DS/kernels.py:9-29).
+    K / KS: the native pool's FP8 and float32 views; UNIT f32 [1024, 128];
+    PERM i32 [1024]; FLAG i32 (-1 when META[2] is set).  grid = (64,)."""
+    require(UNIT.dtype == torch.float32 and UNIT.numel() >= 1024 * 128, "UNIT: float32 [1024, 128]")
+    require(PERM.dtype == torch.int32 and FLAG.dtype == torch.int32 and TABLE.dtype == torch.int32,
+            "initialize: PERM/FLAG/TABLE int32")
+    _lib.call("v1x_initialize", ptr(K), _native_pages(K), ptr(TABLE), ptr(META), ptr(UNIT), ptr(PERM),
+              ptr(FLAG), ptr(status_word(K.device)), _s(K), device=K.device)
+
+
+@_op
+def assemble(grid, K, KS, TABLE, META, IDS, TMP, TMPS, CENTERS, CS, MAP):
+    """Reordered tmp pages, centres and logical members (DS/kernels.py:32-54).
+    TMP/TMPS and CENTERS/CS are FP8 and float32 views of [16, 8448] and
+    [2, 8448] byte buffers.  grid = (16, 8)."""
+    require(IDS.dtype == torch.int32 and MAP.dtype == torch.int32, "assemble: IDS/MAP int32")
+    require(TMP.numel() >= 16 * 8448 and CENTERS.numel() >= 2 * 8448, "assemble: TMP [16, 8448], CENTERS [2, 8448]")
+    _lib.call("v1x_assemble", ptr(K), _native_pages(K), ptr(TABLE), ptr(META), ptr(IDS), ptr(TMP), ptr(CENTERS),
+              ptr(MAP), _s(K), device=K.device)
 
 
 # ---------------------------------------------------------------------------

@@ -13,12 +13,14 @@ Mirrors the page part of the reference's ``Indexer``
   Build.compute    :230-270   per bucket: fingerprint -> match_pages ->
                               allocate -> publish
 
-One bucket is 1024 tokens = 16 pages of 64.  The reference builds a bucket's
-reordered pages, members and centres from the native cache (``assemble`` and
-the grouping sort, the index build, which is outside this path); here the
-caller supplies them through ``bucket_source(owner, bucket) -> (tmp, mapping,
+One bucket is 1024 tokens = 16 pages of 64.  A bucket's reordered pages,
+members and centres come from ``bucket_source(owner, bucket) -> (tmp, mapping,
 centers)``: tmp uint8 [16, 8448] packed pages, mapping int32 [16, 64] logical
-token positions, centers uint8 [2, 8448] the bucket's 128 packed centres.
+token positions, centers uint8 [2, 8448] the bucket's 128 packed centres.  The
+Indexer's source is the index build of index_build.py over the native cache
+(Build.compute's initialize / grouping / assemble); ``batch(owner, buckets)``,
+when given, is called once with all new buckets of a prepare first, so that
+source can build them in one launch.
 
 With ``graphs=True`` (the reference's ``Config.graphs``) the four kernels of a
 bucket run as one captured CUDA graph over fixed input buffers, as the
@@ -117,7 +119,7 @@ class PageArena:
         self._graph.replay()
 
     # -- requests ---------------------------------------------------------------
-    def prepare(self, owner, length: int, bucket_source):
+    def prepare(self, owner, length: int, bucket_source, batch=None):
         """Index every newly complete bucket of `owner` up to `length` tokens
         (reference Indexer._prepare, DS/runtime.py:806-825)."""
         if not 0 <= length <= self.pages * 64:
@@ -131,7 +133,13 @@ class PageArena:
                 raise ValueError("V1 request capacity exceeded")
             state = self.states[owner] = State(self.pages, self.device)
         complete = length // 1024
-        for bucket in range(len(state.leases), complete):
+        new = range(len(state.leases), complete)
+        # the buckets that will get a lease (the loop raises at the first one
+        # that does not, as the reference does, keeping those already built)
+        ready = list(new)[:len(self.free_leases)]
+        if batch is not None and ready:
+            batch(owner, ready)
+        for bucket in new:
             if not self.free_leases:
                 raise RuntimeError("V1 bucket records exhausted")
             lease = self.free_leases.pop()

@@ -50,6 +50,7 @@ extern "C" {
 #define V1X_STATUS_OK 0
 #define V1X_STATUS_ARENA_EXHAUSTED 1 /* allocate: free stack smaller than needed */
 #define V1X_STATUS_TIMEOUT 2         /* a bounded device-side wait gave up          */
+#define V1X_STATUS_BAD_PAGE 3        /* build: a source page id outside the native pool */
 
 /* Library identity: returns 0x010000 * major + 0x100 * minor + patch. */
 V1X_API int v1x_version(void);
@@ -129,6 +130,62 @@ V1X_API int v1x_group_offsets(const float* S, int32_t* offsets, int64_t N, int64
 V1X_API int v1x_sort_segments_grouped(const int32_t* P, int32_t* O, const float* S, const int32_t* flag,
                       int32_t* offsets, int64_t N, int64_t groups, int64_t heads, int64_t key_range,
                       void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Index build of 1024-token buckets -- replaces Build.compute's first stages
+ * (DS/runtime.py:170-233): initialize (DS/kernels.py:9-29), the seven grouping
+ * levels of _dots / _anchor / _sort (NA/fused_grouping.py:39-76) and assemble
+ * (DS/kernels.py:32-54).  Native pool: u8 [native_pages, 8448] packed pages; a
+ * source page id outside [0, native_pages) reads as zeros and writes
+ * V1X_STATUS_BAD_PAGE to *status (may be NULL). */
+
+/* Workspace bytes v1x_build_buckets needs for `buckets` buckets. */
+V1X_API int64_t v1x_build_workspace_bytes(int64_t buckets);
+
+/* Whole build of `buckets` buckets in one launch (one 8-CTA cluster each): the
+ * 44 launches of the reference's per-bucket sequence.  source i32 [buckets, 16]
+ * (native page of each bucket page), starts i32 [buckets] (the bucket's first
+ * logical token) -> tmp u8 [buckets, 16, 8448], centers u8 [buckets, 2, 8448],
+ * mapping i32 [buckets, 16, 64] (Build.tmp / .centers / .mapping), perm i32
+ * [buckets, 1024] (the final member order, Build.perm[current]; may be NULL).
+ * work: v1x_build_workspace_bytes(buckets) bytes, 16-byte aligned; native and
+ * tmp 16-byte aligned. */
+V1X_API int v1x_build_buckets(const uint8_t* native, int64_t native_pages, const int32_t* source,
+                      const int32_t* starts, uint8_t* tmp, uint8_t* centers, int32_t* mapping,
+                      int32_t* perm, void* work, int32_t* status, int64_t buckets, void* stream);
+
+/* DS/kernels.py:9-29 (initialize, grid (64,)).  table i32 [16], meta i32 [3]
+ * {start, lease, active} -> unit f32 [1024, 128], perm i32 [1024], flag i32
+ * (-1 when active, else 0). */
+V1X_API int v1x_initialize(const uint8_t* native, int64_t native_pages, const int32_t* table,
+                   const int32_t* meta, float* unit, int32_t* perm, int32_t* flag, int32_t* status,
+                   void* stream);
+
+/* NA/fused_grouping.py:27-37 (_init, grid (256, heads)).  k: [slots, heads, 128]
+ * bf16 (k_is_f32 = 0) or f32 with element strides ks0, ks1; req i32 slot map ->
+ * u f32 [heads, 4096, 128], p i32 [heads, 4096] = start + i.  No-op unless *flag < 0. */
+V1X_API int v1x_group_init(const void* k, int k_is_f32, const int32_t* req, float* u, int32_t* p,
+                   const int32_t* flag, int64_t start, int64_t ks0, int64_t ks1, int64_t heads,
+                   void* stream);
+
+/* NA/fused_grouping.py:39-54 (_dots, grid (count/16, heads)).  u f32 [heads, 4096,
+ * 128] (heads = 1: [count, 128]), p i32 and s f32 [heads, 4096], anchor i32
+ * [heads, 256, 2]; count positions per head (a multiple of 4 and of n). */
+V1X_API int v1x_group_dots(const float* u, const int32_t* p, const int32_t* anchor, float* s,
+                   const int32_t* flag, int64_t n, int64_t start, int mode, int64_t count,
+                   int64_t heads, void* stream);
+
+/* NA/fused_grouping.py:56-63 (_anchor, grid (count/n, heads)): the leftmost
+ * minimum of each group of n -> anchor[h, group, slot] = p[...]. */
+V1X_API int v1x_group_anchor(const int32_t* p, int32_t* anchor, const float* s, const int32_t* flag,
+                     int64_t n, int slot, int64_t count, int64_t heads, void* stream);
+
+/* DS/kernels.py:32-54 (assemble, grid (16, 8)).  table i32 [16], meta i32 [3],
+ * ids i32 [1024] (the member order) -> tmp u8 [16, 8448], centers u8 [2, 8448],
+ * mapping i32 [16, 64]. */
+V1X_API int v1x_assemble(const uint8_t* native, int64_t native_pages, const int32_t* table,
+                 const int32_t* meta, const int32_t* ids, uint8_t* tmp, uint8_t* centers,
+                 int32_t* mapping, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Page lifecycle -- replace DS/kernels.py:57-179.  meta i32[3] =

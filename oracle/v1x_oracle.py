@@ -497,6 +497,196 @@ def sort_segments(P, S, flag, N, groups, heads, O=None):
     return O
 
 
+# --------------------------------------------------------------------------
+# index build of one 1024-token bucket: initialize -> grouping -> assemble
+# (DS/runtime.py:170-233, Build.compute's first three stages)
+# --------------------------------------------------------------------------
+BUILD_LEVELS = (1024, 512, 256, 128, 64, 32, 16)
+
+
+def sum128(p):
+    """tl.sum over a last axis of 128 float32 values as the Triton interpreter
+    evaluates it (np.sum, numpy's pairwise float32 summation for n = 128):
+    eight strided accumulators r_j = p[j] + p[8+j] + ... + p[120+j] in that
+    order, then ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7))."""
+    p = np.asarray(p, np.float32)
+    r = p[..., 0:8].copy()
+    for i in range(1, 16):
+        r = r + p[..., 8 * i:8 * i + 8]
+    return ((r[..., 0] + r[..., 1]) + (r[..., 2] + r[..., 3])) + ((r[..., 4] + r[..., 5]) + (r[..., 6] + r[..., 7]))
+
+
+_E4M3_POS = E4M3[:0x7F].astype(np.float64)   # codes 0x00..0x7E: 0 .. 448 ascending
+
+
+def e4m3_from_f32(x):
+    """float32 -> OCP e4m3fn bytes: round to nearest, ties to the even code,
+    saturating at +-448 (the conversion `.to(float8e4nv)` of values that
+    already lie within +-448); -0 -> 0x80, NaN -> 0x7F."""
+    x = np.asarray(x, np.float32)
+    a = np.minimum(np.abs(x).astype(np.float64), 448.0)
+    hi = np.clip(np.searchsorted(_E4M3_POS, a, side="left"), 0, 126)
+    lo = np.clip(hi - 1, 0, 126)
+    dhi, dlo = _E4M3_POS[hi] - a, a - _E4M3_POS[lo]
+    code = np.where(dlo < dhi, lo, np.where(dhi < dlo, hi, np.where(lo % 2 == 0, lo, hi)))
+    code = np.where(_E4M3_POS[hi] == a, hi, code).astype(np.uint8)
+    code = code | (np.signbit(x).astype(np.uint8) << 7)
+    return np.where(np.isnan(x), np.uint8(0x7F), code).astype(np.uint8)
+
+
+def pow2_ceil(v):
+    """Smallest power of two >= v (v > 0, float32), exactly.  The reference
+    writes exp2(ceil(log2(v))) (DS/kernels.py:48-50); with a correctly rounded
+    log2 the two agree except for v a few ulps above a power of two, where the
+    floating-point log2 rounds down onto the integer."""
+    v = np.asarray(v, np.float32)
+    bits = v.view(np.uint32)
+    exact = (bits & 0x007FFFFF) == 0
+    up = ((bits >> 23) + 1).astype(np.uint32) << 23
+    return np.where(exact, v, up.view(np.float32)).astype(np.float32)
+
+
+def build_initialize(native_u8, table):
+    """DS/kernels.py:9-29 (initialize).  Token i in [0, 1024) of the bucket:
+    page = TABLE[i // 64]; x = e4m3(K[page, i % 64]) * scale (fp32 multiply);
+    unit = x / max(sqrt(sum(x*x)), 1e-12).  Returns (unit f32 [1024, 128],
+    perm i32 [1024] = 0..1023).  FLAG = -1 when active (:12-13)."""
+    native_u8 = np.asarray(native_u8, np.uint8).reshape(-1, PAGE_BYTES)
+    table = np.asarray(table, np.int64).reshape(-1)
+    i = np.arange(1024)
+    page = table[i // 64]
+    kb = native_u8[page[:, None], (i % 64)[:, None] * 128 + np.arange(128)[None, :]]
+    scale = native_u8.view(np.float32).reshape(-1, PAGE_WORDS)[page, SCALE_WORD + i % 64]
+    x = (e4m3_to_f32(kb) * scale[:, None].astype(np.float32)).astype(np.float32)
+    norm = np.sqrt(sum128(x * x)).astype(np.float32)
+    unit = (x / np.maximum(norm, np.float32(1e-12))[:, None]).astype(np.float32)
+    return unit, i.astype(np.int32)
+
+
+def group_init(k_f32, req, start, heads):
+    """NA/fused_grouping.py:27-37 (_init): for the 4096 positions i of head h,
+    x = float(K[REQ[START + i], h]) and U[h, i] = x / max(sqrt(sum(x*x)), 1e-12);
+    P[h, i] = START + i.  k_f32: [slots, heads, 128] float32 values of K."""
+    k = np.asarray(k_f32, np.float32)
+    slots = np.asarray(req, np.int64)[start:start + 4096]
+    x = np.transpose(k[slots], (1, 0, 2))           # [heads, 4096, 128]
+    norm = np.sqrt(sum128(x * x)).astype(np.float32)
+    unit = (x / np.maximum(norm, np.float32(1e-12))[..., None]).astype(np.float32)
+    P = np.tile(np.arange(4096, dtype=np.int32) + np.int32(start), (heads, 1))
+    return unit, P
+
+
+def group_levels(unit, P, start, levels, count, heads):
+    """The level loop of FusedGroups.run / Build.compute over `count` positions
+    per head (NA/fused_grouping.py:103-111): three _dots, two _anchor and one
+    _sort per level n."""
+    P = np.asarray(P, np.int32).reshape(-1).copy()
+    A = np.zeros(heads * 512, np.int32)
+    S = np.zeros(heads * 4096 if heads > 1 else count, np.float32)
+    for n in levels:
+        for mode in (0, 1, 2):
+            S = group_dots(unit, P, A, S, n, start, mode, count=count, heads=heads)
+            if mode < 2:
+                A = group_anchor(P, A, S, n, mode, count=count, heads=heads)
+        P = sort_segments(P, S, -1, n, count // n, heads, O=np.zeros_like(P))
+    return P
+
+
+def group_dots(unit, P, A, S, N, start, mode, count=1024, heads=1):
+    """NA/fused_grouping.py:39-54 (_dots).  Position i of head h (flat index
+    h*4096 + i, i < count): ids = P[.] - START; the anchor is the group's first
+    member P[h*4096 + (i//N)*N] (MODE 0) or A[h*256 + i//N, MODE-1] (MODE 1, 2),
+    minus START; value = sum(U[h, ids] * U[h, anchor]); MODE 2 subtracts the
+    previous S.  U rows are [heads, stride, 128] with stride = 4096 for heads > 1
+    (the 4K FusedGroups layout) and the compact bucket otherwise."""
+    P = np.asarray(P, np.int64).reshape(-1)
+    A = np.asarray(A, np.int64).reshape(-1)
+    S = np.array(S, np.float32, copy=True).reshape(-1)
+    U = np.asarray(unit, np.float32).reshape(heads, -1, 128)
+    i = np.arange(count)
+    for h in range(heads):
+        f = h * 4096 + i
+        ids = P[f] - start
+        if mode == 0:
+            anc = P[h * 4096 + (i // N) * N] - start
+        else:
+            anc = A[(h * 256 + i // N) * 2 + (mode - 1)] - start
+        value = sum128(U[h, ids] * U[h, anc])
+        S[f] = (value - S[f]).astype(np.float32) if mode == 2 else value
+    return S
+
+
+def group_anchor(P, A, S, N, slot, count=1024, heads=1):
+    """NA/fused_grouping.py:56-63 (_anchor): for every group of N positions the
+    position of the minimum score, leftmost on ties -> A[h*256+group, SLOT] =
+    P[...+pos]."""
+    P = np.asarray(P, np.int32).reshape(-1)
+    S = np.asarray(S, np.float32).reshape(-1)
+    A = np.array(A, np.int32, copy=True).reshape(-1)
+    for h in range(heads):
+        for g in range(count // N):
+            b = h * 4096 + g * N
+            A[(h * 256 + g) * 2 + slot] = P[b + int(np.argmin(S[b:b + N]))]
+    return A
+
+
+def group_bucket(unit, start=0, levels=BUILD_LEVELS):
+    """The grouping loop of Build.compute (DS/runtime.py:183-215): for each
+    level n, per group of n positions: MODE 0 dots against the first member,
+    the farthest member b (anchor slot 0), MODE 1 dots against b, the farthest
+    member a from b (slot 1), MODE 2 margin = dot(x, a) - dot(x, b), then the
+    stable descending sort of the margins; the next level halves the groups.
+    Returns the final member permutation (int32 [1024], offset by START)."""
+    P = np.arange(1024, dtype=np.int32) + start
+    A = np.zeros(2 * 256, np.int32)
+    S = np.zeros(1024, np.float32)
+    for n in levels:
+        for mode in (0, 1, 2):
+            S = group_dots(unit, P, A, S, n, start, mode)
+            if mode < 2:
+                A = group_anchor(P, A, S, n, mode)
+        P = sort_segments(P, S, -1, n, 1024 // n, 1, O=np.zeros_like(P))
+    return P
+
+
+def build_assemble(native_u8, table, start, ids):
+    """DS/kernels.py:32-54 (assemble), 16 pages x 8 groups of 8 members.
+    Member i of page p: src = IDS[p*64 + i]; its K bytes and scale (native page
+    TABLE[src // 64], row src % 64) are copied to TMP[p, i]; MAP[p, i] = START +
+    src.  Each group's centre: mean = (sum over the 8 members, in order, of
+    e4m3(K) * scale) / 8; cs = pow2_ceil(max(max|mean|, 1e-4) / 448); centre c =
+    p*8 + g is written as e4m3(mean / cs) at CENTERS[c // 64, c % 64] with scale
+    cs.  Returns (tmp u8 [16, 8448], centers u8 [2, 8448], mapping i32 [16, 64])."""
+    native_u8 = np.asarray(native_u8, np.uint8).reshape(-1, PAGE_BYTES)
+    table = np.asarray(table, np.int64).reshape(-1)
+    src = np.asarray(ids, np.int64).reshape(16, 64)
+    page = table[src // 64]
+    kb = native_u8[page[..., None], (src % 64)[..., None] * 128 + np.arange(128)]
+    scale = native_u8.view(np.float32).reshape(-1, PAGE_WORDS)[page, SCALE_WORD + src % 64]
+    tmp = np.zeros((16, PAGE_BYTES), np.uint8)
+    tmp[:, :K_BYTES] = kb.reshape(16, K_BYTES)
+    tmp.view(np.float32)[:, SCALE_WORD:] = scale
+    mapping = (start + src).astype(np.int32)
+    x = (e4m3_to_f32(kb) * scale[..., None].astype(np.float32)).astype(np.float32).reshape(16, 8, 8, 128)
+    acc = x[:, :, 0].copy()
+    for j in range(1, 8):
+        acc = acc + x[:, :, j]
+    mean = (acc / np.float32(8.0)).astype(np.float32).reshape(128, 128)
+    vmax = np.maximum(np.abs(mean).max(-1), np.float32(1e-4)).astype(np.float32)
+    cs = pow2_ceil((vmax / np.float32(448.0)).astype(np.float32))
+    centers = np.zeros((2, PAGE_BYTES), np.uint8)
+    centers[:, :K_BYTES] = e4m3_from_f32(mean / cs[:, None]).reshape(2, K_BYTES)
+    centers.view(np.float32)[:, SCALE_WORD:] = cs.reshape(2, 64)
+    return tmp, centers, mapping
+
+
+def build_bucket(native_u8, table, start):
+    """initialize -> grouping -> assemble of one bucket (DS/runtime.py:170-233)."""
+    unit, _ = build_initialize(native_u8, table)
+    perm = group_bucket(unit)
+    return build_assemble(native_u8, table, start, perm)
+
+
 def group_offsets(keys_sorted_desc: np.ndarray, key_range: int) -> np.ndarray:
     """Exclusive descending-key offsets of one sorted segment (an extension:
     the reference emits only the permutation).  offs[j] = number of records

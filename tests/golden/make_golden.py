@@ -449,6 +449,60 @@ def gen_route_topk_example():
          physical_sorted=expected_physical.sort(1).values, candidate_ids=candidate_ids)
 
 
+def gen_build(dk, fg):
+    """Index build of one bucket (DS/runtime.py:170-233 Build.compute's
+    initialize, grouping levels and assemble), run on the reference's kernels.
+    Bucket 0: random keys.  Bucket 1: duplicated tokens (exact dot ties), all-zero
+    tokens (unit vectors of zero) and one page of a single repeated token."""
+    gen = torch.Generator().manual_seed(11)
+    native = fp8_pages(gen, 40)
+    # adversarial pages 20..35: duplicates, zero tokens, a constant page
+    adv = native[20:36].clone()
+    kb = adv[:, :8192].view(16, 64, 128)
+    sc = adv.view(torch.float32)[:, 2048:]
+    for _ in range(120):
+        a, b = torch.randint(0, 16 * 64, (2,), generator=gen).tolist()
+        kb[b // 64, b % 64] = kb[a // 64, a % 64]
+        sc[b // 64, b % 64] = sc[a // 64, a % 64]
+    for t in torch.randint(0, 16 * 64, (40,), generator=gen).tolist():
+        kb[t // 64, t % 64] = 0
+    kb[5] = kb[5, 0]
+    sc[5] = sc[5, 0]
+    native[20:36] = adv
+    tables = torch.stack([torch.randperm(20, generator=gen)[:16], 20 + torch.randperm(16, generator=gen)]).int()
+    starts = torch.tensor([4096, 65536], dtype=torch.int32)
+    out = dict(native=native, tables=tables, starts=starts)
+    fp8 = native.view(torch.float8_e4m3fn)
+    f32 = native.view(torch.float32)
+    for b in range(2):
+        source = tables[b].clone()
+        meta = torch.tensor([int(starts[b]), 0, 1], dtype=torch.int32)
+        unit = torch.empty((1024, 128))
+        perm = [torch.empty(1024, dtype=torch.int32) for _ in range(2)]
+        anchor = torch.empty((64, 2), dtype=torch.int32)
+        scores = torch.empty(1024)
+        flag = torch.zeros((), dtype=torch.int32)
+        dk.initialize[(64,)](fp8, f32, source, meta, unit, perm[0], flag, num_warps=4)
+        cur = 0
+        for n in (1024, 512, 256, 128, 64, 32, 16):
+            for mode in (0, 1, 2):
+                fg._dots[(64, 1)](unit, perm[cur], anchor, scores, flag, n, 0, mode, num_warps=4,
+                                  enable_fp_fusion=False)
+                if mode < 2:
+                    fg._anchor[(1024 // n, 1)](perm[cur], anchor, scores, flag, n, mode, num_warps=4)
+            fg._sort[(1024 // n, 1)](perm[cur], perm[1 - cur], scores, flag, n, num_warps=4)
+            cur = 1 - cur
+        tmp = torch.zeros((16, 8448), dtype=torch.uint8)
+        centers = torch.zeros((2, 8448), dtype=torch.uint8)
+        mapping = torch.zeros((16, 64), dtype=torch.int32)
+        dk.assemble[(16, 8)](fp8, f32, source, meta, perm[cur], tmp.view(torch.float8_e4m3fn),
+                             tmp.view(torch.float32), centers.view(torch.float8_e4m3fn), centers.view(torch.float32),
+                             mapping, num_warps=4)
+        out.update({f"unit{b}": unit, f"perm{b}": perm[cur].clone(), f"tmp{b}": tmp, f"centers{b}": centers,
+                    f"mapping{b}": mapping, f"flag{b}": flag.reshape(1)})
+    save("build", **out)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
@@ -461,7 +515,7 @@ def main():
     jobs = dict(sort=lambda: gen_sort(fg), gather=lambda: gen_gather(nk),
                 pages=lambda: gen_pages(dk), tail_meta=lambda: gen_tail_and_meta(dk),
                 select_maps=lambda: gen_select_maps(dk), scores=lambda: gen_scores(dk),
-                route_topk=gen_route_topk_example)
+                route_topk=gen_route_topk_example, build=lambda: gen_build(dk, fg))
     for name, job in jobs.items():
         if args.only and name not in args.only.split(","):
             continue
