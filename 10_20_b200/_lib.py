@@ -60,6 +60,7 @@ SIGNATURES = {
                          P],
     "v1x_build_workspace_bytes": [I64],
     "v1x_build_buckets": [P, I64, P, P, P, P, P, P, P, P, I64, P],
+    "v1x_build_buckets_noalloc": [P, I64, P, P, P, P, P, P, P, I64, P],
     "v1x_initialize": [P, I64, P, P, P, P, P, P, P],
     "v1x_group_init": [P, I32, P, P, P, P, I64, I64, I64, I64, P],
     "v1x_group_dots": [P, P, P, P, P, I64, I64, I32, I64, I64, P],

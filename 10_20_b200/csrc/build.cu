@@ -542,6 +542,66 @@ extern "C" int v1x_build_buckets(const uint8_t* native, int64_t native_pages, co
   return launch_status("v1x_build_buckets");
 }
 
+// ---------------------------------------------------------------------------
+// No-allocation entry point: the same build with its workspace in a fixed
+// array inside the library instead of a caller-supplied buffer.
+// ---------------------------------------------------------------------------
+namespace v1x {
+namespace {
+constexpr int kNoAllocBuckets = 8;  // 8 x 536,832 bytes = 4.3 MB of device memory
+}  // namespace
+static __device__ __align__(256) uint8_t g_build_scratch[kNoAllocBuckets * kWorkBytes];
+}  // namespace v1x
+
+extern "C" int v1x_build_buckets_noalloc(const uint8_t* native, int64_t native_pages, const int32_t* source,
+                                         const int32_t* starts, uint8_t* tmp, uint8_t* centers, int32_t* mapping,
+                                         int32_t* perm, int32_t* status, int64_t buckets, void* stream) {
+  using namespace v1x;
+  clear_error();
+  V1X_CHECK_ARG(buckets >= 0 && buckets <= kNoAllocBuckets,
+                "build_buckets_noalloc: at most %d buckets per call (got %lld); split the call, or use "
+                "v1x_build_buckets with a caller-supplied workspace",
+                kNoAllocBuckets, (long long)buckets);
+  V1X_CHECK_ARG(native_pages > 0, "build_buckets_noalloc: empty native pool");
+  V1X_CHECK_ARG((reinterpret_cast<uintptr_t>(native) & 15) == 0 && (reinterpret_cast<uintptr_t>(tmp) & 15) == 0,
+                "build_buckets_noalloc: native and tmp must be 16-byte aligned");
+  if (buckets == 0) return V1X_OK;
+  // the scratch array's address on the current device, looked up once per
+  // device with that device current
+  static void* scratch[DeviceOnce::kMaxDevices] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= DeviceOnce::kMaxDevices) {
+    set_error("build_buckets_noalloc: no current device (%s)", cudaGetErrorString(e));
+    return V1X_ERR_CUDA;
+  }
+  if (scratch[dev] == nullptr) {
+    void* addr = nullptr;
+    e = cudaGetSymbolAddress(&addr, g_build_scratch);
+    if (e != cudaSuccess || addr == nullptr) {
+      set_error("build_buckets_noalloc: scratch lookup failed (%s)", cudaGetErrorString(e));
+      return V1X_ERR_CUDA;
+    }
+    scratch[dev] = addr;
+  }
+  static DeviceOnce once;
+  if (once.first()) set_smem_attr(reinterpret_cast<const void*>(build_bucket_kernel));
+  BuildArgs a{native, native_pages, source, starts, tmp, centers, mapping, perm, static_cast<uint8_t*>(scratch[dev]),
+              status};
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kBuildCtas, static_cast<unsigned>(buckets));
+  cfg.blockDim = dim3(kBuildThreads);
+  cfg.dynamicSmemBytes = sizeof(BuildSmem);
+  cfg.stream = as_stream(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributePriority;
+  attr[0].val.priority = greatest_priority();
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, build_bucket_kernel, a);
+  return launch_status("v1x_build_buckets_noalloc");
+}
+
 extern "C" int v1x_initialize(const uint8_t* native, int64_t native_pages, const int32_t* table,
                               const int32_t* meta, float* unit, int32_t* perm, int32_t* flag, int32_t* status,
                               void* stream) {

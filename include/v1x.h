@@ -154,6 +154,22 @@ V1X_API int v1x_build_buckets(const uint8_t* native, int64_t native_pages, const
                       const int32_t* starts, uint8_t* tmp, uint8_t* centers, int32_t* mapping,
                       int32_t* perm, void* work, int32_t* status, int64_t buckets, void* stream);
 
+/* No counterpart in the reference.  v1x_build_buckets without a workspace
+ * argument, for callers that cannot allocate device memory when they call: an
+ * engine that has handed all free device memory to its own pool, or a plain
+ * C / FFI host with no device allocator at hand.  The workspace is a fixed 4.3 MB
+ * array inside the library (8 buckets' worth); more than 8 buckets per call is
+ * rejected with V1X_ERR_INVALID.  The call allocates nothing.  Nothing in the
+ * scratch has to start at zero: every word the kernel reads was written earlier
+ * in the same launch.  The scratch is shared by every call on a device, so
+ * calls that can overlap (other streams, other host threads) race on it and must
+ * be serialised by the caller.  Its address is looked up once per device, with
+ * that device current, on the first call there; make that first call before any
+ * stream capture on the device. */
+V1X_API int v1x_build_buckets_noalloc(const uint8_t* native, int64_t native_pages, const int32_t* source,
+                              const int32_t* starts, uint8_t* tmp, uint8_t* centers, int32_t* mapping,
+                              int32_t* perm, int32_t* status, int64_t buckets, void* stream);
+
 /* DS/kernels.py:9-29 (initialize, grid (64,)).  table i32 [16], meta i32 [3]
  * {start, lease, active} -> unit f32 [1024, 128], perm i32 [1024], flag i32
  * (-1 when active, else 0). */
