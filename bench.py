@@ -1,7 +1,7 @@
 """Benchmark of the V1 query-side selection path on B200 (one process per GPU).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload decode|single]
+                    [--workload decode|single|sort|gather|pages|build]
 
 Workloads (synthetic, seeded; shapes of the benchmark configurations):
   decode  128 requests per GPU, context ~U[32K, 128K] tokens, 64 index heads,
@@ -10,6 +10,8 @@ Workloads (synthetic, seeded; shapes of the benchmark configurations):
           bf16 MLA latent (single output: K and V are the same latent).
   single  1024 single-head queries over 64 built pages + 65-token tail
           (2688 candidates), route -> score -> Top-2048 (no gather).
+Component workloads (one line each): sort (_sort + group offsets), gather
+(_gather_slots), pages (page lifecycle), build (index build of 1024 buckets).
 A step is one pass of the whole selection path over one batch.  Three
 independent batches (separate pools, same context lengths) are in flight on three
 streams, in turn, so the gather of one batch overlaps the selection of the next
@@ -484,6 +486,59 @@ def run_pages_workload(args, world, rank, device, dist):
     return line
 
 
+def run_build_workload(args, world, rank, device, dist):
+    """Index build (Build.compute's initialize / grouping / assemble): 1024
+    buckets per step (16 native pages each, a 138 MB native pool read once per
+    step) built in one launch, one 8-CTA cluster per bucket; also the latency of
+    a single bucket (the reference's unit of work)."""
+    import numpy as np
+    ib = importlib.import_module("10_20_b200.index_build")
+    oracle = importlib.import_module("oracle.v1x_oracle")
+    nb = 1024
+    gen = torch.Generator().manual_seed(41 + rank)
+    pages = nb * 16
+    k = torch.randn((pages, 64, 128), generator=gen).to(torch.float8_e4m3fn)
+    host = torch.zeros((pages, 8448), dtype=torch.uint8)
+    host[:, :8192] = k.view(torch.uint8).reshape(pages, 8192)
+    host.view(torch.float32)[:, 2048:] = torch.rand((pages, 64), generator=gen) + 0.25
+    native = host.to(device)
+    source = torch.randperm(pages, generator=gen).to(torch.int32).reshape(nb, 16).to(device)
+    starts = (torch.arange(nb, dtype=torch.int32) * 1024).to(device)
+    builder = ib.BucketBuilder(device, nb)
+    g = _capture(lambda: builder.build(native, source, starts), device)
+    ms, clk = _timed_replays(g, args.steps, args.warmup, dist, device)
+    value = nb * args.steps * world / (ms / 1e3)
+    # one bucket at a time (latency), back to back
+    one = ib.BucketBuilder(device, 1)
+    g1 = _capture(lambda: one.build(native, source[:1], starts[:1]), device)
+    ms1, _ = _timed_replays(g1, 200, 5, None, device)
+    per_bucket = 16 * 8448 + 16 * 8448 + 2 * 8448 + 1024 * 4 + 1024 * 4
+    # parity spot check: four buckets against the oracle
+    tmp, centers, mapping, perm = (x.cpu().numpy() for x in builder.build(native, source, starts))
+    src_np, pool = source.cpu().numpy(), host.numpy()
+    parity = True
+    for b in (0, 1, 511, nb - 1):
+        unit, _ = oracle.build_initialize(pool, src_np[b])
+        e_perm = oracle.group_bucket(unit)
+        e_tmp, e_centers, e_map = oracle.build_assemble(pool, src_np[b], b * 1024, e_perm)
+        parity = parity and all(np.array_equal(x, y) for x, y in
+                                ((perm[b], e_perm), (tmp[b], e_tmp), (centers[b], e_centers), (mapping[b], e_map)))
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        rate, n, el = _cpu_rate(lambda: oracle.build_bucket(pool, src_np[0], 0), 1)
+        cpu = {"value": rate, "unit": "buckets/s", "cores": 1, "kind": "port",
+               "sample": f"{n} calls of one bucket, oracle build_bucket (numpy), {el:.1f} s"}
+    line = _component_line(args, world, "index-built buckets/s (initialize + 7 grouping levels + assemble)",
+                           "buckets/s", value, args.steps, ms, clk,
+                           {"workload": "build", "buckets_per_step": nb, "native_pages": pages,
+                            "bytes_per_bucket": per_bucket,
+                            "l2": "the 138 MB native pool is read once per step (larger than L2)"},
+                           per_bucket * nb, "build_bucket_kernel", 1, cpu, parity)
+    line["ms_per_bucket_single"] = ms1 / 200
+    line["workspace_bytes_per_bucket"] = int(builder.work.numel() // nb)
+    return line
+
+
 def run_component(args):
     world, rank, device, dist = _dist_setup()
     importlib.import_module("10_20_b200").load()
@@ -491,6 +546,8 @@ def run_component(args):
         line = run_sort_workload(args, world, rank, device, dist)
     elif args.workload == "gather":
         line = run_gather_workload(args, world, rank, device, dist)
+    elif args.workload == "build":
+        line = run_build_workload(args, world, rank, device, dist)
     else:
         line = run_pages_workload(args, world, rank, device, dist)
     if rank == 0:
@@ -509,14 +566,16 @@ def main():
     ap.add_argument("--requests", type=int, default=0,
                     help="override the per-GPU batch (small cases for profiling; not a bench config)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "single", "sort", "gather", "pages"],
+    ap.add_argument("--workload", default="decode",
+                    choices=["decode", "single", "sort", "gather", "pages", "build"],
                     help="decode (the headline), single (1024 single-head queries), sort (_sort, 256 x 65,536 "
-                         "records), gather (_gather_slots, 1024 x 2048 slots of 576 bf16), pages (page lifecycle)")
+                         "records), gather (_gather_slots, 1024 x 2048 slots of 576 bf16), pages (page "
+                         "lifecycle), build (index build, 1024 buckets per step)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--inflight", type=int, default=3,
                     help="independent batches in flight (the gather of one overlaps the selection of the next)")
     args = ap.parse_args()
-    if args.workload in ("sort", "gather", "pages"):
+    if args.workload in ("sort", "gather", "pages", "build"):
         return run_component(args)
     cfg = workload_cfg(args.workload)
     if args.requests:
