@@ -11,11 +11,14 @@
 // Here one thread-block cluster of 8 CTAs x 1024 threads builds one bucket in a
 // single launch (many buckets per launch, one cluster each).  CTA r owns
 // positions (and, at initialisation, tokens) [128r, 128r + 128); eight lanes
-// share a position.  Levels whose groups span CTAs (n = 1024, 512, 256) exchange
-// the argmin partials, margins and the next permutation through the bucket's
-// global workspace (L2) behind hardware cluster barriers; from n = 128 down a
-// group lies inside one CTA and the levels run from shared memory with block
-// barriers only.  There is no spin-wait anywhere.
+// share a position and keep its member's unit vector in registers for the three
+// dot modes of a level.  The unit vectors live in the bucket's workspace (L2).
+// Levels whose groups span CTAs (n = 1024, 512, 256) send the argmin partials,
+// the sort keys and the next permutation straight into the shared memory of the
+// group's CTAs (distributed shared memory) behind hardware cluster barriers; from
+// n = 128 down a group lies inside one CTA, whose members' vectors are copied
+// into shared memory once, and the levels run with block barriers only.  There
+// is no spin-wait anywhere.
 //
 // Fixed fp32 evaluation order (the one the reference's kernels produce in the
 // Triton interpreter, whose tl.sum is numpy's pairwise float32 sum): a 128-term
@@ -44,13 +47,9 @@ constexpr int kSlice = 128;            // positions per CTA
 constexpr int kBucket = 1024;          // tokens per bucket
 constexpr int kWarps = kBuildThreads / 32;
 
-// per-bucket workspace (bytes): lane-major unit vectors, two permutations,
-// margins, argmin partials of two modes
-constexpr int64_t kUnitBytes = int64_t(kBucket) * 128 * 4;
-constexpr int64_t kPermOff = kUnitBytes;
-constexpr int64_t kScoreOff = kPermOff + 2 * kBucket * 4;
-constexpr int64_t kPartOff = kScoreOff + kBucket * 4;
-constexpr int64_t kWorkBytes = (kPartOff + 2 * kBuildCtas * 8 + 255) / 256 * 256;
+// per-bucket workspace: the bucket's unit vectors, lane-major (512 KB, read by
+// every CTA of the cluster from L2)
+constexpr int64_t kWorkBytes = int64_t(kBucket) * 128 * 4;
 
 struct BuildArgs {
   const uint8_t* native;
@@ -66,11 +65,17 @@ struct BuildArgs {
 };
 
 struct BuildSmem {
-  float xs[kSlice][128];                 // dequantised rows of the CTA's positions (assemble)
+  // levels <= 128: unit vectors of the slice's members (lane-major rows);
+  // assemble: the dequantised rows of the CTA's positions
+  float xs[kSlice][128];
   unsigned long long keys[kBucket];      // sort keys of the current group
-  int ploc[2][kSlice];                   // the CTA's permutation slice (levels <= 128)
+  int pg[2][kSlice];                     // levels >= 256: member at each of the CTA's positions
+  int ploc[2][kSlice];                   // levels <= 128: xs row at each position
+  int tok[kSlice];                       // member of each xs row
+  int4 part[2][kBuildCtas];              // MODE 0/1 argmin partials: (value bits, position, member)
   float wv[kWarps];
   int wp[kWarps];
+  int wt[kWarps];
   float gv[kWarps];
   int gp[kWarps];
   float cmax[16][2];
@@ -89,18 +94,37 @@ __device__ __forceinline__ float lanes8_sum(float r) {
   return r;
 }
 
-// lane j of 8: r_j = p[j] + p[8+j] + ... over 16 products of lane-major rows
-__device__ __forceinline__ float dot_lane_major(const float* __restrict__ x, const float* __restrict__ y) {
-  float r = 0.0f;
+// lane j's 16 values of a lane-major workspace row (16 contiguous floats)
+__device__ __forceinline__ void load_row16(const float* __restrict__ src, float (&x)[16]) {
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
-    const float4 a = __ldcg(reinterpret_cast<const float4*>(x) + c);
-    const float4 b = __ldcg(reinterpret_cast<const float4*>(y) + c);
-    r = c == 0 ? __fmul_rn(a.x, b.x) : __fadd_rn(r, __fmul_rn(a.x, b.x));
-    r = __fadd_rn(r, __fmul_rn(a.y, b.y));
-    r = __fadd_rn(r, __fmul_rn(a.z, b.z));
-    r = __fadd_rn(r, __fmul_rn(a.w, b.w));
+    const float4 v = __ldcg(reinterpret_cast<const float4*>(src) + c);
+    x[4 * c] = v.x;
+    x[4 * c + 1] = v.y;
+    x[4 * c + 2] = v.z;
+    x[4 * c + 3] = v.w;
   }
+}
+
+// Shared-memory rows are chunk-major: lane j's chunk c (values 4c..4c+3) sits at
+// float4 index c*8 + j, so the eight lanes of a position read eight distinct
+// bank groups in every load.
+__device__ __forceinline__ void load_srow16(const float* row, int j, float (&x)[16]) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const float4 v = reinterpret_cast<const float4*>(row)[c * 8 + j];
+    x[4 * c] = v.x;
+    x[4 * c + 1] = v.y;
+    x[4 * c + 2] = v.z;
+    x[4 * c + 3] = v.w;
+  }
+}
+
+// lane j of 8: r_j = x[0]*y[0] + x[1]*y[1] + ... (dims j, j+8, ...), then the butterfly
+__device__ __forceinline__ float dot_regs(const float (&x)[16], const float (&y)[16]) {
+  float r = __fmul_rn(x[0], y[0]);
+#pragma unroll
+  for (int i = 1; i < 16; ++i) r = __fadd_rn(r, __fmul_rn(x[i], y[i]));
   return lanes8_sum(r);
 }
 
@@ -254,13 +278,13 @@ __global__ void __cluster_dims__(kBuildCtas, 1, 1) __launch_bounds__(kBuildThrea
   const int r = static_cast<int>(cluster.block_rank());
   const int64_t bk = blockIdx.y;
   const int tid = threadIdx.x, q = tid >> 3, j = tid & 7;
+  const int lane = tid & 31, warp = tid >> 5;
   const int32_t* src_pages = a.source + bk * 16;
-  uint8_t* work = a.work + bk * kWorkBytes;
-  float* unit = reinterpret_cast<float*>(work);
-  int* pg[2] = {reinterpret_cast<int*>(work + kPermOff), reinterpret_cast<int*>(work + kPermOff) + kBucket};
-  float* sg = reinterpret_cast<float*>(work + kScoreOff);
-  int2* part = reinterpret_cast<int2*>(work + kPartOff);  // [mode][cta] = (value bits, position)
+  float* unit = reinterpret_cast<float*>(a.work + bk * kWorkBytes);
   const int pos = r * kSlice + q;
+  // member ids index the workspace: kept in [0, 1024) by construction, masked
+  // so that no value can address outside it
+  constexpr int kIdMask = kBucket - 1;
 
   // ---- initialize (DS/kernels.py:9-29): unit vectors, lane-major, identity order
   {
@@ -275,86 +299,108 @@ __global__ void __cluster_dims__(kBuildCtas, 1, 1) __launch_bounds__(kBuildThrea
     for (int c = 0; c < 4; ++c)
       u[c] = make_float4(__fdiv_rn(x[4 * c], m), __fdiv_rn(x[4 * c + 1], m), __fdiv_rn(x[4 * c + 2], m),
                          __fdiv_rn(x[4 * c + 3], m));
-    if (j == 0) pg[0][pos] = pos;
+    if (j == 0) sm.pg[0][q] = pos;
   }
   cluster.sync();
 
-  // ---- levels whose groups span CTAs: n = 1024, 512, 256 (workspace + cluster barriers)
+  // ---- levels whose groups span CTAs: n = 1024, 512, 256.  Vectors come from the
+  // L2 workspace; argmin partials, sort keys and the next order go straight into
+  // the shared memory of the group's CTAs, behind cluster barriers.
   int cur = 0;
   for (int n = kBucket; n > kSlice; n >>= 1, cur ^= 1) {
-    const int* P = pg[cur];
-    const int g0 = pos / n * n;
-    // member ids index the workspace: kept in [0, 1024) by construction, masked
-    // so that no value can address outside it
-    const int t = __ldcg(P + pos) & (kBucket - 1);
-    const float* ut = unit + static_cast<int64_t>(t) * 128 + j * 16;
+    const int g0 = pos / n * n, c0 = g0 / kSlice, m = n / kSlice;  // the group's CTAs: c0 .. c0+m-1
+    const int t = sm.pg[cur][q] & kIdMask;
+    float x[16], y[16];
+    load_row16(unit + static_cast<int64_t>(t) * 128 + j * 16, x);
+    int anchor = *cluster.map_shared_rank(&sm.pg[cur][0], c0) & kIdMask;  // MODE 0: the group's first member
     float s1 = 0.0f;
-    int anchor = __ldcg(P + g0) & (kBucket - 1);  // MODE 0: the group's first member
     for (int mode = 0; mode < 3; ++mode) {
-      float s = dot_lane_major(ut, unit + static_cast<int64_t>(anchor) * 128 + j * 16);
+      load_row16(unit + static_cast<int64_t>(anchor) * 128 + j * 16, y);
+      float s = dot_regs(x, y);
       if (mode == 2) {
         s = __fsub_rn(s, s1);
-        if (j == 0) sg[pos] = s;
+        if (j < m) *cluster.map_shared_rank(&sm.keys[pos - g0], c0 + j) = sort_key(s, pos - g0);
         break;
       }
       s1 = s;
-      // argmin over the CTA's positions, then over the group's CTAs
-      int p = pos;
+      // argmin over the CTA's positions (all in one group), sent to the group's CTAs
       float v = s;
-      warp_argmin4(v, p);
-      const int lane = tid & 31, warp = tid >> 5;
+      int p = pos;
+      int tk = t;
+#pragma unroll
+      for (int o = 8; o <= 16; o <<= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+        const int op = __shfl_xor_sync(0xffffffffu, p, o);
+        const int ot = __shfl_xor_sync(0xffffffffu, tk, o);
+        if (argmin_better(ov, op, v, p)) {
+          v = ov;
+          p = op;
+          tk = ot;
+        }
+      }
       if (lane == 0) {
         sm.wv[warp] = v;
         sm.wp[warp] = p;
+        sm.wt[warp] = tk;
       }
       __syncthreads();
       if (warp == 0) {
         float gv = sm.wv[lane];
-        int gp = sm.wp[lane];
+        int gp = sm.wp[lane], gt = sm.wt[lane];
         for (int o = 16; o >= 1; o >>= 1) {
           const float ov = __shfl_xor_sync(0xffffffffu, gv, o);
           const int op = __shfl_xor_sync(0xffffffffu, gp, o);
+          const int ot = __shfl_xor_sync(0xffffffffu, gt, o);
           if (argmin_better(ov, op, gv, gp)) {
             gv = ov;
             gp = op;
+            gt = ot;
           }
         }
-        if (lane == 0) part[mode * kBuildCtas + r] = make_int2(__float_as_int(gv), gp);
+        if (lane < m) *cluster.map_shared_rank(&sm.part[mode][r], c0 + lane) = make_int4(__float_as_int(gv), gp, gt, 0);
       }
       cluster.sync();
-      float bv = 0.0f;
-      int bp = -1;
-      for (int c = g0 / kSlice; c < (g0 + n) / kSlice; ++c) {
-        const int2 e = __ldcg(part + mode * kBuildCtas + c);
-        const float ev = __int_as_float(e.x);
-        if (bp < 0 || argmin_better(ev, e.y, bv, bp)) {
-          bv = ev;
-          bp = e.y;
-        }
+      int4 best = sm.part[mode][c0];
+      for (int c = c0 + 1; c < c0 + m; ++c) {
+        const int4 e = sm.part[mode][c];
+        if (argmin_better(__int_as_float(e.x), e.y, __int_as_float(best.x), best.y)) best = e;
       }
-      anchor = __ldcg(P + (bp & (kBucket - 1))) & (kBucket - 1);  // b after MODE 0, a after MODE 1
+      anchor = best.z & kIdMask;  // b after MODE 0, a after MODE 1
     }
-    cluster.sync();  // margins of the whole group are in the workspace
+    cluster.sync();  // the group's keys are complete in every CTA of the group
     // stable descending sort of the group's margins (NA/fused_grouping.py:64-76)
-    for (int k = tid; k < n; k += kBuildThreads) sm.keys[k] = sort_key(__ldcg(sg + g0 + k), k);
-    __syncthreads();
-    const int rank = rank_in_group(sm.keys, n, sort_key(__ldcg(sg + pos), pos - g0), j);
-    if (j == 0) pg[cur ^ 1][g0 + rank] = t;
+    const int rank = rank_in_group(sm.keys, n, sm.keys[pos - g0], j);
+    const int dest = g0 + rank;
+    if (j == 0) *cluster.map_shared_rank(&sm.pg[cur ^ 1][dest % kSlice], dest / kSlice) = t;
     cluster.sync();
   }
 
-  // ---- levels inside one CTA: n = 128 .. 16 (shared memory, block barriers)
-  int lc = 0;
-  if (j == 0) sm.ploc[0][q] = __ldcg(pg[cur] + pos);
+  // ---- levels inside one CTA: n = 128 .. 16.  The slice's member vectors are
+  // copied into shared memory once; positions then hold xs rows.
+  {
+    const int t = sm.pg[cur][q] & kIdMask;
+    float x[16];
+    load_row16(unit + static_cast<int64_t>(t) * 128 + j * 16, x);
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      reinterpret_cast<float4*>(sm.xs[q])[c * 8 + j] = make_float4(x[4 * c], x[4 * c + 1], x[4 * c + 2], x[4 * c + 3]);
+    if (j == 0) {
+      sm.tok[q] = t;
+      sm.ploc[0][q] = q;
+    }
+  }
   __syncthreads();
+  int lc = 0;
   for (int n = kSlice; n >= 16; n >>= 1, lc ^= 1) {
     const int g0 = q / n * n;
-    const int t = sm.ploc[lc][q];
-    const float* ut = unit + static_cast<int64_t>(t) * 128 + j * 16;
+    const int row = sm.ploc[lc][q];
+    float x[16], y[16];
+    load_srow16(sm.xs[row], j, x);
     int anchor = sm.ploc[lc][g0];
     float s1 = 0.0f, s = 0.0f;
     for (int mode = 0; mode < 3; ++mode) {
-      s = dot_lane_major(ut, unit + static_cast<int64_t>(anchor) * 128 + j * 16);
+      load_srow16(sm.xs[anchor], j, y);
+      s = dot_regs(x, y);
       if (mode == 2) {
         s = __fsub_rn(s, s1);
         break;
@@ -364,14 +410,19 @@ __global__ void __cluster_dims__(kBuildCtas, 1, 1) __launch_bounds__(kBuildThrea
     }
     if (j == 0) sm.keys[q] = sort_key(s, q - g0);
     __syncthreads();
-    const int rank = rank_in_group(sm.keys + g0, n, sort_key(s, q - g0), j);
-    if (j == 0) sm.ploc[lc ^ 1][g0 + rank] = t;
+    const int rank = rank_in_group(sm.keys + g0, n, sm.keys[q], j);
+    if (j == 0) sm.ploc[lc ^ 1][g0 + rank] = row;
     __syncthreads();
   }
-  if (a.perm && j == 0) a.perm[bk * kBucket + pos] = sm.ploc[lc][q];
+  if (j == 0) {
+    const int member = sm.tok[sm.ploc[lc][q]];
+    sm.pg[0][q] = member;
+    if (a.perm) a.perm[bk * kBucket + pos] = member;
+  }
+  __syncthreads();
 
   // ---- assemble (DS/kernels.py:32-54)
-  assemble_slice(a, src_pages, a.starts[bk], sm.ploc[lc], r, a.tmp + bk * 16 * kPageBytes,
+  assemble_slice(a, src_pages, a.starts[bk], sm.pg[0], r, a.tmp + bk * 16 * kPageBytes,
                  a.centers + bk * 2 * kPageBytes, a.mapping + bk * kBucket, sm);
 }
 
