@@ -599,7 +599,7 @@ extern "C" int v1x_build_buckets(const uint8_t* native, int64_t native_pages, co
 // ---------------------------------------------------------------------------
 namespace v1x {
 namespace {
-constexpr int kNoAllocBuckets = 8;  // 8 x 536,832 bytes = 4.3 MB of device memory
+constexpr int kNoAllocBuckets = 8;  // 8 x 512 KB = 4 MB of device memory
 }  // namespace
 static __device__ __align__(256) uint8_t g_build_scratch[kNoAllocBuckets * kWorkBytes];
 }  // namespace v1x

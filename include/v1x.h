@@ -157,7 +157,7 @@ V1X_API int v1x_build_buckets(const uint8_t* native, int64_t native_pages, const
 /* No counterpart in the reference.  v1x_build_buckets without a workspace
  * argument, for callers that cannot allocate device memory when they call: an
  * engine that has handed all free device memory to its own pool, or a plain
- * C / FFI host with no device allocator at hand.  The workspace is a fixed 4.3 MB
+ * C / FFI host with no device allocator at hand.  The workspace is a fixed 4 MB
  * array inside the library (8 buckets' worth); more than 8 buckets per call is
  * rejected with V1X_ERR_INVALID.  The call allocates nothing.  Nothing in the
  * scratch has to start at zero: every word the kernel reads was written earlier
