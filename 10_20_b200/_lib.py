@@ -22,6 +22,7 @@ V1X_ERR_UNSUPPORTED = -3
 V1X_STATUS_ARENA_EXHAUSTED = 1
 V1X_STATUS_TIMEOUT = 2
 V1X_STATUS_BAD_PAGE = 3
+V1X_STATUS_CAPACITY = 4
 
 P = ctypes.c_void_p
 I64 = ctypes.c_int64
@@ -66,6 +67,11 @@ SIGNATURES = {
     "v1x_group_dots": [P, P, P, P, P, I64, I64, I32, I64, I64, P],
     "v1x_group_anchor": [P, P, P, P, I64, I32, I64, I64, P],
     "v1x_assemble": [P, I64, P, P, P, P, P, P, P],
+    "v1x_stage_union": [P, I64, P, I64, P, I64, P, P, I64, P, P, I64, I64, P, P],
+    "v1x_shared_tables": [P, P, P, P, P, P, P, P, I64, I64, I64, I64, I64, I64, I32, I64, P],
+    "v1x_shared_normalize": [P, I64, P, P, P, P, P, I64, P, I64, I64, I64, I64, I32, I64, P],
+    "v1x_shared_map_topk": [P, P, P, P, P, P, P, I64, P, I64, P, P, I64, I64, I64, I64, I64, P],
+    "v1x_route_physical": [P, I64, P, P, P, P, P, I64, I64, I64, P],
 }
 # entry points whose return type is not int
 RESTYPES = {"v1x_last_error": ctypes.c_char_p, "v1x_build_workspace_bytes": ctypes.c_int64}

@@ -51,6 +51,7 @@ extern "C" {
 #define V1X_STATUS_ARENA_EXHAUSTED 1 /* allocate: free stack smaller than needed */
 #define V1X_STATUS_TIMEOUT 2         /* a bounded device-side wait gave up          */
 #define V1X_STATUS_BAD_PAGE 3        /* build: a source page id outside the native pool */
+#define V1X_STATUS_CAPACITY 4        /* stage_union: the union needs more pages than dst holds */
 
 /* Library identity: returns 0x010000 * major + 0x100 * minor + patch. */
 V1X_API int v1x_version(void);
@@ -202,6 +203,60 @@ V1X_API int v1x_group_anchor(const int32_t* p, int32_t* anchor, const float* s, 
 V1X_API int v1x_assemble(const uint8_t* native, int64_t native_pages, const int32_t* table,
                  const int32_t* meta, const int32_t* ids, uint8_t* tmp, uint8_t* centers,
                  int32_t* mapping, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Published-end shared-tail variant: one request's chunk of query rows with
+ * non-decreasing lengths shares one staged copy of its sink and tail pages.
+ * experiments/tail_union_lab_20261021/union.py:10-40 and
+ * experiments/fine_pool_shared_20261021/{kernels.py:8-76, route_shared.cu:12-54}.
+ * A row's tail starts at the published index end indexed_end[0] (device word):
+ * s = min(n, sink), t = max(s, min(min(max(end, 0), n), max(s, n - window))),
+ * count = s + n - t. */
+
+/* union.py:16-40 (stage_union).  src / dst u8 [pages, 8448]; nt i32 [nt_len]
+ * (the request's logical -> physical page table); lens i32 [rows] -> dst pages
+ * [0, total) = the sink pages [0, sp) then the tail pages [tp, ep) of nt,
+ * meta i32 [rows, 3] = (s, t, count), desc i32 [4] = (sp, tp, ep, total).  A union
+ * larger than dst_pages copies what fits and writes V1X_STATUS_CAPACITY. */
+V1X_API int v1x_stage_union(const uint8_t* src, int64_t src_pages, const int32_t* nt, int64_t nt_len,
+                    const int32_t* lens, int64_t rows, const int32_t* indexed_end, uint8_t* dst,
+                    int64_t dst_pages, int32_t* meta, int32_t* desc, int64_t sink, int64_t window,
+                    int32_t* status, void* stream);
+
+/* kernels.py:13-41 (tables): ft i32 [rows, fp] (selected pages, then the staged
+ * pages: shared -> cap + union page, else cap + row*scratch + k), dglens i32
+ * [rows] = max(take*64 + scored span, 1), clens i32 [rows] = take*64 + count. */
+V1X_API int v1x_shared_tables(const int32_t* lens, const int32_t* indexed_end, const int32_t* takes,
+                      const int32_t* selected, const int32_t* desc, int32_t* ft, int32_t* dglens,
+                      int32_t* clens, int64_t cap, int64_t max_take, int64_t scratch, int64_t fp,
+                      int64_t sink, int64_t window, int shared, int64_t rows, void* stream);
+
+/* kernels.py:43-63 (normalize): out f32 [rows, width] = the canonical candidate
+ * order [selected members | sink | tail] read from raw f32 [rows, stride], masked
+ * (-inf) before Top-K; members i32 [member_rows, 64]. */
+V1X_API int v1x_shared_normalize(const float* raw, int64_t stride, const int32_t* lens,
+                         const int32_t* indexed_end, const int32_t* takes, const int32_t* selected,
+                         const int32_t* members, int64_t member_rows, float* out, int64_t max_take,
+                         int64_t width, int64_t sink, int64_t window, int shared, int64_t rows,
+                         void* stream);
+
+/* kernels.py:65-76 (map_topk): Top-K ids i64 / values f32 [rows, top] ->
+ * logical and physical slot ids i32 [rows, top] (-1 for -inf picks and
+ * positions outside [0, n)); nt = the request's page table. */
+V1X_API int v1x_shared_map_topk(const int64_t* ids, const float* values, const int32_t* lens,
+                        const int32_t* indexed_end, const int32_t* takes, const int32_t* selected,
+                        const int32_t* members, int64_t member_rows, const int32_t* nt, int64_t nt_len,
+                        int32_t* logical, int32_t* slots, int64_t max_take, int64_t top, int64_t sink,
+                        int64_t window, int64_t rows, void* stream);
+
+/* route_shared.cu:12-54 (route_physical): per row the top take = min(max(budget,
+ * 0), clamp(published, 0, pages), take_stride) published pages by the max of
+ * their 8 centre scores (stable, ties by the blocked rank of a 128-thread
+ * layout) written as physical ids rt[row, page] into selected i32 [rows,
+ * take_stride] (0 past take); takes i32 [rows]. */
+V1X_API int v1x_route_physical(const float* scores, int64_t score_stride, const int32_t* published,
+                       const int32_t* budgets, const int32_t* rt, int32_t* selected, int32_t* takes,
+                       int64_t pages, int64_t take_stride, int64_t rows, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Page lifecycle -- replace DS/kernels.py:57-179.  meta i32[3] =

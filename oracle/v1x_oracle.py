@@ -876,3 +876,192 @@ def gather_slots(K, V, REQ, IDS, rows, top, head):
     kg = np.where(valid[:, None], K[phys, head], 0).astype(K.dtype)
     vg = None if V is None else np.where(valid[:, None], V[phys, head], 0).astype(V.dtype)
     return kg, vg
+
+
+# --------------------------------------------------------------------------
+# published-end shared-tail variant (one request's chunk of query rows)
+#   EXP/tail_union_lab_20261021/union.py:10-40        bounds, stage_union
+#   EXP/fine_pool_shared_20261021/kernels.py:8-76     tables, normalize, map_topk
+#   EXP/fine_pool_shared_20261021/route_shared.cu:12-54  route_physical
+# EXP = experiments
+# --------------------------------------------------------------------------
+
+def shared_bounds(n, end, sink, window):
+    """(s, t, c) of a row of n visible tokens given the published index end
+    (union.py:10-14): sink = min(n, S); tail = max(s, min(min(max(end, 0), n),
+    max(s, n - W))); count = s + n - tail."""
+    s = min(n, sink)
+    t = max(s, min(min(max(end, 0), n), max(s, n - window)))
+    return s, t, s + n - t
+
+
+def stage_union(src_u8, nt, lens, end, dst_pages, sink, window, dst=None):
+    """union.py:16-40.  The chunk's union of sink pages [0, sp) and tail pages
+    [tp, ep) of the ONE page table `nt` (sp = ceil(min(last, S) / 64), tp =
+    max(sp, tail(first) // 64), ep = ceil(last / 64)), copied page by page into
+    dst[u] (u < total = sp + max(ep - tp, 0)); meta[r] = (s, t, c) per row; desc
+    = (sp, tp, ep, total).  dst pages at and past `total` keep their contents."""
+    src = np.asarray(src_u8, np.uint8).reshape(-1, PAGE_BYTES)
+    nt = np.asarray(nt, np.int64).reshape(-1)
+    lens = [int(x) for x in np.asarray(lens).reshape(-1)]
+    first, last = lens[0], lens[-1]
+    _, tail, _ = shared_bounds(first, end, sink, window)
+    sp = (min(last, sink) + 63) // 64
+    tp = max(sp, tail // 64)
+    ep = (last + 63) // 64
+    total = sp + max(ep - tp, 0)
+    out = np.zeros((dst_pages, PAGE_BYTES), np.uint8) if dst is None else np.array(dst, np.uint8, copy=True)
+    for u in range(min(total, dst_pages)):
+        lp = u if u < sp else tp + u - sp
+        out[u] = src[nt[lp]]
+    meta = np.array([shared_bounds(n, end, sink, window) for n in lens], np.int32).reshape(-1, 3)
+    desc = np.array([sp, tp, ep, total], np.int32)
+    return out, meta, desc
+
+
+def shared_tables(lens, end, takes, selected, desc, cap, max_take, scratch, fp, sink, window, shared):
+    """kernels.py:13-41 (tables).  Row r, column j < FP: the first `take`
+    columns are the selected pages; then the staged pages -- shared: the
+    chunk's union pages (sink page k -> CAP + k, tail page -> CAP + desc.sp +
+    tp_r - desc.tp + k - sp_r), else the row's own scratch pages CAP + r*SCRATCH
+    + k -- and 0 past them.  dglens = max(take*64 + span, 1) with span the
+    scored tail span (page-aligned in shared mode); clens = take*64 + count."""
+    R = len(lens)
+    ft = np.zeros((R, fp), np.int32)
+    dg = np.zeros(R, np.int32)
+    cl = np.zeros(R, np.int32)
+    selected = np.asarray(selected, np.int64).reshape(R, -1)
+    gsp, gtp = int(desc[0]), int(desc[1])
+    for r in range(R):
+        n, take = int(lens[r]), int(takes[r])
+        s, t, c = shared_bounds(n, end, sink, window)
+        if shared:
+            sp = (s + 63) // 64
+            tp = max(sp, t // 64)
+            ep = (n + 63) // 64
+            pages = sp + max(ep - tp, 0)
+            span = sp * 64 + n - tp * 64 if ep > tp else n
+        else:
+            pages = (c + 63) // 64
+            span = c
+        for j in range(fp):
+            k = j - take
+            if j < take:
+                page = int(selected[r, j]) if j < max_take else 0
+            elif 0 <= k < pages:
+                if shared:
+                    page = cap + k if k < sp else cap + gsp + tp - gtp + k - sp
+                else:
+                    page = cap + r * scratch + k
+            else:
+                page = 0
+            ft[r, j] = page
+        dg[r] = max(take * 64 + span, 1)
+        cl[r] = take * 64 + c
+    return ft, dg, cl
+
+
+def shared_normalize(raw, lens, end, takes, selected, members, max_take, width, sink, window, shared):
+    """kernels.py:43-63 (normalize): the canonical compact candidate order
+    [selected pages' members | sink | tail] with the masks applied before
+    Top-K: a selected member outside [s, t) or at/after n or the published end
+    -> -inf; candidates past the count -> -inf.  Shared mode reads a tail
+    candidate from its page-aligned slot in the union layout."""
+    raw = np.asarray(raw, np.float32)
+    R = len(lens)
+    members = np.asarray(members, np.int64).reshape(-1)
+    selected = np.asarray(selected, np.int64).reshape(R, -1)
+    out = np.full((R, width), NEG_INF, np.float32)
+    j = np.arange(width)
+    for r in range(R):
+        n, take = int(lens[r]), int(takes[r])
+        s, t, c = shared_bounds(n, end, sink, window)
+        hist = take * 64
+        fine = j < hist
+        x = j - hist
+        col = j // 64
+        page = np.where(fine & (col < max_take), selected[r, np.minimum(col, max_take - 1)] if max_take else 0, 0)
+        ok = (page >= 0) & (page * 64 < len(members))
+        member = np.where(fine & ok, members[np.where(ok, page * 64 + j % 64, 0)], -1)
+        logical = np.where(x < s, x, t + x - s)
+        if shared:
+            sp = (s + 63) // 64
+            tp = max(sp, t // 64)
+            slot = np.where(logical < sp * 64, logical, sp * 64 + logical - tp * 64)
+            source = np.where(fine, j, hist + slot)
+        else:
+            source = j
+        valid = np.where(fine, (member >= s) & (member < t) & (member < n) & (member < end), (x >= 0) & (x < c))
+        valid &= source < raw.shape[1]     # a column past the raw row reads as masked
+        out[r, valid] = raw[r, source[valid]]
+    return out
+
+
+def shared_map_topk(ids, values, lens, end, takes, selected, members, nt, max_take, sink, window):
+    """kernels.py:65-76 (map_topk): Top-K candidate rank -> logical position
+    (a selected page's member, or the sink/tail position) -> physical slot
+    through the request's page table; -inf picks and positions outside [0, n)
+    -> -1."""
+    ids = np.asarray(ids, np.int64)
+    values = np.asarray(values, np.float32)
+    R, top = ids.shape
+    members = np.asarray(members, np.int64).reshape(-1)
+    nt = np.asarray(nt, np.int64).reshape(-1)
+    selected = np.asarray(selected, np.int64).reshape(R, -1)
+    logical = np.full((R, top), -1, np.int32)
+    slots = np.full((R, top), -1, np.int32)
+    for r in range(R):
+        n, take = int(lens[r]), int(takes[r])
+        s, t, c = shared_bounds(n, end, sink, window)
+        rank = ids[r].astype(np.int32).astype(np.int64)
+        fine = (rank >= 0) & (rank < take * 64)
+        col = np.where(fine, rank // 64, 0)
+        page = np.where(fine & (col < max_take), selected[r, np.clip(col, 0, max(max_take - 1, 0))], 0)
+        ok = (page >= 0) & (page * 64 < len(members))
+        member = np.where(fine & ok, members[np.where(ok, page * 64 + rank % 64, 0)], -1)
+        x = rank - take * 64
+        lg = np.where(fine, member, np.where(x < s, x, t + x - s))
+        valid = (values[r] != NEG_INF) & (lg >= 0) & (lg < n) & (lg // 64 < len(nt))
+        phys = np.where(valid, nt[np.clip(lg // 64, 0, len(nt) - 1)] * 64 + lg % 64, -1)
+        logical[r] = np.where(valid, lg, -1)
+        slots[r] = phys
+    return logical, slots
+
+
+def route_physical(scores, published, budgets, rt, take_stride):
+    """route_shared.cu:12-54.  active = clamp(published, 0, pages); take =
+    min(max(budget, 0), active, take_stride).  take == 0 or take == active:
+    selected[i] = rt[i] for i < take.  Otherwise the page score is the max of
+    its 8 centres (an all -inf active page becomes -FLT_MAX, so it still
+    precedes padding), padding slots -inf, a stable descending radix sort over
+    the blocked layout of 128 threads x ITEMS (ITEMS the smallest power of two
+    with 128*ITEMS >= pages; ties keep blocked rank (p % 128)*ITEMS + p // 128,
+    -0 == +0) and selected[rank] = rt[page] for rank < take.  Padding entries
+    are 0.  Returns (selected int32 [R, take_stride], takes int32 [R])."""
+    scores = np.asarray(scores, np.float32)
+    rt = np.asarray(rt, np.int64)
+    R, pages = rt.shape
+    items = 1
+    while items * 128 < pages:
+        items *= 2
+    n_items = 128 * items
+    rank = np.arange(n_items)
+    p_of_rank = rank // items + (rank % items) * 128
+    sel = np.zeros((R, take_stride), np.int32)
+    takes = np.zeros(R, np.int32)
+    for r in range(R):
+        active = min(max(int(published[r]), 0), pages)
+        take = min(min(max(int(budgets[r]), 0), active), take_stride)
+        takes[r] = take
+        if take == 0 or take == active:
+            sel[r, :take] = rt[r, :take]
+            continue
+        vals = np.full(n_items, NEG_INF, np.float32)
+        valid = p_of_rank < active
+        m = np.fmax.reduce(scores[r, :active * 8].reshape(active, 8), axis=1)
+        m = np.where(m == NEG_INF, np.float32(-np.finfo(np.float32).max), m).astype(np.float32)
+        vals[valid] = m[p_of_rank[valid]]
+        key = twiddle_key(vals).astype(np.int64)
+        order = np.lexsort((rank, 0xFFFFFFFF - key))
+        sel[r, :take] = rt[r, p_of_rank[order][:take]]
+    return sel, takes

@@ -503,6 +503,68 @@ def gen_build(dk, fg):
     save("build", **out)
 
 
+def gen_shared(un, sk):
+    """Published-end shared-tail variant (experiments/tail_union_lab_20261021/
+    union.py, experiments/fine_pool_shared_20261021/kernels.py) on small chunks:
+    an on-time end, a lagging unaligned end, zero window, and empty rows."""
+    import triton
+    gen = torch.Generator().manual_seed(12)
+    out = {}
+    cases = [(4096, 8, 17, 64, 4096), (4096 + 100, 16, 64, 128, 3000), (2051, 6, 65, 0, 1025), (0, 4, 65, 0, 0)]
+    for ci, (h, R, S, W, end) in enumerate(cases):
+        np_pages = max(1, -(-(h + R) // 64)) + 3
+        src = fp8_pages(gen, np_pages)
+        nt = torch.randperm(np_pages, generator=gen).to(torch.int32)
+        lens = torch.arange(h + 1, h + R + 1, dtype=torch.int32) if h else torch.zeros(R, dtype=torch.int32)
+        iend = torch.tensor([end], dtype=torch.int32)
+        cap_pages = np_pages + 2
+        dst = torch.full((cap_pages, 8448), 165, dtype=torch.uint8)
+        meta = torch.zeros((R, 3), dtype=torch.int32)
+        desc = torch.zeros(4, dtype=torch.int32)
+        un.launch(src, nt, lens, iend, dst, meta, desc, S, W, block=256)
+        pre = f"c{ci}_"
+        out.update({pre + "case": torch.tensor([h, R, S, W, end, cap_pages]), pre + "src": src, pre + "nt": nt,
+                    pre + "dst": dst, pre + "meta": meta, pre + "desc": desc})
+        # tables / normalize / map_topk over this chunk
+        CAP, MAXTAKE, SCRATCH = 48, 5, 3
+        FP = 16
+        takes = torch.randint(0, MAXTAKE + 1, (R,), generator=gen).to(torch.int32)
+        selected = torch.randint(0, CAP, (R, MAXTAKE), generator=gen).to(torch.int32)
+        members = torch.randint(-2, h + R + 2, (CAP, 64), generator=gen).to(torch.int32)
+        # width as the reference's fixture sizes it: every row's history plus its
+        # page-aligned tail span fits (experiments/fine_pool_shared_20261021/experiment.py:41-42)
+        n_last = h + R if h else 0
+        s_last = min(n_last, S)
+        t_last = max(s_last, min(min(max(end, 0), n_last), max(s_last, n_last - W)))
+        WIDTH = -(-(MAXTAKE * 64 + s_last + n_last - t_last + 128) // 256) * 256
+        STRIDE = WIDTH + 32
+        raw = torch.randn((R, STRIDE), generator=gen)
+        TOP = 96
+        ids = torch.randint(0, WIDTH, (R, TOP), generator=gen).to(torch.int64)
+        values = torch.randn((R, TOP), generator=gen)
+        values[torch.rand((R, TOP), generator=gen) < 0.1] = float("-inf")
+        out.update({pre + "width": torch.tensor(WIDTH), pre + "takes": takes, pre + "selected": selected,
+                    pre + "members": members, pre + "raw": raw,
+                    pre + "ids": ids, pre + "values": values})
+        for shared in (0, 1):
+            ft = torch.full((R, FP), -9, dtype=torch.int32)
+            dg = torch.zeros(R, dtype=torch.int32)
+            cl = torch.zeros(R, dtype=torch.int32)
+            sk.tables[(R,)](lens, iend, takes, selected, desc, ft, dg, cl, CAP, MAXTAKE, SCRATCH, FP, S, W,
+                            triton.next_power_of_2(FP), shared, num_warps=4)
+            norm = torch.zeros((R, WIDTH))
+            sk.normalize[(R, -(-WIDTH // 256))](raw, lens, iend, takes, selected, members, norm, MAXTAKE, WIDTH,
+                                               STRIDE, S, W, 256, shared, num_warps=4)
+            out.update({pre + f"ft{shared}": ft, pre + f"dg{shared}": dg, pre + f"cl{shared}": cl,
+                        pre + f"norm{shared}": norm})
+        logical = torch.zeros((R, TOP), dtype=torch.int32)
+        slots = torch.zeros((R, TOP), dtype=torch.int32)
+        sk.map_topk[(R,)](ids, values, lens, iend, takes, selected, members, nt, logical, slots, MAXTAKE, TOP, S, W,
+                          triton.next_power_of_2(TOP), num_warps=4)
+        out.update({pre + "logical": logical, pre + "slots": slots})
+    save("shared_tail", **out)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
@@ -515,7 +577,11 @@ def main():
     jobs = dict(sort=lambda: gen_sort(fg), gather=lambda: gen_gather(nk),
                 pages=lambda: gen_pages(dk), tail_meta=lambda: gen_tail_and_meta(dk),
                 select_maps=lambda: gen_select_maps(dk), scores=lambda: gen_scores(dk),
-                route_topk=gen_route_topk_example, build=lambda: gen_build(dk, fg))
+                route_topk=gen_route_topk_example, build=lambda: gen_build(dk, fg),
+                shared_tail=lambda: gen_shared(load("ref_union", Path(args.reference) /
+                                                    "experiments/tail_union_lab_20261021/union.py"),
+                                               load("ref_shared_kernels", Path(args.reference) /
+                                                    "experiments/fine_pool_shared_20261021/kernels.py")))
     for name, job in jobs.items():
         if args.only and name not in args.only.split(","):
             continue
