@@ -1,7 +1,7 @@
 """Benchmark of the V1 query-side selection path on B200 (one process per GPU).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload decode|single|sort|gather|pages|build]
+                    [--workload decode|single|sort|gather|pages|build|shared]
 
 Workloads (synthetic, seeded; shapes of the benchmark configurations):
   decode  128 requests per GPU, context ~U[32K, 128K] tokens, 64 index heads,
@@ -11,7 +11,8 @@ Workloads (synthetic, seeded; shapes of the benchmark configurations):
   single  1024 single-head queries over 64 built pages + 65-token tail
           (2688 candidates), route -> score -> Top-2048 (no gather).
 Component workloads (one line each): sort (_sort + group offsets), gather
-(_gather_slots), pages (page lifecycle), build (index build of 1024 buckets).
+(_gather_slots), pages (page lifecycle), build (index build of 1024 buckets),
+shared (published-end shared-tail preparation of a 4096-row chunk).
 A step is one pass of the whole selection path over one batch.  Three
 independent batches (separate pools, same context lengths) are in flight on three
 streams, in turn, so the gather of one batch overlaps the selection of the next
@@ -539,6 +540,118 @@ def run_build_workload(args, world, rank, device, dist):
     return line
 
 
+def run_shared_workload(args, world, rank, device, dist):
+    """Published-end shared-tail preparation (experiments/tail_union_lab_20261021,
+    fine_pool_shared_20261021) at the reference's configuration: a 4096-row chunk
+    of one request after 65,536 tokens, sink 64, window 2048, published end
+    65,536, 40 selected pages per row.  One step = stage_union + tables (the
+    reference's `prepare`), captured as a graph; diagnostics: stage_union alone
+    for 1024 and 4096 rows, and normalize over the chunk's fine scores."""
+    import numpy as np
+    ST = importlib.import_module("10_20_b200.shared_tail")
+    oracle = importlib.import_module("oracle.v1x_oracle")
+    history, rows, sink, window, take = 65536, (args.requests or 4096), 64, 2048, 40
+    gen = torch.Generator().manual_seed(51 + rank)
+    npg = -(-(history + rows) // 64) + 2
+    k = torch.randn((npg, 64, 128), generator=gen).to(torch.float8_e4m3fn)
+    host = torch.zeros((npg, 8448), dtype=torch.uint8)
+    host[:, :8192] = k.view(torch.uint8).reshape(npg, 8192)
+    host.view(torch.float32)[:, 2048:] = torch.rand((npg, 64), generator=gen) + 0.05
+    src = host.to(device)
+    nt = torch.randperm(npg, generator=gen).to(torch.int32).to(device)
+    lens = torch.arange(history + 1, history + rows + 1, dtype=torch.int32, device=device)
+    end = torch.tensor([history], dtype=torch.int32, device=device)
+    cap = 64
+    union_cap = 1 + -(-(history + rows) // 64) - (history - window) // 64 + 2
+    fine = torch.zeros((cap + union_cap, 8448), dtype=torch.uint8, device=device)
+    meta = torch.zeros((rows, 3), dtype=torch.int32, device=device)
+    desc = torch.zeros(4, dtype=torch.int32, device=device)
+    c_max = oracle.shared_bounds(history + rows, history, sink, window)[2]
+    width = -(-(take * 64 + c_max + 128) // 256) * 256
+    fp = width // 64
+    takes = torch.full((rows,), take, dtype=torch.int32, device=device)
+    selected = ((torch.arange(take, device=device)[None, :] + torch.arange(rows, device=device)[:, None]) % cap).int()
+    ft = torch.zeros((rows, fp), dtype=torch.int32, device=device)
+    dg = torch.zeros(rows, dtype=torch.int32, device=device)
+    cl = torch.zeros(rows, dtype=torch.int32, device=device)
+    stage = ST.PreparedStage(src, nt, lens, end, fine[cap:], meta, desc, sink, window)
+
+    def prepare():
+        stage()
+        ST.tables[(rows,)](lens, end, takes, selected, desc, ft, dg, cl, cap, take, 0, fp, sink, window, fp, True)
+
+    # 20 prepares per captured graph (as the reference's do_bench_cudagraph
+    # measures), so a replay's launch cost is spread over them
+    per_graph = 20
+
+    def prepare_n():
+        for _ in range(per_graph):
+            prepare()
+
+    g = _capture(prepare_n, device)
+    ms, clk = _timed_replays(g, args.steps, args.warmup, dist, device)
+    ms /= per_graph
+    value = rows * args.steps * world / (ms / 1e3)
+    desc_h = desc.cpu().numpy()
+    union_pages = int(desc_h[3])
+    bytes_per_step = union_pages * 8448 * 2 + rows * (3 + fp + 2) * 4 + rows * take * 4 + rows * 4
+    # diagnostics: the union staging alone (1024 and the full chunk) and normalize
+    diag = {}
+    for r_sub in sorted({1024, rows}):
+        sub = ST.PreparedStage(src, nt, lens[:r_sub], end, fine[cap:], meta[:r_sub], desc, sink, window)
+
+        def sub_n(sub=sub):
+            for _ in range(per_graph):
+                sub()
+
+        gs = _capture(sub_n, device)
+        ms_s, _ = _timed_replays(gs, 50, 5, None, device)
+        diag[f"stage_union_us_rows_{r_sub}"] = ms_s / (50 * per_graph) * 1e3
+    members = torch.randint(0, history, (cap, 64), generator=gen, dtype=torch.int32).to(device)
+    raw = torch.randn((rows, width), generator=gen).to(device)
+    norm = torch.empty_like(raw)
+    gn = _capture(lambda: ST.normalize[(rows, width // 256)](raw, lens, end, takes, selected, members, norm, take,
+                                                             width, width, sink, window, 256, True), device)
+    ms_n, _ = _timed_replays(gn, 50, 3, None, device)
+    diag["normalize_us"] = ms_n / 50 * 1e3
+    # parity spot check: the union, bounds and tables against the oracle
+    prepare()
+    torch.cuda.synchronize()
+    e_dst, e_meta, e_desc = oracle.stage_union(host.numpy(), nt.cpu().numpy(), lens.cpu().numpy(), history,
+                                               union_cap, sink, window)
+    e_ft, e_dg, e_cl = oracle.shared_tables(lens.cpu().numpy(), history, takes.cpu().numpy(),
+                                            selected.cpu().numpy(), e_desc, cap, take, 0, fp, sink, window, True)
+    tot = int(e_desc[3])
+    parity = bool(np.array_equal(fine[cap:cap + tot].cpu().numpy(), e_dst[:tot])
+                  and np.array_equal(meta.cpu().numpy(), e_meta) and np.array_equal(desc_h, e_desc)
+                  and np.array_equal(ft.cpu().numpy(), e_ft) and np.array_equal(dg.cpu().numpy(), e_dg)
+                  and np.array_equal(cl.cpu().numpy(), e_cl))
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        hn, ntn, ln = host.numpy(), nt.cpu().numpy(), lens.cpu().numpy()
+        tk, sl = takes.cpu().numpy(), selected.cpu().numpy()
+
+        def cpu_prepare():
+            _, _, dd = oracle.stage_union(hn, ntn, ln, history, union_cap, sink, window)
+            oracle.shared_tables(ln, history, tk, sl, dd, cap, take, 0, fp, sink, window, True)
+
+        rate, n, el = _cpu_rate(cpu_prepare, rows)
+        cpu = {"value": rate, "unit": "rows/s", "cores": 1, "kind": "port",
+               "sample": f"{n} calls of the whole {rows}-row prepare, oracle (numpy), {el:.1f} s"}
+    line = _component_line(args, world, "shared-tail prepared rows/s (stage_union + tables)", "rows/s", value,
+                           args.steps, ms, clk,
+                           {"workload": "shared", "history": history, "rows": rows, "sink": sink, "window": window,
+                            "indexed_end": history, "take": take, "union_pages": union_pages, "width": width,
+                            "bytes_per_step": bytes_per_step,
+                            "l2": "small working set (union 0.8 MB): replays run from L2; latency-bound"},
+                           bytes_per_step, "stage_union_kernel + shared_tables_kernel", 2, cpu, parity)
+    line["us_per_step"] = ms / args.steps * 1e3
+    line["prepares_per_graph"] = per_graph
+    line["gpu_launches"] = 2 * per_graph * args.steps
+    line["diagnostics"] = diag
+    return line
+
+
 def run_component(args):
     world, rank, device, dist = _dist_setup()
     importlib.import_module("10_20_b200").load()
@@ -548,6 +661,8 @@ def run_component(args):
         line = run_gather_workload(args, world, rank, device, dist)
     elif args.workload == "build":
         line = run_build_workload(args, world, rank, device, dist)
+    elif args.workload == "shared":
+        line = run_shared_workload(args, world, rank, device, dist)
     else:
         line = run_pages_workload(args, world, rank, device, dist)
     if rank == 0:
@@ -567,15 +682,16 @@ def main():
                     help="override the per-GPU batch (small cases for profiling; not a bench config)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="decode",
-                    choices=["decode", "single", "sort", "gather", "pages", "build"],
+                    choices=["decode", "single", "sort", "gather", "pages", "build", "shared"],
                     help="decode (the headline), single (1024 single-head queries), sort (_sort, 256 x 65,536 "
                          "records), gather (_gather_slots, 1024 x 2048 slots of 576 bf16), pages (page "
-                         "lifecycle), build (index build, 1024 buckets per step)")
+                         "lifecycle), build (index build, 1024 buckets per step), shared (published-end "
+                         "shared-tail preparation, 4096-row chunk)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--inflight", type=int, default=3,
                     help="independent batches in flight (the gather of one overlaps the selection of the next)")
     args = ap.parse_args()
-    if args.workload in ("sort", "gather", "pages", "build"):
+    if args.workload in ("sort", "gather", "pages", "build", "shared"):
         return run_component(args)
     cfg = workload_cfg(args.workload)
     if args.requests:
