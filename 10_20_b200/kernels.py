@@ -43,7 +43,10 @@ def status_word(device: torch.device) -> torch.Tensor:
     with _status_lock:
         t = _status.get(idx)
         if t is None:
-            t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+            # a normal tensor even when first asked for under inference mode, so
+            # that check_status can reset it anywhere
+            with torch.inference_mode(False):
+                t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
             _status[idx] = t
     return t
 

@@ -81,7 +81,8 @@ class PageArena:
         self.matches = torch.zeros(16, dtype=torch.int32, device=d)
         self.new = torch.zeros(16, dtype=torch.bool, device=d)
         self.meta = torch.zeros(3, dtype=torch.int32, device=d)
-        self.status = torch.zeros(1, dtype=torch.int32, device=d)
+        with torch.inference_mode(False):   # check() resets it in place from any mode
+            self.status = torch.zeros(1, dtype=torch.int32, device=d)
         self.graphs = graphs
         self._graph = None
 
