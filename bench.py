@@ -692,6 +692,13 @@ def main():
                     help="independent batches in flight (the gather of one overlaps the selection of the next)")
     args = ap.parse_args()
     if args.workload in ("sort", "gather", "pages", "build", "shared"):
+        if args.impl == "reference":
+            if int(os.environ.get("RANK", "0")) == 0:
+                print(json.dumps({"impl": "reference", "workload": args.workload,
+                                  "unavailable": "the reference arm times the decode and single workloads; each "
+                                                 "component line carries its CPU port timing in cpu_baseline"}),
+                      flush=True)
+            return 0
         return run_component(args)
     cfg = workload_cfg(args.workload)
     if args.requests:
