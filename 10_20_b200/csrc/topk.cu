@@ -29,14 +29,11 @@ namespace v1x {
 namespace {
 
 constexpr int kTopkThreads = 512;
-constexpr int kTopkWarps = kTopkThreads / 32;
 constexpr int kTopkMaxSmemKeys = 48 * 1024;  // 192 KB of staged keys per CTA
 constexpr uint32_t kNegInfKey = 0x007FFFFFu;  // order_key(-inf)
-constexpr int kRankCache = kTopkMaxSmemKeys / 64;  // ranks whose page ids live in smem
 constexpr int kStageTake = 128;    // ranks whose 64 members are staged (32 KB)
 constexpr int kStageNt = 4096;     // native-table entries staged (16 KB)
 constexpr int kRegKeys = 16;       // keys per thread kept in registers (cols <= 8192)
-constexpr int kMaxSlices = kTopkMaxSmemKeys / kTopkThreads;
 constexpr int kMaskQueue = 256;
 constexpr int kMaxBin = 2048;      // threshold-bin keys resolved exactly (else bitwise search)
 constexpr int kSmallBin = 96;      // bins up to this size are ranked pairwise directly
@@ -75,7 +72,22 @@ struct RowCtx {
   int n, take, sink, tail, L;
 };
 
+// Per-CTA geometry.  512 threads: rows of up to 48K staged keys.  256 threads
+// (mode 2 only, rows of up to 4096 keys): a quarter of the shared memory, so four
+// CTAs fit an SM when a batch has many more rows than SMs.
+template <int kThreads>
+struct TopkShape {
+  static constexpr int kWarps = kThreads / 32;
+  static constexpr int kMaxKeys = kThreads >= 512 ? kTopkMaxSmemKeys : 4096;  // staged keys per CTA
+  static constexpr int kRankCache = kMaxKeys / 64;    // ranks whose page ids live in smem
+  static constexpr int kMaxSlices = kMaxKeys / kThreads;
+};
+
+template <int kThreads>
 struct TopkSmem {
+  using Shape = TopkShape<kThreads>;
+  static constexpr int kRankCache = Shape::kRankCache;
+  static constexpr int kWarps = Shape::kWarps;
   int pgc[kRankCache];              // page of rank r used for the mapping
   int rpg[kRankCache];              // reordered page of rank r used for the mask
   uint8_t bflag[kRankCache];        // rank r < take is a boundary bucket
@@ -86,14 +98,14 @@ struct TopkSmem {
     } h;
     struct {
       int2 cand[kMaxBin];           // keys + indices of the threshold bin
-      int2 cnt[kMaxSlices * kTopkWarps];  // per (slice, warp) counts, then their scan
+      int2 cnt[Shape::kMaxSlices * kWarps];  // per (slice, warp) counts, then their scan
     } c;
   } u;
-  uint32_t selbit[kTopkMaxSmemKeys / 32];  // threshold-bin keys that are selected
+  uint32_t selbit[Shape::kMaxKeys / 32];  // threshold-bin keys that are selected
   int hist2[256];                   // second level over the threshold bin
   int2 cand2[kMaxBin2];
-  int warp_tot[kTopkWarps + 1];
-  int4 red[2 * kTopkWarps];
+  int warp_tot[kWarps + 1];
+  int4 red[2 * kWarps];
   int4 res, res2;
   int2 carry;
   int nbnd, ncand, ncand2;
@@ -142,15 +154,20 @@ __device__ __forceinline__ void mask_page(const TopkArgs& a, const RowCtx& c, fl
 // kMode 0: keys read from global memory at every use (rows too long for smem);
 // 1: keys staged in shared memory; 2: staged and also held in registers
 // (cols <= kRegKeys * 512).
-template <int kMode>
-__global__ void __launch_bounds__(kTopkThreads, 2) topk_kernel(const __grid_constant__ TopkArgs a) {
+// kThreads 256 (mode 2 only): four CTAs per SM for batches of many rows.
+template <int kMode, int kThreads>
+__global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 2 : 4) topk_kernel(const __grid_constant__ TopkArgs a) {
+  using Shape = TopkShape<kThreads>;
+  constexpr int kTopkWarps = Shape::kWarps;
+  constexpr int kRankCache = Shape::kRankCache;
+  constexpr int kMaxSlices = Shape::kMaxSlices;
   constexpr bool kStaged = kMode > 0;
   extern __shared__ __align__(16) uint32_t dyn[];
-  __shared__ TopkSmem sm;
+  __shared__ TopkSmem<kThreads> sm;
   uint32_t* keys = dyn;
   int* memb = reinterpret_cast<int*>(dyn) + a.memb_off;
   int* ntab = reinterpret_cast<int*>(dyn) + a.ntab_off;
-  const int tid = threadIdx.x, nt = kTopkThreads;
+  const int tid = threadIdx.x, nt = kThreads;
   const int lane = tid & 31, warp = tid >> 5;
   RowCtx c;
   c.row = blockIdx.x;
@@ -309,7 +326,7 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_kernel(const __grid_cons
     TopBin tb{0, 0, 0};
     if constexpr (kStaged) {
       int* hist = sm.u.h.hist;
-      zero_hist<kTopkThreads>(hist);
+      zero_hist<kThreads>(hist);
       for (int w = tid; w < (c.L + 31) / 32; w += nt) sm.selbit[w] = 0u;
       if (tid < 256) sm.hist2[tid] = 0;
       if (tid == 0) {
@@ -327,7 +344,7 @@ __global__ void __launch_bounds__(kTopkThreads, 2) topk_kernel(const __grid_cons
         for (int i = tid; i < c.L; i += nt) atomicAdd(&hist[bin_of(keys[i])], 1);
       }
       __syncthreads();
-      tb = find_top_bin<kTopkThreads>(a.topk, hist, sm.warp_tot, &sm.res);
+      tb = find_top_bin<kThreads>(a.topk, hist, sm.warp_tot, &sm.res);
       // the histogram is dead: the candidate list reuses its storage.  The bin's
       // key range is tracked while compacting it: a bin of one repeated value
       // (ReLU zeros of single-head scores, for instance) needs no ranking -- its
@@ -591,12 +608,37 @@ extern "C" int v1x_topk(float* scores, int64_t score_stride, int64_t cols, const
   V1X_CHECK_ARG(take_stride <= 65536, "topk: take stride too large");
   // dynamic shared memory of the staged modes: keys | staged members | staged
   // native-table row; rows whose keys alone do not fit take the unstaged mode
-  const int64_t limit = 227 * 1024 - static_cast<int64_t>(sizeof(TopkSmem)) - 1024;
   const int64_t cols_pad = (cols + 3) & ~int64_t(3);
+  const int64_t rank_bound = direct_fine ? fine_table_cols : take_stride;
+  const int64_t stake0 =
+      (reinterpret_cast<uintptr_t>(members) & 15) == 0 ? std::min<int64_t>(rank_bound, kStageTake) : 0;
+  const int64_t snt0 = std::min<int64_t>(pages, kStageNt);
+  const dim3 grid(static_cast<unsigned>(batch));
+  // Many more rows than SMs (1024 single-head queries): 256-thread CTAs, four
+  // per SM, when the row's keys fit their registers and a quarter of an SM's
+  // shared memory.  Otherwise 512 threads, two per SM.
+  if (batch > 2 * static_cast<int64_t>(num_sms()) && cols <= kRegKeys * 256 &&
+      cols <= TopkShape<256>::kMaxKeys) {
+    const int64_t limit4 = 228 * 1024 / 4 - static_cast<int64_t>(sizeof(TopkSmem<256>)) - 1024;
+    int64_t stake = stake0, snt = snt0;
+    auto bytes = [&] { return (cols_pad + stake * 64 + snt) * 4; };
+    if (bytes() > limit4) snt = 0;
+    if (bytes() > limit4) stake = 0;
+    if (bytes() <= limit4) {
+      a.stage_take = static_cast<int>(stake);
+      a.stage_nt = static_cast<int>(snt);
+      a.memb_off = static_cast<int>(cols_pad);
+      a.ntab_off = static_cast<int>(cols_pad + stake * 64);
+      static DeviceOnce once4;
+      if (once4.first())
+        cudaFuncSetAttribute(topk_kernel<2, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(limit4));
+      launch_kernel(topk_kernel<2, 256>, grid, dim3(256), static_cast<size_t>(bytes()), s, a);
+      return launch_status("v1x_topk");
+    }
+  }
+  const int64_t limit = 227 * 1024 - static_cast<int64_t>(sizeof(TopkSmem<kTopkThreads>)) - 1024;
   if (cols <= kTopkMaxSmemKeys && cols_pad * 4 <= limit) {
-    const int64_t rank_bound = direct_fine ? fine_table_cols : take_stride;
-    int64_t stake = (reinterpret_cast<uintptr_t>(members) & 15) == 0 ? std::min<int64_t>(rank_bound, kStageTake) : 0;
-    int64_t snt = std::min<int64_t>(pages, kStageNt);
+    int64_t stake = stake0, snt = snt0;
     auto bytes = [&] { return (cols_pad + stake * 64 + snt) * 4; };
     if (bytes() > limit) snt = 0;
     if (bytes() > limit) stake = 0;
@@ -606,16 +648,18 @@ extern "C" int v1x_topk(float* scores, int64_t score_stride, int64_t cols, const
     a.ntab_off = static_cast<int>(cols_pad + stake * 64);
     static DeviceOnce once;
     if (once.first()) {
-      cudaFuncSetAttribute(topk_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(limit));
-      cudaFuncSetAttribute(topk_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(limit));
+      cudaFuncSetAttribute(topk_kernel<1, kTopkThreads>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(limit));
+      cudaFuncSetAttribute(topk_kernel<2, kTopkThreads>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(limit));
     }
     if (cols <= kRegKeys * kTopkThreads)
-      launch_kernel(topk_kernel<2>, dim3(static_cast<unsigned>(batch)), dim3(kTopkThreads), static_cast<size_t>(bytes()), s, a);
+      launch_kernel(topk_kernel<2, kTopkThreads>, grid, dim3(kTopkThreads), static_cast<size_t>(bytes()), s, a);
     else
-      launch_kernel(topk_kernel<1>, dim3(static_cast<unsigned>(batch)), dim3(kTopkThreads), static_cast<size_t>(bytes()), s, a);
+      launch_kernel(topk_kernel<1, kTopkThreads>, grid, dim3(kTopkThreads), static_cast<size_t>(bytes()), s, a);
   } else {
     a.stage_take = a.stage_nt = a.memb_off = a.ntab_off = 0;
-    launch_kernel(topk_kernel<0>, dim3(static_cast<unsigned>(batch)), dim3(kTopkThreads), 0, s, a);
+    launch_kernel(topk_kernel<0, kTopkThreads>, grid, dim3(kTopkThreads), 0, s, a);
   }
   return launch_status("v1x_topk");
 }

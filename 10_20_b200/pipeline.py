@@ -58,6 +58,12 @@ class SelectionStep:
         self.page_scores = torch.empty((B, c.P), dtype=torch.float32, device=d)
         self.selected = torch.empty((B, c.take), dtype=torch.int32, device=d)
         self.width = c.width
+        # Columns top-k reads: with the fixed page budget a row holds at most
+        # take*64 + sink + max(window, 1024) candidates (the tail spans at most a
+        # window, or the unbuilt remainder of the last bucket); the ratio rule
+        # can take more pages, so it reads the whole row.
+        span = c.take * 64 + 64 + max(c.window, 1024)
+        self.topk_cols = min(self.width, (span + 3) // 4 * 4) if ratio is None else self.width
         self.fine_table = torch.zeros((B, self.width // 64), dtype=torch.int32, device=d)
         self.scores = torch.empty((B, self.width), dtype=torch.float32, device=d)
         self.physical = torch.empty((B, c.topk), dtype=torch.int32, device=d)
@@ -112,7 +118,7 @@ class SelectionStep:
         c = self.case
         scoring.fp8_paged_mqa_logits(c.q8[rs], c.fine, c.w[rs], self.dg_lens[rs], self.fine_table[rs], None,
                                      self.width, out=self.scores[rs], clean_logits=False)
-        self.fused.topk(self.scores[rs], self.fine_lens[rs], c.members, c.reordered_table[rs],
+        self.fused.topk(self.scores[rs, :self.topk_cols], self.fine_lens[rs], c.members, c.reordered_table[rs],
                         c.native_table[rs], self.selected[rs], c.lens[rs], self.takes[rs], self.physical[rs],
                         self.logical[rs], self.raw[rs], c.window, True, self.expanded[rs], True, True,
                         self.fine_table[rs], False)

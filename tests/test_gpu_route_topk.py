@@ -183,6 +183,34 @@ def test_topk_random(L, T, tie, cuda_dev):
             assert np.array_equal(exp.cpu().numpy(), e["expanded"])
 
 
+@pytest.mark.parametrize("L,cols,T", [(2688, 3648, 2048), (4096, 4096, 2048), (1500, 2000, 1024)])
+@pytest.mark.parametrize("tie", ["float", "zeros"])
+def test_topk_many_rows(L, cols, T, tie, cuda_dev):
+    """More rows than two waves of SMs and rows of at most 4096 columns: the
+    256-thread variant (four CTAs per SM) -- same results as the oracle,
+    including strided score rows (a column slice of a wider buffer)."""
+    rng = np.random.default_rng(L + cols + len(tie))
+    B, take = 320, 12
+    members, rt, nt, selected, lens, takes, scores, fl, ft = _topk_case(rng, B, L, T, take, tie=tie)
+    wide = np.full((B, cols + 64), 7.0, np.float32)
+    wide[:, :scores.shape[1]] = scores
+    work = dev(wide)
+    phys = torch.full((B, T), -9, dtype=torch.int32, device="cuda")
+    logical, raw = torch.full_like(phys, -9), torch.full_like(phys, -9)
+    noexp = torch.empty_strided((B, 0), (0, 1), device="cuda", dtype=torch.int32)
+    qf.module().topk(work[:, :cols], dev(np.minimum(fl, cols).astype(np.int32)), dev(members), dev(rt), dev(nt),
+                     dev(selected), dev(lens), dev(takes), phys, logical, raw, 64, True, noexp, True, True, dev(ft),
+                     False)
+    fl2 = np.minimum(fl, cols).astype(np.int32)
+    e = O.topk(wide[:, :cols].copy(), fl2, members, rt, nt, selected, lens, takes, 64, True, T, 0, True, True, ft,
+               False)
+    assert np.array_equal(work[:, :cols].cpu().numpy(), e["scores"])
+    assert np.array_equal(raw.cpu().numpy(), e["raw"])
+    assert np.array_equal(logical.cpu().numpy(), e["logical"])
+    assert np.array_equal(phys.cpu().numpy(), e["physical"])
+    assert bool((work[:, cols:] == 7.0).all())
+
+
 def test_topk_streaming_path_and_all_neginf(cuda_dev):
     """Rows wider than the shared-memory stage (60000 cols) and all -inf rows."""
     rng = np.random.default_rng(3)
