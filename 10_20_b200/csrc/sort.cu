@@ -80,6 +80,7 @@ __global__ void __launch_bounds__(kThreads) sort_radix_kernel(const int32_t* __r
     typename Scan::TempStorage scan;
   } temp;
   __shared__ uint32_t red_and[kThreads / 32], red_or[kThreads / 32];
+  __shared__ int red_min[kThreads / 32];
   if (*flag >= 0) return;
   constexpr int N = kThreads * kItems;
   const int64_t base = static_cast<int64_t>(blockIdx.y) * 4096 + static_cast<int64_t>(blockIdx.x) * N;
@@ -98,12 +99,32 @@ __global__ void __launch_bounds__(kThreads) sort_radix_kernel(const int32_t* __r
 #pragma unroll
     for (int k = 0; k < kItems; ++k) s[k] = S[base + i0 + k];
   }
+  // Integer scores (group ids carried as floats): when every score of the segment
+  // is an integer of magnitude <= 2^24, v - min is an order-preserving key (-0 and
+  // +0 both map to 0, as the ordered key folds them) spanning far fewer bits than
+  // the float bit patterns (12 instead of ~19 for ids 0..4095), so fewer passes.
+  bool ints = true;
+  int imin = 0x7FFFFFFF;
+#pragma unroll
+  for (int k = 0; k < kItems; ++k) {
+    const bool is_int = fabsf(s[k]) <= 16777216.0f && s[k] == truncf(s[k]);  // false for NaN / inf
+    ints = ints && is_int;
+    if (is_int) imin = min(imin, static_cast<int>(s[k]));
+  }
+  ints = __syncthreads_and(ints) != 0;
+  if (ints) {
+    imin = __reduce_min_sync(0xffffffffu, imin);
+    if ((threadIdx.x & 31) == 0) red_min[threadIdx.x >> 5] = imin;
+    __syncthreads();
+#pragma unroll
+    for (int w = 0; w < kThreads / 32; ++w) imin = min(imin, red_min[w]);
+  }
   uint32_t key[kItems];
   int pos[kItems];
   uint32_t kand = 0xFFFFFFFFu, kor = 0u;
 #pragma unroll
   for (int k = 0; k < kItems; ++k) {
-    key[k] = ordered_score(s[k]);
+    key[k] = ints ? static_cast<uint32_t>(static_cast<int>(s[k]) - imin) : ordered_score(s[k]);
     pos[k] = i0 + k;
     kand &= key[k];
     kor |= key[k];
@@ -142,6 +163,13 @@ __global__ void __launch_bounds__(kThreads) sort_radix_kernel(const int32_t* __r
     int nvalid = 0, last = -1;
 #pragma unroll
     for (int k = 0; k < kItems; ++k) {
+      if (ints) {
+        const int ki = static_cast<int>(key[k]) + imin;
+        v[k] = ki >= 0 && ki < key_range ? ki : -1;
+        nvalid += v[k] >= 0;
+        if (v[k] >= 0) last = v[k];
+        continue;
+      }
       const uint32_t b = (key[k] & 0x80000000u) ? (key[k] ^ 0x80000000u) : ~key[k];
       const float x = __uint_as_float(b);
       const int ki = static_cast<int>(x);
