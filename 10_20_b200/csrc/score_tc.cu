@@ -12,6 +12,12 @@
 //   Q[H x 128]^T with tcgen05.mma kind::f8f6f4 (E4M3 x E4M3 -> F32), four K=32
 //   steps, accumulator in TMEM (four accumulators in flight).
 //
+// One head (2 FLOP per key byte) also runs here: the per-key dot products are
+// what bounds a CUDA-core scorer (~90 instructions per 16 key bytes), and on
+// the tensor cores they cost nothing.  The MMA takes its smallest N, 16: the q
+// box is the row's query and the next 15 rows' (zero past the batch), and the
+// epilogue reads only column 0 of the accumulator.
+//
 // Warp roles in a persistent CTA (352 threads, two CTAs per SM):
 //   warps 0-1  TMA producers (alternate tiles): two 8 KB page boxes (3-D tensor
 //              map over the packed pool, 128-byte swizzle) and the two pages'
@@ -61,7 +67,7 @@ struct TcArgs {
   int64_t out_stride, max_len;
   float* page_max;
   int64_t page_stride;
-  int B, H, relu, clean, w_rows, lens_kind;
+  int B, H, N, relu, clean, w_rows, lens_kind;  // N: MMA width (H, or 16 for one head)
   uint32_t tmem_cols;
   int32_t* status;
 };
@@ -129,12 +135,13 @@ __global__ void __launch_bounds__(kTcThreads, 2)
                     const __grid_constant__ CUtensorMap scale_map, const __grid_constant__ TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const uint32_t q_bytes = static_cast<uint32_t>(a.H) * 128;
+  const uint32_t q_bytes = static_cast<uint32_t>(a.N) * 128;
   uint8_t* stages = base;                                               // kTcStages x 16 KB (A operand)
   uint8_t* qring = stages + kTcStages * 16384;                          // kQSlots x H*128 (B operand)
   float* sring = reinterpret_cast<float*>(qring + kQSlots * q_bytes);   // kScaleSlots x 128 scales
   float* wsm = sring + kScaleSlots * 128;                               // head weights of this CTA's rows
-  TcShared& sh = *reinterpret_cast<TcShared*>(wsm + a.w_rows * a.H);
+  TcShared& sh = *reinterpret_cast<TcShared*>(
+      (reinterpret_cast<uintptr_t>(wsm + a.w_rows * a.H) + 15) & ~uintptr_t(15));  // 16-byte aligned
   int* prefix = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(&sh) + sizeof(TcShared));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
@@ -237,7 +244,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   } else if (warp == kMmaWarp) {
     // ---------------- MMA issuer (also loads q at row changes) ----------------
     if (lane == 0 && ntiles > 0) {
-      const uint32_t idesc = idesc_e4m3_f32(128, a.H);
+      const uint32_t idesc = idesc_e4m3_f32(128, a.N);
       TileCursor cur;
       cur.start(prefix, a.B, T0);
       int q_rows = 0, cur_b = -1, it = 0;
@@ -270,7 +277,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         tc_fence_after();
         const uint32_t sa = smem_u32(stages + s * 16384);
         const uint32_t sb = smem_u32(qring + ((q_rows - 1) % kQSlots) * q_bytes);
-        const uint32_t d = tmem + static_cast<uint32_t>(acc * a.H);
+        const uint32_t d = tmem + static_cast<uint32_t>(acc * a.N);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           umma_f8(d, umma_desc_sw128(sa + 32 * k), umma_desc_sw128(sb + 32 * k), idesc, k > 0 ? 1u : 0u);
@@ -312,8 +319,14 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       const float scale = sring[r * 128 + i];
       tc_fence_after();
       float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
-      const uint32_t ta = tmem + (static_cast<uint32_t>(q4 * 32) << 16) + static_cast<uint32_t>(acc * a.H);
-      for (int c0 = 0; c0 < a.H; c0 += 32) {
+      const uint32_t ta = tmem + (static_cast<uint32_t>(q4 * 32) << 16) + static_cast<uint32_t>(acc * a.N);
+      if (a.H == 1) {  // column 0 only: the other 15 belong to the next rows' queries
+        float v0 = __uint_as_float(tmem_ld1(ta));
+        tmem_ld_wait();
+        if (a.relu) v0 = fmaxf(v0, 0.0f);
+        s0 = fmaf(wr[0], v0, s0);
+      }
+      for (int c0 = 0; a.H > 1 && c0 < a.H; c0 += 32) {
         uint32_t v[32];
         tmem_ld32(ta + c0, v);
         tmem_ld_wait();
@@ -402,8 +415,8 @@ int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t 
                  const int32_t* table, int64_t table_stride, float* out, int64_t out_stride, int64_t max_len,
                  float* page_max, int64_t page_stride, int64_t heads, int relu, int clean, int lens_kind,
                  int64_t batch, int32_t* status, cudaStream_t stream) {
-  if (heads % 32 != 0 || heads > 128 || batch > kMaxTcRows || pool_pages >= (int64_t(1) << 31)) {
-    set_error("score_fp8 (tensor core): heads must be a multiple of 32 <= 128 and batch <= %d", kMaxTcRows);
+  if ((heads != 1 && heads % 32 != 0) || heads > 128 || batch > kMaxTcRows || pool_pages >= (int64_t(1) << 31)) {
+    set_error("score_fp8 (tensor core): heads must be 1 or a multiple of 32 <= 128 and batch <= %d", kMaxTcRows);
     return V1X_ERR_UNSUPPORTED;
   }
   if (((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(w)) & 15) != 0) {
@@ -415,6 +428,7 @@ int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t 
     set_error("score_fp8: cuTensorMapEncodeTiled unavailable");
     return V1X_ERR_CUDA;
   }
+  const int64_t n_mma = heads == 1 ? 16 : heads;
   CUtensorMap pool_map, q_map, scale_map;
   {
     // keys: {128 bytes, 64 tokens, pages}, one page per box, 128-byte swizzle
@@ -426,10 +440,11 @@ int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t 
       return rc;
   }
   {
-    // q: {128 bytes, batch*heads rows}, one row's H heads per box
+    // q: {128 bytes, batch*heads rows}, one row's H heads per box (one head:
+    // 16 rows from the row's own, zero-filled past the batch)
     const cuuint64_t dims[2] = {128, static_cast<cuuint64_t>(batch * heads)};
     const cuuint64_t strides[1] = {128};
-    const cuuint32_t box[2] = {128, static_cast<cuuint32_t>(heads)};
+    const cuuint32_t box[2] = {128, static_cast<cuuint32_t>(n_mma)};
     if (int rc = encode(enc, &q_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, q, dims, strides, box,
                         CU_TENSOR_MAP_SWIZZLE_128B, "q"))
       return rc;
@@ -444,7 +459,7 @@ int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t 
       return rc;
   }
   uint32_t cols = 32;
-  while (cols < static_cast<uint32_t>(kMaxAcc * heads)) cols <<= 1;
+  while (cols < static_cast<uint32_t>(kMaxAcc * n_mma)) cols <<= 1;
   const int64_t max_tiles = batch * ((max_len + 127) / 128);
   const int64_t sms = num_sms();
   // head-weight rows staged per CTA: a range of ceil(total/grid) tiles touches at
@@ -452,7 +467,7 @@ int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t 
   // spans more rows reads the weights from global memory)
   auto plan = [&](int64_t grid, int64_t& w_rows) {
     w_rows = std::min<int64_t>({batch, (std::max<int64_t>(max_tiles, 1) + grid - 1) / grid + 1, kMaxWRows});
-    return static_cast<size_t>(1024 + kTcStages * 16384 + kQSlots * heads * 128 + kScaleSlots * 512 +
+    return static_cast<size_t>(1024 + kTcStages * 16384 + kQSlots * n_mma * 128 + kScaleSlots * 512 +
                                w_rows * heads * 4 + sizeof(TcShared) + (batch + 1) * 4 + 16);
   };
   int64_t grid = std::min<int64_t>(sms * 2, std::max<int64_t>(max_tiles, 1)), w_rows = 0;
@@ -466,7 +481,8 @@ int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t 
     return V1X_ERR_UNSUPPORTED;
   }
   TcArgs args{lens, table, table_stride, w, out, out_stride, max_len, page_max, page_stride,
-              static_cast<int>(batch), static_cast<int>(heads), relu, clean, static_cast<int>(w_rows), lens_kind,
+              static_cast<int>(batch), static_cast<int>(heads), static_cast<int>(n_mma), relu, clean,
+              static_cast<int>(w_rows), lens_kind,
               cols, status};
   static DeviceOnce once;
   if (once.first())

@@ -40,7 +40,7 @@ def fp8_paged_mqa_logits(q, kv_cache, weights, context_lens, block_table, schedu
     q: e4m3 [B, H, 128] or [B, 1, H, 128]; kv_cache: packed uint8 [pages, 8448] or
     [pages, 64, 1, 132]; weights: float32 [B, H]; context_lens: int32 [B] or [B, 1];
     block_table: int32 [B, max_blocks].  impl: "auto" (tensor cores when H is a
-    multiple of 32), "simt" (fixed fp32 evaluation order, H <= 64) or "tensor_core".
+    multiple of 32, or 1), "simt" (fixed fp32 evaluation order, H <= 64) or "tensor_core".
     clean_logits=False leaves columns >= context_lens[b] untouched.
     page_max (extension): float32 [B, >= ceil(max_context_len / 8)] receiving the max of
     every 8 consecutive logits (fused.route's page score); logits=False skips the

@@ -80,7 +80,7 @@ def test_score_tensor_core_rejects_unsupported_heads(cuda_dev):
                                impl="tensor_core")
 
 
-@pytest.mark.parametrize("H", [32, 64, 96, 128])
+@pytest.mark.parametrize("H", [1, 32, 64, 96, 128])
 @pytest.mark.parametrize("relu", [True, False])
 def test_score_tensor_core_vs_oracle(H, relu, cuda_dev):
     """tcgen05 scorer: ragged rows (empty, one key, partial tiles, longer than
@@ -196,7 +196,7 @@ def test_selection_step_graph_replay(cuda_dev):
     assert torch.equal(step.physical, ref)
 
 
-@pytest.mark.parametrize("impl,H", [("simt", 1), ("simt", 16), ("tensor_core", 64)])
+@pytest.mark.parametrize("impl,H", [("simt", 1), ("simt", 16), ("tensor_core", 1), ("tensor_core", 64)])
 def test_page_max_and_route_pages(impl, H, cuda_dev):
     """Scoring page maxima + route_pages == route over the centre logits (bit-exact)."""
     rng = np.random.default_rng(H)
