@@ -13,6 +13,22 @@
 //    reference device_asserts on an exhausted arena, this kernel writes
 //    V1X_STATUS_ARENA_EXHAUSTED to a status word and changes nothing.
 //  - publish (:134-167), release (:170-179): as the reference, vectorised.
+//
+// Batched prepare (extension): the buckets of one or more prepares, in the
+// reference's canonical order, in five launches instead of six per bucket --
+// fingerprints of every page; ONE whole-GPU sweep of the arena that lists the
+// live pages whose fingerprint equals a batch page's (a shared-memory hash
+// table of the batch's fingerprints: one probe per live arena page), and the
+// batch pages with an equal fingerprint in an earlier bucket; one warp per
+// listed pair comparing bytes and members, keeping the lowest live match and
+// the earliest equal batch page; one warp that takes the buckets in order and
+// makes the reference's sequential decisions from shared memory -- a page with
+// no live match takes the slot of its earliest equal batch page, fresh pages
+// pop the free stack as allocate does -- and one publish over all buckets.
+// The answers equal the sequential per-bucket calls: refcounts only grow during
+// a prepare, so a page live at the start stays live; a page content is live at
+// most once (a second copy would have matched the first); and a page that is
+// not live at the start can only match a page published inside the batch.
 #include <climits>
 
 #include "common.cuh"
@@ -21,13 +37,24 @@ namespace v1x {
 namespace {
 
 constexpr int kMaxMatchPages = 32;
+constexpr uint8_t kAborted = 2;  // new-page flag of a bucket whose allocation failed
 
+// pages_per_meta: pages sharing one meta record of meta_stride ints (16 and 4
+// for a bucket batch; all pages and 3 for the single-bucket call); match, when
+// given, is reset to "no match" (and first, the batch's earliest-equal page,
+// to "none"; counters, the batch's pair counters and flags, to 0).
 __global__ void __launch_bounds__(256) fingerprint_kernel(const uint8_t* __restrict__ tmp,
                                                           const int32_t* __restrict__ map,
                                                           const int32_t* __restrict__ meta,
-                                                          int64_t* __restrict__ hash) {
-  if (meta[2] == 0) return;
+                                                          int64_t* __restrict__ hash, int64_t pages_per_meta,
+                                                          int meta_stride, int32_t* __restrict__ match,
+                                                          int32_t* __restrict__ first,
+                                                          int32_t* __restrict__ counters) {
   const int64_t p = blockIdx.x;
+  if (match && threadIdx.x == 0) match[p] = INT_MAX;
+  if (first && threadIdx.x == 0) first[p] = INT_MAX;
+  if (counters && p == 0 && threadIdx.x < 4) counters[threadIdx.x] = 0;
+  if (meta[(p / pages_per_meta) * meta_stride + 2] == 0) return;
   const uint4* src = reinterpret_cast<const uint4*>(tmp + p * kPageBytes);
   uint64_t a = 0, b = 0;
   for (int c = threadIdx.x; c < kPageBytes / 16; c += blockDim.x) {
@@ -64,6 +91,22 @@ __global__ void __launch_bounds__(256) fingerprint_kernel(const uint8_t* __restr
     hash[p * 2] = static_cast<int64_t>(ta);
     hash[p * 2 + 1] = static_cast<int64_t>(tb);
   }
+}
+
+// Warp-wide exact comparison of two pages: 8448 bytes and 64 members.
+__device__ __forceinline__ bool warp_pages_equal(const uint8_t* x, const int32_t* xm, const uint8_t* y,
+                                                 const int32_t* ym) {
+  const int lane = threadIdx.x & 31;
+  const uint4* a = reinterpret_cast<const uint4*>(x);
+  const uint4* b = reinterpret_cast<const uint4*>(y);
+  bool diff = false;
+  for (int c = lane; c < kPageBytes / 16; c += 32) {
+    const uint4 u = a[c], v = b[c];
+    diff |= (u.x != v.x) | (u.y != v.y) | (u.z != v.z) | (u.w != v.w);
+  }
+  diff |= xm[lane] != ym[lane];
+  diff |= xm[lane + 32] != ym[lane + 32];
+  return !__any_sync(0xffffffffu, diff);
 }
 
 __global__ void match_init_kernel(const int32_t* __restrict__ meta, int32_t* __restrict__ match,
@@ -110,17 +153,9 @@ __global__ void __launch_bounds__(256) match_scan_kernel(
       while (pmask) {
         const int p = __ffs(pmask) - 1;
         pmask &= pmask - 1;
-        // warp-wide exact comparison of 8448 bytes and 64 members
-        const uint4* x = reinterpret_cast<const uint4*>(tmp + static_cast<int64_t>(p) * kPageBytes);
-        const uint4* y = reinterpret_cast<const uint4*>(fine + jc * kPageBytes);
-        bool diff = false;
-        for (int c = lane; c < kPageBytes / 16; c += 32) {
-          const uint4 u = x[c], v = y[c];
-          diff |= (u.x != v.x) | (u.y != v.y) | (u.z != v.z) | (u.w != v.w);
-        }
-        diff |= map[p * 64 + lane] != members[jc * 64 + lane];
-        diff |= map[p * 64 + lane + 32] != members[jc * 64 + lane + 32];
-        if (!__any_sync(0xffffffffu, diff) && lane == 0) atomicMin(&match[p], static_cast<int32_t>(jc));
+        const bool eq = warp_pages_equal(tmp + static_cast<int64_t>(p) * kPageBytes, map + p * 64,
+                                         fine + jc * kPageBytes, members + jc * 64);
+        if (eq && lane == 0) atomicMin(&match[p], static_cast<int32_t>(jc));
       }
     }
   }
@@ -139,6 +174,8 @@ __global__ void allocate_kernel(const int32_t* __restrict__ meta, const int32_t*
   const int needed = __popc(fm);
   const int cnt = *count;
   if (cnt < needed) {
+    // nothing changes; the flags tell publish that the bucket was not allocated
+    if (lane < 16) new_flags[lane] = kAborted;
     if (lane == 0 && status) *status = V1X_STATUS_ARENA_EXHAUSTED;
     return;
   }
@@ -157,9 +194,19 @@ __global__ void __launch_bounds__(256) publish_kernel(
     const int32_t* __restrict__ map, const int64_t* __restrict__ hash,
     const int32_t* __restrict__ meta, const int32_t* __restrict__ tables,
     const uint8_t* __restrict__ new_flags, uint8_t* __restrict__ fine, uint8_t* __restrict__ centers,
-    float* __restrict__ cs, int32_t* __restrict__ members, int64_t* __restrict__ hashes) {
+    float* __restrict__ cs, int32_t* __restrict__ members, int64_t* __restrict__ hashes, int meta_stride) {
+  // block = (bucket, page): the single-bucket call launches 16 blocks
+  const int64_t b = blockIdx.x / 16;
+  const int p = blockIdx.x % 16;
+  meta += b * meta_stride;
   if (meta[2] == 0) return;
-  const int p = blockIdx.x;
+  tmp += b * 16 * kPageBytes;
+  tc += b * 2 * kPageBytes;
+  tcs += b * 2 * kPageWords;
+  map += b * 16 * 64;
+  hash += b * 16 * 2;
+  new_flags += b * 16;
+  if (new_flags[p] == kAborted) return;  // allocation failed: the bucket changes nothing
   const int64_t lease = meta[1];
   if (new_flags[p]) {
     const int64_t dst = tables[lease * 16 + p];
@@ -196,7 +243,350 @@ __global__ void release_kernel(const int32_t* __restrict__ table, int32_t* __res
   if (dead) free_stack[base + rank] = page;
 }
 
+// ---------------------------------------------------------------------------
+// Batched prepare: buckets of one or more prepares in one pass (see the header)
+// ---------------------------------------------------------------------------
+constexpr int kBatchBuckets = 64;                 // buckets per call
+constexpr int kBatchPages = kBatchBuckets * 16;   // pages per call
+constexpr int kQTable = 2 * kBatchPages;          // hash-table slots (load <= 1/2)
+constexpr uint32_t kQMask = kQTable - 1;
+constexpr int kBatchMeta = 4;                     // per bucket: token start, lease, active, state row
+constexpr int kPairCap = 4 * kBatchPages;         // hash-equal pairs kept per list
+// work ints: counters and flags, arena pairs, batch pairs, earliest equal page
+constexpr int kWorkHead = 4;
+constexpr int kWorkInts = kWorkHead + 2 * kPairCap + 2 * kPairCap + kBatchPages;
+static_assert(kWorkInts == V1X_PREPARE_WORK_INTS, "v1x.h states the work size");
+constexpr int kFlagArenaOverflow = 1;
+constexpr int32_t kFirstNone = INT_MAX, kFirstCollision = -2;  // values of BatchWork::first
+
+struct BatchWork {
+  int32_t* head;     // [0] arena pairs, [1] batch pairs, [2] overflow flags
+  int2* arena;       // (arena page j, batch page q) with equal fingerprints
+  int2* batch;       // (q', q): q' the lowest earlier-bucket batch page with q's fingerprint
+  int32_t* first;    // q' if its bytes equal q's; kFirstNone; kFirstCollision (search in decide)
+  __device__ explicit BatchWork(int32_t* w)
+      : head(w),
+        arena(reinterpret_cast<int2*>(w + kWorkHead)),
+        batch(reinterpret_cast<int2*>(w + kWorkHead) + kPairCap),
+        first(w + kWorkHead + 4 * kPairCap) {}
+};
+
+__device__ __forceinline__ uint32_t fp_slot(int64_t h0, int64_t h1) {
+  uint64_t x = static_cast<uint64_t>(h0) * 0x9E3779B97F4A7C15ull ^ static_cast<uint64_t>(h1);
+  x ^= x >> 29;
+  return static_cast<uint32_t>(x >> 32) & kQMask;
+}
+
+// Inserts page q (entry q + 1; 0 = empty) by linear probing.
+__device__ __forceinline__ void fp_insert(int32_t* table, uint32_t slot, int q) {
+  while (atomicCAS(&table[slot], 0, q + 1) != 0) slot = (slot + 1) & kQMask;
+}
+
+// Shared-memory hash table of the batch's active pages, in every CTA.
+struct QueryTable {
+  int64_t h0[kBatchPages], h1[kBatchPages];
+  int32_t slot[kQTable];
+};
+
+__device__ void build_query_table(QueryTable& t, const int64_t* hash, const int32_t* meta, int nq) {
+  for (int i = threadIdx.x; i < kQTable; i += blockDim.x) t.slot[i] = 0;
+  for (int q = threadIdx.x; q < nq; q += blockDim.x) {
+    t.h0[q] = hash[2 * q];
+    t.h1[q] = hash[2 * q + 1];
+  }
+  __syncthreads();
+  for (int q = threadIdx.x; q < nq; q += blockDim.x)
+    if (meta[(q / 16) * kBatchMeta + 2] != 0) fp_insert(t.slot, fp_slot(t.h0[q], t.h1[q]), q);
+  __syncthreads();
+}
+
+// Next batch page after `slot` on the probe chain with fingerprint (a, b), or
+// -1 at the end of the chain (slot becomes -1 too).
+__device__ __forceinline__ int next_equal(const QueryTable& t, int& slot, int64_t a, int64_t b) {
+  while (slot >= 0) {
+    const int e = t.slot[slot];
+    if (e == 0) {
+      slot = -1;
+      return -1;
+    }
+    slot = static_cast<int>((slot + 1) & kQMask);
+    if (t.h0[e - 1] == a && t.h1[e - 1] == b) return e - 1;
+  }
+  return -1;
+}
+
+// The arena sweep with every hash hit confirmed by the warp that found it (the
+// exact path when the pair list overflows).
+__device__ void sweep_inline(const QueryTable& t, const uint8_t* tmp, const int32_t* map, const uint8_t* fine,
+                             const int32_t* members, const int64_t* hashes, const int32_t* refs, int32_t* match,
+                             int64_t cap) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  const int64_t gw = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  for (int64_t base = gw * 32; base < cap; base += warps * 32) {
+    const int64_t j = base + lane;
+    int64_t a = 0, b = 0;
+    int slot = -1;
+    if (j < cap && refs[j] > 0) {
+      a = hashes[j * 2];
+      b = hashes[j * 2 + 1];
+      slot = static_cast<int>(fp_slot(a, b));
+    }
+    while (true) {
+      const int cand = next_equal(t, slot, a, b);
+      unsigned todo = __ballot_sync(0xffffffffu, cand >= 0);
+      if (!todo) break;
+      while (todo) {
+        const int src = __ffs(todo) - 1;
+        todo &= todo - 1;
+        const int q = __shfl_sync(0xffffffffu, cand, src);
+        const int64_t jc = base + src;
+        const bool eq = warp_pages_equal(tmp + static_cast<int64_t>(q) * kPageBytes, map + q * 64,
+                                         fine + jc * kPageBytes, members + jc * 64);
+        if (eq && lane == 0) atomicMin(&match[q], static_cast<int32_t>(jc));
+      }
+    }
+  }
+}
+
+// Hash-equal pairs: every live arena page whose fingerprint equals a batch
+// page's, and for every batch page the lowest page of an earlier bucket with
+// the same fingerprint (one pair per page, whatever the number of copies).  No
+// bytes are compared here; confirm_kernel does that in parallel.
+__global__ void __launch_bounds__(256) match_batch_kernel(const int64_t* __restrict__ hash,
+                                                          const int32_t* __restrict__ meta,
+                                                          const int64_t* __restrict__ hashes,
+                                                          const int32_t* __restrict__ refs, int64_t cap, int nq,
+                                                          int32_t* __restrict__ work) {
+  __shared__ QueryTable t;
+  BatchWork w(work);
+  build_query_table(t, hash, meta, nq);
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  for (int64_t j = tid; j < cap; j += stride) {
+    if (refs[j] <= 0) continue;
+    const int64_t a = hashes[j * 2], b = hashes[j * 2 + 1];
+    int slot = static_cast<int>(fp_slot(a, b));
+    for (int q = next_equal(t, slot, a, b); q >= 0; q = next_equal(t, slot, a, b)) {
+      const int k = atomicAdd(&w.head[0], 1);
+      if (k < kPairCap) w.arena[k] = make_int2(static_cast<int>(j), q);
+      else atomicOr(&w.head[2], kFlagArenaOverflow);
+    }
+  }
+  for (int64_t q = tid; q < nq; q += stride) {
+    if (meta[(q / 16) * kBatchMeta + 2] == 0) continue;
+    const int64_t a = t.h0[q], b = t.h1[q];
+    int slot = static_cast<int>(fp_slot(a, b));
+    int lowest = INT_MAX;
+    for (int p = next_equal(t, slot, a, b); p >= 0; p = next_equal(t, slot, a, b))
+      if (p / 16 < q / 16) lowest = min(lowest, p);  // earlier buckets only
+    if (lowest != INT_MAX) w.batch[atomicAdd(&w.head[1], 1)] = make_int2(lowest, static_cast<int>(q));
+  }
+}
+
+// One warp per pair compares the bytes and members: the lowest confirmed arena
+// page is the live match; a batch page whose lowest equal-fingerprint earlier
+// page has equal bytes takes it as its earliest equal page, and one whose bytes
+// differ (a fingerprint collision) is left to decide_kernel's exact search.  If
+// the arena list overflowed, the sweep runs again with inline confirmation
+// instead (exact, slower).
+__global__ void __launch_bounds__(256) confirm_kernel(const uint8_t* __restrict__ tmp, const int32_t* __restrict__ map,
+                                                      const int64_t* __restrict__ hash, const int32_t* __restrict__ meta,
+                                                      const uint8_t* __restrict__ fine,
+                                                      const int32_t* __restrict__ members,
+                                                      const int64_t* __restrict__ hashes,
+                                                      const int32_t* __restrict__ refs, int32_t* __restrict__ match,
+                                                      int64_t cap, int nq, int32_t* __restrict__ work) {
+  BatchWork w(work);
+  const int flags = w.head[2];
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  const int64_t gw = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int na = min(w.head[0], kPairCap), nb = min(w.head[1], kPairCap);
+  if (flags & kFlagArenaOverflow) {
+    __shared__ QueryTable t;
+    build_query_table(t, hash, meta, nq);
+    sweep_inline(t, tmp, map, fine, members, hashes, refs, match, cap);
+  } else {
+    for (int64_t k = gw; k < na; k += warps) {
+      const int2 pr = w.arena[k];
+      const bool eq = warp_pages_equal(tmp + static_cast<int64_t>(pr.y) * kPageBytes, map + pr.y * 64,
+                                       fine + static_cast<int64_t>(pr.x) * kPageBytes, members + pr.x * 64);
+      if (eq && lane == 0) atomicMin(&match[pr.y], pr.x);
+    }
+  }
+  for (int64_t k = gw; k < nb; k += warps) {
+    const int2 pr = w.batch[k];
+    const bool eq = warp_pages_equal(tmp + static_cast<int64_t>(pr.y) * kPageBytes, map + pr.y * 64,
+                                     tmp + static_cast<int64_t>(pr.x) * kPageBytes, map + pr.x * 64);
+    if (lane == 0) w.first[pr.y] = eq ? pr.x : kFirstCollision;
+  }
+}
+
+// The sequential part, one warp: buckets in order, lanes 0-15 = the bucket's
+// pages.  A page without a live match takes the slot of its earliest equal
+// page in an earlier bucket of the batch (that page was fresh: an equal page
+// with a live match would have given this page the same match; after a
+// fingerprint collision the fresh pages so far are searched and compared
+// here, in a shared-memory hash table of them); then the
+// reference's allocate (fresh pages pop FREE[count-1-rank], staged in shared
+// memory from the top of the stack), refcounts, lease table and new-page
+// flags.  The first bucket that finds the free stack too short writes
+// V1X_STATUS_ARENA_EXHAUSTED and it and every later bucket change nothing
+// (flags = aborted).  With state_tables, the request's page-table row (state
+// row from the meta record) and centre-table row receive the bucket's pages,
+// as the driver's copies of the lease tables do after each reference Build.
+struct StateRows {
+  int32_t* tables;
+  int64_t table_stride;
+  int32_t* centers;
+  int64_t center_stride;
+  const int32_t* center_pages;
+};
+
+__global__ void __launch_bounds__(128) decide_kernel(
+    const uint8_t* __restrict__ tmp, const int32_t* __restrict__ map, const int64_t* __restrict__ hash,
+    const int32_t* __restrict__ meta, const int32_t* __restrict__ match, int nb, const int32_t* __restrict__ free_stack,
+    int32_t* __restrict__ count, int32_t* __restrict__ refs, int32_t* __restrict__ tables,
+    uint8_t* __restrict__ new_flags, int32_t* __restrict__ status, const StateRows rows,
+    const int32_t* __restrict__ work) {
+  __shared__ int64_t sh0[kBatchPages], sh1[kBatchPages];
+  __shared__ int32_t sdst[kBatchPages];   // live match (INT_MAX: none), then the page's arena slot
+  __shared__ int32_t sfirst[kBatchPages]; // BatchWork::first
+  __shared__ int32_t sfree[kBatchPages];  // sfree[i] = FREE[count0 - 1 - i]
+  __shared__ int32_t table[kQTable];      // fresh pages so far (searched after a collision)
+  __shared__ int32_t smeta[kBatchBuckets * kBatchMeta];
+  const BatchWork w(const_cast<int32_t*>(work));
+  const int nq = nb * 16;
+  const int cnt0 = *count;
+  for (int i = threadIdx.x; i < kQTable; i += blockDim.x) table[i] = 0;
+  for (int q = threadIdx.x; q < nq; q += blockDim.x) {
+    sh0[q] = hash[2 * q];
+    sh1[q] = hash[2 * q + 1];
+    sdst[q] = match[q];
+    sfirst[q] = w.first[q];
+  }
+  for (int i = threadIdx.x; i < min(nq, cnt0); i += blockDim.x) sfree[i] = free_stack[cnt0 - 1 - i];
+  for (int i = threadIdx.x; i < nb * kBatchMeta; i += blockDim.x) smeta[i] = meta[i];
+  __syncthreads();
+  if (threadIdx.x >= 32) return;
+  const int lane = threadIdx.x;
+  const uint32_t lt = (1u << lane) - 1u;
+  int cnt = cnt0;
+  bool aborted = false;
+  for (int b = 0; b < nb; ++b) {
+    const int* bm = smeta + b * kBatchMeta;  // token start, lease, active, state row
+    if (bm[2] == 0) continue;                 // inactive bucket: nothing to do
+    const int qi = b * 16 + lane;
+    if (aborted) {
+      if (lane < 16) new_flags[qi] = kAborted;
+      continue;
+    }
+    int m = -1;
+    if (lane < 16 && sdst[qi] != INT_MAX) m = sdst[qi];
+    const int f = lane < 16 ? sfirst[qi] : kFirstNone;
+    if (m < 0 && f >= 0 && f != kFirstNone) m = sdst[f];
+    if (__any_sync(0xffffffffu, lane < 16 && m < 0 && f == kFirstCollision)) {
+      int slot = (lane < 16 && m < 0 && f == kFirstCollision) ? static_cast<int>(fp_slot(sh0[qi], sh1[qi])) : -1;
+      while (true) {
+        int cand = -1;
+        while (slot >= 0) {
+          const int e = table[slot];
+          if (e == 0) {
+            slot = -1;
+            break;
+          }
+          slot = static_cast<int>((slot + 1) & kQMask);
+          if (sh0[e - 1] == sh0[qi] && sh1[e - 1] == sh1[qi]) {
+            cand = e - 1;
+            break;
+          }
+        }
+        unsigned todo = __ballot_sync(0xffffffffu, cand >= 0);
+        if (!todo) break;
+        while (todo) {
+          const int src = __ffs(todo) - 1;
+          todo &= todo - 1;
+          const int q2 = __shfl_sync(0xffffffffu, cand, src);
+          const int q1 = b * 16 + src;
+          const bool eq = warp_pages_equal(tmp + static_cast<int64_t>(q1) * kPageBytes, map + q1 * 64,
+                                           tmp + static_cast<int64_t>(q2) * kPageBytes, map + q2 * 64);
+          if (lane == src && eq) {
+            m = sdst[q2];
+            slot = -1;
+          }
+        }
+      }
+    }
+    const bool fresh = lane < 16 && m < 0;
+    const unsigned fm = __ballot_sync(0xffffffffu, fresh);
+    const int needed = __popc(fm);
+    if (cnt < needed) {
+      aborted = true;
+      if (lane < 16) new_flags[qi] = kAborted;
+      if (lane == 0 && status) *status = V1X_STATUS_ARENA_EXHAUSTED;
+      continue;
+    }
+    if (lane < 16) {
+      const int dst = fresh ? sfree[(cnt0 - cnt) + __popc(fm & lt)] : m;
+      atomicAdd(&refs[dst], 1);
+      tables[static_cast<int64_t>(bm[1]) * 16 + lane] = dst;
+      new_flags[qi] = fresh ? 1 : 0;
+      sdst[qi] = dst;
+      if (fresh) fp_insert(table, fp_slot(sh0[qi], sh1[qi]), qi);
+      if (rows.tables) {
+        const int64_t bucket = bm[0] / 1024;
+        rows.tables[bm[3] * rows.table_stride + bucket * 16 + lane] = dst;
+        if (lane < 2)
+          rows.centers[bm[3] * rows.center_stride + bucket * 2 + lane] =
+              rows.center_pages[static_cast<int64_t>(bm[1]) * 2 + lane];
+      }
+    }
+    cnt -= needed;
+    __syncwarp();
+  }
+  if (lane == 0) *count = cnt;
+}
+
+// Releases of several requests in order, one CTA.  A request's pages are
+// distinct (its buckets cover disjoint token positions and a page's members are
+// part of its identity), so all of a request's leases are decremented at once;
+// the pages that reach zero are pushed in (lease, lane) order -- the order of
+// the reference's per-lease release calls -- by a block scan.  Requests follow
+// one another, since different requests may share pages.
+constexpr int kReleaseThreads = 1024;
+
+__global__ void __launch_bounds__(kReleaseThreads) release_many_kernel(
+    const int32_t* __restrict__ tables, const int32_t* __restrict__ leases, const int32_t* __restrict__ offsets,
+    int requests, int32_t* __restrict__ refs, int32_t* __restrict__ free_stack, int32_t* __restrict__ count) {
+  __shared__ int warp_tot[kReleaseThreads / 32 + 1];
+  int cnt = *count;
+  for (int r = 0; r < requests; ++r) {
+    const int64_t o0 = static_cast<int64_t>(offsets[r]) * 16, o1 = static_cast<int64_t>(offsets[r + 1]) * 16;
+    for (int64_t c = o0; c < o1; c += kReleaseThreads) {
+      const int64_t i = c + threadIdx.x;
+      int page = 0, dead = 0;
+      if (i < o1) {
+        page = tables[static_cast<int64_t>(leases[i / 16]) * 16 + i % 16];
+        dead = atomicSub(&refs[page], 1) == 1;
+      }
+      int total;
+      const int rank = block_exclusive_scan(dead, warp_tot, &total);
+      if (dead) free_stack[cnt + rank] = page;
+      cnt += total;
+    }
+  }
+  if (threadIdx.x == 0) *count = cnt;
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Host-side offsets into the work array (as BatchWork on the device).
+struct BatchWorkHost {
+  int32_t* head;
+  int32_t* first;
+  explicit BatchWorkHost(int32_t* w) : head(w), first(w + kWorkHead + 4 * kPairCap) {}
+};
 
 }  // namespace
 }  // namespace v1x
@@ -207,7 +597,8 @@ extern "C" int v1x_fingerprint(const uint8_t* tmp, const int32_t* map, const int
   clear_error();
   V1X_CHECK_ARG(n_pages >= 0 && aligned16(tmp), "fingerprint: tmp must be 16-byte aligned");
   if (n_pages == 0) return V1X_OK;
-  fingerprint_kernel<<<static_cast<unsigned>(n_pages), 256, 0, as_stream(stream)>>>(tmp, map, meta, hash);
+  fingerprint_kernel<<<static_cast<unsigned>(n_pages), 256, 0, as_stream(stream)>>>(tmp, map, meta, hash, n_pages, 3,
+                                                                                 nullptr, nullptr, nullptr);
   return launch_status("v1x_fingerprint");
 }
 
@@ -255,7 +646,7 @@ extern "C" int v1x_publish(const uint8_t* tmp, const uint8_t* tc_bytes, const fl
                 "publish: page pools must be 16-byte aligned");
   publish_kernel<<<16, 256, 0, as_stream(stream)>>>(tmp, tc_bytes, tc_scales, map, hash, meta, tables,
                                                     new_flags, fine, centers, center_scales, members,
-                                                    hashes);
+                                                    hashes, 3);
   return launch_status("v1x_publish");
 }
 
@@ -265,4 +656,55 @@ extern "C" int v1x_release(const int32_t* table, int32_t* refs, int32_t* free_st
   clear_error();
   release_kernel<<<1, 32, 0, as_stream(stream)>>>(table, refs, free_stack, count);
   return launch_status("v1x_release");
+}
+
+extern "C" int v1x_prepare_buckets(const uint8_t* tmp, const uint8_t* tc_bytes, const float* tc_scales,
+                                   const int32_t* map, const int32_t* meta, int64_t buckets, int64_t* hash,
+                                   int32_t* match, uint8_t* new_flags, uint8_t* fine, uint8_t* centers,
+                                   float* center_scales, int32_t* members, int64_t* hashes, int32_t* refs,
+                                   int32_t* free_stack, int32_t* count, int32_t* tables,
+                                   const int32_t* center_pages, int32_t* state_tables, int64_t state_table_stride,
+                                   int32_t* state_centers, int64_t state_center_stride, int64_t cap,
+                                   int32_t* work, int32_t* status, void* stream) {
+  using namespace v1x;
+  clear_error();
+  V1X_CHECK_ARG(buckets >= 0 && buckets <= kBatchBuckets, "prepare_buckets: at most %d buckets per call",
+                kBatchBuckets);
+  V1X_CHECK_ARG(cap > 0 && cap < INT_MAX, "prepare_buckets: bad capacity");
+  V1X_CHECK_ARG(aligned16(tmp) && aligned16(fine) && aligned16(tc_bytes) && aligned16(centers),
+                "prepare_buckets: page pools must be 16-byte aligned");
+  V1X_CHECK_ARG(!state_tables || (state_centers && center_pages && state_table_stride >= 16 &&
+                                  state_center_stride >= 2),
+                "prepare_buckets: state rows need both tables, the centre pages and their strides");
+  if (buckets == 0) return V1X_OK;
+  cudaStream_t s = as_stream(stream);
+  const int nq = static_cast<int>(buckets) * 16;
+  V1X_CHECK_ARG(work != nullptr, "prepare_buckets: work (V1X_PREPARE_WORK_INTS ints) is required");
+  BatchWorkHost wh(work);
+  fingerprint_kernel<<<nq, 256, 0, s>>>(tmp, map, meta, hash, 16, kBatchMeta, match, wh.first, wh.head);
+  int64_t blocks = (cap + 255) / 256;
+  const int64_t maxb = static_cast<int64_t>(num_sms()) * 4;
+  if (blocks > maxb) blocks = maxb;
+  match_batch_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(hash, meta, hashes, refs, cap, nq, work);
+  confirm_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(tmp, map, hash, meta, fine, members, hashes, refs,
+                                                                match, cap, nq, work);
+  const StateRows rows{state_tables, state_table_stride, state_centers, state_center_stride, center_pages};
+  decide_kernel<<<1, 128, 0, s>>>(tmp, map, hash, meta, match, static_cast<int>(buckets), free_stack, count, refs,
+                                  tables, new_flags, status, rows, work);
+  publish_kernel<<<nq, 256, 0, s>>>(tmp, tc_bytes, tc_scales, map, hash, meta, tables, new_flags, fine, centers,
+                                    center_scales, members, hashes, kBatchMeta);
+  return launch_status("v1x_prepare_buckets");
+}
+
+extern "C" int v1x_release_many(const int32_t* tables, const int32_t* leases, const int32_t* offsets,
+                                int64_t requests, int32_t* refs, int32_t* free_stack, int32_t* count,
+                                void* stream) {
+  using namespace v1x;
+  clear_error();
+  V1X_CHECK_ARG(requests >= 0 && requests < INT_MAX, "release_many: bad request count");
+  if (requests == 0) return V1X_OK;
+  release_many_kernel<<<1, kReleaseThreads, 0, as_stream(stream)>>>(tables, leases, offsets,
+                                                                    static_cast<int>(requests), refs, free_stack,
+                                                                    count);
+  return launch_status("v1x_release_many");
 }

@@ -28,6 +28,15 @@ reference's ``Build`` execution does; the bucket's inputs are copied into
 those buffers first.  Every launch is asynchronous: an exhausted arena is
 recorded in the device status word (the reference traps) and raised by
 ``check()``.
+
+``prepare_many`` (an extension) prepares several requests at once: all their
+new buckets, in the same canonical order, go through ``v1x_prepare_buckets``
+(up to 64 buckets per call, five launches per call), which also writes the
+requests' page-table rows.  The arena afterwards equals that of ``prepare``
+called for each request in turn.  Request tables live as rows of one arena
+tensor, so a batch updates them without per-request copies.  ``release_many``
+releases several requests in one launch (``v1x_release_many``), with the arena
+state of ``release`` called for each in turn.
 """
 from __future__ import annotations
 
@@ -37,16 +46,21 @@ from . import _lib
 from . import kernels as K
 
 PAGE_BYTES = 8448
+BATCH_BUCKETS = 64      # buckets per v1x_prepare_buckets call
+PREPARE_WORK_INTS = 4 + 4 * 4096 + 1024   # V1X_PREPARE_WORK_INTS
 
 
 class State:
-    """A request's index state (reference State, DS/runtime.py:681-690)."""
+    """A request's index state (reference State, DS/runtime.py:681-690).  The
+    tables are given views (rows of the arena's tensors) or allocated here."""
 
-    def __init__(self, pages: int, device):
-        self.table = torch.zeros(pages, dtype=torch.int32, device=device)
-        self.center_table = torch.zeros(pages // 8, dtype=torch.int32, device=device)
+    def __init__(self, pages: int, device, table=None, center_table=None, row: int = -1):
+        self.table = torch.zeros(pages, dtype=torch.int32, device=device) if table is None else table
+        self.center_table = (torch.zeros(pages // 8, dtype=torch.int32, device=device) if center_table is None
+                             else center_table)
         self.leases: list[int] = []
         self.length = 0
+        self.row = row
 
 
 class PageArena:
@@ -85,9 +99,21 @@ class PageArena:
             self.status = torch.zeros(1, dtype=torch.int32, device=d)
         self.graphs = graphs
         self._graph = None
+        # request tables: one row per live request (State.table / center_table are views)
+        self.state_tables = torch.zeros((self.max_requests, pages), dtype=torch.int32, device=d)
+        self.state_centers = torch.zeros((self.max_requests, pages // 8), dtype=torch.int32, device=d)
+        self.free_rows = list(range(self.max_requests - 1, -1, -1))
+        self.kernel_launches = 0   # kernels this driver has launched (reported by the bench)
+        # batched prepare: meta records and per-page scratch of one call
+        self.batch_meta = torch.zeros((BATCH_BUCKETS, 4), dtype=torch.int32, device=d)
+        self.batch_hash = torch.zeros((BATCH_BUCKETS * 16, 2), dtype=torch.int64, device=d)
+        self.batch_match = torch.zeros(BATCH_BUCKETS * 16, dtype=torch.int32, device=d)
+        self.batch_new = torch.zeros(BATCH_BUCKETS * 16, dtype=torch.uint8, device=d)
+        self.batch_work = torch.zeros(PREPARE_WORK_INTS, dtype=torch.int32, device=d)
 
     # -- one bucket ------------------------------------------------------------
     def _kernels(self, tmp, mapping, centers):
+        self.kernel_launches += 6   # fingerprint, match (3), allocate, publish
         K.fingerprint[(16,)](tmp, mapping, self.meta, self.hash)
         K.match_pages[(16,)](tmp, mapping, self.hash, self.meta, self.fine, self.members, self.hashes,
                              self.refs, self.matches, self.capacity)
@@ -132,7 +158,7 @@ class PageArena:
         if state is None:
             if len(self.states) >= self.max_requests:
                 raise ValueError("V1 request capacity exceeded")
-            state = self.states[owner] = State(self.pages, self.device)
+            state = self._new_state(owner)
         complete = length // 1024
         new = range(len(state.leases), complete)
         # the buckets that will get a lease (the loop raises at the first one
@@ -159,6 +185,87 @@ class PageArena:
             for lease in state.leases:
                 K.release[(1,)](self.tables[lease], self.refs, self.free, self.free_count)
                 self.free_leases.append(lease)
+                self.kernel_launches += 1
+            self.free_rows.append(state.row)
+
+    def release_many(self, owners):
+        """``release(owner)`` for every owner in order, in one launch
+        (v1x_release_many); unknown owners are skipped as release skips them."""
+        states = [(o, self.states.pop(o)) for o in owners if o in self.states]
+        if not states:
+            return
+        leases = [lease for _, st in states for lease in st.leases]
+        offsets = [0]
+        for _, st in states:
+            offsets.append(offsets[-1] + len(st.leases))
+        idx = torch.tensor(leases + offsets, dtype=torch.int32).to(self.device, non_blocking=True)
+        _lib.call("v1x_release_many", _lib.ptr(self.tables), _lib.ptr(idx), _lib.ptr(idx[len(leases):]),
+                  len(states), _lib.ptr(self.refs), _lib.ptr(self.free), _lib.ptr(self.free_count),
+                  torch.cuda.current_stream(self.device).cuda_stream, device=self.device)
+        self.kernel_launches += 1
+        for _, st in states:
+            self.free_leases.extend(st.leases)
+            self.free_rows.append(st.row)
+
+    def _new_state(self, owner):
+        row = self.free_rows.pop()
+        self.state_tables[row].zero_()
+        self.state_centers[row].zero_()
+        state = self.states[owner] = State(self.pages, self.device, self.state_tables[row], self.state_centers[row],
+                                           row)
+        return state
+
+    # -- several requests at once (extension) ----------------------------------
+    def prepare_many(self, requests, batch_source):
+        """``prepare(owner, length)`` for every (owner, length) of `requests`, in
+        order, with all new buckets indexed by batched calls.  batch_source(pairs)
+        -> (tmp uint8 [n, 16, 8448], mapping int32 [n, 16, 64], centers uint8
+        [n, 2, 8448]) for the (owner, bucket) pairs in order.  Errors are those of
+        ``prepare``, raised at the same request (buckets before it are indexed)."""
+        pending = []
+        try:
+            for owner, length in requests:
+                if not 0 <= length <= self.pages * 64:
+                    raise ValueError("Index context capacity exceeded")
+                state = self.states.get(owner)
+                if state is not None and length < state.length:
+                    self._flush(pending, batch_source)
+                    self.release(owner)
+                    state = None
+                if state is None:
+                    if len(self.states) >= self.max_requests:
+                        raise ValueError("V1 request capacity exceeded")
+                    state = self._new_state(owner)
+                for bucket in range(len(state.leases), length // 1024):
+                    if not self.free_leases:
+                        raise RuntimeError("V1 bucket records exhausted")
+                    lease = self.free_leases.pop()
+                    state.leases.append(lease)
+                    pending.append((owner, bucket, lease, state.row))
+                state.length = length
+        finally:
+            self._flush(pending, batch_source)
+
+    def _flush(self, pending, batch_source):
+        for i in range(0, len(pending), BATCH_BUCKETS):
+            chunk = pending[i:i + BATCH_BUCKETS]
+            n = len(chunk)
+            tmp, mapping, centers = batch_source([(o, b) for o, b, _, _ in chunk])
+            meta = torch.tensor([[b * 1024, lease, 1, row] for _, b, lease, row in chunk], dtype=torch.int32)
+            self.batch_meta[:n].copy_(meta, non_blocking=True)
+            tmp, mapping, centers = tmp.contiguous(), mapping.contiguous(), centers.contiguous()
+            self.kernel_launches += 5
+            _lib.call("v1x_prepare_buckets", _lib.ptr(tmp), _lib.ptr(centers), _lib.ptr(centers.view(torch.float32)),
+                      _lib.ptr(mapping), _lib.ptr(self.batch_meta), n, _lib.ptr(self.batch_hash),
+                      _lib.ptr(self.batch_match), _lib.ptr(self.batch_new), _lib.ptr(self.fine),
+                      _lib.ptr(self.centers), _lib.ptr(self.centers.view(torch.float32)), _lib.ptr(self.members),
+                      _lib.ptr(self.hashes), _lib.ptr(self.refs), _lib.ptr(self.free), _lib.ptr(self.free_count),
+                      _lib.ptr(self.tables), _lib.ptr(self.center_pages), _lib.ptr(self.state_tables),
+                      self.state_tables.stride(0), _lib.ptr(self.state_centers), self.state_centers.stride(0),
+                      self.capacity, _lib.ptr(self.batch_work), _lib.ptr(self.status),
+                      torch.cuda.current_stream(self.device).cuda_stream,
+                      device=self.device)
+        pending.clear()
 
     def check(self):
         """Raise ArenaExhausted if an allocation found too few free pages (the

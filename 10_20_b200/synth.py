@@ -241,3 +241,13 @@ class LifecycleWorkload:
         tmp, mapping, centers = contents
         return lambda owner, bucket: (tmp[self.chains[owner][bucket]], mapping[self.chains[owner][bucket]],
                                       centers[self.chains[owner][bucket]])
+
+    def batch_source(self, contents):
+        """batch_source(pairs) for PageArena.prepare_many: the (owner, bucket)
+        pairs' contents stacked in order."""
+        tmp, mapping, centers = contents
+
+        def fetch(pairs):
+            ids = torch.tensor([self.chains[o][b] for o, b in pairs], dtype=torch.long, device=tmp.device)
+            return tmp.index_select(0, ids), mapping.index_select(0, ids), centers.index_select(0, ids)
+        return fetch

@@ -278,15 +278,18 @@ V1X_API int v1x_match_pages(const uint8_t* tmp, const int32_t* map, const int64_
 
 /* DS/kernels.py:116-131. 16 lanes. free i32 [cap], count i32 scalar, refs i32
  * [cap], tables i32 [leases, 16], new_flags u8 (torch.bool) [16].  If the free
- * stack holds fewer pages than needed, *status = V1X_STATUS_ARENA_EXHAUSTED and
- * nothing else is written (the reference traps).  status may be NULL. */
+ * stack holds fewer pages than needed, *status = V1X_STATUS_ARENA_EXHAUSTED,
+ * every new_flags entry is set to 2 ("bucket not allocated", so that
+ * v1x_publish skips the bucket) and nothing else is written (the reference
+ * traps).  status may be NULL. */
 V1X_API int v1x_allocate(const int32_t* meta, const int32_t* match, int32_t* free_stack,
                  int32_t* count, int32_t* refs, int32_t* tables, uint8_t* new_flags,
                  int32_t* status, void* stream);
 
 /* DS/kernels.py:134-167. tmp u8 [16, 8448]; tc_bytes u8 / tc_scales f32 = the
  * bucket's 2 centre pages (byte and float views); fine u8 [cap, 8448];
- * centers u8 / center_scales f32 = centre pool views; members i32; hashes i64. */
+ * centers u8 / center_scales f32 = centre pool views; members i32; hashes i64.
+ * A bucket whose new_flags hold 2 (allocation failed) writes nothing. */
 V1X_API int v1x_publish(const uint8_t* tmp, const uint8_t* tc_bytes, const float* tc_scales,
                 const int32_t* map, const int64_t* hash, const int32_t* meta,
                 const int32_t* tables, const uint8_t* new_flags, uint8_t* fine,
@@ -296,6 +299,49 @@ V1X_API int v1x_publish(const uint8_t* tmp, const uint8_t* tc_bytes, const float
 /* DS/kernels.py:170-179. table i32 [16] (one lease's row). */
 V1X_API int v1x_release(const int32_t* table, int32_t* refs, int32_t* free_stack, int32_t* count,
                 void* stream);
+
+/* Scratch of v1x_prepare_buckets, in int32 words: 4 counters/flags, two lists of
+ * 4096 fingerprint-equal pairs (int32 x 2 each), 1024 earliest-equal entries. */
+#define V1X_PREPARE_WORK_INTS (4 + 4 * 4096 + 1024)
+
+/* Extension (no reference counterpart): the page part of Build.compute
+ * (DS/runtime.py:230-270: fingerprint -> match_pages -> allocate -> publish,
+ * DS/kernels.py:57-167) for up to 64 buckets in canonical order, in five
+ * launches instead of six per bucket.  The arena state afterwards equals that
+ * of the per-bucket calls in the same order.
+ * tmp u8 [buckets, 16, 8448]; tc_bytes u8 / tc_scales f32 [buckets, 2, 8448]
+ * (byte and float views); map i32 [buckets, 16, 64]; meta i32 [buckets, 4] =
+ * (token start, lease, active, state row); scratch: hash i64 [buckets*16, 2],
+ * match i32 [buckets*16], new_flags u8 [buckets*16], work i32
+ * [V1X_PREPARE_WORK_INTS] (no initial contents needed).  Arena arrays as in
+ * v1x_match_pages / v1x_allocate / v1x_publish; center_pages i32 [leases, 2].
+ * state_tables i32 [rows, state_table_stride] and state_centers i32 [rows,
+ * state_center_stride] (may be NULL together): the request page-table rows,
+ * receiving tables[lease] at columns start/1024*16 and center_pages[lease] at
+ * start/1024*2 of the bucket's state row.  The first bucket that finds the
+ * free stack too short writes V1X_STATUS_ARENA_EXHAUSTED to *status; it and
+ * every later bucket of the call change nothing. */
+/* Extension (no reference counterpart): Indexer._release (DS/runtime.py:771-780,
+ * kernel DS/kernels.py:170-179) for several requests in one launch.  leases i32
+ * = the requests' lease ids, request after request, each request's in order;
+ * offsets i32 [requests + 1] = where each request's leases start (CSR).  The
+ * refcounts, free stack and count afterwards equal those of v1x_release called
+ * for every lease in that order, provided a request's leases hold distinct
+ * pages (true of every arena state the prepare paths build: a request's
+ * buckets cover disjoint token positions, which are part of a page's
+ * identity). */
+V1X_API int v1x_release_many(const int32_t* tables, const int32_t* leases, const int32_t* offsets,
+                     int64_t requests, int32_t* refs, int32_t* free_stack, int32_t* count,
+                     void* stream);
+
+V1X_API int v1x_prepare_buckets(const uint8_t* tmp, const uint8_t* tc_bytes, const float* tc_scales,
+                        const int32_t* map, const int32_t* meta, int64_t buckets, int64_t* hash,
+                        int32_t* match, uint8_t* new_flags, uint8_t* fine, uint8_t* centers,
+                        float* center_scales, int32_t* members, int64_t* hashes, int32_t* refs,
+                        int32_t* free_stack, int32_t* count, int32_t* tables,
+                        const int32_t* center_pages, int32_t* state_tables, int64_t state_table_stride,
+                        int32_t* state_centers, int64_t state_center_stride, int64_t cap,
+                        int32_t* work, int32_t* status, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Per-row query metadata and staging. */

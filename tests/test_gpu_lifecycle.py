@@ -77,3 +77,99 @@ def test_lifecycle_limits(cuda_dev):
     assert len(arena.states[a].leases) == 1 and int(arena.free_count.item()) == 16
     arena.release(a)
     assert int(arena.free_count.item()) == 32 and bool((arena.refs == 0).all())
+
+
+def _rounds_batched(gpu, cpu, wl, contents, host):
+    """Each round's consecutive prepares as one prepare_many call and its
+    consecutive releases as one release_many call; the CPU port takes the same
+    operations one by one."""
+    bsrc, src_cpu = wl.batch_source(contents), wl.source(host)
+    for ops in wl.ops:
+        prep, rel = [], []
+        for op in ops + [("end",)]:
+            if op[0] != "prepare" and prep:
+                gpu.prepare_many(prep, bsrc)
+                prep = []
+            if op[0] != "release" and rel:
+                gpu.release_many(rel)
+                rel = []
+            if op[0] == "prepare":
+                prep.append((op[1], op[2]))
+                cpu.prepare(op[1], op[2], src_cpu)
+            elif op[0] == "release":
+                rel.append(op[1])
+                cpu.release(op[1])
+        gpu.check()
+        torch.cuda.synchronize()
+        _compare(gpu, cpu)
+
+
+@pytest.mark.parametrize("requests,grow", [(10, 3), (40, 4)])
+def test_prepare_many_matches_cpu_port(requests, grow, cuda_dev):
+    """Batched prepare (extension) == the reference's per-bucket sequence: every
+    arena array and request table after every round.  (40, 4) puts more than 64
+    buckets in a round (several calls); shared prefixes give matches both
+    against pages live before a call and against pages published inside it."""
+    cap, pages = 4096, 256
+    wl = synth.LifecycleWorkload(requests=requests, max_buckets=8, rounds=4, seed=11 + requests,
+                                 max_leases=cap // 16, share=0.6, grow=grow)
+    contents = wl.contents("cuda")
+    host = tuple(x.cpu().numpy() for x in contents)
+    gpu = lifecycle.PageArena(cap, pages, "cuda", max_requests=64)
+    cpu = port.ArenaPort(cap, pages, max_requests=64)
+    _rounds_batched(gpu, cpu, wl, contents, host)
+    assert (cpu.refs > 1).sum() > 0
+
+
+def test_prepare_many_inside_batch_sharing(cuda_dev):
+    """Two requests with the same chain prepared in ONE call: the second one's
+    pages match the pages the first one published earlier in the same call."""
+    cap, pages = 1024, 128
+    wl = synth.LifecycleWorkload(requests=1, max_buckets=4, rounds=1, seed=2, max_leases=cap // 16, share=0.0)
+    (a,) = list(wl.chains)
+    wl.chains[a + 1] = list(wl.chains[a])
+    contents = wl.contents("cuda")
+    host = tuple(x.cpu().numpy() for x in contents)
+    n = len(wl.chains[a]) * 1024 + 3
+    gpu = lifecycle.PageArena(cap, pages, "cuda", max_requests=4)
+    cpu = port.ArenaPort(cap, pages, max_requests=4)
+    gpu.prepare_many([(a, n), (a + 1, n)], wl.batch_source(contents))
+    for o in (a, a + 1):
+        cpu.prepare(o, n, wl.source(host))
+    gpu.check()
+    _compare(gpu, cpu)
+    assert int((cpu.refs == 2).sum()) == 16 * len(wl.chains[a])
+
+
+@pytest.mark.parametrize("batched", [False, True])
+def test_exhausted_free_stack_changes_nothing(batched, cuda_dev):
+    """A free stack shorter than a bucket needs (only reachable by changing the
+    arena by hand: the driver's lease records bound the live pages): the status
+    word reports it and that bucket and the later ones change nothing -- the
+    arena equals the CPU port's at the failing bucket (the reference traps)."""
+    cap, pages = 256, 64
+    wl = synth.LifecycleWorkload(requests=3, max_buckets=3, rounds=1, seed=4, max_leases=cap // 16, share=0.0)
+    a = min(wl.chains)
+    wl.chains[a] = [0, 1, 2]                 # three distinct buckets
+    contents = wl.contents("cuda")
+    host = tuple(x.cpu().numpy() for x in contents)
+    gpu = lifecycle.PageArena(cap, pages, "cuda", max_requests=2)
+    cpu = port.ArenaPort(cap, pages, max_requests=2)
+    gpu.free_count.fill_(20)
+    cpu.count = 20
+    n = 3 * 1024
+    if batched:
+        gpu.prepare_many([(a, n)], wl.batch_source(contents))
+    else:
+        gpu.prepare(a, n, wl.source(contents))
+    with pytest.raises(port.O.ArenaExhausted):
+        cpu.prepare(a, n, wl.source(host))
+    with pytest.raises(Exception, match="exhausted"):
+        gpu.check()
+    torch.cuda.synchronize()
+    assert int(gpu.free_count.item()) == cpu.count == 4
+    for name in ("refs", "free", "members", "hashes"):
+        assert np.array_equal(getattr(gpu, name).cpu().numpy(), getattr(cpu, name)), name
+    assert np.array_equal(gpu.fine.cpu().numpy(), cpu.fine)
+    assert np.array_equal(gpu.centers.cpu().numpy(), cpu.centers)
+    assert np.array_equal(gpu.tables.cpu().numpy(), cpu.tables)
