@@ -453,6 +453,8 @@ def run_pages_workload(args, world, rank, device, dist):
         torch.cuda.synchronize()
         launches0 = arena.kernel_launches
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        # an NVTX range names the timed launches for profilers (ncu --nvtx-include)
+        torch.cuda.nvtx.range_push("lifecycle_batched" if batched else "lifecycle_per_bucket")
         with Clocks(device) as clk:
             t0 = time.perf_counter()
             a.record()
@@ -460,6 +462,7 @@ def run_pages_workload(args, world, rank, device, dist):
             b.record()
             torch.cuda.synchronize()
             wall = time.perf_counter() - t0
+        torch.cuda.nvtx.range_pop()
         arena.check()
         ms = a.elapsed_time(b)
         tt = torch.tensor([ms], dtype=torch.float64, device=device)
