@@ -26,6 +26,7 @@ namespace {
 
 constexpr int kScoreThreads = 128;
 constexpr int kSimtMaxHeads = 64;
+constexpr int64_t kTcMaxRows = 8192;  // rows the tensor-core scorer takes per call (score_tc.cu)
 
 struct ScoreArgs {
   const uint8_t* q;
@@ -207,7 +208,11 @@ int score_dispatch(const uint8_t* q, const float* w, const uint8_t* pool, int64_
   V1X_CHECK_ARG(table_stride >= 0 && impl >= 0 && impl <= 2, "score_fp8: bad table stride / impl");
   V1X_CHECK_ARG(lens_kind == 0 || lens_kind == 1, "score_fp8: lens_kind must be 0 or 1");
   if (batch == 0 || max_len == 0) return V1X_OK;
-  const bool tc = impl == 2 || (impl == 0 && (heads == 1 || (heads % 32 == 0 && heads <= 128)));
+  // automatic: the tensor cores where they take the shape (one head, or a
+  // multiple of 32 up to 128; batch <= kTcMaxRows; pool < 2^31 pages), else SIMT
+  const bool tc_shape = (heads == 1 || (heads % 32 == 0 && heads <= 128)) && batch <= kTcMaxRows &&
+                        pool_pages < (int64_t(1) << 31);
+  const bool tc = impl == 2 || (impl == 0 && tc_shape);
   if (tc)
     return score_fp8_tc(q, w, pool, pool_pages, lens, table, table_stride, out, out_stride, max_len, page_max,
                         page_stride, heads, relu, clean, lens_kind, batch, status, as_stream(stream));

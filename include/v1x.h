@@ -425,7 +425,7 @@ V1X_API int v1x_expand_logical(const int32_t* logical, int32_t* out, int64_t top
  * per-page centre maximum that fused.route computes (VQ:26-41), produced in the
  * scoring epilogue.
  * relu = 0 gives the signed variant.  impl: 0 = automatic (tensor cores when
- * heads is 1 or a multiple of 32 up to 128, else SIMT), 1 = SIMT (fixed fp32
+ * heads is 1 or a multiple of 32 up to 128 and batch <= 8192, else SIMT), 1 = SIMT (fixed fp32
  * evaluation order, bit-identical to a sequential fp32 restatement, heads <= 64),
  * 2 = tensor cores (heads in {1, 32, 64, 96, 128}; batch <= 8192).  status: optional i32 device
  * word receiving V1X_STATUS_TIMEOUT if a bounded device wait gave up. */

@@ -70,6 +70,29 @@ def test_score_simt_exact_vs_oracle(H, cuda_dev):
     close(out, O.score_paged(q8, w, pool, table, lens, 1300, exact=False))
 
 
+def test_score_auto_single_head_beyond_tensor_core_rows(cuda_dev):
+    """Automatic dispatch takes the tensor cores for one head only up to 8192
+    rows; a larger batch runs on the SIMT scorer (bit-identical to impl="simt"
+    and to the oracle's exact mode) instead of failing."""
+    rng = np.random.default_rng(5)
+    B, NP = 8193, 12
+    pool = np.zeros((NP, 8448), np.uint8)
+    kb = torch.randn((NP, 64, 128), generator=torch.Generator().manual_seed(5)).to(torch.float8_e4m3fn)
+    pool[:, :8192] = kb.view(torch.uint8).reshape(NP, 8192).numpy()
+    pool.view(np.float32)[:, 2048:] = rng.random((NP, 64)).astype(np.float32) + 0.1
+    q = torch.randn((B, 1, 128), generator=torch.Generator().manual_seed(6)).to(torch.float8_e4m3fn)
+    w = rng.random((B, 1)).astype(np.float32)
+    table = rng.integers(0, NP, size=(B, 2)).astype(np.int32)
+    lens = rng.integers(0, 129, size=B).astype(np.int32)
+    args = (q.cuda(), dev(pool), dev(w), dev(lens), dev(table), None, 128)
+    auto = S.fp8_paged_mqa_logits(*args).cpu().numpy()
+    simt = S.fp8_paged_mqa_logits(*args, impl="simt").cpu().numpy()
+    assert np.array_equal(auto, simt)
+    rows = [0, 1, 4096, 8191, 8192]
+    exp = O.score_paged(q.view(torch.uint8).numpy()[rows], w[rows], pool, table[rows], lens[rows], 128, exact=True)
+    assert np.array_equal(auto[rows], exp)
+
+
 def test_score_tensor_core_rejects_unsupported_heads(cuda_dev):
     q = torch.zeros((2, 256, 128), dtype=torch.float8_e4m3fn, device="cuda")
     pool = torch.zeros((4, 8448), dtype=torch.uint8, device="cuda")
