@@ -13,10 +13,12 @@ physical slot ids -- or of the x4 expanded logical positions when
 
 ``prepare`` builds every new bucket from the native cache through the
 request's native page table (Build.compute, :170-270): the index build of
-index_build.py for all new buckets of the call in one launch, then per bucket
-fingerprint / match / allocate / publish.  The optional ``bucket_source(owner,
-bucket) -> (tmp, mapping, centers)`` replaces the index build with supplied
-bucket contents (see lifecycle.PageArena).
+index_build.py for all new buckets of the call in one launch, then the
+fingerprint / match / allocate / publish of all of them through the batched
+page lifecycle (``PageArena.prepare_many``; the arena state equals that of the
+reference's per-bucket sequence).  The optional ``bucket_source(owner, bucket)
+-> (tmp, mapping, centers)`` replaces the index build with supplied bucket
+contents (see lifecycle.PageArena).
 """
 from __future__ import annotations
 
@@ -136,29 +138,31 @@ class Indexer:
         if torch.cuda.is_current_stream_capturing():
             raise RuntimeError("V1 index subgraphs must execute outside full-model capture")
 
-    def _source(self, owner, bucket):
-        return self.bucket_source(owner, bucket)
-
     def _prepare(self, owner, native_table, length):
         if not 0 <= length <= self.config.max_context:
             raise ValueError("Index context capacity exceeded")
         if (native_table.dtype != torch.int32 or native_table.device != self.device or native_table.ndim != 1
                 or native_table.numel() < -(-length // 64) or not native_table.is_contiguous()):
             raise ValueError("Invalid compact native page table")
+        # The request's new buckets go through the batched page lifecycle
+        # (v1x_prepare_buckets, up to 64 buckets per call), with the arena
+        # state of the reference's per-bucket Build sequence.
         if self.bucket_source is not None:
-            return self.arena.prepare(owner, length, self._source)
-        built = {}
-
-        def batch(_owner, buckets):
-            # consecutive new buckets: their native pages are one slice of the table
-            b0, n = buckets[0], len(buckets)
-            source = native_table[b0 * 16:(b0 + n) * 16].view(n, 16)
-            tmp, centers, mapping, _ = self.builder.build(self.native, source, [b * 1024 for b in buckets],
-                                                          self.arena.status)
-            for i, b in enumerate(buckets):
-                built[b] = (tmp[i], mapping[i], centers[i])
-
-        return self.arena.prepare(owner, length, lambda _o, b: built[b], batch=batch)
+            def batch_source(pairs):
+                parts = [self.bucket_source(o, b) for o, b in pairs]
+                return tuple(torch.stack([p[i] for p in parts]) for i in range(3))
+        else:
+            def batch_source(pairs):
+                # consecutive new buckets of one request: their native pages are
+                # one slice of its table, built in one launch
+                buckets = [b for _, b in pairs]
+                b0, n = buckets[0], len(buckets)
+                source = native_table[b0 * 16:(b0 + n) * 16].view(n, 16)
+                tmp, centers, mapping, _ = self.builder.build(self.native, source, [b * 1024 for b in buckets],
+                                                              self.arena.status)
+                return tmp, mapping, centers
+        self.arena.prepare_many([(owner, length)], batch_source)
+        return self.arena.states[owner]
 
     @torch.inference_mode()
     def prepare(self, owner, native_table, length):
