@@ -173,3 +173,60 @@ def test_exhausted_free_stack_changes_nothing(batched, cuda_dev):
     assert np.array_equal(gpu.fine.cpu().numpy(), cpu.fine)
     assert np.array_equal(gpu.centers.cpu().numpy(), cpu.centers)
     assert np.array_equal(gpu.tables.cpu().numpy(), cpu.tables)
+
+
+def _collide(mapping_page):
+    """Members whose fingerprint equals the page's (same bytes): +1, -2, +1 at
+    members 0..2 leave both fingerprint sums unchanged, the content differs."""
+    m = mapping_page.clone()
+    m[0] += 1
+    m[1] -= 2
+    m[2] += 1
+    return m
+
+
+def test_prepare_many_fingerprint_collisions(cuda_dev):
+    """Pages with equal fingerprints but different members must never match:
+    against a live arena page (the confirmation fails), and inside one call,
+    where a page's lowest equal-fingerprint earlier page is the colliding one
+    and its true equal page comes later in the call (the decision warp's exact
+    search)."""
+    cap, pages = 1024, 128
+    gen = torch.Generator().manual_seed(8)
+    n = 4
+    tmp = torch.randint(0, 256, (n, 16, 8448), generator=gen, dtype=torch.uint8)
+    centers = torch.randint(0, 256, (n, 2, 8448), generator=gen, dtype=torch.uint8)
+    mapping = torch.stack([torch.randperm(1024, generator=gen).to(torch.int32).view(16, 64) for _ in range(n)])
+    # one call: content 0 (X at page 3), content 1 (Y at page 3: X's bytes with
+    # colliding members), content 2 (Y again at page 3): the lowest earlier
+    # equal-fingerprint page of the second Y is X, its true copy the first Y.
+    # Second call: content 3 page 5 collides with content 0 page 5, live by then.
+    tmp[1, 3] = tmp[0, 3]
+    mapping[1, 3] = _collide(mapping[0, 3])
+    tmp[2, 3] = tmp[1, 3]
+    mapping[2, 3] = mapping[1, 3]
+    tmp[3, 5] = tmp[0, 5]
+    mapping[3, 5] = _collide(mapping[0, 5])
+    chains = {10: [0], 11: [1, 2], 12: [3]}
+    host = (tmp.numpy(), mapping.numpy(), centers.numpy())
+    dev_c = (tmp.cuda(), mapping.cuda(), centers.cuda())
+
+    def src(c):
+        return lambda o, b: tuple(x[chains[o][b]] for x in c)
+
+    def bsrc(pairs):
+        ids = torch.tensor([chains[o][b] for o, b in pairs], dtype=torch.long, device="cuda")
+        return tuple(x.index_select(0, ids) for x in dev_c)
+
+    gpu = lifecycle.PageArena(cap, pages, "cuda", max_requests=4)
+    cpu = port.ArenaPort(cap, pages, max_requests=4)
+    for group in ([(10, 1024), (11, 2048)], [(12, 1024)]):
+        gpu.prepare_many(group, bsrc)
+        for o, length in group:
+            cpu.prepare(o, length, src(host))
+        gpu.check()
+        torch.cuda.synchronize()
+        _compare(gpu, cpu)
+    t = {o: cpu.states[o]["table"] for o in chains}
+    assert t[11][16 + 3] == t[11][3] != t[10][3]     # the copy shares its page, not the collision's
+    assert t[12][5] != t[10][5]
