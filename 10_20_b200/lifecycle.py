@@ -50,6 +50,38 @@ BATCH_BUCKETS = 64      # buckets per v1x_prepare_buckets call
 PREPARE_WORK_INTS = 4 + 4 * 4096 + 1024   # V1X_PREPARE_WORK_INTS
 
 
+class HostStaging:
+    """Host -> device copies of small integer arrays without a host wait.
+
+    A copy from pageable host memory may wait for the stream (the driver stages
+    it), which would serialise the driver's host loop with the GPU; the values go
+    through a ring of pinned buffers instead, each rewritten only after the copy
+    that last read it has completed (an event per slot)."""
+
+    def __init__(self, length: int, device, dtype=torch.int32, slots: int = 8):
+        self.device = torch.device(device)
+        self.buf = torch.empty((slots, length), dtype=dtype).pin_memory()
+        self.host = self.buf.numpy()
+        self.events = [None] * slots
+        self.k = 0
+
+    def copy(self, values, dst):
+        """dst[:len(values)] = values (dst a contiguous device tensor), enqueued
+        on the current stream."""
+        n = len(values)
+        k = self.k
+        self.k = (k + 1) % len(self.events)
+        ev = self.events[k]
+        if ev is not None:
+            ev.synchronize()
+        else:
+            ev = self.events[k] = torch.cuda.Event()
+        self.host[k, :n] = values
+        dst.view(-1)[:n].copy_(self.buf[k, :n], non_blocking=True)
+        ev.record(torch.cuda.current_stream(self.device))
+        return dst
+
+
 class State:
     """A request's index state (reference State, DS/runtime.py:681-690).  The
     tables are given views (rows of the arena's tensors) or allocated here."""
@@ -110,6 +142,8 @@ class PageArena:
         self.batch_match = torch.zeros(BATCH_BUCKETS * 16, dtype=torch.int32, device=d)
         self.batch_new = torch.zeros(BATCH_BUCKETS * 16, dtype=torch.uint8, device=d)
         self.batch_work = torch.zeros(PREPARE_WORK_INTS, dtype=torch.int32, device=d)
+        self.release_idx = torch.zeros(self.max_leases + self.max_requests + 1, dtype=torch.int32, device=d)
+        self.staging = HostStaging(max(BATCH_BUCKETS * 4, self.release_idx.numel()), d) if d.type == "cuda" else None
 
     # -- one bucket ------------------------------------------------------------
     def _kernels(self, tmp, mapping, centers):
@@ -198,7 +232,7 @@ class PageArena:
         offsets = [0]
         for _, st in states:
             offsets.append(offsets[-1] + len(st.leases))
-        idx = torch.tensor(leases + offsets, dtype=torch.int32).to(self.device, non_blocking=True)
+        idx = self.staging.copy(leases + offsets, self.release_idx)
         _lib.call("v1x_release_many", _lib.ptr(self.tables), _lib.ptr(idx), _lib.ptr(idx[len(leases):]),
                   len(states), _lib.ptr(self.refs), _lib.ptr(self.free), _lib.ptr(self.free_count),
                   torch.cuda.current_stream(self.device).cuda_stream, device=self.device)
@@ -251,8 +285,7 @@ class PageArena:
             chunk = pending[i:i + BATCH_BUCKETS]
             n = len(chunk)
             tmp, mapping, centers = batch_source([(o, b) for o, b, _, _ in chunk])
-            meta = torch.tensor([[b * 1024, lease, 1, row] for _, b, lease, row in chunk], dtype=torch.int32)
-            self.batch_meta[:n].copy_(meta, non_blocking=True)
+            self.staging.copy([x for _, b, lease, row in chunk for x in (b * 1024, lease, 1, row)], self.batch_meta)
             tmp, mapping, centers = tmp.contiguous(), mapping.contiguous(), centers.contiguous()
             self.kernel_launches += 5
             _lib.call("v1x_prepare_buckets", _lib.ptr(tmp), _lib.ptr(centers), _lib.ptr(centers.view(torch.float32)),

@@ -245,9 +245,13 @@ class LifecycleWorkload:
     def batch_source(self, contents):
         """batch_source(pairs) for PageArena.prepare_many: the (owner, bucket)
         pairs' contents stacked in order."""
+        from .lifecycle import BATCH_BUCKETS, HostStaging
+
         tmp, mapping, centers = contents
+        ids_dev = torch.zeros(BATCH_BUCKETS, dtype=torch.long, device=tmp.device)
+        staging = HostStaging(BATCH_BUCKETS, tmp.device, dtype=torch.long)
 
         def fetch(pairs):
-            ids = torch.tensor([self.chains[o][b] for o, b in pairs], dtype=torch.long, device=tmp.device)
+            ids = staging.copy([self.chains[o][b] for o, b in pairs], ids_dev)[:len(pairs)]
             return tmp.index_select(0, ids), mapping.index_select(0, ids), centers.index_select(0, ids)
         return fetch
