@@ -136,13 +136,15 @@ class PageArena:
         self.state_centers = torch.zeros((self.max_requests, pages // 8), dtype=torch.int32, device=d)
         self.free_rows = list(range(self.max_requests - 1, -1, -1))
         self.kernel_launches = 0   # kernels this driver has launched (reported by the bench)
+        self._prepare_args = None
         # batched prepare: meta records and per-page scratch of one call
         self.batch_meta = torch.zeros((BATCH_BUCKETS, 4), dtype=torch.int32, device=d)
         self.batch_hash = torch.zeros((BATCH_BUCKETS * 16, 2), dtype=torch.int64, device=d)
         self.batch_match = torch.zeros(BATCH_BUCKETS * 16, dtype=torch.int32, device=d)
         self.batch_new = torch.zeros(BATCH_BUCKETS * 16, dtype=torch.uint8, device=d)
         self.batch_work = torch.zeros(PREPARE_WORK_INTS, dtype=torch.int32, device=d)
-        self.release_idx = torch.zeros(self.max_leases + self.max_requests + 1, dtype=torch.int32, device=d)
+        # release_many's leases, offsets and the released requests' table rows
+        self.release_idx = torch.zeros(self.max_leases + 2 * self.max_requests + 1, dtype=torch.int32, device=d)
         self.staging = HostStaging(max(BATCH_BUCKETS * 4, self.release_idx.numel()), d) if d.type == "cuda" else None
 
     # -- one bucket ------------------------------------------------------------
@@ -220,7 +222,14 @@ class PageArena:
                 K.release[(1,)](self.tables[lease], self.refs, self.free, self.free_count)
                 self.free_leases.append(lease)
                 self.kernel_launches += 1
-            self.free_rows.append(state.row)
+            self._free_row(state.row)
+
+    def _free_row(self, row):
+        # request table rows are zeroed when freed (they start zeroed), so a new
+        # request's State needs no launch
+        self.state_tables[row].zero_()
+        self.state_centers[row].zero_()
+        self.free_rows.append(row)
 
     def release_many(self, owners):
         """``release(owner)`` for every owner in order, in one launch
@@ -232,19 +241,23 @@ class PageArena:
         offsets = [0]
         for _, st in states:
             offsets.append(offsets[-1] + len(st.leases))
-        idx = self.staging.copy(leases + offsets, self.release_idx)
+        rows = [st.row for _, st in states]
+        idx = self.staging.copy(leases + offsets + rows, self.release_idx)
         _lib.call("v1x_release_many", _lib.ptr(self.tables), _lib.ptr(idx), _lib.ptr(idx[len(leases):]),
                   len(states), _lib.ptr(self.refs), _lib.ptr(self.free), _lib.ptr(self.free_count),
                   torch.cuda.current_stream(self.device).cuda_stream, device=self.device)
+        # the released requests' table rows, zeroed in one pass each
+        r0 = len(leases) + len(offsets)
+        row_ids = idx[r0:r0 + len(rows)].long()
+        self.state_tables.index_fill_(0, row_ids, 0)
+        self.state_centers.index_fill_(0, row_ids, 0)
         self.kernel_launches += 1
         for _, st in states:
             self.free_leases.extend(st.leases)
-            self.free_rows.append(st.row)
+        self.free_rows.extend(rows)
 
     def _new_state(self, owner):
-        row = self.free_rows.pop()
-        self.state_tables[row].zero_()
-        self.state_centers[row].zero_()
+        row = self.free_rows.pop()     # zeroed when it was freed (or never used)
         state = self.states[owner] = State(self.pages, self.device, self.state_tables[row], self.state_centers[row],
                                            row)
         return state
@@ -289,16 +302,22 @@ class PageArena:
             tmp, mapping, centers = tmp.contiguous(), mapping.contiguous(), centers.contiguous()
             self.kernel_launches += 5
             _lib.call("v1x_prepare_buckets", _lib.ptr(tmp), _lib.ptr(centers), _lib.ptr(centers.view(torch.float32)),
-                      _lib.ptr(mapping), _lib.ptr(self.batch_meta), n, _lib.ptr(self.batch_hash),
-                      _lib.ptr(self.batch_match), _lib.ptr(self.batch_new), _lib.ptr(self.fine),
-                      _lib.ptr(self.centers), _lib.ptr(self.centers.view(torch.float32)), _lib.ptr(self.members),
-                      _lib.ptr(self.hashes), _lib.ptr(self.refs), _lib.ptr(self.free), _lib.ptr(self.free_count),
-                      _lib.ptr(self.tables), _lib.ptr(self.center_pages), _lib.ptr(self.state_tables),
-                      self.state_tables.stride(0), _lib.ptr(self.state_centers), self.state_centers.stride(0),
-                      self.capacity, _lib.ptr(self.batch_work), _lib.ptr(self.status),
-                      torch.cuda.current_stream(self.device).cuda_stream,
-                      device=self.device)
+                      _lib.ptr(mapping), _lib.ptr(self.batch_meta), n, *self._arena_args(),
+                      torch.cuda.current_stream(self.device).cuda_stream, device=self.device)
         pending.clear()
+
+    def _arena_args(self):
+        """v1x_prepare_buckets' arguments after `buckets` up to `status`: the
+        arena's own buffers, which never move, converted once."""
+        if self._prepare_args is None:
+            p = _lib.ptr
+            self._prepare_args = (
+                p(self.batch_hash), p(self.batch_match), p(self.batch_new), p(self.fine), p(self.centers),
+                p(self.centers.view(torch.float32)), p(self.members), p(self.hashes), p(self.refs), p(self.free),
+                p(self.free_count), p(self.tables), p(self.center_pages), p(self.state_tables),
+                self.state_tables.stride(0), p(self.state_centers), self.state_centers.stride(0), self.capacity,
+                p(self.batch_work), p(self.status))
+        return self._prepare_args
 
     def check(self):
         """Raise ArenaExhausted if an allocation found too few free pages (the
