@@ -290,12 +290,18 @@ class PageArena:
                     state.leases.append(lease)
                     pending.append((owner, bucket, lease, state.row))
                 state.length = length
-        finally:
+        except BaseException:
+            # as prepare() does, the buckets granted before the error are indexed
             self._flush(pending, batch_source)
+            raise
+        self._flush(pending, batch_source)
 
     def _flush(self, pending, batch_source):
-        for i in range(0, len(pending), BATCH_BUCKETS):
-            chunk = pending[i:i + BATCH_BUCKETS]
+        """Index the pending buckets, 64 per call; each chunk leaves `pending`
+        before its call, so no bucket is indexed twice."""
+        while pending:
+            chunk = pending[:BATCH_BUCKETS]
+            del pending[:BATCH_BUCKETS]
             n = len(chunk)
             tmp, mapping, centers = batch_source([(o, b) for o, b, _, _ in chunk])
             self.staging.copy([x for _, b, lease, row in chunk for x in (b * 1024, lease, 1, row)], self.batch_meta)
@@ -304,7 +310,6 @@ class PageArena:
             _lib.call("v1x_prepare_buckets", _lib.ptr(tmp), _lib.ptr(centers), _lib.ptr(centers.view(torch.float32)),
                       _lib.ptr(mapping), _lib.ptr(self.batch_meta), n, *self._arena_args(),
                       torch.cuda.current_stream(self.device).cuda_stream, device=self.device)
-        pending.clear()
 
     def _arena_args(self):
         """v1x_prepare_buckets' arguments after `buckets` up to `status`: the

@@ -230,3 +230,30 @@ def test_prepare_many_fingerprint_collisions(cuda_dev):
     t = {o: cpu.states[o]["table"] for o in chains}
     assert t[11][16 + 3] == t[11][3] != t[10][3]     # the copy shares its page, not the collision's
     assert t[12][5] != t[10][5]
+
+
+def test_prepare_many_error_matches_prepare(cuda_dev):
+    """Lease records running out inside a batched call: the same error as the
+    per-bucket driver, raised at the same bucket, and the same arena (the
+    buckets granted before it are indexed, none twice)."""
+    cap, pages = 64, 64                      # 4 lease records
+    wl = synth.LifecycleWorkload(requests=6, max_buckets=3, rounds=1, seed=9, max_leases=cap // 16, share=0.0)
+    a, b = sorted(wl.chains)[:2]
+    wl.chains[a], wl.chains[b] = [0, 1, 2], [3, 4, 5]
+    contents = wl.contents("cuda")
+    batched = lifecycle.PageArena(cap, pages, "cuda", max_requests=2)
+    single = lifecycle.PageArena(cap, pages, "cuda", max_requests=2)
+    with pytest.raises(RuntimeError, match="bucket records exhausted"):
+        batched.prepare_many([(a, 3 * 1024), (b, 3 * 1024)], wl.batch_source(contents))
+    single.prepare(a, 3 * 1024, wl.source(contents))
+    with pytest.raises(RuntimeError, match="bucket records exhausted"):
+        single.prepare(b, 3 * 1024, wl.source(contents))
+    batched.check()
+    single.check()
+    torch.cuda.synchronize()
+    for name in ("refs", "free", "free_count", "tables", "members", "hashes", "fine", "centers"):
+        assert torch.equal(getattr(batched, name), getattr(single, name)), name
+    for o in (a, b):
+        assert batched.states[o].leases == single.states[o].leases
+        assert torch.equal(batched.states[o].table, single.states[o].table)
+    assert len(batched.states[b].leases) == 1 and int(batched.free_count.item()) == 0
