@@ -670,6 +670,9 @@ extern "C" int v1x_prepare_buckets(const uint8_t* tmp, const uint8_t* tc_bytes, 
   clear_error();
   V1X_CHECK_ARG(buckets >= 0 && buckets <= kBatchBuckets, "prepare_buckets: at most %d buckets per call",
                 kBatchBuckets);
+  V1X_CHECK_ARG(tmp && tc_bytes && tc_scales && map && meta && hash && match && new_flags && fine && centers &&
+                    center_scales && members && hashes && refs && free_stack && count && tables,
+                "prepare_buckets: a required buffer is NULL");
   V1X_CHECK_ARG(cap > 0 && cap < INT_MAX, "prepare_buckets: bad capacity");
   V1X_CHECK_ARG(aligned16(tmp) && aligned16(fine) && aligned16(tc_bytes) && aligned16(centers),
                 "prepare_buckets: page pools must be 16-byte aligned");
@@ -702,6 +705,8 @@ extern "C" int v1x_release_many(const int32_t* tables, const int32_t* leases, co
   using namespace v1x;
   clear_error();
   V1X_CHECK_ARG(requests >= 0 && requests < INT_MAX, "release_many: bad request count");
+  V1X_CHECK_ARG(requests == 0 || (tables && leases && offsets && refs && free_stack && count),
+                "release_many: a required buffer is NULL");
   if (requests == 0) return V1X_OK;
   release_many_kernel<<<1, kReleaseThreads, 0, as_stream(stream)>>>(tables, leases, offsets,
                                                                     static_cast<int>(requests), refs, free_stack,
