@@ -18,7 +18,8 @@
 // box is the row's query and the next 15 rows' (zero past the batch), and the
 // epilogue reads only column 0 of the accumulator.
 //
-// Warp roles in a persistent CTA (352 threads, two CTAs per SM):
+// Warp roles in a persistent CTA (352 threads, two CTAs per SM; one head: 224
+// threads, a single epilogue group):
 //   warps 0-1  TMA producers (alternate tiles): two 8 KB page boxes (3-D tensor
 //              map over the packed pool, 128-byte swizzle) and the two pages'
 //              256-byte scale vectors.  Several issuing warps are needed: one
@@ -26,7 +27,8 @@
 //   warp 2     TMEM owner + single-thread MMA issuer; loads the row's q tile
 //              (H x 128) when the row changes; commits release the smem stage
 //              and publish the accumulator.
-//   warps 3-10 two epilogue groups (alternate tiles): tcgen05.ld of the
+//   warps 3-10 two epilogue groups (alternate tiles; one head: warps 3-6,
+//              one group): tcgen05.ld of the
 //              accumulator (one key per thread), ReLU, weighted head sum with
 //              the head weights staged in smem, per-key scale, coalesced store.
 // Each CTA owns a contiguous range of tiles (row, 128-key block), computed from
@@ -49,7 +51,9 @@ using namespace sm100;
 constexpr int kProducers = 2;                      // TMA issuing warps
 constexpr int kMmaWarp = kProducers;
 constexpr int kEpiWarp0 = kProducers + 1;          // first epilogue warp
-constexpr int kTcThreads = 32 * (kProducers + 1 + 8);
+constexpr int kTcThreads = 32 * (kProducers + 1 + 8);  // two epilogue groups (the most)
+template <int kGroups>
+constexpr int tc_threads() { return 32 * (kProducers + 1 + 4 * kGroups); }
 constexpr int kTcStages = 4;      // key smem stages (2 pages each)
 constexpr int kScaleSlots = 8;    // per-tile key scales (2 x 256 B), consumed by the epilogues
 constexpr int kQSlots = 2;        // per-row q tiles
@@ -130,7 +134,12 @@ struct TileCursor {
   }
 };
 
-__global__ void __launch_bounds__(kTcThreads, 2)
+// kGroups epilogue groups of four warps: two for many heads (a key's H columns
+// take a while to reduce), one for a single head, whose epilogue is one TMEM
+// column per key -- that CTA has 224 threads and at most 97 registers each, so
+// two of them leave an SM room for another batch's top-k or route CTA.
+template <int kGroups>
+__global__ void __launch_bounds__(tc_threads<kGroups>(), kGroups == 2 ? 2 : 3)
     score_tc_kernel(const __grid_constant__ CUtensorMap pool_map, const __grid_constant__ CUtensorMap q_map,
                     const __grid_constant__ CUtensorMap scale_map, const __grid_constant__ TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
@@ -178,7 +187,8 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     tma_prefetch_desc(&scale_map);
   }
   {
-    const int chunk = (a.B + kTcThreads - 1) / kTcThreads;
+    constexpr int kThreads = tc_threads<kGroups>();
+    const int chunk = (a.B + kThreads - 1) / kThreads;
     const int beg = min(tid * chunk, a.B), end = min(beg + chunk, a.B);
     int local = 0;
     for (int b = beg; b < end; ++b) local += tiles_of(a, b);
@@ -297,15 +307,15 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     const int i = q4 * 32 + lane;                 // key of the 128-key tile == TMEM lane
     // the epilogue warps alone stage the head weights (off the producers' path)
     if (w_staged)
-      for (int e = tid - 32 * kEpiWarp0; e < (b_last - b_first + 1) * a.H; e += kTcThreads - 32 * kEpiWarp0)
+      for (int e = tid - 32 * kEpiWarp0; e < (b_last - b_first + 1) * a.H; e += 128 * kGroups)
         wsm[e] = a.w[static_cast<int64_t>(b_first) * a.H + e];
-    asm volatile("bar.sync 1, %0;" ::"r"(kTcThreads - 32 * kEpiWarp0) : "memory");
+    asm volatile("bar.sync 1, %0;" ::"r"(128 * kGroups) : "memory");
     TileCursor cur;
     if (ntiles > g) {
       cur.start(prefix, a.B, T0);
       cur.advance(prefix, g);
     }
-    for (int it = g; it < ntiles; it += 2) {
+    for (int it = g; it < ntiles; it += kGroups) {
       const int acc = it % kMaxAcc, r = it % kScaleSlots;
       const int b = cur.b;
       const int64_t eff = row_eff(a, b);
@@ -360,17 +370,17 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
         if ((lane & 7) == 0 && key < a.max_len) a.page_max[b * a.page_stride + (key >> 3)] = m;
       }
-      cur.advance(prefix, 2);
+      cur.advance(prefix, kGroups);
     }
     // columns past the last tile: -inf logits (clean) and -inf page maxima (always)
-    const int e = tid - 32 * kEpiWarp0;   // 0..255 across both groups
+    const int e = tid - 32 * kEpiWarp0;   // 0 .. 128 * kGroups - 1 across the groups
     for (int b = blockIdx.x; b < a.B; b += gridDim.x) {
       const int64_t eff = row_eff(a, b);
       const int64_t start = eff > 0 ? (eff + 127) / 128 * 128 : 0;
       if (a.clean && a.out)
-        for (int64_t j = start + e; j < a.max_len; j += 256) a.out[b * a.out_stride + j] = -CUDART_INF_F;
+        for (int64_t j = start + e; j < a.max_len; j += 128 * kGroups) a.out[b * a.out_stride + j] = -CUDART_INF_F;
       if (a.page_max)
-        for (int64_t gg = start / 8 + e; gg < (a.max_len + 7) / 8; gg += 256)
+        for (int64_t gg = start / 8 + e; gg < (a.max_len + 7) / 8; gg += 128 * kGroups)
           a.page_max[b * a.page_stride + gg] = -CUDART_INF_F;
     }
   }
@@ -485,10 +495,16 @@ int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t 
               static_cast<int>(w_rows), lens_kind,
               cols, status};
   static DeviceOnce once;
-  if (once.first())
-    cudaFuncSetAttribute(score_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-  launch_kernel(score_tc_kernel, dim3(static_cast<unsigned>(grid)), dim3(kTcThreads), smem, stream, pool_map, q_map,
-             scale_map, args);
+  if (once.first()) {
+    cudaFuncSetAttribute(score_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(score_tc_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  }
+  if (heads == 1)
+    launch_kernel(score_tc_kernel<1>, dim3(static_cast<unsigned>(grid)), dim3(tc_threads<1>()), smem, stream,
+                  pool_map, q_map, scale_map, args);
+  else
+    launch_kernel(score_tc_kernel<2>, dim3(static_cast<unsigned>(grid)), dim3(tc_threads<2>()), smem, stream,
+                  pool_map, q_map, scale_map, args);
   return launch_status("v1x_score_fp8 (tensor core)");
 }
 
