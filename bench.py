@@ -853,7 +853,8 @@ def main():
     # L2 eviction before each diagnostic timing: a read of 256 MB that nothing
     # writes, so no dirty lines are left to be written back inside the timing
     flush = torch.ones(256 << 20, dtype=torch.uint8, device=device)
-    launches_per_step = 6 + (1 if gather_on else 0)
+    # per step: query_prepare, centre scoring, route, fine scoring, top-k (+ gather)
+    launches_per_step = 5 + (1 if gather_on else 0)
     main_stream = torch.cuda.current_stream(device)
 
     def timed(graph, n):
