@@ -547,6 +547,7 @@ def run_pages_workload(args, world, rank, device, dist):
                            per_bucket * buckets, "confirm_kernel + publish", 5, cpu, parity)
     line["steps"] = len(wl.ops) - 1
     line["ms_per_bucket"] = ms / max(buckets, 1)
+    line["stage_tail_shared"] = _stage_tail_shared_diag(device, rank)
     line["per_bucket_driver"] = {"value": pb_buckets * world / (pb_ms / 1e3), "unit": "buckets/s",
                                  "ms_per_bucket": pb_ms / max(pb_buckets, 1),
                                  "how": "PageArena.prepare: one captured graph of the four kernels per bucket "
@@ -554,6 +555,61 @@ def run_pages_workload(args, world, rank, device, dist):
     line["wall_s"] = wall
     line["gpu_launches"] = launches
     return line
+
+
+def _stage_tail_shared_diag(device, rank):
+    """The sink/tail staging of the d3 configuration: 1024 query rows in groups of
+    four sharing one request's tail (the owner row stages, the others read its
+    copy), as DS/test_page_management_and_tail_small.py:59-88 pairs them, after a
+    64K-token history; the reference's launch (grid (B/32, 68), 32 rows per
+    program).  Device time per launch from replays of a graph of 20 launches,
+    and a bit-exact spot check of a small case against the oracle."""
+    import numpy as np
+    K = importlib.import_module("10_20_b200.kernels")
+    oracle = importlib.import_module("oracle.v1x_oracle")
+    B, NP, pool, cap, scratch = 1024, 1026, 32768, 64, 68
+    gen = torch.Generator(device=device).manual_seed(61 + rank)
+    native = torch.randint(0, 256, (pool, 8448), generator=gen, device=device, dtype=torch.uint8)
+    nt = torch.randint(0, pool, (B, NP), generator=gen, device=device, dtype=torch.int32)
+    lens = (65536 + torch.arange(B, device=device) % 4).to(torch.int32)
+    owners = (torch.arange(B, device=device) // 4 * 4).to(torch.int32)
+    fine = torch.zeros((cap + B * scratch, 8448), dtype=torch.uint8, device=device)
+    own_each = torch.arange(B, device=device, dtype=torch.int32)   # every row its own tail (no sharing)
+    out = {}
+    for tag, own, window in (("groups_of_4", owners, 64), ("groups_of_4", owners, 2048),
+                             ("every_row_owns", own_each, 2048)):
+        def launch(own=own, window=window):
+            K.stage_tail_shared[((B + 31) // 32, scratch)](native, native.view(torch.float32), nt, lens, fine,
+                                                          fine.view(torch.float32), own, cap, NP, scratch, 64,
+                                                          window, ROWS=B, GROUP=32)
+
+        def launch_n():
+            for _ in range(20):
+                launch()
+        g = _capture(launch_n, device)
+        ms, _ = _timed_replays(g, 50, 3, None, device)
+        us = ms / (50 * 20) * 1e3
+        count = 64 + min(window, 65536 - 64)                 # staged tokens per owner (sink + window)
+        moved = int((own == torch.arange(B, device=device)).sum()) * -(-count // 64) * 8448 * 2
+        out[f"{tag}_window_{window}"] = {"us_per_launch": us, "bytes_moved": moved,
+                                         "gb_per_s": moved / (us * 1e-6) / 1e9}
+    # spot check: 8 rows (two groups of four) of a small pool against the oracle
+    b, np_, pl = 8, 20, 64
+    nat_s = torch.randint(0, 256, (pl, 8448), generator=gen, device=device, dtype=torch.uint8)
+    nt_s = torch.randint(0, pl, (b, np_), generator=gen, device=device, dtype=torch.int32)
+    lens_s = torch.tensor([1100, 1101, 1102, 1103, 1230, 1231, 1232, 1233], dtype=torch.int32, device=device)
+    own_s = torch.tensor([0, 0, 0, 0, 4, 4, 4, 4], dtype=torch.int32, device=device)
+    fine_s = torch.full((4 + b * scratch, 8448), 7, dtype=torch.uint8, device=device)
+    K.stage_tail_shared[((b + 31) // 32, scratch)](nat_s, nat_s.view(torch.float32), nt_s, lens_s, fine_s,
+                                                  fine_s.view(torch.float32), own_s, 4, np_, scratch, 64, 64,
+                                                  ROWS=b, GROUP=32)
+    exp = oracle.stage_tail_shared(nat_s.cpu().numpy(), nt_s.cpu().numpy(), lens_s.cpu().numpy(),
+                                   np.full((4 + b * scratch, 8448), 7, np.uint8), own_s.cpu().numpy(), 4, np_,
+                                   scratch, 64, 64, b, 32, (b + 31) // 32, scratch)
+    out["parity_spot_check"] = bool(np.array_equal(fine_s.cpu().numpy(), exp))
+    out["config"] = ("1024 rows after a 64K-token history (+0..3 tokens), sink 64; owners stage sink + tail "
+                     "pages (read + write counted); grid (32, 68), 32 rows per program")
+    return out
 
 
 def run_build_workload(args, world, rank, device, dist):
