@@ -32,13 +32,19 @@ __global__ void __launch_bounds__(1024) sort_kernel(const int32_t* __restrict__ 
                                                     const float* __restrict__ S,
                                                     const int32_t* __restrict__ flag, int N) {
   extern __shared__ unsigned long long list[];
-  if (*flag >= 0) return;
+  int* sP = reinterpret_cast<int*>(list + N);  // the segment's P values, for the final permutation
+  // the flag, the scores and P are loaded together (no dependent round trips)
+  const int f = *flag;
   const int64_t base = static_cast<int64_t>(blockIdx.y) * 4096 + static_cast<int64_t>(blockIdx.x) * N;
-  for (int i = threadIdx.x; i < N; i += blockDim.x) list[i] = sort_key(S[base + i], i);
+  for (int i = threadIdx.x; i < N; i += blockDim.x) {
+    list[i] = sort_key(S[base + i], i);
+    sP[i] = P[base + i];
+  }
+  if (f >= 0) return;
   bitonic_sort_desc(list, N);
   for (int i = threadIdx.x; i < N; i += blockDim.x) {
     const int pos = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(list[i] & 0xFFFFFFFFull));
-    O[base + i] = P[base + pos];
+    O[base + i] = sP[pos];
   }
 }
 
@@ -255,7 +261,7 @@ extern "C" int v1x_sort_segments(const int32_t* P, int32_t* O, const float* S, c
     case 32: sort_radix_kernel<32, 1, false><<<grid, 32, 0, s>>>(P, O, S, flag, nullptr, 0, 0); break;
     default: {  // below 32 records, or unaligned scores / output
       const int threads = static_cast<int>(N / 2 < 1024 ? (N / 2 < 32 ? 32 : N / 2) : 1024);
-      sort_kernel<<<grid, threads, static_cast<size_t>(N) * 8, s>>>(P, O, S, flag, static_cast<int>(N));
+      sort_kernel<<<grid, threads, static_cast<size_t>(N) * 12, s>>>(P, O, S, flag, static_cast<int>(N));
     }
   }
   return launch_status("v1x_sort_segments");

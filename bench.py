@@ -297,6 +297,17 @@ def run_sort_workload(args, world, rank, device, dist):
 
     g = _capture(step, device)
     ms, clk = _timed_replays(g, args.steps, args.warmup, dist, device)
+    # the reference's published configuration: one grouping level of one head
+    # (4096 records in segments of N), one _sort launch, timed in a graph of 20
+    one_level = {}
+    out1 = torch.empty_like(P[0])                 # its own output: out feeds the parity check
+    for n in (1024, 512, 256, 128, 64, 32, 16):
+        def level(n=n):
+            for _ in range(20):
+                fg._sort[(4096 // n, 1)](P[0], out1, S[0], flag, n)
+        gl = _capture(level, device)
+        ml, _ = _timed_replays(gl, 50, 3, None, device)
+        one_level[f"N={n}"] = ml / (50 * 20) * 1e3
     records = heads * 4096
     value = records * args.steps * world / (ms / 1e3)
     bytes_per_step = records * 12 + heads * 4097 * 4
@@ -313,12 +324,14 @@ def run_sort_workload(args, world, rank, device, dist):
         rate, n, el = _cpu_rate(lambda: oracle.sort_segments(Pn, k16, -1, 4096, 1, 16), 16 * 4096)
         cpu = {"value": rate, "unit": "records/s", "cores": 1, "kind": "port",
                "sample": f"{n} calls of one 16 x 4096 instance, oracle sort_segments (numpy lexsort), {el:.1f} s"}
-    return _component_line(args, world, "stable-grouped records/s (_sort + group offsets)", "records/s", value,
+    line = _component_line(args, world, "stable-grouped records/s (_sort + group offsets)", "records/s", value,
                            args.steps, ms, clk,
                            {"workload": "sort", "instances_per_gpu": inst, "records_per_instance": 65536,
                             "segments": "16 x 4096 per instance", "keys": "group ids U[0,4096), ~30% duplicate runs",
                             "bytes_per_step": bytes_per_step}, bytes_per_step, "sort_radix_kernel<512,8,offsets>",
                            1, cpu, parity)
+    line["one_level_one_head_us"] = one_level   # _sort[(4096 // N, 1)] on 4096 records, per launch
+    return line
 
 
 def run_gather_workload(args, world, rank, device, dist):
