@@ -176,7 +176,8 @@ def run_reference(args, cfg):
     value = done / el
     cores = os.cpu_count()
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / max(done, 1) * 1e3,
+            "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "fp8-e4m3 keys, f32 scores, bf16 latent", "data": "synthetic",
             "config": {"workload": args.workload, **{k: v for k, v in cfg.items()}},
             "cpu_baseline": {"value": value, "unit": "queries/s", "cores": cores, "kind": "port",
