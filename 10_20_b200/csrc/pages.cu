@@ -27,8 +27,11 @@
 // pop the free stack as allocate does -- and one publish over all buckets.
 // The answers equal the sequential per-bucket calls: refcounts only grow during
 // a prepare, so a page live at the start stays live; a page content is live at
-// most once (a second copy would have matched the first); and a page that is
-// not live at the start can only match a page published inside the batch.
+// most once (a second copy would have matched the first -- given that a
+// bucket's own 16 pages are distinct, their members being disjoint token
+// positions); and a page that is not live at the start can only match a page
+// published inside the batch.  (The CPU test suite restates this algorithm in
+// numpy and compares it with the per-bucket sequence on randomised calls.)
 #include <climits>
 
 #include "common.cuh"

@@ -320,7 +320,11 @@ V1X_API int v1x_release(const int32_t* table, int32_t* refs, int32_t* free_stack
  * receiving tables[lease] at columns start/1024*16 and center_pages[lease] at
  * start/1024*2 of the bucket's state row.  The first bucket that finds the
  * free stack too short writes V1X_STATUS_ARENA_EXHAUSTED to *status; it and
- * every later bucket of the call change nothing. */
+ * every later bucket of the call change nothing.  Precondition: a bucket's 16
+ * pages are distinct (their members are disjoint token positions, as every
+ * index build produces); two identical pages in one bucket would both be
+ * published, and a later bucket of the same call could then take the other
+ * copy than the per-bucket sequence's lowest one. */
 /* Extension (no reference counterpart): Indexer._release (DS/runtime.py:771-780,
  * kernel DS/kernels.py:170-179) for several requests in one launch.  leases i32
  * = the requests' lease ids, request after request, each request's in order;

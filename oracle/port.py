@@ -127,3 +127,115 @@ class ArenaPort:
             for lease in st["leases"]:
                 self.count = O.release(self.tables[lease], self.refs, self.free, self.count)
                 self.free_leases.append(lease)
+
+
+# --------------------------------------------------------------------------
+# batched lifecycle (the algorithm of v1x_prepare_buckets / v1x_release_many),
+# restated to check that it gives the per-bucket sequence's arena state
+# --------------------------------------------------------------------------
+
+COLLISION = -2
+
+
+def _same_page(bytes_a, bytes_b, members_a, members_b):
+    return np.array_equal(bytes_a, bytes_b) and np.array_equal(members_a, members_b)
+
+
+def prepare_buckets_batched(arena, tmp, centers, mapping, meta):
+    """The batched prepare on an ArenaPort's arrays: tmp u8 [nb, 16, 8448],
+    centers u8 [nb, 2, 8448], mapping i32 [nb, 16, 64], meta i32 [nb, 3] =
+    (token start, lease, active).  Steps: fingerprints; each page's lowest
+    match among the pages live at the START of the call; each page's lowest
+    equal-fingerprint page in an earlier bucket, kept if its bytes and members
+    are equal, else marked as a collision; then bucket by bucket the allocate
+    decision -- no live match: the slot of the earliest equal page (or, after a
+    collision, of an equal page published earlier in the call); fresh pages pop
+    the free stack -- and the first bucket that finds the stack too short stops
+    the call (it and the later buckets change nothing); finally publish.
+    Returns (new flags [nb*16] with 2 = not allocated, exhausted: bool)."""
+    nb = tmp.shape[0]
+    nq = nb * 16
+    tp = tmp.reshape(nq, O.PAGE_BYTES)
+    mp = mapping.reshape(nq, 64)
+    active = np.repeat(np.asarray(meta)[:, 2] != 0, 16)
+    h = O.fingerprint(tp, mp)
+    live = arena.refs[:arena.capacity] > 0          # snapshot at the start of the call
+    match = np.full(nq, -1, np.int64)
+    for q in np.nonzero(active)[0]:
+        cand = np.nonzero(live & (arena.hashes[:, 0] == h[q, 0]) & (arena.hashes[:, 1] == h[q, 1]))[0]
+        for j in cand:
+            if _same_page(arena.fine[j], tp[q], arena.members[j], mp[q]):
+                match[q] = j
+                break
+    first = {}
+    for q in np.nonzero(active)[0]:
+        b0 = q // 16 * 16
+        earlier = [p for p in range(b0) if active[p] and h[p, 0] == h[q, 0] and h[p, 1] == h[q, 1]]
+        if earlier:
+            p = earlier[0]
+            first[q] = p if _same_page(tp[p], tp[q], mp[p], mp[q]) else COLLISION
+    dst = np.full(nq, -1, np.int64)
+    new = np.zeros(nq, np.uint8)
+    fresh_so_far = []
+    exhausted = False
+    for b in range(nb):
+        if meta[b][2] == 0:
+            continue
+        qs = list(range(b * 16, b * 16 + 16))
+        if exhausted:
+            new[qs] = 2
+            continue
+        m = []
+        for q in qs:
+            mq = match[q]
+            if mq < 0 and q in first:
+                if first[q] != COLLISION:
+                    mq = dst[first[q]]
+                else:
+                    for p in fresh_so_far:
+                        if (h[p] == h[q]).all() and _same_page(tp[p], tp[q], mp[p], mp[q]):
+                            mq = dst[p]
+                            break
+            m.append(mq)
+        fresh = [x < 0 for x in m]
+        needed = sum(fresh)
+        if arena.count < needed:
+            exhausted = True
+            new[qs] = 2
+            continue
+        rank = 0
+        lease = int(meta[b][1])
+        for i, q in enumerate(qs):
+            if fresh[i]:
+                d = int(arena.free[arena.count - 1 - rank])
+                rank += 1
+                fresh_so_far.append(q)
+            else:
+                d = int(m[i])
+            arena.refs[d] += 1
+            arena.tables[lease, i] = d
+            dst[q] = d
+            new[q] = 1 if fresh[i] else 0
+        arena.count -= needed
+    for b in range(nb):
+        if meta[b][2] != 0 and new[b * 16] != 2:
+            O.publish(tmp[b], centers[b], mapping[b], h[b * 16:(b + 1) * 16], meta[b], arena.tables,
+                      new[b * 16:(b + 1) * 16].astype(bool), arena.fine, arena.centers, arena.members, arena.hashes)
+    return new, exhausted
+
+
+def release_many(arena, requests_leases):
+    """The batched release on an ArenaPort's arrays: requests one after another;
+    within a request every lease's pages are decremented at once and the pages
+    that reach zero are pushed in (lease, lane) order.  Equals the per-lease
+    release sequence when a request's pages are distinct (asserted)."""
+    for leases in requests_leases:
+        pages = [int(arena.tables[lease, i]) for lease in leases for i in range(16)]
+        assert len(set(pages)) == len(pages), "a request's pages must be distinct"
+        dead = []
+        for page in pages:
+            arena.refs[page] -= 1
+            if arena.refs[page] == 0:
+                dead.append(page)
+        arena.free[arena.count:arena.count + len(dead)] = dead
+        arena.count += len(dead)
