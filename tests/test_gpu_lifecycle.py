@@ -257,3 +257,80 @@ def test_prepare_many_error_matches_prepare(cuda_dev):
         assert batched.states[o].leases == single.states[o].leases
         assert torch.equal(batched.states[o].table, single.states[o].table)
     assert len(batched.states[b].leases) == 1 and int(batched.free_count.item()) == 0
+
+
+@pytest.mark.parametrize("seed", range(4))
+def test_prepare_buckets_entry_point_random_batches(seed, cuda_dev):
+    """v1x_prepare_buckets called directly (the C ABI), on randomised calls with
+    inactive buckets, pages live before the call, pages published earlier in the
+    call, fingerprint collisions and (some seeds) a short free stack, against the
+    numpy restatement of the batched algorithm -- which the CPU tests tie to the
+    reference's per-bucket sequence."""
+    import copy
+
+    import oracle.v1x_oracle as O
+    _lib = importlib.import_module("10_20_b200._lib")
+    rng = np.random.default_rng(200 + seed)
+    cap, pages = 512, 256
+    cpu = port.ArenaPort(cap, pages, max_requests=8)
+    live = []
+    for b in range(3):
+        tmp = rng.integers(0, 256, (16, 8448), dtype=np.uint8)
+        mp = (100000 * (b + 1) + np.arange(1024)).astype(np.int32).reshape(16, 64)
+        cpu._bucket(tmp, mp, rng.integers(0, 256, (2, 8448), dtype=np.uint8), b * 1024, b)
+        live += [(tmp[i], mp[i]) for i in range(16)]
+    nb = 8
+    tmp = np.zeros((nb, 16, 8448), np.uint8)
+    mp = np.zeros((nb, 16, 64), np.int32)
+    made = []
+    for b in range(nb):
+        seen = set()
+        for i in range(16):
+            while True:
+                kind = rng.integers(0, 4)
+                if kind == 0 or (kind == 2 and not made):
+                    x = rng.integers(0, 256, 8448, dtype=np.uint8)
+                    m = (900000 + 4096 * b + 64 * i + np.arange(64)).astype(np.int32)
+                elif kind == 1:
+                    x, m = live[int(rng.integers(len(live)))]
+                elif kind == 2:
+                    x, m = made[int(rng.integers(len(made)))]
+                else:
+                    x, m = (live + made)[int(rng.integers(len(live) + len(made)))]
+                    m = m.copy()
+                    m[:3] += np.array([1, -2, 1], np.int32)
+                if (x.tobytes(), m.tobytes()) not in seen:
+                    seen.add((x.tobytes(), m.tobytes()))
+                    break
+            tmp[b, i], mp[b, i] = x, m
+        made += [(tmp[b, i].copy(), mp[b, i].copy()) for i in range(16)]
+    centers = rng.integers(0, 256, (nb, 2, 8448), dtype=np.uint8)
+    active = (rng.random(nb) > 0.25).astype(np.int32)
+    meta3 = np.array([[b * 1024, 3 + b, active[b]] for b in range(nb)], np.int32)
+    if seed % 2:
+        cpu.count = int(rng.integers(10, 60))
+    exp = copy.deepcopy(cpu)
+    new_exp, exhausted_exp = port.prepare_buckets_batched(exp, tmp, centers, mp, meta3)
+    # the same starting arena on the GPU
+    gpu = lifecycle.PageArena(cap, pages, "cuda", max_requests=8)
+    for name in ("refs", "free", "tables", "members", "hashes", "fine", "centers"):
+        getattr(gpu, name).copy_(torch.from_numpy(np.ascontiguousarray(getattr(cpu, name))))
+    gpu.free_count.fill_(cpu.count)
+    meta = torch.tensor([[b * 1024, 3 + b, active[b], 0] for b in range(nb)], dtype=torch.int32, device="cuda")
+    t, m, c = (torch.from_numpy(a).cuda() for a in (tmp, mp, centers))
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    work = torch.zeros(lifecycle.PREPARE_WORK_INTS, dtype=torch.int32, device="cuda")
+    hsh = torch.zeros((nb * 16, 2), dtype=torch.int64, device="cuda")
+    match = torch.zeros(nb * 16, dtype=torch.int32, device="cuda")
+    new = torch.zeros(nb * 16, dtype=torch.uint8, device="cuda")
+    p = _lib.ptr
+    _lib.call("v1x_prepare_buckets", p(t), p(c), p(c.view(torch.float32)), p(m), p(meta), nb, p(hsh), p(match),
+              p(new), p(gpu.fine), p(gpu.centers), p(gpu.centers.view(torch.float32)), p(gpu.members),
+              p(gpu.hashes), p(gpu.refs), p(gpu.free), p(gpu.free_count), p(gpu.tables), p(gpu.center_pages),
+              None, 0, None, 0, cap, p(work), p(status), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert int(gpu.free_count.item()) == exp.count
+    for name in ("refs", "free", "tables", "members", "hashes", "fine", "centers"):
+        assert np.array_equal(getattr(gpu, name).cpu().numpy(), getattr(exp, name)), name
+    assert (int(status.item()) == _lib.V1X_STATUS_ARENA_EXHAUSTED) == exhausted_exp
+    assert np.array_equal(new.cpu().numpy(), new_exp)
