@@ -29,6 +29,7 @@
 // centre's mean adds its 8 members in order.  The centre scale is the smallest
 // power of two >= max|mean| / 448 (exactly; the reference's exp2(ceil(log2()))
 // can land one power lower a few ulps above a power of two).
+#include <atomic>
 #include <cooperative_groups.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -577,7 +578,7 @@ extern "C" int v1x_build_buckets(const uint8_t* native, int64_t native_pages, co
                 "build_buckets: native, tmp and work must be 16-byte aligned");
   if (buckets == 0) return V1X_OK;
   static DeviceOnce once;
-  if (once.first()) set_smem_attr(reinterpret_cast<const void*>(build_bucket_kernel));
+  once.run([] { set_smem_attr(reinterpret_cast<const void*>(build_bucket_kernel)); });
   BuildArgs a{native, native_pages, source, starts, tmp, centers, mapping, perm, static_cast<uint8_t*>(work), status};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(kBuildCtas, static_cast<unsigned>(buckets));
@@ -617,27 +618,30 @@ extern "C" int v1x_build_buckets_noalloc(const uint8_t* native, int64_t native_p
   V1X_CHECK_ARG((reinterpret_cast<uintptr_t>(native) & 15) == 0 && (reinterpret_cast<uintptr_t>(tmp) & 15) == 0,
                 "build_buckets_noalloc: native and tmp must be 16-byte aligned");
   if (buckets == 0) return V1X_OK;
-  // the scratch array's address on the current device, looked up once per
-  // device with that device current
-  static void* scratch[DeviceOnce::kMaxDevices] = {};
+  // The scratch array's address on the current device, looked up once per
+  // device with that device current.  Host code may not pass the array's name
+  // to a kernel: on the host it names a stand-in, not device memory.  The
+  // per-device slots are atomics, so first calls from several host threads do
+  // not race; a failed lookup leaves the slot empty and is retried next call.
+  static std::atomic<void*> scratch[DeviceOnce::kMaxDevices];
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess || dev < 0 || dev >= DeviceOnce::kMaxDevices) {
     set_error("build_buckets_noalloc: no current device (%s)", cudaGetErrorString(e));
     return V1X_ERR_CUDA;
   }
-  if (scratch[dev] == nullptr) {
-    void* addr = nullptr;
-    e = cudaGetSymbolAddress(&addr, g_build_scratch);
-    if (e != cudaSuccess || addr == nullptr) {
+  void* work = scratch[dev].load(std::memory_order_acquire);
+  if (work == nullptr) {
+    e = cudaGetSymbolAddress(&work, g_build_scratch);
+    if (e != cudaSuccess || work == nullptr) {
       set_error("build_buckets_noalloc: scratch lookup failed (%s)", cudaGetErrorString(e));
       return V1X_ERR_CUDA;
     }
-    scratch[dev] = addr;
+    scratch[dev].store(work, std::memory_order_release);  // every thread finds the same address
   }
   static DeviceOnce once;
-  if (once.first()) set_smem_attr(reinterpret_cast<const void*>(build_bucket_kernel));
-  BuildArgs a{native, native_pages, source, starts, tmp, centers, mapping, perm, static_cast<uint8_t*>(scratch[dev]),
+  once.run([] { set_smem_attr(reinterpret_cast<const void*>(build_bucket_kernel)); });
+  BuildArgs a{native, native_pages, source, starts, tmp, centers, mapping, perm, static_cast<uint8_t*>(work),
               status};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(kBuildCtas, static_cast<unsigned>(buckets));
@@ -713,7 +717,7 @@ extern "C" int v1x_assemble(const uint8_t* native, int64_t native_pages, const i
                     (reinterpret_cast<uintptr_t>(tmp) & 15) == 0,
                 "assemble: native and tmp must be 16-byte aligned");
   static DeviceOnce once;
-  if (once.first()) set_smem_attr(reinterpret_cast<const void*>(assemble_kernel));
+  once.run([] { set_smem_attr(reinterpret_cast<const void*>(assemble_kernel)); });
   BuildArgs a{native, native_pages, table, nullptr, tmp, centers, mapping, nullptr, nullptr, nullptr};
   assemble_kernel<<<kBucket / kSlice, kBuildThreads, sizeof(BuildSmem), as_stream(stream)>>>(a, meta, ids);
   return launch_status("v1x_assemble");

@@ -5,6 +5,9 @@
 #include <stdint.h>
 #include <math_constants.h>
 
+#include <mutex>
+#include <utility>
+
 #include "../../include/v1x.h"
 
 namespace v1x {
@@ -28,16 +31,21 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 
 int num_sms();
 
-// Per-device "first time" flag for one-off host set-up (function attributes).
+// Per-device one-off host set-up (function attributes).  run(f) calls f once
+// per device, the current one, under std::call_once: a thread that arrives
+// while another runs the set-up waits for it to finish, so no launch can
+// precede its kernel's attributes.
 struct DeviceOnce {
   static constexpr int kMaxDevices = 64;
-  volatile bool done[kMaxDevices] = {};
-  bool first() {
+  std::once_flag flags[kMaxDevices];
+  template <typename F>
+  void run(F&& f) {
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return true;
-    if (done[dev]) return false;
-    done[dev] = true;
-    return true;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+      f();  // no usable device index: set up every time (idempotent attributes)
+      return;
+    }
+    std::call_once(flags[dev], std::forward<F>(f));
   }
 };
 

@@ -11,7 +11,10 @@
 //    atomicMin keeps the lowest confirmed j -- the same answer for any CAP.
 //  - allocate (:116-131): fresh pages pop FREE[count-1-rank]; where the
 //    reference device_asserts on an exhausted arena, this kernel writes
-//    V1X_STATUS_ARENA_EXHAUSTED to a status word and changes nothing.
+//    V1X_STATUS_ARENA_EXHAUSTED to a status word and changes nothing in the
+//    arena; the lease's table row reads -1 (no page).  The status is sticky:
+//    later allocations on the same word abort as well until the host clears
+//    it, as nothing runs after the reference's trap.  release skips -1 entries.
 //  - publish (:134-167), release (:170-179): as the reference, vectorised.
 //
 // Batched prepare (extension): the buckets of one or more prepares, in the
@@ -176,9 +179,18 @@ __global__ void allocate_kernel(const int32_t* __restrict__ meta, const int32_t*
   const int rank = __popc(fm & ((1u << lane) - 1u));
   const int needed = __popc(fm);
   const int cnt = *count;
-  if (cnt < needed) {
-    // nothing changes; the flags tell publish that the bucket was not allocated
-    if (lane < 16) new_flags[lane] = kAborted;
+  // An exhaustion is sticky: once the status word holds it, every later
+  // allocation on that word aborts too (the reference traps at the first one),
+  // until the host reads and clears it.
+  const bool sticky = status != nullptr && *status == V1X_STATUS_ARENA_EXHAUSTED;
+  if (cnt < needed || sticky) {
+    // nothing in the arena changes; the flags tell publish that the bucket was
+    // not allocated, and the lease's table row reads -1 (no page), so a later
+    // release of the lease touches no refcount
+    if (lane < 16) {
+      new_flags[lane] = kAborted;
+      tables[static_cast<int64_t>(meta[1]) * 16 + lane] = -1;
+    }
     if (lane == 0 && status) *status = V1X_STATUS_ARENA_EXHAUSTED;
     return;
   }
@@ -236,7 +248,7 @@ __global__ void release_kernel(const int32_t* __restrict__ table, int32_t* __res
   bool dead = false;
   if (lane < 16) {
     page = table[lane];
-    dead = atomicSub(&refs[page], 1) == 1;
+    dead = page >= 0 && atomicSub(&refs[page], 1) == 1;  // -1: a lease whose allocation aborted
   }
   const unsigned dm = __ballot_sync(0xffffffffu, dead);
   const int rank = __popc(dm & ((1u << lane) - 1u));
@@ -436,7 +448,8 @@ __global__ void __launch_bounds__(256) confirm_kernel(const uint8_t* __restrict_
 // memory from the top of the stack), refcounts, lease table and new-page
 // flags.  The first bucket that finds the free stack too short writes
 // V1X_STATUS_ARENA_EXHAUSTED and it and every later bucket change nothing
-// (flags = aborted).  With state_tables, the request's page-table row (state
+// (flags = aborted, lease table rows = -1); a status word that already holds
+// the exhaustion aborts every bucket of the call.  With state_tables, the request's page-table row (state
 // row from the meta record) and centre-table row receive the bucket's pages,
 // as the driver's copies of the lease tables do after each reference Build.
 struct StateRows {
@@ -476,13 +489,18 @@ __global__ void __launch_bounds__(128) decide_kernel(
   const int lane = threadIdx.x;
   const uint32_t lt = (1u << lane) - 1u;
   int cnt = cnt0;
-  bool aborted = false;
+  // sticky exhaustion: an earlier call's exhaustion, not yet cleared by the
+  // host, aborts this call too
+  bool aborted = status != nullptr && *status == V1X_STATUS_ARENA_EXHAUSTED;
   for (int b = 0; b < nb; ++b) {
     const int* bm = smeta + b * kBatchMeta;  // token start, lease, active, state row
     if (bm[2] == 0) continue;                 // inactive bucket: nothing to do
     const int qi = b * 16 + lane;
     if (aborted) {
-      if (lane < 16) new_flags[qi] = kAborted;
+      if (lane < 16) {
+        new_flags[qi] = kAborted;
+        tables[static_cast<int64_t>(bm[1]) * 16 + lane] = -1;
+      }
       continue;
     }
     int m = -1;
@@ -526,7 +544,10 @@ __global__ void __launch_bounds__(128) decide_kernel(
     const int needed = __popc(fm);
     if (cnt < needed) {
       aborted = true;
-      if (lane < 16) new_flags[qi] = kAborted;
+      if (lane < 16) {
+        new_flags[qi] = kAborted;
+        tables[static_cast<int64_t>(bm[1]) * 16 + lane] = -1;
+      }
       if (lane == 0 && status) *status = V1X_STATUS_ARENA_EXHAUSTED;
       continue;
     }
@@ -571,7 +592,7 @@ __global__ void __launch_bounds__(kReleaseThreads) release_many_kernel(
       int page = 0, dead = 0;
       if (i < o1) {
         page = tables[static_cast<int64_t>(leases[i / 16]) * 16 + i % 16];
-        dead = atomicSub(&refs[page], 1) == 1;
+        dead = page >= 0 && atomicSub(&refs[page], 1) == 1;  // -1: an aborted lease
       }
       int total;
       const int rank = block_exclusive_scan(dead, warp_tot, &total);

@@ -233,13 +233,13 @@ int route_launch(bool pages_in, const float* scores, int64_t score_stride, int64
               fill_table && pages <= kRouteMaxItems ? 1 : 0};
   const size_t smem = kRouteListOff + static_cast<size_t>(n_items) * 8 + (a.stage_rt ? static_cast<size_t>(pages) * 4 : 0);
   static DeviceOnce once;
-  if (once.first()) {
+  once.run([] {
     const int most = static_cast<int>(kRouteListOff + kRouteMaxItems * 12);
     cudaFuncSetAttribute(route_kernel<false, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
     cudaFuncSetAttribute(route_kernel<true, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
     cudaFuncSetAttribute(route_kernel<false, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
     cudaFuncSetAttribute(route_kernel<true, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
-  }
+  });
   const dim3 grid(static_cast<unsigned>(batch)), block(kRouteThreads);
   static_assert(kRouteSmallItems <= 2 * kRouteThreads && kRouteMaxItems <= 16 * kRouteThreads, "route slots per thread");
   if (n_items <= kRouteSmallItems) {

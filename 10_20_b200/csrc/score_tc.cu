@@ -495,10 +495,10 @@ int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t 
               static_cast<int>(w_rows), lens_kind,
               cols, status};
   static DeviceOnce once;
-  if (once.first()) {
+  once.run([] {
     cudaFuncSetAttribute(score_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     cudaFuncSetAttribute(score_tc_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-  }
+  });
   if (heads == 1)
     launch_kernel(score_tc_kernel<1>, dim3(static_cast<unsigned>(grid)), dim3(tc_threads<1>()), smem, stream,
                   pool_map, q_map, scale_map, args);

@@ -380,11 +380,11 @@ extern "C" int v1x_route_physical(const float* scores, int64_t score_stride, con
   const int n_items = items * 128;
   const size_t smem = kPhysListOff + static_cast<size_t>(n_items) * 8;
   static DeviceOnce once;
-  if (once.first()) {
+  once.run([] {
     const int most = static_cast<int>(kPhysListOff + kPhysMaxItems * 8);
     cudaFuncSetAttribute(route_physical_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
     cudaFuncSetAttribute(route_physical_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
-  }
+  });
   const dim3 grid(static_cast<unsigned>(rows)), block(kPhysThreads);
   if (n_items <= 2 * kPhysThreads)
     launch_kernel(route_physical_kernel<2>, grid, block, smem, as_stream(stream), scores, score_stride, published,

@@ -630,8 +630,9 @@ extern "C" int v1x_topk(float* scores, int64_t score_stride, int64_t cols, const
       a.memb_off = static_cast<int>(cols_pad);
       a.ntab_off = static_cast<int>(cols_pad + stake * 64);
       static DeviceOnce once4;
-      if (once4.first())
+      once4.run([&] {
         cudaFuncSetAttribute(topk_kernel<2, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(limit4));
+      });
       launch_kernel(topk_kernel<2, 256>, grid, dim3(256), static_cast<size_t>(bytes()), s, a);
       return launch_status("v1x_topk");
     }
@@ -647,12 +648,12 @@ extern "C" int v1x_topk(float* scores, int64_t score_stride, int64_t cols, const
     a.memb_off = static_cast<int>(cols_pad);
     a.ntab_off = static_cast<int>(cols_pad + stake * 64);
     static DeviceOnce once;
-    if (once.first()) {
+    once.run([&] {
       cudaFuncSetAttribute(topk_kernel<1, kTopkThreads>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(limit));
       cudaFuncSetAttribute(topk_kernel<2, kTopkThreads>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(limit));
-    }
+    });
     if (cols <= kRegKeys * kTopkThreads)
       launch_kernel(topk_kernel<2, kTopkThreads>, grid, dim3(kTopkThreads), static_cast<size_t>(bytes()), s, a);
     else

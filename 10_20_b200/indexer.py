@@ -201,7 +201,8 @@ class Indexer:
                     max_rows[key] = i
             for key, i in max_rows.items():
                 self._prepare(key, native_tables[i], cpu[i])
-            self.arena.check()
+            if self.arena.pending_check:      # new buckets: read the status word (a sync)
+                self.arena.check()
             outputs = []
             for start in range(0, n, c.q_buckets[-1]):
                 end = min(n, start + c.q_buckets[-1])

@@ -136,6 +136,9 @@ class PageArena:
         self.state_centers = torch.zeros((self.max_requests, pages // 8), dtype=torch.int32, device=d)
         self.free_rows = list(range(self.max_requests - 1, -1, -1))
         self.kernel_launches = 0   # kernels this driver has launched (reported by the bench)
+        # (owner, bucket, lease) of every bucket launched since the last check(),
+        # in launch order: an exhaustion aborts a suffix of them
+        self.unchecked: list = []
         self._prepare_args = None
         # batched prepare: meta records and per-page scratch of one call
         self.batch_meta = torch.zeros((BATCH_BUCKETS, 4), dtype=torch.int32, device=d)
@@ -208,6 +211,7 @@ class PageArena:
             lease = self.free_leases.pop()
             tmp, mapping, centers = bucket_source(owner, bucket)
             self._bucket(tmp, mapping, centers, bucket * 1024, lease)
+            self.unchecked.append((owner, bucket, lease))
             state.leases.append(lease)
             state.table[bucket * 16:(bucket + 1) * 16].copy_(self.tables[lease])
             state.center_table[bucket * 2:(bucket + 1) * 2].copy_(self.center_pages[lease])
@@ -289,6 +293,7 @@ class PageArena:
                     lease = self.free_leases.pop()
                     state.leases.append(lease)
                     pending.append((owner, bucket, lease, state.row))
+                    self.unchecked.append((owner, bucket, lease))
                 state.length = length
         except BaseException:
             # as prepare() does, the buckets granted before the error are indexed
@@ -324,12 +329,44 @@ class PageArena:
                 p(self.batch_work), p(self.status))
         return self._prepare_args
 
+    @property
+    def pending_check(self) -> bool:
+        """True when buckets were launched since the last check()."""
+        return bool(self.unchecked)
+
     def check(self):
         """Raise ArenaExhausted if an allocation found too few free pages (the
-        reference's device_assert); the arena is unchanged by that bucket."""
+        reference's device_assert; it synchronises with the device).  The
+        exhausted bucket and every bucket launched after it until this check
+        changed nothing in the arena (the status word is sticky) and wrote -1 to
+        their lease table rows; their leases are taken back from their requests
+        here, each request keeps the buckets before its first aborted one (its
+        indexed length ends there), and those buckets' page-table entries return
+        to 0 -- so the host state again describes the arena, and a later
+        release or prepare of the request sees only its allocated buckets."""
+        unchecked, self.unchecked = self.unchecked, []
         code = int(self.status.item())
         if code:
+            if code == _lib.V1X_STATUS_ARENA_EXHAUSTED:
+                self._take_back_aborted(unchecked)
             self.status.zero_()
             if code == _lib.V1X_STATUS_ARENA_EXHAUSTED:
                 raise K.ArenaExhausted("V1 DeepSeek page arena exhausted")
             raise RuntimeError(f"v1x device status {code}")
+
+    def _take_back_aborted(self, launched):
+        """Undo the host bookkeeping of the aborted suffix of `launched`."""
+        if not launched:
+            return
+        rows = self.tables[torch.tensor([lease for _, _, lease in launched], device=self.device)].cpu()
+        aborted = (rows < 0).all(dim=1).tolist()
+        first = next((i for i, a in enumerate(aborted) if a), len(launched))
+        for owner, bucket, lease in reversed(launched[first:]):
+            state = self.states.get(owner)
+            if state is None or lease not in state.leases:
+                continue            # released since: the lease went back already
+            state.leases.remove(lease)
+            self.free_leases.append(lease)
+            state.table[bucket * 16:(bucket + 1) * 16].zero_()
+            state.center_table[bucket * 2:(bucket + 1) * 2].zero_()
+            state.length = min(state.length, bucket * 1024)

@@ -280,8 +280,12 @@ V1X_API int v1x_match_pages(const uint8_t* tmp, const int32_t* map, const int64_
  * [cap], tables i32 [leases, 16], new_flags u8 (torch.bool) [16].  If the free
  * stack holds fewer pages than needed, *status = V1X_STATUS_ARENA_EXHAUSTED,
  * every new_flags entry is set to 2 ("bucket not allocated", so that
- * v1x_publish skips the bucket) and nothing else is written (the reference
- * traps).  status may be NULL. */
+ * v1x_publish skips the bucket), the lease's table row is set to -1 (no page;
+ * v1x_release and v1x_release_many skip -1 entries) and nothing else is written
+ * (the reference traps).  The exhaustion is sticky: while *status holds it,
+ * every later call on the same word aborts the same way, as nothing runs after
+ * the reference's trap; the host reads and clears the word.  status may be
+ * NULL. */
 V1X_API int v1x_allocate(const int32_t* meta, const int32_t* match, int32_t* free_stack,
                  int32_t* count, int32_t* refs, int32_t* tables, uint8_t* new_flags,
                  int32_t* status, void* stream);
@@ -296,7 +300,8 @@ V1X_API int v1x_publish(const uint8_t* tmp, const uint8_t* tc_bytes, const float
                 uint8_t* centers, float* center_scales, int32_t* members, int64_t* hashes,
                 void* stream);
 
-/* DS/kernels.py:170-179. table i32 [16] (one lease's row). */
+/* DS/kernels.py:170-179. table i32 [16] (one lease's row).  Entries of -1 (a
+ * lease whose allocation aborted) are skipped. */
 V1X_API int v1x_release(const int32_t* table, int32_t* refs, int32_t* free_stack, int32_t* count,
                 void* stream);
 
@@ -320,7 +325,9 @@ V1X_API int v1x_release(const int32_t* table, int32_t* refs, int32_t* free_stack
  * receiving tables[lease] at columns start/1024*16 and center_pages[lease] at
  * start/1024*2 of the bucket's state row.  The first bucket that finds the
  * free stack too short writes V1X_STATUS_ARENA_EXHAUSTED to *status; it and
- * every later bucket of the call change nothing.  Precondition: a bucket's 16
+ * every later bucket of the call change nothing (new_flags 2, lease table rows
+ * -1, state rows untouched); a status word that already holds the exhaustion
+ * aborts the whole call (sticky, as v1x_allocate).  Precondition: a bucket's 16
  * pages are distinct (their members are disjoint token positions, as every
  * index build produces); two identical pages in one bucket would both be
  * published, and a later bucket of the same call could then take the other

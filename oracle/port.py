@@ -96,7 +96,13 @@ class ArenaPort:
         meta = np.array([start, lease, 1], np.int32)
         h = O.fingerprint(tmp, mapping)
         match = O.match_pages(tmp, mapping, h, self.fine, self.members, self.hashes, self.refs, self.capacity)
-        self.count, new = O.allocate(meta, match, self.free, self.count, self.refs, self.tables)
+        try:
+            self.count, new = O.allocate(meta, match, self.free, self.count, self.refs, self.tables)
+        except O.ArenaExhausted:
+            # the arena is unchanged; the lease's table row reads "no page" (the
+            # CUDA allocate's contract: a later release of the lease is a no-op)
+            self.tables[lease] = -1
+            raise
         O.publish(tmp, centers, mapping, h, meta, self.tables, new, self.fine, self.centers, self.members,
                   self.hashes)
 
@@ -184,6 +190,7 @@ def prepare_buckets_batched(arena, tmp, centers, mapping, meta):
         qs = list(range(b * 16, b * 16 + 16))
         if exhausted:
             new[qs] = 2
+            arena.tables[int(meta[b][1])] = -1
             continue
         m = []
         for q in qs:
@@ -202,6 +209,7 @@ def prepare_buckets_batched(arena, tmp, centers, mapping, meta):
         if arena.count < needed:
             exhausted = True
             new[qs] = 2
+            arena.tables[int(meta[b][1])] = -1
             continue
         rank = 0
         lease = int(meta[b][1])
@@ -230,7 +238,8 @@ def release_many(arena, requests_leases):
     that reach zero are pushed in (lease, lane) order.  Equals the per-lease
     release sequence when a request's pages are distinct (asserted)."""
     for leases in requests_leases:
-        pages = [int(arena.tables[lease, i]) for lease in leases for i in range(16)]
+        pages = [int(arena.tables[lease, i]) for lease in leases for i in range(16)
+                 if arena.tables[lease, i] >= 0]          # -1: an aborted lease
         assert len(set(pages)) == len(pages), "a request's pages must be distinct"
         dead = []
         for page in pages:

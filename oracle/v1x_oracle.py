@@ -781,10 +781,14 @@ def publish(tmp, tc_u8, mapping, hsh, meta, tables, new, fine, centers_u8, membe
 
 def release(table, refs, free, count):
     """DS/kernels.py:170-179: decrement refs; pages that hit zero are pushed
-    to the free stack in lane order.  Returns the new count."""
+    to the free stack in lane order.  Returns the new count.  An entry of -1
+    (a lease whose allocation aborted; the reference would have trapped before)
+    is skipped, as the CUDA release does."""
     count = int(count)
     dead = []
     for page in np.asarray(table).reshape(-1)[:16]:
+        if page < 0:
+            continue
         old = int(refs[page])
         refs[page] = old - 1
         if old == 1:

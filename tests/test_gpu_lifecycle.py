@@ -173,6 +173,22 @@ def test_exhausted_free_stack_changes_nothing(batched, cuda_dev):
     assert np.array_equal(gpu.fine.cpu().numpy(), cpu.fine)
     assert np.array_equal(gpu.centers.cpu().numpy(), cpu.centers)
     assert np.array_equal(gpu.tables.cpu().numpy(), cpu.tables)
+    # the host state again describes the arena: the owner keeps its first
+    # bucket, the aborted leases are free, their page-table entries read 0
+    st = gpu.states[a]
+    assert len(st.leases) == len(cpu.states[a]["leases"]) == 1 and st.length == 1024
+    assert not st.table[16:48].any() and gpu.pending_check is False
+    # releasing the owner afterwards touches only its allocated pages
+    if batched:
+        gpu.release_many([a])
+    else:
+        gpu.release(a)
+    cpu.release(a)
+    torch.cuda.synchronize()
+    assert int(gpu.free_count.item()) == cpu.count == 20
+    for name in ("refs", "free"):
+        assert np.array_equal(getattr(gpu, name).cpu().numpy(), getattr(cpu, name)), name
+    assert len(gpu.free_leases) == gpu.max_leases
 
 
 def _collide(mapping_page):

@@ -3,9 +3,17 @@ the composed selection step vs the oracle.
 
 Tolerances: the few-head SIMT scorer follows the oracle's fixed fp32 order and
 must match it exactly; the tensor-core scorer (many heads) must be within
-rtol = 1e-2 of the fp64 reference math (the north-star score tolerance), with
-an absolute floor of 1e-3 x the row's largest |score|.  Selection parity is
-bit-exact given the device scores.
+rtol = 1e-2 of the fp64 reference math (the north-star score tolerance) for
+every score of at least 1/10 of its row's largest |score|, and within
+1e-3 x that largest |score| below it.  Why the floor: a score near zero is a
+sum whose head terms cancel (w_h * relu(q_h . k) with q_h . k itself a signed
+128-term sum), and the rounding error of any fp32 summation order is bounded by
+eps x the sum of the terms' magnitudes, not by |result|; the reference's own
+DeepGEMM and Triton restatement sum in different orders and differ there too.
+Every score of at least 1/10 of the row maximum meets the pure relative bar.
+Selection parity is bit-exact given the device scores; how often the score
+tolerance changes the selected set is measured separately (selection
+agreement, test_gpu_full_configs.py).
 """
 import importlib
 
@@ -35,8 +43,9 @@ def close(got, exp):
         e, g = exp[r][fin[r]], got[r][fin[r]]
         if e.size == 0:
             continue
-        atol = 1e-3 * np.abs(e).max()
-        assert np.all(np.abs(g - e) <= atol + RTOL * np.abs(e)), r
+        # 1e-2 relative, with the floor 1e-3 x row max only below 1/10 of it
+        bound = np.maximum(RTOL * np.abs(e), 1e-3 * np.abs(e).max())
+        assert np.all(np.abs(g - e) <= bound), r
 
 
 def test_score_golden_formula(golden, cuda_dev):

@@ -80,13 +80,19 @@ def test_batched_prepare_equals_per_bucket_sequence(seed):
     if seed % 4 == 1:                     # a free stack shorter than the call needs
         seq.count = bat.count = int(rng.integers(0, 40))
     # the reference: one bucket after another; it traps at the first short stack
+    # (here: that bucket and, the status being sticky, every later one abort,
+    # each leaving its lease table row at -1)
+    trapped = False
     for b in range(nb):
         if not active[b]:
+            continue
+        if trapped:
+            seq.tables[int(meta[b, 1])] = -1
             continue
         try:
             seq._bucket(tmp[b], mp[b], centers[b], int(meta[b, 0]), int(meta[b, 1]))
         except O.ArenaExhausted:
-            break
+            trapped = True
     new, exhausted = port.prepare_buckets_batched(bat, tmp, centers, mp, meta)
     _compare(seq, bat)
     assert set(np.unique(new)) <= {0, 1, 2}
