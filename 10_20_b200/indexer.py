@@ -26,9 +26,10 @@ import threading
 
 import torch
 
+from . import kernels as K
 from .config import Config
 from .index_build import BucketBuilder
-from .lifecycle import PageArena
+from .lifecycle import HostStaging, PageArena
 from .pipeline import SelectionStep
 from .synth import QueryCase
 
@@ -51,10 +52,20 @@ class _Query:
             center_table=torch.zeros((rows, c.pages // 8), dtype=torch.int32, device=d),
             capacity=a.capacity)
         ratio = c.ratio
-        self.step = SelectionStep(self.case, gather=False, ratio=(ratio.numerator, ratio.denominator),
-                                  expand=c.expand_output)
+        # The reference's fixed-budget hook: a caller that replaces the metadata
+        # op with BudgetMetadata(budget) (as qwen_gqa_probe_backend.py:48 does)
+        # gets take = min(pages, budget) instead of the ratio rule.
+        budget = getattr(K.query_metadata, "budget", None)
+        if budget is not None:
+            self.step = SelectionStep(self.case, gather=False, budget=budget, expand=c.expand_output)
+        else:
+            self.step = SelectionStep(self.case, gather=False, ratio=(ratio.numerator, ratio.denominator),
+                                      expand=c.expand_output)
         self.graph = None
         self.graphs = c.graphs
+        # arena rows of the staged requests, for one gather of their page tables
+        self.row_ids = torch.zeros(rows, dtype=torch.int64, device=d)
+        self.staging = HostStaging(rows, d, dtype=torch.int64)
 
     def _execute(self):
         if not self.graphs:
@@ -84,14 +95,12 @@ class _Query:
         if n < self.rows:
             for t in (c.q8.view(torch.uint8), c.w, c.lens, c.native_table, c.reordered_table, c.center_table):
                 t[n:].zero_()
-        row = 0
-        while row < n:
-            end = row + 1
-            while end < n and states[end] is states[row]:
-                end += 1
-            c.reordered_table[row:end].copy_(states[row].table[None].expand(end - row, -1))
-            c.center_table[row:end].copy_(states[row].center_table[None].expand(end - row, -1))
-            row = end
+        # every row's reordered and centre page tables: rows of the arena's request
+        # tables, gathered in one launch each
+        a = self.owner.arena
+        ids = self.staging.copy([st.row for st in states], self.row_ids)[:n]
+        torch.index_select(a.state_tables, 0, ids, out=c.reordered_table[:n])
+        torch.index_select(a.state_centers, 0, ids, out=c.center_table[:n])
         self._execute()
         out = self.step.expanded if self.owner.config.expand_output else self.step.physical
         result = out[:n].clone()
@@ -200,6 +209,10 @@ class Indexer:
                 if key not in max_rows or cpu[i] > cpu[max_rows[key]]:
                     max_rows[key] = i
             for key, i in max_rows.items():
+                st = self.states.get(key)
+                if st is not None and cpu[i] >= st.length and cpu[i] // 1024 == len(st.leases):
+                    st.length = cpu[i]        # no newly complete bucket: nothing to index
+                    continue
                 self._prepare(key, native_tables[i], cpu[i])
             if self.arena.pending_check:      # new buckets: read the status word (a sync)
                 self.arena.check()

@@ -39,16 +39,21 @@ class SelectionStep:
     """
 
     def __init__(self, case, gather: bool = True, gather_v: bool = False, fused_route_pages: bool = True,
-                 keep_logits: bool = False, ratio=None, expand: bool = False):
-        """ratio=None: the fixed page budget take = min(pages, case.take) (the
-        reference's BudgetMetadata); ratio=(num, den): the reference's default take
-        rule min(pages, max(ceil(pages*num/den), ceil(topk/64))).  expand: also
-        write the x4 expanded logical positions ([B, 4*topk+64], -1 padded)."""
+                 keep_logits: bool = False, ratio=None, expand: bool = False, budget=None):
+        """ratio=None: the fixed page budget take = min(pages, budget) (the
+        reference's BudgetMetadata; budget an int32 device tensor of one element,
+        by default holding case.take, which bounds it); ratio=(num, den): the
+        reference's default take rule min(pages, max(ceil(pages*num/den),
+        ceil(topk/64))).  expand: also write the x4 expanded logical positions
+        ([B, 4*topk+64], -1 padded)."""
         c = self.case = case
         d = c.lens.device
         B = c.B
         self.ratio = (1, 2) if ratio is None else (int(ratio[0]), int(ratio[1]))
-        self.budget = torch.tensor([c.take], dtype=torch.int32, device=d) if ratio is None else None
+        if ratio is None:
+            self.budget = torch.tensor([c.take], dtype=torch.int32, device=d) if budget is None else budget
+        else:
+            self.budget = None
         self.fine_lens = torch.zeros(B, dtype=torch.int32, device=d)
         self.takes = torch.zeros(B, dtype=torch.int32, device=d)
         self.dg_lens = torch.zeros(B, dtype=torch.int32, device=d)
@@ -114,10 +119,13 @@ class SelectionStep:
                                       self.fine_table[rs], self.tail_rows[rs], c.capacity, c.P, c.take,
                                       self.width // 64, 68)
 
-    def _fine_topk(self, rs):
+    def _fine(self, rs):
         c = self.case
         scoring.fp8_paged_mqa_logits(c.q8[rs], c.fine, c.w[rs], self.dg_lens[rs], self.fine_table[rs], None,
                                      self.width, out=self.scores[rs], clean_logits=False)
+
+    def _topk(self, rs):
+        c = self.case
         self.fused.topk(self.scores[rs, :self.topk_cols], self.fine_lens[rs], c.members, c.reordered_table[rs],
                         c.native_table[rs], self.selected[rs], c.lens[rs], self.takes[rs], self.physical[rs],
                         self.logical[rs], self.raw[rs], c.window, True, self.expanded[rs], True, True,
@@ -131,20 +139,38 @@ class SelectionStep:
                      self.kv2[rs] if self.gather_v else None, n, c.topk, 0, *lat.stride(),
                      *(lat.stride() if self.gather_v else (0, 0, 0)), self.physical.stride(0))
 
-    def run(self):
+    def run(self, marks=None):
+        """Launch the step on the current stream.  marks: a list that receives
+        (stage name, CUDA event recorded after the stage) -- a per-stage time
+        split for diagnostics (not for graph capture)."""
         c = self.case
         B = c.B
         rs = slice(0, B)
+
+        def mark(name):
+            if marks is not None:
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record()
+                marks.append((name, ev))
+
+        mark("start")
         # query metadata with the fixed page budget + sink/tail staging, one launch
         K.query_prepare(c.lens, c.native_table, self.fine_lens, self.takes, self.dg_lens, self.center_lens,
                         self.tail_rows, c.P, c.topk, self.ratio[0], self.ratio[1], 64, c.window, c.native,
                         c.native.view(torch.float32), c.fine, c.fine.view(torch.float32), c.capacity, 68,
                         budget=self.budget)
+        mark("prepare")
         self._centres(rs)
+        mark("centre_scores")
         self._route(rs)
-        self._fine_topk(rs)
+        mark("route")
+        self._fine(rs)
+        mark("fine_scores")
+        self._topk(rs)
+        mark("topk")
         if self.gather:
             self._gather(rs)
+            mark("gather")
 
     def capture(self, warmup: int = 2):
         s = torch.cuda.Stream(device=self.case.lens.device)

@@ -40,6 +40,13 @@ if str(ROOT) not in sys.path:
 
 METRIC = "indexed queries/sec (route+FP8 score+Top2048+gather); HBM GB/s as % of peak"
 
+# DRAM traffic of one decode gather launch (128 requests x 2048 slots of 1152 B),
+# dram__bytes_read.sum + dram__bytes_write.sum from one ncu capture; not
+# measured in the run that prints it (the roofline line says so)
+GATHER_DECODE_DRAM_BYTES = 303167744 + 250278400
+GATHER_DECODE_DRAM_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one gather_rows_kernel launch "
+                             "of this workload, captured separately (profiles/gather_rows_decode_dram.md)")
+
 
 def peaks():
     p = ROOT / "MEASURED_PEAKS.json"
@@ -129,60 +136,97 @@ class Clocks:
                 "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
-def cpu_port_rate(cfg, seed, rows, budget_s=20.0):
-    """Queries/s of the oracle port on a bounded CPU sample (all host cores for BLAS)."""
+def _port_sample(cfg, lens_all, count):
+    """`count` request indices spread over the job's batch (a fixed stride), so
+    the sample's lengths follow the batch's."""
+    n = len(lens_all)
+    stride = 37 if n % 37 else 1
+    return [(k * stride) % n for k in range(count)]
+
+
+def _port_case(cfg, n, seed):
+    """One request of context n as a numpy case for the oracle port (the latent
+    pool is a lazily zeroed array: the gather only copies bytes)."""
+    import numpy as np
     import oracle.port as port
 
     synth = importlib.import_module("10_20_b200.synth")
-    torch.set_num_threads(os.cpu_count() or 1)
-    case = make_case(synth, cfg, seed, "cpu", rows=rows)
+    case = synth.make_query_case(1, cfg["H"], [n], P=cfg["P"], take=cfg["take"], window=cfg["window"],
+                                 topk=cfg["topk"], seed=seed, device="cpu", latent_dim=0)
     c = port.to_numpy_case(case)
-    port.run_rows(c, rows=[0])            # warm-up (page-in, BLAS init)
-    done, t0 = 0, time.perf_counter()
-    while True:
-        port.run_rows(c, rows=[done % rows])
+    if cfg["latent"]:
+        c["latent"] = np.zeros((case.native.shape[0] * 64, 1, cfg["latent"]), np.int16)
+    return c
+
+
+def cpu_port_rate(cfg, lens_all, budget_s=20.0):
+    """Queries/s of the oracle port on a bounded CPU sample: one query at a time,
+    each request of the sample built with its own pools (untimed), its step
+    timed; the sample's requests are spread over the GPU batch's lengths."""
+    import oracle.port as port
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    port.run_rows(_port_case(cfg, lens_all[0], 999), rows=[0])      # warm-up (page-in, BLAS init)
+    timed = 0.0
+    done = 0
+    sample = []
+    for i in _port_sample(cfg, lens_all, len(lens_all)):
+        c = _port_case(cfg, lens_all[i], 1000 + i)
+        t0 = time.perf_counter()
+        port.run_rows(c, rows=[0])
+        timed += time.perf_counter() - t0
         done += 1
-        el = time.perf_counter() - t0
-        if el >= budget_s or done >= 64 * rows:
+        sample.append(lens_all[i])
+        if timed >= budget_s:
             break
-    return done / el, dict(rows=done, seconds=round(el, 3), sample_requests=rows,
-                           lens=[int(x) for x in c["lens"]])
+    mean_batch = sum(lens_all) / len(lens_all)
+    mean_sample = sum(sample) / len(sample)
+    return done / timed, (f"{done} requests of the GPU batch's {len(lens_all)} (mean context {mean_sample:.0f} "
+                          f"tokens vs the batch's {mean_batch:.0f}), one query each, oracle port (numpy + BLAS, "
+                          f"{torch.get_num_threads()} threads), {timed:.2f} s timed")
 
 
 def run_reference(args, cfg):
-    """The reference arm: the CPU port of the path on the host cores.  One step
-    = one query row of a 4-request (decode) / 32-request (single) sample of the
-    workload; the arm stops after ~60 s of timed steps and reports the rate over
-    the steps it timed."""
+    """The reference arm: the CPU port of the path on the host cores (the
+    reference's own route/top-k are CUDA for sm_90 with unvendored headers, and
+    its scorer is the external DeepGEMM, so the restatement stands in for it).
+    One step = one query of one request of the GPU batch -- the same context
+    lengths, taken at a fixed stride -- built with its own pools (untimed);
+    the arm reports the rate over the steps it timed."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
     import oracle.port as port
 
-    synth = importlib.import_module("10_20_b200.synth")
     torch.set_num_threads(os.cpu_count() or 1)
-    rows = 4 if args.workload == "decode" else 32
-    case = make_case(synth, cfg, 1000, "cpu", rows=rows)
-    c = port.to_numpy_case(case)
+    lens_all = _request_lens(cfg, 1)
+    order = _port_sample(cfg, lens_all, max(args.warmup, 1) + args.steps)
     for k in range(max(args.warmup, 1)):
-        port.run_rows(c, rows=[k % rows])
-    done, t0 = 0, time.perf_counter()
-    for k in range(args.steps):
-        port.run_rows(c, rows=[k % rows])
+        port.run_rows(_port_case(cfg, lens_all[order[k]], 1000 + order[k]), rows=[0])
+    timed, done, t_start = 0.0, 0, time.perf_counter()
+    sample = []
+    for k in order[max(args.warmup, 1):]:
+        c = _port_case(cfg, lens_all[k], 1000 + k)
+        t0 = time.perf_counter()
+        port.run_rows(c, rows=[0])
+        timed += time.perf_counter() - t0
         done += 1
-        if time.perf_counter() - t0 > 60.0:
+        sample.append(lens_all[k])
+        if time.perf_counter() - t_start > 120.0:
             break
-    el = time.perf_counter() - t0
-    value = done / el
+    value = done / timed
     cores = os.cpu_count()
+    mean_batch = sum(lens_all) / len(lens_all)
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / max(done, 1) * 1e3,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": timed / max(done, 1) * 1e3,
             "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "fp8-e4m3 keys, f32 scores, bf16 latent", "data": "synthetic",
             "config": {"workload": args.workload, **{k: v for k, v in cfg.items()}},
             "cpu_baseline": {"value": value, "unit": "queries/s", "cores": cores, "kind": "port",
-                             "sample": f"{done} of {args.steps} steps timed ({el:.1f} s), one query row of a "
-                                       f"{rows}-request sample per step, oracle port (numpy + BLAS)"},
+                             "sample": f"{done} of {args.steps} steps timed ({timed:.1f} s): one query of one "
+                                       f"request of the GPU batch per step (mean context "
+                                       f"{sum(sample) / max(len(sample), 1):.0f} vs the batch's {mean_batch:.0f}), "
+                                       f"oracle port (numpy + BLAS, {torch.get_num_threads()} threads)"},
             "e2e": {"value": value, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
@@ -400,7 +444,7 @@ def run_gather_workload(args, world, rank, device, dist):
 
 def run_pages_workload(args, world, rank, device, dist):
     """d3: the page lifecycle on a 131,072-page arena: 256 live requests whose
-    bucket chains (1-64 buckets) grow by up to 8 buckets per round, half of them
+    bucket chains (1-128 buckets, 16-2048 pages) grow by up to 8 buckets per round, half of them
     sharing a prefix of another request's chain, a quarter completing (released)
     after every round; 8 rounds, the first untimed.  Per bucket: fingerprint ->
     match_pages -> allocate -> publish as one captured graph (the reference's
@@ -409,7 +453,7 @@ def run_pages_workload(args, world, rank, device, dist):
     synth = importlib.import_module("10_20_b200.synth")
     lifecycle = importlib.import_module("10_20_b200.lifecycle")
     cap, pages, requests = 131072, 2048, 256
-    wl = synth.LifecycleWorkload(requests, 64, 8, 31 + rank, cap // 16, share=0.5, grow=8)
+    wl = synth.LifecycleWorkload(requests, 128, 8, 31 + rank, cap // 16, share=0.5, grow=8)
     contents = wl.contents(device)
     src, bsrc = wl.source(contents), wl.batch_source(contents)
 
@@ -811,6 +855,348 @@ def run_component(args):
     return 0
 
 
+def _request_lens(cfg, world):
+    """The job's context lengths: world * B requests from the benchmark seed."""
+    synth = importlib.import_module("10_20_b200.synth")
+    if cfg["lo"] == cfg["hi"]:
+        return [cfg["lo"]] * (world * cfg["B"])
+    return synth.decode_lens(world * cfg["B"], cfg["lo"], cfg["hi"], 1000)
+
+
+def _shard(cfg, lens_all, world, rank, per_rank):
+    """This rank's share of the job's requests (longest first by bytes)."""
+    if world == 1:
+        return list(lens_all)
+    sharding = importlib.import_module("10_20_b200.sharding")
+    row = cfg["latent"] * 2
+    costs = [sharding.row_bytes(n, cfg["H"], cfg["take"], cfg["window"], cfg["topk"], row)["total"]
+             for n in lens_all]
+    return [lens_all[i] for i in sharding.shard_requests(costs, world, per_rank=per_rank)[rank]]
+
+
+class Batches:
+    """`inflight` independent batches of the same request lengths (each its own
+    seeded pools, tables and queries), each step captured as one CUDA graph on
+    its own stream; steps alternate over the batches, so the gather of one
+    overlaps the selection of the next and consecutive steps touch disjoint
+    data.  Events on the caller's stream bracket a run."""
+
+    def __init__(self, cfg, lens, seed, inflight, device):
+        synth = importlib.import_module("10_20_b200.synth")
+        pipeline = importlib.import_module("10_20_b200.pipeline")
+        self.device = device
+        self.sets = []
+        for i in range(inflight):
+            case = make_case(synth, dict(cfg, B=len(lens)), seed + 7919 * i, device, lens=lens)
+            step = pipeline.SelectionStep(case, gather=cfg["latent"] > 0)
+            st = torch.cuda.Stream(device=device)
+            st.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(st):
+                for _ in range(2):
+                    step.run()
+            st.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=st):
+                step.run()
+            st.synchronize()
+            self.sets.append(dict(case=case, step=step, stream=st, graph=g))
+        for st in self.sets:   # pinned host copies of the step's inputs and output
+            c = st["case"]
+            st["pin"] = [(c.q8.view(torch.uint8), c.q8.view(torch.uint8).cpu().pin_memory()),
+                         (c.w, c.w.cpu().pin_memory()), (c.lens, c.lens.cpu().pin_memory()),
+                         (c.native_table, c.native_table.cpu().pin_memory())]
+            st["out_host"] = torch.empty(st["step"].physical.shape, dtype=torch.int32).pin_memory()
+        self.h2d = sum(h.numel() * h.element_size() for _, h in self.sets[0]["pin"])
+        self.d2h = self.sets[0]["out_host"].numel() * 4
+
+    def run(self, n, e2e=False):
+        main = torch.cuda.current_stream(self.device)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(main)
+        for st in self.sets:
+            st["stream"].wait_stream(main)
+        for k in range(n):
+            st = self.sets[k % len(self.sets)]
+            with torch.cuda.stream(st["stream"]):
+                if e2e:     # host -> device inputs of this step, from pinned memory
+                    for dst, hst in st["pin"]:
+                        dst.copy_(hst, non_blocking=True)
+                st["graph"].replay()
+                if e2e:     # device -> host: the step's physical slot ids
+                    st["out_host"].copy_(st["step"].physical, non_blocking=True)
+        for st in self.sets:
+            main.wait_stream(st["stream"])
+        b.record(main)
+        return a, b
+
+    def release(self):
+        for st in self.sets:
+            st.pop("graph", None)
+
+
+def _timed(fn, dist, device, clocks=False):
+    """Barrier, then time fn() (which returns an event pair); max over ranks."""
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clk = Clocks(device) if clocks else None
+    if clk:
+        clk.__enter__()
+    t0 = time.perf_counter()
+    a, b = fn()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    if clk:
+        clk.__exit__()
+    ms = a.elapsed_time(b)
+    t = torch.tensor([ms], dtype=torch.float64, device=device)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item()), wall, (clk.summary() if clk else None)
+
+
+def _stage_split(step, reps=5):
+    """Per-stage device time (us) of one batch run eagerly with events between
+    its launches, after a 256 MB L2-evicting read; mean over reps."""
+    flush = torch.ones(256 << 20, dtype=torch.uint8, device=step.case.lens.device)
+    acc = {}
+    for _ in range(reps):
+        flush.sum()
+        marks = []
+        step.run(marks=marks)
+        torch.cuda.synchronize()
+        for (_, a), (name, b) in zip(marks, marks[1:]):
+            acc[name] = acc.get(name, 0.0) + a.elapsed_time(b) * 1e3 / reps
+    return {k: round(v, 2) for k, v in acc.items()}
+
+
+def _indexer_e2e(case, cfg, steps, warmup, device, dist):
+    """End to end through the reference-facing API: per step, pinned host ->
+    device copies of q, weights, native page tables and lengths, then
+    Indexer.query (runtime.py:828-907; the fixed page budget installed as the
+    reference's benchmark does, qwen_gqa_probe_backend.py:48) and
+    GatherWorkspace.gather of the returned slots (NA/kernels.py:102-111), and a
+    device -> host copy of the slot ids.  One batch at a time on one stream, as
+    a model layer runs.  Returns (ms for `steps` steps, h2d bytes, d2h bytes)."""
+    pkg = "10_20_b200"
+    Config = importlib.import_module(pkg + ".config").Config
+    Indexer = importlib.import_module(pkg + ".indexer").Indexer
+    K = importlib.import_module(pkg + ".kernels")
+    gmod = importlib.import_module(pkg + ".gather")
+    B = case.B
+    qb = tuple(sorted({1, 4, 16, 64, B}))
+    conf = Config(max_context=case.P * 64, heads=case.H, max_requests=B, topk=case.topk,
+                  page_fraction=case.take / case.topk, window=case.window, q_buckets=qb, budget_bytes=1 << 40)
+    saved = K.query_metadata
+    K.query_metadata = K.BudgetMetadata(torch.tensor([case.take], dtype=torch.int32, device=device))
+    try:
+        ix = Indexer(case.native, conf)
+        lens_cpu = case.lens.cpu().tolist()
+        owners = list(range(B))
+        pins = [(torch.empty_like(case.q8.view(torch.uint8)), case.q8.view(torch.uint8).cpu().pin_memory()),
+                (torch.empty_like(case.w), case.w.cpu().pin_memory()),
+                (torch.empty_like(case.native_table), case.native_table.cpu().pin_memory()),
+                (torch.empty_like(case.lens), case.lens.cpu().pin_memory())]
+        out_host = torch.empty((B, case.topk), dtype=torch.int32).pin_memory()
+        ws = gmod.GatherWorkspace(B, device, case.latent.dtype, dim=case.latent.shape[-1], top=case.topk)
+
+        def one():
+            for dst, hst in pins:
+                dst.copy_(hst, non_blocking=True)
+            q, w, nt, ln = (pins[0][0].view(torch.float8_e4m3fn), pins[1][0], pins[2][0], pins[3][0])
+            ids = ix.query(q, w, nt, ln, owners, lens_cpu)
+            ws.gather(case.latent, None, None, ids, 0)
+            out_host.copy_(ids, non_blocking=True)
+
+        one()                      # builds every request's index (prepare), captures the query graph
+        torch.cuda.synchronize()
+        for _ in range(max(warmup, 3)):
+            one()
+
+        def run():
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(steps):
+                one()
+            b.record()
+            return a, b
+        ms, _, _ = _timed(run, dist, device)
+        h2d = sum(h.numel() * h.element_size() for _, h in pins)
+        ix.close()
+        return ms, h2d, out_host.numel() * 4
+    finally:
+        K.query_metadata = saved
+
+
+def run_decode(args, cfg):
+    world, rank, device, dist = _dist_setup()
+    importlib.import_module("10_20_b200").load()
+    B = cfg["B"]
+    inflight = max(1, args.inflight)
+    lens_all = _request_lens(cfg, world)
+    lens = _shard(cfg, lens_all, world, rank, B)
+    bat = Batches(cfg, lens, 1000 + rank, inflight, device)
+    case, step = bat.sets[0]["case"], bat.sets[0]["step"]
+    acct = step.algorithmic_bytes()
+    gather_on = step.gather
+
+    # ---- the headline: K steps, three batches in flight ----------------------------
+    for _ in range(max(args.warmup, 3)):
+        bat.run(inflight)
+    total_ms, wall, clocks = _timed(lambda: bat.run(args.steps), dist, device, clocks=True)
+    queries = B * args.steps * world
+    value = queries / (total_ms / 1e3)
+
+    # ---- diagnostics of one batch ---------------------------------------------------
+    s = bat.sets[0]["stream"]
+
+    def capture(fn):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            fn()
+        s.synchronize()
+        return g
+
+    step.gather = False
+    sel_graph = capture(step.run)
+    step.gather = gather_on
+    gat_graph = None
+    if gather_on:
+        gmod = importlib.import_module("10_20_b200.gather")
+        lat = case.latent
+        gat_graph = capture(lambda: gmod._gather_impl((1,), lat, None, None, step.physical, step.kv, None, B,
+                                                      case.topk, 0, *lat.stride(), 0, 0, 0,
+                                                      step.physical.stride(0)))
+    flush = torch.ones(256 << 20, dtype=torch.uint8, device=device)
+
+    def timed_each(graph, n, flush_first=True):
+        evs = []
+        for _ in range(n):
+            if flush_first:
+                flush.sum()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            graph.replay()
+            b.record()
+            evs.append((a, b))
+        torch.cuda.synchronize()
+        return [a.elapsed_time(b) for a, b in evs]
+
+    diag_steps = min(args.steps, 20)
+    one_ms = timed_each(bat.sets[0]["graph"], diag_steps)
+    sel_ms = timed_each(sel_graph, diag_steps)
+    # the gather kernel alone, replayed back to back: its 604 MB per launch is far
+    # larger than L2, and its own write-backs stay in the timing
+    gather_ms = timed_each(gat_graph, diag_steps + 1, flush_first=False)[1:] if gat_graph is not None else [0.0]
+    split = _stage_split(step)
+
+    # ---- end to end -----------------------------------------------------------------
+    bat.run(2 * inflight, e2e=True)
+    e2e_ms, _, _ = _timed(lambda: bat.run(args.steps, e2e=True), dist, device)
+    e2e_graph_value = queries / (e2e_ms / 1e3)
+    api = None
+    if gather_on and args.workload == "decode":
+        api_steps = min(args.steps, 200)
+        api_ms, api_h2d, api_d2h = _indexer_e2e(case, cfg, api_steps, args.warmup, device, dist)
+        api = {"value": B * api_steps * world / (api_ms / 1e3), "unit": "queries/s", "h2d_bytes_per_step": api_h2d,
+               "d2h_bytes_per_step": api_d2h, "steps": api_steps, "ms_per_step": api_ms / api_steps}
+
+    # ---- strong scaling: ONE job of B requests split across the ranks ---------------
+    strong = None
+    if world > 1 and B % world == 0:
+        bs = B // world
+        # the N = 1 batch's requests (the benchmark's 128), split by bytes
+        lens_s = _shard(cfg, _request_lens(cfg, 1), world, rank, bs)
+        sb = Batches(dict(cfg, B=bs), lens_s, 2000 + rank, inflight, device)
+        for _ in range(max(args.warmup, 3)):
+            sb.run(inflight)
+        sms, _, _ = _timed(lambda: sb.run(args.steps), dist, device)
+        strong = {"job_requests": B, "requests_per_gpu": bs, "value": B * args.steps / (sms / 1e3),
+                  "unit": "queries/s", "ms_per_step": sms / args.steps,
+                  "single_batch_stage_us": _stage_split(sb.sets[0]["step"])}
+        sb.release()
+        del sb
+
+    # ---- parity spot check (rank 0): sampled rows of batch 0 against the oracle -----
+    parity = None
+    if rank == 0 and not args.no_parity:
+        SC = importlib.import_module("oracle.selection_check")
+        bat.sets[0]["graph"].replay()
+        torch.cuda.synchronize()
+        ln = case.lens.cpu().numpy()
+        order = ln.argsort(kind="stable")
+        rows = sorted({int(order[0]), int(order[-1]), int(order[len(order) // 2]), 1 % B})
+        t0 = time.perf_counter()
+        parity = SC.check_rows(step, case, rows)
+        parity["seconds"] = round(time.perf_counter() - t0, 1)
+
+    if rank == 0:
+        hbm, kind = peaks()
+        if gather_on:
+            dom_bytes, dom_ms, dom = acct["gather"], statistics.mean(gather_ms), "gather_rows_kernel"
+        else:
+            dom_bytes, dom_ms, dom = acct["total"], statistics.mean(sel_ms), "selection graph"
+        achieved = dom_bytes / (dom_ms / 1e3) / 1e9
+        traffic = traffic_src = None
+        if gather_on and args.workload == "decode" and B == 128:
+            # DRAM bytes of one decode gather launch (128 requests x 2048 slots of 1152 B)
+            traffic = GATHER_DECODE_DRAM_BYTES
+            traffic_src = GATHER_DECODE_DRAM_SOURCE
+        one_batch = statistics.mean(one_ms)
+        line = {
+            "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp8-e4m3 keys, f32 scores, bf16 latent",
+            "data": "synthetic",
+            "config": {"workload": args.workload, "requests_per_gpu": B, "heads": case.H,
+                       "page_budget": case.take, "topk": case.topk, "window": case.window,
+                       "context": [cfg["lo"], cfg["hi"]], "latent_dim": cfg["latent"],
+                       "parallelism": f"requests sharded by bytes (longest first), {world} ranks x "
+                                      f"{B} requests, no data-path collective",
+                       "batches_in_flight": inflight,
+                       "l2": "inputs larger than L2: consecutive steps alternate between independent batches "
+                             "(separate pools, ~12 GB each); single-batch diagnostics after a 256 MB read",
+                       "algorithmic_bytes_per_step": acct["total"]},
+            "step_hbm_gbs": acct["total"] / (total_ms / args.steps / 1e3) / 1e9,
+            "step_frac_of_peak": acct["total"] / (total_ms / args.steps / 1e3) / 1e9 / hbm,
+            "single_batch": {"ms": one_batch, "hbm_gbs": acct["total"] / (one_batch / 1e3) / 1e9,
+                             "frac_of_peak": acct["total"] / (one_batch / 1e3) / 1e9 / hbm},
+            "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "peak_kind": kind, "traffic": traffic,
+                         "traffic_source": traffic_src},
+            "stage_ms": {"step": total_ms / args.steps, "single_batch_latency": one_batch,
+                         "selection_alone": statistics.mean(sel_ms), "gather_alone": statistics.mean(gather_ms)},
+            "stage_us_one_batch": split,
+            "e2e": api if api is not None else
+                   {"value": e2e_graph_value, "unit": "queries/s", "h2d_bytes_per_step": bat.h2d,
+                    "d2h_bytes_per_step": bat.d2h},
+            "e2e_step_graphs": {"value": e2e_graph_value, "unit": "queries/s", "h2d_bytes_per_step": bat.h2d,
+                                "d2h_bytes_per_step": bat.d2h,
+                                "how": "SelectionStep graph replays, batches in flight, pinned copies per step"},
+            "gpu_launches": (5 + (1 if gather_on else 0)) * args.steps,
+            "clocks": clocks,
+            "wall_s": wall,
+        }
+        if api is not None:
+            line["e2e"]["how"] = ("Indexer.query + GatherWorkspace.gather per step, one batch at a time: pinned "
+                                  "H2D of q, weights, native tables, lengths; D2H of the slot ids")
+        if strong is not None:
+            line["strong_scaling"] = strong
+        if parity is not None:
+            line["parity"] = parity
+        if world == 1 and not args.no_cpu_baseline:
+            v, meta = cpu_port_rate(cfg, lens_all, budget_s=15.0)
+            line["cpu_baseline"] = {"value": v, "unit": "queries/s", "cores": os.cpu_count(), "kind": "port",
+                                    "sample": meta}
+        print(json.dumps(line), flush=True)
+    if dist:
+        bat.release()
+        del sel_graph, gat_graph
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -827,6 +1213,7 @@ def main():
                          "lifecycle), build (index build, 1024 buckets per step), shared (published-end "
                          "shared-tail preparation, 4096-row chunk)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the oracle spot check of sampled rows")
     ap.add_argument("--inflight", type=int, default=3,
                     help="independent batches in flight (the gather of one overlaps the selection of the next)")
     args = ap.parse_args()
@@ -844,235 +1231,7 @@ def main():
         cfg["B"] = args.requests
     if args.impl == "reference":
         return run_reference(args, cfg)
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    dist = None
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
-
-    pkg = importlib.import_module("10_20_b200")
-    pkg.load()
-    synth = importlib.import_module("10_20_b200.synth")
-    pipeline = importlib.import_module("10_20_b200.pipeline")
-
-    # the job's requests: world * B context lengths from one seed, split across the
-    # ranks by bytes (longest first, B requests per rank); each rank builds its own
-    # pools and tables for its share
-    sharding = importlib.import_module("10_20_b200.sharding")
-    lens = None
-    if cfg["lo"] != cfg["hi"]:
-        lens_all = synth.decode_lens(world * cfg["B"], cfg["lo"], cfg["hi"], 1000)
-        if world > 1:
-            row = cfg["latent"] * 2
-            costs = [sharding.row_bytes(n, cfg["H"], cfg["take"], cfg["window"], cfg["topk"], row)["total"]
-                     for n in lens_all]
-            lens = [lens_all[i] for i in sharding.shard_requests(costs, world, per_rank=cfg["B"])[rank]]
-        else:
-            lens = lens_all
-    # `inflight` independent batches (each its own seeded pools, tables and
-    # queries; the same context lengths, so every step moves the same bytes) are
-    # processed alternately on their own streams: the gather of one batch runs
-    # while the next batch is selected.  Consecutive steps touch disjoint data.
-    inflight = max(1, args.inflight)
-    sets = []
-    for i in range(inflight):
-        case_i = make_case(synth, cfg, 1000 + rank + 7919 * i, device, lens=lens)
-        step_i = pipeline.SelectionStep(case_i, gather=cfg["latent"] > 0)
-        st = torch.cuda.Stream(device=device)
-        st.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(st):
-            for _ in range(2):
-                step_i.run()
-        st.synchronize()
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=st):
-            step_i.run()
-        st.synchronize()
-        sets.append(dict(case=case_i, step=step_i, stream=st, graph=g))
-    case, step = sets[0]["case"], sets[0]["step"]
-    acct = step.algorithmic_bytes()
-    gather_on = step.gather
-    s = sets[0]["stream"]
-
-    def capture(fn):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=s):
-            fn()
-        s.synchronize()
-        return g
-
-    # diagnostics of one batch: selection alone and the gather kernel alone (the
-    # roofline's dominant kernel)
-    step.gather = False
-    sel_graph = capture(step.run)
-    step.gather = gather_on
-    gat_graph = None
-    if gather_on:
-        from importlib import import_module
-        gmod = import_module("10_20_b200.gather")
-        lat = case.latent
-        gat_graph = capture(lambda: gmod._gather_impl((1,), lat, None, None, step.physical, step.kv, None, case.B,
-                                                      case.topk, 0, *lat.stride(), 0, 0, 0,
-                                                      step.physical.stride(0)))
-    # L2 eviction before each diagnostic timing: a read of 256 MB that nothing
-    # writes, so no dirty lines are left to be written back inside the timing
-    flush = torch.ones(256 << 20, dtype=torch.uint8, device=device)
-    # per step: query_prepare, centre scoring, route, fine scoring, top-k (+ gather)
-    launches_per_step = 5 + (1 if gather_on else 0)
-    main_stream = torch.cuda.current_stream(device)
-
-    def timed(graph, n):
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
-        for a, b in evs:
-            flush.sum()
-            a.record()
-            graph.replay()
-            b.record()
-        return evs
-
-    # end-to-end pieces: pinned inputs of every batch and a pinned output
-    for st in sets:
-        c = st["case"]
-        st["pin"] = [(c.q8.view(torch.uint8), c.q8.view(torch.uint8).cpu().pin_memory()),
-                     (c.w, c.w.cpu().pin_memory()), (c.lens, c.lens.cpu().pin_memory()),
-                     (c.native_table, c.native_table.cpu().pin_memory())]
-        st["out_host"] = torch.empty(st["step"].physical.shape, dtype=torch.int32).pin_memory()
-    h2d = sum(hst.numel() * hst.element_size() for _, hst in sets[0]["pin"])
-    d2h = sets[0]["out_host"].numel() * 4
-
-    def run_steps(n, e2e=False):
-        """Launch n steps alternating over the batches; events on the main stream."""
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(main_stream)
-        for st in sets:
-            st["stream"].wait_stream(main_stream)
-        for k in range(n):
-            st = sets[k % inflight]
-            with torch.cuda.stream(st["stream"]):
-                if e2e:     # host -> device inputs of this step, from pinned memory
-                    for dst, hst in st["pin"]:
-                        dst.copy_(hst, non_blocking=True)
-                st["graph"].replay()
-                if e2e:     # device -> host: the step's physical slot ids
-                    st["out_host"].copy_(st["step"].physical, non_blocking=True)
-        for st in sets:
-            main_stream.wait_stream(st["stream"])
-        b.record(main_stream)
-        return a, b
-
-    for _ in range(max(args.warmup, 3)):
-        run_steps(inflight)
-    torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
-    with Clocks(device) as clk:
-        t0 = time.perf_counter()
-        ev = run_steps(args.steps)
-        torch.cuda.synchronize()
-        wall = time.perf_counter() - t0
-    if dist:
-        dist.barrier()
-    total_ms = ev[0].elapsed_time(ev[1])
-    t = torch.tensor([total_ms], dtype=torch.float64, device=device)
-    if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    total_ms = float(t.item())
-    queries = case.B * args.steps * world
-    value = queries / (total_ms / 1e3)
-
-    diag_steps = min(args.steps, 20)
-    one_ev = timed(sets[0]["graph"], diag_steps)
-    sel_ev = timed(sel_graph, diag_steps)
-    # the gather kernel alone, replayed back to back: its 604 MB of traffic per
-    # launch is far larger than L2, and its own write-backs stay in the timing
-    gat_ev = []
-    if gat_graph is not None:
-        for _ in range(diag_steps + 1):
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
-            gat_graph.replay()
-            b.record()
-            gat_ev.append((a, b))
-        gat_ev = gat_ev[1:]
-    torch.cuda.synchronize()
-    one_ms = [a.elapsed_time(b) for a, b in one_ev]
-    sel_ms = [a.elapsed_time(b) for a, b in sel_ev]
-    gather_ms = [a.elapsed_time(b) for a, b in gat_ev] or [0.0]
-
-    # end to end through the public step: pinned host -> device copies of q, w,
-    # lengths and native tables, the step, device -> host copy of the slot ids
-    run_steps(2 * inflight, e2e=True)
-    torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
-    ee = run_steps(args.steps, e2e=True)
-    torch.cuda.synchronize()
-    e2e_ms = ee[0].elapsed_time(ee[1])
-    te = torch.tensor([e2e_ms], dtype=torch.float64, device=device)
-    if dist:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_value = queries / (float(te.item()) / 1e3)
-
-    if rank == 0:
-        hbm, kind = peaks()
-        if gather_on:
-            dom_bytes, dom_ms, dom = acct["gather"], statistics.mean(gather_ms), "gather_rows_kernel"
-        else:
-            dom_bytes, dom_ms, dom = acct["total"], statistics.mean(sel_ms), "selection graph"
-        achieved = dom_bytes / (dom_ms / 1e3) / 1e9
-        # DRAM bytes of one decode gather launch (128 requests x 2048 slots of 1152 B),
-        # measured with ncu (dram__bytes_read.sum + dram__bytes_write.sum, one pass):
-        # reads 303,167,744 B = the algorithmic reads (no re-reads); writes
-        # 250,278,400 B, the rest of the 302 MB still in L2 when the kernel ends
-        traffic = 303167744 + 250278400 if (gather_on and args.workload == "decode" and case.B == 128) else None
-        line = {
-            "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "fp8-e4m3 keys, f32 scores, bf16 latent",
-            "data": "synthetic",
-            "config": {"workload": args.workload, "requests_per_gpu": case.B, "heads": case.H,
-                       "page_budget": case.take, "topk": case.topk, "window": case.window,
-                       "context": [cfg["lo"], cfg["hi"]], "latent_dim": cfg["latent"],
-                       "parallelism": f"requests sharded by bytes (longest first), {world} ranks x "
-                                      f"{case.B} requests, no data-path collective",
-                       "batches_in_flight": inflight,
-                       "l2": "inputs larger than L2: consecutive steps alternate between independent batches "
-                             "(separate pools, ~12 GB each); single-batch diagnostics after a 256 MB read",
-                       "algorithmic_bytes_per_step": acct["total"]},
-            "step_hbm_gbs": acct["total"] / (total_ms / args.steps / 1e3) / 1e9,
-            "step_frac_of_peak": acct["total"] / (total_ms / args.steps / 1e3) / 1e9 / hbm,
-            "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                         "frac": achieved / hbm, "peak_kind": kind, "traffic": traffic},
-            "stage_ms": {"step": total_ms / args.steps, "single_batch_latency": statistics.mean(one_ms),
-                         "selection_alone": statistics.mean(sel_ms), "gather_alone": statistics.mean(gather_ms)},
-            "e2e": {"value": e2e_value, "unit": "queries/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h},
-            "gpu_launches": launches_per_step * args.steps,
-            "clocks": clk.summary(),
-            "wall_s": wall,
-        }
-        if world == 1 and not args.no_cpu_baseline:
-            rows = 4 if args.workload == "decode" else 32
-            v, meta = cpu_port_rate(cfg, 1000, rows, budget_s=15.0)
-            line["cpu_baseline"] = {"value": v, "unit": "queries/s", "cores": os.cpu_count(), "kind": "port",
-                                    "sample": f"{meta['rows']} queries from a {rows}-request sample of the "
-                                              f"same workload, oracle port (numpy + BLAS), "
-                                              f"{meta['seconds']} s"}
-        print(json.dumps(line), flush=True)
-    if dist:
-        for st in sets:
-            del st["graph"]
-        del sel_graph, gat_graph
-        dist.destroy_process_group()
-    return 0
+    return run_decode(args, cfg)
 
 
 if __name__ == "__main__":

@@ -721,10 +721,13 @@ def match_pages(tmp, mapping, hsh, fine, members, hashes, refs, cap):
     hashes = np.asarray(hashes, np.int64).reshape(-1, 2)
     refs = np.asarray(refs, np.int32).reshape(-1)
     out = np.full(tmp.shape[0], -1, np.int32)
-    live = refs[:cap] > 0
+    hsh = np.asarray(hsh, np.int64).reshape(-1, 2)
+    live = np.nonzero(refs[:cap] > 0)[0]              # ascending page ids
+    h = hashes[live]
+    # candidates of every tmp page at once: live pages with both hashes equal
+    hit = (h[:, None, 0] == hsh[None, :, 0]) & (h[:, None, 1] == hsh[None, :, 1])
     for p in range(tmp.shape[0]):
-        good = live & (hashes[:cap, 0] == hsh[p][0]) & (hashes[:cap, 1] == hsh[p][1])
-        for j in np.nonzero(good)[0]:
+        for j in live[hit[:, p]]:
             if np.array_equal(fine[j], tmp[p]) and np.array_equal(members[j], mapping[p]):
                 out[p] = j
                 break
