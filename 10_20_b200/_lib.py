@@ -75,6 +75,8 @@ SIGNATURES = {
     "v1x_shared_normalize": [P, I64, P, P, P, P, P, I64, P, I64, I64, I64, I64, I32, I64, P],
     "v1x_shared_map_topk": [P, P, P, P, P, P, P, I64, P, I64, P, P, I64, I64, I64, I64, I64, P],
     "v1x_route_physical": [P, I64, P, P, P, P, P, I64, I64, I64, P],
+    "v1x_select_fused": [P, P, I64, P, P, I64, I64, P, P, I64, P, I64, P, I64, P, I64, P, I64, I64, I64, I64, I64,
+                         I64, P, P, P, P, P, P, P, P, P, P, P, I64, P, I64, I64, P, P],
 }
 # entry points whose return type is not int
 RESTYPES = {"v1x_last_error": ctypes.c_char_p, "v1x_build_workspace_bytes": ctypes.c_int64}

@@ -18,11 +18,20 @@ All buffers are allocated once; `run()` only launches kernels on the current
 stream (no host synchronisation), so the whole step can be captured in a CUDA
 graph with `capture()`.  Rows <= 512 take the same fused top-k: its outputs
 equal the reference's non-fused topk_transform + output_ids path.
+
+By default (`fused=True`) steps 1 and 3-6 are one launch per batch,
+v1x_select_fused: each row's metadata, route, fine scoring (sink and tail keys
+read from the native pages, so nothing is staged), boundary mask, Top-2048 and
+mapping in one CTA, the fine logits kept on chip.  The step is then three
+launches: centre scoring, selection, gather.  `fused=False` runs the
+operator-by-operator sequence above (the reference-shaped ops, also used by
+the parity tests as a second opinion).
 """
 from __future__ import annotations
 
 import torch
 
+from . import _lib
 from . import kernels as K
 from . import query_fused, scoring
 from .gather import _gather_impl
@@ -39,7 +48,8 @@ class SelectionStep:
     """
 
     def __init__(self, case, gather: bool = True, gather_v: bool = False, fused_route_pages: bool = True,
-                 keep_logits: bool = False, ratio=None, expand: bool = False, budget=None):
+                 keep_logits: bool = False, ratio=None, expand: bool = False, budget=None,
+                 fused: bool = True):
         """ratio=None: the fixed page budget take = min(pages, budget) (the
         reference's BudgetMetadata; budget an int32 device tensor of one element,
         by default holding case.take, which bounds it); ratio=(num, den): the
@@ -90,6 +100,13 @@ class SelectionStep:
         # outputs to route(center_logits) + fine_table_shared.
         self.fused_route_pages = fused_route_pages
         self.keep_logits = keep_logits or not fused_route_pages
+        # one-launch selection (route + fine scoring + top-k per row); the fine
+        # logits reach HBM only when they are kept for checks
+        self.fused_select = fused and fused_route_pages and (c.H == 1 or c.H % 32 == 0)
+        self.fine_scores_kept = keep_logits or not self.fused_select
+        if self.fused_select and not self.fine_scores_kept:
+            self.scores = None
+        self.status = torch.zeros(1, dtype=torch.int32, device=d)
 
     # -- the step ------------------------------------------------------------
     def _centres(self, rs):
@@ -131,6 +148,22 @@ class SelectionStep:
                         self.logical[rs], self.raw[rs], c.window, True, self.expanded[rs], True, True,
                         self.fine_table[rs], False)
 
+    def _select(self):
+        """v1x_select_fused over the whole batch (see the module docstring)."""
+        c = self.case
+        p = _lib.ptr
+        num, den = (0, 0) if self.budget is not None else self.ratio
+        scores = self.scores if self.fine_scores_kept else None
+        _lib.call("v1x_select_fused", p(c.q8), p(c.w), c.H, p(c.lens), p(self.budget), num, den,
+                  p(c.native_table), p(c.reordered_table), c.P, p(self.page_scores), self.page_scores.stride(0),
+                  p(c.fine), c.fine.shape[0], p(c.members), c.members.shape[0], p(c.native), c.native.shape[0],
+                  c.capacity, c.topk, c.window, self.selected.shape[1], self.fine_table.shape[1], p(self.fine_lens),
+                  p(self.takes), p(self.dg_lens), p(self.center_lens), p(self.tail_rows), p(self.selected),
+                  p(self.fine_table), p(self.physical), p(self.logical), p(self.raw),
+                  p(self.expanded) if self.expanded.shape[1] else None, self.expanded.shape[1], p(scores),
+                  scores.stride(0) if scores is not None else 0, c.B, p(self.status),
+                  torch.cuda.current_stream(c.lens.device).cuda_stream, device=c.lens.device)
+
     def _gather(self, rs):
         c = self.case
         lat = c.latent
@@ -154,6 +187,15 @@ class SelectionStep:
                 marks.append((name, ev))
 
         mark("start")
+        if self.fused_select:
+            self._centres(rs)
+            mark("centre_scores")
+            self._select()
+            mark("select")
+            if self.gather:
+                self._gather(rs)
+                mark("gather")
+            return
         # query metadata with the fixed page budget + sink/tail staging, one launch
         K.query_prepare(c.lens, c.native_table, self.fine_lens, self.takes, self.dg_lens, self.center_lens,
                         self.tail_rows, c.P, c.topk, self.ratio[0], self.ratio[1], 64, c.window, c.native,
@@ -192,6 +234,11 @@ class SelectionStep:
             self.graph.replay()
 
     # -- accounting ----------------------------------------------------------
+    def launches(self) -> int:
+        """Kernels one run() launches (centre scoring + selection, or the five
+        operators; + the gather)."""
+        return (2 if self.fused_select else 5) + (1 if self.gather else 0)
+
     def algorithmic_bytes(self) -> dict:
         """Compulsory bytes of one step, each input byte once, each output once
         (the per-request sum of `sharding.row_bytes`)."""
@@ -199,6 +246,7 @@ class SelectionStep:
         row = c.latent.shape[-1] * c.latent.element_size() if self.gather else 0
         total = {}
         for n in c.lens.tolist():
-            for k, v in row_bytes(n, c.H, c.take, c.window, c.topk, row, 2 if self.gather_v else 1).items():
+            for k, v in row_bytes(n, c.H, c.take, c.window, c.topk, row, 2 if self.gather_v else 1,
+                                  staging=not self.fused_select).items():
                 total[k] = total.get(k, 0) + v
         return total

@@ -13,12 +13,14 @@ import heapq
 
 
 def row_bytes(n: int, heads: int, take: int, window: int, topk: int, latent_row_bytes: int = 0,
-              outputs: int = 1) -> dict:
+              outputs: int = 1, staging: bool = True) -> dict:
     """Compulsory bytes of one request of token length n (each input byte once,
     each output byte once): q/w, centre keys (132 B per centre, 8 per built
-    page), sink/tail staging (read + write), fine keys + members of the selected
-    pages, the three int32 Top-k outputs and the latent gather (read once, written
-    `outputs` times)."""
+    page), sink/tail staging (read + write; only for the operator sequence that
+    copies those keys into the fine pool -- the fused selection scores them in
+    place, `staging=False`), fine keys (selected pages and the sink/tail
+    tokens) + members of the selected pages, the three int32 Top-k outputs and
+    the latent gather (read once, written `outputs` times)."""
     pages = max(n - 1, 0) // 1024 * 16
     tk = min(pages, take)
     sink = min(64, n)
@@ -26,7 +28,7 @@ def row_bytes(n: int, heads: int, take: int, window: int, topk: int, latent_row_
     count = sink + n - tail
     q = heads * (128 + 4)
     centres = pages * 8 * 132
-    staging = count * 132 * 2
+    staging = count * 132 * 2 if staging else 0
     fine = (tk * 64 + count) * 132 + tk * 64 * 4
     out = topk * 4 * 3
     gather = topk * latent_row_bytes * (1 + outputs) if latent_row_bytes else 0

@@ -1174,7 +1174,7 @@ def run_decode(args, cfg):
             "e2e_step_graphs": {"value": e2e_graph_value, "unit": "queries/s", "h2d_bytes_per_step": bat.h2d,
                                 "d2h_bytes_per_step": bat.d2h,
                                 "how": "SelectionStep graph replays, batches in flight, pinned copies per step"},
-            "gpu_launches": (5 + (1 if gather_on else 0)) * args.steps,
+            "gpu_launches": step.launches() * args.steps,
             "clocks": clocks,
             "wall_s": wall,
         }

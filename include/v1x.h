@@ -108,6 +108,50 @@ V1X_API int v1x_topk(float* scores, int64_t score_stride, int64_t cols, const in
              void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Extension (no reference counterpart): the query selection of one row per CTA
+ * -- query metadata (DS/kernels.py:568-591, fixed budget of
+ * bench_v1_dynamic_budget_metadata.py:5-28 or the ratio rule), fused.route over
+ * page maxima (VQ:7-49), fine_table_shared (DS/kernels.py:488-514), the FP8
+ * fine logits of the row's candidates (DeepGEMM contract, runtime.py:538-548,
+ * formula DS/kernels.py:310-313, ReLU scoring), the in-kernel boundary mask
+ * (bucket from rank) and fused.topk with physical output (VQ:62-153) -- in one
+ * launch.  The sink and tail candidates are scored from the native pool
+ * directly (stage_tail_shared's copies into the fine pool, DS/kernels.py:
+ * 518-564, are not made; the fine-table entries that name those staging pages
+ * are still written).
+ * q e4m3 [batch, heads, 128]; w f32 [batch, heads]; lens i32 [batch];
+ * budget: i32 device word (take = min(built pages, *budget)) or NULL with
+ * ratio_num/ratio_den > 0 (take = min(pages, max(ceil(pages*num/den),
+ * ceil(topk/64)))); take is clamped to take_stride.  native_table,
+ * reordered_table i32 [batch, pages]; page_scores f32 [batch, page_stride] (the
+ * max of each built page's 8 centre logits, -inf past them; v1x_score_fp8's
+ * page_max).  fine u8 [fine_pages, 8448] reordered pages; members i32
+ * [member_rows, 64]; native u8 [native_pages, 8448].
+ * Outputs: fine_lens, takes, dg_lens, center_lens, tail_rows i32 [batch];
+ * selected i32 [batch, take_stride]; fine_table i32 [batch, fine_cols];
+ * physical, logical, raw i32 [batch, topk]; expanded i32 [batch,
+ * expansion_stride] (stride 0 or 4*topk+64); scores_out f32 [batch,
+ * score_stride] or NULL: the masked fine logits of columns < fine_lens (for
+ * checks; score_stride >= take_stride*64 + 64 + max(window, 1024)).
+ * Selection and outputs equal those of v1x_query_metadata + v1x_route_pages +
+ * v1x_score_fp8 + v1x_topk(mask, bucket_from_rank, physical_output) on the
+ * same inputs.  Checks: heads 1 or a multiple of 32 <= 128, 0 < topk <= 2048,
+ * 0 <= window <= 4096, 64 <= pages <= 4096, 0 < take_stride <= min(pages, 128),
+ * fine_cols >= take_stride; q, pools and members 16-byte aligned.  status: a
+ * bounded wait that expires writes V1X_STATUS_TIMEOUT (may be NULL). */
+V1X_API int v1x_select_fused(const uint8_t* q, const float* w, int64_t heads, const int32_t* lens,
+                     const int32_t* budget, int64_t ratio_num, int64_t ratio_den,
+                     const int32_t* native_table, const int32_t* reordered_table, int64_t pages,
+                     const float* page_scores, int64_t page_stride, const uint8_t* fine,
+                     int64_t fine_pages, const int32_t* members, int64_t member_rows,
+                     const uint8_t* native, int64_t native_pages, int64_t capacity, int64_t topk,
+                     int64_t window, int64_t take_stride, int64_t fine_cols, int32_t* fine_lens,
+                     int32_t* takes, int32_t* dg_lens, int32_t* center_lens, int32_t* tail_rows,
+                     int32_t* selected, int32_t* fine_table, int32_t* physical, int32_t* logical,
+                     int32_t* raw, int32_t* expanded, int64_t expansion_stride, float* scores_out,
+                     int64_t score_stride, int64_t batch, int32_t* status, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* _sort -- replaces the Triton kernel NA/fused_grouping.py:64-76.
  * P (i32), S (f32), O (i32) are [heads, 4096]; segment (g, h) is the N
  * entries at h*4096 + g*N.  flag i32 scalar: the call is a no-op unless

@@ -165,10 +165,12 @@ def _small_case(B=24, H=64, seed=5, latent=576):
 
 
 def test_selection_step_end_to_end(cuda_dev):
-    """Every stage of the step vs the oracle: metadata exact, centre/fine scores
-    within tolerance, route/top-k/gather bit-exact given the device scores."""
+    """Every stage of the operator sequence vs the oracle: metadata exact,
+    centre/fine scores within tolerance, route/top-k/gather bit-exact given the
+    device scores.  (The one-launch selection is compared with this sequence in
+    test_gpu_select_fused.py.)"""
     case = _small_case()
-    step = pipeline.SelectionStep(case, gather=True, keep_logits=True)
+    step = pipeline.SelectionStep(case, gather=True, keep_logits=True, fused=False)
     step.run()
     torch.cuda.synchronize()
     c = case
