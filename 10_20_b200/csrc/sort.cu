@@ -6,13 +6,18 @@
 // (:70-74) -- score desc, position asc -- and O[... + i] = P[... + pos_i].  All
 // keys are unique, so any correct sort of them is bit-identical.
 //
-// One CTA sorts one segment.  Segments of 32..4096 records use a stable block
-// radix sort (CUB's header-only BlockRadixSort compiled into this kernel) of the
-// 32-bit ordered scores carrying their positions: descending, and stable, so
+// Segments of up to 256 records: one thread per record, several segments per
+// 256-thread CTA.  A record's output slot is its rank -- the number of records
+// of its segment with a larger ordered score, plus those with an equal score at
+// a lower position -- counted over the segment's keys in shared memory, and the
+// record's P value is stored straight to that slot.  The flag, scores and P
+// values are loaded together, so a launch costs one memory round trip.
+// Segments of 512..4096 records: one CTA per segment, a stable block radix sort
+// (CUB's header-only BlockRadixSort compiled into this kernel) of the 32-bit
+// ordered scores carrying the records' P values: descending, and stable, so
 // equal scores keep ascending positions -- the reference's composite key order.
-// A shared-memory bitonic network of all log2(N)*(log2(N)+1)/2 stages moves 32 B
-// of shared memory per compare-exchange and was bound by shared-memory bandwidth
-// (3% of HBM on 256 x 65,536 records); it remains for segments below 32 records.
+// A shared-memory bitonic network of all log2(N)*(log2(N)+1)/2 stages remains
+// for scores or outputs that are not 16-byte aligned.
 #include <cub/block/block_radix_sort.cuh>
 
 #include "common.cuh"
@@ -54,6 +59,47 @@ __device__ __forceinline__ uint32_t ordered_score(float s) {
   return b ^ ((b & 0x80000000u) ? 0xFFFFFFFFu : 0x80000000u);
 }
 
+// Segments of N <= 256 records, 256 / N of them per CTA (see the header).
+template <int N>
+__global__ void __launch_bounds__(256) sort_rank_kernel(const int32_t* __restrict__ P, int32_t* __restrict__ O,
+                                                        const float* __restrict__ S,
+                                                        const int32_t* __restrict__ flag, int groups) {
+  static_assert(N >= 2 && N <= 256 && (N & (N - 1)) == 0, "segment size");
+  constexpr int kSegs = 256 / N;
+  __shared__ __align__(16) uint32_t skey[256];
+  const int t = threadIdx.x;
+  const int g = blockIdx.x * kSegs + t / N;   // segment of this record
+  const int i = t % N;                        // its position in the segment
+  const bool live = g < groups;
+  const int64_t seg = static_cast<int64_t>(blockIdx.y) * 4096 + static_cast<int64_t>(g) * N;
+  // flag, score and P in one round trip
+  const int f = *flag;
+  float sc = 0.0f;
+  int pv = 0;
+  if (live) {
+    sc = S[seg + i];
+    pv = P[seg + i];
+  }
+  const uint32_t k = ordered_score(sc);
+  skey[t] = k;
+  __syncthreads();
+  if (f >= 0 || !live) return;
+  const uint32_t* keys = skey + (t / N) * N;
+  int rank = 0;
+  if constexpr (N >= 4) {
+#pragma unroll 8
+    for (int u = 0; u < N; u += 4) {
+      const uint4 v = *reinterpret_cast<const uint4*>(keys + u);
+      rank += (v.x > k) + (v.y > k) + (v.z > k) + (v.w > k);
+      rank += (v.x == k && u < i) + (v.y == k && u + 1 < i) + (v.z == k && u + 2 < i) + (v.w == k && u + 3 < i);
+    }
+  } else {
+#pragma unroll
+    for (int u = 0; u < N; ++u) rank += (keys[u] > k) + (keys[u] == k && u < i);
+  }
+  O[seg + rank] = pv;
+}
+
 struct LastValid {  // scan operator: the most recent valid (>= 0) value
   __device__ __forceinline__ int operator()(int a, int b) const { return b >= 0 ? b : a; }
 };
@@ -87,11 +133,13 @@ __global__ void __launch_bounds__(kThreads) sort_radix_kernel(const int32_t* __r
   } temp;
   __shared__ uint32_t red_and[kThreads / 32], red_or[kThreads / 32];
   __shared__ int red_min[kThreads / 32];
-  if (*flag >= 0) return;
   constexpr int N = kThreads * kItems;
   const int64_t base = static_cast<int64_t>(blockIdx.y) * 4096 + static_cast<int64_t>(blockIdx.x) * N;
   const int i0 = threadIdx.x * kItems;
+  // the flag, the scores and the P values (the sort's payload) in one round trip
+  const int f = *flag;
   float s[kItems];
+  int pv[kItems];
   if constexpr (kItems % 4 == 0) {   // 16-byte loads: segments start at multiples of N records
 #pragma unroll
     for (int k = 0; k < kItems; k += 4) {
@@ -100,11 +148,20 @@ __global__ void __launch_bounds__(kThreads) sort_radix_kernel(const int32_t* __r
       s[k + 1] = v.y;
       s[k + 2] = v.z;
       s[k + 3] = v.w;
+      const int4 q = *reinterpret_cast<const int4*>(P + base + i0 + k);
+      pv[k] = q.x;
+      pv[k + 1] = q.y;
+      pv[k + 2] = q.z;
+      pv[k + 3] = q.w;
     }
   } else {
 #pragma unroll
-    for (int k = 0; k < kItems; ++k) s[k] = S[base + i0 + k];
+    for (int k = 0; k < kItems; ++k) {
+      s[k] = S[base + i0 + k];
+      pv[k] = P[base + i0 + k];
+    }
   }
+  if (f >= 0) return;
   // Integer scores (group ids carried as floats): when every score of the segment
   // is an integer of magnitude <= 2^24, v - min is an order-preserving key (-0 and
   // +0 both map to 0, as the ordered key folds them) spanning far fewer bits than
@@ -126,12 +183,10 @@ __global__ void __launch_bounds__(kThreads) sort_radix_kernel(const int32_t* __r
     for (int w = 0; w < kThreads / 32; ++w) imin = min(imin, red_min[w]);
   }
   uint32_t key[kItems];
-  int pos[kItems];
   uint32_t kand = 0xFFFFFFFFu, kor = 0u;
 #pragma unroll
   for (int k = 0; k < kItems; ++k) {
     key[k] = ints ? static_cast<uint32_t>(static_cast<int>(s[k]) - imin) : ordered_score(s[k]);
-    pos[k] = i0 + k;
     kand &= key[k];
     kor |= key[k];
   }
@@ -150,18 +205,15 @@ __global__ void __launch_bounds__(kThreads) sort_radix_kernel(const int32_t* __r
   const uint32_t diff = kand ^ kor;   // bits that differ between some keys
   if (diff != 0u) {                   // all keys equal: the stable order is the identity
     const int begin = __ffs(diff) - 1, end = 32 - __clz(diff);
-    Sorter(temp.sort).SortDescending(key, pos, begin, end);
+    Sorter(temp.sort).SortDescending(key, pv, begin, end);
   }
-  int o[kItems];
-#pragma unroll
-  for (int k = 0; k < kItems; ++k) o[k] = P[base + pos[k]];
   if constexpr (kItems % 4 == 0) {
 #pragma unroll
     for (int k = 0; k < kItems; k += 4)
-      *reinterpret_cast<int4*>(O + base + i0 + k) = make_int4(o[k], o[k + 1], o[k + 2], o[k + 3]);
+      *reinterpret_cast<int4*>(O + base + i0 + k) = make_int4(pv[k], pv[k + 1], pv[k + 2], pv[k + 3]);
   } else {
 #pragma unroll
-    for (int k = 0; k < kItems; ++k) O[base + i0 + k] = o[k];
+    for (int k = 0; k < kItems; ++k) O[base + i0 + k] = pv[k];
   }
   if constexpr (kOffsets) {
     // sorted keys back to scores; -1 marks records outside the integer key range
@@ -250,16 +302,28 @@ extern "C" int v1x_sort_segments(const int32_t* P, int32_t* O, const float* S, c
   const dim3 grid(static_cast<unsigned>(groups), static_cast<unsigned>(heads));
   cudaStream_t s = as_stream(stream);
   const bool al = ((reinterpret_cast<uintptr_t>(S) | reinterpret_cast<uintptr_t>(O)) & 15) == 0;
-  switch (al ? N : 0) {
+  const int g = static_cast<int>(groups);
+  auto rank_grid = [&](int n) {
+    return dim3(static_cast<unsigned>((groups + 256 / n - 1) / (256 / n)), static_cast<unsigned>(heads));
+  };
+  switch (N) {   // records of up to 256 per segment: rank counting, any alignment
+    case 256: sort_rank_kernel<256><<<rank_grid(256), 256, 0, s>>>(P, O, S, flag, g); return launch_status("v1x_sort_segments");
+    case 128: sort_rank_kernel<128><<<rank_grid(128), 256, 0, s>>>(P, O, S, flag, g); return launch_status("v1x_sort_segments");
+    case 64: sort_rank_kernel<64><<<rank_grid(64), 256, 0, s>>>(P, O, S, flag, g); return launch_status("v1x_sort_segments");
+    case 32: sort_rank_kernel<32><<<rank_grid(32), 256, 0, s>>>(P, O, S, flag, g); return launch_status("v1x_sort_segments");
+    case 16: sort_rank_kernel<16><<<rank_grid(16), 256, 0, s>>>(P, O, S, flag, g); return launch_status("v1x_sort_segments");
+    case 8: sort_rank_kernel<8><<<rank_grid(8), 256, 0, s>>>(P, O, S, flag, g); return launch_status("v1x_sort_segments");
+    case 4: sort_rank_kernel<4><<<rank_grid(4), 256, 0, s>>>(P, O, S, flag, g); return launch_status("v1x_sort_segments");
+    case 2: sort_rank_kernel<2><<<rank_grid(2), 256, 0, s>>>(P, O, S, flag, g); return launch_status("v1x_sort_segments");
+    default: break;
+  }
+  const bool alp = al && (reinterpret_cast<uintptr_t>(P) & 15) == 0;
+  switch (alp ? N : 0) {
     case 4096: sort_radix_kernel<512, 8, false><<<grid, 512, 0, s>>>(P, O, S, flag, nullptr, 0, 0); break;
     case 2048: sort_radix_kernel<256, 8, false><<<grid, 256, 0, s>>>(P, O, S, flag, nullptr, 0, 0); break;
     case 1024: sort_radix_kernel<128, 8, false><<<grid, 128, 0, s>>>(P, O, S, flag, nullptr, 0, 0); break;
     case 512: sort_radix_kernel<64, 8, false><<<grid, 64, 0, s>>>(P, O, S, flag, nullptr, 0, 0); break;
-    case 256: sort_radix_kernel<32, 8, false><<<grid, 32, 0, s>>>(P, O, S, flag, nullptr, 0, 0); break;
-    case 128: sort_radix_kernel<32, 4, false><<<grid, 32, 0, s>>>(P, O, S, flag, nullptr, 0, 0); break;
-    case 64: sort_radix_kernel<32, 2, false><<<grid, 32, 0, s>>>(P, O, S, flag, nullptr, 0, 0); break;
-    case 32: sort_radix_kernel<32, 1, false><<<grid, 32, 0, s>>>(P, O, S, flag, nullptr, 0, 0); break;
-    default: {  // below 32 records, or unaligned scores / output
+    default: {  // unaligned scores, P or output
       const int threads = static_cast<int>(N / 2 < 1024 ? (N / 2 < 32 ? 32 : N / 2) : 1024);
       sort_kernel<<<grid, threads, static_cast<size_t>(N) * 12, s>>>(P, O, S, flag, static_cast<int>(N));
     }
@@ -290,8 +354,9 @@ extern "C" int v1x_sort_segments_grouped(const int32_t* P, int32_t* O, const flo
                 "sort_segments_grouped: N must be a power of two in [256, 4096]");
   V1X_CHECK_ARG(groups >= 0 && heads >= 0 && groups * N <= 4096, "sort_segments_grouped: groups*N exceeds 4096");
   V1X_CHECK_ARG(key_range >= 1 && key_range <= (1 << 20), "sort_segments_grouped: key_range in [1, 2^20]");
-  V1X_CHECK_ARG(((reinterpret_cast<uintptr_t>(S) | reinterpret_cast<uintptr_t>(O)) & 15) == 0,
-                "sort_segments_grouped: S and O must be 16-byte aligned");
+  V1X_CHECK_ARG(((reinterpret_cast<uintptr_t>(S) | reinterpret_cast<uintptr_t>(O) |
+                  reinterpret_cast<uintptr_t>(P)) & 15) == 0,
+                "sort_segments_grouped: S, P and O must be 16-byte aligned");
   if (groups == 0 || heads == 0) return V1X_OK;
   const dim3 grid(static_cast<unsigned>(groups), static_cast<unsigned>(heads));
   cudaStream_t s = as_stream(stream);

@@ -171,7 +171,7 @@ V1X_API int v1x_group_offsets(const float* S, int32_t* offsets, int64_t N, int64
 /* Extension (no reference counterpart): _sort and v1x_group_offsets in one pass
  * for N in {256, ..., 4096}: O as v1x_sort_segments, offsets [heads*groups,
  * key_range+1] as v1x_group_offsets (key_range <= 2^20), derived from the sorted
- * keys.  S and O 16-byte aligned. */
+ * keys.  S, P and O 16-byte aligned. */
 V1X_API int v1x_sort_segments_grouped(const int32_t* P, int32_t* O, const float* S, const int32_t* flag,
                       int32_t* offsets, int64_t N, int64_t groups, int64_t heads, int64_t key_range,
                       void* stream);

@@ -39,7 +39,7 @@ def test_sort_golden(golden, cuda_dev):
     assert np.array_equal(o.cpu().numpy(), g["o4096"])
 
 
-@pytest.mark.parametrize("N", [2, 16, 32, 64, 128, 256, 512, 1024, 2048, 4096])
+@pytest.mark.parametrize("N", [2, 4, 8, 16, 32, 64, 128, 256, 512, 1024, 2048, 4096])
 def test_sort_random_sizes(N, cuda_dev):
     rng = np.random.default_rng(N)
     heads = 16
@@ -53,6 +53,33 @@ def test_sort_random_sizes(N, cuda_dev):
     o = torch.full((heads, 4096), -7, dtype=torch.int32, device="cuda")
     FG._sort[(4096 // N, heads)](dev(P), o, dev(S), flag, N)
     assert np.array_equal(o.cpu().numpy().reshape(-1), O.sort_segments(P, S, -1, N, 4096 // N, heads))
+
+
+@pytest.mark.parametrize("N,groups", [(16, 5), (64, 3), (256, 1), (1024, 2)])
+def test_sort_partial_grid(N, groups, cuda_dev):
+    """A grid of fewer groups than 4096 / N sorts only those segments; the rest
+    of O is untouched.  Unaligned (offset) views take the same answers."""
+    rng = np.random.default_rng(N + groups)
+    heads = 3
+    S = rng.integers(0, 7, size=(heads, 4096)).astype(np.float32)
+    P = rng.permutation(heads * 4096).astype(np.int32).reshape(heads, 4096)
+    flag = torch.tensor(-1, dtype=torch.int32, device="cuda")
+    o = torch.full((heads, 4096), -7, dtype=torch.int32, device="cuda")
+    FG._sort[(groups, heads)](dev(P), o, dev(S), flag, N)
+    got = o.cpu().numpy()
+    exp = np.full((heads, 4096), -7, np.int32)
+    full = O.sort_segments(P, S, -1, N, groups, heads).reshape(heads, 4096)
+    exp[:, :groups * N] = full[:, :groups * N]
+    assert np.array_equal(got, exp)
+    # 4-byte (not 16-byte) aligned views of the same data
+    Sb = torch.zeros(heads * 4096 + 1, device="cuda")
+    Sb[1:] = dev(S).reshape(-1)
+    Pb = torch.zeros(heads * 4096 + 1, dtype=torch.int32, device="cuda")
+    Pb[1:] = dev(P).reshape(-1)
+    ob = torch.full((heads * 4096 + 1,), -7, dtype=torch.int32, device="cuda")
+    FG._sort[(groups, heads)](Pb[1:].view(heads, 4096), ob[1:].view(heads, 4096), Sb[1:].view(heads, 4096), flag,
+                              N)
+    assert np.array_equal(ob[1:].view(heads, 4096).cpu().numpy(), exp)
 
 
 def test_sort_baseline_records_and_offsets(cuda_dev):
