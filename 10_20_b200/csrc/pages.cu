@@ -438,20 +438,28 @@ __global__ void __launch_bounds__(256) confirm_kernel(const uint8_t* __restrict_
   }
 }
 
-// The sequential part, one warp: buckets in order, lanes 0-15 = the bucket's
-// pages.  A page without a live match takes the slot of its earliest equal
-// page in an earlier bucket of the batch (that page was fresh: an equal page
-// with a live match would have given this page the same match; after a
-// fingerprint collision the fresh pages so far are searched and compared
-// here, in a shared-memory hash table of them); then the
-// reference's allocate (fresh pages pop FREE[count-1-rank], staged in shared
-// memory from the top of the stack), refcounts, lease table and new-page
-// flags.  The first bucket that finds the free stack too short writes
-// V1X_STATUS_ARENA_EXHAUSTED and it and every later bucket change nothing
-// (flags = aborted, lease table rows = -1); a status word that already holds
-// the exhaustion aborts every bucket of the call.  With state_tables, the request's page-table row (state
-// row from the meta record) and centre-table row receive the bucket's pages,
-// as the driver's copies of the lease tables do after each reference Build.
+// The allocate decisions of every bucket of the call, one CTA of 1024 threads
+// (one per batch page).  The reference decides bucket after bucket; the same
+// answers come from closed forms:
+//   * a page is FRESH iff it has no live match and no page of an earlier
+//     bucket of the call has equal bytes and members -- the earliest such page
+//     is BatchWork::first (its lowest equal-fingerprint page when that one's
+//     bytes are equal; after a fingerprint collision a warp searches the
+//     earlier pages here);
+//   * that earliest equal page is itself fresh (an equal page with a live
+//     match would have given this page the same match; an earlier equal page
+//     would be earlier still), so the page takes its slot;
+//   * bucket b's fresh pages pop FREE[count-1-off_b-rank], off_b the fresh
+//     pages of the active buckets before b (a scan over the buckets), rank the
+//     page's place among its bucket's fresh pages;
+//   * the first bucket whose fresh pages exceed the free pages left writes
+//     V1X_STATUS_ARENA_EXHAUSTED; it and every later bucket change nothing
+//     (flags = aborted, lease table rows = -1); a status word that already
+//     holds the exhaustion aborts every bucket of the call.
+// Then refcounts (atomic adds: several pages may share a slot), lease tables,
+// new-page flags and, with state_tables, the request's page-table row (state
+// row from the meta record) and centre-table row, as the driver's copies of the
+// lease tables do after each reference Build.
 struct StateRows {
   int32_t* tables;
   int64_t table_stride;
@@ -460,116 +468,124 @@ struct StateRows {
   const int32_t* center_pages;
 };
 
-__global__ void __launch_bounds__(128) decide_kernel(
+constexpr int kDecideThreads = kBatchPages;   // 1024: one thread per batch page
+
+__global__ void __launch_bounds__(kDecideThreads) decide_kernel(
     const uint8_t* __restrict__ tmp, const int32_t* __restrict__ map, const int64_t* __restrict__ hash,
     const int32_t* __restrict__ meta, const int32_t* __restrict__ match, int nb, const int32_t* __restrict__ free_stack,
     int32_t* __restrict__ count, int32_t* __restrict__ refs, int32_t* __restrict__ tables,
     uint8_t* __restrict__ new_flags, int32_t* __restrict__ status, const StateRows rows,
     const int32_t* __restrict__ work) {
   __shared__ int64_t sh0[kBatchPages], sh1[kBatchPages];
-  __shared__ int32_t sdst[kBatchPages];   // live match (INT_MAX: none), then the page's arena slot
-  __shared__ int32_t sfirst[kBatchPages]; // BatchWork::first
-  __shared__ int32_t sfree[kBatchPages];  // sfree[i] = FREE[count0 - 1 - i]
-  __shared__ int32_t table[kQTable];      // fresh pages so far (searched after a collision)
-  __shared__ int32_t smeta[kBatchBuckets * kBatchMeta];
+  __shared__ int32_t ssrc[kBatchPages];      // earliest equal page of an earlier bucket, or -1
+  __shared__ int32_t sfree[kBatchPages];     // sfree[i] = FREE[count0 - 1 - i]
+  __shared__ uint32_t sfresh[kBatchBuckets]; // per bucket: lane mask of its fresh pages
+  __shared__ int32_t soff[kBatchBuckets + 1];
+  __shared__ int32_t scoll[kBatchPages];     // pages left to the collision search
+  __shared__ int ncoll, abort_from;
   const BatchWork w(const_cast<int32_t*>(work));
+  const int q = threadIdx.x, lane = q & 31;
   const int nq = nb * 16;
+  const int b = q >> 4;
   const int cnt0 = *count;
-  for (int i = threadIdx.x; i < kQTable; i += blockDim.x) table[i] = 0;
-  for (int q = threadIdx.x; q < nq; q += blockDim.x) {
+  const bool sticky = status != nullptr && *status == V1X_STATUS_ARENA_EXHAUSTED;
+  const bool in = q < nq;
+  const bool active = in && meta[b * kBatchMeta + 2] != 0;
+  int m = -1, f = kFirstNone;
+  if (in) {
     sh0[q] = hash[2 * q];
     sh1[q] = hash[2 * q + 1];
-    sdst[q] = match[q];
-    sfirst[q] = w.first[q];
+    const int mq = match[q];
+    m = mq != INT_MAX ? mq : -1;
+    f = w.first[q];
   }
-  for (int i = threadIdx.x; i < min(nq, cnt0); i += blockDim.x) sfree[i] = free_stack[cnt0 - 1 - i];
-  for (int i = threadIdx.x; i < nb * kBatchMeta; i += blockDim.x) smeta[i] = meta[i];
+  for (int i = q; i < min(nq, cnt0); i += kDecideThreads) sfree[i] = free_stack[cnt0 - 1 - i];
+  if (q == 0) ncoll = 0;
   __syncthreads();
-  if (threadIdx.x >= 32) return;
-  const int lane = threadIdx.x;
-  const uint32_t lt = (1u << lane) - 1u;
-  int cnt = cnt0;
-  // sticky exhaustion: an earlier call's exhaustion, not yet cleared by the
-  // host, aborts this call too
-  bool aborted = status != nullptr && *status == V1X_STATUS_ARENA_EXHAUSTED;
-  for (int b = 0; b < nb; ++b) {
-    const int* bm = smeta + b * kBatchMeta;  // token start, lease, active, state row
-    if (bm[2] == 0) continue;                 // inactive bucket: nothing to do
-    const int qi = b * 16 + lane;
-    if (aborted) {
-      if (lane < 16) {
-        new_flags[qi] = kAborted;
-        tables[static_cast<int64_t>(bm[1]) * 16 + lane] = -1;
-      }
-      continue;
-    }
-    int m = -1;
-    if (lane < 16 && sdst[qi] != INT_MAX) m = sdst[qi];
-    const int f = lane < 16 ? sfirst[qi] : kFirstNone;
-    if (m < 0 && f >= 0 && f != kFirstNone) m = sdst[f];
-    if (__any_sync(0xffffffffu, lane < 16 && m < 0 && f == kFirstCollision)) {
-      int slot = (lane < 16 && m < 0 && f == kFirstCollision) ? static_cast<int>(fp_slot(sh0[qi], sh1[qi])) : -1;
-      while (true) {
-        int cand = -1;
-        while (slot >= 0) {
-          const int e = table[slot];
-          if (e == 0) {
-            slot = -1;
-            break;
-          }
-          slot = static_cast<int>((slot + 1) & kQMask);
-          if (sh0[e - 1] == sh0[qi] && sh1[e - 1] == sh1[qi]) {
-            cand = e - 1;
-            break;
-          }
-        }
-        unsigned todo = __ballot_sync(0xffffffffu, cand >= 0);
-        if (!todo) break;
-        while (todo) {
-          const int src = __ffs(todo) - 1;
-          todo &= todo - 1;
-          const int q2 = __shfl_sync(0xffffffffu, cand, src);
-          const int q1 = b * 16 + src;
-          const bool eq = warp_pages_equal(tmp + static_cast<int64_t>(q1) * kPageBytes, map + q1 * 64,
-                                           tmp + static_cast<int64_t>(q2) * kPageBytes, map + q2 * 64);
-          if (lane == src && eq) {
-            m = sdst[q2];
-            slot = -1;
-          }
-        }
-      }
-    }
-    const bool fresh = lane < 16 && m < 0;
-    const unsigned fm = __ballot_sync(0xffffffffu, fresh);
-    const int needed = __popc(fm);
-    if (cnt < needed) {
-      aborted = true;
-      if (lane < 16) {
-        new_flags[qi] = kAborted;
-        tables[static_cast<int64_t>(bm[1]) * 16 + lane] = -1;
-      }
-      if (lane == 0 && status) *status = V1X_STATUS_ARENA_EXHAUSTED;
-      continue;
-    }
-    if (lane < 16) {
-      const int dst = fresh ? sfree[(cnt0 - cnt) + __popc(fm & lt)] : m;
-      atomicAdd(&refs[dst], 1);
-      tables[static_cast<int64_t>(bm[1]) * 16 + lane] = dst;
-      new_flags[qi] = fresh ? 1 : 0;
-      sdst[qi] = dst;
-      if (fresh) fp_insert(table, fp_slot(sh0[qi], sh1[qi]), qi);
-      if (rows.tables) {
-        const int64_t bucket = bm[0] / 1024;
-        rows.tables[bm[3] * rows.table_stride + bucket * 16 + lane] = dst;
-        if (lane < 2)
-          rows.centers[bm[3] * rows.center_stride + bucket * 2 + lane] =
-              rows.center_pages[static_cast<int64_t>(bm[1]) * 2 + lane];
-      }
-    }
-    cnt -= needed;
-    __syncwarp();
+  int src = -1;
+  if (active && m < 0) {
+    if (f >= 0 && f != kFirstNone) src = f;
+    else if (f == kFirstCollision) scoll[atomicAdd(&ncoll, 1)] = q;
   }
-  if (lane == 0) *count = cnt;
+  if (in) ssrc[q] = src;
+  __syncthreads();
+  // after a fingerprint collision: the earliest page of an earlier bucket with
+  // equal bytes and members (one warp per such page; rare)
+  for (int k = q >> 5; k < ncoll; k += kDecideThreads / 32) {
+    const int qc = scoll[k];
+    const int lim = (qc >> 4) << 4;           // pages of earlier buckets
+    int found = -1;
+    for (int p0 = 0; p0 < lim && found < 0; p0 += 32) {
+      const int p = p0 + lane;
+      const bool cand = p < lim && meta[(p >> 4) * kBatchMeta + 2] != 0 && sh0[p] == sh0[qc] && sh1[p] == sh1[qc];
+      unsigned todo = __ballot_sync(0xffffffffu, cand);
+      while (todo && found < 0) {
+        const int pc = p0 + __ffs(todo) - 1;
+        todo &= todo - 1;
+        if (warp_pages_equal(tmp + static_cast<int64_t>(qc) * kPageBytes, map + qc * 64,
+                             tmp + static_cast<int64_t>(pc) * kPageBytes, map + pc * 64))
+          found = pc;
+      }
+    }
+    if (lane == 0) ssrc[qc] = found;
+  }
+  __syncthreads();
+  // fresh pages, per bucket
+  const bool fresh = active && m < 0 && ssrc[q] < 0;
+  const unsigned bal = __ballot_sync(0xffffffffu, fresh);
+  const uint32_t mine = (bal >> (q & 16)) & 0xFFFFu;   // this half-warp's bucket
+  if ((q & 15) == 0 && b < kBatchBuckets) sfresh[b] = b < nb ? mine : 0u;
+  __syncthreads();
+  // exclusive scan of the buckets' fresh counts and the first exhausted bucket
+  if (q < 32) {
+    int c0 = 0, c1 = 0;
+    const int b0 = 2 * q, b1 = 2 * q + 1;
+    if (b0 < nb) c0 = __popc(sfresh[b0]);
+    if (b1 < nb) c1 = __popc(sfresh[b1]);
+    const int inc = warp_inclusive_scan(c0 + c1);
+    const int o0 = inc - c0 - c1, o1 = o0 + c0;
+    soff[b0] = o0;
+    soff[b1] = o1;
+    if (q == 31) soff[kBatchBuckets] = inc;
+    // bucket bb aborts when its fresh pages exceed what the buckets before it left
+    const bool x0 = b0 < nb && cnt0 - o0 < c0, x1 = b1 < nb && cnt0 - o1 < c1;
+    const int first_ab = __reduce_min_sync(0xffffffffu, x0 ? b0 : (x1 ? b1 : nb));
+    if (q == 0) abort_from = sticky ? 0 : first_ab;
+  }
+  __syncthreads();
+  const int ab = abort_from;
+  if (active) {
+    const int64_t lease = meta[b * kBatchMeta + 1];
+    if (b >= ab) {
+      new_flags[q] = kAborted;
+      tables[lease * 16 + (q & 15)] = -1;
+    } else {
+      int dst;
+      if (m >= 0) {
+        dst = m;
+      } else {
+        // this page's, or its earliest equal page's, place on the free stack
+        const int p = fresh ? q : ssrc[q];
+        const int pb = p >> 4;
+        dst = sfree[soff[pb] + __popc(sfresh[pb] & ((1u << (p & 15)) - 1u))];
+      }
+      atomicAdd(&refs[dst], 1);
+      tables[lease * 16 + (q & 15)] = dst;
+      new_flags[q] = fresh ? 1 : 0;
+      if (rows.tables) {
+        const int64_t bucket = meta[b * kBatchMeta] / 1024;
+        const int64_t srow = meta[b * kBatchMeta + 3];
+        rows.tables[srow * rows.table_stride + bucket * 16 + (q & 15)] = dst;
+        if ((q & 15) < 2)
+          rows.centers[srow * rows.center_stride + bucket * 2 + (q & 15)] =
+              rows.center_pages[lease * 2 + (q & 15)];
+      }
+    }
+  }
+  if (q == 0) {
+    if (ab < nb && status && !sticky) *status = V1X_STATUS_ARENA_EXHAUSTED;
+    *count = cnt0 - soff[min(ab, nb) == nb ? kBatchBuckets : ab];
+  }
 }
 
 // Releases of several requests in order, one CTA.  A request's pages are
@@ -716,8 +732,8 @@ extern "C" int v1x_prepare_buckets(const uint8_t* tmp, const uint8_t* tc_bytes, 
   confirm_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(tmp, map, hash, meta, fine, members, hashes, refs,
                                                                 match, cap, nq, work);
   const StateRows rows{state_tables, state_table_stride, state_centers, state_center_stride, center_pages};
-  decide_kernel<<<1, 128, 0, s>>>(tmp, map, hash, meta, match, static_cast<int>(buckets), free_stack, count, refs,
-                                  tables, new_flags, status, rows, work);
+  decide_kernel<<<1, kDecideThreads, 0, s>>>(tmp, map, hash, meta, match, static_cast<int>(buckets), free_stack,
+                                           count, refs, tables, new_flags, status, rows, work);
   publish_kernel<<<nq, 256, 0, s>>>(tmp, tc_bytes, tc_scales, map, hash, meta, tables, new_flags, fine, centers,
                                     center_scales, members, hashes, kBatchMeta);
   return launch_status("v1x_prepare_buckets");
