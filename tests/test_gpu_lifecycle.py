@@ -350,3 +350,62 @@ def test_prepare_buckets_entry_point_random_batches(seed, cuda_dev):
         assert np.array_equal(getattr(gpu, name).cpu().numpy(), getattr(exp, name)), name
     assert (int(status.item()) == _lib.V1X_STATUS_ARENA_EXHAUSTED) == exhausted_exp
     assert np.array_equal(new.cpu().numpy(), new_exp)
+
+
+def test_prepare_buckets_pair_list_overflow(cuda_dev):
+    """More fingerprint-equal (live page, batch page) pairs than the pair list
+    holds: 80 live arena pages and 128 batch pages that all share one
+    fingerprint (the same bytes, members differing by multiples of the
+    +1/-2/+1 collision pattern) give 10,240 pairs, so the call takes its exact
+    fallback (the sweep with inline confirmation).  Some batch pages equal a
+    live page, some are new, some repeat a new page of an earlier bucket behind
+    a colliding one.  The arena afterwards equals the restated algorithm's."""
+    import copy
+
+    _lib = importlib.import_module("10_20_b200._lib")
+    cap, pages = 2048, 256
+    rng = np.random.default_rng(77)
+    x = rng.integers(0, 256, 8448, dtype=np.uint8)
+    m0 = (5000 + np.arange(64)).astype(np.int32)
+    delta = np.zeros(64, np.int32)
+    delta[:3] = (1, -2, 1)
+    variant = lambda k: (m0 + k * delta).astype(np.int32)
+    cpu = port.ArenaPort(cap, pages, max_requests=8)
+    for b in range(5):                       # 80 live variants k = 0..79
+        tmp = np.stack([x] * 16)
+        mp = np.stack([variant(16 * b + i) for i in range(16)])
+        cpu._bucket(tmp, mp, rng.integers(0, 256, (2, 8448), dtype=np.uint8), b * 1024, b)
+    nb = 8
+    ks = []
+    for b in range(nb):                      # live k < 80, new k in [80, 120): repeats across buckets
+        ks.append(rng.choice(np.arange(120), size=16, replace=False))
+    tmp = np.stack([np.stack([x] * 16) for _ in range(nb)])
+    mp = np.stack([np.stack([variant(int(k)) for k in row]) for row in ks])
+    centers = rng.integers(0, 256, (nb, 2, 8448), dtype=np.uint8)
+    meta3 = np.array([[b * 1024, 5 + b, 1] for b in range(nb)], np.int32)
+    exp = copy.deepcopy(cpu)
+    new_exp, exhausted_exp = port.prepare_buckets_batched(exp, tmp, centers, mp, meta3)
+    gpu = lifecycle.PageArena(cap, pages, "cuda", max_requests=8)
+    for name in ("refs", "free", "tables", "members", "hashes", "fine", "centers"):
+        getattr(gpu, name).copy_(torch.from_numpy(np.ascontiguousarray(getattr(cpu, name))))
+    gpu.free_count.fill_(cpu.count)
+    meta = torch.tensor([[b * 1024, 5 + b, 1, 0] for b in range(nb)], dtype=torch.int32, device="cuda")
+    t, m, c = (torch.from_numpy(a).cuda() for a in (tmp, mp, centers))
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    work = torch.zeros(lifecycle.PREPARE_WORK_INTS, dtype=torch.int32, device="cuda")
+    hsh = torch.zeros((nb * 16, 2), dtype=torch.int64, device="cuda")
+    match = torch.zeros(nb * 16, dtype=torch.int32, device="cuda")
+    new = torch.zeros(nb * 16, dtype=torch.uint8, device="cuda")
+    p = _lib.ptr
+    _lib.call("v1x_prepare_buckets", p(t), p(c), p(c.view(torch.float32)), p(m), p(meta), nb, p(hsh), p(match),
+              p(new), p(gpu.fine), p(gpu.centers), p(gpu.centers.view(torch.float32)), p(gpu.members),
+              p(gpu.hashes), p(gpu.refs), p(gpu.free), p(gpu.free_count), p(gpu.tables), p(gpu.center_pages),
+              None, 0, None, 0, cap, p(work), p(status), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert int(work[2].item()) & 1, "the pair list did not overflow"
+    assert not exhausted_exp and int(status.item()) == 0
+    assert int(gpu.free_count.item()) == exp.count
+    for name in ("refs", "free", "tables", "members", "hashes", "fine", "centers"):
+        assert np.array_equal(getattr(gpu, name).cpu().numpy(), getattr(exp, name)), name
+    assert np.array_equal(new.cpu().numpy(), new_exp)
+    assert 0 < int(new_exp.sum()) < nb * 16          # both fresh pages and matches occurred
