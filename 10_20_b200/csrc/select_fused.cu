@@ -694,7 +694,8 @@ __global__ void __launch_bounds__(kSfThreads, kPer <= 2 ? 2 : 1)
         const int lp = sh.natp[2 * t + h];
         if (lp >= 0 && lp < a.pages) {
           const int lg = lp * 64 + slot;
-          if (lg < sink) col = lg;
+          // raw columns: [take*64 selected keys | sink | tail]
+          if (lg < sink) col = tk * 64 + lg;
           else if (lg >= tail && lg < sh.n) col = tk * 64 + sink + lg - tail;
         }
       } else {
