@@ -62,18 +62,28 @@ __global__ void __launch_bounds__(256) fingerprint_kernel(const uint8_t* __restr
   if (counters && p == 0 && threadIdx.x < 4) counters[threadIdx.x] = 0;
   if (meta[(p / pages_per_meta) * meta_stride + 2] == 0) return;
   const uint4* src = reinterpret_cast<const uint4*>(tmp + p * kPageBytes);
-  uint64_t a = 0, b = 0;
+  // byte i = 16c + j of the page (j < 16): x_i * (i + 1) = x_i * 16c + x_i * (j + 1),
+  // so per 16-byte chunk two byte dot products (dp4a) give sum x and sum x*(j+1);
+  // sum x_i*(i+7) = sum x_i*(i+1) + 6 * sum x_i.  Partial sums stay in 32 bits
+  // (a thread's chunks sum to < 2^32), the totals wrap in 64 bits as the
+  // reference's int64 sums do.
+  uint32_t s1 = 0, s0 = 0;
   for (int c = threadIdx.x; c < kPageBytes / 16; c += blockDim.x) {
     const uint4 v = src[c];
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int q = 0; q < 16; ++q) {
-      const uint64_t x = (w[q >> 2] >> (8 * (q & 3))) & 0xFFu;
-      const uint64_t i = static_cast<uint64_t>(c) * 16 + q;
-      a += x * (i + 1);
-      b += x * ((i + 7) * 1000003ull);
-    }
+    uint32_t lo = 0, cs = 0;
+    lo = __dp4a(v.x, 0x04030201u, lo);
+    lo = __dp4a(v.y, 0x08070605u, lo);
+    lo = __dp4a(v.z, 0x0C0B0A09u, lo);
+    lo = __dp4a(v.w, 0x100F0E0Du, lo);
+    cs = __dp4a(v.x, 0x01010101u, cs);
+    cs = __dp4a(v.y, 0x01010101u, cs);
+    cs = __dp4a(v.z, 0x01010101u, cs);
+    cs = __dp4a(v.w, 0x01010101u, cs);
+    s1 += lo + cs * static_cast<uint32_t>(16 * c);
+    s0 += cs;
   }
+  uint64_t a = s1;
+  uint64_t b = (static_cast<uint64_t>(s1) + 6ull * s0) * 1000003ull;
   if (threadIdx.x < 64) {
     const uint64_t m = static_cast<uint64_t>(static_cast<int64_t>(map[p * 64 + threadIdx.x]));
     a += m * 104729ull;
