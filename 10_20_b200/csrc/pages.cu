@@ -35,6 +35,7 @@
 // positions); and a page that is not live at the start can only match a page
 // published inside the batch.  (The CPU test suite restates this algorithm in
 // numpy and compares it with the per-bucket sequence on randomised calls.)
+#include <algorithm>
 #include <climits>
 
 #include "common.cuh"
@@ -378,7 +379,7 @@ __device__ void sweep_inline(const QueryTable& t, const uint8_t* tmp, const int3
 // page's, and for every batch page the lowest page of an earlier bucket with
 // the same fingerprint (one pair per page, whatever the number of copies).  No
 // bytes are compared here; confirm_kernel does that in parallel.
-__global__ void __launch_bounds__(256) match_batch_kernel(const int64_t* __restrict__ hash,
+__global__ void __launch_bounds__(1024) match_batch_kernel(const int64_t* __restrict__ hash,
                                                           const int32_t* __restrict__ meta,
                                                           const int64_t* __restrict__ hashes,
                                                           const int32_t* __restrict__ refs, int64_t cap, int nq,
@@ -738,7 +739,10 @@ extern "C" int v1x_prepare_buckets(const uint8_t* tmp, const uint8_t* tc_bytes, 
   int64_t blocks = (cap + 255) / 256;
   const int64_t maxb = static_cast<int64_t>(num_sms()) * 4;
   if (blocks > maxb) blocks = maxb;
-  match_batch_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(hash, meta, hashes, refs, cap, nq, work);
+  // the sweep: one 1024-thread CTA per SM, each builds the call's fingerprint
+  // table in shared memory (one insert per thread) and sweeps its share of the arena
+  const int64_t sweep_blocks = std::min<int64_t>((cap + 1023) / 1024, num_sms());
+  match_batch_kernel<<<static_cast<unsigned>(sweep_blocks), 1024, 0, s>>>(hash, meta, hashes, refs, cap, nq, work);
   confirm_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(tmp, map, hash, meta, fine, members, hashes, refs,
                                                                 match, cap, nq, work);
   const StateRows rows{state_tables, state_table_stride, state_centers, state_center_stride, center_pages};
