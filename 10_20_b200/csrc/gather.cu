@@ -80,8 +80,12 @@ __global__ void __launch_bounds__(256) gather_vec_kernel(const __grid_constant__
 // (kCpr * kR is a multiple of 32, so no lane idles).  Per chunk this is a handful
 // of instructions -- the general path above spends a 64-bit division per chunk,
 // which at ~37M chunks per decode step is as long as the copy itself.
+// Single-output gathers (K only, the MMA latent) are capped at 64 registers so
+// that four 256-thread CTAs fit an SM: 32 warps of 9 loads in flight instead of
+// 24 (89% -> 93% of HBM on the 1024 x 2048-slot gather); with V as well the
+// cap would spill, so those keep the default.
 template <int kCpr, int kR, bool kHasV>
-__global__ void __launch_bounds__(256) gather_rows_kernel(const __grid_constant__ GatherArgs a) {
+__global__ void __launch_bounds__(256, kHasV ? 1 : 4) gather_rows_kernel(const __grid_constant__ GatherArgs a) {
   static_assert((kCpr * kR) % 32 == 0, "a row group must fill the warp's lanes");
   constexpr int kPer = kCpr * kR / 32;
   const int lane = threadIdx.x & 31;

@@ -458,6 +458,7 @@ __global__ void __launch_bounds__(kSfThreads, kPer <= 2 ? 2 : 1)
   // row view of the union: scores (keys after the Top-T conversion) + members
   float* sc = reinterpret_cast<float*>(uni);
   int* memb = reinterpret_cast<int*>(uni + static_cast<size_t>(a.max_cand) * 4);
+  int* sntab = memb + a.take_stride * 64;                                 // the row's native pages
   SfShared& sh = *reinterpret_cast<SfShared*>(base + a.off_sh);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t row = blockIdx.x;
@@ -548,38 +549,49 @@ __global__ void __launch_bounds__(kSfThreads, kPer <= 2 ? 2 : 1)
   const int ntiles = sh.ntiles, nnat = sh.ntiles_nat;
   const uint32_t q_bytes = static_cast<uint32_t>(a.N) * 128;
 
-  // producer: one tile's loads (tile t: native pages first, then selected ranks)
+  // producer warp: one tile's loads (tile t: native pages first, then selected
+  // ranks).  Lane 0 waits for the stage and arms the barriers; lanes 0-1 issue
+  // the two page boxes and lanes 2-3 the two scale vectors, in parallel.
   auto issue = [&](int t) -> bool {
     const int s = t % S, r = t % SS;
-    if (!mbar_wait(&sh.empty[s], ((t / S) & 1) ^ 1, &sh.abort, kSfWaitNs) ||
-        !mbar_wait(&sh.sempty[r], ((t / SS) & 1) ^ 1, &sh.abort, kSfWaitNs))
-      return false;
-    int pg[2];
-    bool nat = t < nnat;
-    if (nat) {
-      for (int h = 0; h < 2; ++h) {
+    bool ok = true;
+    if (lane == 0)
+      ok = mbar_wait(&sh.empty[s], ((t / S) & 1) ^ 1, &sh.abort, kSfWaitNs) &&
+           mbar_wait(&sh.sempty[r], ((t / SS) & 1) ^ 1, &sh.abort, kSfWaitNs);
+    if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) return false;
+    const bool nat = t < nnat;
+    int pg = -1;                              // lanes 0-1 and 2-3: page of half lane & 1
+    if (lane < 4) {
+      const int h = lane & 1;
+      if (nat) {
         const int lp = sh.natp[2 * t + h];
-        pg[h] = (lp >= 0 && lp < a.pages) ? a.nt[row * a.pages + lp] : -1;
+        pg = (lp >= 0 && lp < a.pages) ? a.nt[row * a.pages + lp] : -1;
+      } else {
+        const int k = t - nnat;
+        pg = 2 * k + h < sh.take ? spage[2 * k + h] : -1;
       }
-    } else {
-      const int k = t - nnat;
-      for (int h = 0; h < 2; ++h) pg[h] = 2 * k + h < sh.take ? spage[2 * k + h] : -1;
     }
-    const int halves = (pg[0] >= 0 ? 1 : 0) + (pg[1] >= 0 ? 1 : 0);
-    mbar_arrive_expect_tx(&sh.full[s], 8192u * halves);
-    mbar_arrive_expect_tx(&sh.sfull[r], 256u * halves);
-    for (int h = 0; h < 2; ++h) {
-      if (pg[h] < 0) continue;
-      tma_load_3d(stages + s * 16384 + h * 8192, nat ? &nat_map : &fine_map, &sh.full[s], 0, 0, pg[h]);
-      tma_load_2d(sring + r * 128 + h * 64, nat ? &nat_scales : &fine_scales, &sh.sfull[r], 0, pg[h]);
+    const unsigned have = __ballot_sync(0xffffffffu, lane < 2 && pg >= 0);
+    if (lane == 0) {
+      const uint32_t halves = __popc(have);
+      mbar_arrive_expect_tx(&sh.full[s], 8192u * halves);
+      mbar_arrive_expect_tx(&sh.sfull[r], 256u * halves);
+    }
+    __syncwarp();
+    if (lane < 4 && pg >= 0) {
+      const int h = lane & 1;
+      if (lane < 2) tma_load_3d(stages + s * 16384 + h * 8192, nat ? &nat_map : &fine_map, &sh.full[s], 0, 0, pg);
+      else tma_load_2d(sring + r * 128 + h * 64, nat ? &nat_scales : &fine_scales, &sh.sfull[r], 0, pg);
     }
     return true;
   };
 
   int issued = 0;
-  if (warp == kProdWarp && lane == 0) {
-    mbar_arrive_expect_tx(&sh.qfull, q_bytes);
-    tma_load_2d(qsm, &q_map, &sh.qfull, 0, static_cast<int>(row) * a.H);
+  if (warp == kProdWarp) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&sh.qfull, q_bytes);
+      tma_load_2d(qsm, &q_map, &sh.qfull, 0, static_cast<int>(row) * a.H);
+    }
     // the sink / tail tiles do not depend on the route: their loads fly while it runs
     const int pre = min(nnat, min(S, SS));
     for (; issued < pre; ++issued)
@@ -591,20 +603,18 @@ __global__ void __launch_bounds__(kSfThreads, kPer <= 2 ? 2 : 1)
   // (sf_route ends with a barrier: spage / sbnd are visible)
 
   if (warp == kProdWarp) {
-    if (lane == 0) {
-      int t = issued;
-      for (; t < ntiles; ++t) {
-        if (*reinterpret_cast<volatile int*>(&sh.abort)) break;
-        if (!issue(t)) {
-          sf_abort(sh, a.status);
-          break;
-        }
+    int t = issued;
+    for (; t < ntiles; ++t) {
+      if (__shfl_sync(0xffffffffu, *reinterpret_cast<volatile int*>(&sh.abort), 0)) break;
+      if (!issue(t)) {
+        if (lane == 0) sf_abort(sh, a.status);
+        break;
       }
-      if (*reinterpret_cast<volatile int*>(&sh.abort)) {  // let recent loads land before exit
-        for (int k = 0, it = t - 1; k < S && it >= 0; ++k, --it) {
-          mbar_wait(&sh.full[it % S], (it / S) & 1, &sh.zero, kSfWaitNs);
-          mbar_wait(&sh.sfull[it % SS], (it / SS) & 1, &sh.zero, kSfWaitNs);
-        }
+    }
+    if (lane == 0 && *reinterpret_cast<volatile int*>(&sh.abort)) {  // let recent loads land before exit
+      for (int k = 0, it = t - 1; k < S && it >= 0; ++k, --it) {
+        mbar_wait(&sh.full[it % S], (it / S) & 1, &sh.zero, kSfWaitNs);
+        mbar_wait(&sh.sfull[it % SS], (it / SS) & 1, &sh.zero, kSfWaitNs);
       }
     }
   } else if (warp == kMmaWarp) {
@@ -715,6 +725,10 @@ __global__ void __launch_bounds__(kSfThreads, kPer <= 2 ? 2 : 1)
         if (gout) gout[col] = score;
       }
     }
+  } else {
+    // warps 6-7: the row's native page table, for the output mapping
+    const int np = min(a.pages, (sh.n + 63) / 64);
+    for (int v = tid - 32 * (kEpiWarp0 + 4); v < np; v += 64) sntab[v] = a.nt[row * a.pages + v];
   }
   __syncthreads();
   if (!*reinterpret_cast<volatile int*>(&sh.abort)) {
@@ -723,7 +737,6 @@ __global__ void __launch_bounds__(kSfThreads, kPer <= 2 ? 2 : 1)
     uint32_t* keys = reinterpret_cast<uint32_t*>(sc);
     for (int j = tid; j < Lr; j += kSfThreads) keys[j] = order_key(sc[j]);
     __syncthreads();
-    const int32_t* ntrow = a.nt + row * a.pages;
     auto emit = [&](int pos, int rawi) {
       int lg = -1;
       if (rawi >= 0 && rawi < Lr && keys[rawi] != kNegInfKey) {
@@ -738,7 +751,7 @@ __global__ void __launch_bounds__(kSfThreads, kPer <= 2 ? 2 : 1)
       const int64_t dst = row * a.topk + pos;
       a.logical[dst] = lg;
       int ph = -1;
-      if (lg >= 0 && (lg >> 6) < a.pages) ph = ntrow[lg >> 6] * 64 + (lg & 63);
+      if (lg >= 0 && (lg >> 6) < a.pages) ph = sntab[lg >> 6] * 64 + (lg & 63);
       a.physical[dst] = ph;
       a.raw[dst] = rawi;
       if (a.expansion_stride) {
@@ -879,7 +892,7 @@ extern "C" int v1x_select_fused(const uint8_t* q, const float* w, int64_t heads,
   off = align(off + static_cast<int64_t>(sizeof(SfShared)), 16);
   const int off_u = static_cast<int>(off);
   const int64_t route_bytes = 16384 + static_cast<int64_t>(n_items) * 8;
-  const int64_t row_bytes = static_cast<int64_t>(max_cand) * 4 + take_stride * 64 * 4;
+  const int64_t row_bytes = static_cast<int64_t>(max_cand) * 4 + take_stride * 64 * 4 + pages * 4;
   off += std::max(route_bytes, row_bytes);
   const int64_t topk_scratch = 32768 + (max_cand + 1023) / 1024 * 128 +
                                ((max_cand + kSfThreads - 1) / kSfThreads) * kSfWarps * 8 + 1024 + kSfMaxBin2 * 8;
