@@ -63,6 +63,7 @@ class _Query:
                                       expand=c.expand_output)
         self.graph = None
         self.graphs = c.graphs
+        self.filled = 0        # rows [filled, rows) of the staged inputs are known to be zero
         # arena rows of the staged requests, for one gather of their page tables
         self.row_ids = torch.zeros(rows, dtype=torch.int64, device=d)
         self.staging = HostStaging(rows, d, dtype=torch.int64)
@@ -92,9 +93,10 @@ class _Query:
         c.native_table[:n, : native_tables.shape[1]].copy_(native_tables)
         if native_tables.shape[1] < c.native_table.shape[1]:
             c.native_table[:n, native_tables.shape[1]:].zero_()
-        if n < self.rows:
+        if n < self.filled:    # rows past n written by an earlier, longer call: zero them again
             for t in (c.q8.view(torch.uint8), c.w, c.lens, c.native_table, c.reordered_table, c.center_table):
-                t[n:].zero_()
+                t[n:self.filled].zero_()
+        self.filled = n
         # every row's reordered and centre page tables: rows of the arena's request
         # tables, gathered in one launch each
         a = self.owner.arena
@@ -194,7 +196,7 @@ class Indexer:
         ):
             raise ValueError("Unsupported V1 FP8/page64 query inputs")
         cpu = [int(x) for x in lengths_cpu]
-        if any(x < 0 or x > c.max_context or (x + 63) // 64 > native_tables.shape[1] for x in cpu):
+        if cpu and (min(cpu) < 0 or max(cpu) > min(c.max_context, native_tables.shape[1] * 64)):
             raise ValueError("Query lengths exceed page-table/context capacity")
         with self.lock:
             self._begin()
@@ -204,16 +206,17 @@ class Indexer:
                 return (empty, torch.empty((0, c.topk), device=self.device, dtype=torch.int32)) \
                     if return_logical else empty
             # build each request to its largest visible length before querying
-            max_rows = {}
-            for i, key in enumerate(owners):
-                if key not in max_rows or cpu[i] > cpu[max_rows[key]]:
-                    max_rows[key] = i
-            for key, i in max_rows.items():
-                st = self.states.get(key)
-                if st is not None and cpu[i] >= st.length and cpu[i] // 1024 == len(st.leases):
-                    st.length = cpu[i]        # no newly complete bucket: nothing to index
+            longest = {}              # owner -> (length, row) of its longest row (ties: first row)
+            for i, (key, x) in enumerate(zip(owners, cpu)):
+                if x > longest.get(key, (-1, 0))[0]:
+                    longest[key] = (x, i)
+            states = self.states
+            for key, (x, i) in longest.items():
+                st = states.get(key)
+                if st is not None and x >= st.length and x // 1024 == len(st.leases):
+                    st.length = x             # no newly complete bucket: nothing to index
                     continue
-                self._prepare(key, native_tables[i], cpu[i])
+                self._prepare(key, native_tables[i], x)
             if self.arena.pending_check:      # new buckets: read the status word (a sync)
                 self.arena.check()
             outputs = []
