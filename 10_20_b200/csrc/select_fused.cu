@@ -50,11 +50,11 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kSfThreads = 256;
-constexpr int kSfWarps = kSfThreads / 32;
+constexpr int kSfMaxThreads = 512;
+constexpr int kSfMaxWarps = kSfMaxThreads / 32;
 constexpr int kProdWarp = 0;
 constexpr int kMmaWarp = 1;
-constexpr int kEpiWarp0 = 2;               // warps 2-5
+constexpr int kEpiWarp0 = 2;               // warps 2-5 (and 6-9: the second group of 512-thread CTAs)
 constexpr int kSfAcc = 4;                  // TMEM accumulators in flight
 constexpr int kMaxStages = 8;
 constexpr int kMaxScaleSlots = 16;
@@ -92,7 +92,7 @@ struct SfArgs {
   uint32_t tmem_cols;
   int32_t* status;
   // dynamic shared-memory offsets (bytes from the 1024-aligned base)
-  int off_q, off_sring, off_w, off_sel, off_sh, off_u;
+  int off_q, off_sring, off_w, off_sel, off_sh, off_tab, off_u;
 };
 
 struct SfShared {
@@ -106,8 +106,10 @@ struct SfShared {
   int n, take, sink, tail, L, tail_row, ntiles_nat, ntiles;
   int natp[kMaxNativePages];   // logical page numbers of the sink / tail pages
   // route / Top-T scratch
-  int4 red[2 * kSfWarps];
-  int warp_tot[kSfWarps + 1];
+  int4 red[2 * kSfMaxWarps];
+  int warp_tot[kSfMaxWarps + 1];
+  int2 wcnt[kSfMaxWarps];      // per warp: threshold-bin candidates, then their offsets
+  uint32_t wmin[kSfMaxWarps], wmax[kSfMaxWarps];
   int4 res, res2;
   int2 carry;
   int count, ncand, ncand2;
@@ -131,13 +133,13 @@ __device__ __forceinline__ void sf_abort(SfShared& sh, int32_t* status) {
 // blocked rank asc).  Writes selected[0:take_stride], the fine table, and the
 // row's selected pages / boundary flags into shared memory.
 // ---------------------------------------------------------------------------
-template <int kPer>
+template <int kThreads, int kPer>
 __device__ void sf_route(const SfArgs& a, SfShared& sh, int64_t row, int* hist, unsigned long long* list,
-                         int* spage, uint8_t* sbnd) {
-  const int tid = threadIdx.x, nt = kSfThreads;
+                         int* spage, uint8_t* sbnd, const float* spsc, const int* rtrow) {
+  constexpr int kWarps = kThreads / 32;
+  const int tid = threadIdx.x, nt = kThreads;
   const int n = sh.n, take = sh.take;
   const int active = max(n - 1, 0) / 1024 * 16;
-  const int32_t* rtrow = a.rt + row * a.pages;
   int32_t* ftrow = a.fine_table + row * a.fine_cols;
   const int64_t base_ft = a.capacity + static_cast<int64_t>(sh.tail_row) * 68;
   for (int64_t j = take + tid; j < a.fine_cols; j += nt)
@@ -160,26 +162,25 @@ __device__ void sf_route(const SfArgs& a, SfShared& sh, int64_t row, int* hist, 
     return;
   }
   if (tid == 0) sh.count = 0;
-  const int act = static_cast<int>(min(static_cast<int64_t>(active), a.page_stride));
-  const float* srow = a.page_scores + row * a.page_stride;
+  const int act = min(active, a.pages);
   uint32_t kr[kPer];
   const int nv = a.n_items > tid ? (a.n_items - tid + nt - 1) / nt : 0;
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {
     const int p = tid + j * nt;
-    kr[j] = order_key(p < act ? srow[p] : -CUDART_INF_F);
+    kr[j] = order_key(p < act ? spsc[p] : -CUDART_INF_F);
   }
-  zero_hist<kSfThreads>(hist);
+  zero_hist<kThreads>(hist);
   __syncthreads();
 #pragma unroll
   for (int j = 0; j < kPer; ++j)
     if (j < nv) atomicAdd(&hist[bin_of(kr[j])], 1);
   __syncthreads();
-  const TopBin tb = find_top_bin<kSfThreads>(want, hist, sh.warp_tot, &sh.res);
+  const TopBin tb = find_top_bin<kThreads>(want, hist, sh.warp_tot, &sh.res);
   uint32_t lo = static_cast<uint32_t>(tb.bin) << (32 - kBinBits);
   if (tb.above + tb.in > kRankDirectSf) {
     int gt = 0;
-    lo = block_kth_largest<kSfWarps>(
+    lo = block_kth_largest<kWarps>(
         want,
         [&](uint32_t c1, uint32_t c2, uint32_t c3, int& n1, int& n2, int& n3) {
           n1 = n2 = n3 = 0;
@@ -232,9 +233,10 @@ __device__ void sf_route(const SfArgs& a, SfShared& sh, int64_t row, int* hist, 
 // slot in ascending raw order.  scratch: >= 16 KB histogram + 16 KB candidate
 // list + bit flags + per-(slice, warp) counts (the stage ring, free by now).
 // ---------------------------------------------------------------------------
-template <class Emit>
+template <int kThreads, class Emit>
 __device__ void sf_topk(SfShared& sh, const uint32_t* keys, int L, int T, uint8_t* scratch, Emit emit) {
-  const int tid = threadIdx.x, nt = kSfThreads, lane = tid & 31, warp = tid >> 5;
+  constexpr int kWarps = kThreads / 32;
+  const int tid = threadIdx.x, nt = kThreads, lane = tid & 31, warp = tid >> 5;
   if (L <= T) {
     for (int t = tid; t < T; t += nt) emit(t, t < L ? t : -1);
     return;
@@ -244,40 +246,70 @@ __device__ void sf_topk(SfShared& sh, const uint32_t* keys, int L, int T, uint8_
   uint32_t* selbit = reinterpret_cast<uint32_t*>(scratch + 32768);              // L/32 words
   const int nsl = (L + nt - 1) / nt;
   int2* cnt = reinterpret_cast<int2*>(scratch + 32768 + ((L + 1023) / 1024) * 128);  // nsl * warps
-  int* hist2 = reinterpret_cast<int*>(cnt + nsl * kSfWarps);                    // 256
+  int* hist2 = reinterpret_cast<int*>(cnt + nsl * kWarps);                      // 256
   int2* cand2 = reinterpret_cast<int2*>(hist2 + 256);                           // kSfMaxBin2
-  zero_hist<kSfThreads>(hist);
+  zero_hist<kThreads>(hist);
   for (int wd = tid; wd < (L + 31) / 32; wd += nt) selbit[wd] = 0u;
-  hist2[tid] = 0;  // 256 threads, 256 sub-bins
+  if (tid < 256) hist2[tid] = 0;
   if (tid == 0) {
-    sh.ncand = 0;
     sh.ncand2 = 0;
-    sh.kmin = sh.kmin2 = 0xFFFFFFFFu;
-    sh.kmax = sh.kmax2 = 0u;
+    sh.kmin2 = 0xFFFFFFFFu;
+    sh.kmax2 = 0u;
   }
   __syncthreads();
   for (int i = tid; i < L; i += nt) atomicAdd(&hist[bin_of(keys[i])], 1);
   __syncthreads();
-  const TopBin tb = find_top_bin<kSfThreads>(T, hist, sh.warp_tot, &sh.res);
+  const TopBin tb = find_top_bin<kThreads>(T, hist, sh.warp_tot, &sh.res);
   const bool keep = tb.in <= kSfMaxBin;
   {
+    // the threshold bin's keys: per-warp counts and key range (no shared
+    // atomics), a scan of the warps' counts, then each warp writes its own
+    // candidates in index order
     const uint32_t ltm = lanemask_lt();
+    int wc = 0;
+    uint32_t lo = 0xFFFFFFFFu, hi = 0u;
     for (int j = 0; j < nsl; ++j) {
       const int i = j * nt + tid;
       const uint32_t k = i < L ? keys[i] : 0u;
       const bool mm = i < L && bin_of(k) == tb.bin;
-      const unsigned bal = __ballot_sync(0xffffffffu, mm);
-      if (bal == 0u) continue;
-      const uint32_t lo = __reduce_min_sync(0xffffffffu, mm ? k : 0xFFFFFFFFu);
-      const uint32_t hi = __reduce_max_sync(0xffffffffu, mm ? k : 0u);
-      int b0 = 0;
-      if (lane == 0) {
-        atomicMin(&sh.kmin, lo);
-        atomicMax(&sh.kmax, hi);
-        if (keep) b0 = atomicAdd(&sh.ncand, __popc(bal));
+      wc += __popc(__ballot_sync(0xffffffffu, mm));
+      if (mm) {
+        lo = min(lo, k);
+        hi = max(hi, k);
       }
-      b0 = __shfl_sync(0xffffffffu, b0, 0);
-      if (keep && mm) cand[b0 + __popc(bal & ltm)] = make_int2(static_cast<int>(k), i);
+    }
+    lo = __reduce_min_sync(0xffffffffu, lo);
+    hi = __reduce_max_sync(0xffffffffu, hi);
+    if (lane == 0) {
+      sh.wcnt[warp] = make_int2(wc, 0);
+      sh.wmin[warp] = lo;
+      sh.wmax[warp] = hi;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      int run = 0;
+      uint32_t mn = 0xFFFFFFFFu, mx = 0u;
+      for (int w = 0; w < kWarps; ++w) {
+        const int c = sh.wcnt[w].x;
+        sh.wcnt[w].y = run;
+        run += c;
+        mn = min(mn, sh.wmin[w]);
+        mx = max(mx, sh.wmax[w]);
+      }
+      sh.kmin = mn;
+      sh.kmax = mx;
+    }
+    __syncthreads();
+    if (keep) {
+      int b0 = sh.wcnt[warp].y;
+      for (int j = 0; j < nsl; ++j) {
+        const int i = j * nt + tid;
+        const uint32_t k = i < L ? keys[i] : 0u;
+        const bool mm = i < L && bin_of(k) == tb.bin;
+        const unsigned bal = __ballot_sync(0xffffffffu, mm);
+        if (mm) cand[b0 + __popc(bal & ltm)] = make_int2(static_cast<int>(k), i);
+        b0 += __popc(bal);
+      }
     }
   }
   __syncthreads();
@@ -369,7 +401,7 @@ __device__ void sf_topk(SfShared& sh, const uint32_t* keys, int L, int T, uint8_
   int need = tie_need;
   if (!by_bin && !have_tie) {
     int gt = 0;
-    thr = block_kth_largest<kSfWarps>(
+    thr = block_kth_largest<kWarps>(
         T,
         [&](uint32_t c1, uint32_t c2, uint32_t c3, int& n1, int& n2, int& n3) {
           n1 = n2 = n3 = 0;
@@ -398,11 +430,11 @@ __device__ void sf_topk(SfShared& sh, const uint32_t* keys, int L, int T, uint8_
     const int kl = klass(i, i < L ? keys[i] : 0u);
     const unsigned gb = __ballot_sync(0xffffffffu, kl == 1);
     const unsigned eb = __ballot_sync(0xffffffffu, kl == 2);
-    if (lane == 0) cnt[j * kSfWarps + warp] = make_int2(__popc(gb), __popc(eb));
+    if (lane == 0) cnt[j * kWarps + warp] = make_int2(__popc(gb), __popc(eb));
   }
   __syncthreads();
   if (warp == 0) {
-    const int E = nsl * kSfWarps;
+    const int E = nsl * kWarps;
     const int ch = (E + 31) / 32;
     const int beg = min(lane * ch, E), end = min(beg + ch, E);
     int sg = 0, se = 0;
@@ -426,7 +458,7 @@ __device__ void sf_topk(SfShared& sh, const uint32_t* keys, int L, int T, uint8_
     const int kl = klass(i, i < L ? keys[i] : 0u);
     const unsigned gb = __ballot_sync(0xffffffffu, kl == 1);
     const unsigned eb = __ballot_sync(0xffffffffu, kl == 2);
-    const int2 b0 = cnt[j * kSfWarps + warp];
+    const int2 b0 = cnt[j * kWarps + warp];
     const int gt_lt = b0.x + __popc(gb & lt);
     const int eq_lt = b0.y + __popc(eb & lt);
     if (kl == 1 || (kl == 2 && eq_lt < need)) emit(gt_lt + min(eq_lt, need), i);
@@ -436,13 +468,18 @@ __device__ void sf_topk(SfShared& sh, const uint32_t* keys, int L, int T, uint8_
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-// kPer: route keys per thread (2 for page tables of up to 512 padded slots,
-// whose CTAs also fit two per SM -- one head, many rows; 16 otherwise).
-template <int kPer>
-__global__ void __launch_bounds__(kSfThreads, kPer <= 2 ? 2 : 1)
+// kThreads 512: rows fewer than the SMs (one CTA per SM, the row's latency is
+// the step's): two epilogue groups of four warps take alternate tiles, and 16
+// warps share the route and the Top-T.  kThreads 256: many more rows than SMs
+// (one head, 1024 rows): one epilogue group, two CTAs per SM.
+// kPer: route keys per thread (n_items / kThreads rounded up).
+template <int kThreads, int kPer>
+__global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 1 : 2)
     select_fused_kernel(const __grid_constant__ CUtensorMap fine_map, const __grid_constant__ CUtensorMap fine_scales,
                         const __grid_constant__ CUtensorMap nat_map, const __grid_constant__ CUtensorMap nat_scales,
                         const __grid_constant__ CUtensorMap q_map, const __grid_constant__ SfArgs a) {
+  constexpr int kGroups = kThreads >= 512 ? 2 : 1;       // epilogue groups
+  constexpr int kHelper0 = kEpiWarp0 + 4 * kGroups;      // first warp idle during scoring
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = base;                                                  // stages x 16 KB
@@ -451,6 +488,10 @@ __global__ void __launch_bounds__(kSfThreads, kPer <= 2 ? 2 : 1)
   float* wsm = reinterpret_cast<float*>(base + a.off_w);                   // H
   int* spage = reinterpret_cast<int*>(base + a.off_sel);                   // take_stride
   uint8_t* sbnd = reinterpret_cast<uint8_t*>(spage + a.take_stride);       // take_stride
+  // the row's tables, copied at the start: page maxima, reordered and native pages
+  float* spsc = reinterpret_cast<float*>(base + a.off_tab);
+  int* srt = reinterpret_cast<int*>(spsc + a.pages);
+  int* sntab = srt + a.pages;
   uint8_t* uni = base + a.off_u;
   // route view of the union: histogram + winner list
   int* rhist = reinterpret_cast<int*>(uni);
@@ -458,12 +499,33 @@ __global__ void __launch_bounds__(kSfThreads, kPer <= 2 ? 2 : 1)
   // row view of the union: scores (keys after the Top-T conversion) + members
   float* sc = reinterpret_cast<float*>(uni);
   int* memb = reinterpret_cast<int*>(uni + static_cast<size_t>(a.max_cand) * 4);
-  int* sntab = memb + a.take_stride * 64;                                 // the row's native pages
   SfShared& sh = *reinterpret_cast<SfShared*>(base + a.off_sh);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t row = blockIdx.x;
   const int S = a.stages, SS = a.scale_slots;
 
+  // ---- the row's tables: asynchronous copies, in flight during the set-up ---------
+  {
+    const float* ps = a.page_scores + row * a.page_stride;
+    const int32_t* rt = a.rt + row * a.pages;
+    const int32_t* ntr = a.nt + row * a.pages;
+    const bool v16 = ((reinterpret_cast<uintptr_t>(ps) | reinterpret_cast<uintptr_t>(rt) |
+                       reinterpret_cast<uintptr_t>(ntr)) & 15) == 0 && (a.pages & 3) == 0;
+    if (v16) {
+      for (int v = tid; v < a.pages / 4; v += kThreads) {
+        sf_cp_async16(spsc + 4 * v, ps + 4 * v);
+        sf_cp_async16(srt + 4 * v, rt + 4 * v);
+        sf_cp_async16(sntab + 4 * v, ntr + 4 * v);
+      }
+    } else {
+      for (int v = tid; v < a.pages; v += kThreads) {
+        spsc[v] = ps[v];
+        srt[v] = rt[v];
+        sntab[v] = ntr[v];
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
   // ---- set-up: barriers, TMEM, tensor-map prefetch -------------------------------
   if (tid == 0) {
     sh.abort = 0;
@@ -497,6 +559,7 @@ __global__ void __launch_bounds__(kSfThreads, kPer <= 2 ? 2 : 1)
   }
   // ---- metadata (DS/kernels.py:568-591; fixed budget or ratio take rule) ---------
   const int n = a.lens[row];
+  const int n0 = a.lens[0];
   const int built_pages = max(n - 1, 0) / 1024 * 16;
   int take;
   if (a.budget) {
@@ -509,17 +572,19 @@ __global__ void __launch_bounds__(kSfThreads, kPer <= 2 ? 2 : 1)
   const RowBounds rb = row_bounds(n, 64, a.window);
   const int L = take * 64 + rb.sink + n - rb.tail;
   // shared-tail owner: row 0 when this row has row 0's length and the same native
-  // pages at page 0 and pages tail/64 ... (up to 127 of them)
-  bool differs = false;
-  if (tid < 128) {
-    const int page = tid == 0 ? 0 : rb.tail / 64 + tid - 1;
-    const bool valid = n > 0 && (tid == 0 || page < (n + 63) / 64) && page < a.pages;
-    const int mine = valid ? a.nt[row * a.pages + page] : -1;
-    const int first = valid ? a.nt[page] : -1;
-    differs = mine != first;
-  }
-  const int any_differs = __syncthreads_or(differs);   // every thread takes part
-  const bool share = n == a.lens[0] && !any_differs;
+  // pages at page 0 and pages tail/64 ... (up to 127 of them); row 0's entries
+  // are read from global memory (every CTA reads the same ones), this row's from
+  // its staged table
+  int first = -1;
+  const int tpage = tid == 0 ? 0 : rb.tail / 64 + tid - 1;
+  const bool tvalid = tid < 128 && n > 0 && (tid == 0 || tpage < (n + 63) / 64) && tpage < a.pages;
+  if (tvalid && n == n0) first = a.nt[tpage];
+  if (tid < a.H) wsm[tid] = a.w[row * a.H + tid];
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncthreads();
+  const bool differs = tid < 128 && (tvalid ? sntab[tpage] : -1) != (tvalid ? first : -1);
+  const int any_differs = __syncthreads_or(differs && n == n0);   // every thread takes part
+  const bool share = n == n0 && !any_differs;
   if (tid == 0) {
     sh.n = n;
     sh.take = take;
@@ -542,7 +607,6 @@ __global__ void __launch_bounds__(kSfThreads, kPer <= 2 ? 2 : 1)
     sh.ntiles = sh.ntiles_nat + (take + 1) / 2;
     for (int p = np; p < 2 * sh.ntiles_nat; ++p) sh.natp[p] = -1;
   }
-  if (tid < a.H) wsm[tid] = a.w[row * a.H + tid];
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sh.tmem_base;
@@ -565,7 +629,7 @@ __global__ void __launch_bounds__(kSfThreads, kPer <= 2 ? 2 : 1)
       const int h = lane & 1;
       if (nat) {
         const int lp = sh.natp[2 * t + h];
-        pg = (lp >= 0 && lp < a.pages) ? a.nt[row * a.pages + lp] : -1;
+        pg = (lp >= 0 && lp < a.pages) ? sntab[lp] : -1;
       } else {
         const int k = t - nnat;
         pg = 2 * k + h < sh.take ? spage[2 * k + h] : -1;
@@ -599,7 +663,7 @@ __global__ void __launch_bounds__(kSfThreads, kPer <= 2 ? 2 : 1)
   }
 
   // ---- route (all threads) ----------------------------------------------------------
-  sf_route<kPer>(a, sh, row, rhist, rlist, spage, sbnd);
+  sf_route<kThreads, kPer>(a, sh, row, rhist, rlist, spage, sbnd, spsc, srt);
   // (sf_route ends with a barrier: spage / sbnd are visible)
 
   if (warp == kProdWarp) {
@@ -645,11 +709,13 @@ __global__ void __launch_bounds__(kSfThreads, kPer <= 2 ? 2 : 1)
       if (*reinterpret_cast<volatile int*>(&sh.abort) && t > 0)
         mbar_wait(&sh.tfull[(t - 1) % kSfAcc], ((t - 1) / kSfAcc) & 1, &sh.zero, kSfWaitNs);
     }
-  } else if (warp < kEpiWarp0 + 4) {
-    // ---- epilogue: members of the selected pages, then one key per thread --------------
-    const int e = tid - 32 * kEpiWarp0;      // 0..127
+  } else if (warp < kHelper0) {
+    // ---- epilogue: members of the selected pages, then one key per thread; group
+    // g takes tiles g, g + kGroups, ... ------------------------------------------------
+    const int e = tid - 32 * kEpiWarp0;      // 0 .. 128 * kGroups - 1
+    const int g = e >> 7;
     const int tk = sh.take, sink = sh.sink, tail = sh.tail;
-    for (int rr = e; rr < tk; rr += 128) {
+    for (int rr = e; rr < tk; rr += 128 * kGroups) {
       const int page = spage[rr];
       if (page >= 0 && page < a.member_rows) {
         const int32_t* src = a.members + static_cast<int64_t>(page) * 64;
@@ -661,12 +727,12 @@ __global__ void __launch_bounds__(kSfThreads, kPer <= 2 ? 2 : 1)
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
     asm volatile("cp.async.wait_all;" ::: "memory");
-    asm volatile("bar.sync 1, 128;" ::: "memory");
+    asm volatile("bar.sync 1, %0;" ::"r"(128 * kGroups) : "memory");
     const int q4 = warp & 3;
     const int i = q4 * 32 + lane;            // key of the tile == TMEM lane
     const int h = i >> 6, slot = i & 63;
     float* gout = a.scores_out ? a.scores_out + row * a.score_stride : nullptr;
-    for (int t = 0; t < ntiles; ++t) {
+    for (int t = g; t < ntiles; t += kGroups) {
       const int acc = t % kSfAcc, r = t % SS;
       if (!mbar_wait(&sh.sfull[r], (t / SS) & 1, &sh.abort, kSfWaitNs) ||
           !mbar_wait(&sh.tfull[acc], (t / kSfAcc) & 1, &sh.abort, kSfWaitNs)) {
@@ -725,17 +791,13 @@ __global__ void __launch_bounds__(kSfThreads, kPer <= 2 ? 2 : 1)
         if (gout) gout[col] = score;
       }
     }
-  } else {
-    // warps 6-7: the row's native page table, for the output mapping
-    const int np = min(a.pages, (sh.n + 63) / 64);
-    for (int v = tid - 32 * (kEpiWarp0 + 4); v < np; v += 64) sntab[v] = a.nt[row * a.pages + v];
   }
   __syncthreads();
   if (!*reinterpret_cast<volatile int*>(&sh.abort)) {
     // ---- Top-T + mapping (all threads) ------------------------------------------------
     const int Lr = sh.L, tk = sh.take, sink = sh.sink, tail = sh.tail, nn = sh.n;
     uint32_t* keys = reinterpret_cast<uint32_t*>(sc);
-    for (int j = tid; j < Lr; j += kSfThreads) keys[j] = order_key(sc[j]);
+    for (int j = tid; j < Lr; j += kThreads) keys[j] = order_key(sc[j]);
     __syncthreads();
     auto emit = [&](int pos, int rawi) {
       int lg = -1;
@@ -760,9 +822,9 @@ __global__ void __launch_bounds__(kSfThreads, kPer <= 2 ? 2 : 1)
             lg < 0 ? make_int4(-1, -1, -1, -1) : make_int4(b4, b4 + 1, b4 + 2, b4 + 3);
       }
     };
-    sf_topk(sh, keys, Lr, a.topk, stages, emit);
+    sf_topk<kThreads>(sh, keys, Lr, a.topk, stages, emit);
     if (a.expansion_stride)
-      for (int64_t j = static_cast<int64_t>(a.topk) * 4 + tid; j < a.expansion_stride; j += kSfThreads)
+      for (int64_t j = static_cast<int64_t>(a.topk) * 4 + tid; j < a.expansion_stride; j += kThreads)
         a.expanded[row * a.expansion_stride + j] = -1;
   }
   __syncthreads();
@@ -866,42 +928,56 @@ extern "C" int v1x_select_fused(const uint8_t* q, const float* w, int64_t heads,
       return rc;
   }
   // route geometry of the reference (v1_query.cuh:175-177)
-  int threads, items;
-  if (pages <= 128) { threads = 64; items = 2; }
-  else if (pages <= 256) { threads = 64; items = 4; }
-  else if (pages <= 512) { threads = 64; items = 8; }
-  else if (pages <= 1024) { threads = 128; items = 8; }
-  else if (pages <= 2048) { threads = 128; items = 16; }
-  else { threads = 128; items = 32; }
-  const int n_items = threads * items;
+  int r_threads, r_items;
+  if (pages <= 128) { r_threads = 64; r_items = 2; }
+  else if (pages <= 256) { r_threads = 64; r_items = 4; }
+  else if (pages <= 512) { r_threads = 64; r_items = 8; }
+  else if (pages <= 1024) { r_threads = 128; r_items = 8; }
+  else if (pages <= 2048) { r_threads = 128; r_items = 16; }
+  else { r_threads = 128; r_items = 32; }
+  const int n_items = r_threads * r_items;
   const int max_cand = static_cast<int>(take_stride * 64 + 64 + std::max<int64_t>(window, 1024));
-  // shared memory plan
-  const int stages = heads == 1 ? 4 : 8;
-  const int scale_slots = 2 * stages;
+  // 512 threads (one CTA per SM) when the rows fit one wave; 256 (two per SM)
+  // for batches of many more rows than SMs
+  const int threads = batch <= static_cast<int64_t>(num_sms()) ? 512 : 256;
+  const int warps = threads / 32;
+  // shared memory plan: everything but the stage ring, then as many 16 KB
+  // stages (4 to 8) as fit the CTA's share of the SM
   auto align = [](int64_t x, int64_t al) { return (x + al - 1) / al * al; };
-  int64_t off = static_cast<int64_t>(stages) * 16384;
-  const int off_q = static_cast<int>(off);
-  off = align(off + n_mma * 128, 1024);
-  const int off_sring = static_cast<int>(off);
-  off += static_cast<int64_t>(scale_slots) * 512;
-  const int off_w = static_cast<int>(off);
-  off = align(off + heads * 4, 16);
-  const int off_sel = static_cast<int>(off);
-  off = align(off + take_stride * 5, 16);
-  const int off_sh = static_cast<int>(off);
-  off = align(off + static_cast<int64_t>(sizeof(SfShared)), 16);
-  const int off_u = static_cast<int>(off);
   const int64_t route_bytes = 16384 + static_cast<int64_t>(n_items) * 8;
-  const int64_t row_bytes = static_cast<int64_t>(max_cand) * 4 + take_stride * 64 * 4 + pages * 4;
-  off += std::max(route_bytes, row_bytes);
+  const int64_t row_bytes = static_cast<int64_t>(max_cand) * 4 + take_stride * 64 * 4;
   const int64_t topk_scratch = 32768 + (max_cand + 1023) / 1024 * 128 +
-                               ((max_cand + kSfThreads - 1) / kSfThreads) * kSfWarps * 8 + 1024 + kSfMaxBin2 * 8;
-  V1X_CHECK_ARG(topk_scratch <= static_cast<int64_t>(stages) * 16384, "select_fused: top-k scratch exceeds stages");
-  const size_t smem = static_cast<size_t>(off) + 1024;
-  if (smem > 227 * 1024) {
-    set_error("select_fused: shared memory %zu too large", smem);
+                               ((max_cand + threads - 1) / threads) * warps * 8 + 1024 + kSfMaxBin2 * 8;
+  auto plan = [&](int stages, int64_t* offs) {   // offs: q, sring, w, sel, sh, tab, u; returns total bytes
+    int64_t off = static_cast<int64_t>(stages) * 16384;
+    offs[0] = off;
+    off = align(off + n_mma * 128, 1024);
+    offs[1] = off;
+    off += static_cast<int64_t>(2 * stages) * 512;
+    offs[2] = off;
+    off = align(off + heads * 4, 16);
+    offs[3] = off;
+    off = align(off + take_stride * 5, 16);
+    offs[4] = off;
+    off = align(off + static_cast<int64_t>(sizeof(SfShared)), 16);
+    offs[5] = off;
+    off = align(off + pages * 12, 16);
+    offs[6] = off;
+    off += std::max(route_bytes, row_bytes);
+    return off + 1024;
+  };
+  const int64_t budget_bytes = threads == 512 ? 227 * 1024 : 113 * 1024;
+  int stages = 8;
+  int64_t offs[7];
+  while (stages > 4 && (plan(stages, offs) > budget_bytes || (heads == 1 && stages > 4))) --stages;
+  const int64_t total = plan(stages, offs);
+  if (total > 227 * 1024 || topk_scratch > static_cast<int64_t>(stages) * 16384) {
+    set_error("select_fused: shared memory %lld too large (pages %lld, window %lld)", (long long)total,
+              (long long)pages, (long long)window);
     return V1X_ERR_UNSUPPORTED;
   }
+  const size_t smem = static_cast<size_t>(total);
+  const int scale_slots = 2 * stages;
   uint32_t cols = 32;
   while (cols < static_cast<uint32_t>(kSfAcc * n_mma)) cols <<= 1;
   SfArgs args{lens, budget, static_cast<int>(ratio_num), static_cast<int>(ratio_den), native_table,
@@ -910,17 +986,29 @@ extern "C" int v1x_select_fused(const uint8_t* q, const float* w, int64_t heads,
               static_cast<int>(window), static_cast<int>(take_stride), fine_cols, fine_lens, takes, dg_lens,
               center_lens, tail_rows, selected, fine_table, physical, logical, raw, expanded, expansion_stride,
               scores_out, score_stride, static_cast<int>(batch), stages, scale_slots, n_items, n_items / 128,
-              max_cand, cols, status, off_q, off_sring, off_w, off_sel, off_sh, off_u};
+              max_cand, cols, status, static_cast<int>(offs[0]), static_cast<int>(offs[1]),
+              static_cast<int>(offs[2]), static_cast<int>(offs[3]), static_cast<int>(offs[4]),
+              static_cast<int>(offs[5]), static_cast<int>(offs[6])};
   static DeviceOnce once;
   once.run([] {
-    cudaFuncSetAttribute(select_fused_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    cudaFuncSetAttribute(select_fused_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(select_fused_kernel<512, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(select_fused_kernel<512, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(select_fused_kernel<256, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(select_fused_kernel<256, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   });
-  const dim3 grid(static_cast<unsigned>(batch)), block(kSfThreads);
+  const dim3 grid(static_cast<unsigned>(batch)), block(threads);
   cudaStream_t s = as_stream(stream);
-  if (n_items <= 2 * kSfThreads)
-    launch_kernel(select_fused_kernel<2>, grid, block, smem, s, fine_map, fine_sc, nat_map, nat_sc, q_map, args);
-  else
-    launch_kernel(select_fused_kernel<16>, grid, block, smem, s, fine_map, fine_sc, nat_map, nat_sc, q_map, args);
+  if (threads == 512) {
+    if (n_items <= 2 * 512)
+      launch_kernel(select_fused_kernel<512, 2>, grid, block, smem, s, fine_map, fine_sc, nat_map, nat_sc, q_map, args);
+    else
+      launch_kernel(select_fused_kernel<512, 8>, grid, block, smem, s, fine_map, fine_sc, nat_map, nat_sc, q_map, args);
+  } else {
+    if (n_items <= 2 * 256)
+      launch_kernel(select_fused_kernel<256, 2>, grid, block, smem, s, fine_map, fine_sc, nat_map, nat_sc, q_map, args);
+    else
+      launch_kernel(select_fused_kernel<256, 16>, grid, block, smem, s, fine_map, fine_sc, nat_map, nat_sc, q_map,
+                    args);
+  }
   return launch_status("v1x_select_fused");
 }
