@@ -54,7 +54,7 @@ constexpr int kSfMaxThreads = 512;
 constexpr int kSfMaxWarps = kSfMaxThreads / 32;
 constexpr int kProdWarp = 0;
 constexpr int kMmaWarp = 1;
-constexpr int kEpiWarp0 = 2;               // warps 2-5 (and 6-9: the second group of 512-thread CTAs)
+constexpr int kEpiWarp0 = 2;               // warps 2-5 (and 6-9: a second group with 512 threads)
 constexpr int kSfAcc = 4;                  // TMEM accumulators in flight
 constexpr int kMaxStages = 8;
 constexpr int kMaxScaleSlots = 16;
@@ -468,11 +468,10 @@ __device__ void sf_topk(SfShared& sh, const uint32_t* keys, int L, int T, uint8_
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-// kThreads 512: rows fewer than the SMs (one CTA per SM, the row's latency is
-// the step's): two epilogue groups of four warps take alternate tiles, and 16
-// warps share the route and the Top-T.  kThreads 256: many more rows than SMs
-// (one head, 1024 rows): one epilogue group, two CTAs per SM.
-// kPer: route keys per thread (n_items / kThreads rounded up).
+// kThreads: 256 as launched (one epilogue group; warps 6-7 join warp 0 as
+// producers after the route); the code also serves 512 (two epilogue groups on
+// alternate tiles, warps 10-15 producers).  kPer: route keys per thread
+// (n_items / kThreads rounded up).
 template <int kThreads, int kPer>
 __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 1 : 2)
     select_fused_kernel(const __grid_constant__ CUtensorMap fine_map, const __grid_constant__ CUtensorMap fine_scales,
@@ -658,27 +657,48 @@ __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 1 : 2)
     }
     // the sink / tail tiles do not depend on the route: their loads fly while it runs
     const int pre = min(nnat, min(S, SS));
-    for (; issued < pre; ++issued)
-      if (!issue(issued)) break;
+    for (; issued < pre; ++issued) {
+      if (!issue(issued)) {
+        if (lane == 0) sf_abort(sh, a.status);
+        break;
+      }
+    }
   }
 
   // ---- route (all threads) ----------------------------------------------------------
   sf_route<kThreads, kPer>(a, sh, row, rhist, rlist, spage, sbnd, spsc, srt);
   // (sf_route ends with a barrier: spage / sbnd are visible)
 
-  if (warp == kProdWarp) {
-    int t = issued;
-    for (; t < ntiles; ++t) {
-      if (__shfl_sync(0xffffffffu, *reinterpret_cast<volatile int*>(&sh.abort), 0)) break;
-      if (!issue(t)) {
-        if (lane == 0) sf_abort(sh, a.status);
-        break;
+  if (warp == kProdWarp || warp >= kHelper0) {
+    // producers after the route: warp 0 and the warps idle during scoring
+    // (one warp issues about one tile per microsecond; the issue rate sets the
+    // scoring time).  Every stage is fed by one producer, in tile order: a
+    // stage's next tile is issued only by the warp that issued its previous
+    // one, so the parity waits on its barriers can never see a phase two
+    // behind (tiles before the route were issued by warp 0 before it).
+    const int pidx = warp == kProdWarp ? 0 : 1 + warp - kHelper0;
+    const int nprod = min(1 + kThreads / 32 - kHelper0, S);
+    const int pre = min(nnat, min(S, SS));
+    const auto mine = [&](int t) { return t < pre ? pidx == 0 : (t % S) % nprod == pidx; };
+    int last = -1;
+    if (pidx < nprod) {
+      for (int t = pre; t < ntiles; ++t) {
+        if (!mine(t)) continue;
+        if (__shfl_sync(0xffffffffu, *reinterpret_cast<volatile int*>(&sh.abort), 0)) break;
+        if (!issue(t)) {
+          if (lane == 0) sf_abort(sh, a.status);
+          break;
+        }
+        last = t;
       }
     }
-    if (lane == 0 && *reinterpret_cast<volatile int*>(&sh.abort)) {  // let recent loads land before exit
-      for (int k = 0, it = t - 1; k < S && it >= 0; ++k, --it) {
+    if (warp == kProdWarp && issued > 0 && last < 0) last = issued - 1;
+    if (lane == 0 && *reinterpret_cast<volatile int*>(&sh.abort)) {  // let this warp's recent loads land
+      for (int k = 0, it = last; k < S && it >= 0; --it) {
+        if (!mine(it) || (it < pre && it >= issued)) continue;
         mbar_wait(&sh.full[it % S], (it / S) & 1, &sh.zero, kSfWaitNs);
         mbar_wait(&sh.sfull[it % SS], (it / SS) & 1, &sh.zero, kSfWaitNs);
+        ++k;
       }
     }
   } else if (warp == kMmaWarp) {
@@ -937,9 +957,12 @@ extern "C" int v1x_select_fused(const uint8_t* q, const float* w, int64_t heads,
   else { r_threads = 128; r_items = 32; }
   const int n_items = r_threads * r_items;
   const int max_cand = static_cast<int>(take_stride * 64 + 64 + std::max<int64_t>(window, 1024));
-  // 512 threads (one CTA per SM) when the rows fit one wave; 256 (two per SM)
-  // for batches of many more rows than SMs
-  const int threads = batch <= static_cast<int64_t>(num_sms()) ? 512 : 256;
+  // 256 threads: three producer warps after the route keep the scoring fed,
+  // and a CTA leaves room on its SM for an independent batch's gather CTAs
+  // (512-thread CTAs took the whole register file for 3 us less latency per
+  // row, and cut the throughput of batches in flight from 922K to 735K
+  // queries/s)
+  const int threads = 256;
   const int warps = threads / 32;
   // shared memory plan: everything but the stage ring, then as many 16 KB
   // stages (4 to 8) as fit the CTA's share of the SM
@@ -966,7 +989,8 @@ extern "C" int v1x_select_fused(const uint8_t* q, const float* w, int64_t heads,
     off += std::max(route_bytes, row_bytes);
     return off + 1024;
   };
-  const int64_t budget_bytes = threads == 512 ? 227 * 1024 : 113 * 1024;
+  // two CTAs per SM when they fit (one head, many rows), else one
+  const int64_t budget_bytes = heads == 1 ? 113 * 1024 : 227 * 1024;
   int stages = 8;
   int64_t offs[7];
   while (stages > 4 && (plan(stages, offs) > budget_bytes || (heads == 1 && stages > 4))) --stages;
@@ -991,24 +1015,14 @@ extern "C" int v1x_select_fused(const uint8_t* q, const float* w, int64_t heads,
               static_cast<int>(offs[5]), static_cast<int>(offs[6])};
   static DeviceOnce once;
   once.run([] {
-    cudaFuncSetAttribute(select_fused_kernel<512, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    cudaFuncSetAttribute(select_fused_kernel<512, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     cudaFuncSetAttribute(select_fused_kernel<256, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     cudaFuncSetAttribute(select_fused_kernel<256, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   });
   const dim3 grid(static_cast<unsigned>(batch)), block(threads);
   cudaStream_t s = as_stream(stream);
-  if (threads == 512) {
-    if (n_items <= 2 * 512)
-      launch_kernel(select_fused_kernel<512, 2>, grid, block, smem, s, fine_map, fine_sc, nat_map, nat_sc, q_map, args);
-    else
-      launch_kernel(select_fused_kernel<512, 8>, grid, block, smem, s, fine_map, fine_sc, nat_map, nat_sc, q_map, args);
-  } else {
-    if (n_items <= 2 * 256)
-      launch_kernel(select_fused_kernel<256, 2>, grid, block, smem, s, fine_map, fine_sc, nat_map, nat_sc, q_map, args);
-    else
-      launch_kernel(select_fused_kernel<256, 16>, grid, block, smem, s, fine_map, fine_sc, nat_map, nat_sc, q_map,
-                    args);
-  }
+  if (n_items <= 2 * 256)
+    launch_kernel(select_fused_kernel<256, 2>, grid, block, smem, s, fine_map, fine_sc, nat_map, nat_sc, q_map, args);
+  else
+    launch_kernel(select_fused_kernel<256, 16>, grid, block, smem, s, fine_map, fine_sc, nat_map, nat_sc, q_map, args);
   return launch_status("v1x_select_fused");
 }
