@@ -230,25 +230,28 @@ __device__ void sf_route(const SfArgs& a, SfShared& sh, int64_t row, int* hist, 
 // ---------------------------------------------------------------------------
 // Top-T of the row's keys in shared memory (order-preserving uint32 keys,
 // kNegInfKey for -inf), (key desc, index asc); emit(pos, raw) for every output
-// slot in ascending raw order.  scratch: >= 16 KB histogram + 16 KB candidate
-// list + bit flags + per-(slice, warp) counts (the stage ring, free by now).
+// slot in ascending raw order.  hist: the keys' 12-bit histogram, already
+// counted (the scoring epilogue adds each key as it writes it).  Every pass
+// over the keys is blocked -- thread t owns the contiguous keys [t*per,
+// (t+1)*per) -- so one block scan of per-thread counts places a thread's
+// candidates and outputs in index order.  scratch: 16 KB candidate list + bit
+// flags + 1 KB + the sub-bin list (the stage ring, free by now).
 // ---------------------------------------------------------------------------
 template <int kThreads, class Emit>
-__device__ void sf_topk(SfShared& sh, const uint32_t* keys, int L, int T, uint8_t* scratch, Emit emit) {
+__device__ void sf_topk(SfShared& sh, const uint32_t* keys, const int* hist, int L, int T, uint8_t* scratch,
+                        Emit emit) {
   constexpr int kWarps = kThreads / 32;
-  const int tid = threadIdx.x, nt = kThreads, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x, nt = kThreads, lane = tid & 31;
   if (L <= T) {
     for (int t = tid; t < T; t += nt) emit(t, t < L ? t : -1);
     return;
   }
-  int* hist = reinterpret_cast<int*>(scratch);                                  // 16 KB
-  int2* cand = reinterpret_cast<int2*>(scratch + 16384);                        // 16 KB
-  uint32_t* selbit = reinterpret_cast<uint32_t*>(scratch + 32768);              // L/32 words
-  const int nsl = (L + nt - 1) / nt;
-  int2* cnt = reinterpret_cast<int2*>(scratch + 32768 + ((L + 1023) / 1024) * 128);  // nsl * warps
-  int* hist2 = reinterpret_cast<int*>(cnt + nsl * kWarps);                      // 256
+  int2* cand = reinterpret_cast<int2*>(scratch);                                // 16 KB
+  uint32_t* selbit = reinterpret_cast<uint32_t*>(scratch + 16384);              // L/32 words
+  int* hist2 = reinterpret_cast<int*>(scratch + 16384 + ((L + 1023) / 1024) * 128);  // 256
   int2* cand2 = reinterpret_cast<int2*>(hist2 + 256);                           // kSfMaxBin2
-  zero_hist<kThreads>(hist);
+  const int per = (L + nt - 1) / nt;
+  const int i0 = min(tid * per, L), i1 = min(i0 + per, L);
   for (int wd = tid; wd < (L + 31) / 32; wd += nt) selbit[wd] = 0u;
   if (tid < 256) hist2[tid] = 0;
   if (tid == 0) {
@@ -256,24 +259,17 @@ __device__ void sf_topk(SfShared& sh, const uint32_t* keys, int L, int T, uint8_
     sh.kmin2 = 0xFFFFFFFFu;
     sh.kmax2 = 0u;
   }
-  __syncthreads();
-  for (int i = tid; i < L; i += nt) atomicAdd(&hist[bin_of(keys[i])], 1);
-  __syncthreads();
-  const TopBin tb = find_top_bin<kThreads>(T, hist, sh.warp_tot, &sh.res);
+  const TopBin tb = find_top_bin<kThreads>(T, hist, sh.warp_tot, &sh.res);   // (contains barriers)
   const bool keep = tb.in <= kSfMaxBin;
   {
-    // the threshold bin's keys: per-warp counts and key range (no shared
-    // atomics), a scan of the warps' counts, then each warp writes its own
-    // candidates in index order
-    const uint32_t ltm = lanemask_lt();
-    int wc = 0;
+    // the threshold bin's keys: this thread's count and key range, a block scan
+    // of the counts, then each thread writes its candidates in index order
+    int c = 0;
     uint32_t lo = 0xFFFFFFFFu, hi = 0u;
-    for (int j = 0; j < nsl; ++j) {
-      const int i = j * nt + tid;
-      const uint32_t k = i < L ? keys[i] : 0u;
-      const bool mm = i < L && bin_of(k) == tb.bin;
-      wc += __popc(__ballot_sync(0xffffffffu, mm));
-      if (mm) {
+    for (int i = i0; i < i1; ++i) {
+      const uint32_t k = keys[i];
+      if (bin_of(k) == tb.bin) {
+        ++c;
         lo = min(lo, k);
         hi = max(hi, k);
       }
@@ -281,36 +277,25 @@ __device__ void sf_topk(SfShared& sh, const uint32_t* keys, int L, int T, uint8_
     lo = __reduce_min_sync(0xffffffffu, lo);
     hi = __reduce_max_sync(0xffffffffu, hi);
     if (lane == 0) {
-      sh.wcnt[warp] = make_int2(wc, 0);
-      sh.wmin[warp] = lo;
-      sh.wmax[warp] = hi;
+      sh.wmin[tid >> 5] = lo;
+      sh.wmax[tid >> 5] = hi;
     }
-    __syncthreads();
+    int tot;
+    int b0 = block_exclusive_scan(c, sh.warp_tot, &tot);   // (barriers make wmin / wmax visible)
     if (tid == 0) {
-      int run = 0;
       uint32_t mn = 0xFFFFFFFFu, mx = 0u;
       for (int w = 0; w < kWarps; ++w) {
-        const int c = sh.wcnt[w].x;
-        sh.wcnt[w].y = run;
-        run += c;
         mn = min(mn, sh.wmin[w]);
         mx = max(mx, sh.wmax[w]);
       }
       sh.kmin = mn;
       sh.kmax = mx;
     }
-    __syncthreads();
-    if (keep) {
-      int b0 = sh.wcnt[warp].y;
-      for (int j = 0; j < nsl; ++j) {
-        const int i = j * nt + tid;
-        const uint32_t k = i < L ? keys[i] : 0u;
-        const bool mm = i < L && bin_of(k) == tb.bin;
-        const unsigned bal = __ballot_sync(0xffffffffu, mm);
-        if (mm) cand[b0 + __popc(bal & ltm)] = make_int2(static_cast<int>(k), i);
-        b0 += __popc(bal);
+    if (keep && c > 0)
+      for (int i = i0; i < i1; ++i) {
+        const uint32_t k = keys[i];
+        if (bin_of(k) == tb.bin) cand[b0++] = make_int2(static_cast<int>(k), i);
       }
-    }
   }
   __syncthreads();
   bool by_bin = false, have_tie = false;
@@ -328,19 +313,19 @@ __device__ void sf_topk(SfShared& sh, const uint32_t* keys, int L, int T, uint8_
     if (tb.in > kSfSmallBin) {
       for (int q = tid; q < tb.in; q += nt) atomicAdd(&hist2[(cand[q].x >> (24 - kBinBits)) & 255], 1);
       __syncthreads();
-      if (warp == 0) {
-        const int hi = 256 - lane * 8;
-        int cc[8], s = 0;
+      if (tid < 32) {
+        const int hb = 256 - lane * 8;
+        int cc[8], sm = 0;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          cc[j] = hist2[hi - 8 + j];
-          s += cc[j];
+          cc[j] = hist2[hb - 8 + j];
+          sm += cc[j];
         }
-        int cum = warp_inclusive_scan(s) - s;
-        if (cum < need_bin && cum + s >= need_bin) {
+        int cum = warp_inclusive_scan(sm) - sm;
+        if (cum < need_bin && cum + sm >= need_bin) {
 #pragma unroll
           for (int j = 7; j >= 0; --j) {
-            if (cum < need_bin && cum + cc[j] >= need_bin) sh.res2 = make_int4(hi - 8 + j, cum, cc[j], 0);
+            if (cum < need_bin && cum + cc[j] >= need_bin) sh.res2 = make_int4(hb - 8 + j, cum, cc[j], 0);
             cum += cc[j];
           }
         }
@@ -405,7 +390,7 @@ __device__ void sf_topk(SfShared& sh, const uint32_t* keys, int L, int T, uint8_
         T,
         [&](uint32_t c1, uint32_t c2, uint32_t c3, int& n1, int& n2, int& n3) {
           n1 = n2 = n3 = 0;
-          for (int i = tid; i < L; i += nt) {
+          for (int i = i0; i < i1; ++i) {
             const uint32_t k = keys[i];
             n1 += k >= c1;
             n2 += k >= c2;
@@ -415,53 +400,32 @@ __device__ void sf_topk(SfShared& sh, const uint32_t* keys, int L, int T, uint8_
         sh.red, &gt);
     need = T - gt;
   }
+  // class of candidate i with key k: 1 = selected outright, 2 = tie of thr
+  // (selected while fewer than `need` ties precede it), 0 = not selected
   auto klass = [&](int i, uint32_t k) -> int {
-    if (i >= L) return 0;
     if (by_bin) {
       const int b = bin_of(k);
       return (b > tb.bin || (b == tb.bin && ((selbit[i >> 5] >> (i & 31)) & 1u))) ? 1 : 0;
     }
     return k > thr ? 1 : (k == thr ? 2 : 0);
   };
-  const uint32_t lt = lanemask_lt();
-#pragma unroll 1
-  for (int j = 0; j < nsl; ++j) {
-    const int i = j * nt + tid;
-    const int kl = klass(i, i < L ? keys[i] : 0u);
-    const unsigned gb = __ballot_sync(0xffffffffu, kl == 1);
-    const unsigned eb = __ballot_sync(0xffffffffu, kl == 2);
-    if (lane == 0) cnt[j * kWarps + warp] = make_int2(__popc(gb), __popc(eb));
+  // this thread's (selected, tie) counts -> one block scan -> output slots
+  int g = 0, e = 0;
+  for (int i = i0; i < i1; ++i) {
+    const int kl = klass(i, keys[i]);
+    g += kl == 1;
+    e += kl == 2;
   }
-  __syncthreads();
-  if (warp == 0) {
-    const int E = nsl * kWarps;
-    const int ch = (E + 31) / 32;
-    const int beg = min(lane * ch, E), end = min(beg + ch, E);
-    int sg = 0, se = 0;
-    for (int q = beg; q < end; ++q) {
-      sg += cnt[q].x;
-      se += cnt[q].y;
-    }
-    const int ig = warp_inclusive_scan(sg), ie = warp_inclusive_scan(se);
-    int rg = ig - sg, re = ie - se;
-    for (int q = beg; q < end; ++q) {
-      const int2 v = cnt[q];
-      cnt[q] = make_int2(rg, re);
-      rg += v.x;
-      re += v.y;
-    }
-  }
-  __syncthreads();
-#pragma unroll 1
-  for (int j = 0; j < nsl; ++j) {
-    const int i = j * nt + tid;
-    const int kl = klass(i, i < L ? keys[i] : 0u);
-    const unsigned gb = __ballot_sync(0xffffffffu, kl == 1);
-    const unsigned eb = __ballot_sync(0xffffffffu, kl == 2);
-    const int2 b0 = cnt[j * kWarps + warp];
-    const int gt_lt = b0.x + __popc(gb & lt);
-    const int eq_lt = b0.y + __popc(eb & lt);
-    if (kl == 1 || (kl == 2 && eq_lt < need)) emit(gt_lt + min(eq_lt, need), i);
+  long long tot;
+  const long long packed = block_exclusive_scan((static_cast<long long>(g) << 32) | e,
+                                                reinterpret_cast<long long*>(sh.red), &tot);
+  int gt_lt = static_cast<int>(packed >> 32), eq_lt = static_cast<int>(packed & 0xFFFFFFFFll);
+  for (int i = i0; i < i1; ++i) {
+    const int kl = klass(i, keys[i]);
+    if (kl == 1) emit(gt_lt + min(eq_lt, need), i);
+    else if (kl == 2 && eq_lt < need) emit(gt_lt + eq_lt, i);
+    gt_lt += kl == 1;
+    eq_lt += kl == 2;
   }
 }
 
@@ -491,6 +455,7 @@ __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 1 : 2)
   float* spsc = reinterpret_cast<float*>(base + a.off_tab);
   int* srt = reinterpret_cast<int*>(spsc + a.pages);
   int* sntab = srt + a.pages;
+  int* thist = reinterpret_cast<int*>(base + a.off_tab + ((a.pages * 12 + 15) & ~15));  // the keys' histogram
   uint8_t* uni = base + a.off_u;
   // route view of the union: histogram + winner list
   int* rhist = reinterpret_cast<int*>(uni);
@@ -745,6 +710,8 @@ __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 1 : 2)
         for (int q = 0; q < 64; ++q) memb[rr * 64 + q] = -1;
       }
     }
+    // the Top-T histogram, counted as the keys are written
+    for (int v = e; v < kBins / 4; v += 128 * kGroups) reinterpret_cast<int4*>(thist)[v] = make_int4(0, 0, 0, 0);
     asm volatile("cp.async.commit_group;" ::: "memory");
     asm volatile("cp.async.wait_all;" ::: "memory");
     asm volatile("bar.sync 1, %0;" ::"r"(128 * kGroups) : "memory");
@@ -807,7 +774,9 @@ __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 1 : 2)
         }
       }
       if (col >= 0) {
-        sc[col] = score;
+        const uint32_t key = order_key(score);
+        reinterpret_cast<uint32_t*>(sc)[col] = key;
+        atomicAdd(&thist[bin_of(key)], 1);
         if (gout) gout[col] = score;
       }
     }
@@ -816,9 +785,7 @@ __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 1 : 2)
   if (!*reinterpret_cast<volatile int*>(&sh.abort)) {
     // ---- Top-T + mapping (all threads) ------------------------------------------------
     const int Lr = sh.L, tk = sh.take, sink = sh.sink, tail = sh.tail, nn = sh.n;
-    uint32_t* keys = reinterpret_cast<uint32_t*>(sc);
-    for (int j = tid; j < Lr; j += kThreads) keys[j] = order_key(sc[j]);
-    __syncthreads();
+    const uint32_t* keys = reinterpret_cast<const uint32_t*>(sc);   // order keys, written by the epilogue
     auto emit = [&](int pos, int rawi) {
       int lg = -1;
       if (rawi >= 0 && rawi < Lr && keys[rawi] != kNegInfKey) {
@@ -842,7 +809,7 @@ __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 1 : 2)
             lg < 0 ? make_int4(-1, -1, -1, -1) : make_int4(b4, b4 + 1, b4 + 2, b4 + 3);
       }
     };
-    sf_topk<kThreads>(sh, keys, Lr, a.topk, stages, emit);
+    sf_topk<kThreads>(sh, keys, thist, Lr, a.topk, stages, emit);
     if (a.expansion_stride)
       for (int64_t j = static_cast<int64_t>(a.topk) * 4 + tid; j < a.expansion_stride; j += kThreads)
         a.expanded[row * a.expansion_stride + j] = -1;
@@ -963,14 +930,12 @@ extern "C" int v1x_select_fused(const uint8_t* q, const float* w, int64_t heads,
   // row, and cut the throughput of batches in flight from 922K to 735K
   // queries/s)
   const int threads = 256;
-  const int warps = threads / 32;
   // shared memory plan: everything but the stage ring, then as many 16 KB
   // stages (4 to 8) as fit the CTA's share of the SM
   auto align = [](int64_t x, int64_t al) { return (x + al - 1) / al * al; };
   const int64_t route_bytes = 16384 + static_cast<int64_t>(n_items) * 8;
   const int64_t row_bytes = static_cast<int64_t>(max_cand) * 4 + take_stride * 64 * 4;
-  const int64_t topk_scratch = 32768 + (max_cand + 1023) / 1024 * 128 +
-                               ((max_cand + threads - 1) / threads) * warps * 8 + 1024 + kSfMaxBin2 * 8;
+  const int64_t topk_scratch = 16384 + (max_cand + 1023) / 1024 * 128 + 1024 + kSfMaxBin2 * 8;
   auto plan = [&](int stages, int64_t* offs) {   // offs: q, sring, w, sel, sh, tab, u; returns total bytes
     int64_t off = static_cast<int64_t>(stages) * 16384;
     offs[0] = off;
@@ -984,16 +949,20 @@ extern "C" int v1x_select_fused(const uint8_t* q, const float* w, int64_t heads,
     offs[4] = off;
     off = align(off + static_cast<int64_t>(sizeof(SfShared)), 16);
     offs[5] = off;
-    off = align(off + pages * 12, 16);
+    off = align(align(off + pages * 12, 16) + 4 * kBins, 16);
     offs[6] = off;
     off += std::max(route_bytes, row_bytes);
     return off + 1024;
   };
   // two CTAs per SM when they fit (one head, many rows), else one
   const int64_t budget_bytes = heads == 1 ? 113 * 1024 : 227 * 1024;
-  int stages = 8;
+  // one head: three stages, so that two CTAs share an SM; else six (eight gave
+  // the same row latency, but a CTA of 219 KB of shared memory leaves its SM
+  // almost no L1 for an independent batch's gather running beside it: 832K
+  // against 930K queries/s with batches in flight)
+  int stages = heads == 1 ? 3 : 6;
   int64_t offs[7];
-  while (stages > 4 && (plan(stages, offs) > budget_bytes || (heads == 1 && stages > 4))) --stages;
+  while (stages > 4 && plan(stages, offs) > budget_bytes) --stages;
   const int64_t total = plan(stages, offs);
   if (total > 227 * 1024 || topk_scratch > static_cast<int64_t>(stages) * 16384) {
     set_error("select_fused: shared memory %lld too large (pages %lld, window %lld)", (long long)total,
