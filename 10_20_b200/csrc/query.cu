@@ -305,6 +305,71 @@ __global__ void expand_logical_kernel(const int32_t* __restrict__ logical, int32
   }
 }
 
+// ---- row staging of a query bucket (runtime.py:643-666) ----------------------
+// One CTA per bucket row: the caller's q, weights, length and native page table
+// row, the request's reordered and centre table rows (arena rows named by id),
+// or zeros for a row past the caller's n.  The ids travel in the launch's
+// parameters, so no host -> device copy precedes the kernel.
+constexpr int kStageRowsMax = 256;
+
+struct QueryStageArgs {
+  const uint8_t* q;
+  const float* w;
+  const int32_t* lens;
+  const int32_t* nt;
+  const int32_t* state_tables;
+  const int32_t* state_centers;
+  uint8_t* q_out;
+  float* w_out;
+  int32_t* lens_out;
+  int32_t* nt_out;
+  int32_t* rt_out;
+  int32_t* ct_out;
+  int64_t heads, width, pages, n;
+  int32_t rows[kStageRowsMax];
+};
+
+// dst[0, bytes) = src[0, bytes) (src null: zeros) by the CTA's threads, with
+// 16-byte accesses where both addresses allow them.
+__device__ __forceinline__ void stage_bytes(uint8_t* dst, const uint8_t* src, int64_t bytes) {
+  const int t = threadIdx.x, nt = blockDim.x;
+  const uintptr_t al = reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src);
+  int64_t done = 0;
+  if ((al & 15) == 0) {
+    const int64_t n16 = bytes >> 4;
+    uint4* d = reinterpret_cast<uint4*>(dst);
+    const uint4* s = reinterpret_cast<const uint4*>(src);
+    for (int64_t i = t; i < n16; i += nt) d[i] = src ? s[i] : make_uint4(0, 0, 0, 0);
+    done = n16 << 4;
+  } else if ((al & 3) == 0) {
+    const int64_t n4 = bytes >> 2;
+    uint32_t* d = reinterpret_cast<uint32_t*>(dst);
+    const uint32_t* s = reinterpret_cast<const uint32_t*>(src);
+    for (int64_t i = t; i < n4; i += nt) d[i] = src ? s[i] : 0u;
+    done = n4 << 2;
+  }
+  for (int64_t i = done + t; i < bytes; i += nt) dst[i] = src ? src[i] : 0;
+}
+
+__global__ void __launch_bounds__(256) query_stage_kernel(const __grid_constant__ QueryStageArgs a) {
+  const int64_t i = blockIdx.x;
+  const bool live = i < a.n;
+  const int64_t qb = a.heads * 128, cp = a.pages / 8;
+  const int64_t wb = live ? a.width * 4 : 0;
+  stage_bytes(a.q_out + i * qb, live ? a.q + i * qb : nullptr, qb);
+  stage_bytes(reinterpret_cast<uint8_t*>(a.w_out + i * a.heads),
+              live ? reinterpret_cast<const uint8_t*>(a.w + i * a.heads) : nullptr, a.heads * 4);
+  uint8_t* nt = reinterpret_cast<uint8_t*>(a.nt_out + i * a.pages);
+  stage_bytes(nt, live ? reinterpret_cast<const uint8_t*>(a.nt + i * a.width) : nullptr, wb);
+  stage_bytes(nt + wb, nullptr, a.pages * 4 - wb);
+  const int64_t r = live ? a.rows[i] : 0;
+  stage_bytes(reinterpret_cast<uint8_t*>(a.rt_out + i * a.pages),
+              live ? reinterpret_cast<const uint8_t*>(a.state_tables + r * a.pages) : nullptr, a.pages * 4);
+  stage_bytes(reinterpret_cast<uint8_t*>(a.ct_out + i * cp),
+              live ? reinterpret_cast<const uint8_t*>(a.state_centers + r * cp) : nullptr, cp * 4);
+  if (threadIdx.x == 0) a.lens_out[i] = live ? a.lens[i] : 0;
+}
+
 }  // namespace
 }  // namespace v1x
 
@@ -444,4 +509,46 @@ extern "C" int v1x_expand_logical(const int32_t* logical, int32_t* out, int64_t 
   if (batch == 0 || stride == 0) return V1X_OK;
   expand_logical_kernel<<<static_cast<unsigned>(batch), 256, 0, as_stream(stream)>>>(logical, out, topk, stride);
   return launch_status("v1x_expand_logical");
+}
+
+extern "C" int v1x_query_stage(const uint8_t* q, const float* w, const int32_t* lens, const int32_t* native_tables,
+                               int64_t width, const int32_t* rows, const int32_t* state_tables,
+                               const int32_t* state_centers, int64_t state_rows, uint8_t* q_out, float* w_out,
+                               int32_t* lens_out, int32_t* nt_out, int32_t* rt_out, int32_t* ct_out,
+                               int64_t heads, int64_t pages, int64_t n, int64_t filled, void* stream) {
+  clear_error();
+  V1X_CHECK_ARG(heads > 0 && pages > 0 && pages % 8 == 0 && width >= 0 && width <= pages && n >= 0 &&
+                    filled >= 0 && state_rows >= 0,
+                "query_stage: bad geometry");
+  V1X_CHECK_ARG(q_out && w_out && lens_out && nt_out && rt_out && ct_out, "query_stage: null output");
+  V1X_CHECK_ARG(n == 0 || (q && w && lens && rows && state_tables && state_centers && (native_tables || !width)),
+                "query_stage: null input");
+  for (int64_t i = 0; i < n; ++i)
+    V1X_CHECK_ARG(rows[i] >= 0 && rows[i] < state_rows, "query_stage: row id %d of row %lld out of range",
+                  rows[i], static_cast<long long>(i));
+  const int64_t total = std::max(n, filled);
+  for (int64_t s = 0; s < total; s += kStageRowsMax) {
+    const int64_t m = std::min<int64_t>(kStageRowsMax, total - s);
+    const int64_t live = std::min<int64_t>(std::max<int64_t>(n - s, 0), m);
+    QueryStageArgs a{};
+    a.q = live ? q + s * heads * 128 : nullptr;
+    a.w = live ? w + s * heads : nullptr;
+    a.lens = live ? lens + s : nullptr;
+    a.nt = live ? native_tables + s * width : nullptr;
+    a.state_tables = state_tables;
+    a.state_centers = state_centers;
+    a.q_out = q_out + s * heads * 128;
+    a.w_out = w_out + s * heads;
+    a.lens_out = lens_out + s;
+    a.nt_out = nt_out + s * pages;
+    a.rt_out = rt_out + s * pages;
+    a.ct_out = ct_out + s * (pages / 8);
+    a.heads = heads;
+    a.width = width;
+    a.pages = pages;
+    a.n = live;
+    for (int64_t i = 0; i < live; ++i) a.rows[i] = rows[s + i];
+    launch_kernel(query_stage_kernel, dim3(static_cast<unsigned>(m)), dim3(256), 0, as_stream(stream), a);
+  }
+  return launch_status("v1x_query_stage");
 }

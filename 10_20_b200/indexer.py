@@ -23,13 +23,16 @@ contents (see lifecycle.PageArena).
 from __future__ import annotations
 
 import threading
+from array import array
 
 import torch
 
+from . import _lib
 from . import kernels as K
+from ._lib import ptr
 from .config import Config
 from .index_build import BucketBuilder
-from .lifecycle import HostStaging, PageArena
+from .lifecycle import PageArena
 from .pipeline import SelectionStep
 from .synth import QueryCase
 
@@ -64,9 +67,13 @@ class _Query:
         self.graph = None
         self.graphs = c.graphs
         self.filled = 0        # rows [filled, rows) of the staged inputs are known to be zero
-        # arena rows of the staged requests, for one gather of their page tables
-        self.row_ids = torch.zeros(rows, dtype=torch.int64, device=d)
-        self.staging = HostStaging(rows, d, dtype=torch.int64)
+        self.device = d
+        # the staging call's fixed arguments: the arena's request tables and the
+        # bucket's capture-stable inputs
+        self.stage_args = (ptr(a.state_tables), ptr(a.state_centers), a.state_tables.shape[0], ptr(self.case.q8),
+                           ptr(self.case.w), ptr(self.case.lens), ptr(self.case.native_table),
+                           ptr(self.case.reordered_table), ptr(self.case.center_table))
+        self.views: dict[int, tuple] = {}   # n -> the outputs' first n rows
 
     def _execute(self):
         if not self.graphs:
@@ -84,30 +91,29 @@ class _Query:
             return
         self.graph.replay()
 
-    def run(self, q, w, native_tables, lengths, states, return_logical=False):
-        c = self.case
-        n = len(q)
-        c.q8[:n].copy_(q)
-        c.w[:n].copy_(w)
-        c.lens[:n].copy_(lengths)
-        c.native_table[:n, : native_tables.shape[1]].copy_(native_tables)
-        if native_tables.shape[1] < c.native_table.shape[1]:
-            c.native_table[:n, native_tables.shape[1]:].zero_()
-        if n < self.filled:    # rows past n written by an earlier, longer call: zero them again
-            for t in (c.q8.view(torch.uint8), c.w, c.lens, c.native_table, c.reordered_table, c.center_table):
-                t[n:self.filled].zero_()
+    def run(self, q, w, native_tables, lengths, rows, return_logical=False):
+        """Stage n rows (``rows``: each row's arena row id), run the step and
+        return clones of the outputs' first n rows (:643-678).  The staging --
+        inputs, zeroed padding rows and the requests' table rows -- is one
+        launch (v1x_query_stage)."""
+        n = q.shape[0]
+        c = self.owner.config
+        ids = array("i", rows)
+        stream = torch.cuda.current_stream(self.device)
+        _lib.call("v1x_query_stage", q.data_ptr(), w.data_ptr(), lengths.data_ptr(), native_tables.data_ptr(),
+                  native_tables.shape[1], ids.buffer_info()[0], *self.stage_args, c.heads, c.pages, n, self.filled,
+                  stream.cuda_stream, device=self.device)
         self.filled = n
-        # every row's reordered and centre page tables: rows of the arena's request
-        # tables, gathered in one launch each
-        a = self.owner.arena
-        ids = self.staging.copy([st.row for st in states], self.row_ids)[:n]
-        torch.index_select(a.state_tables, 0, ids, out=c.reordered_table[:n])
-        torch.index_select(a.state_centers, 0, ids, out=c.center_table[:n])
         self._execute()
-        out = self.step.expanded if self.owner.config.expand_output else self.step.physical
-        result = out[:n].clone()
+        views = self.views.get(n)
+        if views is None:
+            out = self.step.expanded if c.expand_output else self.step.physical
+            views = self.views[n] = (out[:n], self.step.logical[:n])
+        result = views[0].clone()
         if return_logical:
-            result = (result, self.step.logical[:n].clone())
+            result = (result, views[1].clone())
+        for t in (q, w, native_tables, lengths):     # read on this stream (:676-677)
+            t.record_stream(stream)
         return result
 
 
@@ -175,6 +181,30 @@ class Indexer:
         self.arena.prepare_many([(owner, length)], batch_source)
         return self.arena.states[owner]
 
+    def _ready_rows(self, owners, cpu):
+        """The arena rows of the owners when no row needs a prepare -- every
+        owner known, no row shorter than its request's indexed length and no
+        newly complete bucket -- recording each row's length as the request's;
+        None otherwise (the full prepare path then runs, with the same result)."""
+        rows, done = [], []
+        for st, x in zip(map(self.arena.states.get, owners), cpu):
+            if st is None or x < st.length or x >> 10 != len(st.leases):
+                for st0, old in reversed(done):     # undo: the prepare path decides
+                    st0.length = old
+                return None
+            done.append((st, st.length))
+            st.length = x
+            rows.append(st.row)
+        return rows
+
+    def _bucket(self, n):
+        """The query bucket of the smallest configured size >= n (:881-884)."""
+        rows = next(r for r in self.config.q_buckets if r >= n)
+        qb = self.queries.get(rows)
+        if qb is None:
+            qb = self.queries[rows] = _Query(self, rows)
+        return qb
+
     @torch.inference_mode()
     def prepare(self, owner, native_table, length):
         with self.lock:
@@ -205,30 +235,29 @@ class Indexer:
                                     dtype=torch.int32)
                 return (empty, torch.empty((0, c.topk), device=self.device, dtype=torch.int32)) \
                     if return_logical else empty
-            # build each request to its largest visible length before querying
-            longest = {}              # owner -> (length, row) of its longest row (ties: first row)
-            for i, (key, x) in enumerate(zip(owners, cpu)):
-                if x > longest.get(key, (-1, 0))[0]:
-                    longest[key] = (x, i)
-            states = self.states
-            for key, (x, i) in longest.items():
-                st = states.get(key)
-                if st is not None and x >= st.length and x // 1024 == len(st.leases):
-                    st.length = x             # no newly complete bucket: nothing to index
-                    continue
-                self._prepare(key, native_tables[i], x)
-            if self.arena.pending_check:      # new buckets: read the status word (a sync)
-                self.arena.check()
+            rows = self._ready_rows(owners, cpu)
+            if rows is None:
+                # build each request to its largest visible length before querying
+                longest = {}              # owner -> (length, row) of its longest row (ties: first row)
+                for i, (key, x) in enumerate(zip(owners, cpu)):
+                    if x > longest.get(key, (-1, 0))[0]:
+                        longest[key] = (x, i)
+                for key, (x, i) in longest.items():
+                    self._prepare(key, native_tables[i], x)
+                if self.arena.pending_check:      # new buckets: read the status word (a sync)
+                    self.arena.check()
+                states = self.states
+                rows = [states[x].row for x in owners]
+            step = c.q_buckets[-1]
+            if n <= step:                     # one bucket: the caller's tensors as they are
+                return self._bucket(n).run(q, weights, native_tables, lengths, rows, return_logical)
             outputs = []
-            for start in range(0, n, c.q_buckets[-1]):
-                end = min(n, start + c.q_buckets[-1])
-                rows = next(r for r in c.q_buckets if r >= end - start)
-                if rows not in self.queries:
-                    self.queries[rows] = _Query(self, rows)
-                outputs.append(self.queries[rows].run(q[start:end], weights[start:end], native_tables[start:end],
-                                                      lengths.reshape(-1)[start:end],
-                                                      [self.states[x] for x in owners[start:end]],
-                                                      return_logical))
+            for start in range(0, n, step):
+                end = min(n, start + step)
+                outputs.append(self._bucket(end - start).run(q[start:end], weights[start:end],
+                                                             native_tables[start:end],
+                                                             lengths.reshape(-1)[start:end], rows[start:end],
+                                                             return_logical))
             if len(outputs) == 1:
                 return outputs[0]
             if return_logical:

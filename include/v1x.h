@@ -464,6 +464,21 @@ V1X_API int v1x_output_ids(const int32_t* raw, const float* scores, const int32_
                    int64_t width, int64_t topk, int64_t sink, int64_t window, int map_physical,
                    int direct_fine, int64_t fp, int64_t batch, void* stream);
 
+/* The row staging of the reference's Query.run (DS/runtime.py:643-666) in one
+ * launch (the reference issues a copy per tensor and per run of equal owners).
+ * For rows i < n: q_out[i] = q[i] (heads*128 bytes), w_out[i] = w[i] (heads
+ * floats), lens_out[i] = lens[i], nt_out[i] = native_tables[i] (width entries,
+ * zeros up to pages), rt_out[i] = state_tables[rows[i]] (pages entries),
+ * ct_out[i] = state_centers[rows[i]] (pages/8 entries).  Rows n <= i < filled
+ * of every output are zeroed.  rows is a HOST array of n arena row ids, each in
+ * [0, state_rows) (checked; it travels in the launch parameters).  Outputs are
+ * dense [*, heads*128] / [*, heads] / [*] / [*, pages] / [*, pages] / [*, pages/8]. */
+V1X_API int v1x_query_stage(const uint8_t* q, const float* w, const int32_t* lens, const int32_t* native_tables,
+                    int64_t width, const int32_t* rows, const int32_t* state_tables,
+                    const int32_t* state_centers, int64_t state_rows, uint8_t* q_out, float* w_out,
+                    int32_t* lens_out, int32_t* nt_out, int32_t* rt_out, int32_t* ct_out, int64_t heads,
+                    int64_t pages, int64_t n, int64_t filled, void* stream);
+
 /* DS/kernels.py:594-600. logical i32 [batch, topk] -> out i32 [batch, stride]. */
 V1X_API int v1x_expand_logical(const int32_t* logical, int32_t* out, int64_t topk, int64_t stride,
                        int64_t batch, void* stream);

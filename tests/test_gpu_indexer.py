@@ -64,3 +64,30 @@ def test_indexer_expanded_output_and_checks(cuda_dev):
         bad = list(lens)
         bad[0] = 192 * 64 + 1
         ix.query(case.q8, case.w, case.native_table, case.lens, list(range(B)), bad)
+
+
+def test_indexer_padding_narrow_tables_and_repeated_owners(cuda_dev):
+    """A shorter call after a longer one on the same bucket (its padding rows are
+    zeroed again), native tables narrower than the configured page count, and
+    one request on several rows with different lengths (each row masks to its
+    own length; the request is built to the longest)."""
+    B, case, ix, ref, lens = _setup(True)
+    owners = list(range(B))
+    assert torch.equal(ix.query(case.q8, case.w, case.native_table, case.lens, owners, lens), ref.physical)
+    part = ix.query(case.q8[:5], case.w[:5], case.native_table[:5], case.lens[:5], owners[:5], lens[:5])
+    assert torch.equal(part, ref.physical[:5])
+    width = max(-(-x // 64) for x in lens)
+    narrow = case.native_table[:, :width].contiguous()
+    assert torch.equal(ix.query(case.q8, case.w, narrow, case.lens, owners, lens), ref.physical)
+    # request r on two rows, the second 5 tokens shorter (same complete buckets)
+    r = next(i for i in range(B) if lens[i] % 1024 >= 8 and i != 1)
+    idx = [1, r, r]
+    rl = [lens[1], lens[r], lens[r] - 5]
+    out = ix.query(case.q8[idx], case.w[idx], case.native_table[idx].contiguous(),
+                   torch.tensor(rl, dtype=torch.int32, device="cuda"), [owners[i] for i in idx], rl)
+    assert torch.equal(out[:2], ref.physical[[1, r]])
+    assert ix.states[r].length == lens[r]
+    alone = ix.query(case.q8[[r]], case.w[[r]], case.native_table[[r]].contiguous(),
+                     torch.tensor([lens[r] - 5], dtype=torch.int32, device="cuda"), [r], [lens[r] - 5])
+    assert torch.equal(out[2:], alone)
+    ix.close()
