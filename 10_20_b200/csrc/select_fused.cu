@@ -28,13 +28,17 @@
 //     while the route runs.  The selected pages' tiles follow.
 //   * epilogue (4 warps, one key per thread): tcgen05.ld of the H head columns,
 //     ReLU, the weighted head sum, the key's scale, the boundary-bucket mask;
-//     each score lands in shared memory at its raw candidate column;
+//     each score's order key lands in shared memory at its raw candidate
+//     column and is counted in the Top-T histogram as it is written;
 //   * Top-T over the shared-memory row (histogram bin, exact ranking of the
 //     threshold bin, ties to the lower index), outputs in ascending raw order,
 //     mapped through the staged members and the native page table.
-// Warp roles during scoring: warp 0 TMA producer, warp 1 TMEM owner and MMA
-// issuer, warps 2-5 epilogue; every warp takes part in the metadata, route and
-// Top-T phases.  Every mbarrier wait is bounded (2 s): on expiry the CTA
+// Warp roles during scoring: warp 1 TMEM owner and MMA issuer, warps 2-5
+// epilogue, warp 0 and the warps past the epilogue (6-7) TMA producers -- warp 0
+// alone issues the sink/tail tiles before the route, then each ring stage is fed
+// by one producer warp in tile order (a stage fed by two warps could see a
+// parity wait pass two phases behind); every warp takes part in the metadata,
+// route and Top-T phases.  Every mbarrier wait is bounded (2 s): on expiry the CTA
 // writes V1X_STATUS_TIMEOUT, lets what it issued retire, frees its TMEM and
 // leaves the row's outputs unwritten.
 #include <cudaTypedefs.h>

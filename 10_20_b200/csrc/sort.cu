@@ -59,45 +59,63 @@ __device__ __forceinline__ uint32_t ordered_score(float s) {
   return b ^ ((b & 0x80000000u) ? 0xFFFFFFFFu : 0x80000000u);
 }
 
-// Segments of N <= 256 records, 256 / N of them per CTA (see the header).
-template <int N>
+// Segments of N <= 256 records by rank counting: a record's output slot is the
+// number of records of its segment with a greater key, plus the equal keys
+// before it (the stable order).  T threads share one record, each counting over
+// N / T of the segment's keys, and a CTA of 256 threads takes R = 256 / T
+// consecutive records -- so the 4096 records of a head row spread over 4096 / R
+// CTAs (up to a few per SM) instead of the 4096 / 256 that one thread per record
+// would give.  The CTA stages the keys of every segment it touches: its own R
+// records when R >= N, else the whole segment its records lie in.
+template <int N, int T>
 __global__ void __launch_bounds__(256) sort_rank_kernel(const int32_t* __restrict__ P, int32_t* __restrict__ O,
                                                         const float* __restrict__ S,
-                                                        const int32_t* __restrict__ flag, int groups) {
-  static_assert(N >= 2 && N <= 256 && (N & (N - 1)) == 0, "segment size");
-  constexpr int kSegs = 256 / N;
-  __shared__ __align__(16) uint32_t skey[256];
+                                                        const int32_t* __restrict__ flag, int records) {
+  static_assert(N >= 2 && N <= 1024 && (N & (N - 1)) == 0, "segment size");
+  static_assert(T >= 1 && T <= 32 && (T & (T - 1)) == 0 && T <= N, "threads per record");
+  constexpr int R = 256 / T;            // records per CTA
+  constexpr int C = N / T;              // keys compared per thread
+  constexpr int K = R >= N ? R : N;     // keys staged per CTA
+  __shared__ __align__(16) uint32_t skey[K];
   const int t = threadIdx.x;
-  const int g = blockIdx.x * kSegs + t / N;   // segment of this record
-  const int i = t % N;                        // its position in the segment
-  const bool live = g < groups;
-  const int64_t seg = static_cast<int64_t>(blockIdx.y) * 4096 + static_cast<int64_t>(g) * N;
-  // flag, score and P in one round trip
+  const int64_t row = static_cast<int64_t>(blockIdx.y) * 4096;
+  const int base = blockIdx.x * R;                  // first record of the CTA
+  const int kbase = R >= N ? base : base / N * N;   // first staged key
+  // flag, scores and P in one round trip
   const int f = *flag;
-  float sc = 0.0f;
-  int pv = 0;
-  if (live) {
-    sc = S[seg + i];
-    pv = P[seg + i];
+#pragma unroll
+  for (int y = t; y < K; y += 256) {
+    const int x = kbase + y;
+    skey[y] = x < records ? ordered_score(S[row + x]) : 0u;
   }
-  const uint32_t k = ordered_score(sc);
-  skey[t] = k;
+  const int r = t / T, part = t % T;
+  const int rec = base + r;
+  const bool live = rec < records;
+  const int pv = live && part == 0 ? P[row + rec] : 0;
   __syncthreads();
-  if (f >= 0 || !live) return;
-  const uint32_t* keys = skey + (t / N) * N;
+  if (f >= 0) return;
+  const int li = rec - kbase;           // the record's staged key
+  const int sb = li / N * N;            // its segment's first staged key
+  const int i = li - sb;                // its position in the segment
+  const uint32_t k = skey[li];
+  const uint32_t* keys = skey + sb + part * C;
+  const int u0 = part * C;
   int rank = 0;
-  if constexpr (N >= 4) {
-#pragma unroll 8
-    for (int u = 0; u < N; u += 4) {
+  if constexpr (C >= 4) {
+#pragma unroll
+    for (int u = 0; u < C; u += 4) {
       const uint4 v = *reinterpret_cast<const uint4*>(keys + u);
+      const int j = u0 + u;
       rank += (v.x > k) + (v.y > k) + (v.z > k) + (v.w > k);
-      rank += (v.x == k && u < i) + (v.y == k && u + 1 < i) + (v.z == k && u + 2 < i) + (v.w == k && u + 3 < i);
+      rank += (v.x == k && j < i) + (v.y == k && j + 1 < i) + (v.z == k && j + 2 < i) + (v.w == k && j + 3 < i);
     }
   } else {
 #pragma unroll
-    for (int u = 0; u < N; ++u) rank += (keys[u] > k) + (keys[u] == k && u < i);
+    for (int u = 0; u < C; ++u) rank += (keys[u] > k) + (keys[u] == k && u0 + u < i);
   }
-  O[seg + rank] = pv;
+#pragma unroll
+  for (int o = T / 2; o >= 1; o >>= 1) rank += __shfl_xor_sync(0xffffffffu, rank, o);
+  if (live && part == 0) O[row + rec - i + rank] = pv;
 }
 
 struct LastValid {  // scan operator: the most recent valid (>= 0) value
@@ -303,18 +321,23 @@ extern "C" int v1x_sort_segments(const int32_t* P, int32_t* O, const float* S, c
   cudaStream_t s = as_stream(stream);
   const bool al = ((reinterpret_cast<uintptr_t>(S) | reinterpret_cast<uintptr_t>(O)) & 15) == 0;
   const int g = static_cast<int>(groups);
-  auto rank_grid = [&](int n) {
-    return dim3(static_cast<unsigned>((groups + 256 / n - 1) / (256 / n)), static_cast<unsigned>(heads));
+  const int recs = static_cast<int>(groups * N);
+  auto rank_grid = [&](int t) {   // 256 / t records per CTA
+    const int r = 256 / t;
+    return dim3(static_cast<unsigned>((recs + r - 1) / r), static_cast<unsigned>(heads));
   };
+#define V1X_RANK(n, t) \
+  case n: sort_rank_kernel<n, t><<<rank_grid(t), 256, 0, s>>>(P, O, S, flag, recs); return launch_status("v1x_sort_segments");
   switch (N) {   // records of up to 256 per segment: rank counting, any alignment
-    case 256: sort_rank_kernel<256><<<rank_grid(256), 256, 0, s>>>(P, O, S, flag, g); return launch_status("v1x_sort_segments");
-    case 128: sort_rank_kernel<128><<<rank_grid(128), 256, 0, s>>>(P, O, S, flag, g); return launch_status("v1x_sort_segments");
-    case 64: sort_rank_kernel<64><<<rank_grid(64), 256, 0, s>>>(P, O, S, flag, g); return launch_status("v1x_sort_segments");
-    case 32: sort_rank_kernel<32><<<rank_grid(32), 256, 0, s>>>(P, O, S, flag, g); return launch_status("v1x_sort_segments");
-    case 16: sort_rank_kernel<16><<<rank_grid(16), 256, 0, s>>>(P, O, S, flag, g); return launch_status("v1x_sort_segments");
-    case 8: sort_rank_kernel<8><<<rank_grid(8), 256, 0, s>>>(P, O, S, flag, g); return launch_status("v1x_sort_segments");
-    case 4: sort_rank_kernel<4><<<rank_grid(4), 256, 0, s>>>(P, O, S, flag, g); return launch_status("v1x_sort_segments");
-    case 2: sort_rank_kernel<2><<<rank_grid(2), 256, 0, s>>>(P, O, S, flag, g); return launch_status("v1x_sort_segments");
+    V1X_RANK(256, 32)
+    V1X_RANK(128, 8)
+    V1X_RANK(64, 8)
+    V1X_RANK(32, 4)
+    V1X_RANK(16, 2)
+    V1X_RANK(8, 1)
+    V1X_RANK(4, 1)
+    V1X_RANK(2, 1)
+#undef V1X_RANK
     default: break;
   }
   const bool alp = al && (reinterpret_cast<uintptr_t>(P) & 15) == 0;

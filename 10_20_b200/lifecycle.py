@@ -40,6 +40,7 @@ state of ``release`` called for each in turn.
 """
 from __future__ import annotations
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -95,6 +96,34 @@ class State:
         self.row = row
 
 
+class _Pending:
+    """The buckets a batched prepare will index, as flat lists in launch order:
+    owner, bucket, lease, and the owner's request-table row."""
+
+    def __init__(self):
+        self.clear()
+
+    def clear(self):
+        self.owners, self.buckets, self.leases, self.rows = [], [], [], []
+
+    def add(self, owner, first, leases, row):
+        n = len(leases)
+        self.owners.extend([owner] * n)
+        self.buckets.extend(range(first, first + n))
+        self.leases.extend(leases)
+        self.rows.extend([row] * n)
+
+    def meta(self):
+        """v1x_prepare_buckets' meta records, flat: (start token, lease, 1, row)."""
+        m = np.empty((len(self.owners), 4), dtype=np.int32)
+        m[:, 0] = self.buckets
+        m[:, 0] *= 1024
+        m[:, 1] = self.leases
+        m[:, 2] = 1
+        m[:, 3] = self.rows
+        return m.reshape(-1)
+
+
 class PageArena:
     def __init__(self, capacity: int, pages: int, device, max_requests: int | None = None,
                  graphs: bool = False, staging_rows: int = 0):
@@ -136,8 +165,9 @@ class PageArena:
         self.state_centers = torch.zeros((self.max_requests, pages // 8), dtype=torch.int32, device=d)
         self.free_rows = list(range(self.max_requests - 1, -1, -1))
         self.kernel_launches = 0   # kernels this driver has launched (reported by the bench)
-        # (owner, bucket, lease) of every bucket launched since the last check(),
-        # in launch order: an exhaustion aborts a suffix of them
+        # (owner, first bucket, leases) of every run of consecutive buckets of one
+        # request launched since the last check(), in launch order: an exhaustion
+        # aborts a suffix of the buckets
         self.unchecked: list = []
         self._prepare_args = None
         # batched prepare: meta records and per-page scratch of one call
@@ -211,7 +241,7 @@ class PageArena:
             lease = self.free_leases.pop()
             tmp, mapping, centers = bucket_source(owner, bucket)
             self._bucket(tmp, mapping, centers, bucket * 1024, lease)
-            self.unchecked.append((owner, bucket, lease))
+            self.unchecked.append((owner, bucket, [lease]))
             state.leases.append(lease)
             state.table[bucket * 16:(bucket + 1) * 16].copy_(self.tables[lease])
             state.center_table[bucket * 2:(bucket + 1) * 2].copy_(self.center_pages[lease])
@@ -273,47 +303,57 @@ class PageArena:
         -> (tmp uint8 [n, 16, 8448], mapping int32 [n, 16, 64], centers uint8
         [n, 2, 8448]) for the (owner, bucket) pairs in order.  Errors are those of
         ``prepare``, raised at the same request (buckets before it are indexed)."""
-        pending = []
+        pend = _Pending()
         try:
             for owner, length in requests:
                 if not 0 <= length <= self.pages * 64:
                     raise ValueError("Index context capacity exceeded")
                 state = self.states.get(owner)
                 if state is not None and length < state.length:
-                    self._flush(pending, batch_source)
+                    self._flush(pend, batch_source)
                     self.release(owner)
                     state = None
                 if state is None:
                     if len(self.states) >= self.max_requests:
                         raise ValueError("V1 request capacity exceeded")
                     state = self._new_state(owner)
-                for bucket in range(len(state.leases), length // 1024):
-                    if not self.free_leases:
+                have, want = len(state.leases), length >> 10
+                if want > have:
+                    # leases are popped from the end of the free list, one per bucket
+                    free = self.free_leases
+                    n = min(want - have, len(free))
+                    if n:
+                        got = free[-n:]
+                        del free[-n:]
+                        got.reverse()
+                        state.leases.extend(got)
+                        pend.add(owner, have, got, state.row)
+                        self.unchecked.append((owner, have, got))
+                    if n < want - have:
                         raise RuntimeError("V1 bucket records exhausted")
-                    lease = self.free_leases.pop()
-                    state.leases.append(lease)
-                    pending.append((owner, bucket, lease, state.row))
-                    self.unchecked.append((owner, bucket, lease))
                 state.length = length
         except BaseException:
             # as prepare() does, the buckets granted before the error are indexed
-            self._flush(pending, batch_source)
+            self._flush(pend, batch_source)
             raise
-        self._flush(pending, batch_source)
+        self._flush(pend, batch_source)
 
-    def _flush(self, pending, batch_source):
-        """Index the pending buckets, 64 per call; each chunk leaves `pending`
+    def _flush(self, pend, batch_source):
+        """Index the pending buckets, 64 per call; each chunk leaves `pend`
         before its call, so no bucket is indexed twice."""
-        while pending:
-            chunk = pending[:BATCH_BUCKETS]
-            del pending[:BATCH_BUCKETS]
-            n = len(chunk)
-            tmp, mapping, centers = batch_source([(o, b) for o, b, _, _ in chunk])
-            self.staging.copy([x for _, b, lease, row in chunk for x in (b * 1024, lease, 1, row)], self.batch_meta)
+        if not pend.owners:
+            return
+        meta = pend.meta()
+        owners, buckets = pend.owners, pend.buckets
+        pend.clear()
+        for s in range(0, len(owners), BATCH_BUCKETS):
+            e = min(s + BATCH_BUCKETS, len(owners))
+            tmp, mapping, centers = batch_source(list(zip(owners[s:e], buckets[s:e])))
+            self.staging.copy(meta[4 * s:4 * e], self.batch_meta)
             tmp, mapping, centers = tmp.contiguous(), mapping.contiguous(), centers.contiguous()
             self.kernel_launches += 5
             _lib.call("v1x_prepare_buckets", _lib.ptr(tmp), _lib.ptr(centers), _lib.ptr(centers.view(torch.float32)),
-                      _lib.ptr(mapping), _lib.ptr(self.batch_meta), n, *self._arena_args(),
+                      _lib.ptr(mapping), _lib.ptr(self.batch_meta), e - s, *self._arena_args(),
                       torch.cuda.current_stream(self.device).cuda_stream, device=self.device)
 
     def _arena_args(self):
@@ -355,13 +395,15 @@ class PageArena:
             raise RuntimeError(f"v1x device status {code}")
 
     def _take_back_aborted(self, launched):
-        """Undo the host bookkeeping of the aborted suffix of `launched`."""
-        if not launched:
+        """Undo the host bookkeeping of the aborted suffix of `launched` (runs
+        (owner, first bucket, leases) in launch order)."""
+        flat = [(owner, b0 + i, lease) for owner, b0, leases in launched for i, lease in enumerate(leases)]
+        if not flat:
             return
-        rows = self.tables[torch.tensor([lease for _, _, lease in launched], device=self.device)].cpu()
+        rows = self.tables[torch.tensor([lease for _, _, lease in flat], device=self.device)].cpu()
         aborted = (rows < 0).all(dim=1).tolist()
-        first = next((i for i, a in enumerate(aborted) if a), len(launched))
-        for owner, bucket, lease in reversed(launched[first:]):
+        first = next((i for i, a in enumerate(aborted) if a), len(flat))
+        for owner, bucket, lease in reversed(flat[first:]):
             state = self.states.get(owner)
             if state is None or lease not in state.leases:
                 continue            # released since: the lease went back already

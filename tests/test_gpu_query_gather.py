@@ -193,3 +193,20 @@ def test_query_prepare_equals_metadata_then_staging(cuda_dev):
     assert np.array_equal(outs[0][0], outs[1][0])
     assert outs[0][0][4][1] == 0                       # the shared row points at row 0
     assert np.array_equal(outs[0][1], outs[1][1])
+
+
+def test_gather_latent_bulk_path_edges(cuda_dev):
+    """The single-output 576-wide path: a slot map (REQ), strided id rows, a
+    last row group of fewer than four rows, and negative ids."""
+    rng = np.random.default_rng(23)
+    slots, rows, top = 3000, 5, 1027
+    pool = torch.randn((slots, 1, 576), dtype=torch.bfloat16, device="cuda")
+    req = torch.as_tensor(rng.permutation(slots).astype(np.int32)).cuda()
+    ids_full = torch.as_tensor(rng.integers(-1, slots, size=(rows, top + 5)).astype(np.int32)).cuda()
+    ids = ids_full[:, :top]                      # row stride top + 5
+    out = torch.full((rows, top, 1, 576), 7.0, dtype=torch.bfloat16, device="cuda")
+    G._gather_impl((1,), pool, None, req, ids, out, None, rows, top, 0, *pool.stride(), IS0=ids_full.stride(0))
+    torch.cuda.synchronize()
+    e, _ = O.gather_slots(pool.view(torch.int16).cpu().numpy(), None, req.cpu().numpy(),
+                          ids.contiguous().cpu().numpy(), rows, top, 0)
+    assert np.array_equal(out.view(torch.int16).reshape(-1, 576).cpu().numpy(), e)
