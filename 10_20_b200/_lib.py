@@ -44,8 +44,8 @@ SIGNATURES = {
     "v1x_publish": [P, P, P, P, P, P, P, P, P, P, P, P, P, P],
     "v1x_release": [P, P, P, P, P],
     "v1x_release_many": [P, P, P, I64, P, P, P, P],
-    "v1x_prepare_buckets": [P, P, P, P, P, I64, P, P, P, P, P, P, P, P, P, P, P, P, P, P, I64, P, I64, I64, P, P,
-                            P],
+    "v1x_prepare_buckets": [P, P, P, P, P, P, I64, I64, P, P, P, P, P, P, P, P, P, P, P, P, P, P, I64, P, I64, I64,
+                            P, P, P],
     "v1x_query_metadata": [P, P, P, P, P, P, P, I64, I64, I64, I64, I64, I64, P, I64, P],
     "v1x_query_lengths": [P, P, P, I64, I64, I64, I64, I64, I64, P],
     "v1x_fine_table_shared": [P, P, I32, P, P, P, I64, I64, I64, I64, I64, I64, P],

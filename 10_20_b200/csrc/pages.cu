@@ -18,16 +18,18 @@
 //  - publish (:134-167), release (:170-179): as the reference, vectorised.
 //
 // Batched prepare (extension): the buckets of one or more prepares, in the
-// reference's canonical order, in five launches instead of six per bucket --
-// fingerprints of every page; ONE whole-GPU sweep of the arena that lists the
+// reference's canonical order, in six launches per call instead of six per
+// bucket -- the call's meta records (passed in the launch parameters) written
+// to the work array; fingerprints of every page; ONE whole-GPU sweep of the arena that lists the
 // live pages whose fingerprint equals a batch page's (a shared-memory hash
 // table of the batch's fingerprints: one probe per live arena page), and the
 // batch pages with an equal fingerprint in an earlier bucket; one warp per
 // listed pair comparing bytes and members, keeping the lowest live match and
-// the earliest equal batch page; one warp that takes the buckets in order and
-// makes the reference's sequential decisions from shared memory -- a page with
-// no live match takes the slot of its earliest equal batch page, fresh pages
-// pop the free stack as allocate does -- and one publish over all buckets.
+// the earliest equal batch page; one CTA (a thread per batch page) that makes
+// the reference's allocate decisions in closed form (decide_kernel) --
+// a page with no live match takes the slot of its earliest equal batch page,
+// fresh pages pop the free stack as allocate does -- and one publish over all
+// buckets.
 // The answers equal the sequential per-bucket calls: refcounts only grow during
 // a prepare, so a page live at the start stays live; a page content is live at
 // most once (a second copy would have matched the first -- given that a
@@ -38,6 +40,8 @@
 #include <algorithm>
 #include <climits>
 
+#include <cstring>
+
 #include "common.cuh"
 
 namespace v1x {
@@ -45,6 +49,15 @@ namespace {
 
 constexpr int kMaxMatchPages = 32;
 constexpr uint8_t kAborted = 2;  // new-page flag of a bucket whose allocation failed
+
+// Where bucket b of a call reads its tmp pages, members and centre pages:
+// source bucket src[b] of the pools (the identity when src is NULL; the host
+// checks the ids).
+struct BucketSrc {
+  const int32_t* src;
+  __device__ __forceinline__ int64_t bucket(int64_t b) const { return src ? src[b] : b; }
+  __device__ __forceinline__ int64_t page(int64_t p) const { return src ? bucket(p >> 4) * 16 + (p & 15) : p; }
+};
 
 // pages_per_meta: pages sharing one meta record of meta_stride ints (16 and 4
 // for a bucket batch; all pages and 3 for the single-bucket call); match, when
@@ -56,13 +69,14 @@ __global__ void __launch_bounds__(256) fingerprint_kernel(const uint8_t* __restr
                                                           int64_t* __restrict__ hash, int64_t pages_per_meta,
                                                           int meta_stride, int32_t* __restrict__ match,
                                                           int32_t* __restrict__ first,
-                                                          int32_t* __restrict__ counters) {
+                                                          int32_t* __restrict__ counters, const BucketSrc bs) {
   const int64_t p = blockIdx.x;
   if (match && threadIdx.x == 0) match[p] = INT_MAX;
   if (first && threadIdx.x == 0) first[p] = INT_MAX;
   if (counters && p == 0 && threadIdx.x < 4) counters[threadIdx.x] = 0;
   if (meta[(p / pages_per_meta) * meta_stride + 2] == 0) return;
-  const uint4* src = reinterpret_cast<const uint4*>(tmp + p * kPageBytes);
+  const int64_t sp = bs.page(p);
+  const uint4* src = reinterpret_cast<const uint4*>(tmp + sp * kPageBytes);
   // byte i = 16c + j of the page (j < 16): x_i * (i + 1) = x_i * 16c + x_i * (j + 1),
   // so per 16-byte chunk two byte dot products (dp4a) give sum x and sum x*(j+1);
   // sum x_i*(i+7) = sum x_i*(i+1) + 6 * sum x_i.  Partial sums stay in 32 bits
@@ -86,7 +100,7 @@ __global__ void __launch_bounds__(256) fingerprint_kernel(const uint8_t* __restr
   uint64_t a = s1;
   uint64_t b = (static_cast<uint64_t>(s1) + 6ull * s0) * 1000003ull;
   if (threadIdx.x < 64) {
-    const uint64_t m = static_cast<uint64_t>(static_cast<int64_t>(map[p * 64 + threadIdx.x]));
+    const uint64_t m = static_cast<uint64_t>(static_cast<int64_t>(map[sp * 64 + threadIdx.x]));
     a += m * 104729ull;
     b += m * (static_cast<uint64_t>(threadIdx.x) + 1) * 65537ull;
   }
@@ -220,16 +234,18 @@ __global__ void __launch_bounds__(256) publish_kernel(
     const int32_t* __restrict__ map, const int64_t* __restrict__ hash,
     const int32_t* __restrict__ meta, const int32_t* __restrict__ tables,
     const uint8_t* __restrict__ new_flags, uint8_t* __restrict__ fine, uint8_t* __restrict__ centers,
-    float* __restrict__ cs, int32_t* __restrict__ members, int64_t* __restrict__ hashes, int meta_stride) {
+    float* __restrict__ cs, int32_t* __restrict__ members, int64_t* __restrict__ hashes, int meta_stride,
+    const BucketSrc bs) {
   // block = (bucket, page): the single-bucket call launches 16 blocks
   const int64_t b = blockIdx.x / 16;
   const int p = blockIdx.x % 16;
   meta += b * meta_stride;
   if (meta[2] == 0) return;
-  tmp += b * 16 * kPageBytes;
-  tc += b * 2 * kPageBytes;
-  tcs += b * 2 * kPageWords;
-  map += b * 16 * 64;
+  const int64_t sb = bs.bucket(b);
+  tmp += sb * 16 * kPageBytes;
+  tc += sb * 2 * kPageBytes;
+  tcs += sb * 2 * kPageWords;
+  map += sb * 16 * 64;
   hash += b * 16 * 2;
   new_flags += b * 16;
   if (new_flags[p] == kAborted) return;  // allocation failed: the bucket changes nothing
@@ -280,7 +296,9 @@ constexpr int kBatchMeta = 4;                     // per bucket: token start, le
 constexpr int kPairCap = 4 * kBatchPages;         // hash-equal pairs kept per list
 // work ints: counters and flags, arena pairs, batch pairs, earliest equal page
 constexpr int kWorkHead = 4;
-constexpr int kWorkInts = kWorkHead + 2 * kPairCap + 2 * kPairCap + kBatchPages;
+constexpr int kMetaInts = kBatchBuckets * (kBatchMeta + 1);   // meta records, then source ids
+constexpr int kWorkMeta = kWorkHead + 4 * kPairCap + kBatchPages;
+constexpr int kWorkInts = kWorkMeta + kMetaInts;
 static_assert(kWorkInts == V1X_PREPARE_WORK_INTS, "v1x.h states the work size");
 constexpr int kFlagArenaOverflow = 1;
 constexpr int32_t kFirstNone = INT_MAX, kFirstCollision = -2;  // values of BatchWork::first
@@ -343,9 +361,9 @@ __device__ __forceinline__ int next_equal(const QueryTable& t, int& slot, int64_
 
 // The arena sweep with every hash hit confirmed by the warp that found it (the
 // exact path when the pair list overflows).
-__device__ void sweep_inline(const QueryTable& t, const uint8_t* tmp, const int32_t* map, const uint8_t* fine,
-                             const int32_t* members, const int64_t* hashes, const int32_t* refs, int32_t* match,
-                             int64_t cap) {
+__device__ void sweep_inline(const QueryTable& t, const uint8_t* tmp, const int32_t* map, const BucketSrc& bs,
+                             const uint8_t* fine, const int32_t* members, const int64_t* hashes, const int32_t* refs,
+                             int32_t* match, int64_t cap) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   const int64_t gw = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -367,8 +385,9 @@ __device__ void sweep_inline(const QueryTable& t, const uint8_t* tmp, const int3
         todo &= todo - 1;
         const int q = __shfl_sync(0xffffffffu, cand, src);
         const int64_t jc = base + src;
-        const bool eq = warp_pages_equal(tmp + static_cast<int64_t>(q) * kPageBytes, map + q * 64,
-                                         fine + jc * kPageBytes, members + jc * 64);
+        const int64_t sq = bs.page(q);
+        const bool eq = warp_pages_equal(tmp + sq * kPageBytes, map + sq * 64, fine + jc * kPageBytes,
+                                         members + jc * 64);
         if (eq && lane == 0) atomicMin(&match[q], static_cast<int32_t>(jc));
       }
     }
@@ -422,7 +441,8 @@ __global__ void __launch_bounds__(256) confirm_kernel(const uint8_t* __restrict_
                                                       const int32_t* __restrict__ members,
                                                       const int64_t* __restrict__ hashes,
                                                       const int32_t* __restrict__ refs, int32_t* __restrict__ match,
-                                                      int64_t cap, int nq, int32_t* __restrict__ work) {
+                                                      int64_t cap, int nq, int32_t* __restrict__ work,
+                                                      const BucketSrc bs) {
   BatchWork w(work);
   const int flags = w.head[2];
   const int lane = threadIdx.x & 31;
@@ -432,19 +452,20 @@ __global__ void __launch_bounds__(256) confirm_kernel(const uint8_t* __restrict_
   if (flags & kFlagArenaOverflow) {
     __shared__ QueryTable t;
     build_query_table(t, hash, meta, nq);
-    sweep_inline(t, tmp, map, fine, members, hashes, refs, match, cap);
+    sweep_inline(t, tmp, map, bs, fine, members, hashes, refs, match, cap);
   } else {
     for (int64_t k = gw; k < na; k += warps) {
       const int2 pr = w.arena[k];
-      const bool eq = warp_pages_equal(tmp + static_cast<int64_t>(pr.y) * kPageBytes, map + pr.y * 64,
+      const int64_t sy = bs.page(pr.y);
+      const bool eq = warp_pages_equal(tmp + sy * kPageBytes, map + sy * 64,
                                        fine + static_cast<int64_t>(pr.x) * kPageBytes, members + pr.x * 64);
       if (eq && lane == 0) atomicMin(&match[pr.y], pr.x);
     }
   }
   for (int64_t k = gw; k < nb; k += warps) {
     const int2 pr = w.batch[k];
-    const bool eq = warp_pages_equal(tmp + static_cast<int64_t>(pr.y) * kPageBytes, map + pr.y * 64,
-                                     tmp + static_cast<int64_t>(pr.x) * kPageBytes, map + pr.x * 64);
+    const int64_t sy = bs.page(pr.y), sx = bs.page(pr.x);
+    const bool eq = warp_pages_equal(tmp + sy * kPageBytes, map + sy * 64, tmp + sx * kPageBytes, map + sx * 64);
     if (lane == 0) w.first[pr.y] = eq ? pr.x : kFirstCollision;
   }
 }
@@ -486,7 +507,7 @@ __global__ void __launch_bounds__(kDecideThreads) decide_kernel(
     const int32_t* __restrict__ meta, const int32_t* __restrict__ match, int nb, const int32_t* __restrict__ free_stack,
     int32_t* __restrict__ count, int32_t* __restrict__ refs, int32_t* __restrict__ tables,
     uint8_t* __restrict__ new_flags, int32_t* __restrict__ status, const StateRows rows,
-    const int32_t* __restrict__ work) {
+    const int32_t* __restrict__ work, const BucketSrc bs) {
   __shared__ int64_t sh0[kBatchPages], sh1[kBatchPages];
   __shared__ int32_t ssrc[kBatchPages];      // earliest equal page of an earlier bucket, or -1
   __shared__ int32_t sfree[kBatchPages];     // sfree[i] = FREE[count0 - 1 - i]
@@ -533,8 +554,8 @@ __global__ void __launch_bounds__(kDecideThreads) decide_kernel(
       while (todo && found < 0) {
         const int pc = p0 + __ffs(todo) - 1;
         todo &= todo - 1;
-        if (warp_pages_equal(tmp + static_cast<int64_t>(qc) * kPageBytes, map + qc * 64,
-                             tmp + static_cast<int64_t>(pc) * kPageBytes, map + pc * 64))
+        const int64_t sq = bs.page(qc), sc = bs.page(pc);
+        if (warp_pages_equal(tmp + sq * kPageBytes, map + sq * 64, tmp + sc * kPageBytes, map + sc * 64))
           found = pc;
       }
     }
@@ -630,6 +651,16 @@ __global__ void __launch_bounds__(kReleaseThreads) release_many_kernel(
   if (threadIdx.x == 0) *count = cnt;
 }
 
+// The call's meta records and source ids travel in the launch parameters; this
+// kernel writes them to the work array, where the other kernels read them.
+struct MetaBlock {
+  int32_t v[kMetaInts];
+};
+
+__global__ void meta_upload_kernel(const __grid_constant__ MetaBlock mb, int32_t* __restrict__ dst, int n) {
+  for (int i = threadIdx.x; i < n; i += blockDim.x) dst[i] = mb.v[i];
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 // Host-side offsets into the work array (as BatchWork on the device).
@@ -649,7 +680,8 @@ extern "C" int v1x_fingerprint(const uint8_t* tmp, const int32_t* map, const int
   V1X_CHECK_ARG(n_pages >= 0 && aligned16(tmp), "fingerprint: tmp must be 16-byte aligned");
   if (n_pages == 0) return V1X_OK;
   fingerprint_kernel<<<static_cast<unsigned>(n_pages), 256, 0, as_stream(stream)>>>(tmp, map, meta, hash, n_pages, 3,
-                                                                                 nullptr, nullptr, nullptr);
+                                                                                 nullptr, nullptr, nullptr,
+                                                                                 BucketSrc{nullptr});
   return launch_status("v1x_fingerprint");
 }
 
@@ -697,7 +729,7 @@ extern "C" int v1x_publish(const uint8_t* tmp, const uint8_t* tc_bytes, const fl
                 "publish: page pools must be 16-byte aligned");
   publish_kernel<<<16, 256, 0, as_stream(stream)>>>(tmp, tc_bytes, tc_scales, map, hash, meta, tables,
                                                     new_flags, fine, centers, center_scales, members,
-                                                    hashes, 3);
+                                                    hashes, 3, BucketSrc{nullptr});
   return launch_status("v1x_publish");
 }
 
@@ -710,7 +742,8 @@ extern "C" int v1x_release(const int32_t* table, int32_t* refs, int32_t* free_st
 }
 
 extern "C" int v1x_prepare_buckets(const uint8_t* tmp, const uint8_t* tc_bytes, const float* tc_scales,
-                                   const int32_t* map, const int32_t* meta, int64_t buckets, int64_t* hash,
+                                   const int32_t* map, const int32_t* meta_host, const int32_t* src_host,
+                                   int64_t src_buckets, int64_t buckets, int64_t* hash,
                                    int32_t* match, uint8_t* new_flags, uint8_t* fine, uint8_t* centers,
                                    float* center_scales, int32_t* members, int64_t* hashes, int32_t* refs,
                                    int32_t* free_stack, int32_t* count, int32_t* tables,
@@ -721,21 +754,37 @@ extern "C" int v1x_prepare_buckets(const uint8_t* tmp, const uint8_t* tc_bytes, 
   clear_error();
   V1X_CHECK_ARG(buckets >= 0 && buckets <= kBatchBuckets, "prepare_buckets: at most %d buckets per call",
                 kBatchBuckets);
-  V1X_CHECK_ARG(tmp && tc_bytes && tc_scales && map && meta && hash && match && new_flags && fine && centers &&
+  V1X_CHECK_ARG(tmp && tc_bytes && tc_scales && map && meta_host && hash && match && new_flags && fine && centers &&
                     center_scales && members && hashes && refs && free_stack && count && tables,
                 "prepare_buckets: a required buffer is NULL");
   V1X_CHECK_ARG(cap > 0 && cap < INT_MAX, "prepare_buckets: bad capacity");
+  V1X_CHECK_ARG(!src_host || (src_buckets > 0 && src_buckets < INT_MAX),
+                "prepare_buckets: src needs src_buckets > 0");
   V1X_CHECK_ARG(aligned16(tmp) && aligned16(fine) && aligned16(tc_bytes) && aligned16(centers),
                 "prepare_buckets: page pools must be 16-byte aligned");
   V1X_CHECK_ARG(!state_tables || (state_centers && center_pages && state_table_stride >= 16 &&
                                   state_center_stride >= 2),
                 "prepare_buckets: state rows need both tables, the centre pages and their strides");
   if (buckets == 0) return V1X_OK;
+  V1X_CHECK_ARG(work != nullptr, "prepare_buckets: work (V1X_PREPARE_WORK_INTS ints) is required");
+  // the host meta records and source ids, into the launch parameters
+  MetaBlock mb;
+  const int nm = static_cast<int>(buckets) * kBatchMeta;
+  std::memcpy(mb.v, meta_host, sizeof(int32_t) * nm);
+  if (src_host) {
+    for (int64_t b = 0; b < buckets; ++b)
+      V1X_CHECK_ARG(src_host[b] >= 0 && src_host[b] < src_buckets,
+                    "prepare_buckets: source id %d of bucket %lld outside [0, %lld)", src_host[b],
+                    static_cast<long long>(b), static_cast<long long>(src_buckets));
+    std::memcpy(mb.v + nm, src_host, sizeof(int32_t) * buckets);
+  }
   cudaStream_t s = as_stream(stream);
   const int nq = static_cast<int>(buckets) * 16;
-  V1X_CHECK_ARG(work != nullptr, "prepare_buckets: work (V1X_PREPARE_WORK_INTS ints) is required");
   BatchWorkHost wh(work);
-  fingerprint_kernel<<<nq, 256, 0, s>>>(tmp, map, meta, hash, 16, kBatchMeta, match, wh.first, wh.head);
+  int32_t* meta = work + kWorkMeta;
+  const BucketSrc bs{src_host ? meta + nm : nullptr};
+  meta_upload_kernel<<<1, 128, 0, s>>>(mb, meta, nm + (src_host ? static_cast<int>(buckets) : 0));
+  fingerprint_kernel<<<nq, 256, 0, s>>>(tmp, map, meta, hash, 16, kBatchMeta, match, wh.first, wh.head, bs);
   int64_t blocks = (cap + 255) / 256;
   const int64_t maxb = static_cast<int64_t>(num_sms()) * 4;
   if (blocks > maxb) blocks = maxb;
@@ -744,12 +793,12 @@ extern "C" int v1x_prepare_buckets(const uint8_t* tmp, const uint8_t* tc_bytes, 
   const int64_t sweep_blocks = std::min<int64_t>((cap + 1023) / 1024, num_sms());
   match_batch_kernel<<<static_cast<unsigned>(sweep_blocks), 1024, 0, s>>>(hash, meta, hashes, refs, cap, nq, work);
   confirm_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(tmp, map, hash, meta, fine, members, hashes, refs,
-                                                                match, cap, nq, work);
+                                                                match, cap, nq, work, bs);
   const StateRows rows{state_tables, state_table_stride, state_centers, state_center_stride, center_pages};
   decide_kernel<<<1, kDecideThreads, 0, s>>>(tmp, map, hash, meta, match, static_cast<int>(buckets), free_stack,
-                                           count, refs, tables, new_flags, status, rows, work);
+                                           count, refs, tables, new_flags, status, rows, work, bs);
   publish_kernel<<<nq, 256, 0, s>>>(tmp, tc_bytes, tc_scales, map, hash, meta, tables, new_flags, fine, centers,
-                                    center_scales, members, hashes, kBatchMeta);
+                                    center_scales, members, hashes, kBatchMeta, bs);
   return launch_status("v1x_prepare_buckets");
 }
 

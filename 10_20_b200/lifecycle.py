@@ -31,7 +31,7 @@ recorded in the device status word (the reference traps) and raised by
 
 ``prepare_many`` (an extension) prepares several requests at once: all their
 new buckets, in the same canonical order, go through ``v1x_prepare_buckets``
-(up to 64 buckets per call, five launches per call), which also writes the
+(up to 64 buckets per call, six launches per call), which also writes the
 requests' page-table rows.  The arena afterwards equals that of ``prepare``
 called for each request in turn.  Request tables live as rows of one arena
 tensor, so a batch updates them without per-request copies.  ``release_many``
@@ -39,6 +39,8 @@ releases several requests in one launch (``v1x_release_many``), with the arena
 state of ``release`` called for each in turn.
 """
 from __future__ import annotations
+
+import itertools
 
 import numpy as np
 import torch
@@ -48,7 +50,7 @@ from . import kernels as K
 
 PAGE_BYTES = 8448
 BATCH_BUCKETS = 64      # buckets per v1x_prepare_buckets call
-PREPARE_WORK_INTS = 4 + 4 * 4096 + 1024   # V1X_PREPARE_WORK_INTS
+PREPARE_WORK_INTS = 4 + 4 * 4096 + 1024 + 64 * 5   # V1X_PREPARE_WORK_INTS
 
 
 class HostStaging:
@@ -84,44 +86,30 @@ class HostStaging:
 
 
 class State:
-    """A request's index state (reference State, DS/runtime.py:681-690).  The
-    tables are given views (rows of the arena's tensors) or allocated here."""
+    """A request's index state (reference State, DS/runtime.py:681-690): its
+    leases, indexed length and arena row; ``table`` / ``center_table`` are that
+    row of the arena's request tables (views made on first use)."""
 
-    def __init__(self, pages: int, device, table=None, center_table=None, row: int = -1):
-        self.table = torch.zeros(pages, dtype=torch.int32, device=device) if table is None else table
-        self.center_table = (torch.zeros(pages // 8, dtype=torch.int32, device=device) if center_table is None
-                             else center_table)
+    __slots__ = ("arena", "row", "leases", "length", "_views")
+
+    def __init__(self, arena: "PageArena", row: int):
+        self.arena, self.row = arena, row
         self.leases: list[int] = []
         self.length = 0
-        self.row = row
+        self._views = None
 
+    def _view(self, i):
+        if self._views is None:
+            self._views = (self.arena.state_tables[self.row], self.arena.state_centers[self.row])
+        return self._views[i]
 
-class _Pending:
-    """The buckets a batched prepare will index, as flat lists in launch order:
-    owner, bucket, lease, and the owner's request-table row."""
+    @property
+    def table(self):
+        return self._view(0)
 
-    def __init__(self):
-        self.clear()
-
-    def clear(self):
-        self.owners, self.buckets, self.leases, self.rows = [], [], [], []
-
-    def add(self, owner, first, leases, row):
-        n = len(leases)
-        self.owners.extend([owner] * n)
-        self.buckets.extend(range(first, first + n))
-        self.leases.extend(leases)
-        self.rows.extend([row] * n)
-
-    def meta(self):
-        """v1x_prepare_buckets' meta records, flat: (start token, lease, 1, row)."""
-        m = np.empty((len(self.owners), 4), dtype=np.int32)
-        m[:, 0] = self.buckets
-        m[:, 0] *= 1024
-        m[:, 1] = self.leases
-        m[:, 2] = 1
-        m[:, 3] = self.rows
-        return m.reshape(-1)
+    @property
+    def center_table(self):
+        return self._view(1)
 
 
 class PageArena:
@@ -165,20 +153,20 @@ class PageArena:
         self.state_centers = torch.zeros((self.max_requests, pages // 8), dtype=torch.int32, device=d)
         self.free_rows = list(range(self.max_requests - 1, -1, -1))
         self.kernel_launches = 0   # kernels this driver has launched (reported by the bench)
-        # (owner, first bucket, leases) of every run of consecutive buckets of one
-        # request launched since the last check(), in launch order: an exhaustion
-        # aborts a suffix of the buckets
+        # (owner, first bucket, leases, ...) of every run of consecutive buckets
+        # of one request launched since the last check(), in launch order: an
+        # exhaustion aborts a suffix of the buckets
         self.unchecked: list = []
         self._prepare_args = None
+        self._source_key = self._source_val = None
         # batched prepare: meta records and per-page scratch of one call
-        self.batch_meta = torch.zeros((BATCH_BUCKETS, 4), dtype=torch.int32, device=d)
         self.batch_hash = torch.zeros((BATCH_BUCKETS * 16, 2), dtype=torch.int64, device=d)
         self.batch_match = torch.zeros(BATCH_BUCKETS * 16, dtype=torch.int32, device=d)
         self.batch_new = torch.zeros(BATCH_BUCKETS * 16, dtype=torch.uint8, device=d)
         self.batch_work = torch.zeros(PREPARE_WORK_INTS, dtype=torch.int32, device=d)
         # release_many's leases, offsets and the released requests' table rows
         self.release_idx = torch.zeros(self.max_leases + 2 * self.max_requests + 1, dtype=torch.int32, device=d)
-        self.staging = HostStaging(max(BATCH_BUCKETS * 4, self.release_idx.numel()), d) if d.type == "cuda" else None
+        self.staging = HostStaging(self.release_idx.numel(), d) if d.type == "cuda" else None
 
     # -- one bucket ------------------------------------------------------------
     def _kernels(self, tmp, mapping, centers):
@@ -292,8 +280,7 @@ class PageArena:
 
     def _new_state(self, owner):
         row = self.free_rows.pop()     # zeroed when it was freed (or never used)
-        state = self.states[owner] = State(self.pages, self.device, self.state_tables[row], self.state_centers[row],
-                                           row)
+        state = self.states[owner] = State(self, row)
         return state
 
     # -- several requests at once (extension) ----------------------------------
@@ -301,60 +288,91 @@ class PageArena:
         """``prepare(owner, length)`` for every (owner, length) of `requests`, in
         order, with all new buckets indexed by batched calls.  batch_source(pairs)
         -> (tmp uint8 [n, 16, 8448], mapping int32 [n, 16, 64], centers uint8
-        [n, 2, 8448]) for the (owner, bucket) pairs in order.  Errors are those of
+        [n, 2, 8448]) for the (owner, bucket) pairs in order, or -> (tmp, mapping,
+        centers, ids): pools of bucket contents and, per pair, the index of its
+        entry (read in place, nothing is copied).  Errors are those of
         ``prepare``, raised at the same request (buckets before it are indexed)."""
-        pend = _Pending()
+        runs = []        # (owner, first bucket, leases, state row) to index, in order
+        states, free = self.states, self.free_leases
+        limit = self.pages * 64
         try:
             for owner, length in requests:
-                if not 0 <= length <= self.pages * 64:
+                if not 0 <= length <= limit:
                     raise ValueError("Index context capacity exceeded")
-                state = self.states.get(owner)
-                if state is not None and length < state.length:
-                    self._flush(pend, batch_source)
-                    self.release(owner)
-                    state = None
-                if state is None:
-                    if len(self.states) >= self.max_requests:
+                state = states.get(owner)
+                if state is None or length < state.length:
+                    if state is not None:
+                        self._flush(runs, batch_source)
+                        self.release(owner)
+                    if len(states) >= self.max_requests:
                         raise ValueError("V1 request capacity exceeded")
                     state = self._new_state(owner)
-                have, want = len(state.leases), length >> 10
-                if want > have:
+                have = len(state.leases)
+                n = (length >> 10) - have
+                if n > 0:
                     # leases are popped from the end of the free list, one per bucket
-                    free = self.free_leases
-                    n = min(want - have, len(free))
-                    if n:
-                        got = free[-n:]
-                        del free[-n:]
+                    k = min(n, len(free))
+                    if k:
+                        got = free[-k:]
+                        del free[-k:]
                         got.reverse()
-                        state.leases.extend(got)
-                        pend.add(owner, have, got, state.row)
-                        self.unchecked.append((owner, have, got))
-                    if n < want - have:
+                        state.leases += got
+                        run = (owner, have, got, state.row)
+                        runs.append(run)
+                        self.unchecked.append(run)
+                    if k < n:
                         raise RuntimeError("V1 bucket records exhausted")
                 state.length = length
         except BaseException:
             # as prepare() does, the buckets granted before the error are indexed
-            self._flush(pend, batch_source)
+            self._flush(runs, batch_source)
             raise
-        self._flush(pend, batch_source)
+        self._flush(runs, batch_source)
 
-    def _flush(self, pend, batch_source):
-        """Index the pending buckets, 64 per call; each chunk leaves `pend`
-        before its call, so no bucket is indexed twice."""
-        if not pend.owners:
+    def _flush(self, runs, batch_source):
+        """Index the buckets of `runs` (emptied first, so none is indexed twice),
+        64 per call."""
+        if not runs:
             return
-        meta = pend.meta()
-        owners, buckets = pend.owners, pend.buckets
-        pend.clear()
-        for s in range(0, len(owners), BATCH_BUCKETS):
-            e = min(s + BATCH_BUCKETS, len(owners))
-            tmp, mapping, centers = batch_source(list(zip(owners[s:e], buckets[s:e])))
-            self.staging.copy(meta[4 * s:4 * e], self.batch_meta)
-            tmp, mapping, centers = tmp.contiguous(), mapping.contiguous(), centers.contiguous()
-            self.kernel_launches += 5
-            _lib.call("v1x_prepare_buckets", _lib.ptr(tmp), _lib.ptr(centers), _lib.ptr(centers.view(torch.float32)),
-                      _lib.ptr(mapping), _lib.ptr(self.batch_meta), e - s, *self._arena_args(),
-                      torch.cuda.current_stream(self.device).cuda_stream, device=self.device)
+        todo = runs[:]
+        runs.clear()
+        cnt = np.fromiter((len(r[2]) for r in todo), dtype=np.int64, count=len(todo))
+        total = int(cnt.sum())
+        pairs = [(o, b0 + i) for o, b0, leases, _ in todo for i in range(len(leases))]
+        # meta records (start token, lease, 1, state row), then per chunk the source ids
+        meta = np.empty((total, 4), dtype=np.int32)
+        first = np.repeat(np.fromiter((r[1] for r in todo), dtype=np.int64, count=len(todo)) - (np.cumsum(cnt) - cnt),
+                          cnt)
+        meta[:, 0] = (first + np.arange(total)) * 1024
+        meta[:, 1] = np.fromiter(itertools.chain.from_iterable(r[2] for r in todo), dtype=np.int32, count=total)
+        meta[:, 2] = 1
+        meta[:, 3] = np.repeat(np.fromiter((r[3] for r in todo), dtype=np.int32, count=len(todo)), cnt)
+        mp = meta.ctypes.data          # host records: they travel in the launch parameters
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        for s in range(0, total, BATCH_BUCKETS):
+            e = min(s + BATCH_BUCKETS, total)
+            got = batch_source(pairs[s:e])
+            if len(got) == 4:   # pools + the pairs' entries
+                ids = np.asarray(got[3], dtype=np.int32)
+                src, nsrc = ids.ctypes.data, got[0].shape[0]
+            else:
+                src, nsrc = None, 0
+            self.kernel_launches += 6
+            _lib.call("v1x_prepare_buckets", *self._source_ptrs(got), mp + 16 * s, src, nsrc, e - s,
+                      *self._arena_args(), stream, device=self.device)
+
+    def _source_ptrs(self, got):
+        """(tmp, centre bytes, centre floats, mapping) pointers of a batch
+        source's tensors; a pool source hands over the same tensors every call,
+        so their pointers are kept."""
+        key = self._source_key
+        if key is not None and got[0] is key[0] and got[1] is key[1] and got[2] is key[2]:
+            return self._source_val
+        tmp, mapping, centers = (x.contiguous() for x in got[:3])
+        val = (_lib.ptr(tmp), _lib.ptr(centers), _lib.ptr(centers.view(torch.float32)), _lib.ptr(mapping))
+        if len(got) == 4:
+            self._source_key, self._source_val = (got[0], got[1], got[2]), val
+        return val
 
     def _arena_args(self):
         """v1x_prepare_buckets' arguments after `buckets` up to `status`: the
@@ -396,8 +414,8 @@ class PageArena:
 
     def _take_back_aborted(self, launched):
         """Undo the host bookkeeping of the aborted suffix of `launched` (runs
-        (owner, first bucket, leases) in launch order)."""
-        flat = [(owner, b0 + i, lease) for owner, b0, leases in launched for i, lease in enumerate(leases)]
+        (owner, first bucket, leases, ...) in launch order)."""
+        flat = [(run[0], run[1] + i, lease) for run in launched for i, lease in enumerate(run[2])]
         if not flat:
             return
         rows = self.tables[torch.tensor([lease for _, _, lease in flat], device=self.device)].cpu()

@@ -255,3 +255,9 @@ class LifecycleWorkload:
             ids = staging.copy([self.chains[o][b] for o, b in pairs], ids_dev)[:len(pairs)]
             return tmp.index_select(0, ids), mapping.index_select(0, ids), centers.index_select(0, ids)
         return fetch
+
+    def pool_source(self, contents):
+        """batch_source(pairs) for PageArena.prepare_many that hands over the
+        materialised contents as pools with each pair's entry (read in place)."""
+        tmp, mapping, centers = contents
+        return lambda pairs: (tmp, mapping, centers, [self.chains[o][b] for o, b in pairs])

@@ -455,7 +455,8 @@ def run_pages_workload(args, world, rank, device, dist):
     cap, pages, requests = 131072, 2048, 256
     wl = synth.LifecycleWorkload(requests, 128, 8, 31 + rank, cap // 16, share=0.5, grow=8)
     contents = wl.contents(device)
-    src, bsrc = wl.source(contents), wl.batch_source(contents)
+    # the batched driver reads bucket contents in place from the content pool
+    src, bsrc = wl.source(contents), wl.pool_source(contents)
 
     def run_round(arena, ops, batched):
         """One round of operations; batched: consecutive prepares as one
@@ -494,12 +495,6 @@ def run_pages_workload(args, world, rank, device, dist):
         flush_rel()
         return nb
 
-    # warm-up of the workload's own gather of bucket contents (torch index_select
-    # picks a different kernel for up to 16 indices; its first use costs ~50 ms)
-    any_owner = next(iter(wl.chains))
-    for k in (1, 17, 64):
-        bsrc([(any_owner, 0)] * k)
-    torch.cuda.synchronize()
 
     def timed_rounds(batched):
         arena = lifecycle.PageArena(cap, pages, device, max_requests=requests, graphs=not batched)
@@ -545,7 +540,7 @@ def run_pages_workload(args, world, rank, device, dist):
     small = synth.LifecycleWorkload(12, 6, 3, 5, 4096 // 16, share=0.6, grow=3)
     sc = small.contents(device)
     ca = port.ArenaPort(4096, 128, max_requests=16)
-    sg, sb, scpu = small.source(sc), small.batch_source(sc), small.source(tuple(x.cpu().numpy() for x in sc))
+    sg, sb, scpu = small.source(sc), small.pool_source(sc), small.source(tuple(x.cpu().numpy() for x in sc))
     parity = True
     for batched in (False, True):
         ga = lifecycle.PageArena(4096, 128, device, max_requests=16, graphs=True)
@@ -600,7 +595,8 @@ def run_pages_workload(args, world, rank, device, dist):
                             "rounds_timed": len(wl.ops) - 1, "buckets_timed": buckets, "share": 0.5,
                             "bytes_per_bucket": per_bucket,
                             "driver": "prepare_many / release_many: consecutive prepares batched through "
-                                      "v1x_prepare_buckets (<= 64 buckets, 5 launches per call), consecutive "
+                                      "v1x_prepare_buckets (<= 64 buckets, 6 launches per call, bucket contents read in place "
+                                      "from the content pool), consecutive "
                                       "releases through v1x_release_many (1 launch)"},
                            per_bucket * buckets, "confirm_kernel + publish", 5, cpu, parity)
     line["steps"] = len(wl.ops) - 1

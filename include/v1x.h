@@ -350,17 +350,23 @@ V1X_API int v1x_release(const int32_t* table, int32_t* refs, int32_t* free_stack
                 void* stream);
 
 /* Scratch of v1x_prepare_buckets, in int32 words: 4 counters/flags, two lists of
- * 4096 fingerprint-equal pairs (int32 x 2 each), 1024 earliest-equal entries. */
-#define V1X_PREPARE_WORK_INTS (4 + 4 * 4096 + 1024)
+ * 4096 fingerprint-equal pairs (int32 x 2 each), 1024 earliest-equal entries,
+ * the call's 64 meta records and source ids. */
+#define V1X_PREPARE_WORK_INTS (4 + 4 * 4096 + 1024 + 64 * 5)
 
 /* Extension (no reference counterpart): the page part of Build.compute
  * (DS/runtime.py:230-270: fingerprint -> match_pages -> allocate -> publish,
  * DS/kernels.py:57-167) for up to 64 buckets in canonical order, in five
  * launches instead of six per bucket.  The arena state afterwards equals that
  * of the per-bucket calls in the same order.
- * tmp u8 [buckets, 16, 8448]; tc_bytes u8 / tc_scales f32 [buckets, 2, 8448]
- * (byte and float views); map i32 [buckets, 16, 64]; meta i32 [buckets, 4] =
- * (token start, lease, active, state row); scratch: hash i64 [buckets*16, 2],
+ * tmp u8 [*, 16, 8448]; tc_bytes u8 / tc_scales f32 [*, 2, 8448] (byte and
+ * float views); map i32 [*, 16, 64]; bucket b reads entry src[b] of these
+ * (src: a HOST i32 array [buckets], each id checked to lie in [0,
+ * src_buckets)) or entry b when src is NULL, so a caller holding bucket
+ * contents in a pool passes their ids instead of copying them; meta: a HOST
+ * i32 array [buckets, 4] = (token start, lease, active, state row).  meta and
+ * src travel in the launch parameters (no host -> device copy precedes the
+ * call).  Scratch: hash i64 [buckets*16, 2],
  * match i32 [buckets*16], new_flags u8 [buckets*16], work i32
  * [V1X_PREPARE_WORK_INTS] (no initial contents needed).  Arena arrays as in
  * v1x_match_pages / v1x_allocate / v1x_publish; center_pages i32 [leases, 2].
@@ -390,7 +396,8 @@ V1X_API int v1x_release_many(const int32_t* tables, const int32_t* leases, const
                      void* stream);
 
 V1X_API int v1x_prepare_buckets(const uint8_t* tmp, const uint8_t* tc_bytes, const float* tc_scales,
-                        const int32_t* map, const int32_t* meta, int64_t buckets, int64_t* hash,
+                        const int32_t* map, const int32_t* meta, const int32_t* src, int64_t src_buckets,
+                        int64_t buckets, int64_t* hash,
                         int32_t* match, uint8_t* new_flags, uint8_t* fine, uint8_t* centers,
                         float* center_scales, int32_t* members, int64_t* hashes, int32_t* refs,
                         int32_t* free_stack, int32_t* count, int32_t* tables,

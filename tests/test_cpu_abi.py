@@ -64,11 +64,13 @@ def test_batched_lifecycle_rejects_bad_arguments_before_any_launch(v1x):
     _lib = import_module("10_20_b200._lib")
     lib = _lib.lib()
     nulls = [None] * 5
-    rc = lib.v1x_prepare_buckets(*nulls, 1, *([None] * 14), 16, None, 2, 4096, None, None, None)
+    rc = lib.v1x_prepare_buckets(*nulls, None, 0, 1, *([None] * 14), 16, None, 2, 4096, None, None, None)
     assert rc == _lib.V1X_ERR_INVALID
     assert b"NULL" in lib.v1x_last_error()
-    rc = lib.v1x_prepare_buckets(*nulls, 65, *([None] * 14), 16, None, 2, 4096, None, None, None)
+    rc = lib.v1x_prepare_buckets(*nulls, None, 0, 65, *([None] * 14), 16, None, 2, 4096, None, None, None)
     assert rc == _lib.V1X_ERR_INVALID and b"at most 64 buckets" in lib.v1x_last_error()
+    rc = lib.v1x_prepare_buckets(*([1] * 5), 16, 0, 1, *([16] * 14), 16, None, 2, 4096, None, None, None)
+    assert rc == _lib.V1X_ERR_INVALID and b"src_buckets" in lib.v1x_last_error()
     rc = lib.v1x_release_many(None, None, None, 3, None, None, None, None)
     assert rc == _lib.V1X_ERR_INVALID and b"NULL" in lib.v1x_last_error()
     assert lib.v1x_release_many(None, None, None, 0, None, None, None, None) == _lib.V1X_OK

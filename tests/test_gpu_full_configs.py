@@ -155,7 +155,7 @@ def test_d3_lifecycle_full_arena(cuda_dev):
     cpu = port.ArenaPort(cap, pages, max_requests=requests)
     per_bucket = lifecycle.PageArena(cap, pages, "cuda", max_requests=requests, graphs=True)
     batched = lifecycle.PageArena(cap, pages, "cuda", max_requests=requests)
-    src_gpu, bsrc, src_cpu = wl.source(contents), wl.batch_source(contents), wl.source(host)
+    src_gpu, bsrc, src_cpu = wl.source(contents), wl.pool_source(contents), wl.source(host)
     buckets = shared = 0
     for k, ops in enumerate(wl.ops):
         prep, rel = [], []

@@ -79,11 +79,13 @@ def test_lifecycle_limits(cuda_dev):
     assert int(arena.free_count.item()) == 32 and bool((arena.refs == 0).all())
 
 
-def _rounds_batched(gpu, cpu, wl, contents, host):
+def _rounds_batched(gpu, cpu, wl, contents, host, pool=False):
     """Each round's consecutive prepares as one prepare_many call and its
     consecutive releases as one release_many call; the CPU port takes the same
-    operations one by one."""
-    bsrc, src_cpu = wl.batch_source(contents), wl.source(host)
+    operations one by one.  pool: the bucket contents are read in place from
+    the content pool (source ids) instead of copied out per call."""
+    bsrc = wl.pool_source(contents) if pool else wl.batch_source(contents)
+    src_cpu = wl.source(host)
     for ops in wl.ops:
         prep, rel = [], []
         for op in ops + [("end",)]:
@@ -104,8 +106,8 @@ def _rounds_batched(gpu, cpu, wl, contents, host):
         _compare(gpu, cpu)
 
 
-@pytest.mark.parametrize("requests,grow", [(10, 3), (40, 4)])
-def test_prepare_many_matches_cpu_port(requests, grow, cuda_dev):
+@pytest.mark.parametrize("requests,grow,pool", [(10, 3, False), (40, 4, False), (40, 4, True)])
+def test_prepare_many_matches_cpu_port(requests, grow, pool, cuda_dev):
     """Batched prepare (extension) == the reference's per-bucket sequence: every
     arena array and request table after every round.  (40, 4) puts more than 64
     buckets in a round (several calls); shared prefixes give matches both
@@ -117,7 +119,7 @@ def test_prepare_many_matches_cpu_port(requests, grow, cuda_dev):
     host = tuple(x.cpu().numpy() for x in contents)
     gpu = lifecycle.PageArena(cap, pages, "cuda", max_requests=64)
     cpu = port.ArenaPort(cap, pages, max_requests=64)
-    _rounds_batched(gpu, cpu, wl, contents, host)
+    _rounds_batched(gpu, cpu, wl, contents, host, pool)
     assert (cpu.refs > 1).sum() > 0
 
 
@@ -281,7 +283,8 @@ def test_prepare_buckets_entry_point_random_batches(seed, cuda_dev):
     inactive buckets, pages live before the call, pages published earlier in the
     call, fingerprint collisions and (some seeds) a short free stack, against the
     numpy restatement of the batched algorithm -- which the CPU tests tie to the
-    reference's per-bucket sequence."""
+    reference's per-bucket sequence.  Seeds 2-3 pass the bucket contents as ids
+    into a shuffled pool (src)."""
     import copy
 
     import oracle.v1x_oracle as O
@@ -332,15 +335,27 @@ def test_prepare_buckets_entry_point_random_batches(seed, cuda_dev):
     for name in ("refs", "free", "tables", "members", "hashes", "fine", "centers"):
         getattr(gpu, name).copy_(torch.from_numpy(np.ascontiguousarray(getattr(cpu, name))))
     gpu.free_count.fill_(cpu.count)
-    meta = torch.tensor([[b * 1024, 3 + b, active[b], 0] for b in range(nb)], dtype=torch.int32, device="cuda")
+    meta = np.array([[b * 1024, 3 + b, active[b], 0] for b in range(nb)], dtype=np.int32)   # host records
     t, m, c = (torch.from_numpy(a).cuda() for a in (tmp, mp, centers))
+    src, nsrc = None, 0
+    if seed >= 2:
+        # the bucket contents read through ids from a shuffled pool of nb + 3 entries
+        nsrc = nb + 3
+        perm = torch.as_tensor(rng.permutation(nsrc)[:nb], device="cuda")
+        pools = [torch.zeros((nsrc,) + tuple(x.shape[1:]), dtype=x.dtype, device="cuda") for x in (t, m, c)]
+        for pool, x in zip(pools, (t, m, c)):
+            pool[perm] = x
+        t, m, c = pools
+        src = perm.cpu().numpy().astype(np.int32)   # host ids
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
     work = torch.zeros(lifecycle.PREPARE_WORK_INTS, dtype=torch.int32, device="cuda")
     hsh = torch.zeros((nb * 16, 2), dtype=torch.int64, device="cuda")
     match = torch.zeros(nb * 16, dtype=torch.int32, device="cuda")
     new = torch.zeros(nb * 16, dtype=torch.uint8, device="cuda")
     p = _lib.ptr
-    _lib.call("v1x_prepare_buckets", p(t), p(c), p(c.view(torch.float32)), p(m), p(meta), nb, p(hsh), p(match),
+    _lib.call("v1x_prepare_buckets", p(t), p(c), p(c.view(torch.float32)), p(m), meta.ctypes.data,
+              None if src is None else src.ctypes.data, nsrc, nb, p(hsh),
+              p(match),
               p(new), p(gpu.fine), p(gpu.centers), p(gpu.centers.view(torch.float32)), p(gpu.members),
               p(gpu.hashes), p(gpu.refs), p(gpu.free), p(gpu.free_count), p(gpu.tables), p(gpu.center_pages),
               None, 0, None, 0, cap, p(work), p(status), torch.cuda.current_stream().cuda_stream)
@@ -389,15 +404,26 @@ def test_prepare_buckets_pair_list_overflow(cuda_dev):
     for name in ("refs", "free", "tables", "members", "hashes", "fine", "centers"):
         getattr(gpu, name).copy_(torch.from_numpy(np.ascontiguousarray(getattr(cpu, name))))
     gpu.free_count.fill_(cpu.count)
-    meta = torch.tensor([[b * 1024, 5 + b, 1, 0] for b in range(nb)], dtype=torch.int32, device="cuda")
+    meta = np.array([[b * 1024, 5 + b, 1, 0] for b in range(nb)], dtype=np.int32)   # host records
     t, m, c = (torch.from_numpy(a).cuda() for a in (tmp, mp, centers))
+    # the bucket contents read through ids from a pool of nb + 3 entries, in
+    # reverse order (the inline-confirmation sweep reads them through the ids)
+    nsrc = nb + 3
+    perm = torch.arange(nb, 0, -1, device="cuda")
+    pools = [torch.zeros((nsrc,) + tuple(x.shape[1:]), dtype=x.dtype, device="cuda") for x in (t, m, c)]
+    for pool, x in zip(pools, (t, m, c)):
+        pool[perm] = x
+    t, m, c = pools
+    src = perm.cpu().numpy().astype(np.int32)   # host ids
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
     work = torch.zeros(lifecycle.PREPARE_WORK_INTS, dtype=torch.int32, device="cuda")
     hsh = torch.zeros((nb * 16, 2), dtype=torch.int64, device="cuda")
     match = torch.zeros(nb * 16, dtype=torch.int32, device="cuda")
     new = torch.zeros(nb * 16, dtype=torch.uint8, device="cuda")
     p = _lib.ptr
-    _lib.call("v1x_prepare_buckets", p(t), p(c), p(c.view(torch.float32)), p(m), p(meta), nb, p(hsh), p(match),
+    _lib.call("v1x_prepare_buckets", p(t), p(c), p(c.view(torch.float32)), p(m), meta.ctypes.data,
+              None if src is None else src.ctypes.data, nsrc, nb, p(hsh),
+              p(match),
               p(new), p(gpu.fine), p(gpu.centers), p(gpu.centers.view(torch.float32)), p(gpu.members),
               p(gpu.hashes), p(gpu.refs), p(gpu.free), p(gpu.free_count), p(gpu.tables), p(gpu.center_pages),
               None, 0, None, 0, cap, p(work), p(status), torch.cuda.current_stream().cuda_stream)
