@@ -18,9 +18,9 @@
 //  - publish (:134-167), release (:170-179): as the reference, vectorised.
 //
 // Batched prepare (extension): the buckets of one or more prepares, in the
-// reference's canonical order, in six launches per call instead of six per
-// bucket -- the call's meta records (passed in the launch parameters) written
-// to the work array; fingerprints of every page; ONE whole-GPU sweep of the arena that lists the
+// reference's canonical order, in five launches per call instead of six per
+// bucket -- fingerprints of every page (the call's meta records arrive in the
+// launch parameters and are written to the work array on the way); ONE whole-GPU sweep of the arena that lists the
 // live pages whose fingerprint equals a batch page's (a shared-memory hash
 // table of the batch's fingerprints: one probe per live arena page), and the
 // batch pages with an equal fingerprint in an earlier bucket; one warp per
@@ -63,13 +63,11 @@ struct BucketSrc {
 // for a bucket batch; all pages and 3 for the single-bucket call); match, when
 // given, is reset to "no match" (and first, the batch's earliest-equal page,
 // to "none"; counters, the batch's pair counters and flags, to 0).
-__global__ void __launch_bounds__(256) fingerprint_kernel(const uint8_t* __restrict__ tmp,
-                                                          const int32_t* __restrict__ map,
-                                                          const int32_t* __restrict__ meta,
-                                                          int64_t* __restrict__ hash, int64_t pages_per_meta,
-                                                          int meta_stride, int32_t* __restrict__ match,
-                                                          int32_t* __restrict__ first,
-                                                          int32_t* __restrict__ counters, const BucketSrc bs) {
+__device__ __forceinline__ void fingerprint_page(const uint8_t* __restrict__ tmp, const int32_t* __restrict__ map,
+                                                 const int32_t* __restrict__ meta, int64_t* __restrict__ hash,
+                                                 int64_t pages_per_meta, int meta_stride, int32_t* __restrict__ match,
+                                                 int32_t* __restrict__ first, int32_t* __restrict__ counters,
+                                                 const BucketSrc& bs) {
   const int64_t p = blockIdx.x;
   if (match && threadIdx.x == 0) match[p] = INT_MAX;
   if (first && threadIdx.x == 0) first[p] = INT_MAX;
@@ -122,6 +120,38 @@ __global__ void __launch_bounds__(256) fingerprint_kernel(const uint8_t* __restr
     hash[p * 2] = static_cast<int64_t>(ta);
     hash[p * 2 + 1] = static_cast<int64_t>(tb);
   }
+}
+
+__global__ void __launch_bounds__(256) fingerprint_kernel(const uint8_t* __restrict__ tmp,
+                                                          const int32_t* __restrict__ map,
+                                                          const int32_t* __restrict__ meta,
+                                                          int64_t* __restrict__ hash, int64_t pages_per_meta,
+                                                          int meta_stride, int32_t* __restrict__ match,
+                                                          int32_t* __restrict__ first,
+                                                          int32_t* __restrict__ counters) {
+  fingerprint_page(tmp, map, meta, hash, pages_per_meta, meta_stride, match, first, counters, BucketSrc{nullptr});
+}
+
+// The batched call's meta records (and source ids) travel in the launch
+// parameters: the fingerprints read them there, and CTA 0 also writes them to
+// the work array, where the later kernels of the call read them.
+constexpr int kMetaInts = 64 * 5;   // 64 buckets: 4-int meta records, then the source ids
+struct MetaBlock {
+  int32_t v[kMetaInts];
+};
+
+__global__ void __launch_bounds__(256) fingerprint_batch_kernel(const uint8_t* __restrict__ tmp,
+                                                                const int32_t* __restrict__ map,
+                                                                const __grid_constant__ MetaBlock mb, int n_meta,
+                                                                int has_src, int32_t* __restrict__ meta_dst,
+                                                                int64_t* __restrict__ hash,
+                                                                int32_t* __restrict__ match,
+                                                                int32_t* __restrict__ first,
+                                                                int32_t* __restrict__ counters) {
+  const int nb = n_meta / 4;
+  if (blockIdx.x == 0)
+    for (int i = threadIdx.x; i < n_meta + (has_src ? nb : 0); i += blockDim.x) meta_dst[i] = mb.v[i];
+  fingerprint_page(tmp, map, mb.v, hash, 16, 4, match, first, counters, BucketSrc{has_src ? mb.v + n_meta : nullptr});
 }
 
 // Warp-wide exact comparison of two pages: 8448 bytes and 64 members.
@@ -296,7 +326,7 @@ constexpr int kBatchMeta = 4;                     // per bucket: token start, le
 constexpr int kPairCap = 4 * kBatchPages;         // hash-equal pairs kept per list
 // work ints: counters and flags, arena pairs, batch pairs, earliest equal page
 constexpr int kWorkHead = 4;
-constexpr int kMetaInts = kBatchBuckets * (kBatchMeta + 1);   // meta records, then source ids
+static_assert(kMetaInts == kBatchBuckets * (kBatchMeta + 1), "meta records, then source ids");
 constexpr int kWorkMeta = kWorkHead + 4 * kPairCap + kBatchPages;
 constexpr int kWorkInts = kWorkMeta + kMetaInts;
 static_assert(kWorkInts == V1X_PREPARE_WORK_INTS, "v1x.h states the work size");
@@ -651,16 +681,6 @@ __global__ void __launch_bounds__(kReleaseThreads) release_many_kernel(
   if (threadIdx.x == 0) *count = cnt;
 }
 
-// The call's meta records and source ids travel in the launch parameters; this
-// kernel writes them to the work array, where the other kernels read them.
-struct MetaBlock {
-  int32_t v[kMetaInts];
-};
-
-__global__ void meta_upload_kernel(const __grid_constant__ MetaBlock mb, int32_t* __restrict__ dst, int n) {
-  for (int i = threadIdx.x; i < n; i += blockDim.x) dst[i] = mb.v[i];
-}
-
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 // Host-side offsets into the work array (as BatchWork on the device).
@@ -680,8 +700,7 @@ extern "C" int v1x_fingerprint(const uint8_t* tmp, const int32_t* map, const int
   V1X_CHECK_ARG(n_pages >= 0 && aligned16(tmp), "fingerprint: tmp must be 16-byte aligned");
   if (n_pages == 0) return V1X_OK;
   fingerprint_kernel<<<static_cast<unsigned>(n_pages), 256, 0, as_stream(stream)>>>(tmp, map, meta, hash, n_pages, 3,
-                                                                                 nullptr, nullptr, nullptr,
-                                                                                 BucketSrc{nullptr});
+                                                                                 nullptr, nullptr, nullptr);
   return launch_status("v1x_fingerprint");
 }
 
@@ -783,8 +802,8 @@ extern "C" int v1x_prepare_buckets(const uint8_t* tmp, const uint8_t* tc_bytes, 
   BatchWorkHost wh(work);
   int32_t* meta = work + kWorkMeta;
   const BucketSrc bs{src_host ? meta + nm : nullptr};
-  meta_upload_kernel<<<1, 128, 0, s>>>(mb, meta, nm + (src_host ? static_cast<int>(buckets) : 0));
-  fingerprint_kernel<<<nq, 256, 0, s>>>(tmp, map, meta, hash, 16, kBatchMeta, match, wh.first, wh.head, bs);
+  fingerprint_batch_kernel<<<nq, 256, 0, s>>>(tmp, map, mb, nm, src_host ? 1 : 0, meta, hash, match, wh.first,
+                                              wh.head);
   int64_t blocks = (cap + 255) / 256;
   const int64_t maxb = static_cast<int64_t>(num_sms()) * 4;
   if (blocks > maxb) blocks = maxb;

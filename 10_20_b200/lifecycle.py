@@ -31,7 +31,7 @@ recorded in the device status word (the reference traps) and raised by
 
 ``prepare_many`` (an extension) prepares several requests at once: all their
 new buckets, in the same canonical order, go through ``v1x_prepare_buckets``
-(up to 64 buckets per call, six launches per call), which also writes the
+(up to 64 buckets per call, five launches per call), which also writes the
 requests' page-table rows.  The arena afterwards equals that of ``prepare``
 called for each request in turn.  Request tables live as rows of one arena
 tensor, so a batch updates them without per-request copies.  ``release_many``
@@ -153,6 +153,7 @@ class PageArena:
         self.state_centers = torch.zeros((self.max_requests, pages // 8), dtype=torch.int32, device=d)
         self.free_rows = list(range(self.max_requests - 1, -1, -1))
         self.kernel_launches = 0   # kernels this driver has launched (reported by the bench)
+        self.buckets_indexed = 0   # buckets launched for indexing (aborted ones included)
         # (owner, first bucket, leases, ...) of every run of consecutive buckets
         # of one request launched since the last check(), in launch order: an
         # exhaustion aborts a suffix of the buckets
@@ -230,6 +231,7 @@ class PageArena:
             tmp, mapping, centers = bucket_source(owner, bucket)
             self._bucket(tmp, mapping, centers, bucket * 1024, lease)
             self.unchecked.append((owner, bucket, [lease]))
+            self.buckets_indexed += 1
             state.leases.append(lease)
             state.table[bucket * 16:(bucket + 1) * 16].copy_(self.tables[lease])
             state.center_table[bucket * 2:(bucket + 1) * 2].copy_(self.center_pages[lease])
@@ -338,6 +340,7 @@ class PageArena:
         runs.clear()
         cnt = np.fromiter((len(r[2]) for r in todo), dtype=np.int64, count=len(todo))
         total = int(cnt.sum())
+        self.buckets_indexed += total
         pairs = [(o, b0 + i) for o, b0, leases, _ in todo for i in range(len(leases))]
         # meta records (start token, lease, 1, state row), then per chunk the source ids
         meta = np.empty((total, 4), dtype=np.int32)
@@ -357,7 +360,7 @@ class PageArena:
                 src, nsrc = ids.ctypes.data, got[0].shape[0]
             else:
                 src, nsrc = None, 0
-            self.kernel_launches += 6
+            self.kernel_launches += 5
             _lib.call("v1x_prepare_buckets", *self._source_ptrs(got), mp + 16 * s, src, nsrc, e - s,
                       *self._arena_args(), stream, device=self.device)
 

@@ -463,14 +463,12 @@ def run_pages_workload(args, world, rank, device, dist):
         prepare_many (v1x_prepare_buckets) and consecutive releases as one
         release_many (v1x_release_many), else per bucket and per lease as the
         reference."""
-        nb, prep, rel = 0, [], []
+        prep, rel = [], []
+        indexed0 = arena.buckets_indexed
 
         def flush_prep():
-            nonlocal nb
             if prep:
-                before = {o: len(arena.states[o].leases) if o in arena.states else 0 for o, _ in prep}
                 arena.prepare_many(prep, bsrc)
-                nb += sum(len(arena.states[o].leases) - before[o] for o in before)
                 prep.clear()
 
         def flush_rel():
@@ -483,9 +481,7 @@ def run_pages_workload(args, world, rank, device, dist):
                 flush_rel()
                 prep.append((op[1], op[2]))
             elif op[0] == "prepare":
-                before = len(arena.states[op[1]].leases) if op[1] in arena.states else 0
                 arena.prepare(op[1], op[2], src)
-                nb += len(arena.states[op[1]].leases) - before
             elif batched:
                 flush_prep()
                 rel.append(op[1])
@@ -493,7 +489,7 @@ def run_pages_workload(args, world, rank, device, dist):
                 arena.release(op[1])
         flush_prep()
         flush_rel()
-        return nb
+        return arena.buckets_indexed - indexed0
 
 
     def timed_rounds(batched):
@@ -595,7 +591,7 @@ def run_pages_workload(args, world, rank, device, dist):
                             "rounds_timed": len(wl.ops) - 1, "buckets_timed": buckets, "share": 0.5,
                             "bytes_per_bucket": per_bucket,
                             "driver": "prepare_many / release_many: consecutive prepares batched through "
-                                      "v1x_prepare_buckets (<= 64 buckets, 6 launches per call, bucket contents read in place "
+                                      "v1x_prepare_buckets (<= 64 buckets, 5 launches per call, bucket contents read in place "
                                       "from the content pool), consecutive "
                                       "releases through v1x_release_many (1 launch)"},
                            per_bucket * buckets, "confirm_kernel + publish", 5, cpu, parity)
