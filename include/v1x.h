@@ -471,8 +471,8 @@ V1X_API int v1x_output_ids(const int32_t* raw, const float* scores, const int32_
                    int64_t width, int64_t topk, int64_t sink, int64_t window, int map_physical,
                    int direct_fine, int64_t fp, int64_t batch, void* stream);
 
-/* The row staging of the reference's Query.run (DS/runtime.py:643-666) in one
- * launch (the reference issues a copy per tensor and per run of equal owners).
+/* Extension (no reference counterpart): the row staging of the reference's
+ * Query.run (DS/runtime.py:643-666) in one launch (the reference issues a copy per tensor and per run of equal owners).
  * For rows i < n: q_out[i] = q[i] (heads*128 bytes), w_out[i] = w[i] (heads
  * floats), lens_out[i] = lens[i], nt_out[i] = native_tables[i] (width entries,
  * zeros up to pages), rt_out[i] = state_tables[rows[i]] (pages entries),
