@@ -66,6 +66,12 @@ constexpr int kMaxNativePages = 72;        // sink page + tail pages (window <= 
 constexpr int kSfMaxBin = 2048;            // threshold-bin keys ranked exactly
 constexpr int kSfSmallBin = 96;
 constexpr int kSfMaxBin2 = 256;
+
+// Bytes of sf_topk's scratch for rows of max_cand candidates: the 16 KB
+// candidate list, the selection bit flags, the sub-bin histogram and list.
+__host__ __device__ constexpr int64_t sf_topk_scratch_bytes(int64_t max_cand) {
+  return 16384 + (max_cand + 1023) / 1024 * 128 + 1024 + kSfMaxBin2 * 8;
+}
 constexpr uint32_t kNegInfKey = 0x007FFFFFu;  // order_key(-inf)
 constexpr uint64_t kSfWaitNs = 2000000000ull;
 constexpr int kRankDirectSf = 256;
@@ -618,19 +624,30 @@ __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 1 : 2)
     return true;
   };
 
-  int issued = 0;
-  if (warp == kProdWarp) {
-    if (lane == 0) {
-      mbar_arrive_expect_tx(&sh.qfull, q_bytes);
-      tma_load_2d(qsm, &q_map, &sh.qfull, 0, static_cast<int>(row) * a.H);
-    }
-    // the sink / tail tiles do not depend on the route: their loads fly while it runs
-    const int pre = min(nnat, min(S, SS));
-    for (; issued < pre; ++issued) {
-      if (!issue(issued)) {
+  // Producers: warp 0 and the warps idle during scoring.  Stage s is fed by
+  // producer s % nprod only, in tile order, before and after the route: a
+  // stage's next tile is issued by the warp that issued its previous one, so
+  // the parity waits on its barriers can never see a phase two behind.
+  const int pidx = warp == kProdWarp ? 0 : (warp >= kHelper0 ? 1 + warp - kHelper0 : -1);
+  const int nprod = min(1 + kThreads / 32 - kHelper0, S);
+  const auto mine = [&](int t) { return (t % S) % nprod == pidx; };
+  const bool producer = pidx >= 0 && pidx < nprod;
+  int last = -1;                             // the last tile this warp issued
+  if (warp == kProdWarp && lane == 0) {
+    mbar_arrive_expect_tx(&sh.qfull, q_bytes);
+    tma_load_2d(qsm, &q_map, &sh.qfull, 0, static_cast<int>(row) * a.H);
+  }
+  // the sink / tail tiles do not depend on the route: their loads fly while it
+  // runs (each producer issues those on its own stages)
+  const int pre = min(nnat, min(S, SS));
+  if (producer) {
+    for (int t = 0; t < pre; ++t) {
+      if (!mine(t)) continue;
+      if (!issue(t)) {
         if (lane == 0) sf_abort(sh, a.status);
         break;
       }
+      last = t;
     }
   }
 
@@ -639,18 +656,8 @@ __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 1 : 2)
   // (sf_route ends with a barrier: spage / sbnd are visible)
 
   if (warp == kProdWarp || warp >= kHelper0) {
-    // producers after the route: warp 0 and the warps idle during scoring
-    // (one warp issues about one tile per microsecond; the issue rate sets the
-    // scoring time).  Every stage is fed by one producer, in tile order: a
-    // stage's next tile is issued only by the warp that issued its previous
-    // one, so the parity waits on its barriers can never see a phase two
-    // behind (tiles before the route were issued by warp 0 before it).
-    const int pidx = warp == kProdWarp ? 0 : 1 + warp - kHelper0;
-    const int nprod = min(1 + kThreads / 32 - kHelper0, S);
-    const int pre = min(nnat, min(S, SS));
-    const auto mine = [&](int t) { return t < pre ? pidx == 0 : (t % S) % nprod == pidx; };
-    int last = -1;
-    if (pidx < nprod) {
+    // producers after the route, on their own stages
+    if (producer && !*reinterpret_cast<volatile int*>(&sh.abort)) {
       for (int t = pre; t < ntiles; ++t) {
         if (!mine(t)) continue;
         if (__shfl_sync(0xffffffffu, *reinterpret_cast<volatile int*>(&sh.abort), 0)) break;
@@ -661,10 +668,9 @@ __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 1 : 2)
         last = t;
       }
     }
-    if (warp == kProdWarp && issued > 0 && last < 0) last = issued - 1;
     if (lane == 0 && *reinterpret_cast<volatile int*>(&sh.abort)) {  // let this warp's recent loads land
       for (int k = 0, it = last; k < S && it >= 0; --it) {
-        if (!mine(it) || (it < pre && it >= issued)) continue;
+        if (!mine(it)) continue;
         mbar_wait(&sh.full[it % S], (it / S) & 1, &sh.zero, kSfWaitNs);
         mbar_wait(&sh.sfull[it % SS], (it / SS) & 1, &sh.zero, kSfWaitNs);
         ++k;
@@ -790,6 +796,14 @@ __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 1 : 2)
     // ---- Top-T + mapping (all threads) ------------------------------------------------
     const int Lr = sh.L, tk = sh.take, sink = sh.sink, tail = sh.tail, nn = sh.n;
     const uint32_t* keys = reinterpret_cast<const uint32_t*>(sc);   // order keys, written by the epilogue
+    // the outputs are staged in shared memory (after the Top-T scratch in the
+    // stage ring) and written to global memory in coalesced rows afterwards:
+    // a thread's outputs are a run of positions, so direct stores would touch a
+    // sector per lane
+    const int T = a.topk;
+    int* ol = reinterpret_cast<int*>(stages + ((sf_topk_scratch_bytes(a.max_cand) + 15) & ~int64_t(15)));
+    int* op = ol + T;
+    int* orw = op + T;
     auto emit = [&](int pos, int rawi) {
       int lg = -1;
       if (rawi >= 0 && rawi < Lr && keys[rawi] != kNegInfKey) {
@@ -801,22 +815,39 @@ __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 1 : 2)
         }
       }
       if (!(lg >= 0 && lg < nn)) lg = -1;
-      const int64_t dst = row * a.topk + pos;
-      a.logical[dst] = lg;
       int ph = -1;
       if (lg >= 0 && (lg >> 6) < a.pages) ph = sntab[lg >> 6] * 64 + (lg & 63);
-      a.physical[dst] = ph;
-      a.raw[dst] = rawi;
-      if (a.expansion_stride) {
-        const int b4 = lg * 4;
-        reinterpret_cast<int4*>(a.expanded + row * a.expansion_stride)[pos] =
-            lg < 0 ? make_int4(-1, -1, -1, -1) : make_int4(b4, b4 + 1, b4 + 2, b4 + 3);
-      }
+      ol[pos] = lg;
+      op[pos] = ph;
+      orw[pos] = rawi;
     };
-    sf_topk<kThreads>(sh, keys, thist, Lr, a.topk, stages, emit);
-    if (a.expansion_stride)
-      for (int64_t j = static_cast<int64_t>(a.topk) * 4 + tid; j < a.expansion_stride; j += kThreads)
-        a.expanded[row * a.expansion_stride + j] = -1;
+    sf_topk<kThreads>(sh, keys, thist, Lr, T, stages, emit);
+    __syncthreads();
+    int32_t* gl = a.logical + row * T;
+    int32_t* gp = a.physical + row * T;
+    int32_t* gr = a.raw + row * T;
+    if (T % 4 == 0 && ((reinterpret_cast<uintptr_t>(gl) | reinterpret_cast<uintptr_t>(gp) |
+                        reinterpret_cast<uintptr_t>(gr)) & 15) == 0) {
+      for (int j = tid; j < T / 4; j += kThreads) {
+        reinterpret_cast<int4*>(gl)[j] = reinterpret_cast<const int4*>(ol)[j];
+        reinterpret_cast<int4*>(gp)[j] = reinterpret_cast<const int4*>(op)[j];
+        reinterpret_cast<int4*>(gr)[j] = reinterpret_cast<const int4*>(orw)[j];
+      }
+    } else {
+      for (int j = tid; j < T; j += kThreads) {
+        gl[j] = ol[j];
+        gp[j] = op[j];
+        gr[j] = orw[j];
+      }
+    }
+    if (a.expansion_stride) {
+      int32_t* ex = a.expanded + row * a.expansion_stride;
+      for (int pos = tid; pos < T; pos += kThreads) {
+        const int lg = ol[pos], b4 = lg * 4;
+        reinterpret_cast<int4*>(ex)[pos] = lg < 0 ? make_int4(-1, -1, -1, -1) : make_int4(b4, b4 + 1, b4 + 2, b4 + 3);
+      }
+      for (int64_t j = static_cast<int64_t>(T) * 4 + tid; j < a.expansion_stride; j += kThreads) ex[j] = -1;
+    }
   }
   __syncthreads();
   if (warp == kMmaWarp) {
@@ -939,7 +970,8 @@ extern "C" int v1x_select_fused(const uint8_t* q, const float* w, int64_t heads,
   auto align = [](int64_t x, int64_t al) { return (x + al - 1) / al * al; };
   const int64_t route_bytes = 16384 + static_cast<int64_t>(n_items) * 8;
   const int64_t row_bytes = static_cast<int64_t>(max_cand) * 4 + take_stride * 64 * 4;
-  const int64_t topk_scratch = 16384 + (max_cand + 1023) / 1024 * 128 + 1024 + kSfMaxBin2 * 8;
+  // the Top-T scratch and the staged outputs share the stage ring
+  const int64_t topk_scratch = ((sf_topk_scratch_bytes(max_cand) + 15) & ~int64_t(15)) + 3 * topk * 4;
   auto plan = [&](int stages, int64_t* offs) {   // offs: q, sring, w, sel, sh, tab, u; returns total bytes
     int64_t off = static_cast<int64_t>(stages) * 16384;
     offs[0] = off;
