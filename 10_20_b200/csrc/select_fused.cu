@@ -796,15 +796,20 @@ __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 1 : 2)
     // ---- Top-T + mapping (all threads) ------------------------------------------------
     const int Lr = sh.L, tk = sh.take, sink = sh.sink, tail = sh.tail, nn = sh.n;
     const uint32_t* keys = reinterpret_cast<const uint32_t*>(sc);   // order keys, written by the epilogue
-    // the outputs are staged in shared memory (after the Top-T scratch in the
-    // stage ring) and written to global memory in coalesced rows afterwards:
-    // a thread's outputs are a run of positions, so direct stores would touch a
-    // sector per lane
+    // the Top-T places each selected candidate's raw column at its output slot
+    // in shared memory (after the Top-T scratch in the stage ring); then every
+    // thread maps raw -> logical -> physical for consecutive slots, so the
+    // mapping runs in parallel over the slots and the rows are written coalesced
     const int T = a.topk;
-    int* ol = reinterpret_cast<int*>(stages + ((sf_topk_scratch_bytes(a.max_cand) + 15) & ~int64_t(15)));
-    int* op = ol + T;
-    int* orw = op + T;
-    auto emit = [&](int pos, int rawi) {
+    int* orw = reinterpret_cast<int*>(stages + ((sf_topk_scratch_bytes(a.max_cand) + 15) & ~int64_t(15)));
+    sf_topk<kThreads>(sh, keys, thist, Lr, T, stages, [&](int pos, int rawi) { orw[pos] = rawi; });
+    __syncthreads();
+    int32_t* gl = a.logical + row * T;
+    int32_t* gp = a.physical + row * T;
+    int32_t* gr = a.raw + row * T;
+    int32_t* ex = a.expansion_stride ? a.expanded + row * a.expansion_stride : nullptr;
+    for (int pos = tid; pos < T; pos += kThreads) {
+      const int rawi = orw[pos];
       int lg = -1;
       if (rawi >= 0 && rawi < Lr && keys[rawi] != kNegInfKey) {
         if (rawi < tk * 64) {
@@ -817,37 +822,16 @@ __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 1 : 2)
       if (!(lg >= 0 && lg < nn)) lg = -1;
       int ph = -1;
       if (lg >= 0 && (lg >> 6) < a.pages) ph = sntab[lg >> 6] * 64 + (lg & 63);
-      ol[pos] = lg;
-      op[pos] = ph;
-      orw[pos] = rawi;
-    };
-    sf_topk<kThreads>(sh, keys, thist, Lr, T, stages, emit);
-    __syncthreads();
-    int32_t* gl = a.logical + row * T;
-    int32_t* gp = a.physical + row * T;
-    int32_t* gr = a.raw + row * T;
-    if (T % 4 == 0 && ((reinterpret_cast<uintptr_t>(gl) | reinterpret_cast<uintptr_t>(gp) |
-                        reinterpret_cast<uintptr_t>(gr)) & 15) == 0) {
-      for (int j = tid; j < T / 4; j += kThreads) {
-        reinterpret_cast<int4*>(gl)[j] = reinterpret_cast<const int4*>(ol)[j];
-        reinterpret_cast<int4*>(gp)[j] = reinterpret_cast<const int4*>(op)[j];
-        reinterpret_cast<int4*>(gr)[j] = reinterpret_cast<const int4*>(orw)[j];
-      }
-    } else {
-      for (int j = tid; j < T; j += kThreads) {
-        gl[j] = ol[j];
-        gp[j] = op[j];
-        gr[j] = orw[j];
-      }
-    }
-    if (a.expansion_stride) {
-      int32_t* ex = a.expanded + row * a.expansion_stride;
-      for (int pos = tid; pos < T; pos += kThreads) {
-        const int lg = ol[pos], b4 = lg * 4;
+      gl[pos] = lg;
+      gp[pos] = ph;
+      gr[pos] = rawi;
+      if (ex) {
+        const int b4 = lg * 4;
         reinterpret_cast<int4*>(ex)[pos] = lg < 0 ? make_int4(-1, -1, -1, -1) : make_int4(b4, b4 + 1, b4 + 2, b4 + 3);
       }
-      for (int64_t j = static_cast<int64_t>(T) * 4 + tid; j < a.expansion_stride; j += kThreads) ex[j] = -1;
     }
+    if (ex)
+      for (int64_t j = static_cast<int64_t>(T) * 4 + tid; j < a.expansion_stride; j += kThreads) ex[j] = -1;
   }
   __syncthreads();
   if (warp == kMmaWarp) {
@@ -970,8 +954,8 @@ extern "C" int v1x_select_fused(const uint8_t* q, const float* w, int64_t heads,
   auto align = [](int64_t x, int64_t al) { return (x + al - 1) / al * al; };
   const int64_t route_bytes = 16384 + static_cast<int64_t>(n_items) * 8;
   const int64_t row_bytes = static_cast<int64_t>(max_cand) * 4 + take_stride * 64 * 4;
-  // the Top-T scratch and the staged outputs share the stage ring
-  const int64_t topk_scratch = ((sf_topk_scratch_bytes(max_cand) + 15) & ~int64_t(15)) + 3 * topk * 4;
+  // the Top-T scratch and the staged output slots share the stage ring
+  const int64_t topk_scratch = ((sf_topk_scratch_bytes(max_cand) + 15) & ~int64_t(15)) + topk * 4;
   auto plan = [&](int stages, int64_t* offs) {   // offs: q, sring, w, sel, sh, tab, u; returns total bytes
     int64_t off = static_cast<int64_t>(stages) * 16384;
     offs[0] = off;
