@@ -419,19 +419,27 @@ __device__ void sf_topk(SfShared& sh, const uint32_t* keys, const int* hist, int
     }
     return k > thr ? 1 : (k == thr ? 2 : 0);
   };
-  // this thread's (selected, tie) counts -> one block scan -> output slots
+  // this thread's (selected, tie) counts -> one block scan -> output slots; the
+  // classes of a thread's first 32 keys are kept as bit masks between the two
+  // passes
   int g = 0, e = 0;
+  uint32_t m1 = 0u, m2 = 0u;
   for (int i = i0; i < i1; ++i) {
     const int kl = klass(i, keys[i]);
     g += kl == 1;
     e += kl == 2;
+    if (i - i0 < 32) {
+      m1 |= static_cast<uint32_t>(kl == 1) << (i - i0);
+      m2 |= static_cast<uint32_t>(kl == 2) << (i - i0);
+    }
   }
   long long tot;
   const long long packed = block_exclusive_scan((static_cast<long long>(g) << 32) | e,
                                                 reinterpret_cast<long long*>(sh.red), &tot);
   int gt_lt = static_cast<int>(packed >> 32), eq_lt = static_cast<int>(packed & 0xFFFFFFFFll);
   for (int i = i0; i < i1; ++i) {
-    const int kl = klass(i, keys[i]);
+    const int j = i - i0;
+    const int kl = j < 32 ? static_cast<int>(((m1 >> j) & 1u) | (((m2 >> j) & 1u) << 1)) : klass(i, keys[i]);
     if (kl == 1) emit(gt_lt + min(eq_lt, need), i);
     else if (kl == 2 && eq_lt < need) emit(gt_lt + eq_lt, i);
     gt_lt += kl == 1;
