@@ -71,6 +71,14 @@ def test_batched_lifecycle_rejects_bad_arguments_before_any_launch(v1x):
     assert rc == _lib.V1X_ERR_INVALID and b"at most 64 buckets" in lib.v1x_last_error()
     rc = lib.v1x_prepare_buckets(*([1] * 5), 16, 0, 1, *([16] * 14), 16, None, 2, 4096, None, None, None)
     assert rc == _lib.V1X_ERR_INVALID and b"src_buckets" in lib.v1x_last_error()
+    # host meta records and source ids: an id outside [0, src_buckets) is
+    # rejected before anything is launched (the device pointers are never used)
+    import numpy as np
+    meta = np.zeros((2, 4), np.int32)
+    src = np.array([0, 5], np.int32)
+    rc = lib.v1x_prepare_buckets(16, 16, 16, 16, meta.ctypes.data, src.ctypes.data, 5, 2, *([16] * 13), None, 0,
+                                 None, 0, 4096, 16, None, None)
+    assert rc == _lib.V1X_ERR_INVALID and b"source id 5 of bucket 1" in lib.v1x_last_error()
     rc = lib.v1x_release_many(None, None, None, 3, None, None, None, None)
     assert rc == _lib.V1X_ERR_INVALID and b"NULL" in lib.v1x_last_error()
     assert lib.v1x_release_many(None, None, None, 0, None, None, None, None) == _lib.V1X_OK
