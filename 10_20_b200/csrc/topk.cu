@@ -65,6 +65,14 @@ struct TopkArgs {
   int direct_fine;
   // shared-memory staging plan (staged modes): word offsets in the dynamic area
   int stage_take, stage_nt, memb_off, ntab_off;
+  // page-table transform mode (TopK-v2's transform): out = page_table[row,
+  // raw >> page_bits] << page_bits | (raw & page mask), through original_ids
+  // when given; no mask and no V1 mapping
+  const int32_t* page_table;
+  int64_t table_stride;
+  int page_bits;
+  const int32_t* original_ids;
+  int transform;
 };
 
 struct RowCtx {
@@ -186,7 +194,7 @@ __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 2 : 4) topk_kernel
     }
   }
   const int64_t rank0 = tid < a.take_stride ? load_index(a.selected, a.sel64, c.row * a.take_stride + tid) : -1;
-  c.take = a.takes[c.row];
+  c.take = a.takes ? a.takes[c.row] : 0;
   const RowBounds rb = row_bounds(c.n, 64, a.window);
   c.sink = rb.sink;
   c.tail = rb.tail;
@@ -266,6 +274,17 @@ __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 2 : 4) topk_kernel
 
   // ---- mapping epilogue for one output slot (VQ:121-148) ----------------------------
   auto emit = [&](int pos, int raw) {
+    if (a.transform) {
+      int32_t o = -1;
+      if (raw >= 0) {
+        const int32_t idx = (a.page_table[c.row * a.table_stride + (raw >> a.page_bits)] << a.page_bits) |
+                            (raw & ((1 << a.page_bits) - 1));
+        o = a.original_ids ? a.original_ids[idx] : idx;
+      }
+      a.physical[c.row * a.topk + pos] = o;
+      if (a.raw) a.raw[c.row * a.topk + pos] = raw;
+      return;
+    }
     bool live = false;
     if (raw >= 0 && raw < c.L) live = kStaged ? keys[raw] != kNegInfKey : srow[raw] != -CUDART_INF_F;
     int lg = -1;
@@ -579,6 +598,13 @@ __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 2 : 4) topk_kernel
 }  // namespace
 }  // namespace v1x
 
+namespace v1x {
+namespace {
+int topk_launch(TopkArgs a, int64_t cols, int64_t batch, int64_t stake0, int64_t snt0, cudaStream_t s,
+                const char* what);
+}  // namespace
+}  // namespace v1x
+
 extern "C" int v1x_topk(float* scores, int64_t score_stride, int64_t cols, const int32_t* fine_lens,
                         const int32_t* members, int64_t member_rows, const int32_t* rt,
                         const int32_t* nt, int64_t pages, const void* selected, int selected_is_i64,
@@ -603,16 +629,26 @@ extern "C" int v1x_topk(float* scores, int64_t score_stride, int64_t cols, const
              selected_is_i64, take_stride, lens, takes, physical, logical, raw,
              static_cast<int>(topk), static_cast<int>(window), mask, expanded, expansion_stride,
              physical_output, bucket_from_rank, fine_table, fine_table_cols, direct_fine,
-             0, 0, 0, 0};
-  cudaStream_t s = as_stream(stream);
+             0, 0, 0, 0, nullptr, 0, 0, nullptr, 0};
   V1X_CHECK_ARG(take_stride <= 65536, "topk: take stride too large");
-  // dynamic shared memory of the staged modes: keys | staged members | staged
-  // native-table row; rows whose keys alone do not fit take the unstaged mode
-  const int64_t cols_pad = (cols + 3) & ~int64_t(3);
   const int64_t rank_bound = direct_fine ? fine_table_cols : take_stride;
   const int64_t stake0 =
       (reinterpret_cast<uintptr_t>(members) & 15) == 0 ? std::min<int64_t>(rank_bound, kStageTake) : 0;
   const int64_t snt0 = std::min<int64_t>(pages, kStageNt);
+  return topk_launch(a, cols, batch, stake0, snt0, as_stream(stream), "v1x_topk");
+}
+
+namespace v1x {
+namespace {
+
+// Launches topk_kernel for `batch` rows of `cols` columns: the shared-memory plan
+// (keys | staged members | staged native-table row, up to stake0 ranks and snt0
+// entries) picks the CTA shape and the staged or unstaged mode.
+int topk_launch(TopkArgs a, int64_t cols, int64_t batch, int64_t stake0, int64_t snt0, cudaStream_t s,
+                const char* what) {
+  // dynamic shared memory of the staged modes: keys | staged members | staged
+  // native-table row; rows whose keys alone do not fit take the unstaged mode
+  const int64_t cols_pad = (cols + 3) & ~int64_t(3);
   const dim3 grid(static_cast<unsigned>(batch));
   // Many more rows than SMs (1024 single-head queries): 256-thread CTAs, four
   // per SM, when the row's keys fit their registers and a quarter of an SM's
@@ -634,7 +670,7 @@ extern "C" int v1x_topk(float* scores, int64_t score_stride, int64_t cols, const
         cudaFuncSetAttribute(topk_kernel<2, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(limit4));
       });
       launch_kernel(topk_kernel<2, 256>, grid, dim3(256), static_cast<size_t>(bytes()), s, a);
-      return launch_status("v1x_topk");
+      return launch_status(what);
     }
   }
   const int64_t limit = 227 * 1024 - static_cast<int64_t>(sizeof(TopkSmem<kTopkThreads>)) - 1024;
@@ -662,5 +698,30 @@ extern "C" int v1x_topk(float* scores, int64_t score_stride, int64_t cols, const
     a.stage_take = a.stage_nt = a.memb_off = a.ntab_off = 0;
     launch_kernel(topk_kernel<0, kTopkThreads>, grid, dim3(kTopkThreads), 0, s, a);
   }
-  return launch_status("v1x_topk");
+  return launch_status(what);
+}
+
+}  // namespace
+}  // namespace v1x
+
+extern "C" int v1x_topk_transform(const float* scores, int64_t score_stride, int64_t cols, const int32_t* seq_lens,
+                                  const int32_t* page_table, int64_t table_stride, int64_t page_size,
+                                  const int32_t* original_ids, int32_t* out, int32_t* raw, int64_t topk,
+                                  int64_t batch, void* stream) {
+  using namespace v1x;
+  clear_error();
+  V1X_CHECK_ARG(batch >= 0 && cols >= 0 && score_stride >= cols, "topk_transform: bad score geometry");
+  V1X_CHECK_ARG(topk > 0 && topk <= 2048, "topk must be in (0, 2048]");
+  V1X_CHECK_ARG(score_stride % 4 == 0, "score_stride must be a multiple of 4 (16-byte vectorized load)");
+  V1X_CHECK_ARG(page_size > 0 && (page_size & (page_size - 1)) == 0 && page_size <= (1 << 20),
+                "page_size must be power of 2");
+  V1X_CHECK_ARG(table_stride >= 0, "topk_transform: bad page-table stride");
+  if (batch == 0) return V1X_OK;
+  V1X_CHECK_ARG(scores && seq_lens && page_table && out, "topk_transform: a required buffer is NULL");
+  int page_bits = 0;
+  while ((int64_t(1) << page_bits) < page_size) ++page_bits;
+  TopkArgs a{const_cast<float*>(scores), score_stride, cols, seq_lens, nullptr, 0, nullptr, nullptr, 0, nullptr,
+             0, 0, seq_lens, nullptr, out, nullptr, raw, static_cast<int>(topk), 0, 0, nullptr, 0, 0, 0,
+             nullptr, 0, 0, 0, 0, 0, 0, page_table, table_stride, page_bits, original_ids, 1};
+  return topk_launch(a, cols, batch, 0, 0, as_stream(stream), "v1x_topk_transform");
 }

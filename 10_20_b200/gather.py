@@ -1,6 +1,6 @@
-"""Drop-in for the slot gather of ``v1_native/kernels.py``: ``_gather_slots``
+"""Drop-in for ``v1_native/kernels.py``: the slot gather ``_gather_slots``
 (:62-77) and ``GatherWorkspace`` (:80-111), backed by the sm_100a copy kernel
-of libv1x.so.
+of libv1x.so, and ``mask_scores`` (:47-59).
 
 Extension: the head dimension D is not fixed to 128 (the MLA latent is 576
 bf16 values), and ``v_pool`` may be None for a single-output gather when K and
@@ -30,6 +30,19 @@ def _gather_impl(grid, K, V, REQ, IDS, KG, VG, ROWS, TOP, HEAD, KS0, KS1, KS2, V
 
 _gather_slots = _Op(_gather_impl)
 _gather_slots.__doc__ = "KG[t] = K[REQ[IDS[t]], HEAD] (zeros for negative ids); NA/kernels.py:62-77."
+
+
+def mask_scores(scores, table, mapping, positions, dedup_cols=0, fixed_start=0):
+    """NA/kernels.py:47-59: in place, column c of row r becomes -inf when its
+    logical token l = mapping[table[r, c // 64], c % 64] is < 0, > positions[r],
+    or (c < dedup_cols and (l < 64 or l >= fixed_start))."""
+    require(scores.dtype == torch.float32 and scores.dim() == 2 and scores.stride(1) == 1, "scores: float32 rows")
+    require(table.dtype == torch.int32 and table.dim() == 2 and table.stride(1) == 1, "table: int32 [rows, -1]")
+    require(mapping.dtype == torch.int32 and mapping.is_contiguous(), "mapping: int32 [pages, 64]")
+    require(positions.dtype == torch.int32 and positions.numel() >= scores.shape[0], "positions: int32 [rows]")
+    _lib.call("v1x_mask_scores", ptr(scores), scores.stride(0), scores.shape[1], ptr(table), table.stride(0),
+              ptr(mapping), ptr(positions), int(dedup_cols), int(fixed_start), scores.shape[0],
+              _lib.stream_of(scores), device=scores.device)
 
 
 class GatherWorkspace:

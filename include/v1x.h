@@ -107,6 +107,23 @@ V1X_API int v1x_topk(float* scores, int64_t score_stride, int64_t cols, const in
              const int32_t* fine_table, int64_t fine_table_cols, int direct_fine, int64_t batch,
              void* stream);
 
+/* TopK-v2's transform -- replaces TopKKernel::transform of the vendored
+ * topk_v2.cuh that NA/deps/topk2048.py:15-32 (identity page table) and
+ * NA/deps/topk2048_mapped_20261012.py:13-21 (with original ids) call.  For row
+ * b: the topk largest of scores[b, :seq_lens[b]] (cols columns at most),
+ * ordered by (value desc, index asc); out[b, t] = -1 for an empty slot, else
+ * idx = page_table[b*table_stride + (raw >> log2(page_size))] * page_size + raw %
+ * page_size, or original_ids[idx] when original_ids is not NULL; raw[b, t] = raw
+ * (raw may be NULL).  A row with seq_lens[b] <= topk lists raw = t for t <
+ * seq_lens[b] and -1 after, as the reference's trivial transform.  Outputs in
+ * ascending raw order (the reference leaves the order unspecified).
+ * table_stride may be 0 (one shared row).  Checks: 0 < topk <= 2048,
+ * score_stride % 4 == 0 and >= cols, page_size a power of two. */
+V1X_API int v1x_topk_transform(const float* scores, int64_t score_stride, int64_t cols, const int32_t* seq_lens,
+                       const int32_t* page_table, int64_t table_stride, int64_t page_size,
+                       const int32_t* original_ids, int32_t* out, int32_t* raw, int64_t topk, int64_t batch,
+                       void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Extension (no reference counterpart): the query selection of one row per CTA
  * -- query metadata (DS/kernels.py:568-591, fixed budget of
@@ -485,6 +502,15 @@ V1X_API int v1x_query_stage(const uint8_t* q, const float* w, const int32_t* len
                     const int32_t* state_centers, int64_t state_rows, uint8_t* q_out, float* w_out,
                     int32_t* lens_out, int32_t* nt_out, int32_t* rt_out, int32_t* ct_out, int64_t heads,
                     int64_t pages, int64_t n, int64_t filled, void* stream);
+
+/* NA/kernels.py:47-59 (mask_scores of the v1_native backend).  scores f32
+ * [rows, width] row stride score_stride; table i32 row stride table_stride (fine
+ * page of each 64 columns); mapping i32 [pages, 64] logical tokens; positions
+ * i32 [rows].  Column c of row r becomes -inf when its logical token l is < 0,
+ * > positions[r], or (c < dedup_cols and (l < 64 or l >= fixed_start)). */
+V1X_API int v1x_mask_scores(float* scores, int64_t score_stride, int64_t width, const int32_t* table,
+                    int64_t table_stride, const int32_t* mapping, const int32_t* positions,
+                    int64_t dedup_cols, int64_t fixed_start, int64_t rows, void* stream);
 
 /* DS/kernels.py:594-600. logical i32 [batch, topk] -> out i32 [batch, stride]. */
 V1X_API int v1x_expand_logical(const int32_t* logical, int32_t* out, int64_t topk, int64_t stride,

@@ -1072,3 +1072,84 @@ def route_physical(scores, published, budgets, rt, take_stride):
         order = np.lexsort((rank, 0xFFFFFFFF - key))
         sel[r, :take] = rt[r, p_of_rank[order][:take]]
     return sel, takes
+
+
+# --------------------------------------------------------------------------
+# v1_native (signed-score Qwen) operators
+# --------------------------------------------------------------------------
+
+def topk_transform(scores, seq_lens, page_table, page_size, topk, original_ids=None):
+    """TopK-v2's transform as the v1_native backend calls it
+    (NA/deps/topk2048.py:15-32 with an identity page table,
+    NA/deps/topk2048_mapped_20261012.py:13-21 with original ids).
+
+    Per row b: raw = select_topk(scores[b, :seq_lens[b]], topk) -- the topk
+    largest by (value desc, index asc) in ascending index order, or [0, L) then
+    -1 when L <= topk (the trivial transform, topk_v2.cuh:139-144); out = -1
+    for raw < 0, else idx = page_table[b, raw >> bits] << bits | raw & mask
+    (page_to_indices, topk_impl.cuh:162-165), through original_ids[idx] when
+    given (transform_output, :187-190).  page_table rows may all be one row
+    (stride 0 in the reference).  Returns (out, raw) int32 [B, topk].
+    """
+    s = np.asarray(scores, np.float32)
+    B, cols = s.shape
+    pt = np.asarray(page_table, np.int64)
+    if pt.ndim == 1:
+        pt = np.broadcast_to(pt, (B, pt.shape[0]))
+    bits = int(page_size).bit_length() - 1
+    out = np.full((B, topk), -1, np.int32)
+    raw = np.full((B, topk), -1, np.int32)
+    for b in range(B):
+        L = min(int(seq_lens[b]), cols)
+        r = select_topk(s[b, :max(L, 0)], topk)
+        raw[b] = r
+        ok = r >= 0
+        idx = (pt[b, r[ok] >> bits] << bits) | (r[ok] & ((1 << bits) - 1))
+        out[b, ok] = idx if original_ids is None else np.asarray(original_ids, np.int64)[idx]
+    return out, raw
+
+
+def mask_scores(scores, table, mapping, positions, dedup_cols=0, fixed_start=0):
+    """NA/kernels.py:47-59: column c of row r becomes -inf when its logical token
+    l = mapping[table[r, c // 64], c % 64] is < 0, > positions[r], or (c <
+    dedup_cols and (l < 64 or l >= fixed_start)).  Returns a masked copy."""
+    s = np.array(scores, np.float32, copy=True)
+    B, W = s.shape
+    table = np.asarray(table, np.int64)
+    mapping = np.asarray(mapping, np.int64)
+    cols = np.arange(W)
+    for r in range(B):
+        lg = mapping[table[r, cols // 64], cols % 64]
+        bad = (lg < 0) | (lg > int(positions[r])) | ((cols < dedup_cols) & ((lg < 64) | (lg >= fixed_start)))
+        s[r, bad] = NEG_INF
+    return s
+
+
+def page_route(scores, pages, take):
+    """NA/deps/route.py:20-49 (the route extension, any THREADS it accepts).
+
+    n = the smallest of 128, 256, ..., 4096 holding the pages; blocked rank
+    r holds page p = r // (n / 128) + (r % (n / 128)) * 128, scored as the
+    fmaxf of its 8 centres (p < pages) or -inf; a stable descending radix
+    sort (CUB keys, -0 == +0) and the first `take` page ids per row.
+    Returns (ids int32 [B, take], bitmap uint8 [B, pages]).
+    """
+    s = np.asarray(scores, np.float32)
+    B = s.shape[0]
+    n = 128
+    while n < pages:
+        n *= 2
+    base = n // 128
+    rank = np.arange(n)
+    p_of_rank = rank // base + (rank % base) * 128
+    ids = np.empty((B, take), np.int32)
+    bitmap = np.zeros((B, pages), np.uint8)
+    valid = p_of_rank < pages
+    for r in range(B):
+        vals = np.full(n, NEG_INF, np.float32)
+        vals[valid] = np.fmax.reduce(s[r, :pages * 8].reshape(pages, 8), axis=1)[p_of_rank[valid]]
+        key = twiddle_key(vals).astype(np.int64)
+        order = np.lexsort((rank, 0xFFFFFFFF - key))
+        ids[r] = p_of_rank[order[:take]]
+        bitmap[r, ids[r][ids[r] < pages]] = 1
+    return ids, bitmap

@@ -1,0 +1,87 @@
+"""Known answers for the oracle's restatements of the signed-score path's
+operators (TopK-v2 transform, mask_scores, the route extension)."""
+import numpy as np
+import pytest
+
+from oracle import v1x_oracle as O
+
+
+def test_topk_transform_small_known_answer():
+    # page_size 2: raw r -> table[r >> 1] << 1 | r & 1
+    s = np.array([[5, 1, 5, 9, 0, 5, 7, -1]], np.float32)
+    table = np.array([[3, 0, 7, 1]], np.int32)
+    out, raw = O.topk_transform(s, [8], table, 2, 4)
+    # largest four by (value desc, index asc): 9@3, 7@6, 5@0, 5@2 -> ascending
+    assert raw.tolist() == [[0, 2, 3, 6]]
+    assert out.tolist() == [[6, 0, 1, 2]]
+    ids = np.arange(16, dtype=np.int32) * 10
+    out2, _ = O.topk_transform(s, [8], table[0], 2, 4, original_ids=ids)    # one shared table row
+    assert out2.tolist() == [[60, 0, 10, 20]]
+
+
+def test_topk_transform_trivial_rows():
+    s = np.zeros((3, 10), np.float32)
+    out, raw = O.topk_transform(s, [0, 3, 10], np.arange(10, dtype=np.int32)[None].repeat(3, 0), 1, 4)
+    assert raw.tolist() == [[-1] * 4, [0, 1, 2, -1], [0, 1, 2, 3]]
+    assert out.tolist() == raw.tolist()
+
+
+def test_topk_transform_identity_table_is_select_topk():
+    rng = np.random.default_rng(0)
+    s = rng.integers(-3, 3, (4, 700)).astype(np.float32)
+    table = np.arange(11, dtype=np.int32)[None].repeat(4, 0)
+    out, raw = O.topk_transform(s, [700] * 4, table, 64, 256)
+    for r in range(4):
+        assert raw[r].tolist() == O.select_topk(s[r], 256).tolist()
+    assert (out == raw).all()
+
+
+def test_mask_scores_known_answer():
+    s = np.ones((2, 128), np.float32)
+    table = np.array([[1, 0], [0, 0]], np.int32)
+    mapping = np.stack([np.arange(64), np.arange(64) + 100]).astype(np.int32)
+    mapping[1, 5] = -1
+    got = O.mask_scores(s, table, mapping, positions=[130, 40])
+    # row 0: columns 0..63 read page 1 (logical 100..163; > 130 masked, col 5 invalid), 64.. page 0
+    want0 = np.ones(128, np.float32)
+    want0[31:64] = -np.inf
+    want0[5] = -np.inf
+    assert np.array_equal(got[0], want0)
+    want1 = np.where(np.arange(128) % 64 > 40, -np.inf, 1).astype(np.float32)
+    assert np.array_equal(got[1], want1)
+    # dedup: the first 64 columns also drop logical < 64 and >= fixed_start
+    got = O.mask_scores(s, table, mapping, positions=[1000, 1000], dedup_cols=64, fixed_start=120)
+    assert np.isinf(got[0, 20:64]).all() and np.isinf(got[0, 5])
+    assert not np.isinf(np.delete(got[0, :20], 5)).any() and not np.isinf(got[0, 64:]).any()
+    assert np.isinf(got[1, :64]).all() and not np.isinf(got[1, 64:]).any()
+
+
+def test_page_route_tie_order_two_per_thread():
+    # 200 pages -> n = 256, two blocked ranks per 128: ties keep rank order
+    # 0, 128, 1, 129, ... (page p at rank 2 * (p % 128) + p // 128)
+    s = np.zeros((1, 200 * 8), np.float32)
+    ids, bm = O.page_route(s, 200, 6)
+    assert ids.tolist() == [[0, 128, 1, 129, 2, 130]]
+    assert bm.sum() == 6 and bm[0, [0, 1, 2, 128, 129, 130]].all()
+    s[0, 8 * 150 + 3] = 1.0
+    s[0, 8 * 7] = -0.0
+    ids, _ = O.page_route(s, 200, 3)
+    assert ids.tolist() == [[150, 0, 128]]
+
+
+def test_page_route_all_inf_reaches_padding_ids():
+    s = np.full((1, 200 * 8), -np.inf, np.float32)
+    ids, bm = O.page_route(s, 200, 200)
+    assert (ids >= 200).sum() > 0          # blocked ranks of pages 200..255 interleave
+    assert bm.sum() == (ids < 200).sum()
+
+
+@pytest.mark.parametrize("pages,take", [(64, 10), (100, 99), (256, 256), (1000, 300), (4096, 2048)])
+def test_page_route_equals_vq_route_ranking(pages, take):
+    rng = np.random.default_rng(pages)
+    s = rng.integers(-3, 3, (3, pages * 8)).astype(np.float32)
+    ids, _ = O.page_route(s, pages, take)
+    n = (pages + 15) // 16 * 1024 + 1
+    sel, _ = O.route(s, np.full(3, n), np.full(3, min(take, pages - 1)), take, pages,
+                     np.zeros((3, pages), np.int32), np.zeros((3, take), np.int32), np.zeros(3), 1, False)
+    assert (ids == sel).all()
