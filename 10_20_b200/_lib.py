@@ -27,6 +27,7 @@ V1X_STATUS_CAPACITY = 4
 P = ctypes.c_void_p
 I64 = ctypes.c_int64
 I32 = ctypes.c_int
+F32 = ctypes.c_float
 
 # name -> argument types (return type is int unless noted)
 SIGNATURES = {
@@ -60,6 +61,8 @@ SIGNATURES = {
     "v1x_query_stage": [P, P, P, P, I64, P, P, P, I64, P, P, P, P, P, P, I64, I64, I64, I64, P],
     "v1x_score_fp8": [P, P, P, I64, P, P, I64, P, I64, I64, P, I64, I64, I32, I32, I32, P, I64, P],
     "v1x_score_fp8_ex": [P, P, P, I64, P, P, I64, P, I64, I64, P, I64, I64, I32, I32, I32, I32, P, I64, P],
+    "v1x_mqa_logits_fp8": [P, P, P, P, I64, P, P, P, I64, I64, I32, I32, I64, P],
+    "v1x_pack_q": [P, I32, I64, I64, I64, I64, I64, I64, F32, P, P, P],
     "v1x_selftest_wait_timeout": [I64, P, P, P],
     "v1x_query_prepare": [P, P, P, P, P, P, P, I64, I64, I64, I64, I64, I64, P, P, P, P, P, I64, I64, I64, P],
     "v1x_route_pages": [P, I64, P, P, P, I32, I64, I64, P, P, I64, P, I64, I32, I64, P],

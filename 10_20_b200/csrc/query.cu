@@ -7,6 +7,10 @@
 //   stage_tail_shared :518-564, query_metadata :568-591, expand_logical :594-600;
 //   the fixed-budget take rule of bench_v1_dynamic_budget_metadata.py:5-27.
 // All index arithmetic is 64-bit (the pools exceed 2 GiB).
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+
 #include <algorithm>
 
 #include "common.cuh"
@@ -574,8 +578,69 @@ __global__ void mask_scores_kernel(float* __restrict__ scores, int64_t score_str
     scores[row * score_stride + col] = -CUDART_INF_F;
 }
 
+// pack_q of the signed-score path (qwen_gqa_probe_kernels.py:15-20; the same
+// math as the Scorer's quantize + head padding, NA/scoring.py:66-71 with
+// NA/grouping.py:41-44): one warp per (row, head) of the padded output; heads
+// below qheads of rows below `rows` are quantised with the power of two
+// >= max(absmax, 1e-4) / 448 (exactly) and get weight scale * w_mul, the rest
+// are zero.  A lane holds 4 of the 128 values.
+__device__ __forceinline__ float pq_pow2_ceil(float v) {
+  const uint32_t b = __float_as_uint(v);
+  return (b & 0x007FFFFFu) == 0 ? v : __uint_as_float(((b >> 23) + 1u) << 23);
+}
+
+__global__ void pack_q_kernel(const void* __restrict__ q, int dtype, int64_t qs0, int64_t qs1, int64_t rows,
+                              int64_t out_rows, int64_t qheads, int64_t out_heads, float w_mul,
+                              uint8_t* __restrict__ q8, float* __restrict__ w) {
+  const int64_t unit = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (unit >= out_rows * out_heads) return;
+  const int64_t row = unit / out_heads, h = unit % out_heads;
+  float x[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  const bool live = row < rows && h < qheads;
+  if (live) {
+    const int64_t off = row * qs0 + h * qs1 + lane * 4;
+    if (dtype == 0) {
+      const float* src = static_cast<const float*>(q) + off;
+      for (int i = 0; i < 4; ++i) x[i] = src[i];
+    } else if (dtype == 1) {
+      const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(q) + off;
+      for (int i = 0; i < 4; ++i) x[i] = __bfloat162float(src[i]);
+    } else {
+      const __half* src = static_cast<const __half*>(q) + off;
+      for (int i = 0; i < 4; ++i) x[i] = __half2float(src[i]);
+    }
+  }
+  float m = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
+  for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const float scale = pq_pow2_ceil(__fdiv_rn(fmaxf(m, 1e-4f), 448.0f));
+  uint32_t packed = 0;
+  for (int i = 0; i < 4; ++i) {
+    const __nv_fp8_storage_t b = __nv_cvt_float_to_fp8(__fdiv_rn(x[i], scale), __NV_SATFINITE, __NV_E4M3);
+    packed |= static_cast<uint32_t>(b) << (8 * i);
+  }
+  reinterpret_cast<uint32_t*>(q8 + unit * 128)[lane] = packed;
+  if (lane == 0) w[unit] = live ? __fmul_rn(scale, w_mul) : 0.0f;
+}
+
 }  // namespace
 }  // namespace v1x
+
+extern "C" int v1x_pack_q(const void* q, int dtype, int64_t qs0, int64_t qs1, int64_t rows, int64_t out_rows,
+                          int64_t qheads, int64_t out_heads, float w_mul, uint8_t* q8, float* w, void* stream) {
+  clear_error();
+  V1X_CHECK_ARG(dtype >= 0 && dtype <= 2, "pack_q: dtype must be 0 (f32), 1 (bf16) or 2 (f16)");
+  V1X_CHECK_ARG(rows >= 0 && out_rows >= rows && qheads >= 0 && out_heads >= qheads && qs0 >= 0 && qs1 >= 0,
+                "pack_q: bad geometry");
+  const int64_t units = out_rows * out_heads;
+  if (units == 0) return V1X_OK;
+  V1X_CHECK_ARG(q8 && w && (q || rows == 0 || qheads == 0), "pack_q: a required buffer is NULL");
+  V1X_CHECK_ARG((reinterpret_cast<uintptr_t>(q8) & 3) == 0, "pack_q: q8 must be 4-byte aligned");
+  V1X_CHECK_ARG((units + 7) / 8 < (int64_t(1) << 31), "pack_q: too many rows");
+  pack_q_kernel<<<static_cast<unsigned>((units + 7) / 8), 256, 0, as_stream(stream)>>>(
+      q, dtype, qs0, qs1, rows, out_rows, qheads, out_heads, w_mul, q8, w);
+  return launch_status("v1x_pack_q");
+}
 
 extern "C" int v1x_mask_scores(float* scores, int64_t score_stride, int64_t width, const int32_t* table,
                                int64_t table_stride, const int32_t* mapping, const int32_t* positions,

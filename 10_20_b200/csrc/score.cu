@@ -41,6 +41,10 @@ struct ScoreArgs {
   int64_t page_stride;
   int heads, relu, clean;
   int lens_kind;
+  // flat layout (fp8_mqa_logits): `pool` holds key j at j * 128, `flat_scale`
+  // its scale, `lens` the row's end ke and `starts` its start ks
+  const float* flat_scale;
+  const int32_t* starts;
 };
 
 __device__ __forceinline__ float2 e4m3x2_to_float2(uint16_t v) {
@@ -55,8 +59,9 @@ constexpr int kWarpKeys = 4 * kKeyLoads;
 // kHeads: 1 compiles the single-head case (the lane's 16 query values in
 // registers, 128 registers per thread for four resident CTAs per SM); 0 takes the
 // head count from the arguments (up to kSimtMaxHeads) with the query in shared
-// memory.  The arithmetic per key is the same.
-template <int kHeads>
+// memory.  The arithmetic per key is the same.  kFlat: keys and scales in two
+// flat arrays instead of pages, and a row scores keys [starts[b], lens[b]).
+template <int kHeads, bool kFlat = false>
 __global__ void __launch_bounds__(kScoreThreads, kHeads == 1 ? 4 : 1)
     score_simt_kernel(const __grid_constant__ ScoreArgs a) {
   __shared__ __align__(16) float qs[kHeads == 1 ? 4 : kSimtMaxHeads * 128];
@@ -94,20 +99,32 @@ __global__ void __launch_bounds__(kScoreThreads, kHeads == 1 ? 4 : 1)
   // row; the next block's bytes are loaded while the current one is evaluated.
   const int64_t n = score_len(a.lens[b], a.lens_kind);
   const int64_t lim = min(n, a.max_len);  // keys j < lim are scored
+  const int64_t lo = kFlat ? max(a.starts[b], 0) : 0;  // and j >= lo
   const int64_t live = (lim + kWarpKeys - 1) / kWarpKeys;  // blocks holding a scored key
   const int64_t wstep = static_cast<int64_t>(gridDim.y) * (kScoreThreads / 32);
   auto load = [&](int64_t blk, uint4 (&kw)[kKeyLoads], float& scale) {
     const int64_t k0 = blk * kWarpKeys;
     if (blk < live) {
-      const int64_t page = a.table[b * a.table_stride + k0 / 64];
-      const uint8_t* base = a.pool + page * kPageBytes;
+      if constexpr (kFlat) {
 #pragma unroll
-      for (int u = 0; u < kKeyLoads; ++u) {
-        const int64_t key = k0 + u * 4 + grp;
-        kw[u] = key < lim ? reinterpret_cast<const uint4*>(base + (key % 64) * 128)[part] : make_uint4(0, 0, 0, 0);
+        for (int u = 0; u < kKeyLoads; ++u) {
+          const int64_t key = k0 + u * 4 + grp;
+          kw[u] = key < lim && key >= lo ? reinterpret_cast<const uint4*>(a.pool + key * 128)[part]
+                                         : make_uint4(0, 0, 0, 0);
+        }
+        const int64_t ks = k0 + lane;
+        scale = ks < lim && ks >= lo ? a.flat_scale[ks] : 0.0f;
+      } else {
+        const int64_t page = a.table[b * a.table_stride + k0 / 64];
+        const uint8_t* base = a.pool + page * kPageBytes;
+#pragma unroll
+        for (int u = 0; u < kKeyLoads; ++u) {
+          const int64_t key = k0 + u * 4 + grp;
+          kw[u] = key < lim ? reinterpret_cast<const uint4*>(base + (key % 64) * 128)[part] : make_uint4(0, 0, 0, 0);
+        }
+        const int64_t ks = k0 + lane;  // lane i holds the scale of the block's key i
+        scale = ks < lim ? reinterpret_cast<const float*>(base)[kScaleWord + ks % 64] : 0.0f;
       }
-      const int64_t ks = k0 + lane;  // lane i holds the scale of the block's key i
-      scale = ks < lim ? reinterpret_cast<const float*>(base)[kScaleWord + ks % 64] : 0.0f;
     }
   };
   uint4 cur[kKeyLoads], nxt[kKeyLoads];
@@ -156,8 +173,10 @@ __global__ void __launch_bounds__(kScoreThreads, kHeads == 1 ? 4 : 1)
       }
       const float scale = __shfl_sync(0xffffffffu, cur_scale, u * 4 + grp);
       const int64_t key = k0 + u * 4 + grp;
-      res[u] = key < lim ? __fmul_rn(acc, scale) : -CUDART_INF_F;
-      if (part == u && a.out && key < a.max_len && (key < n || a.clean)) a.out[b * a.out_stride + key] = res[u];
+      const bool in = key < lim && key >= lo;
+      res[u] = in ? __fmul_rn(acc, scale) : -CUDART_INF_F;
+      if (part == u && a.out && key < a.max_len && ((key < n && key >= lo) || a.clean))
+        a.out[b * a.out_stride + key] = res[u];
     }
     if (a.page_max) {  // max over each group of 8 consecutive keys: loads u, u+1 of the four key lanes
 #pragma unroll
@@ -233,6 +252,27 @@ int score_dispatch(const uint8_t* q, const float* w, const uint8_t* pool, int64_
   else launch_kernel(score_simt_kernel<0>, grid, dim3(kScoreThreads), 0, as_stream(stream), a);
   return launch_status("v1x_score_fp8");
 }
+
+int mqa_flat(const uint8_t* q, const float* w, const uint8_t* k, const float* k_scale, int64_t kv_len,
+             const int32_t* starts, const int32_t* ends, float* out, int64_t out_stride, int64_t heads, int relu,
+             int clean, int64_t batch, void* stream) {
+  clear_error();
+  V1X_CHECK_ARG(heads >= 1 && heads <= kSimtMaxHeads, "mqa_logits: heads must be in [1, 64]");
+  V1X_CHECK_ARG(batch >= 0 && kv_len >= 0 && out_stride >= kv_len, "mqa_logits: bad geometry");
+  V1X_CHECK_ARG(batch < (int64_t(1) << 31), "mqa_logits: too many rows");
+  V1X_CHECK_ARG((reinterpret_cast<uintptr_t>(k) & 15) == 0 && (reinterpret_cast<uintptr_t>(q) & 15) == 0,
+                "mqa_logits: q and k must be 16-byte aligned");
+  if (batch == 0 || kv_len == 0) return V1X_OK;
+  ScoreArgs a{q, w, k, ends, nullptr, 0, out, out_stride, kv_len, nullptr, 0,
+              static_cast<int>(heads), relu, clean, 0, k_scale, starts};
+  const int64_t blocks = (kv_len + kScoreThreads - 1) / kScoreThreads;
+  const int64_t wave = static_cast<int64_t>(num_sms()) * 4;
+  const int64_t per_row = std::max<int64_t>(1, std::min<int64_t>({(wave + batch - 1) / batch, blocks, 8}));
+  const dim3 grid(static_cast<unsigned>(batch), static_cast<unsigned>(per_row));
+  if (heads == 1) launch_kernel(score_simt_kernel<1, true>, grid, dim3(kScoreThreads), 0, as_stream(stream), a);
+  else launch_kernel(score_simt_kernel<0, true>, grid, dim3(kScoreThreads), 0, as_stream(stream), a);
+  return launch_status("v1x_mqa_logits_fp8");
+}
 }  // namespace
 }  // namespace v1x
 
@@ -252,4 +292,11 @@ extern "C" int v1x_score_fp8_ex(const uint8_t* q, const float* w, const uint8_t*
                                 int lens_kind, int32_t* status, int64_t batch, void* stream) {
   return v1x::score_dispatch(q, w, pool, pool_pages, lens, table, table_stride, out, out_stride, max_len, page_max,
                              page_stride, heads, relu, clean, impl, lens_kind, status, batch, stream);
+}
+
+extern "C" int v1x_mqa_logits_fp8(const uint8_t* q, const float* w, const uint8_t* k, const float* k_scale,
+                                  int64_t kv_len, const int32_t* starts, const int32_t* ends, float* out,
+                                  int64_t out_stride, int64_t heads, int relu, int clean, int64_t batch,
+                                  void* stream) {
+  return v1x::mqa_flat(q, w, k, k_scale, kv_len, starts, ends, out, out_stride, heads, relu, clean, batch, stream);
 }

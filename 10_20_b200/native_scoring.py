@@ -1,0 +1,213 @@
+"""Drop-in for the v1_native backend's signed-score selection: ``Scorer``
+(NA/scoring.py:25-99), its shared-page variant ``select`` / ``select_tensors``
+(NA/shared_scoring.py:9-62) and ``quantize`` (NA/grouping.py:41-44), composed
+from libv1x.so's operators:
+
+- q packing (quantise the four query heads, pad to the 32 the scorer takes,
+  fold the softmax scale into the head weights): ``v1x_pack_q``;
+- signed FP8 paged logits (the no-ReLU DeepGEMM fork the reference loads):
+  ``scoring.fp8_paged_mqa_logits(..., relu=False)``; the ``dsa`` mode's flat
+  logits: ``scoring.fp8_mqa_logits(..., relu=False)``;
+- page route: ``native_route`` (route.py's tie order);
+- ``gather.mask_scores``; the mapped Top-2048: ``topk2048_mapped``; the
+  ``dsa`` mode's plain Top-2048: ``topk2048``.
+
+The backend's host state (its arenas, ``state`` / ``arena`` objects) is the
+caller's, duck-typed as in the reference: ``state.pages``, ``state.centers``,
+``state.valid``, ``state.fine``, ``state.mapping`` (flat [heads, pages * 64]),
+``state.flat_k`` / ``state.flat_scale`` for ``dsa``; the shared variant reads
+``state.arena`` (``centers``, ``valid``, ``fine``, ``mapping``, ``identity``,
+``record()``), ``state.table``, ``state.wait()``, ``state.full_bucket_append``
+and ``state.fixed_start``.  Query graphs (the reference's
+``SGLANG_V1_*QUERY_GRAPH`` options) need the shared arenas' graph pools, which
+the caller supplies as ``state.query_graph_pool`` exactly as in the reference.
+"""
+from __future__ import annotations
+
+import os
+
+import torch
+
+from . import _lib
+from ._lib import ptr, require
+from . import scoring
+from .gather import mask_scores
+from .native_route import extension, rank_pages
+from .topk2048 import topk2048
+from .topk2048_mapped import mapped_top2048
+
+_DTYPES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
+
+
+def query_graph_enabled(decode: bool = False) -> bool:
+    """NA/config.py:16-19."""
+    return (os.environ.get("SGLANG_V1_INDEX_GRAPHS", "0") == "1"
+            or os.environ.get("SGLANG_V1_QUERY_GRAPH", "0") == "1"
+            or (decode and os.environ.get("SGLANG_V1_DECODE_QUERY_GRAPH", "0") == "1"))
+
+
+def pack_q(q, scale, out_heads: int = 32, out=None):
+    """(q8 e4m3 [rows, out_heads, 128], weights float32 [rows, out_heads]) of q
+    [rows, qheads, 128] (float32 / bf16 / fp16, unit inner stride): per (row,
+    head) the power-of-two scale >= max(max|q|, 1e-4) / 448, q8 = q / scale,
+    weight = scale * softmax scale / qheads; heads >= qheads are zero
+    (NA/scoring.py:66-71, qwen_gqa_probe_kernels.py:15-20).  ``out`` = (q8,
+    weights) buffers with at least as many rows to write into."""
+    require(q.dim() == 3 and q.shape[2] == 128 and q.stride(2) == 1 and q.dtype in _DTYPES,
+            "q: [rows, heads, 128] float32 / bfloat16 / float16 with unit inner stride")
+    rows, qheads = q.shape[0], q.shape[1]
+    require(qheads <= out_heads, "more query heads than output heads")
+    if out is None:
+        q8 = torch.empty((rows, out_heads, 128), dtype=torch.float8_e4m3fn, device=q.device)
+        w = torch.empty((rows, out_heads), dtype=torch.float32, device=q.device)
+    else:
+        q8, w = out
+        require(q8.dim() == 3 and q8.shape[1:] == (out_heads, 128) and q8.is_contiguous()
+                and q8.dtype in (torch.float8_e4m3fn, torch.uint8) and q8.shape[0] >= rows,
+                "q8: contiguous e4m3 [>= rows, out_heads, 128]")
+        require(w.shape == (q8.shape[0], out_heads) and w.dtype == torch.float32 and w.is_contiguous(),
+                "weights: contiguous float32 [q8 rows, out_heads]")
+    require(q.is_cuda, "pack_q: q must be a CUDA tensor")
+    _lib.same_device(q, q8, w)
+    _lib.call("v1x_pack_q", ptr(q), _DTYPES[q.dtype], q.stride(0), q.stride(1), rows, q8.shape[0], qheads,
+              out_heads, float(scale) / qheads, ptr(q8), ptr(w), _lib.stream_of(q), device=q.device)
+    return q8, w
+
+
+def quantize(x):
+    """NA/grouping.py:41-44: (x / scale as e4m3, scale) with scale the power of
+    two >= max(max|x|, 1e-4) / 448 over the last axis (128 wide)."""
+    require(x.shape[-1] == 128, "quantize: last axis of 128")
+    lead = x.shape[:-1]
+    flat = x.reshape(-1, 1, 128)
+    q8, w = pack_q(flat, 1.0, out_heads=1)
+    return q8.reshape(*lead, 128), w.reshape(lead)
+
+
+class Scorer:
+    """NA/scoring.py:25-99 on libv1x.so (sm_100a; the reference requires SM90 and
+    its no-ReLU DeepGEMM fork).  ``impl`` (extension) picks the scorer of
+    ``scoring.fp8_paged_mqa_logits``: "auto" (tensor cores at 32 heads) or
+    "simt" (fixed fp32 evaluation order)."""
+
+    def __init__(self, config, device):
+        self.config = config
+        self.sms = torch.cuda.get_device_properties(device).multi_processor_count
+        self.query_graph = query_graph_enabled()
+        self.decode_query_graph = query_graph_enabled(decode=True)
+        self.impl = "auto"
+
+    def select_decode(self, q, state, head, prefix, offset, total, fixed, scale):
+        if self.decode_query_graph and self._graph_eligible(state):
+            return self._select_graph(q, state, head, prefix, offset, total, fixed, scale)
+        return self.select_eager(q, state, head, prefix, offset, total, fixed, scale)
+
+    def _graph_eligible(self, state):
+        return (self.config.mode == "v1" and self.config.share_active_pages
+                and getattr(state, "full_bucket_append", False) and state.pages > 0)
+
+    def _select_graph(self, q, state, head, prefix, offset, total, fixed, scale):
+        if getattr(state, "query_graph_pool", None) is None:
+            raise RuntimeError("Query graph pool was not initialized with the backend")
+        return state.query_graph_pool.select(self, q, state, head, prefix, offset, total, fixed, scale)
+
+    def paged(self, q8, weights, cache, table, count):
+        """Signed paged logits [rows, count] of q8 [rows, 32, 128] over `cache`
+        (packed pages [n, 64, 1, 132]) through `table` (NA/scoring.py:48-53)."""
+        lengths = torch.full((len(q8), 1), count, device=q8.device, dtype=torch.int32)
+        return scoring.fp8_paged_mqa_logits(q8, cache, weights, lengths, table, None, count,
+                                            clean_logits=False, relu=False, impl=self.impl)
+
+    def select(self, q, state, head, prefix, offset, total, fixed, scale):
+        if self.query_graph and self._graph_eligible(state):
+            return self._select_graph(q, state, head, prefix, offset, total, fixed, scale)
+        return self.select_eager(q, state, head, prefix, offset, total, fixed, scale)
+
+    def select_eager(self, q, state, head, prefix, offset, total, fixed, scale):
+        if self.config.share_active_pages:
+            return select(self, q, state, head, prefix, offset, total, fixed, scale)
+        rows, qheads, dim = q.shape
+        if dim != 128 or qheads != 4:
+            raise ValueError("This backend preserves Qwen's four-Q-head routing group")
+        q8, weights = pack_q(q, scale)
+        positions = torch.arange(prefix + offset, prefix + offset + rows, device=q.device, dtype=torch.int32)
+        if self.config.mode == "dsa":
+            scores = scoring.fp8_mqa_logits(q8, (state.flat_k[head, :total], state.flat_scale[head, :total]),
+                                            weights, torch.zeros_like(positions), positions + 1, True, relu=False)
+            return topk2048(scores, need_values=False)[1].int()
+        pages = state.pages
+        centers = pages * 8
+        center_pages = (centers + 63) // 64
+        ct = torch.arange(center_pages, device=q.device, dtype=torch.int32)[None].expand(rows, -1).contiguous()
+        coarse = self.paged(q8, weights, state.centers[head], ct, centers)
+        coarse = coarse[:, :centers]
+        coarse.masked_fill_(~state.valid[head, :centers][None], -torch.inf)
+        take = self.config.budget(pages)
+        table = torch.empty((rows, take + len(fixed)), device=q.device, dtype=torch.int32)
+        table[:, take:] = fixed[None]
+        if take == pages:
+            table[:, :take] = torch.arange(pages, device=q.device, dtype=torch.int32)
+        else:
+            _route_into(coarse, table, pages, take)
+        scores = self.paged(q8, weights, state.fine[head], table, table.shape[1] * 64)
+        mask_scores(scores, table, state.mapping[head], positions)
+        # logical original token positions (not physical slots, no x4 expansion)
+        return mapped_top2048(scores, table, state.mapping[head])
+
+
+def _route_into(coarse, table, pages, take):
+    """The reference's route choice (NA/scoring.py:92-95): the route extension
+    for 32 < pages <= 4096; fewer pages take the same ranking (the reference
+    uses an unsorted torch top-k there, same set up to ties); more than 4096
+    pages the torch top-k as in the reference."""
+    if 32 < pages <= 4096:
+        extension(64, 4).route(coarse, table, pages, take)
+    elif pages <= 32:
+        table[:, :take] = rank_pages(coarse, pages, take)
+    else:
+        rows = coarse.shape[0]
+        table[:, :take] = coarse.reshape(rows, pages, 8).amax(-1).topk(take, sorted=False).indices.int()
+
+
+def select(scorer, q, state, head, prefix, offset, total, fixed, scale):
+    """NA/shared_scoring.py:9-27: the selection over shared physical index pages."""
+    arena = state.arena
+    state.wait()
+    fixed.record_stream(torch.cuda.current_stream(q.device))
+    rows, qheads, dim = q.shape
+    if (qheads, dim) != (4, 128):
+        raise ValueError("Expected four Q heads of dimension 128")
+    q8, weights = pack_q(q, scale)
+    positions = torch.arange(prefix + offset, prefix + offset + rows, device=q.device, dtype=torch.int32)
+    ids = select_tensors(scorer, q8, weights, arena, head, state.table[head], fixed[head], positions,
+                         state.full_bucket_append, state.fixed_start)
+    arena.record()
+    return ids
+
+
+def select_tensors(scorer, q8, weights, arena, head, page_ids, fixed_ids, positions, full_bucket_append,
+                   fixed_start, decode_meta=None):
+    """NA/shared_scoring.py:30-62: query kernels only (stream dependencies and
+    the page lifecycle stay with the caller); returns physical reordered
+    storage ids through ``arena.identity``."""
+    if decode_meta is not None:
+        raise ValueError("decode_meta masks belong to the shared arenas' decode query graph, "
+                         "which this library does not provide")
+    rows = len(q8)
+    pages, take = page_ids.numel(), scorer.config.budget(page_ids.numel())
+    selected = torch.empty((rows, take), device=q8.device, dtype=torch.int32)
+    if take == pages:
+        selected[:] = torch.arange(pages, device=q8.device, dtype=torch.int32)
+    else:
+        ct = page_ids[None].expand(rows, -1).contiguous()
+        coarse = scorer.paged(q8, weights, arena.centers[head], ct, pages * 64)
+        coarse = coarse.reshape(rows, pages, 64)[:, :, :8].contiguous()
+        valid = arena.valid[head, page_ids.long()]
+        coarse.masked_fill_(~valid[None], -torch.inf)
+        coarse = coarse.reshape(rows, pages * 8)
+        _route_into(coarse, selected, pages, take)
+    table = torch.cat((page_ids[selected.long()], fixed_ids[None].expand(rows, -1)), 1).contiguous()
+    scores = scorer.paged(q8, weights, arena.fine[head], table, table.shape[1] * 64)
+    mask_scores(scores, table, arena.mapping[head], positions,
+                take * 64 if full_bucket_append else 0, fixed_start if full_bucket_append else 0)
+    return mapped_top2048(scores, table, arena.identity)

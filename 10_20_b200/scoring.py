@@ -85,3 +85,40 @@ def fp8_paged_mqa_logits(q, kv_cache, weights, context_lens, block_table, schedu
               ptr(status_word(q.device)), B,
               _lib.stream_of(q), device=q.device)
     return out if logits else page_max
+
+
+def fp8_mqa_logits(q, kv, weights, cu_seqlen_ks, cu_seqlen_ke, clean_logits: bool = True, relu: bool = True,
+                   out: torch.Tensor | None = None):
+    """DeepGEMM ``fp8_mqa_logits`` over a flat key array, as the signed-score
+    Scorer's ``dsa`` mode (NA/scoring.py:74-78) and the probe backend
+    (qwen_gqa_probe_backend.py:184) call it: logits [M, N] float32 with
+    logits[i, j] = sum_h w[i, h] * relu(q[i, h, :] . k[j]) * k_scale[j] for
+    ks[i] <= j < ke[i] (-inf elsewhere when clean_logits, else untouched).
+
+    q: e4m3 [M, H, 128] (H <= 64); kv = (k e4m3 [N, 128], k_scale float32 [N]);
+    weights float32 [M, H]; cu_seqlen_ks / cu_seqlen_ke int32 [M].  relu=False
+    (extension) is the signed variant the Scorer uses.
+    """
+    k, k_scale = kv
+    require(q.dim() == 3 and q.shape[2] == 128 and q.dtype in (torch.float8_e4m3fn, torch.uint8)
+            and q.is_contiguous(), "q: contiguous float8_e4m3fn [M, H, 128]")
+    M, H = q.shape[0], q.shape[1]
+    require(k.dim() == 2 and k.shape[1] == 128 and k.dtype in (torch.float8_e4m3fn, torch.uint8)
+            and k.is_contiguous(), "kv[0]: contiguous float8_e4m3fn [N, 128]")
+    N = k.shape[0]
+    k_scale = k_scale.reshape(-1)
+    require(k_scale.numel() == N and k_scale.dtype == torch.float32 and k_scale.is_contiguous(),
+            "kv[1]: float32 [N]")
+    require(weights.shape == (M, H) and weights.dtype == torch.float32 and weights.is_contiguous(),
+            "weights: float32 [M, H]")
+    for name, t in (("cu_seqlen_ks", cu_seqlen_ks), ("cu_seqlen_ke", cu_seqlen_ke)):
+        require(t.shape == (M,) and t.dtype == torch.int32 and t.is_contiguous(), f"{name}: int32 [M]")
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float32, device=q.device)
+    require(out.dtype == torch.float32 and out.dim() == 2 and out.shape[0] == M and out.shape[1] >= N
+            and out.stride(1) == 1, "out: float32 [M, >= N]")
+    _lib.same_device(q, k, k_scale, weights, cu_seqlen_ks, cu_seqlen_ke, out)
+    _lib.call("v1x_mqa_logits_fp8", ptr(q), ptr(weights), ptr(k), ptr(k_scale), N, ptr(cu_seqlen_ks),
+              ptr(cu_seqlen_ke), ptr(out), out.stride(0), H, int(bool(relu)), int(bool(clean_logits)), M,
+              _lib.stream_of(q), device=q.device)
+    return out

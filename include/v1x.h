@@ -503,6 +503,18 @@ V1X_API int v1x_query_stage(const uint8_t* q, const float* w, const int32_t* len
                     int32_t* lens_out, int32_t* nt_out, int32_t* rt_out, int32_t* ct_out, int64_t heads,
                     int64_t pages, int64_t n, int64_t filled, void* stream);
 
+/* pack_q of the signed-score path -- replaces qwen_gqa_probe_kernels.py:15-20 and
+ * the Scorer's quantize + head padding (NA/scoring.py:66-71, NA/grouping.py:41-44).
+ * q [rows, qheads, 128] of dtype 0 = f32, 1 = bf16, 2 = f16 with element strides
+ * qs0 (row) and qs1 (head), unit inner stride; q8 u8 (e4m3) [out_rows, out_heads,
+ * 128]; w f32 [out_rows, out_heads].  For row < rows and head < qheads: scale = the
+ * power of two >= max(max|q|, 1e-4) / 448 (exactly; the reference's
+ * exp2(ceil(log2(.))) agrees except a few ulps above a power of two), q8 =
+ * e4m3(q / scale) (round to nearest even), w = scale * w_mul (the reference's
+ * softmax scale / 4); every other entry of q8 and w is 0. */
+V1X_API int v1x_pack_q(const void* q, int dtype, int64_t qs0, int64_t qs1, int64_t rows, int64_t out_rows,
+                  int64_t qheads, int64_t out_heads, float w_mul, uint8_t* q8, float* w, void* stream);
+
 /* NA/kernels.py:47-59 (mask_scores of the v1_native backend).  scores f32
  * [rows, width] row stride score_stride; table i32 row stride table_stride (fine
  * page of each 64 columns); mapping i32 [pages, 64] logical tokens; positions
@@ -548,6 +560,19 @@ V1X_API int v1x_score_fp8_ex(const uint8_t* q, const float* w, const uint8_t* po
                   int64_t out_stride, int64_t max_len, float* page_max, int64_t page_stride,
                   int64_t heads, int relu, int clean, int impl, int lens_kind, int32_t* status,
                   int64_t batch, void* stream);
+
+/* FP8 MQA logits over a flat key array -- the DeepGEMM fp8_mqa_logits contract
+ * the signed-score Scorer calls in its `dsa` mode (NA/scoring.py:74-78) and the
+ * probe backend at qwen_gqa_probe_backend.py:184: out[b, j] = sum_h w[b,h] *
+ * relu(q[b,h,:] . k_j) * k_scale[j] for starts[b] <= j < ends[b] (ends clamped to
+ * kv_len); with clean != 0 every other column j < kv_len is -inf, else untouched.
+ * q u8 (e4m3) [batch, heads, 128], 16-byte aligned; w f32 [batch, heads]; k u8
+ * (e4m3) [kv_len, 128], 16-byte aligned; k_scale f32 [kv_len]; out f32 [batch,
+ * out_stride >= kv_len].  relu = 0 gives the signed variant.  heads <= 64, the
+ * SIMT scorer's fixed fp32 evaluation order. */
+V1X_API int v1x_mqa_logits_fp8(const uint8_t* q, const float* w, const uint8_t* k, const float* k_scale,
+                  int64_t kv_len, const int32_t* starts, const int32_t* ends, float* out,
+                  int64_t out_stride, int64_t heads, int relu, int clean, int64_t batch, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* _gather_slots -- replaces NA/kernels.py:62-77 (GatherWorkspace.gather, :102-111).

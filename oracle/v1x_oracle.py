@@ -1153,3 +1153,36 @@ def page_route(scores, pages, take):
         ids[r] = p_of_rank[order[:take]]
         bitmap[r, ids[r][ids[r] < pages]] = 1
     return ids, bitmap
+
+
+def pack_q(q, out_heads, w_mul, out_rows=None):
+    """qwen_gqa_probe_kernels.py:15-20 (and NA/scoring.py:66-71 with
+    NA/grouping.py:41-44): q float [rows, qheads, 128] -> (q8 uint8 e4m3
+    [out_rows, out_heads, 128], w float32 [out_rows, out_heads]); scale = the
+    power of two >= max(max|q|, 1e-4) / 448 (pow2_ceil), q8 = e4m3(q / scale),
+    w = scale * w_mul for the live (row, head) entries, zeros elsewhere."""
+    q = np.asarray(q, np.float32)
+    rows, qheads, _ = q.shape
+    out_rows = rows if out_rows is None else out_rows
+    q8 = np.zeros((out_rows, out_heads, 128), np.uint8)
+    w = np.zeros((out_rows, out_heads), np.float32)
+    m = np.maximum(np.abs(q).max(-1), np.float32(1e-4)).astype(np.float32)
+    scale = pow2_ceil((m / np.float32(448)).astype(np.float32))
+    q8[:rows, :qheads] = e4m3_from_f32((q / scale[..., None]).astype(np.float32))
+    w[:rows, :qheads] = (scale * np.float32(w_mul)).astype(np.float32)
+    return q8, w
+
+
+def mqa_logits(q_u8, w, k_u8, k_scale, starts, ends, relu=True, clean=True):
+    """DeepGEMM fp8_mqa_logits (NA/scoring.py:75-77): [M, N] float32 with
+    logits[i, j] = score_row over keys starts[i] <= j < ends[i], -inf elsewhere
+    (clean) -- the same fixed fp32 evaluation order as score_row(exact=True)."""
+    k = e4m3_to_f32(np.asarray(k_u8, np.uint8)).reshape(-1, 128)
+    sc = np.asarray(k_scale, np.float32).reshape(-1)
+    M, N = len(starts), k.shape[0]
+    out = np.full((M, N), NEG_INF, np.float32)
+    for i in range(M):
+        lo, hi = max(int(starts[i]), 0), min(int(ends[i]), N)
+        if hi > lo:
+            out[i, lo:hi] = score_row(q_u8[i], w[i], k[lo:hi], sc[lo:hi], relu, True)
+    return out

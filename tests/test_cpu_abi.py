@@ -34,6 +34,22 @@ def test_ctypes_table_covers_header(v1x):
     assert sorted(_lib.SIGNATURES) == declared_symbols()
 
 
+def declared_arg_counts():
+    text = re.sub(r"/\*.*?\*/", "", (ROOT / "include" / "v1x.h").read_text(), flags=re.S)
+    out = {}
+    for name, args in re.findall(r"V1X_API\s+[\w\s\*]*?\b(v1x_\w+)\s*\(([^)]*)\)", text):
+        args = args.strip()
+        out[name] = 0 if args in ("", "void") else args.count(",") + 1
+    return out
+
+
+def test_ctypes_argument_counts_match_header(v1x):
+    from importlib import import_module
+    _lib = import_module("10_20_b200._lib")
+    for name, n in declared_arg_counts().items():
+        assert len(_lib.SIGNATURES[name]) == n, name
+
+
 def test_shims_reject_cpu_tensors(v1x):
     from importlib import import_module
     qf = import_module("10_20_b200.query_fused")

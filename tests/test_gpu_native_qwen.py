@@ -2,6 +2,7 @@
 transform (plain and through original ids), mask_scores and the page route
 extension, called through their drop-in modules."""
 import importlib
+import math
 
 import numpy as np
 import pytest
@@ -181,3 +182,196 @@ def test_page_route_extension_rejects_bad_arguments():
         ext.route(s[:, :8 * 199], t, 200, 10)
     with pytest.raises(ValueError):
         native_route.extension(96, 4)
+
+
+# ---------------------------------------------------------------------------
+# q packing, flat MQA logits and the composed Scorer
+# ---------------------------------------------------------------------------
+
+native_scoring = importlib.import_module("10_20_b200.native_scoring")
+scoring = importlib.import_module("10_20_b200.scoring")
+synth = importlib.import_module("10_20_b200.synth")
+
+
+def _u8(t):
+    return t.view(torch.uint8).cpu().numpy()
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32, torch.float16])
+def test_pack_q_matches_oracle(dtype):
+    g = torch.Generator().manual_seed(7)
+    q = (torch.randn((37, 6, 128), generator=g) * torch.logspace(-6, 3, 37)[:, None, None]).to(dtype)
+    q[3] = 0                                   # all-zero rows take the 1e-4 floor
+    q[5, :, 7] = 448.0 * 2 ** -3               # absmax / 448 an exact power of two
+    qd = q.to(DEV)
+    big = torch.empty((40, 7, 128), dtype=dtype, device=DEV)
+    big[:, :6] = torch.zeros_like(big[:, :6])
+    big[:37, :6] = qd
+    view = big[:37, :6]                        # head stride 128, row stride 7 * 128
+    q8, w = native_scoring.pack_q(view[:, :4], 0.0883883, out_heads=32)
+    want_q8, want_w = O.pack_q(q[:, :4].float().numpy(), 32, np.float32(0.0883883 / 4))
+    np.testing.assert_array_equal(_u8(q8), want_q8)
+    np.testing.assert_array_equal(w.cpu().numpy(), want_w)
+    qq, sc = native_scoring.quantize(qd)
+    want_q8, want_w = O.pack_q(q.float().numpy().reshape(-1, 1, 128), 1, 1.0)
+    np.testing.assert_array_equal(_u8(qq).reshape(-1, 128), want_q8.reshape(-1, 128))
+    np.testing.assert_array_equal(sc.cpu().numpy().reshape(-1), want_w.reshape(-1))
+
+
+@pytest.mark.parametrize("relu,heads", [(False, 32), (True, 4), (False, 1)])
+def test_mqa_logits_matches_oracle(relu, heads):
+    rng = np.random.default_rng(heads)
+    M, N = 11, 3001
+    q8 = O.e4m3_from_f32(rng.standard_normal((M, heads, 128)).astype(np.float32))
+    w = rng.uniform(-1, 1, (M, heads)).astype(np.float32)
+    k8 = O.e4m3_from_f32(rng.standard_normal((N, 128)).astype(np.float32))
+    ks = rng.uniform(0.01, 2, N).astype(np.float32)
+    starts = np.array([0, 0, 5, 100, 3000, 3001, 0, 17, 2999, 40, 0], np.int32)
+    ends = np.array([1, 3001, 6, 99, 3001, 3001, 5000, 2048, 3000, 2500, 0], np.int32)
+    t = lambda a: torch.from_numpy(a).to(DEV)
+    out = scoring.fp8_mqa_logits(t(q8).view(torch.float8_e4m3fn), (t(k8).view(torch.float8_e4m3fn), t(ks)), t(w),
+                                 t(starts), t(ends), clean_logits=True, relu=relu)
+    want = O.mqa_logits(q8, w, k8, ks, starts, ends, relu=relu, clean=True)
+    np.testing.assert_array_equal(out.cpu().numpy(), want)
+    # clean_logits=False leaves the columns outside [ks, ke) untouched
+    keep = torch.full((M, N + 3), 3.5, device=DEV)
+    scoring.fp8_mqa_logits(t(q8).view(torch.float8_e4m3fn), (t(k8).view(torch.float8_e4m3fn), t(ks)), t(w),
+                           t(starts), t(ends), clean_logits=False, relu=relu, out=keep)
+    got = keep.cpu().numpy()
+    live = np.isfinite(want)
+    np.testing.assert_array_equal(got[:, :N][live], want[live])
+    assert (got[:, :N][~live] == 3.5).all() and (got[:, N:] == 3.5).all()
+
+
+class _Config:
+    def __init__(self, mode, fraction, share=False):
+        self.mode, self.fraction, self.share_active_pages = mode, fraction, share
+
+    def budget(self, pages):
+        return min(pages, math.ceil(pages * self.fraction))
+
+
+class _State:
+    pass
+
+
+def _pool(rng, pages):
+    """Packed pages [pages, 64, 1, 132] of random FP8 keys with random scales."""
+    k8 = O.e4m3_from_f32(rng.standard_normal((pages, 64, 128)).astype(np.float32))
+    sc = rng.uniform(0.01, 1, (pages, 64)).astype(np.float32)
+    raw = np.concatenate([k8.reshape(pages, 8192), sc.view(np.uint8).reshape(pages, 256)], 1)
+    return raw.reshape(pages, 64, 1, 132)
+
+
+def _oracle_v1(q, scale, centers_u8, valid, fine_u8, mapping, fixed, pages, take, positions):
+    rows = q.shape[0]
+    q8, w = O.pack_q(q, 32, np.float32(scale / 4))
+    C = pages * 8
+    ct = np.arange((C + 63) // 64)[None].repeat(rows, 0)
+    coarse = O.score_paged(q8, w, centers_u8, ct, [C] * rows, C, relu=False)
+    coarse[:, ~valid[:C]] = -np.inf
+    if take == pages:
+        sel = np.arange(pages)[None].repeat(rows, 0)
+    else:
+        sel, _ = O.page_route(coarse, pages, take)
+    table = np.concatenate([sel, np.asarray(fixed)[None].repeat(rows, 0)], 1).astype(np.int32)
+    W = table.shape[1] * 64
+    fine = O.score_paged(q8, w, fine_u8, table, [W] * rows, W, relu=False)
+    fine = O.mask_scores(fine, table, mapping.reshape(-1, 64), positions)
+    out, _ = O.topk_transform(fine, [W] * rows, table, 64, 2048, original_ids=mapping)
+    return out
+
+
+@pytest.mark.parametrize("pages,fraction", [(100, 0.3), (30, 0.5), (48, 1.0)])
+def test_scorer_v1_matches_oracle(pages, fraction):
+    rng = np.random.default_rng(pages)
+    heads, rows, nfixed = 2, 6, 36 if pages == 30 else 4
+    C = pages * 8
+    cp = (C + 63) // 64
+    fp = pages + nfixed
+    st = _State()
+    st.pages = pages
+    centers = np.stack([_pool(rng, cp) for _ in range(heads)])
+    fine = np.stack([_pool(rng, fp) for _ in range(heads)])
+    valid = rng.random((heads, C)) > 0.1
+    mapping = rng.integers(-1, 5000, (heads, fp * 64)).astype(np.int32)
+    st.centers, st.fine = torch.from_numpy(centers).to(DEV), torch.from_numpy(fine).to(DEV)
+    st.valid, st.mapping = torch.from_numpy(valid).to(DEV), torch.from_numpy(mapping).to(DEV)
+    fixed = np.arange(pages, fp, dtype=np.int32)
+    q = torch.randn((rows, 4, 128), generator=torch.Generator().manual_seed(pages)).to(torch.bfloat16)
+    scorer = native_scoring.Scorer(_Config("v1", fraction), DEV)
+    scorer.impl = "simt"
+    take = scorer.config.budget(pages)
+    prefix, offset = 4000, 3
+    positions = np.arange(prefix + offset, prefix + offset + rows)
+    for head in range(heads):
+        got = scorer.select(q.to(DEV), st, head, prefix, offset, 0, torch.from_numpy(fixed).to(DEV), 0.0883883)
+        want = _oracle_v1(q.float().numpy(), 0.0883883, centers[head], valid[head], fine[head], mapping[head],
+                          fixed, pages, take, positions)
+        np.testing.assert_array_equal(got.cpu().numpy(), want)
+    # the tensor-core scorer (the default) selects the same tokens up to near-ties
+    scorer.impl = "auto"
+    got = scorer.select(q.to(DEV), st, 0, prefix, offset, 0, torch.from_numpy(fixed).to(DEV), 0.0883883).cpu()
+    want = _oracle_v1(q.float().numpy(), 0.0883883, centers[0], valid[0], fine[0], mapping[0], fixed, pages, take,
+                      positions)
+    agree = np.mean([len(np.intersect1d(got[r].numpy(), want[r])) / len(np.unique(want[r])) for r in range(rows)])
+    assert agree > 0.95
+
+
+def test_scorer_dsa_matches_oracle():
+    rng = np.random.default_rng(9)
+    heads, rows, N = 2, 5, 4100
+    st = _State()
+    k8 = O.e4m3_from_f32(rng.standard_normal((heads, N, 128)).astype(np.float32))
+    ks = rng.uniform(0.01, 1, (heads, N)).astype(np.float32)
+    st.flat_k = torch.from_numpy(k8).to(DEV).view(torch.float8_e4m3fn)
+    st.flat_scale = torch.from_numpy(ks).to(DEV)
+    scorer = native_scoring.Scorer(_Config("dsa", 0.5), DEV)
+    q = torch.randn((rows, 4, 128), generator=torch.Generator().manual_seed(1)).to(torch.bfloat16)
+    prefix, offset, total = 3000, 90, 3500
+    got = scorer.select(q.to(DEV), st, 1, prefix, offset, total, None, 0.125)
+    q8, w = O.pack_q(q.float().numpy(), 32, np.float32(0.125 / 4))
+    pos = np.arange(prefix + offset, prefix + offset + rows)
+    logits = O.mqa_logits(q8, w, k8[1, :total], ks[1, :total], np.zeros(rows), pos + 1, relu=False)
+    want = np.stack([O.select_topk(logits[r], 2048) for r in range(rows)])
+    assert got.dtype == torch.int32
+    np.testing.assert_array_equal(got.cpu().numpy(), want)
+
+
+def test_shared_select_matches_oracle():
+    rng = np.random.default_rng(21)
+    heads, rows, phys, pages, nfixed = 2, 4, 150, 90, 6
+    arena = _State()
+    centers = np.stack([_pool(rng, phys) for _ in range(heads)])
+    fine = np.stack([_pool(rng, phys) for _ in range(heads)])
+    valid = rng.random((heads, phys, 8)) > 0.05
+    mapping = rng.integers(-1, 9000, (heads, phys * 64)).astype(np.int32)
+    arena.centers, arena.fine = torch.from_numpy(centers).to(DEV), torch.from_numpy(fine).to(DEV)
+    arena.valid, arena.mapping = torch.from_numpy(valid).to(DEV), torch.from_numpy(mapping).to(DEV)
+    arena.identity = torch.arange(phys * 64, dtype=torch.int32, device=DEV)
+    arena.record = lambda: None
+    st = _State()
+    st.arena, st.wait = arena, (lambda: None)
+    page_ids = np.stack([rng.permutation(phys)[:pages] for _ in range(heads)]).astype(np.int32)
+    fixed = np.stack([rng.permutation(phys)[:nfixed] for _ in range(heads)]).astype(np.int32)
+    st.table = torch.from_numpy(page_ids).to(DEV)
+    st.full_bucket_append, st.fixed_start, st.pages = True, 6000, pages
+    scorer = native_scoring.Scorer(_Config("v1", 0.3, share=True), DEV)
+    scorer.impl = "simt"
+    q = torch.randn((rows, 4, 128), generator=torch.Generator().manual_seed(2)).to(torch.bfloat16)
+    prefix, offset = 7000, 0
+    got = scorer.select(q.to(DEV), st, 1, prefix, offset, 0, torch.from_numpy(fixed).to(DEV), 0.1)
+    take = scorer.config.budget(pages)
+    q8, w = O.pack_q(q.float().numpy(), 32, np.float32(0.1 / 4))
+    ids = page_ids[1]
+    coarse = O.score_paged(q8, w, centers[1], ids[None].repeat(rows, 0), [pages * 64] * rows, pages * 64,
+                           relu=False)
+    coarse = coarse.reshape(rows, pages, 64)[:, :, :8].copy()
+    coarse[:, ~valid[1][ids]] = -np.inf
+    sel, _ = O.page_route(coarse.reshape(rows, -1), pages, take)
+    table = np.concatenate([ids[sel], fixed[1][None].repeat(rows, 0)], 1).astype(np.int32)
+    W = table.shape[1] * 64
+    sc = O.score_paged(q8, w, fine[1], table, [W] * rows, W, relu=False)
+    sc = O.mask_scores(sc, table, mapping[1].reshape(-1, 64), np.arange(prefix, prefix + rows), take * 64, 6000)
+    want, _ = O.topk_transform(sc, [W] * rows, table, 64, 2048, original_ids=np.arange(phys * 64))
+    np.testing.assert_array_equal(got.cpu().numpy(), want)

@@ -85,3 +85,31 @@ def test_page_route_equals_vq_route_ranking(pages, take):
     sel, _ = O.route(s, np.full(3, n), np.full(3, min(take, pages - 1)), take, pages,
                      np.zeros((3, pages), np.int32), np.zeros((3, take), np.int32), np.zeros(3), 1, False)
     assert (ids == sel).all()
+
+
+def test_pack_q_known_answer():
+    q = np.zeros((2, 5, 128), np.float32)
+    q[0, 0, :3] = [56.0, -28.0, 1.0]      # absmax / 448 = 1/8 exactly: scale 1/8
+    q[0, 1, 0] = 57.0                      # just above: scale 1/4
+    q[1, 2, 5] = 1e-9                      # below the 1e-4 floor: scale 2^-22
+    q8, w = O.pack_q(q[:, :4], 8, np.float32(0.5), out_rows=3)
+    assert q8.shape == (3, 8, 128) and w.shape == (3, 8)
+    assert O.e4m3_to_f32(q8[0, 0, :3]).tolist() == [448.0, -224.0, 8.0]
+    assert w[0, 0] == np.float32(0.125 * 0.5) and w[0, 1] == np.float32(0.25 * 0.5)
+    assert O.e4m3_to_f32(q8[0, 1, :1]).tolist() == [224.0]     # 57 / 0.25 = 228 -> 224 (step 16)
+    assert w[1, 2] == np.float32(2.0 ** -22 * 0.5)
+    assert (q8[:, 4:] == 0).all() and (w[:, 4:] == 0).all() and (q8[2] == 0).all() and (w[2] == 0).all()
+
+
+def test_mqa_logits_is_score_row_on_each_window():
+    rng = np.random.default_rng(4)
+    q8 = O.e4m3_from_f32(rng.standard_normal((3, 2, 128)).astype(np.float32))
+    w = rng.standard_normal((3, 2)).astype(np.float32)
+    k8 = O.e4m3_from_f32(rng.standard_normal((50, 128)).astype(np.float32))
+    ks = rng.uniform(0.1, 1, 50).astype(np.float32)
+    out = O.mqa_logits(q8, w, k8, ks, [0, 10, 30], [50, 20, 10], relu=False)
+    k = O.e4m3_to_f32(k8)
+    assert np.array_equal(out[0], O.score_row(q8[0], w[0], k, ks, relu=False))
+    assert np.isinf(out[1, :10]).all() and np.isinf(out[1, 20:]).all()
+    assert np.array_equal(out[1, 10:20], O.score_row(q8[1], w[1], k[10:20], ks[10:20], relu=False))
+    assert np.isinf(out[2]).all()
