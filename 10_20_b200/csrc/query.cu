@@ -564,18 +564,24 @@ namespace {
 // whose logical token (members of its fine page) is missing, in the query's
 // future, or -- among the first dedup_cols columns -- a sink token or one at or
 // past fixed_start, scores -inf.
+constexpr int kMaskCols = 4096;
+
 __global__ void mask_scores_kernel(float* __restrict__ scores, int64_t score_stride, int64_t width,
                                    const int32_t* __restrict__ table, int64_t table_stride,
                                    const int32_t* __restrict__ mapping, const int32_t* __restrict__ positions,
                                    int64_t dedup_cols, int64_t fixed_start) {
+  // a CTA takes kMaskCols columns of one row, a thread every 256th of them
   const int64_t row = blockIdx.y;
-  const int64_t col = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (col >= width) return;
-  const int64_t page = table[row * table_stride + col / 64];
-  const int logical = mapping[page * 64 + col % 64];
   const int pos = positions[row];
-  if (logical < 0 || logical > pos || (col < dedup_cols && (logical < 64 || logical >= fixed_start)))
-    scores[row * score_stride + col] = -CUDART_INF_F;
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * kMaskCols + threadIdx.x;
+  const int64_t last = min(width, static_cast<int64_t>(blockIdx.x + 1) * kMaskCols);
+#pragma unroll 4
+  for (int64_t col = first; col < last; col += 256) {
+    const int64_t page = table[row * table_stride + col / 64];
+    const int logical = mapping[page * 64 + col % 64];
+    if (logical < 0 || logical > pos || (col < dedup_cols && (logical < 64 || logical >= fixed_start)))
+      scores[row * score_stride + col] = -CUDART_INF_F;
+  }
 }
 
 // pack_q of the signed-score path (qwen_gqa_probe_kernels.py:15-20; the same
@@ -651,7 +657,7 @@ extern "C" int v1x_mask_scores(float* scores, int64_t score_stride, int64_t widt
   if (rows == 0 || width == 0) return V1X_OK;
   V1X_CHECK_ARG(scores && table && mapping && positions, "mask_scores: a required buffer is NULL");
   V1X_CHECK_ARG(rows < 65536, "mask_scores: at most 65535 rows per call");
-  const dim3 grid(static_cast<unsigned>((width + 255) / 256), static_cast<unsigned>(rows));
+  const dim3 grid(static_cast<unsigned>((width + kMaskCols - 1) / kMaskCols), static_cast<unsigned>(rows));
   mask_scores_kernel<<<grid, 256, 0, as_stream(stream)>>>(scores, score_stride, width, table, table_stride, mapping,
                                                          positions, dedup_cols, fixed_start);
   return launch_status("v1x_mask_scores");

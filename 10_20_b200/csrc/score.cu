@@ -150,6 +150,11 @@ __global__ void __launch_bounds__(kScoreThreads, kHeads == 1 ? 4 : 1)
       }
       float acc = 0.0f;
       for (int h = 0; h < H; ++h) {
+        // a zero weight adds +-0, which leaves the sum unchanged (finite
+        // inputs): skipped, so zero-padded heads cost nothing
+        if constexpr (kHeads != 1) {
+          if (ws[h] == 0.0f) continue;
+        }
         float p = 0.0f;
         if constexpr (kHeads == 1) {
 #pragma unroll

@@ -73,6 +73,9 @@ struct TopkArgs {
   int page_bits;
   const int32_t* original_ids;
   int transform;
+  // unstaged mode: words of the selection bitmap in the dynamic shared memory
+  // (0: the bitwise threshold search over the row in global memory)
+  int sel_words;
 };
 
 struct RowCtx {
@@ -173,6 +176,10 @@ __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 2 : 4) topk_kernel
   extern __shared__ __align__(16) uint32_t dyn[];
   __shared__ TopkSmem<kThreads> sm;
   uint32_t* keys = dyn;
+  // selection bitmap: the staged modes' static one, or the unstaged mode's
+  // dynamic one (one bit per candidate)
+  uint32_t* selbits = kStaged ? sm.selbit : dyn;
+  const bool hist_path = kStaged || a.sel_words > 0;
   int* memb = reinterpret_cast<int*>(dyn) + a.memb_off;
   int* ntab = reinterpret_cast<int*>(dyn) + a.ntab_off;
   const int tid = threadIdx.x, nt = kThreads;
@@ -335,18 +342,20 @@ __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 2 : 4) topk_kernel
       if constexpr (kMode == 0) return order_key(srow[i]);
       else return keys[i];
     };
-    // staged modes: one 12-bit histogram pass finds the bin of the T-th key; the
-    // bin's keys are ranked exactly by (key desc, index asc) and the selected ones
-    // flagged.  Rows whose bin holds more than kMaxBin keys (mass ties) and the
-    // unstaged mode take the bitwise search instead.
+    // one 12-bit histogram pass finds the bin of the T-th key; the bin's keys
+    // are ranked exactly by (key desc, index asc) and the selected ones flagged.
+    // The unstaged mode with a bitmap reads the row twice (histogram, then the
+    // bin's keys and the keys above it, which it flags too) and places from the
+    // bitmap alone.  Rows whose bin holds more than kMaxBin keys (mass ties)
+    // and the unstaged mode without a bitmap take the bitwise search instead.
     bool by_bin = false, have_tie = false;
     uint32_t tie_thr = 0;
     int tie_need = 0;
     TopBin tb{0, 0, 0};
-    if constexpr (kStaged) {
+    if (hist_path) {
       int* hist = sm.u.h.hist;
       zero_hist<kThreads>(hist);
-      for (int w = tid; w < (c.L + 31) / 32; w += nt) sm.selbit[w] = 0u;
+      for (int w = tid; w < (c.L + 31) / 32; w += nt) selbits[w] = 0u;
       if (tid < 256) sm.hist2[tid] = 0;
       if (tid == 0) {
         sm.ncand = 0;
@@ -360,7 +369,7 @@ __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 2 : 4) topk_kernel
         for (int j = 0; j < kRegKeys; ++j)
           if (j * nt + tid < c.L) atomicAdd(&hist[bin_of(kr[j])], 1);
       } else {
-        for (int i = tid; i < c.L; i += nt) atomicAdd(&hist[bin_of(keys[i])], 1);
+        for (int i = tid; i < c.L; i += nt) atomicAdd(&hist[bin_of(kMode == 0 ? order_key(srow[i]) : keys[i])], 1);
       }
       __syncthreads();
       tb = find_top_bin<kThreads>(a.topk, hist, sm.warp_tot, &sm.res);
@@ -374,6 +383,12 @@ __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 2 : 4) topk_kernel
         const uint32_t ltm = lanemask_lt();
         auto append = [&](int j, uint32_t k) {
           const bool m = j * nt + tid < c.L && bin_of(k) == tb.bin;
+          if constexpr (kMode == 0) {
+            // the warp's 32 consecutive candidates are one bitmap word, owned by
+            // this warp in this pass: flag the keys above the bin
+            const unsigned above = __ballot_sync(0xffffffffu, j * nt + tid < c.L && bin_of(k) > tb.bin);
+            if (lane == 0 && j * nt + warp * 32 < c.L) selbits[(j * nt + warp * 32) >> 5] = above;
+          }
           const unsigned bal = __ballot_sync(0xffffffffu, m);
           if (bal == 0u) return;
           const uint32_t lo = __reduce_min_sync(0xffffffffu, m ? k : 0xFFFFFFFFu);
@@ -432,7 +447,7 @@ __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 2 : 4) topk_kernel
             for (int q = tid; q < tb.in; q += nt) {
               const int2 me = cand[q];
               const int sub = (me.x >> (24 - kBinBits)) & 255;
-              if (sub > r2.x) atomicOr(&sm.selbit[me.y >> 5], 1u << (me.y & 31));
+              if (sub > r2.x) atomicOr(&selbits[me.y >> 5], 1u << (me.y & 31));
               else if (sub == r2.x) sm.cand2[atomicAdd(&sm.ncand2, 1)] = me;
             }
             __syncthreads();
@@ -476,7 +491,7 @@ __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 2 : 4) topk_kernel
               const uint32_t ko = static_cast<uint32_t>(o.x);
               r += (ko > k) | ((ko == k) & (o.y < me.y));
             }
-            if (r < need_bin) atomicOr(&sm.selbit[me.y >> 5], 1u << (me.y & 31));
+            if (r < need_bin) atomicOr(&selbits[me.y >> 5], 1u << (me.y & 31));
           }
           __syncthreads();
         }
@@ -516,8 +531,9 @@ __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 2 : 4) topk_kernel
     auto klass = [&](int i, uint32_t k) -> int {
       if (i >= c.L) return 0;
       if (by_bin) {
+        if constexpr (kMode == 0) return static_cast<int>((selbits[i >> 5] >> (i & 31)) & 1u);
         const int b = bin_of(k);
-        return (b > tb.bin || (b == tb.bin && ((sm.selbit[i >> 5] >> (i & 31)) & 1u))) ? 1 : 0;
+        return (b > tb.bin || (b == tb.bin && ((selbits[i >> 5] >> (i & 31)) & 1u))) ? 1 : 0;
       }
       return k > thr ? 1 : (k == thr ? 2 : 0);
     };
@@ -577,13 +593,14 @@ __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 2 : 4) topk_kernel
       int2 carry = make_int2(0, 0);
       for (int j0 = 0; j0 < nsl; j0 += kMaxSlices) {
         const int jn = min(nsl - j0, kMaxSlices);
+        // (the unstaged mode's bitmap classifies without the keys)
         for (int jc = 0; jc < jn; ++jc)
-          count_slice(j0 + jc, jc, (j0 + jc) * nt + tid < c.L ? key_of(j0 + jc) : 0u);
+          count_slice(j0 + jc, jc, (j0 + jc) * nt + tid < c.L && !(kMode == 0 && by_bin) ? key_of(j0 + jc) : 0u);
         __syncthreads();
         scan_counts(jn * kTopkWarps, carry);
         __syncthreads();
         for (int jc = 0; jc < jn; ++jc)
-          place_slice(j0 + jc, jc, (j0 + jc) * nt + tid < c.L ? key_of(j0 + jc) : 0u);
+          place_slice(j0 + jc, jc, (j0 + jc) * nt + tid < c.L && !(kMode == 0 && by_bin) ? key_of(j0 + jc) : 0u);
         carry = sm.carry;
         __syncthreads();
       }
@@ -629,7 +646,7 @@ extern "C" int v1x_topk(float* scores, int64_t score_stride, int64_t cols, const
              selected_is_i64, take_stride, lens, takes, physical, logical, raw,
              static_cast<int>(topk), static_cast<int>(window), mask, expanded, expansion_stride,
              physical_output, bucket_from_rank, fine_table, fine_table_cols, direct_fine,
-             0, 0, 0, 0, nullptr, 0, 0, nullptr, 0};
+             0, 0, 0, 0, nullptr, 0, 0, nullptr, 0, 0};
   V1X_CHECK_ARG(take_stride <= 65536, "topk: take stride too large");
   const int64_t rank_bound = direct_fine ? fine_table_cols : take_stride;
   const int64_t stake0 =
@@ -696,7 +713,16 @@ int topk_launch(TopkArgs a, int64_t cols, int64_t batch, int64_t stake0, int64_t
       launch_kernel(topk_kernel<1, kTopkThreads>, grid, dim3(kTopkThreads), static_cast<size_t>(bytes()), s, a);
   } else {
     a.stage_take = a.stage_nt = a.memb_off = a.ntab_off = 0;
-    launch_kernel(topk_kernel<0, kTopkThreads>, grid, dim3(kTopkThreads), 0, s, a);
+    // the selection bitmap (one bit per column) in the dynamic shared memory
+    const int64_t words = (cols + 31) / 32;
+    a.sel_words = words * 4 <= limit ? static_cast<int>(words) : 0;
+    static DeviceOnce once0;
+    once0.run([&] {
+      cudaFuncSetAttribute(topk_kernel<0, kTopkThreads>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(limit));
+    });
+    launch_kernel(topk_kernel<0, kTopkThreads>, grid, dim3(kTopkThreads), static_cast<size_t>(a.sel_words) * 4, s,
+                  a);
   }
   return launch_status(what);
 }

@@ -1,7 +1,7 @@
 """Benchmark of the V1 query-side selection path on B200 (one process per GPU).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload decode|single|sort|gather|pages|build|shared]
+                    [--workload decode|single|sort|gather|pages|build|shared|signed]
 
 Workloads (synthetic, seeded; shapes of the benchmark configurations):
   decode  128 requests per GPU, context ~U[32K, 128K] tokens, 64 index heads,
@@ -12,7 +12,8 @@ Workloads (synthetic, seeded; shapes of the benchmark configurations):
           (2688 candidates), route -> score -> Top-2048 (no gather).
 Component workloads (one line each): sort (_sort + group offsets), gather
 (_gather_slots), pages (page lifecycle), build (index build of 1024 buckets),
-shared (published-end shared-tail preparation of a 4096-row chunk).
+shared (published-end shared-tail preparation of a 4096-row chunk), signed
+(the signed-score Scorer.select of a 1024-row prefill chunk).
 A step is one pass of the whole selection path over one batch.  Three
 independent batches (separate pools, same context lengths) are in flight on three
 streams, in turn, so the gather of one batch overlaps the selection of the next
@@ -827,6 +828,151 @@ def run_shared_workload(args, world, rank, device, dist):
     return line
 
 
+def run_signed_workload(args, world, rank, device, dist):
+    """The signed-score path (NA/scoring.py:60-99): one Scorer.select in v1 mode
+    over one KV head for a 1024-row prefill chunk after 122,880 tokens of
+    history indexed in 4096-token buckets (1,856 built pages, fraction 0.5 ->
+    928 routed pages, 49 fixed pages of sink + window + chunk; 62,528 fine
+    candidates per row), four query heads padded to 32.  One step = pack_q,
+    the signed centre logits, the route, the signed fine logits, mask_scores
+    and the mapped Top-2048, captured as a graph.  Bytes per step are the
+    designed traffic of that composition (the reference's): both pools once,
+    the centre and fine logit matrices written and read once, q in, ids out."""
+    import math
+    import numpy as np
+    NS = importlib.import_module("10_20_b200.native_scoring")
+    oracle = importlib.import_module("oracle.v1x_oracle")
+    rows = args.requests or 1024
+    prefix, sink, window, bucket = 122880, 64, 2048, 4096
+    pages = (prefix - sink - window) // bucket * 64
+    fixed_n = math.ceil((sink + window + rows) / 64)
+    fp = pages + fixed_n
+    C = pages * 8
+    cp = (C + 63) // 64
+    gen = torch.Generator().manual_seed(61 + rank)
+
+    def pool(n):
+        k = torch.randn((n, 64, 128), generator=gen).to(torch.float8_e4m3fn)
+        buf = torch.zeros((n, 8448), dtype=torch.uint8)
+        buf[:, :8192] = k.view(torch.uint8).reshape(n, 8192)
+        buf.view(torch.float32)[:, 2048:] = torch.rand((n, 64), generator=gen) * 0.5 + 0.05
+        return buf.reshape(n, 64, 1, 132)
+
+    class State:
+        pass
+
+    st = State()
+    st.pages = pages
+    centers_h, fine_h = pool(cp), pool(fp)
+    st.centers, st.fine = centers_h[None].to(device), fine_h[None].to(device)
+    valid_h = torch.rand((1, C), generator=gen) > 0.02
+    st.valid = valid_h.to(device)
+    # middle pages hold history tokens [sink, prefix - window) in a shuffled order
+    # (buckets are reordered by grouping); fixed pages: sink, window, the chunk
+    mid = torch.randperm(prefix - window - sink, generator=gen)[:pages * 64].int() + sink
+    tail = torch.cat((torch.arange(sink), torch.arange(prefix - window, prefix + rows))).int()
+    tail = torch.cat((tail, torch.full((fixed_n * 64 - tail.numel(),), -1, dtype=torch.int32)))
+    mapping_h = torch.cat((mid, tail))[None].contiguous()
+    st.mapping = mapping_h.to(device)
+    fixed = torch.arange(pages, fp, dtype=torch.int32, device=device)
+
+    class Cfg:
+        mode, share_active_pages, fraction = "v1", False, 0.5
+
+        def budget(self, n):
+            return min(n, math.ceil(n * self.fraction))
+
+    scorer = NS.Scorer(Cfg(), device)
+    q = torch.randn((rows, 4, 128), generator=gen).to(torch.bfloat16).to(device)
+    take = Cfg().budget(pages)
+    W = (take + fixed_n) * 64
+    out = {}
+
+    def step():
+        out["ids"] = scorer.select(q, st, 0, prefix, 0, 0, fixed, 0.0883883)
+
+    g = _capture(step, device)
+    ms, clk = _timed_replays(g, args.steps, args.warmup, dist, device)
+    value = rows * args.steps * world / (ms / 1e3)
+    bytes_per_step = (cp + fp) * 8448 + rows * (C * 4 * 2 + W * 4 * 2 + 4 * 128 * 2 + 2048 * 4)
+    # stage split of one select (eager, events between the operators)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(8)]
+    q8, w = NS.pack_q(q, 0.0883883)
+    ct = torch.arange(cp, device=device, dtype=torch.int32)[None].expand(rows, -1).contiguous()
+    table = torch.empty((rows, take + fixed_n), device=device, dtype=torch.int32)
+    table[:, take:] = fixed[None]
+    positions = torch.arange(prefix, prefix + rows, device=device, dtype=torch.int32)
+    split = {}
+    for rep in range(4):
+        ev[0].record()
+        q8, w = NS.pack_q(q, 0.0883883)
+        ev[1].record()
+        coarse = scorer.paged(q8, w, st.centers[0], ct, C)
+        ev[2].record()
+        coarse.masked_fill_(~st.valid[0, :C][None], -torch.inf)
+        NS.extension(64, 4).route(coarse, table, pages, take)
+        ev[3].record()
+        sc = scorer.paged(q8, w, st.fine[0], table, W)
+        ev[4].record()
+        NS.mask_scores(sc, table, st.mapping[0], positions)
+        ev[5].record()
+        NS.mapped_top2048(sc, table, st.mapping[0])
+        ev[6].record()
+        torch.cuda.synchronize()
+        if rep:
+            for i, name in enumerate(("pack_q", "centre_logits", "mask_and_route", "fine_logits", "mask_scores",
+                                      "mapped_top2048")):
+                split.setdefault(name, []).append(ev[i].elapsed_time(ev[i + 1]) * 1e3)
+    split = {k: statistics.median(v) for k, v in split.items()}
+    fine_flop = 2.0 * rows * W * 32 * 128
+    split["fine_logits_tflops_32_heads"] = fine_flop / (split["fine_logits"] * 1e-6) / 1e12
+    del coarse, sc
+    # parity spot check: two rows through the fixed-order scorer against the oracle's composition
+    parity = None
+    if not args.no_parity:
+        scorer.impl = "simt"
+        got = scorer.select(q[:2], st, 0, prefix, 0, 0, fixed, 0.0883883).cpu().numpy()
+        scorer.impl = "auto"
+        q8o, wo = oracle.pack_q(q[:2].float().cpu().numpy(), 32, np.float32(0.0883883 / 4))
+        co = oracle.score_paged(q8o, wo, centers_h.numpy(), np.arange(cp)[None].repeat(2, 0), [C] * 2, C,
+                                relu=False)
+        co[:, ~valid_h[0].numpy()] = -np.inf
+        sel, _ = oracle.page_route(co, pages, take)
+        tb = np.concatenate([sel, np.arange(pages, fp)[None].repeat(2, 0)], 1).astype(np.int32)
+        fo = oracle.score_paged(q8o, wo, fine_h.numpy(), tb, [W] * 2, W, relu=False)
+        fo = oracle.mask_scores(fo, tb, mapping_h[0].numpy().reshape(-1, 64), np.arange(prefix, prefix + 2))
+        want, _ = oracle.topk_transform(fo, [W] * 2, tb, 64, 2048, original_ids=mapping_h[0].numpy())
+        parity = {"rows": 2, "scorer": "simt (fixed order)", "bit_exact": bool(np.array_equal(got, want)),
+                  "ids_differing": int((got != want).sum())}
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        q8o, wo = oracle.pack_q(q[:1].float().cpu().numpy(), 32, np.float32(0.0883883 / 4))
+        ch, fh, mh = centers_h.numpy(), fine_h.numpy(), mapping_h[0].numpy()
+
+        def cpu_row():
+            co = oracle.score_paged(q8o, wo, ch, np.arange(cp)[None], [C], C, relu=False, exact=False)
+            co[:, ~valid_h[0].numpy()] = -np.inf
+            sel, _ = oracle.page_route(co, pages, take)
+            tb = np.concatenate([sel, np.arange(pages, fp)[None]], 1).astype(np.int32)
+            fo = oracle.score_paged(q8o, wo, fh, tb, [W], W, relu=False, exact=False)
+            fo = oracle.mask_scores(fo, tb, mh.reshape(-1, 64), [prefix])
+            oracle.topk_transform(fo, [W], tb, 64, 2048, original_ids=mh)
+
+        rate, n, el = _cpu_rate(cpu_row, 1)
+        cpu = {"value": rate, "unit": "rows/s", "cores": torch.get_num_threads(), "kind": "port",
+               "sample": f"{n} single-row selects of this workload, oracle (numpy, BLAS logits), {el:.1f} s"}
+    line = _component_line(args, world, "signed-score selected rows/s (Scorer.select, v1 mode)", "rows/s", value,
+                           args.steps, ms, clk,
+                           {"workload": "signed", "rows": rows, "prefix": prefix, "built_pages": pages,
+                            "take": take, "fixed_pages": fixed_n, "fine_candidates": W, "q_heads": 4,
+                            "scored_heads": 32, "bytes_per_step": bytes_per_step,
+                            "l2": "the logit matrices (61 + 256 MB) exceed L2 every step"},
+                           bytes_per_step, "score_tc_kernel (fine logits)", 6, cpu, parity)
+    line["us_per_step"] = ms / args.steps * 1e3
+    line["stage_us"] = split
+    return line
+
+
 def run_component(args):
     world, rank, device, dist = _dist_setup()
     importlib.import_module("10_20_b200").load()
@@ -838,6 +984,8 @@ def run_component(args):
         line = run_build_workload(args, world, rank, device, dist)
     elif args.workload == "shared":
         line = run_shared_workload(args, world, rank, device, dist)
+    elif args.workload == "signed":
+        line = run_signed_workload(args, world, rank, device, dist)
     else:
         line = run_pages_workload(args, world, rank, device, dist)
     if rank == 0:
@@ -1254,17 +1402,18 @@ def main():
                     help="override the per-GPU batch (small cases for profiling; not a bench config)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="decode",
-                    choices=["decode", "single", "sort", "gather", "pages", "build", "shared"],
+                    choices=["decode", "single", "sort", "gather", "pages", "build", "shared", "signed"],
                     help="decode (the headline), single (1024 single-head queries), sort (_sort, 256 x 65,536 "
                          "records), gather (_gather_slots, 1024 x 2048 slots of 576 bf16), pages (page "
                          "lifecycle), build (index build, 1024 buckets per step), shared (published-end "
-                         "shared-tail preparation, 4096-row chunk)")
+                         "shared-tail preparation, 4096-row chunk), signed (the signed-score Scorer.select of "
+                         "a 1024-row chunk)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-parity", action="store_true", help="skip the oracle spot check of sampled rows")
     ap.add_argument("--inflight", type=int, default=3,
                     help="independent batches in flight (the gather of one overlaps the selection of the next)")
     args = ap.parse_args()
-    if args.workload in ("sort", "gather", "pages", "build", "shared"):
+    if args.workload in ("sort", "gather", "pages", "build", "shared", "signed"):
         if args.impl == "reference":
             if int(os.environ.get("RANK", "0")) == 0:
                 print(json.dumps({"impl": "reference", "workload": args.workload,

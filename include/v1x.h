@@ -569,7 +569,8 @@ V1X_API int v1x_score_fp8_ex(const uint8_t* q, const float* w, const uint8_t* po
  * q u8 (e4m3) [batch, heads, 128], 16-byte aligned; w f32 [batch, heads]; k u8
  * (e4m3) [kv_len, 128], 16-byte aligned; k_scale f32 [kv_len]; out f32 [batch,
  * out_stride >= kv_len].  relu = 0 gives the signed variant.  heads <= 64, the
- * SIMT scorer's fixed fp32 evaluation order. */
+ * SIMT scorer's fixed fp32 evaluation order; heads of weight 0 are skipped (their
+ * terms are +-0 for finite inputs). */
 V1X_API int v1x_mqa_logits_fp8(const uint8_t* q, const float* w, const uint8_t* k, const float* k_scale,
                   int64_t kv_len, const int32_t* starts, const int32_t* ends, float* out,
                   int64_t out_stride, int64_t heads, int relu, int clean, int64_t batch, void* stream);

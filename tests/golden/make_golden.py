@@ -565,6 +565,36 @@ def gen_shared(un, sk):
     save("shared_tail", **out)
 
 
+def gen_signed(nk, pk, gr):
+    """The signed-score path's Triton ops and torch math: NA/kernels.py
+    mask_scores (:40-59), the probe's pack_q (qwen_gqa_probe_kernels.py:14-20)
+    and NA/grouping.py quantize (:41-44)."""
+    gen = torch.Generator().manual_seed(23)
+    out = {}
+    rows, width, pages = 6, 1100, 40
+    for i, (dedup, fixed) in enumerate(((0, 0), (256, 2000))):
+        scores = torch.randn((rows, width + 4), generator=gen)[:, :width]   # row stride 1104
+        table = torch.randint(0, pages, (rows, (width + 63) // 64), generator=gen, dtype=torch.int32)
+        mapping = torch.randint(-5, 3000, (pages * 64,), generator=gen, dtype=torch.int32)
+        positions = torch.randint(0, 3000, (rows,), generator=gen, dtype=torch.int32)
+        pre = f"mask{i}_"
+        out.update({pre + "scores_in": scores.clone(), pre + "table": table, pre + "mapping": mapping,
+                    pre + "positions": positions, pre + "dedup": i32([dedup, fixed])})
+        nk.mask_scores(scores, table, mapping, positions, dedup, fixed)
+        out[pre + "scores_out"] = scores.contiguous()
+    q = torch.randn((5, 8, 128), generator=gen) * torch.logspace(-5, 2, 5)[:, None, None]
+    q[2] = 0
+    q = q.to(torch.bfloat16)
+    qh = q[:, 4:8]                                  # the probe packs a 4-head group of a wider q
+    q8 = torch.zeros((7, 32, 128), dtype=torch.float8_e4m3fn)
+    w = torch.zeros((7, 32), dtype=torch.float32)
+    pk.pack_q[(7, 32)](qh, q8, w, 5, qh.stride(0), qh.stride(1), 0.0883883)
+    qq, qs = gr.quantize(q)
+    out.update(q=q.view(torch.int16), pack_q8=q8.view(torch.uint8), pack_w=w,
+               quant_q8=qq.view(torch.uint8), quant_scale=qs)
+    save("signed", **out)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
@@ -581,7 +611,10 @@ def main():
                 shared_tail=lambda: gen_shared(load("ref_union", Path(args.reference) /
                                                     "experiments/tail_union_lab_20261021/union.py"),
                                                load("ref_shared_kernels", Path(args.reference) /
-                                                    "experiments/fine_pool_shared_20261021/kernels.py")))
+                                                    "experiments/fine_pool_shared_20261021/kernels.py")),
+                signed=lambda: gen_signed(nk, load("ref_probe_kernels", Path(args.reference) /
+                                                   "qwen_gqa_probe_kernels.py"),
+                                          load("ref_grouping", root / "v1_native/grouping.py")))
     for name, job in jobs.items():
         if args.only and name not in args.only.split(","):
             continue

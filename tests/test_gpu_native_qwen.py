@@ -375,3 +375,42 @@ def test_shared_select_matches_oracle():
     sc = O.mask_scores(sc, table, mapping[1].reshape(-1, 64), np.arange(prefix, prefix + rows), take * 64, 6000)
     want, _ = O.topk_transform(sc, [W] * rows, table, 64, 2048, original_ids=np.arange(phys * 64))
     np.testing.assert_array_equal(got.cpu().numpy(), want)
+
+
+def test_mask_scores_and_quantize_golden(golden):
+    g = golden("signed")
+    for i in range(2):
+        pre = f"mask{i}_"
+        dedup, fixed = g[pre + "dedup"].tolist()
+        rows, width = g[pre + "scores_in"].shape
+        buf = torch.zeros((rows, width + 4), device=DEV)
+        buf[:, :width] = torch.from_numpy(g[pre + "scores_in"]).to(DEV)
+        gather.mask_scores(buf[:, :width], torch.from_numpy(g[pre + "table"]).to(DEV),
+                           torch.from_numpy(g[pre + "mapping"]).to(DEV), torch.from_numpy(g[pre + "positions"]).to(DEV),
+                           dedup, fixed)
+        np.testing.assert_array_equal(buf[:, :width].cpu().numpy(), g[pre + "scores_out"])
+    q = torch.from_numpy(g["q"]).view(torch.bfloat16).to(DEV)
+    qq, qs = native_scoring.quantize(q)
+    np.testing.assert_array_equal(_u8(qq), g["quant_q8"])
+    np.testing.assert_array_equal(qs.cpu().numpy(), g["quant_scale"])
+
+
+@pytest.mark.parametrize("levels", [None, 40, 2])
+def test_topk_transform_wide_rows(levels):
+    """Rows wider than the shared-memory stage (the unstaged mode with its
+    selection bitmap): distinct values, a crowded threshold bin, mass ties."""
+    rng = np.random.default_rng(100 + (levels or 0))
+    rows, cols, K = 5, 62532, 2048
+    s = _scores(rng, rows, cols, levels)
+    s[4] = -np.inf
+    lens = np.array([cols, cols - 1000, 50000, 2049, cols], np.int32)
+    P = (cols + 63) // 64
+    table = np.stack([rng.permutation(P) for _ in range(rows)]).astype(np.int32)
+    ids = rng.integers(-1, 1 << 30, P * 64).astype(np.int32)
+    out = torch.empty((rows, K), dtype=torch.int32, device=DEV)
+    raw = torch.empty_like(out)
+    topk2048.transform(torch.from_numpy(s).to(DEV), torch.from_numpy(lens).to(DEV), torch.from_numpy(table).to(DEV),
+                       out, 64, raw, torch.from_numpy(ids).to(DEV))
+    want_out, want_raw = O.topk_transform(s, lens, table, 64, K, original_ids=ids)
+    np.testing.assert_array_equal(raw.cpu().numpy(), want_raw)
+    np.testing.assert_array_equal(out.cpu().numpy(), want_out)
