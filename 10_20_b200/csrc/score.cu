@@ -216,6 +216,11 @@ int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t 
                  const int32_t* table, int64_t table_stride, float* out, int64_t out_stride, int64_t max_len,
                  float* page_max, int64_t page_stride, int64_t heads, int relu, int clean, int lens_kind,
                  int64_t batch, int32_t* status, cudaStream_t stream);
+int score_fp8_tc_grouped(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages,
+                         const int32_t* lens, const int32_t* table, int64_t table_stride, int64_t max_len,
+                         const int32_t* colmap, int64_t colmap_stride, int64_t colmap_pages, float* out,
+                         int64_t out_stride, int64_t group_rows, int64_t real_rows, int relu, int64_t vrows,
+                         int32_t* status, cudaStream_t stream);
 
 namespace {
 int score_dispatch(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages, const int32_t* lens,
@@ -278,8 +283,91 @@ int mqa_flat(const uint8_t* q, const float* w, const uint8_t* k, const float* k_
   else launch_kernel(score_simt_kernel<0, true>, grid, dim3(kScoreThreads), 0, as_stream(stream), a);
   return launch_status("v1x_mqa_logits_fp8");
 }
+// Column map of the grouped scorer, page-major: colmap[p, r] (row stride
+// `cstride`) = a column c of row r whose page table entry is p (-1: none).
+// Every other column of the row -- a second column of the same page, or a page
+// outside the pool -- is listed in `fix` as (row, column, source column or -1)
+// behind a count in fix[0].
+__global__ void column_map_kernel(const int32_t* __restrict__ tables, int64_t tstride, int64_t cols, int64_t rows,
+                                  int64_t pool_pages, int64_t cstride, int32_t* __restrict__ colmap,
+                                  int32_t* __restrict__ fix) {
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (t >= rows * cols) return;
+  const int64_t r = t / cols, c = t % cols;
+  const int64_t p = tables[r * tstride + c];
+  int old = -1;
+  if (p >= 0 && p < pool_pages) {
+    old = atomicCAS(&colmap[p * cstride + r], -1, static_cast<int>(c));
+    if (old == -1) return;
+  }
+  const int k = atomicAdd(fix, 1);
+  fix[1 + 3 * k] = static_cast<int>(r);
+  fix[2 + 3 * k] = static_cast<int>(c);
+  fix[3 + 3 * k] = old;
+}
+
+// The listed columns: a copy of the source column's 64 logits (the same page's
+// keys), or zeros for a page outside the pool (what the per-row scorer's
+// zero-filled loads give).  One warp per entry.
+__global__ void fix_columns_kernel(const int32_t* __restrict__ fix, float* __restrict__ out, int64_t out_stride) {
+  const int n = fix[0];
+  const int lane = threadIdx.x & 31;
+  for (int e = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; e < n; e += (gridDim.x * blockDim.x) >> 5) {
+    const int64_t r = fix[1 + 3 * e], c = fix[2 + 3 * e], src = fix[3 + 3 * e];
+    float* row = out + r * out_stride;
+    for (int j = lane; j < 64; j += 32) row[c * 64 + j] = src >= 0 ? row[src * 64 + j] : 0.0f;
+  }
+}
 }  // namespace
 }  // namespace v1x
+
+extern "C" int v1x_score_fp8_grouped(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages,
+                                     int64_t keys, const int32_t* table, const int32_t* row_tables,
+                                     int64_t row_table_stride, int64_t row_table_cols, int32_t* workspace,
+                                     float* out, int64_t out_stride, int64_t heads, int64_t group_rows,
+                                     int64_t rows, int relu, int32_t* status, void* stream) {
+  using namespace v1x;
+  clear_error();
+  V1X_CHECK_ARG(heads == 4, "score_fp8_grouped: four heads per query row");
+  V1X_CHECK_ARG(group_rows == 8 || group_rows == 16 || group_rows == 32,
+                "score_fp8_grouped: group_rows must be 8, 16 or 32");
+  V1X_CHECK_ARG(rows >= 0 && keys >= 0 && pool_pages > 0 && pool_pages < (int64_t(1) << 31),
+                "score_fp8_grouped: bad geometry");
+  V1X_CHECK_ARG(table, "score_fp8_grouped: the shared key table is required");
+  const int64_t vrows = (rows + group_rows - 1) / group_rows;
+  V1X_CHECK_ARG(vrows <= kTcMaxRows, "score_fp8_grouped: too many rows");
+  if (row_tables) {
+    V1X_CHECK_ARG(workspace && row_table_cols >= 0 && row_table_stride >= row_table_cols &&
+                      out_stride >= row_table_cols * 64,
+                  "score_fp8_grouped: bad row tables / workspace / out stride");
+    V1X_CHECK_ARG(rows * row_table_cols < (int64_t(1) << 31) / 3, "score_fp8_grouped: row tables too large");
+  } else {
+    V1X_CHECK_ARG(out_stride >= keys, "score_fp8_grouped: out row stride < keys");
+  }
+  if (rows == 0 || keys == 0 || (row_tables && row_table_cols == 0)) return V1X_OK;
+  cudaStream_t s = as_stream(stream);
+  int32_t* colmap = nullptr;
+  int32_t* fix = nullptr;
+  const int64_t padded = vrows * group_rows;
+  if (row_tables) {
+    colmap = workspace;
+    fix = workspace + pool_pages * padded;
+    cudaMemsetAsync(colmap, 0xFF, static_cast<size_t>(pool_pages * padded) * 4, s);
+    cudaMemsetAsync(fix, 0, 4, s);
+    const int64_t n = rows * row_table_cols;
+    column_map_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(
+        row_tables, row_table_stride, row_table_cols, rows, pool_pages, padded, colmap, fix);
+    if (int rc = launch_status("v1x_score_fp8_grouped (column map)")) return rc;
+  }
+  if (int rc = score_fp8_tc_grouped(q, w, pool, pool_pages, nullptr, table, 0, keys, colmap, padded, pool_pages,
+                                    out, out_stride, group_rows, rows, relu, vrows, status, s))
+    return rc;
+  if (row_tables) {
+    fix_columns_kernel<<<static_cast<unsigned>(num_sms()), 256, 0, s>>>(fix, out, out_stride);
+    return launch_status("v1x_score_fp8_grouped (fix columns)");
+  }
+  return V1X_OK;
+}
 
 extern "C" int v1x_score_fp8(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages,
                              const int32_t* lens, const int32_t* table, int64_t table_stride,

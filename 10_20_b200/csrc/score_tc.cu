@@ -51,7 +51,7 @@ using namespace sm100;
 constexpr int kProducers = 2;                      // TMA issuing warps
 constexpr int kMmaWarp = kProducers;
 constexpr int kEpiWarp0 = kProducers + 1;          // first epilogue warp
-constexpr int kTcThreads = 32 * (kProducers + 1 + 8);  // two epilogue groups (the most)
+constexpr int kTcThreads = 32 * (kProducers + 1 + 16);  // four epilogue groups (the most)
 template <int kGroups>
 constexpr int tc_threads() { return 32 * (kProducers + 1 + 4 * kGroups); }
 constexpr int kTcStages = 4;      // key smem stages (2 pages each)
@@ -74,6 +74,16 @@ struct TcArgs {
   int B, H, N, relu, clean, w_rows, lens_kind;  // N: MMA width (H, or 16 for one head)
   uint32_t tmem_cols;
   int32_t* status;
+  // grouped mode: a virtual row is group_rows query rows of four heads each
+  // (H = N = 4 * group_rows columns), scored against one shared key table; the
+  // logit of query row r for key j goes to gout[r, colmap[page(j), r] * 64 +
+  // j % 64] (or gout[r, j] without a column map), rows >= real_rows dropped.
+  // colmap is page-major: [colmap_pages, colmap_stride >= virtual rows x group_rows]
+  const int32_t* colmap;
+  int64_t colmap_stride, colmap_pages;
+  float* gout;
+  int64_t gout_stride;
+  int real_rows, group_rows;
 };
 
 struct TcShared {
@@ -104,7 +114,7 @@ __device__ __forceinline__ void raise_abort(TcShared& sh, int32_t* status) {
 }
 
 __device__ __forceinline__ int64_t row_eff(const TcArgs& a, int b) {
-  return min(score_len(a.lens[b], a.lens_kind), a.max_len);
+  return a.lens ? min(score_len(a.lens[b], a.lens_kind), a.max_len) : a.max_len;  // no lengths: every row max_len
 }
 
 __device__ __forceinline__ int tiles_of(const TcArgs& a, int b) {
@@ -138,8 +148,8 @@ struct TileCursor {
 // take a while to reduce), one for a single head, whose epilogue is one TMEM
 // column per key -- that CTA has 224 threads and at most 97 registers each, so
 // two of them leave an SM room for another batch's top-k or route CTA.
-template <int kGroups>
-__global__ void __launch_bounds__(tc_threads<kGroups>(), kGroups == 2 ? 2 : 3)
+template <int kGroups, bool kGrouped = false>
+__global__ void __launch_bounds__(tc_threads<kGroups>(), kGroups == 4 ? 1 : (kGroups == 2 ? 2 : 3))
     score_tc_kernel(const __grid_constant__ CUtensorMap pool_map, const __grid_constant__ CUtensorMap q_map,
                     const __grid_constant__ CUtensorMap scale_map, const __grid_constant__ TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
@@ -330,6 +340,53 @@ __global__ void __launch_bounds__(tc_threads<kGroups>(), kGroups == 2 ? 2 : 3)
       tc_fence_after();
       float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
       const uint32_t ta = tmem + (static_cast<uint32_t>(q4 * 32) << 16) + static_cast<uint32_t>(acc * a.N);
+      if constexpr (kGrouped) {
+        // four heads per query row: columns 4g..4g+3 are row b * G + g; the
+        // head sum keeps the per-row epilogue's order (four partial sums, one
+        // head each, then (s0 + s1) + (s2 + s3)), so the logits are those of
+        // the per-row path with the heads padded by zero weights
+        const bool live = key < eff;
+        // the warp's 32 keys lie in one page: lane l fetches query row b * G + l's
+        // column of it, handed to the other lanes by shuffles below
+        int cm_lane = -1;
+        if (a.colmap) {
+          const int64_t key0 = static_cast<int64_t>(cur.t) * 128 + q4 * 32;
+          const int64_t wpage = key0 < eff ? a.table[b * a.table_stride + (key0 >> 6)] : -1;
+          if (wpage >= 0 && wpage < a.colmap_pages && lane < a.group_rows)
+            cm_lane = a.colmap[wpage * a.colmap_stride + static_cast<int64_t>(b) * a.group_rows + lane];
+        }
+        for (int c0 = 0; c0 < a.N; c0 += 32) {
+          uint32_t v[32];
+          tmem_ld32(ta + c0, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int g4 = 0; g4 < 32; g4 += 4) {
+            const int row = b * a.group_rows + ((c0 + g4) >> 2);
+            const float4 w4 = *reinterpret_cast<const float4*>(wr + c0 + g4);
+            float v0 = __uint_as_float(v[g4]), v1 = __uint_as_float(v[g4 + 1]);
+            float v2 = __uint_as_float(v[g4 + 2]), v3 = __uint_as_float(v[g4 + 3]);
+            if (a.relu) {
+              v0 = fmaxf(v0, 0.0f);
+              v1 = fmaxf(v1, 0.0f);
+              v2 = fmaxf(v2, 0.0f);
+              v3 = fmaxf(v3, 0.0f);
+            }
+            const float sum = (fmaf(w4.x, v0, 0.0f) + fmaf(w4.y, v1, 0.0f)) +
+                              (fmaf(w4.z, v2, 0.0f) + fmaf(w4.w, v3, 0.0f));
+            const int cm = __shfl_sync(0xffffffffu, cm_lane, (c0 + g4) >> 2);
+            if (live && row < a.real_rows) {
+              int64_t col = key;
+              if (a.colmap) col = cm >= 0 ? static_cast<int64_t>(cm) * 64 + (key & 63) : -1;
+              if (col >= 0) a.gout[row * a.gout_stride + col] = sum * scale;
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&sh.tempty[acc]);
+        mbar_arrive(&sh.sempty[r]);
+        cur.advance(prefix, kGroups);
+        continue;
+      }
       if (a.H == 1) {  // column 0 only: the other 15 belong to the next rows' queries
         float v0 = __uint_as_float(tmem_ld1(ta));
         tmem_ld_wait();
@@ -418,6 +475,19 @@ int encode(PFN_cuTensorMapEncodeTiled_v12000 enc, CUtensorMap* m, CUtensorMapDat
   return V1X_OK;
 }
 
+struct GroupedOut {
+  const int32_t* colmap;
+  int64_t colmap_stride, colmap_pages;
+  float* out;
+  int64_t out_stride;
+  int64_t real_rows, group_rows;
+};
+
+int score_tc_launch(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages, const int32_t* lens,
+                    const int32_t* table, int64_t table_stride, float* out, int64_t out_stride, int64_t max_len,
+                    float* page_max, int64_t page_stride, int64_t heads, int relu, int clean, int lens_kind,
+                    int64_t batch, int32_t* status, cudaStream_t stream, const GroupedOut* grp);
+
 }  // namespace
 
 // Launch the tensor-core scorer; returns V1X_ERR_UNSUPPORTED if the shape is not covered.
@@ -425,6 +495,26 @@ int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t 
                  const int32_t* table, int64_t table_stride, float* out, int64_t out_stride, int64_t max_len,
                  float* page_max, int64_t page_stride, int64_t heads, int relu, int clean, int lens_kind,
                  int64_t batch, int32_t* status, cudaStream_t stream) {
+  return score_tc_launch(q, w, pool, pool_pages, lens, table, table_stride, out, out_stride, max_len, page_max,
+                         page_stride, heads, relu, clean, lens_kind, batch, status, stream, nullptr);
+}
+
+// Grouped mode: `vrows` virtual rows of group_rows query rows x 4 heads.
+int score_fp8_tc_grouped(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages,
+                         const int32_t* lens, const int32_t* table, int64_t table_stride, int64_t max_len,
+                         const int32_t* colmap, int64_t colmap_stride, int64_t colmap_pages, float* out,
+                         int64_t out_stride, int64_t group_rows, int64_t real_rows, int relu, int64_t vrows,
+                         int32_t* status, cudaStream_t stream) {
+  const GroupedOut g{colmap, colmap_stride, colmap_pages, out, out_stride, real_rows, group_rows};
+  return score_tc_launch(q, w, pool, pool_pages, lens, table, table_stride, nullptr, 0, max_len, nullptr, 0,
+                         4 * group_rows, relu, 0, 0, vrows, status, stream, &g);
+}
+
+namespace {
+int score_tc_launch(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages, const int32_t* lens,
+                    const int32_t* table, int64_t table_stride, float* out, int64_t out_stride, int64_t max_len,
+                    float* page_max, int64_t page_stride, int64_t heads, int relu, int clean, int lens_kind,
+                    int64_t batch, int32_t* status, cudaStream_t stream, const GroupedOut* grp) {
   if ((heads != 1 && heads % 32 != 0) || heads > 128 || batch > kMaxTcRows || pool_pages >= (int64_t(1) << 31)) {
     set_error("score_fp8 (tensor core): heads must be 1 or a multiple of 32 <= 128 and batch <= %d", kMaxTcRows);
     return V1X_ERR_UNSUPPORTED;
@@ -493,13 +583,24 @@ int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t 
   TcArgs args{lens, table, table_stride, w, out, out_stride, max_len, page_max, page_stride,
               static_cast<int>(batch), static_cast<int>(heads), static_cast<int>(n_mma), relu, clean,
               static_cast<int>(w_rows), lens_kind,
-              cols, status};
+              cols, status, nullptr, 0, 0, nullptr, 0, 0, 0};
   static DeviceOnce once;
   once.run([] {
     cudaFuncSetAttribute(score_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     cudaFuncSetAttribute(score_tc_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(score_tc_kernel<4, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   });
-  if (heads == 1)
+  if (grp) {
+    args.colmap = grp->colmap;
+    args.colmap_stride = grp->colmap_stride;
+    args.colmap_pages = grp->colmap_pages;
+    args.gout = grp->out;
+    args.gout_stride = grp->out_stride;
+    args.real_rows = static_cast<int>(grp->real_rows);
+    args.group_rows = static_cast<int>(grp->group_rows);
+    launch_kernel(score_tc_kernel<4, true>, dim3(static_cast<unsigned>(grid)), dim3(tc_threads<4>()), smem, stream,
+                  pool_map, q_map, scale_map, args);
+  } else if (heads == 1)
     launch_kernel(score_tc_kernel<1>, dim3(static_cast<unsigned>(grid)), dim3(tc_threads<1>()), smem, stream,
                   pool_map, q_map, scale_map, args);
   else
@@ -507,5 +608,6 @@ int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t 
                   pool_map, q_map, scale_map, args);
   return launch_status("v1x_score_fp8 (tensor core)");
 }
+}  // namespace
 
 }  // namespace v1x

@@ -368,8 +368,18 @@ __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 2 : 4) topk_kernel
 #pragma unroll
         for (int j = 0; j < kRegKeys; ++j)
           if (j * nt + tid < c.L) atomicAdd(&hist[bin_of(kr[j])], 1);
+      } else if constexpr (kMode == 0) {
+        // eight loads in flight per thread: the row streams from global memory
+        for (int i0 = tid; i0 < c.L; i0 += 8 * nt) {
+          float v[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) v[u] = i0 + u * nt < c.L ? __ldcg(srow + i0 + u * nt) : 0.0f;
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            if (i0 + u * nt < c.L) atomicAdd(&hist[bin_of(order_key(v[u]))], 1);
+        }
       } else {
-        for (int i = tid; i < c.L; i += nt) atomicAdd(&hist[bin_of(kMode == 0 ? order_key(srow[i]) : keys[i])], 1);
+        for (int i = tid; i < c.L; i += nt) atomicAdd(&hist[bin_of(keys[i])], 1);
       }
       __syncthreads();
       tb = find_top_bin<kThreads>(a.topk, hist, sm.warp_tot, &sm.res);
@@ -406,6 +416,17 @@ __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 2 : 4) topk_kernel
 #pragma unroll
           for (int j = 0; j < kRegKeys; ++j)
             if (j < nsl) append(j, kr[j]);
+        } else if constexpr (kMode == 0) {
+          // four slices' loads in flight before their keys are appended
+          for (int j0 = 0; j0 < nsl; j0 += 4) {
+            uint32_t kk[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              kk[u] = (j0 + u) * nt + tid < c.L ? order_key(__ldcg(srow + (j0 + u) * nt + tid)) : 0u;
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              if (j0 + u < nsl) append(j0 + u, kk[u]);
+          }
         } else {
           for (int j = 0; j < nsl; ++j) append(j, j * nt + tid < c.L ? key_of(j) : 0u);
         }

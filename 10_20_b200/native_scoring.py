@@ -84,11 +84,25 @@ def quantize(x):
     return q8.reshape(*lead, 128), w.reshape(lead)
 
 
+GROUP_ROWS = 32   # query rows per tensor-core operand of the grouped scorer
+
+
+class _Packed:
+    """A chunk's packed queries: ``grouped`` = four heads per row, rows padded to
+    GROUP_ROWS (the grouped scorer); else the reference's 32-head layout."""
+
+    def __init__(self, q8, weights, rows, grouped):
+        self.q8, self.weights, self.rows, self.grouped = q8, weights, rows, grouped
+
+
 class Scorer:
     """NA/scoring.py:25-99 on libv1x.so (sm_100a; the reference requires SM90 and
-    its no-ReLU DeepGEMM fork).  ``impl`` (extension) picks the scorer of
-    ``scoring.fp8_paged_mqa_logits``: "auto" (tensor cores at 32 heads) or
-    "simt" (fixed fp32 evaluation order)."""
+    its no-ReLU DeepGEMM fork).  ``impl`` (extension) picks the paged scorer:
+    "auto" -- the grouped tensor-core scorer, 32 query rows x 4 heads per MMA
+    operand, so that a key tile is read once per 32 rows (same logits as the
+    per-row scorer); "tensor_core" -- the per-row tensor-core scorer over the 32
+    padded heads, as the reference's DeepGEMM call; "simt" -- the fixed fp32
+    evaluation order."""
 
     def __init__(self, config, device):
         self.config = config
@@ -118,6 +132,30 @@ class Scorer:
         return scoring.fp8_paged_mqa_logits(q8, cache, weights, lengths, table, None, count,
                                             clean_logits=False, relu=False, impl=self.impl)
 
+    def _pack(self, q, scale):
+        rows = q.shape[0]
+        if self.impl != "auto":
+            q8, w = pack_q(q, scale)
+            return _Packed(q8, w, rows, False)
+        R = -(-rows // GROUP_ROWS) * GROUP_ROWS
+        q8 = torch.empty((R, 4, 128), dtype=torch.float8_e4m3fn, device=q.device)
+        w = torch.empty((R, 4), dtype=torch.float32, device=q.device)
+        pack_q(q, scale, out_heads=4, out=(q8, w))
+        return _Packed(q8, w, rows, True)
+
+    def _logits(self, qp, cache, pages, keys, row_tables=None):
+        """Logits of the packed rows over `cache`: without row tables [rows, keys]
+        of the keys of `pages` (one table shared by the rows); with row tables
+        [rows, 64 * P] of each row's own pages, every one of them in `pages`."""
+        if qp.grouped:
+            width = row_tables.shape[1] * 64 if row_tables is not None else keys
+            out = torch.empty((qp.rows, width), dtype=torch.float32, device=qp.q8.device)
+            return scoring.paged_logits_grouped(qp.q8, qp.weights, cache, pages, keys, out, row_tables, GROUP_ROWS,
+                                                relu=False, rows=qp.rows)
+        if row_tables is not None:
+            return self.paged(qp.q8, qp.weights, cache, row_tables, row_tables.shape[1] * 64)
+        return self.paged(qp.q8, qp.weights, cache, pages[None].expand(qp.rows, -1).contiguous(), keys)
+
     def select(self, q, state, head, prefix, offset, total, fixed, scale):
         if self.query_graph and self._graph_eligible(state):
             return self._select_graph(q, state, head, prefix, offset, total, fixed, scale)
@@ -129,17 +167,18 @@ class Scorer:
         rows, qheads, dim = q.shape
         if dim != 128 or qheads != 4:
             raise ValueError("This backend preserves Qwen's four-Q-head routing group")
-        q8, weights = pack_q(q, scale)
         positions = torch.arange(prefix + offset, prefix + offset + rows, device=q.device, dtype=torch.int32)
         if self.config.mode == "dsa":
+            q8, weights = pack_q(q, scale)
             scores = scoring.fp8_mqa_logits(q8, (state.flat_k[head, :total], state.flat_scale[head, :total]),
                                             weights, torch.zeros_like(positions), positions + 1, True, relu=False)
             return topk2048(scores, need_values=False)[1].int()
+        qp = self._pack(q, scale)
         pages = state.pages
         centers = pages * 8
         center_pages = (centers + 63) // 64
-        ct = torch.arange(center_pages, device=q.device, dtype=torch.int32)[None].expand(rows, -1).contiguous()
-        coarse = self.paged(q8, weights, state.centers[head], ct, centers)
+        ct = torch.arange(center_pages, device=q.device, dtype=torch.int32)
+        coarse = self._logits(qp, state.centers[head], ct, centers)
         coarse = coarse[:, :centers]
         coarse.masked_fill_(~state.valid[head, :centers][None], -torch.inf)
         take = self.config.budget(pages)
@@ -149,7 +188,15 @@ class Scorer:
             table[:, :take] = torch.arange(pages, device=q.device, dtype=torch.int32)
         else:
             _route_into(coarse, table, pages, take)
-        scores = self.paged(q8, weights, state.fine[head], table, table.shape[1] * 64)
+        # the fine pages any row can name: the route's ids (below the smallest
+        # power of two >= max(pages, 128): its blocked layout's padding ids
+        # appear when -inf pages reach the take) and the fixed pages
+        n = 128
+        while n < pages:
+            n *= 2
+        span = min(n if pages <= 4096 else pages, state.fine[head].numel() // 8448)
+        used = torch.cat((torch.arange(span, device=q.device, dtype=torch.int32), fixed.to(torch.int32)))
+        scores = self._logits(qp, state.fine[head], used, used.numel() * 64, table)
         mask_scores(scores, table, state.mapping[head], positions)
         # logical original token positions (not physical slots, no x4 expansion)
         return mapped_top2048(scores, table, state.mapping[head])
@@ -177,9 +224,9 @@ def select(scorer, q, state, head, prefix, offset, total, fixed, scale):
     rows, qheads, dim = q.shape
     if (qheads, dim) != (4, 128):
         raise ValueError("Expected four Q heads of dimension 128")
-    q8, weights = pack_q(q, scale)
+    qp = scorer._pack(q, scale)
     positions = torch.arange(prefix + offset, prefix + offset + rows, device=q.device, dtype=torch.int32)
-    ids = select_tensors(scorer, q8, weights, arena, head, state.table[head], fixed[head], positions,
+    ids = _select_packed(scorer, qp, arena, head, state.table[head], fixed[head], positions,
                          state.full_bucket_append, state.fixed_start)
     arena.record()
     return ids
@@ -193,21 +240,27 @@ def select_tensors(scorer, q8, weights, arena, head, page_ids, fixed_ids, positi
     if decode_meta is not None:
         raise ValueError("decode_meta masks belong to the shared arenas' decode query graph, "
                          "which this library does not provide")
-    rows = len(q8)
+    return _select_packed(scorer, _Packed(q8, weights, len(q8), False), arena, head, page_ids, fixed_ids, positions,
+                          full_bucket_append, fixed_start)
+
+
+def _select_packed(scorer, qp, arena, head, page_ids, fixed_ids, positions, full_bucket_append, fixed_start):
+    rows = qp.rows
+    dev = qp.q8.device
     pages, take = page_ids.numel(), scorer.config.budget(page_ids.numel())
-    selected = torch.empty((rows, take), device=q8.device, dtype=torch.int32)
+    selected = torch.empty((rows, take), device=dev, dtype=torch.int32)
     if take == pages:
-        selected[:] = torch.arange(pages, device=q8.device, dtype=torch.int32)
+        selected[:] = torch.arange(pages, device=dev, dtype=torch.int32)
     else:
-        ct = page_ids[None].expand(rows, -1).contiguous()
-        coarse = scorer.paged(q8, weights, arena.centers[head], ct, pages * 64)
+        coarse = scorer._logits(qp, arena.centers[head], page_ids.to(torch.int32).contiguous(), pages * 64)
         coarse = coarse.reshape(rows, pages, 64)[:, :, :8].contiguous()
         valid = arena.valid[head, page_ids.long()]
         coarse.masked_fill_(~valid[None], -torch.inf)
         coarse = coarse.reshape(rows, pages * 8)
         _route_into(coarse, selected, pages, take)
     table = torch.cat((page_ids[selected.long()], fixed_ids[None].expand(rows, -1)), 1).contiguous()
-    scores = scorer.paged(q8, weights, arena.fine[head], table, table.shape[1] * 64)
+    used = torch.cat((page_ids, fixed_ids)).to(torch.int32).contiguous()
+    scores = scorer._logits(qp, arena.fine[head], used, used.numel() * 64, table)
     mask_scores(scores, table, arena.mapping[head], positions,
                 take * 64 if full_bucket_append else 0, fixed_start if full_bucket_append else 0)
     return mapped_top2048(scores, table, arena.identity)

@@ -122,3 +122,46 @@ def fp8_mqa_logits(q, kv, weights, cu_seqlen_ks, cu_seqlen_ke, clean_logits: boo
               ptr(cu_seqlen_ke), ptr(out), out.stride(0), H, int(bool(relu)), int(bool(clean_logits)), M,
               _lib.stream_of(q), device=q.device)
     return out
+
+
+def paged_logits_grouped(q8, weights, kv_cache, table, keys: int, out, row_tables=None, group_rows: int = 32,
+                         relu: bool = False, rows: int | None = None):
+    """Extension: the signed-score Scorer's paged logits for query rows of four
+    heads that share one key table (``v1x_score_fp8_grouped``).  q8 e4m3 [R, 4,
+    128] and weights float32 [R, 4] with R a multiple of group_rows (rows past
+    ``rows`` zero); table int32 [>= ceil(keys / 64)] of pool pages.  Without
+    ``row_tables``: out[r, j] = the logit of key j (j < keys).  With
+    ``row_tables`` int32 [rows, P]: out[r, c] = the logit of key (row_tables[r,
+    c // 64], c % 64) for c < 64 * P, every page a row names being in ``table``."""
+    R = q8.shape[0]
+    rows = R if rows is None else int(rows)
+    require(q8.dim() == 3 and q8.shape[1:] == (4, 128) and q8.is_contiguous()
+            and q8.dtype in (torch.float8_e4m3fn, torch.uint8), "q8: contiguous e4m3 [R, 4, 128]")
+    require(weights.shape == (R, 4) and weights.dtype == torch.float32 and weights.is_contiguous(),
+            "weights: contiguous float32 [R, 4]")
+    require(R % group_rows == 0 and rows <= R, "q8 rows: a multiple of group_rows, at least rows")
+    require(kv_cache.dtype == torch.uint8 and kv_cache.is_contiguous() and kv_cache.numel() % 8448 == 0,
+            "kv_cache: contiguous packed uint8 pages of 8448 bytes")
+    require(table.dtype == torch.int32 and table.dim() == 1 and table.is_contiguous()
+            and table.numel() * 64 >= keys, "table: int32 [>= ceil(keys / 64)]")
+    require(out.dtype == torch.float32 and out.dim() == 2 and out.shape[0] >= rows and out.stride(1) == 1,
+            "out: float32 [rows, -1]")
+    pool_pages = kv_cache.numel() // 8448
+    ws = None
+    if row_tables is not None:
+        require(row_tables.dtype == torch.int32 and row_tables.dim() == 2 and row_tables.shape[0] == rows
+                and row_tables.stride(1) == 1, "row_tables: int32 [rows, P]")
+        P = row_tables.shape[1]
+        require(out.shape[1] >= P * 64, "out: at least 64 columns per row-table page")
+        padded = -(-rows // group_rows) * group_rows
+        ws = torch.empty(padded * pool_pages + 1 + 3 * rows * P, dtype=torch.int32, device=q8.device)
+    else:
+        require(out.shape[1] >= keys, "out: at least `keys` columns")
+    from .kernels import status_word
+    _lib.same_device(q8, weights, kv_cache, table, out, row_tables)
+    _lib.call("v1x_score_fp8_grouped", ptr(q8), ptr(weights), ptr(kv_cache), pool_pages, int(keys), ptr(table),
+              ptr(row_tables), row_tables.stride(0) if row_tables is not None else 0,
+              row_tables.shape[1] if row_tables is not None else 0, ptr(ws), ptr(out), out.stride(0), 4,
+              int(group_rows), rows, int(bool(relu)), ptr(status_word(q8.device)), _lib.stream_of(q8),
+              device=q8.device)
+    return out

@@ -897,22 +897,22 @@ def run_signed_workload(args, world, rank, device, dist):
     bytes_per_step = (cp + fp) * 8448 + rows * (C * 4 * 2 + W * 4 * 2 + 4 * 128 * 2 + 2048 * 4)
     # stage split of one select (eager, events between the operators)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(8)]
-    q8, w = NS.pack_q(q, 0.0883883)
-    ct = torch.arange(cp, device=device, dtype=torch.int32)[None].expand(rows, -1).contiguous()
+    ct = torch.arange(cp, device=device, dtype=torch.int32)
     table = torch.empty((rows, take + fixed_n), device=device, dtype=torch.int32)
     table[:, take:] = fixed[None]
     positions = torch.arange(prefix, prefix + rows, device=device, dtype=torch.int32)
+    used = torch.cat((torch.arange(min(2048, fp), device=device, dtype=torch.int32), fixed))
     split = {}
     for rep in range(4):
         ev[0].record()
-        q8, w = NS.pack_q(q, 0.0883883)
+        qp = scorer._pack(q, 0.0883883)
         ev[1].record()
-        coarse = scorer.paged(q8, w, st.centers[0], ct, C)
+        coarse = scorer._logits(qp, st.centers[0], ct, C)
         ev[2].record()
         coarse.masked_fill_(~st.valid[0, :C][None], -torch.inf)
         NS.extension(64, 4).route(coarse, table, pages, take)
         ev[3].record()
-        sc = scorer.paged(q8, w, st.fine[0], table, W)
+        sc = scorer._logits(qp, st.fine[0], used, used.numel() * 64, table)
         ev[4].record()
         NS.mask_scores(sc, table, st.mapping[0], positions)
         ev[5].record()
@@ -924,8 +924,9 @@ def run_signed_workload(args, world, rank, device, dist):
                                       "mapped_top2048")):
                 split.setdefault(name, []).append(ev[i].elapsed_time(ev[i + 1]) * 1e3)
     split = {k: statistics.median(v) for k, v in split.items()}
-    fine_flop = 2.0 * rows * W * 32 * 128
-    split["fine_logits_tflops_32_heads"] = fine_flop / (split["fine_logits"] * 1e-6) / 1e12
+    # the grouped scorer's MMAs: every key of the used pages against 32 rows x 4 heads per group
+    fine_flop = 2.0 * (-(-rows // 32)) * used.numel() * 64 * 128 * 128
+    split["fine_logits_mma_tflops"] = fine_flop / (split["fine_logits"] * 1e-6) / 1e12
     del coarse, sc
     # parity spot check: two rows through the fixed-order scorer against the oracle's composition
     parity = None
@@ -965,7 +966,8 @@ def run_signed_workload(args, world, rank, device, dist):
                            args.steps, ms, clk,
                            {"workload": "signed", "rows": rows, "prefix": prefix, "built_pages": pages,
                             "take": take, "fixed_pages": fixed_n, "fine_candidates": W, "q_heads": 4,
-                            "scored_heads": 32, "bytes_per_step": bytes_per_step,
+                            "scorer": "grouped tensor cores: 32 rows x 4 heads per MMA operand",
+                            "bytes_per_step": bytes_per_step,
                             "l2": "the logit matrices (61 + 256 MB) exceed L2 every step"},
                            bytes_per_step, "score_tc_kernel (fine logits)", 6, cpu, parity)
     line["us_per_step"] = ms / args.steps * 1e3

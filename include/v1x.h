@@ -561,6 +561,27 @@ V1X_API int v1x_score_fp8_ex(const uint8_t* q, const float* w, const uint8_t* po
                   int64_t heads, int relu, int clean, int impl, int lens_kind, int32_t* status,
                   int64_t batch, void* stream);
 
+/* Extension (no reference counterpart): the signed-score Scorer's paged logits
+ * (NA/scoring.py:48-53, DeepGEMM over q padded to 32 heads, four of them live)
+ * for groups of query rows that share one key table.  A group of group_rows
+ * rows x 4 heads is one tensor-core MMA operand (N = 4 * group_rows), so a key
+ * tile is read once per group instead of once per row.  Keys j < keys are
+ * (table[j / 64], j % 64) of the pool.  Without row_tables: out[r, j] = the
+ * logit of row r for key j (j < keys).  With row_tables (i32 [rows,
+ * row_table_stride], pool pages): out[r, c] for c < row_table_cols * 64 = the
+ * logit of row r for key (row_tables[r, c / 64], c % 64) -- the shared table
+ * then lists the pool pages any row uses (every page a row table names must be
+ * in it); columns of a page outside the pool are 0.  The logits equal the
+ * per-row tensor-core scorer's (v1x_score_fp8, heads padded with zero weights).
+ * q u8 (e4m3) [ceil(rows / group_rows) * group_rows, 4, 128] and w f32 [same, 4],
+ * zero past `rows`, both 16-byte aligned; group_rows in {8, 16, 32}; workspace
+ * i32 [ceil(rows / group_rows) * group_rows * pool_pages + 1 + 3 * rows *
+ * row_table_cols] (row tables only). */
+V1X_API int v1x_score_fp8_grouped(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages,
+                  int64_t keys, const int32_t* table, const int32_t* row_tables, int64_t row_table_stride,
+                  int64_t row_table_cols, int32_t* workspace, float* out, int64_t out_stride, int64_t heads,
+                  int64_t group_rows, int64_t rows, int relu, int32_t* status, void* stream);
+
 /* FP8 MQA logits over a flat key array -- the DeepGEMM fp8_mqa_logits contract
  * the signed-score Scorer calls in its `dsa` mode (NA/scoring.py:74-78) and the
  * probe backend at qwen_gqa_probe_backend.py:184: out[b, j] = sum_h w[b,h] *

@@ -414,3 +414,89 @@ def test_topk_transform_wide_rows(levels):
     want_out, want_raw = O.topk_transform(s, lens, table, 64, K, original_ids=ids)
     np.testing.assert_array_equal(raw.cpu().numpy(), want_raw)
     np.testing.assert_array_equal(out.cpu().numpy(), want_out)
+
+
+def _packs(q, scale, rows_pad):
+    """(32-head q8, w) and the grouped layout (4 heads, rows padded) of q."""
+    q8, w = native_scoring.pack_q(q, scale)
+    q8c = torch.empty((rows_pad, 4, 128), dtype=torch.float8_e4m3fn, device=DEV)
+    wc = torch.empty((rows_pad, 4), dtype=torch.float32, device=DEV)
+    native_scoring.pack_q(q, scale, out_heads=4, out=(q8c, wc))
+    return q8, w, q8c, wc
+
+
+@pytest.mark.parametrize("relu", [False, True])
+def test_grouped_logits_equal_per_row_scorer(relu):
+    rng = np.random.default_rng(31 + relu)
+    rows, npool = 45, 300
+    pool = torch.from_numpy(_pool(rng, npool)).to(DEV)
+    q = torch.randn((rows, 4, 128), generator=torch.Generator().manual_seed(5)).to(torch.bfloat16).to(DEV)
+    q8, w, q8c, wc = _packs(q, 0.09, 64)
+    assert (q8c[rows:].view(torch.uint8) == 0).all() and (wc[rows:] == 0).all()
+    shared = torch.from_numpy(rng.permutation(npool)[:200].astype(np.int32)).to(DEV)
+    keys = 200 * 64 - 17
+    got = torch.full((rows, keys + 5), 7.0, device=DEV)
+    scoring.paged_logits_grouped(q8c, wc, pool, shared, keys, got, None, 32, relu=relu, rows=rows)
+    lens = torch.full((rows,), keys, dtype=torch.int32, device=DEV)
+    want = scoring.fp8_paged_mqa_logits(q8, pool, w, lens, shared[None].expand(rows, -1).contiguous(), None, keys,
+                                        clean_logits=False, relu=relu, impl="tensor_core")
+    assert torch.equal(got[:, :keys], want)
+    assert (got[:, keys:] == 7.0).all()
+    # per-row tables over the shared pages, a repeated page and a page outside the pool
+    sh = shared.cpu().numpy()
+    rt = np.stack([rng.choice(sh, 30, replace=False) for _ in range(rows)]).astype(np.int32)
+    rt[3, 7] = rt[3, 2]
+    rt[9, 0] = npool + 5
+    rtd = torch.from_numpy(rt).to(DEV)
+    got = torch.full((rows, 30 * 64), 7.0, device=DEV)
+    scoring.paged_logits_grouped(q8c, wc, pool, shared, 200 * 64, got, rtd, 32, relu=relu, rows=rows)
+    ok = rt.copy()
+    ok[9, 0] = sh[0]
+    lens = torch.full((rows,), 30 * 64, dtype=torch.int32, device=DEV)
+    want = scoring.fp8_paged_mqa_logits(q8, pool, w, lens, torch.from_numpy(ok).to(DEV), None, 30 * 64,
+                                        clean_logits=False, relu=relu, impl="tensor_core")
+    g, wnt = got.cpu(), want.cpu()
+    assert (g[9, :64] == 0).all()
+    g[9, :64] = wnt[9, :64]
+    assert torch.equal(g, wnt)
+
+
+@pytest.mark.parametrize("share", [False, True])
+def test_scorer_grouped_equals_per_row_tensor_core(share):
+    rng = np.random.default_rng(41 + share)
+    rows = 70
+    q = torch.randn((rows, 4, 128), generator=torch.Generator().manual_seed(8)).to(torch.bfloat16).to(DEV)
+    if not share:
+        pages, nfixed = 100, 4
+        C, fp = pages * 8, pages + nfixed
+        st = _State()
+        st.pages = pages
+        st.centers = torch.from_numpy(_pool(rng, (C + 63) // 64)[None]).to(DEV)
+        st.fine = torch.from_numpy(_pool(rng, fp)[None]).to(DEV)
+        st.valid = torch.from_numpy(rng.random((1, C)) > 0.1).to(DEV)
+        st.mapping = torch.from_numpy(rng.integers(-1, 5000, (1, fp * 64)).astype(np.int32)).to(DEV)
+        fixed = torch.arange(pages, fp, dtype=torch.int32, device=DEV)
+        cfg = _Config("v1", 0.3)
+        args = (st, 0, 4000, 0, 0, fixed, 0.0883883)
+    else:
+        phys, pages, nfixed = 150, 90, 6
+        arena = _State()
+        arena.centers = torch.from_numpy(_pool(rng, phys)[None]).to(DEV)
+        arena.fine = torch.from_numpy(_pool(rng, phys)[None]).to(DEV)
+        arena.valid = torch.from_numpy(rng.random((1, phys, 8)) > 0.05).to(DEV)
+        arena.mapping = torch.from_numpy(rng.integers(-1, 9000, (1, phys * 64)).astype(np.int32)).to(DEV)
+        arena.identity = torch.arange(phys * 64, dtype=torch.int32, device=DEV)
+        arena.record = lambda: None
+        st = _State()
+        st.arena, st.wait = arena, (lambda: None)
+        st.table = torch.from_numpy(rng.permutation(phys)[None, :pages].astype(np.int32)).to(DEV)
+        st.full_bucket_append, st.fixed_start, st.pages = True, 6000, pages
+        fixed = torch.from_numpy(rng.permutation(phys)[None, :nfixed].astype(np.int32)).to(DEV)
+        cfg = _Config("v1", 0.3, share=True)
+        args = (st, 0, 7000, 0, 0, fixed, 0.1)
+    scorer = native_scoring.Scorer(cfg, DEV)
+    assert scorer.impl == "auto"
+    got = scorer.select(q, *args)
+    scorer.impl = "tensor_core"
+    want = scorer.select(q, *args)
+    assert torch.equal(got, want)
