@@ -81,6 +81,7 @@ struct TcArgs {
   // colmap is page-major: [colmap_pages, colmap_stride >= virtual rows x group_rows]
   const int32_t* colmap;
   int64_t colmap_stride, colmap_pages;
+  const uint8_t* key_valid;  // grouped mode without a column map: key j's logits are -inf where 0
   float* gout;
   int64_t gout_stride;
   int real_rows, group_rows;
@@ -346,6 +347,7 @@ __global__ void __launch_bounds__(tc_threads<kGroups>(), kGroups == 4 ? 1 : (kGr
         // head each, then (s0 + s1) + (s2 + s3)), so the logits are those of
         // the per-row path with the heads padded by zero weights
         const bool live = key < eff;
+        const bool valid = !(a.key_valid && live) || a.key_valid[key] != 0;
         // the warp's 32 keys lie in one page: lane l fetches query row b * G + l's
         // column of it, handed to the other lanes by shuffles below
         int cm_lane = -1;
@@ -377,7 +379,7 @@ __global__ void __launch_bounds__(tc_threads<kGroups>(), kGroups == 4 ? 1 : (kGr
             if (live && row < a.real_rows) {
               int64_t col = key;
               if (a.colmap) col = cm >= 0 ? static_cast<int64_t>(cm) * 64 + (key & 63) : -1;
-              if (col >= 0) a.gout[row * a.gout_stride + col] = sum * scale;
+              if (col >= 0) a.gout[row * a.gout_stride + col] = valid ? sum * scale : -CUDART_INF_F;
             }
           }
         }
@@ -478,6 +480,7 @@ int encode(PFN_cuTensorMapEncodeTiled_v12000 enc, CUtensorMap* m, CUtensorMapDat
 struct GroupedOut {
   const int32_t* colmap;
   int64_t colmap_stride, colmap_pages;
+  const uint8_t* key_valid;
   float* out;
   int64_t out_stride;
   int64_t real_rows, group_rows;
@@ -502,10 +505,10 @@ int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t 
 // Grouped mode: `vrows` virtual rows of group_rows query rows x 4 heads.
 int score_fp8_tc_grouped(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages,
                          const int32_t* lens, const int32_t* table, int64_t table_stride, int64_t max_len,
-                         const int32_t* colmap, int64_t colmap_stride, int64_t colmap_pages, float* out,
-                         int64_t out_stride, int64_t group_rows, int64_t real_rows, int relu, int64_t vrows,
-                         int32_t* status, cudaStream_t stream) {
-  const GroupedOut g{colmap, colmap_stride, colmap_pages, out, out_stride, real_rows, group_rows};
+                         const int32_t* colmap, int64_t colmap_stride, int64_t colmap_pages,
+                         const uint8_t* key_valid, float* out, int64_t out_stride, int64_t group_rows,
+                         int64_t real_rows, int relu, int64_t vrows, int32_t* status, cudaStream_t stream) {
+  const GroupedOut g{colmap, colmap_stride, colmap_pages, key_valid, out, out_stride, real_rows, group_rows};
   return score_tc_launch(q, w, pool, pool_pages, lens, table, table_stride, nullptr, 0, max_len, nullptr, 0,
                          4 * group_rows, relu, 0, 0, vrows, status, stream, &g);
 }
@@ -583,7 +586,7 @@ int score_tc_launch(const uint8_t* q, const float* w, const uint8_t* pool, int64
   TcArgs args{lens, table, table_stride, w, out, out_stride, max_len, page_max, page_stride,
               static_cast<int>(batch), static_cast<int>(heads), static_cast<int>(n_mma), relu, clean,
               static_cast<int>(w_rows), lens_kind,
-              cols, status, nullptr, 0, 0, nullptr, 0, 0, 0};
+              cols, status, nullptr, 0, 0, nullptr, nullptr, 0, 0, 0};
   static DeviceOnce once;
   once.run([] {
     cudaFuncSetAttribute(score_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
@@ -594,6 +597,7 @@ int score_tc_launch(const uint8_t* q, const float* w, const uint8_t* pool, int64
     args.colmap = grp->colmap;
     args.colmap_stride = grp->colmap_stride;
     args.colmap_pages = grp->colmap_pages;
+    args.key_valid = grp->key_valid;
     args.gout = grp->out;
     args.gout_stride = grp->out_stride;
     args.real_rows = static_cast<int>(grp->real_rows);

@@ -552,7 +552,6 @@ __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 2 : 4) topk_kernel
     auto klass = [&](int i, uint32_t k) -> int {
       if (i >= c.L) return 0;
       if (by_bin) {
-        if constexpr (kMode == 0) return static_cast<int>((selbits[i >> 5] >> (i & 31)) & 1u);
         const int b = bin_of(k);
         return (b > tb.bin || (b == tb.bin && ((selbits[i >> 5] >> (i & 31)) & 1u))) ? 1 : 0;
       }
@@ -600,7 +599,26 @@ __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 2 : 4) topk_kernel
         if (lane == 31) sm.carry = make_int2(carry.x + ig, carry.y + ie);
       }
     };
-    if constexpr (kMode == 2) {
+    if (kMode == 0 && by_bin) {
+      // the bitmap holds every pick: a thread takes consecutive bitmap words,
+      // their counts are scanned, and the set bits are emitted in index order
+      const int nw = (c.L + 31) / 32;
+      const int per = (nw + nt - 1) / nt;
+      const int w0 = min(tid * per, nw), w1 = min(w0 + per, nw);
+      int cnt = 0;
+      for (int w = w0; w < w1; ++w) cnt += __popc(selbits[w]);
+      int total;
+      int pos = block_exclusive_scan(cnt, sm.warp_tot, &total);
+      for (int w = w0; w < w1; ++w) {
+        uint32_t bits = selbits[w];
+        while (bits) {
+          const int b = __ffs(bits) - 1;
+          bits &= bits - 1;
+          if (pos < a.topk) emit(pos, w * 32 + b);
+          ++pos;
+        }
+      }
+    } else if constexpr (kMode == 2) {
       // rolled loops over the staged keys: the unrolled mapping epilogue would be
       // kRegKeys copies of a long code path
 #pragma unroll 1
@@ -614,14 +632,13 @@ __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 2 : 4) topk_kernel
       int2 carry = make_int2(0, 0);
       for (int j0 = 0; j0 < nsl; j0 += kMaxSlices) {
         const int jn = min(nsl - j0, kMaxSlices);
-        // (the unstaged mode's bitmap classifies without the keys)
         for (int jc = 0; jc < jn; ++jc)
-          count_slice(j0 + jc, jc, (j0 + jc) * nt + tid < c.L && !(kMode == 0 && by_bin) ? key_of(j0 + jc) : 0u);
+          count_slice(j0 + jc, jc, (j0 + jc) * nt + tid < c.L ? key_of(j0 + jc) : 0u);
         __syncthreads();
         scan_counts(jn * kTopkWarps, carry);
         __syncthreads();
         for (int jc = 0; jc < jn; ++jc)
-          place_slice(j0 + jc, jc, (j0 + jc) * nt + tid < c.L && !(kMode == 0 && by_bin) ? key_of(j0 + jc) : 0u);
+          place_slice(j0 + jc, jc, (j0 + jc) * nt + tid < c.L ? key_of(j0 + jc) : 0u);
         carry = sm.carry;
         __syncthreads();
       }

@@ -143,18 +143,22 @@ class Scorer:
         pack_q(q, scale, out_heads=4, out=(q8, w))
         return _Packed(q8, w, rows, True)
 
-    def _logits(self, qp, cache, pages, keys, row_tables=None):
+    def _logits(self, qp, cache, pages, keys, row_tables=None, key_valid=None):
         """Logits of the packed rows over `cache`: without row tables [rows, keys]
-        of the keys of `pages` (one table shared by the rows); with row tables
-        [rows, 64 * P] of each row's own pages, every one of them in `pages`."""
+        of the keys of `pages` (one table shared by the rows; -inf where
+        `key_valid` is False); with row tables [rows, 64 * P] of each row's own
+        pages, every one of them in `pages`."""
         if qp.grouped:
             width = row_tables.shape[1] * 64 if row_tables is not None else keys
             out = torch.empty((qp.rows, width), dtype=torch.float32, device=qp.q8.device)
             return scoring.paged_logits_grouped(qp.q8, qp.weights, cache, pages, keys, out, row_tables, GROUP_ROWS,
-                                                relu=False, rows=qp.rows)
+                                                relu=False, rows=qp.rows, key_valid=key_valid)
         if row_tables is not None:
             return self.paged(qp.q8, qp.weights, cache, row_tables, row_tables.shape[1] * 64)
-        return self.paged(qp.q8, qp.weights, cache, pages[None].expand(qp.rows, -1).contiguous(), keys)
+        out = self.paged(qp.q8, qp.weights, cache, pages[None].expand(qp.rows, -1).contiguous(), keys)
+        if key_valid is not None:
+            out[:, :keys].masked_fill_(~key_valid[:keys].bool()[None], -torch.inf)
+        return out
 
     def select(self, q, state, head, prefix, offset, total, fixed, scale):
         if self.query_graph and self._graph_eligible(state):
@@ -178,9 +182,8 @@ class Scorer:
         centers = pages * 8
         center_pages = (centers + 63) // 64
         ct = torch.arange(center_pages, device=q.device, dtype=torch.int32)
-        coarse = self._logits(qp, state.centers[head], ct, centers)
+        coarse = self._logits(qp, state.centers[head], ct, centers, key_valid=state.valid[head, :centers])
         coarse = coarse[:, :centers]
-        coarse.masked_fill_(~state.valid[head, :centers][None], -torch.inf)
         take = self.config.budget(pages)
         table = torch.empty((rows, take + len(fixed)), device=q.device, dtype=torch.int32)
         table[:, take:] = fixed[None]

@@ -125,14 +125,16 @@ def fp8_mqa_logits(q, kv, weights, cu_seqlen_ks, cu_seqlen_ke, clean_logits: boo
 
 
 def paged_logits_grouped(q8, weights, kv_cache, table, keys: int, out, row_tables=None, group_rows: int = 32,
-                         relu: bool = False, rows: int | None = None):
+                         relu: bool = False, rows: int | None = None, key_valid=None):
     """Extension: the signed-score Scorer's paged logits for query rows of four
     heads that share one key table (``v1x_score_fp8_grouped``).  q8 e4m3 [R, 4,
     128] and weights float32 [R, 4] with R a multiple of group_rows (rows past
     ``rows`` zero); table int32 [>= ceil(keys / 64)] of pool pages.  Without
     ``row_tables``: out[r, j] = the logit of key j (j < keys).  With
     ``row_tables`` int32 [rows, P]: out[r, c] = the logit of key (row_tables[r,
-    c // 64], c % 64) for c < 64 * P, every page a row names being in ``table``."""
+    c // 64], c % 64) for c < 64 * P, every page a row names being in ``table``.
+    ``key_valid`` (bool / uint8 [>= keys], without row tables): logits of the
+    keys where it is 0 are -inf."""
     R = q8.shape[0]
     rows = R if rows is None else int(rows)
     require(q8.dim() == 3 and q8.shape[1:] == (4, 128) and q8.is_contiguous()
@@ -157,11 +159,16 @@ def paged_logits_grouped(q8, weights, kv_cache, table, keys: int, out, row_table
         ws = torch.empty(padded * pool_pages + 1 + 3 * rows * P, dtype=torch.int32, device=q8.device)
     else:
         require(out.shape[1] >= keys, "out: at least `keys` columns")
+    if key_valid is not None:
+        require(row_tables is None, "key_valid applies without row tables")
+        require(key_valid.dtype in (torch.bool, torch.uint8) and key_valid.is_contiguous()
+                and key_valid.numel() >= keys, "key_valid: contiguous bool / uint8 [>= keys]")
+        key_valid = key_valid.view(torch.uint8)
     from .kernels import status_word
-    _lib.same_device(q8, weights, kv_cache, table, out, row_tables)
+    _lib.same_device(q8, weights, kv_cache, table, out, row_tables, key_valid)
     _lib.call("v1x_score_fp8_grouped", ptr(q8), ptr(weights), ptr(kv_cache), pool_pages, int(keys), ptr(table),
               ptr(row_tables), row_tables.stride(0) if row_tables is not None else 0,
-              row_tables.shape[1] if row_tables is not None else 0, ptr(ws), ptr(out), out.stride(0), 4,
+              row_tables.shape[1] if row_tables is not None else 0, ptr(key_valid), ptr(ws), ptr(out), out.stride(0), 4,
               int(group_rows), rows, int(bool(relu)), ptr(status_word(q8.device)), _lib.stream_of(q8),
               device=q8.device)
     return out

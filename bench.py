@@ -907,9 +907,8 @@ def run_signed_workload(args, world, rank, device, dist):
         ev[0].record()
         qp = scorer._pack(q, 0.0883883)
         ev[1].record()
-        coarse = scorer._logits(qp, st.centers[0], ct, C)
+        coarse = scorer._logits(qp, st.centers[0], ct, C, key_valid=st.valid[0, :C])
         ev[2].record()
-        coarse.masked_fill_(~st.valid[0, :C][None], -torch.inf)
         NS.extension(64, 4).route(coarse, table, pages, take)
         ev[3].record()
         sc = scorer._logits(qp, st.fine[0], used, used.numel() * 64, table)
@@ -920,7 +919,7 @@ def run_signed_workload(args, world, rank, device, dist):
         ev[6].record()
         torch.cuda.synchronize()
         if rep:
-            for i, name in enumerate(("pack_q", "centre_logits", "mask_and_route", "fine_logits", "mask_scores",
+            for i, name in enumerate(("pack_q", "centre_logits", "route", "fine_logits", "mask_scores",
                                       "mapped_top2048")):
                 split.setdefault(name, []).append(ev[i].elapsed_time(ev[i + 1]) * 1e3)
     split = {k: statistics.median(v) for k, v in split.items()}

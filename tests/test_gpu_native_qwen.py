@@ -442,6 +442,9 @@ def test_grouped_logits_equal_per_row_scorer(relu):
                                         clean_logits=False, relu=relu, impl="tensor_core")
     assert torch.equal(got[:, :keys], want)
     assert (got[:, keys:] == 7.0).all()
+    valid = torch.from_numpy(rng.random(keys + 3) > 0.2).to(DEV)
+    scoring.paged_logits_grouped(q8c, wc, pool, shared, keys, got, None, 32, relu=relu, rows=rows, key_valid=valid)
+    assert torch.equal(got[:, :keys], want.masked_fill(~valid[:keys][None], -torch.inf))
     # per-row tables over the shared pages, a repeated page and a page outside the pool
     sh = shared.cpu().numpy()
     rt = np.stack([rng.choice(sh, 30, replace=False) for _ in range(rows)]).astype(np.int32)
