@@ -219,8 +219,9 @@ int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t 
 int score_fp8_tc_grouped(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages,
                          const int32_t* lens, const int32_t* table, int64_t table_stride, int64_t max_len,
                          const int32_t* colmap, int64_t colmap_stride, int64_t colmap_pages,
-                         const uint8_t* key_valid, float* out, int64_t out_stride, int64_t group_rows,
-                         int64_t real_rows, int relu, int64_t vrows, int32_t* status, cudaStream_t stream);
+                         const uint8_t* key_valid, const int32_t* mask_map, const int32_t* mask_pos, float* out,
+                         int64_t out_stride, int64_t group_rows, int64_t real_rows, int relu, int64_t vrows,
+                         int32_t* status, cudaStream_t stream);
 
 namespace {
 int score_dispatch(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages, const int32_t* lens,
@@ -324,8 +325,10 @@ __global__ void fix_columns_kernel(const int32_t* __restrict__ fix, float* __res
 extern "C" int v1x_score_fp8_grouped(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages,
                                      int64_t keys, const int32_t* table, const int32_t* row_tables,
                                      int64_t row_table_stride, int64_t row_table_cols, const uint8_t* key_valid,
-                                     int32_t* workspace, float* out, int64_t out_stride, int64_t heads,
-                                     int64_t group_rows, int64_t rows, int relu, int32_t* status, void* stream) {
+                                     const int32_t* mask_map, const int32_t* mask_pos, int32_t* workspace,
+                                     float* out, int64_t out_stride,
+                                     int64_t heads, int64_t group_rows, int64_t rows, int relu, int32_t* status,
+                                     void* stream) {
   using namespace v1x;
   clear_error();
   V1X_CHECK_ARG(heads == 4, "score_fp8_grouped: four heads per query row");
@@ -335,6 +338,7 @@ extern "C" int v1x_score_fp8_grouped(const uint8_t* q, const float* w, const uin
                 "score_fp8_grouped: bad geometry");
   V1X_CHECK_ARG(table, "score_fp8_grouped: the shared key table is required");
   V1X_CHECK_ARG(!(key_valid && row_tables), "score_fp8_grouped: key_valid applies without row tables only");
+  V1X_CHECK_ARG(!mask_map || (row_tables && mask_pos), "score_fp8_grouped: the mask needs row tables and positions");
   const int64_t vrows = (rows + group_rows - 1) / group_rows;
   V1X_CHECK_ARG(vrows <= kTcMaxRows, "score_fp8_grouped: too many rows");
   if (row_tables) {
@@ -361,7 +365,8 @@ extern "C" int v1x_score_fp8_grouped(const uint8_t* q, const float* w, const uin
     if (int rc = launch_status("v1x_score_fp8_grouped (column map)")) return rc;
   }
   if (int rc = score_fp8_tc_grouped(q, w, pool, pool_pages, nullptr, table, 0, keys, colmap, padded, pool_pages,
-                                    key_valid, out, out_stride, group_rows, rows, relu, vrows, status, s))
+                                    key_valid, mask_map, mask_pos, out, out_stride, group_rows, rows, relu, vrows,
+                                    status, s))
     return rc;
   if (row_tables) {
     fix_columns_kernel<<<static_cast<unsigned>(num_sms()), 256, 0, s>>>(fix, out, out_stride);

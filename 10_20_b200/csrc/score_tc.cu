@@ -82,6 +82,11 @@ struct TcArgs {
   const int32_t* colmap;
   int64_t colmap_stride, colmap_pages;
   const uint8_t* key_valid;  // grouped mode without a column map: key j's logits are -inf where 0
+  // grouped mode with a column map: mask_scores fused (NA/kernels.py:47-59,
+  // without its dedup columns) -- row r's logit of a key is -inf when the key's
+  // logical token l = mask_map[page * 64 + slot] is < 0 or > mask_pos[r]
+  const int32_t* mask_map;
+  const int32_t* mask_pos;
   float* gout;
   int64_t gout_stride;
   int real_rows, group_rows;
@@ -350,20 +355,31 @@ __global__ void __launch_bounds__(tc_threads<kGroups>(), kGroups == 4 ? 1 : (kGr
         const bool valid = !(a.key_valid && live) || a.key_valid[key] != 0;
         // the warp's 32 keys lie in one page: lane l fetches query row b * G + l's
         // column of it, handed to the other lanes by shuffles below
-        int cm_lane = -1;
+        int cm_lane = -1, pos_lane = 0, logical = 0;
         if (a.colmap) {
           const int64_t key0 = static_cast<int64_t>(cur.t) * 128 + q4 * 32;
           const int64_t wpage = key0 < eff ? a.table[b * a.table_stride + (key0 >> 6)] : -1;
-          if (wpage >= 0 && wpage < a.colmap_pages && lane < a.group_rows)
+          if (wpage >= 0 && wpage < a.colmap_pages && lane < a.group_rows) {
             cm_lane = a.colmap[wpage * a.colmap_stride + static_cast<int64_t>(b) * a.group_rows + lane];
+            if (a.mask_map && b * a.group_rows + lane < a.real_rows) pos_lane = a.mask_pos[b * a.group_rows + lane];
+          }
+          if (a.mask_map && wpage >= 0 && wpage < a.colmap_pages) logical = a.mask_map[wpage * 64 + (key & 63)];
         }
+        const int row0 = b * a.group_rows;
+        const int kcol = static_cast<int>(key & 63);
+        const bool store_ok = live && (!a.key_valid || valid);
+        float* const out0 = a.gout + static_cast<int64_t>(row0) * a.gout_stride;
         for (int c0 = 0; c0 < a.N; c0 += 32) {
           uint32_t v[32];
           tmem_ld32(ta + c0, v);
           tmem_ld_wait();
 #pragma unroll
           for (int g4 = 0; g4 < 32; g4 += 4) {
-            const int row = b * a.group_rows + ((c0 + g4) >> 2);
+            const int rl = (c0 + g4) >> 2;  // row of the group
+            const int cm = __shfl_sync(0xffffffffu, cm_lane, rl);
+            const int pos = __shfl_sync(0xffffffffu, pos_lane, rl);
+            if (a.colmap && cm < 0) continue;  // the row does not name this page (warp-uniform)
+            if (row0 + rl >= a.real_rows) continue;
             const float4 w4 = *reinterpret_cast<const float4*>(wr + c0 + g4);
             float v0 = __uint_as_float(v[g4]), v1 = __uint_as_float(v[g4 + 1]);
             float v2 = __uint_as_float(v[g4 + 2]), v3 = __uint_as_float(v[g4 + 3]);
@@ -375,11 +391,10 @@ __global__ void __launch_bounds__(tc_threads<kGroups>(), kGroups == 4 ? 1 : (kGr
             }
             const float sum = (fmaf(w4.x, v0, 0.0f) + fmaf(w4.y, v1, 0.0f)) +
                               (fmaf(w4.z, v2, 0.0f) + fmaf(w4.w, v3, 0.0f));
-            const int cm = __shfl_sync(0xffffffffu, cm_lane, (c0 + g4) >> 2);
-            if (live && row < a.real_rows) {
-              int64_t col = key;
-              if (a.colmap) col = cm >= 0 ? static_cast<int64_t>(cm) * 64 + (key & 63) : -1;
-              if (col >= 0) a.gout[row * a.gout_stride + col] = valid ? sum * scale : -CUDART_INF_F;
+            if (live) {
+              const int64_t col = a.colmap ? static_cast<int64_t>(cm * 64 + kcol) : key;
+              const bool masked = a.mask_map && (logical < 0 || logical > pos);
+              out0[rl * a.gout_stride + col] = store_ok && !masked ? sum * scale : -CUDART_INF_F;
             }
           }
         }
@@ -481,6 +496,8 @@ struct GroupedOut {
   const int32_t* colmap;
   int64_t colmap_stride, colmap_pages;
   const uint8_t* key_valid;
+  const int32_t* mask_map;
+  const int32_t* mask_pos;
   float* out;
   int64_t out_stride;
   int64_t real_rows, group_rows;
@@ -506,9 +523,11 @@ int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t 
 int score_fp8_tc_grouped(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages,
                          const int32_t* lens, const int32_t* table, int64_t table_stride, int64_t max_len,
                          const int32_t* colmap, int64_t colmap_stride, int64_t colmap_pages,
-                         const uint8_t* key_valid, float* out, int64_t out_stride, int64_t group_rows,
-                         int64_t real_rows, int relu, int64_t vrows, int32_t* status, cudaStream_t stream) {
-  const GroupedOut g{colmap, colmap_stride, colmap_pages, key_valid, out, out_stride, real_rows, group_rows};
+                         const uint8_t* key_valid, const int32_t* mask_map, const int32_t* mask_pos, float* out,
+                         int64_t out_stride, int64_t group_rows, int64_t real_rows, int relu, int64_t vrows,
+                         int32_t* status, cudaStream_t stream) {
+  const GroupedOut g{colmap, colmap_stride, colmap_pages, key_valid, mask_map, mask_pos,
+                     out,    out_stride,    real_rows,    group_rows};
   return score_tc_launch(q, w, pool, pool_pages, lens, table, table_stride, nullptr, 0, max_len, nullptr, 0,
                          4 * group_rows, relu, 0, 0, vrows, status, stream, &g);
 }
@@ -586,7 +605,7 @@ int score_tc_launch(const uint8_t* q, const float* w, const uint8_t* pool, int64
   TcArgs args{lens, table, table_stride, w, out, out_stride, max_len, page_max, page_stride,
               static_cast<int>(batch), static_cast<int>(heads), static_cast<int>(n_mma), relu, clean,
               static_cast<int>(w_rows), lens_kind,
-              cols, status, nullptr, 0, 0, nullptr, nullptr, 0, 0, 0};
+              cols, status, nullptr, 0, 0, nullptr, nullptr, nullptr, nullptr, 0, 0, 0};
   static DeviceOnce once;
   once.run([] {
     cudaFuncSetAttribute(score_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
@@ -598,6 +617,8 @@ int score_tc_launch(const uint8_t* q, const float* w, const uint8_t* pool, int64
     args.colmap_stride = grp->colmap_stride;
     args.colmap_pages = grp->colmap_pages;
     args.key_valid = grp->key_valid;
+    args.mask_map = grp->mask_map;
+    args.mask_pos = grp->mask_pos;
     args.gout = grp->out;
     args.gout_stride = grp->out_stride;
     args.real_rows = static_cast<int>(grp->real_rows);

@@ -143,18 +143,22 @@ class Scorer:
         pack_q(q, scale, out_heads=4, out=(q8, w))
         return _Packed(q8, w, rows, True)
 
-    def _logits(self, qp, cache, pages, keys, row_tables=None, key_valid=None):
+    def _logits(self, qp, cache, pages, keys, row_tables=None, key_valid=None, mask=None):
         """Logits of the packed rows over `cache`: without row tables [rows, keys]
         of the keys of `pages` (one table shared by the rows; -inf where
         `key_valid` is False); with row tables [rows, 64 * P] of each row's own
-        pages, every one of them in `pages`."""
+        pages, every one of them in `pages`, masked by ``gather.mask_scores(out,
+        row_tables, *mask)`` when `mask` = (mapping, positions) is given."""
         if qp.grouped:
             width = row_tables.shape[1] * 64 if row_tables is not None else keys
             out = torch.empty((qp.rows, width), dtype=torch.float32, device=qp.q8.device)
             return scoring.paged_logits_grouped(qp.q8, qp.weights, cache, pages, keys, out, row_tables, GROUP_ROWS,
-                                                relu=False, rows=qp.rows, key_valid=key_valid)
+                                                relu=False, rows=qp.rows, key_valid=key_valid, mask=mask)
         if row_tables is not None:
-            return self.paged(qp.q8, qp.weights, cache, row_tables, row_tables.shape[1] * 64)
+            out = self.paged(qp.q8, qp.weights, cache, row_tables, row_tables.shape[1] * 64)
+            if mask is not None:
+                mask_scores(out, row_tables, *mask)
+            return out
         out = self.paged(qp.q8, qp.weights, cache, pages[None].expand(qp.rows, -1).contiguous(), keys)
         if key_valid is not None:
             out[:, :keys].masked_fill_(~key_valid[:keys].bool()[None], -torch.inf)
@@ -199,8 +203,8 @@ class Scorer:
             n *= 2
         span = min(n if pages <= 4096 else pages, state.fine[head].numel() // 8448)
         used = torch.cat((torch.arange(span, device=q.device, dtype=torch.int32), fixed.to(torch.int32)))
-        scores = self._logits(qp, state.fine[head], used, used.numel() * 64, table)
-        mask_scores(scores, table, state.mapping[head], positions)
+        scores = self._logits(qp, state.fine[head], used, used.numel() * 64, table,
+                              mask=(state.mapping[head], positions))
         # logical original token positions (not physical slots, no x4 expansion)
         return mapped_top2048(scores, table, state.mapping[head])
 

@@ -125,7 +125,7 @@ def fp8_mqa_logits(q, kv, weights, cu_seqlen_ks, cu_seqlen_ke, clean_logits: boo
 
 
 def paged_logits_grouped(q8, weights, kv_cache, table, keys: int, out, row_tables=None, group_rows: int = 32,
-                         relu: bool = False, rows: int | None = None, key_valid=None):
+                         relu: bool = False, rows: int | None = None, key_valid=None, mask=None):
     """Extension: the signed-score Scorer's paged logits for query rows of four
     heads that share one key table (``v1x_score_fp8_grouped``).  q8 e4m3 [R, 4,
     128] and weights float32 [R, 4] with R a multiple of group_rows (rows past
@@ -134,7 +134,9 @@ def paged_logits_grouped(q8, weights, kv_cache, table, keys: int, out, row_table
     ``row_tables`` int32 [rows, P]: out[r, c] = the logit of key (row_tables[r,
     c // 64], c % 64) for c < 64 * P, every page a row names being in ``table``.
     ``key_valid`` (bool / uint8 [>= keys], without row tables): logits of the
-    keys where it is 0 are -inf."""
+    keys where it is 0 are -inf.  ``mask`` = (mapping int32 [pool pages * 64],
+    positions int32 [rows]) with row tables: ``gather.mask_scores(out, row_tables,
+    mapping, positions)`` applied in the same pass."""
     R = q8.shape[0]
     rows = R if rows is None else int(rows)
     require(q8.dim() == 3 and q8.shape[1:] == (4, 128) and q8.is_contiguous()
@@ -164,11 +166,19 @@ def paged_logits_grouped(q8, weights, kv_cache, table, keys: int, out, row_table
         require(key_valid.dtype in (torch.bool, torch.uint8) and key_valid.is_contiguous()
                 and key_valid.numel() >= keys, "key_valid: contiguous bool / uint8 [>= keys]")
         key_valid = key_valid.view(torch.uint8)
+    mmap = mpos = None
+    if mask is not None:
+        mmap, mpos = mask
+        require(row_tables is not None, "mask applies with row tables")
+        require(mmap.dtype == torch.int32 and mmap.is_contiguous() and mmap.numel() >= pool_pages * 64,
+                "mask mapping: contiguous int32 [pool pages * 64]")
+        require(mpos.dtype == torch.int32 and mpos.is_contiguous() and mpos.numel() >= rows, "positions: int32 [rows]")
     from .kernels import status_word
-    _lib.same_device(q8, weights, kv_cache, table, out, row_tables, key_valid)
+    _lib.same_device(q8, weights, kv_cache, table, out, row_tables, key_valid, mmap, mpos)
     _lib.call("v1x_score_fp8_grouped", ptr(q8), ptr(weights), ptr(kv_cache), pool_pages, int(keys), ptr(table),
               ptr(row_tables), row_tables.stride(0) if row_tables is not None else 0,
-              row_tables.shape[1] if row_tables is not None else 0, ptr(key_valid), ptr(ws), ptr(out), out.stride(0), 4,
+              row_tables.shape[1] if row_tables is not None else 0, ptr(key_valid), ptr(mmap), ptr(mpos), ptr(ws),
+              ptr(out), out.stride(0), 4,
               int(group_rows), rows, int(bool(relu)), ptr(status_word(q8.device)), _lib.stream_of(q8),
               device=q8.device)
     return out

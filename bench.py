@@ -911,16 +911,13 @@ def run_signed_workload(args, world, rank, device, dist):
         ev[2].record()
         NS.extension(64, 4).route(coarse, table, pages, take)
         ev[3].record()
-        sc = scorer._logits(qp, st.fine[0], used, used.numel() * 64, table)
+        sc = scorer._logits(qp, st.fine[0], used, used.numel() * 64, table, mask=(st.mapping[0], positions))
         ev[4].record()
-        NS.mask_scores(sc, table, st.mapping[0], positions)
-        ev[5].record()
         NS.mapped_top2048(sc, table, st.mapping[0])
-        ev[6].record()
+        ev[5].record()
         torch.cuda.synchronize()
         if rep:
-            for i, name in enumerate(("pack_q", "centre_logits", "route", "fine_logits", "mask_scores",
-                                      "mapped_top2048")):
+            for i, name in enumerate(("pack_q", "centre_logits", "route", "fine_logits", "mapped_top2048")):
                 split.setdefault(name, []).append(ev[i].elapsed_time(ev[i + 1]) * 1e3)
     split = {k: statistics.median(v) for k, v in split.items()}
     # the grouped scorer's MMAs: every key of the used pages against 32 rows x 4 heads per group

@@ -578,12 +578,16 @@ V1X_API int v1x_score_fp8_ex(const uint8_t* q, const float* w, const uint8_t* po
  * i32 [ceil(rows / group_rows) * group_rows * pool_pages + 1 + 3 * rows *
  * row_table_cols] (row tables only).  key_valid (u8 [keys], may be NULL; without
  * row tables only): the logits of key j are -inf where key_valid[j] == 0 (the
- * Scorer's masked_fill of invalid centres, NA/scoring.py:86). */
+ * Scorer's masked_fill of invalid centres, NA/scoring.py:86).  mask_map (i32
+ * [pool_pages * 64], may be NULL; with row tables only) and mask_pos (i32
+ * [rows]): mask_scores fused (NA/kernels.py:47-59 without dedup columns) -- the
+ * logit of row r for a key whose logical token l = mask_map[page * 64 + slot]
+ * is < 0 or > mask_pos[r] is -inf (columns of a page outside the pool stay 0). */
 V1X_API int v1x_score_fp8_grouped(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages,
                   int64_t keys, const int32_t* table, const int32_t* row_tables, int64_t row_table_stride,
-                  int64_t row_table_cols, const uint8_t* key_valid, int32_t* workspace, float* out,
-                  int64_t out_stride, int64_t heads, int64_t group_rows, int64_t rows, int relu, int32_t* status,
-                  void* stream);
+                  int64_t row_table_cols, const uint8_t* key_valid, const int32_t* mask_map,
+                  const int32_t* mask_pos, int32_t* workspace, float* out, int64_t out_stride, int64_t heads,
+                  int64_t group_rows, int64_t rows, int relu, int32_t* status, void* stream);
 
 /* FP8 MQA logits over a flat key array -- the DeepGEMM fp8_mqa_logits contract
  * the signed-score Scorer calls in its `dsa` mode (NA/scoring.py:74-78) and the

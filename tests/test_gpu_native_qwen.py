@@ -462,6 +462,17 @@ def test_grouped_logits_equal_per_row_scorer(relu):
     assert (g[9, :64] == 0).all()
     g[9, :64] = wnt[9, :64]
     assert torch.equal(g, wnt)
+    # mask_scores fused into the same pass
+    mapping = torch.from_numpy(rng.integers(-3, 4000, npool * 64).astype(np.int32)).to(DEV)
+    positions = torch.from_numpy(rng.integers(0, 4000, rows).astype(np.int32)).to(DEV)
+    scoring.paged_logits_grouped(q8c, wc, pool, shared, 200 * 64, got, rtd, 32, relu=relu, rows=rows,
+                                 mask=(mapping, positions))
+    gather.mask_scores(want, torch.from_numpy(ok).to(DEV), mapping, positions)
+    g, wnt = got.cpu(), want.cpu()
+    assert (g[9, :64] == 0).all()
+    g[9, :64] = wnt[9, :64]
+    assert torch.equal(g, wnt)
+    assert torch.isinf(wnt).any()
 
 
 @pytest.mark.parametrize("share", [False, True])
