@@ -20,6 +20,7 @@ constexpr int kRouteWarps = kRouteThreads / 32;
 constexpr int kRouteMaxItems = 4096;
 constexpr int kRouteSmallItems = 512;  // tables up to this many padded slots take 2 keys per thread
 constexpr int kRankDirect = 256;  // winner lists up to this size are ordered by counting
+constexpr int kBucketRank = 256;  // longer lists: by bins, when no bin holds more keys
 
 struct RouteArgs {
   const float* scores;
@@ -49,6 +50,7 @@ struct RouteSmem {
   int warp_tot[kRouteWarps + 1];
   int4 res;
   int count;
+  int maxbin;
 };
 constexpr size_t kRouteListOff = (sizeof(RouteSmem) + 15) & ~size_t(15);
 
@@ -79,7 +81,7 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
 // ordered by (key desc, rank asc) by counting, or by a bitonic sort when ties
 // make the list long.
 template <bool kPages, int kPer>
-__global__ void __launch_bounds__(kRouteThreads, kPer <= 2 ? 4 : 1) route_kernel(const __grid_constant__ RouteArgs a) {
+__global__ void __launch_bounds__(kRouteThreads, kPer <= 2 ? 4 : 2) route_kernel(const __grid_constant__ RouteArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   RouteSmem& sm = *reinterpret_cast<RouteSmem*>(smem_raw);
   unsigned long long* list = reinterpret_cast<unsigned long long*>(smem_raw + kRouteListOff);
@@ -116,7 +118,10 @@ __global__ void __launch_bounds__(kRouteThreads, kPer <= 2 ? 4 : 1) route_kernel
     }
     return;
   }
-  if (tid == 0) sm.count = 0;
+  if (tid == 0) {
+    sm.count = 0;
+    sm.maxbin = 0;
+  }
   // ---- page keys (VQ:26-41): p < act -> key of the page's max centre, else -inf
   const int act = static_cast<int>(min(static_cast<int64_t>(active), kPages ? a.score_cols : a.score_cols / 8));
   const float* srow = a.scores + row * a.score_stride;
@@ -156,6 +161,68 @@ __global__ void __launch_bounds__(kRouteThreads, kPer <= 2 ? 4 : 1) route_kernel
     if (j < nv) atomicAdd(&sm.hist[bin_of(kr[j])], 1);
   __syncthreads();
   const TopBin tb = find_top_bin<kRouteThreads>(want, sm.hist, sm.warp_tot, &sm.res);
+  auto emit = [&](int pos, unsigned long long comp) {
+    const int r = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(comp & 0xFFFFFFFFull));
+    const int p = r / a.base + (r % a.base) * 128;
+    if (pos < a.take_stride) store_sel(a, row * a.take_stride + pos, p);
+    if (a.fill_table && pos < take && pos < a.fine_pages)
+      a.ft[row * a.fine_pages + pos] = p < a.pages ? (a.stage_rt ? srt[p] : rtrow[p]) : -1;
+  };
+  if (tb.above + tb.in > kRankDirect) {
+    // many winners: ordered through the bins.  The bins from the threshold bin
+    // up are laid out in descending order (a block scan of their counts); each
+    // winner-region key is placed into its bin's range, and its position is the
+    // keys in higher bins plus its rank inside the bin -- counted, when no bin
+    // holds more than kBucketRank keys (else the bitwise search and the sort
+    // below).  hist[b] becomes the end of bin b's range; bin b starts where bin
+    // b + 1 ends.
+    constexpr int kPerBin = kBins / kRouteThreads;
+    const int hib = kBins - tid * kPerBin;  // this thread's bins [hib - kPerBin, hib)
+    int c[kPerBin];
+    int s = 0, mx = 0;
+#pragma unroll
+    for (int j = 0; j < kPerBin; ++j) {
+      const int b = hib - kPerBin + j;
+      c[j] = b >= tb.bin ? sm.hist[b] : 0;
+      s += c[j];
+      mx = max(mx, c[j]);
+    }
+    int tot;
+    int cum = block_exclusive_scan(s, sm.warp_tot, &tot);
+    mx = __reduce_max_sync(0xffffffffu, mx);
+    if ((tid & 31) == 0) atomicMax(&sm.maxbin, mx);
+#pragma unroll
+    for (int j = kPerBin - 1; j >= 0; --j) {
+      const int b = hib - kPerBin + j;
+      if (b >= tb.bin) {
+        sm.hist[b] = cum;
+        cum += c[j];
+      }
+    }
+    __syncthreads();
+    if (sm.maxbin <= kBucketRank) {
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        if (j < nv && bin_of(kr[j]) >= tb.bin) {
+          const int p = tid + j * nt;
+          const uint32_t rank = static_cast<uint32_t>((p & 127) * a.base + (p >> 7));
+          const int e = atomicAdd(&sm.hist[bin_of(kr[j])], 1);
+          list[e] = (static_cast<unsigned long long>(kr[j]) << 32) | (0xFFFFFFFFu - rank);
+        }
+      }
+      if (a.stage_rt) asm volatile("cp.async.wait_all;" ::: "memory");
+      __syncthreads();
+      for (int e = tid; e < tb.above + tb.in; e += nt) {
+        const unsigned long long cc = list[e];
+        const int b = bin_of(static_cast<uint32_t>(cc >> 32));
+        const int beg = b == kBins - 1 ? 0 : sm.hist[b + 1], end = sm.hist[b];
+        int r = 0;
+        for (int f = beg; f < end; ++f) r += list[f] > cc;
+        if (beg + r < want) emit(beg + r, cc);
+      }
+      return;
+    }
+  }
   uint32_t lo = static_cast<uint32_t>(tb.bin) << (32 - kBinBits);
   if (tb.above + tb.in > kRankDirect) {
     int gt = 0;
@@ -186,13 +253,6 @@ __global__ void __launch_bounds__(kRouteThreads, kPer <= 2 ? 4 : 1) route_kernel
   if (a.stage_rt) asm volatile("cp.async.wait_all;" ::: "memory");
   __syncthreads();
   const int m = sm.count;
-  auto emit = [&](int pos, unsigned long long comp) {
-    const int r = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(comp & 0xFFFFFFFFull));
-    const int p = r / a.base + (r % a.base) * 128;
-    if (pos < a.take_stride) store_sel(a, row * a.take_stride + pos, p);
-    if (a.fill_table && pos < take && pos < a.fine_pages)
-      a.ft[row * a.fine_pages + pos] = p < a.pages ? (a.stage_rt ? srt[p] : rtrow[p]) : -1;
-  };
   if (m <= kRankDirect) {
     // composites are unique: a winner's position is the number of larger ones
     for (int e = tid; e < m; e += nt) {

@@ -106,6 +106,24 @@ def test_route_random(P, tie_mode, cuda_dev):
             assert np.array_equal(ft.cpu().numpy(), eft), (P, tie_mode, fill)
 
 
+@pytest.mark.parametrize("P", [300, 1500, 2048, 4096])
+@pytest.mark.parametrize("tie_mode", ["float", "int", "neginf"])
+def test_route_many_winners(P, tie_mode, cuda_dev):
+    """Takes of hundreds to thousands of pages: the winners are ordered through
+    the histogram bins (or, with crowded bins, by the bitwise search and sort)."""
+    rng = np.random.default_rng(P * 11 + len(tie_mode))
+    B = 21
+    K = P // 2 if P < 4096 else 3000
+    lens, takes, scores, rt, tail_rows = _route_case(rng, B, P, K, [K // 3, K - 1, K], tie_mode)
+    ft0 = np.full((B, K + 68), -7, np.int32)
+    sel = torch.full((B, K), -5, dtype=torch.int32, device="cuda")
+    ft = dev(ft0)
+    qf.module().route(dev(scores), dev(lens), dev(takes), sel, P, dev(rt), ft, dev(tail_rows), 1000, True)
+    esel, eft = O.route(scores, lens, takes, K, P, rt, ft0, tail_rows, 1000, True)
+    assert np.array_equal(sel.cpu().numpy(), esel), (P, tie_mode)
+    assert np.array_equal(ft.cpu().numpy(), eft), (P, tie_mode)
+
+
 def test_route_strided_scores_and_checks(cuda_dev):
     rng = np.random.default_rng(5)
     B, P, K = 9, 256, 40
