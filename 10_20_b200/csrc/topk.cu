@@ -166,6 +166,18 @@ __device__ __forceinline__ void mask_page(const TopkArgs& a, const RowCtx& c, fl
 // 1: keys staged in shared memory; 2: staged and also held in registers
 // (cols <= kRegKeys * 512).
 // kThreads 256 (mode 2 only): four CTAs per SM for batches of many rows.
+// Candidates i .. i + 3 of a row of L (the ones past L read as -inf), by one
+// 16-byte load when `vec` (row 16-byte aligned, i a multiple of 4).
+__device__ __forceinline__ float4 load4(const float* row, int i, int L, bool vec) {
+  if (vec && i + 3 < L) return __ldcg(reinterpret_cast<const float4*>(row + i));
+  float4 f = make_float4(-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F);
+  if (i < L) f.x = __ldcg(row + i);
+  if (i + 1 < L) f.y = __ldcg(row + i + 1);
+  if (i + 2 < L) f.z = __ldcg(row + i + 2);
+  if (i + 3 < L) f.w = __ldcg(row + i + 3);
+  return f;
+}
+
 template <int kMode, int kThreads>
 __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 2 : 4) topk_kernel(const __grid_constant__ TopkArgs a) {
   using Shape = TopkShape<kThreads>;
@@ -348,6 +360,9 @@ __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 2 : 4) topk_kernel
     // bin's keys and the keys above it, which it flags too) and places from the
     // bitmap alone.  Rows whose bin holds more than kMaxBin keys (mass ties)
     // and the unstaged mode without a bitmap take the bitwise search instead.
+    // unstaged mode: 16-byte loads when the row is aligned (row strides are
+    // multiples of 4 floats)
+    const bool vec4 = (reinterpret_cast<uintptr_t>(srow) & 15) == 0;
     bool by_bin = false, have_tie = false;
     uint32_t tie_thr = 0;
     int tie_need = 0;
@@ -369,14 +384,20 @@ __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 2 : 4) topk_kernel
         for (int j = 0; j < kRegKeys; ++j)
           if (j * nt + tid < c.L) atomicAdd(&hist[bin_of(kr[j])], 1);
       } else if constexpr (kMode == 0) {
-        // eight loads in flight per thread: the row streams from global memory
-        for (int i0 = tid; i0 < c.L; i0 += 8 * nt) {
-          float v[8];
+        // the row streams from global memory: a warp takes 128 consecutive
+        // candidates at a time (four per lane), four such groups in flight
+        for (int g0 = warp; g0 * 128 < c.L; g0 += 4 * kTopkWarps) {
+          float4 f[4];
 #pragma unroll
-          for (int u = 0; u < 8; ++u) v[u] = i0 + u * nt < c.L ? __ldcg(srow + i0 + u * nt) : 0.0f;
+          for (int q = 0; q < 4; ++q) f[q] = load4(srow, (g0 + q * kTopkWarps) * 128 + lane * 4, c.L, vec4);
 #pragma unroll
-          for (int u = 0; u < 8; ++u)
-            if (i0 + u * nt < c.L) atomicAdd(&hist[bin_of(order_key(v[u]))], 1);
+          for (int q = 0; q < 4; ++q) {
+            const int i = (g0 + q * kTopkWarps) * 128 + lane * 4;
+            const float x[4] = {f[q].x, f[q].y, f[q].z, f[q].w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              if (i + u < c.L) atomicAdd(&hist[bin_of(order_key(x[u]))], 1);
+          }
         }
       } else {
         for (int i = tid; i < c.L; i += nt) atomicAdd(&hist[bin_of(keys[i])], 1);
@@ -393,12 +414,6 @@ __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 2 : 4) topk_kernel
         const uint32_t ltm = lanemask_lt();
         auto append = [&](int j, uint32_t k) {
           const bool m = j * nt + tid < c.L && bin_of(k) == tb.bin;
-          if constexpr (kMode == 0) {
-            // the warp's 32 consecutive candidates are one bitmap word, owned by
-            // this warp in this pass: flag the keys above the bin
-            const unsigned above = __ballot_sync(0xffffffffu, j * nt + tid < c.L && bin_of(k) > tb.bin);
-            if (lane == 0 && j * nt + warp * 32 < c.L) selbits[(j * nt + warp * 32) >> 5] = above;
-          }
           const unsigned bal = __ballot_sync(0xffffffffu, m);
           if (bal == 0u) return;
           const uint32_t lo = __reduce_min_sync(0xffffffffu, m ? k : 0xFFFFFFFFu);
@@ -417,15 +432,38 @@ __global__ void __launch_bounds__(kThreads, kThreads >= 512 ? 2 : 4) topk_kernel
           for (int j = 0; j < kRegKeys; ++j)
             if (j < nsl) append(j, kr[j]);
         } else if constexpr (kMode == 0) {
-          // four slices' loads in flight before their keys are appended
-          for (int j0 = 0; j0 < nsl; j0 += 4) {
-            uint32_t kk[4];
+          // the second pass over the row, 128 candidates per warp step as in the
+          // histogram: the keys above the bin are flagged in the bitmap (lanes
+          // 8w .. 8w + 7 hold word w's 32 bits as nibbles, OR-ed by shuffles),
+          // the bin's keys are listed one by one (a few hundred per row)
+          for (int g0 = warp; g0 * 128 < c.L; g0 += 2 * kTopkWarps) {
+            float4 f[2];
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
-              kk[u] = (j0 + u) * nt + tid < c.L ? order_key(__ldcg(srow + (j0 + u) * nt + tid)) : 0u;
+            for (int q = 0; q < 2; ++q) f[q] = load4(srow, (g0 + q * kTopkWarps) * 128 + lane * 4, c.L, vec4);
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
-              if (j0 + u < nsl) append(j0 + u, kk[u]);
+            for (int q = 0; q < 2; ++q) {
+              const int i = (g0 + q * kTopkWarps) * 128 + lane * 4;
+              const float x[4] = {f[q].x, f[q].y, f[q].z, f[q].w};
+              uint32_t nib = 0;
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                if (i + u >= c.L) continue;
+                const uint32_t k = order_key(x[u]);
+                const int b = bin_of(k);
+                if (b > tb.bin) nib |= 1u << u;
+                if (b == tb.bin) {
+                  atomicMin(&sm.kmin, k);
+                  atomicMax(&sm.kmax, k);
+                  if (keep) cand[atomicAdd(&sm.ncand, 1)] = make_int2(static_cast<int>(k), i + u);
+                }
+              }
+              uint32_t word = nib << (4 * (lane & 7));
+              word |= __shfl_xor_sync(0xffffffffu, word, 1);
+              word |= __shfl_xor_sync(0xffffffffu, word, 2);
+              word |= __shfl_xor_sync(0xffffffffu, word, 4);
+              const int w = (i - 4 * (lane & 7)) >> 5;  // the word of lanes 8w' .. 8w' + 7
+              if ((lane & 7) == 0 && w * 32 < c.L) selbits[w] = word;
+            }
           }
         } else {
           for (int j = 0; j < nsl; ++j) append(j, j * nt + tid < c.L ? key_of(j) : 0u);
