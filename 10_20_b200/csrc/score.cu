@@ -216,6 +216,9 @@ int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t 
                  const int32_t* table, int64_t table_stride, float* out, int64_t out_stride, int64_t max_len,
                  float* page_max, int64_t page_stride, int64_t heads, int relu, int clean, int lens_kind,
                  int64_t batch, int32_t* status, cudaStream_t stream);
+int mqa_tc_grouped(const uint8_t* q, const float* w, const uint8_t* k, const float* k_scale, int64_t keys,
+                   const int32_t* win_lo, const int32_t* win_hi, float* out, int64_t out_stride, int64_t group_rows,
+                   int64_t real_rows, int relu, int64_t vrows, int32_t* status, cudaStream_t stream);
 int score_fp8_tc_grouped(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages,
                          const int32_t* lens, const int32_t* table, int64_t table_stride, int64_t max_len,
                          const int32_t* colmap, int64_t colmap_stride, int64_t colmap_pages,
@@ -398,4 +401,25 @@ extern "C" int v1x_mqa_logits_fp8(const uint8_t* q, const float* w, const uint8_
                                   int64_t out_stride, int64_t heads, int relu, int clean, int64_t batch,
                                   void* stream) {
   return v1x::mqa_flat(q, w, k, k_scale, kv_len, starts, ends, out, out_stride, heads, relu, clean, batch, stream);
+}
+
+extern "C" int v1x_mqa_logits_fp8_grouped(const uint8_t* q, const float* w, const uint8_t* k, const float* k_scale,
+                                          int64_t kv_len, const int32_t* starts, const int32_t* ends, float* out,
+                                          int64_t out_stride, int64_t heads, int64_t group_rows, int64_t rows,
+                                          int relu, int32_t* status, void* stream) {
+  using namespace v1x;
+  clear_error();
+  V1X_CHECK_ARG(heads == 4, "mqa_logits_grouped: four heads per query row");
+  V1X_CHECK_ARG(group_rows == 8 || group_rows == 16 || group_rows == 32,
+                "mqa_logits_grouped: group_rows must be 8, 16 or 32");
+  V1X_CHECK_ARG(rows >= 0 && kv_len >= 0 && out_stride >= kv_len && kv_len < (int64_t(1) << 31) - 128,
+                "mqa_logits_grouped: bad geometry");
+  V1X_CHECK_ARG(((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(k_scale)) & 15) == 0,
+                "mqa_logits_grouped: k and k_scale must be 16-byte aligned");
+  V1X_CHECK_ARG(starts && ends, "mqa_logits_grouped: starts and ends are required");
+  const int64_t vrows = (rows + group_rows - 1) / group_rows;
+  V1X_CHECK_ARG(vrows <= kTcMaxRows, "mqa_logits_grouped: too many rows");
+  if (rows == 0 || kv_len == 0) return V1X_OK;
+  return mqa_tc_grouped(q, w, k, k_scale, kv_len, starts, ends, out, out_stride, group_rows, rows, relu, vrows,
+                        status, as_stream(stream));
 }

@@ -87,6 +87,12 @@ struct TcArgs {
   // logical token l = mask_map[page * 64 + slot] is < 0 or > mask_pos[r]
   const int32_t* mask_map;
   const int32_t* mask_pos;
+  // flat keys (fp8_mqa_logits): key j at j * 128 of a flat array, its scale in
+  // a flat array; no page table (tile t holds keys 128t .. 128t + 127); rows'
+  // logits outside [win_lo[r], win_hi[r]) are -inf
+  int flat;
+  const int32_t* win_lo;
+  const int32_t* win_hi;
   float* gout;
   int64_t gout_stride;
   int real_rows, group_rows;
@@ -243,8 +249,9 @@ __global__ void __launch_bounds__(tc_threads<kGroups>(), kGroups == 4 ? 1 : (kGr
       for (int it = warp; it < ntiles; it += kProducers) {
         const int b = cur.b, t = cur.t;
         const int64_t eff = row_eff(a, b);
-        const int p0 = a.table[b * a.table_stride + 2 * t];
-        const int p1 = (static_cast<int64_t>(2 * t + 1) * 64 < eff) ? a.table[b * a.table_stride + 2 * t + 1] : p0;
+        const int p0 = a.flat ? 2 * t : a.table[b * a.table_stride + 2 * t];
+        const int p1 = (static_cast<int64_t>(2 * t + 1) * 64 < eff) ? (a.flat ? 2 * t + 1 : a.table[b * a.table_stride + 2 * t + 1])
+                                                                     : p0;
         const int s = it % kTcStages, r = it % kScaleSlots;
         if (!mbar_wait(&sh.empty[s], ((it / kTcStages) & 1) ^ 1, &sh.abort, kWaitLimitNs) ||
             !mbar_wait(&sh.sempty[r], ((it / kScaleSlots) & 1) ^ 1, &sh.abort, kWaitLimitNs)) {
@@ -253,10 +260,17 @@ __global__ void __launch_bounds__(tc_threads<kGroups>(), kGroups == 4 ? 1 : (kGr
         }
         mbar_arrive_expect_tx(&sh.full[s], 16384);
         mbar_arrive_expect_tx(&sh.sfull[r], 512);
-        tma_load_3d(stages + s * 16384, &pool_map, &sh.full[s], 0, 0, p0);
-        tma_load_3d(stages + s * 16384 + 8192, &pool_map, &sh.full[s], 0, 0, p1);
-        tma_load_2d(sring + r * 128, &scale_map, &sh.sfull[r], 0, p0);
-        tma_load_2d(sring + r * 128 + 64, &scale_map, &sh.sfull[r], 0, p1);
+        if (a.flat) {  // 64-key boxes of the flat arrays (zero-filled past the last key)
+          tma_load_2d(stages + s * 16384, &pool_map, &sh.full[s], 0, 64 * p0);
+          tma_load_2d(stages + s * 16384 + 8192, &pool_map, &sh.full[s], 0, 64 * p1);
+          tma_load_1d(sring + r * 128, &scale_map, &sh.sfull[r], 64 * p0);
+          tma_load_1d(sring + r * 128 + 64, &scale_map, &sh.sfull[r], 64 * p1);
+        } else {
+          tma_load_3d(stages + s * 16384, &pool_map, &sh.full[s], 0, 0, p0);
+          tma_load_3d(stages + s * 16384 + 8192, &pool_map, &sh.full[s], 0, 0, p1);
+          tma_load_2d(sring + r * 128, &scale_map, &sh.sfull[r], 0, p0);
+          tma_load_2d(sring + r * 128 + 64, &scale_map, &sh.sfull[r], 0, p1);
+        }
         last_it = it;
         cur.advance(prefix, kProducers);
       }
@@ -355,7 +369,11 @@ __global__ void __launch_bounds__(tc_threads<kGroups>(), kGroups == 4 ? 1 : (kGr
         const bool valid = !(a.key_valid && live) || a.key_valid[key] != 0;
         // the warp's 32 keys lie in one page: lane l fetches query row b * G + l's
         // column of it, handed to the other lanes by shuffles below
-        int cm_lane = -1, pos_lane = 0, logical = 0;
+        int cm_lane = -1, pos_lane = 0, logical = 0, lo_lane = 0, hi_lane = 0;
+        if (a.win_lo && lane < a.group_rows && b * a.group_rows + lane < a.real_rows) {
+          lo_lane = a.win_lo[b * a.group_rows + lane];
+          hi_lane = a.win_hi[b * a.group_rows + lane];
+        }
         if (a.colmap) {
           const int64_t key0 = static_cast<int64_t>(cur.t) * 128 + q4 * 32;
           const int64_t wpage = key0 < eff ? a.table[b * a.table_stride + (key0 >> 6)] : -1;
@@ -378,6 +396,7 @@ __global__ void __launch_bounds__(tc_threads<kGroups>(), kGroups == 4 ? 1 : (kGr
             const int rl = (c0 + g4) >> 2;  // row of the group
             const int cm = __shfl_sync(0xffffffffu, cm_lane, rl);
             const int pos = __shfl_sync(0xffffffffu, pos_lane, rl);
+            const int wlo = __shfl_sync(0xffffffffu, lo_lane, rl), whi = __shfl_sync(0xffffffffu, hi_lane, rl);
             if (a.colmap && cm < 0) continue;  // the row does not name this page (warp-uniform)
             if (row0 + rl >= a.real_rows) continue;
             const float4 w4 = *reinterpret_cast<const float4*>(wr + c0 + g4);
@@ -393,7 +412,8 @@ __global__ void __launch_bounds__(tc_threads<kGroups>(), kGroups == 4 ? 1 : (kGr
                               (fmaf(w4.z, v2, 0.0f) + fmaf(w4.w, v3, 0.0f));
             if (live) {
               const int64_t col = a.colmap ? static_cast<int64_t>(cm * 64 + kcol) : key;
-              const bool masked = a.mask_map && (logical < 0 || logical > pos);
+              const bool masked = (a.mask_map && (logical < 0 || logical > pos)) ||
+                                  (a.win_lo && (key < wlo || key >= whi));
               out0[rl * a.gout_stride + col] = store_ok && !masked ? sum * scale : -CUDART_INF_F;
             }
           }
@@ -501,6 +521,10 @@ struct GroupedOut {
   float* out;
   int64_t out_stride;
   int64_t real_rows, group_rows;
+  const float* flat_scale;  // flat keys: `pool` is k [flat_keys, 128], flat_scale [flat_keys]
+  int64_t flat_keys;
+  const int32_t* win_lo;
+  const int32_t* win_hi;
 };
 
 int score_tc_launch(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages, const int32_t* lens,
@@ -526,9 +550,20 @@ int score_fp8_tc_grouped(const uint8_t* q, const float* w, const uint8_t* pool, 
                          const uint8_t* key_valid, const int32_t* mask_map, const int32_t* mask_pos, float* out,
                          int64_t out_stride, int64_t group_rows, int64_t real_rows, int relu, int64_t vrows,
                          int32_t* status, cudaStream_t stream) {
-  const GroupedOut g{colmap, colmap_stride, colmap_pages, key_valid, mask_map, mask_pos,
-                     out,    out_stride,    real_rows,    group_rows};
+  const GroupedOut g{colmap, colmap_stride, colmap_pages, key_valid, mask_map, mask_pos, out,
+                     out_stride, real_rows, group_rows, nullptr, 0, nullptr, nullptr};
   return score_tc_launch(q, w, pool, pool_pages, lens, table, table_stride, nullptr, 0, max_len, nullptr, 0,
+                         4 * group_rows, relu, 0, 0, vrows, status, stream, &g);
+}
+
+// Grouped mode over flat keys (fp8_mqa_logits): out[r, j] for j < keys, -inf
+// outside [win_lo[r], win_hi[r]).
+int mqa_tc_grouped(const uint8_t* q, const float* w, const uint8_t* k, const float* k_scale, int64_t keys,
+                   const int32_t* win_lo, const int32_t* win_hi, float* out, int64_t out_stride, int64_t group_rows,
+                   int64_t real_rows, int relu, int64_t vrows, int32_t* status, cudaStream_t stream) {
+  const GroupedOut g{nullptr, 0,          0,          nullptr, nullptr, nullptr, out,
+                     out_stride, real_rows, group_rows, k_scale, keys,   win_lo,  win_hi};
+  return score_tc_launch(q, w, k, (keys + 63) / 64, nullptr, nullptr, 0, nullptr, 0, keys, nullptr, 0,
                          4 * group_rows, relu, 0, 0, vrows, status, stream, &g);
 }
 
@@ -552,13 +587,35 @@ int score_tc_launch(const uint8_t* q, const float* w, const uint8_t* pool, int64
   }
   const int64_t n_mma = heads == 1 ? 16 : heads;
   CUtensorMap pool_map, q_map, scale_map;
-  {
+  const bool flat = grp && grp->flat_scale;
+  if (flat) {
+    // flat keys: {128 bytes, keys}, 64 keys per box; scales: {keys}, 64 per box
+    const cuuint64_t dims[2] = {128, static_cast<cuuint64_t>(grp->flat_keys)};
+    const cuuint64_t strides[1] = {128};
+    const cuuint32_t box[2] = {128, 64};
+    if (int rc = encode(enc, &pool_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, pool, dims, strides, box,
+                        CU_TENSOR_MAP_SWIZZLE_128B, "flat keys"))
+      return rc;
+    const cuuint64_t sdims[1] = {static_cast<cuuint64_t>(grp->flat_keys)};
+    const cuuint64_t sstrides[1] = {4};
+    const cuuint32_t sbox[1] = {64};
+    if (int rc = encode(enc, &scale_map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 1, grp->flat_scale, sdims, sstrides, sbox,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, "flat scales"))
+      return rc;
+  } else {
     // keys: {128 bytes, 64 tokens, pages}, one page per box, 128-byte swizzle
     const cuuint64_t dims[3] = {128, 64, static_cast<cuuint64_t>(pool_pages)};
     const cuuint64_t strides[2] = {128, static_cast<cuuint64_t>(kPageBytes)};
     const cuuint32_t box[3] = {128, 64, 1};
     if (int rc = encode(enc, &pool_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, pool, dims, strides, box,
                         CU_TENSOR_MAP_SWIZZLE_128B, "pool"))
+      return rc;
+    // the 64 fp32 scales of each page: 256 contiguous bytes at page + 8192
+    const cuuint64_t sdims[2] = {64, static_cast<cuuint64_t>(pool_pages)};
+    const cuuint64_t sstrides[1] = {static_cast<cuuint64_t>(kPageBytes)};
+    const cuuint32_t sbox[2] = {64, 1};
+    if (int rc = encode(enc, &scale_map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, pool + kKeyBytes, sdims, sstrides, sbox,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, "scale"))
       return rc;
   }
   {
@@ -569,15 +626,6 @@ int score_tc_launch(const uint8_t* q, const float* w, const uint8_t* pool, int64
     const cuuint32_t box[2] = {128, static_cast<cuuint32_t>(n_mma)};
     if (int rc = encode(enc, &q_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, q, dims, strides, box,
                         CU_TENSOR_MAP_SWIZZLE_128B, "q"))
-      return rc;
-  }
-  {
-    // the 64 fp32 scales of each page: 256 contiguous bytes at page + 8192
-    const cuuint64_t dims[2] = {64, static_cast<cuuint64_t>(pool_pages)};
-    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kPageBytes)};
-    const cuuint32_t box[2] = {64, 1};
-    if (int rc = encode(enc, &scale_map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, pool + kKeyBytes, dims, strides, box,
-                        CU_TENSOR_MAP_SWIZZLE_NONE, "scale"))
       return rc;
   }
   uint32_t cols = 32;
@@ -605,7 +653,7 @@ int score_tc_launch(const uint8_t* q, const float* w, const uint8_t* pool, int64
   TcArgs args{lens, table, table_stride, w, out, out_stride, max_len, page_max, page_stride,
               static_cast<int>(batch), static_cast<int>(heads), static_cast<int>(n_mma), relu, clean,
               static_cast<int>(w_rows), lens_kind,
-              cols, status, nullptr, 0, 0, nullptr, nullptr, nullptr, nullptr, 0, 0, 0};
+              cols, status, nullptr, 0, 0, nullptr, nullptr, nullptr, 0, nullptr, nullptr, nullptr, 0, 0, 0};
   static DeviceOnce once;
   once.run([] {
     cudaFuncSetAttribute(score_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
@@ -619,6 +667,9 @@ int score_tc_launch(const uint8_t* q, const float* w, const uint8_t* pool, int64
     args.key_valid = grp->key_valid;
     args.mask_map = grp->mask_map;
     args.mask_pos = grp->mask_pos;
+    args.flat = flat ? 1 : 0;
+    args.win_lo = grp->win_lo;
+    args.win_hi = grp->win_hi;
     args.gout = grp->out;
     args.gout_stride = grp->out_stride;
     args.real_rows = static_cast<int>(grp->real_rows);

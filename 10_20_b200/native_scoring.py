@@ -177,9 +177,14 @@ class Scorer:
             raise ValueError("This backend preserves Qwen's four-Q-head routing group")
         positions = torch.arange(prefix + offset, prefix + offset + rows, device=q.device, dtype=torch.int32)
         if self.config.mode == "dsa":
-            q8, weights = pack_q(q, scale)
-            scores = scoring.fp8_mqa_logits(q8, (state.flat_k[head, :total], state.flat_scale[head, :total]),
-                                            weights, torch.zeros_like(positions), positions + 1, True, relu=False)
+            kv = (state.flat_k[head, :total], state.flat_scale[head, :total])
+            qp = self._pack(q, scale)
+            if qp.grouped:
+                scores = scoring.mqa_logits_grouped(qp.q8, qp.weights, kv, torch.zeros_like(positions),
+                                                    positions + 1, rows=rows, group_rows=GROUP_ROWS, relu=False)
+            else:
+                scores = scoring.fp8_mqa_logits(qp.q8, kv, qp.weights, torch.zeros_like(positions), positions + 1,
+                                                True, relu=False)
             return topk2048(scores, need_values=False)[1].int()
         qp = self._pack(q, scale)
         pages = state.pages

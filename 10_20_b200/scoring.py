@@ -182,3 +182,38 @@ def paged_logits_grouped(q8, weights, kv_cache, table, keys: int, out, row_table
               int(group_rows), rows, int(bool(relu)), ptr(status_word(q8.device)), _lib.stream_of(q8),
               device=q8.device)
     return out
+
+
+def mqa_logits_grouped(q8, weights, kv, cu_seqlen_ks, cu_seqlen_ke, rows: int | None = None, group_rows: int = 32,
+                       relu: bool = False, out=None):
+    """Extension: ``fp8_mqa_logits(..., clean_logits=True)`` for query rows of
+    four heads on the tensor cores (``v1x_mqa_logits_fp8_grouped``).  q8 e4m3
+    [R, 4, 128] and weights float32 [R, 4], R a multiple of group_rows, rows
+    past ``rows`` zero; kv = (k e4m3 [N, 128], k_scale float32 [N]); returns
+    logits [rows, N], -inf outside [ks[r], ke[r])."""
+    k, k_scale = kv
+    R = q8.shape[0]
+    rows = R if rows is None else int(rows)
+    require(q8.dim() == 3 and q8.shape[1:] == (4, 128) and q8.is_contiguous()
+            and q8.dtype in (torch.float8_e4m3fn, torch.uint8), "q8: contiguous e4m3 [R, 4, 128]")
+    require(weights.shape == (R, 4) and weights.dtype == torch.float32 and weights.is_contiguous(),
+            "weights: contiguous float32 [R, 4]")
+    require(R % group_rows == 0 and rows <= R, "q8 rows: a multiple of group_rows, at least rows")
+    require(k.dim() == 2 and k.shape[1] == 128 and k.dtype in (torch.float8_e4m3fn, torch.uint8)
+            and k.is_contiguous(), "kv[0]: contiguous float8_e4m3fn [N, 128]")
+    N = k.shape[0]
+    k_scale = k_scale.reshape(-1)
+    require(k_scale.numel() == N and k_scale.dtype == torch.float32 and k_scale.is_contiguous(),
+            "kv[1]: float32 [N]")
+    for name, t in (("cu_seqlen_ks", cu_seqlen_ks), ("cu_seqlen_ke", cu_seqlen_ke)):
+        require(t.dtype == torch.int32 and t.is_contiguous() and t.numel() >= rows, f"{name}: int32 [rows]")
+    if out is None:
+        out = torch.empty((rows, N), dtype=torch.float32, device=q8.device)
+    require(out.dtype == torch.float32 and out.dim() == 2 and out.shape[0] >= rows and out.shape[1] >= N
+            and out.stride(1) == 1, "out: float32 [rows, >= N]")
+    from .kernels import status_word
+    _lib.same_device(q8, weights, k, k_scale, cu_seqlen_ks, cu_seqlen_ke, out)
+    _lib.call("v1x_mqa_logits_fp8_grouped", ptr(q8), ptr(weights), ptr(k), ptr(k_scale), N, ptr(cu_seqlen_ks),
+              ptr(cu_seqlen_ke), ptr(out), out.stride(0), 4, int(group_rows), rows, int(bool(relu)),
+              ptr(status_word(q8.device)), _lib.stream_of(q8), device=q8.device)
+    return out

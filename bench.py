@@ -920,6 +920,15 @@ def run_signed_workload(args, world, rank, device, dist):
             for i, name in enumerate(("pack_q", "centre_logits", "route", "fine_logits", "mapped_top2048")):
                 split.setdefault(name, []).append(ev[i].elapsed_time(ev[i + 1]) * 1e3)
     split = {k: statistics.median(v) for k, v in split.items()}
+    # the dsa mode (flat keys, causal windows) over the same history and rows
+    st.flat_k = torch.randn((1, prefix, 128), generator=gen).to(torch.float8_e4m3fn).to(device)
+    st.flat_scale = (torch.rand((1, prefix), generator=gen) * 0.5 + 0.05).to(device)
+    dsa = NS.Scorer(type("DsaCfg", (Cfg,), {"mode": "dsa"})(), device)
+    gd = _capture(lambda: out.__setitem__("dsa", dsa.select(q, st, 0, prefix - rows, 0, prefix, fixed, 0.0883883)),
+                  device)
+    ms_d, _ = _timed_replays(gd, 10, 3, None, device)
+    split["dsa_select"] = ms_d / 10 * 1e3
+    del gd, st.flat_k, st.flat_scale
     # the grouped scorer's MMAs: every key of the used pages against 32 rows x 4 heads per group
     fine_flop = 2.0 * (-(-rows // 32)) * used.numel() * 64 * 128 * 128
     split["fine_logits_mma_tflops"] = fine_flop / (split["fine_logits"] * 1e-6) / 1e12

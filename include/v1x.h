@@ -589,6 +589,17 @@ V1X_API int v1x_score_fp8_grouped(const uint8_t* q, const float* w, const uint8_
                   const int32_t* mask_pos, int32_t* workspace, float* out, int64_t out_stride, int64_t heads,
                   int64_t group_rows, int64_t rows, int relu, int32_t* status, void* stream);
 
+/* Extension (no reference counterpart): v1x_mqa_logits_fp8 with clean = 1 for
+ * query rows of four heads (the signed-score Scorer's dsa mode), on the tensor
+ * cores: group_rows rows x 4 heads form one MMA operand, so a tile of 128 keys is
+ * read once per group.  q u8 (e4m3) [ceil(rows / group_rows) * group_rows, 4,
+ * 128] and w f32 [same, 4], zero past `rows`; k and k_scale 16-byte aligned;
+ * group_rows in {8, 16, 32}.  Logits equal v1x_score_fp8's per-row tensor-core
+ * order of accumulation, not the SIMT order of v1x_mqa_logits_fp8. */
+V1X_API int v1x_mqa_logits_fp8_grouped(const uint8_t* q, const float* w, const uint8_t* k, const float* k_scale,
+                  int64_t kv_len, const int32_t* starts, const int32_t* ends, float* out, int64_t out_stride,
+                  int64_t heads, int64_t group_rows, int64_t rows, int relu, int32_t* status, void* stream);
+
 /* FP8 MQA logits over a flat key array -- the DeepGEMM fp8_mqa_logits contract
  * the signed-score Scorer calls in its `dsa` mode (NA/scoring.py:74-78) and the
  * probe backend at qwen_gqa_probe_backend.py:184: out[b, j] = sum_h w[b,h] *

@@ -327,6 +327,7 @@ def test_scorer_dsa_matches_oracle():
     st.flat_k = torch.from_numpy(k8).to(DEV).view(torch.float8_e4m3fn)
     st.flat_scale = torch.from_numpy(ks).to(DEV)
     scorer = native_scoring.Scorer(_Config("dsa", 0.5), DEV)
+    scorer.impl = "simt"
     q = torch.randn((rows, 4, 128), generator=torch.Generator().manual_seed(1)).to(torch.bfloat16)
     prefix, offset, total = 3000, 90, 3500
     got = scorer.select(q.to(DEV), st, 1, prefix, offset, total, None, 0.125)
@@ -336,6 +337,47 @@ def test_scorer_dsa_matches_oracle():
     want = np.stack([O.select_topk(logits[r], 2048) for r in range(rows)])
     assert got.dtype == torch.int32
     np.testing.assert_array_equal(got.cpu().numpy(), want)
+    # the tensor-core default selects the same tokens up to near-ties
+    scorer.impl = "auto"
+    got = scorer.select(q.to(DEV), st, 1, prefix, offset, total, None, 0.125).cpu().numpy()
+    assert np.mean([len(np.intersect1d(got[r], want[r])) / 2048 for r in range(rows)]) > 0.99
+
+
+@pytest.mark.parametrize("relu", [False, True])
+def test_mqa_logits_grouped_equals_per_row_tensor_core(relu):
+    rng = np.random.default_rng(61 + relu)
+    rows, N = 45, 3001
+    k8 = O.e4m3_from_f32(rng.standard_normal((N, 128)).astype(np.float32))
+    ks = rng.uniform(0.01, 1, N).astype(np.float32)
+    P = (N + 63) // 64
+    raw = np.zeros((P, 8448), np.uint8)
+    kk = np.zeros((P * 64, 128), np.uint8)
+    kk[:N] = k8
+    sc = np.zeros(P * 64, np.float32)
+    sc[:N] = ks
+    raw[:, :8192] = kk.reshape(P, 8192)
+    raw[:, 8192:] = sc.view(np.uint8).reshape(P, 256)
+    pool = torch.from_numpy(raw).to(DEV)
+    q = torch.randn((rows, 4, 128), generator=torch.Generator().manual_seed(3)).to(torch.bfloat16).to(DEV)
+    q8, w, q8c, wc = _packs(q, 0.07, 64)
+    lens = torch.full((rows,), N, dtype=torch.int32, device=DEV)
+    table = torch.arange(P, dtype=torch.int32, device=DEV)[None].expand(rows, -1).contiguous()
+    want = scoring.fp8_paged_mqa_logits(q8, pool, w, lens, table, None, N, clean_logits=False, relu=relu,
+                                        impl="tensor_core")
+    lo = rng.integers(0, N, rows).astype(np.int32)
+    hi = np.minimum(lo + rng.integers(0, 3 * N // 2, rows), N + 7).astype(np.int32)
+    lo[0], hi[0] = 0, N
+    lo[1], hi[1] = 10, 10
+    kd = torch.from_numpy(k8).to(DEV).view(torch.float8_e4m3fn)
+    got = scoring.mqa_logits_grouped(q8c, wc, (kd, torch.from_numpy(ks).to(DEV)), torch.from_numpy(lo).to(DEV),
+                                     torch.from_numpy(hi).to(DEV), rows=rows, relu=relu)
+    cols = torch.arange(N, device=DEV)[None]
+    inside = (cols >= torch.from_numpy(lo).to(DEV)[:, None].long()) & (cols < torch.from_numpy(hi).to(DEV)[:, None].long())
+    assert torch.equal(got, want.masked_fill(~inside, -torch.inf))
+    ref = O.mqa_logits(_u8(q8), w.cpu().numpy(), k8, ks, lo, hi, relu=relu)
+    fin = np.isfinite(ref)
+    assert (np.isfinite(got.cpu().numpy()) == fin).all()
+    np.testing.assert_allclose(got.cpu().numpy()[fin], ref[fin], rtol=1e-2, atol=1e-3 * np.abs(ref[fin]).max())
 
 
 def test_shared_select_matches_oracle():
