@@ -556,3 +556,34 @@ def test_scorer_grouped_equals_per_row_tensor_core(share):
     scorer.impl = "tensor_core"
     want = scorer.select(q, *args)
     assert torch.equal(got, want)
+
+
+def test_select_tensors_public_api_matches_select():
+    """select_tensors (NA/shared_scoring.py:30-62) with the caller's 32-head q8 /
+    weights, against the shared select of the same query."""
+    rng = np.random.default_rng(71)
+    rows, phys, pages, nfixed = 6, 120, 70, 5
+    arena = _State()
+    arena.centers = torch.from_numpy(_pool(rng, phys)[None]).to(DEV)
+    arena.fine = torch.from_numpy(_pool(rng, phys)[None]).to(DEV)
+    arena.valid = torch.from_numpy(rng.random((1, phys, 8)) > 0.05).to(DEV)
+    arena.mapping = torch.from_numpy(rng.integers(-1, 9000, (1, phys * 64)).astype(np.int32)).to(DEV)
+    arena.identity = torch.arange(phys * 64, dtype=torch.int32, device=DEV)
+    arena.record = lambda: None
+    st = _State()
+    st.arena, st.wait = arena, (lambda: None)
+    page_ids = torch.from_numpy(rng.permutation(phys)[:pages].astype(np.int32)).to(DEV)
+    fixed = torch.from_numpy(rng.permutation(phys)[None, :nfixed].astype(np.int32)).to(DEV)
+    st.table = page_ids[None]
+    st.full_bucket_append, st.fixed_start, st.pages = True, 6000, pages
+    scorer = native_scoring.Scorer(_Config("v1", 0.4, share=True), DEV)
+    scorer.impl = "tensor_core"
+    q = torch.randn((rows, 4, 128), generator=torch.Generator().manual_seed(4)).to(torch.bfloat16).to(DEV)
+    want = scorer.select(q, st, 0, 7000, 2, 0, fixed, 0.1)
+    q8, w = native_scoring.pack_q(q, 0.1)
+    positions = torch.arange(7002, 7002 + rows, dtype=torch.int32, device=DEV)
+    got = native_scoring.select_tensors(scorer, q8, w, arena, 0, page_ids, fixed[0], positions, True, 6000)
+    assert torch.equal(got, want)
+    with pytest.raises(ValueError):
+        native_scoring.select_tensors(scorer, q8, w, arena, 0, page_ids, fixed[0], positions, True, 6000,
+                                      decode_meta=object())
