@@ -351,6 +351,29 @@ __global__ void __launch_bounds__(tc_threads<kGroups>(), kGroups == 4 ? 1 : (kGr
       const int64_t eff = row_eff(a, b);
       const int64_t key = static_cast<int64_t>(cur.t) * 128 + i;
       const float* wr = w_staged ? wsm + (b - b_first) * a.H : a.w + static_cast<int64_t>(b) * a.H;
+      // grouped mode: the tile's row and page values, loaded before the waits
+      // so that their latency overlaps the MMA.  The warp's 32 keys lie in one
+      // page: lane l fetches query row b * G + l's column of it (and its
+      // position / window), handed to the other lanes by shuffles below
+      bool live = false, valid = true;
+      int cm_lane = -1, pos_lane = 0, logical = 0, lo_lane = 0, hi_lane = 0;
+      if constexpr (kGrouped) {
+        live = key < eff;
+        valid = !(a.key_valid && live) || a.key_valid[key] != 0;
+        if (a.win_lo && lane < a.group_rows && b * a.group_rows + lane < a.real_rows) {
+          lo_lane = a.win_lo[b * a.group_rows + lane];
+          hi_lane = a.win_hi[b * a.group_rows + lane];
+        }
+        if (a.colmap) {
+          const int64_t key0 = static_cast<int64_t>(cur.t) * 128 + q4 * 32;
+          const int64_t wpage = key0 < eff ? a.table[b * a.table_stride + (key0 >> 6)] : -1;
+          if (wpage >= 0 && wpage < a.colmap_pages && lane < a.group_rows) {
+            cm_lane = a.colmap[wpage * a.colmap_stride + static_cast<int64_t>(b) * a.group_rows + lane];
+            if (a.mask_map && b * a.group_rows + lane < a.real_rows) pos_lane = a.mask_pos[b * a.group_rows + lane];
+          }
+          if (a.mask_map && wpage >= 0 && wpage < a.colmap_pages) logical = a.mask_map[wpage * 64 + (key & 63)];
+        }
+      }
       if (!mbar_wait(&sh.sfull[r], (it / kScaleSlots) & 1, &sh.abort, kWaitLimitNs) ||
           !mbar_wait(&sh.tfull[acc], (it / kMaxAcc) & 1, &sh.abort, kWaitLimitNs)) {
         raise_abort(sh, a.status);
@@ -365,24 +388,6 @@ __global__ void __launch_bounds__(tc_threads<kGroups>(), kGroups == 4 ? 1 : (kGr
         // head sum keeps the per-row epilogue's order (four partial sums, one
         // head each, then (s0 + s1) + (s2 + s3)), so the logits are those of
         // the per-row path with the heads padded by zero weights
-        const bool live = key < eff;
-        const bool valid = !(a.key_valid && live) || a.key_valid[key] != 0;
-        // the warp's 32 keys lie in one page: lane l fetches query row b * G + l's
-        // column of it, handed to the other lanes by shuffles below
-        int cm_lane = -1, pos_lane = 0, logical = 0, lo_lane = 0, hi_lane = 0;
-        if (a.win_lo && lane < a.group_rows && b * a.group_rows + lane < a.real_rows) {
-          lo_lane = a.win_lo[b * a.group_rows + lane];
-          hi_lane = a.win_hi[b * a.group_rows + lane];
-        }
-        if (a.colmap) {
-          const int64_t key0 = static_cast<int64_t>(cur.t) * 128 + q4 * 32;
-          const int64_t wpage = key0 < eff ? a.table[b * a.table_stride + (key0 >> 6)] : -1;
-          if (wpage >= 0 && wpage < a.colmap_pages && lane < a.group_rows) {
-            cm_lane = a.colmap[wpage * a.colmap_stride + static_cast<int64_t>(b) * a.group_rows + lane];
-            if (a.mask_map && b * a.group_rows + lane < a.real_rows) pos_lane = a.mask_pos[b * a.group_rows + lane];
-          }
-          if (a.mask_map && wpage >= 0 && wpage < a.colmap_pages) logical = a.mask_map[wpage * 64 + (key & 63)];
-        }
         const int row0 = b * a.group_rows;
         const int kcol = static_cast<int>(key & 63);
         const bool store_ok = live && (!a.key_valid || valid);
