@@ -568,8 +568,8 @@ constexpr int kMaskCols = 4096;
 
 __global__ void mask_scores_kernel(float* __restrict__ scores, int64_t score_stride, int64_t width,
                                    const int32_t* __restrict__ table, int64_t table_stride,
-                                   const int32_t* __restrict__ mapping, const int32_t* __restrict__ positions,
-                                   int64_t dedup_cols, int64_t fixed_start) {
+                                   const int32_t* __restrict__ mapping, int64_t mapping_pages,
+                                   const int32_t* __restrict__ positions, int64_t dedup_cols, int64_t fixed_start) {
   // a CTA takes kMaskCols columns of one row, a thread every 256th of them
   const int64_t row = blockIdx.y;
   const int pos = positions[row];
@@ -578,7 +578,8 @@ __global__ void mask_scores_kernel(float* __restrict__ scores, int64_t score_str
 #pragma unroll 4
   for (int64_t col = first; col < last; col += 256) {
     const int64_t page = table[row * table_stride + col / 64];
-    const int logical = mapping[page * 64 + col % 64];
+    // a page outside the mapping reads as no token (masked)
+    const int logical = page >= 0 && page < mapping_pages ? mapping[page * 64 + col % 64] : -1;
     if (logical < 0 || logical > pos || (col < dedup_cols && (logical < 64 || logical >= fixed_start)))
       scores[row * score_stride + col] = -CUDART_INF_F;
   }
@@ -649,7 +650,8 @@ extern "C" int v1x_pack_q(const void* q, int dtype, int64_t qs0, int64_t qs1, in
 }
 
 extern "C" int v1x_mask_scores(float* scores, int64_t score_stride, int64_t width, const int32_t* table,
-                               int64_t table_stride, const int32_t* mapping, const int32_t* positions,
+                               int64_t table_stride, const int32_t* mapping, int64_t mapping_pages,
+                               const int32_t* positions,
                                int64_t dedup_cols, int64_t fixed_start, int64_t rows, void* stream) {
   clear_error();
   V1X_CHECK_ARG(rows >= 0 && width >= 0 && score_stride >= width && table_stride >= 0,
@@ -659,6 +661,6 @@ extern "C" int v1x_mask_scores(float* scores, int64_t score_stride, int64_t widt
   V1X_CHECK_ARG(rows < 65536, "mask_scores: at most 65535 rows per call");
   const dim3 grid(static_cast<unsigned>((width + kMaskCols - 1) / kMaskCols), static_cast<unsigned>(rows));
   mask_scores_kernel<<<grid, 256, 0, as_stream(stream)>>>(scores, score_stride, width, table, table_stride, mapping,
-                                                         positions, dedup_cols, fixed_start);
+                                                         mapping_pages, positions, dedup_cols, fixed_start);
   return launch_status("v1x_mask_scores");
 }

@@ -35,13 +35,14 @@ _gather_slots.__doc__ = "KG[t] = K[REQ[IDS[t]], HEAD] (zeros for negative ids); 
 def mask_scores(scores, table, mapping, positions, dedup_cols=0, fixed_start=0):
     """NA/kernels.py:47-59: in place, column c of row r becomes -inf when its
     logical token l = mapping[table[r, c // 64], c % 64] is < 0, > positions[r],
-    or (c < dedup_cols and (l < 64 or l >= fixed_start))."""
+    or (c < dedup_cols and (l < 64 or l >= fixed_start)); a page outside the
+    mapping reads as l = -1."""
     require(scores.dtype == torch.float32 and scores.dim() == 2 and scores.stride(1) == 1, "scores: float32 rows")
     require(table.dtype == torch.int32 and table.dim() == 2 and table.stride(1) == 1, "table: int32 [rows, -1]")
     require(mapping.dtype == torch.int32 and mapping.is_contiguous(), "mapping: int32 [pages, 64]")
     require(positions.dtype == torch.int32 and positions.numel() >= scores.shape[0], "positions: int32 [rows]")
     _lib.call("v1x_mask_scores", ptr(scores), scores.stride(0), scores.shape[1], ptr(table), table.stride(0),
-              ptr(mapping), ptr(positions), int(dedup_cols), int(fixed_start), scores.shape[0],
+              ptr(mapping), mapping.numel() // 64, ptr(positions), int(dedup_cols), int(fixed_start), scores.shape[0],
               _lib.stream_of(scores), device=scores.device)
 
 

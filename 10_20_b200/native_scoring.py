@@ -270,7 +270,10 @@ def _select_packed(scorer, qp, arena, head, page_ids, fixed_ids, positions, full
         coarse.masked_fill_(~valid[None], -torch.inf)
         coarse = coarse.reshape(rows, pages * 8)
         _route_into(coarse, selected, pages, take)
-    table = torch.cat((page_ids[selected.long()], fixed_ids[None].expand(rows, -1)), 1).contiguous()
+    # a padding id of the route's blocked layout (>= pages, reached only when -inf
+    # pages enter the take) would index past page_ids: it names the last page
+    table = torch.cat((page_ids[selected.long().clamp_(max=pages - 1)], fixed_ids[None].expand(rows, -1)),
+                      1).contiguous()
     used = torch.cat((page_ids, fixed_ids)).to(torch.int32).contiguous()
     scores = scorer._logits(qp, arena.fine[head], used, used.numel() * 64, table)
     mask_scores(scores, table, arena.mapping[head], positions,

@@ -519,10 +519,13 @@ V1X_API int v1x_pack_q(const void* q, int dtype, int64_t qs0, int64_t qs1, int64
  * [rows, width] row stride score_stride; table i32 row stride table_stride (fine
  * page of each 64 columns); mapping i32 [pages, 64] logical tokens; positions
  * i32 [rows].  Column c of row r becomes -inf when its logical token l is < 0,
- * > positions[r], or (c < dedup_cols and (l < 64 or l >= fixed_start)). */
+ * > positions[r], or (c < dedup_cols and (l < 64 or l >= fixed_start)).  A table
+ * entry outside [0, mapping_pages) reads as l = -1 (the reference reads past the
+ * mapping there). */
 V1X_API int v1x_mask_scores(float* scores, int64_t score_stride, int64_t width, const int32_t* table,
-                    int64_t table_stride, const int32_t* mapping, const int32_t* positions,
-                    int64_t dedup_cols, int64_t fixed_start, int64_t rows, void* stream);
+                    int64_t table_stride, const int32_t* mapping, int64_t mapping_pages,
+                    const int32_t* positions, int64_t dedup_cols, int64_t fixed_start, int64_t rows,
+                    void* stream);
 
 /* DS/kernels.py:594-600. logical i32 [batch, topk] -> out i32 [batch, stride]. */
 V1X_API int v1x_expand_logical(const int32_t* logical, int32_t* out, int64_t topk, int64_t stride,

@@ -1112,14 +1112,18 @@ def topk_transform(scores, seq_lens, page_table, page_size, topk, original_ids=N
 def mask_scores(scores, table, mapping, positions, dedup_cols=0, fixed_start=0):
     """NA/kernels.py:47-59: column c of row r becomes -inf when its logical token
     l = mapping[table[r, c // 64], c % 64] is < 0, > positions[r], or (c <
-    dedup_cols and (l < 64 or l >= fixed_start)).  Returns a masked copy."""
+    dedup_cols and (l < 64 or l >= fixed_start)).  A table entry outside the
+    mapping reads as l = -1 (the reference reads past the mapping there).
+    Returns a masked copy."""
     s = np.array(scores, np.float32, copy=True)
     B, W = s.shape
     table = np.asarray(table, np.int64)
     mapping = np.asarray(mapping, np.int64)
     cols = np.arange(W)
     for r in range(B):
-        lg = mapping[table[r, cols // 64], cols % 64]
+        pg = table[r, cols // 64]
+        ok = (pg >= 0) & (pg < mapping.shape[0])
+        lg = np.where(ok, mapping[np.where(ok, pg, 0), cols % 64], -1)
         bad = (lg < 0) | (lg > int(positions[r])) | ((cols < dedup_cols) & ((lg < 64) | (lg >= fixed_start)))
         s[r, bad] = NEG_INF
     return s

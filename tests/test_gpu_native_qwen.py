@@ -132,6 +132,7 @@ def test_mask_scores_matches_oracle(dedup):
     rows, width, pages = 7, 1100, 40
     s = rng.standard_normal((rows, width)).astype(np.float32)
     table = rng.integers(0, pages, (rows, (width + 63) // 64)).astype(np.int32)
+    table[2, 3], table[4, 0] = pages + 3, -1        # outside the mapping: no token
     mapping = rng.integers(-5, 3000, (pages, 64)).astype(np.int32)
     positions = rng.integers(0, 3000, rows).astype(np.int32)
     fixed = 2000 if dedup else 0

@@ -152,3 +152,10 @@ def test_pack_q_and_quantize_golden(golden):
     q8, w = O.pack_q(q.reshape(-1, 1, 128), 1, 1.0)
     assert np.array_equal(q8.reshape(-1), g["quant_q8"].reshape(-1))
     assert np.array_equal(w.reshape(-1), g["quant_scale"].reshape(-1))
+
+
+def test_mask_scores_page_outside_mapping_is_masked():
+    s = np.ones((1, 128), np.float32)
+    mapping = np.zeros((2, 64), np.int32)
+    got = O.mask_scores(s, np.array([[5, -1]], np.int32), mapping, [10])
+    assert np.isinf(got).all()
