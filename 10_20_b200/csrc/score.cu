@@ -18,6 +18,7 @@
 #include <cuda_fp8.h>
 
 #include <algorithm>
+#include <cmath>
 
 #include "common.cuh"
 
@@ -311,15 +312,17 @@ __global__ void column_map_kernel(const int32_t* __restrict__ tables, int64_t ts
 }
 
 // The listed columns: a copy of the source column's 64 logits (the same page's
-// keys), or zeros for a page outside the pool (what the per-row scorer's
-// zero-filled loads give).  One warp per entry.
-__global__ void fix_columns_kernel(const int32_t* __restrict__ fix, float* __restrict__ out, int64_t out_stride) {
+// keys), or for a page outside the pool zeros (what the per-row scorer's
+// zero-filled loads give) -- -inf when the mask is applied (no token there).
+// One warp per entry.
+__global__ void fix_columns_kernel(const int32_t* __restrict__ fix, float* __restrict__ out, int64_t out_stride,
+                                   float outside) {
   const int n = fix[0];
   const int lane = threadIdx.x & 31;
   for (int e = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; e < n; e += (gridDim.x * blockDim.x) >> 5) {
     const int64_t r = fix[1 + 3 * e], c = fix[2 + 3 * e], src = fix[3 + 3 * e];
     float* row = out + r * out_stride;
-    for (int j = lane; j < 64; j += 32) row[c * 64 + j] = src >= 0 ? row[src * 64 + j] : 0.0f;
+    for (int j = lane; j < 64; j += 32) row[c * 64 + j] = src >= 0 ? row[src * 64 + j] : outside;
   }
 }
 }  // namespace
@@ -372,7 +375,8 @@ extern "C" int v1x_score_fp8_grouped(const uint8_t* q, const float* w, const uin
                                     status, s))
     return rc;
   if (row_tables) {
-    fix_columns_kernel<<<static_cast<unsigned>(num_sms()), 256, 0, s>>>(fix, out, out_stride);
+    fix_columns_kernel<<<static_cast<unsigned>(num_sms()), 256, 0, s>>>(fix, out, out_stride,
+                                                                         mask_map ? -INFINITY : 0.0f);
     return launch_status("v1x_score_fp8_grouped (fix columns)");
   }
   return V1X_OK;

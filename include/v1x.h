@@ -585,7 +585,8 @@ V1X_API int v1x_score_fp8_ex(const uint8_t* q, const float* w, const uint8_t* po
  * [pool_pages * 64], may be NULL; with row tables only) and mask_pos (i32
  * [rows]): mask_scores fused (NA/kernels.py:47-59 without dedup columns) -- the
  * logit of row r for a key whose logical token l = mask_map[page * 64 + slot]
- * is < 0 or > mask_pos[r] is -inf (columns of a page outside the pool stay 0). */
+ * is < 0 or > mask_pos[r] is -inf (so are the columns of a page outside the
+ * pool, which are 0 without the mask). */
 V1X_API int v1x_score_fp8_grouped(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages,
                   int64_t keys, const int32_t* table, const int32_t* row_tables, int64_t row_table_stride,
                   int64_t row_table_cols, const uint8_t* key_valid, const int32_t* mask_map,
