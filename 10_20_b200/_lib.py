@@ -60,7 +60,7 @@ SIGNATURES = {
     "v1x_mask_scores": [P, I64, I64, P, I64, P, I64, P, I64, I64, I64, P],
     "v1x_query_stage": [P, P, P, P, I64, P, P, P, I64, P, P, P, P, P, P, I64, I64, I64, I64, P],
     "v1x_score_fp8": [P, P, P, I64, P, P, I64, P, I64, I64, P, I64, I64, I32, I32, I32, P, I64, P],
-    "v1x_score_fp8_ex": [P, P, P, I64, P, P, I64, P, I64, I64, P, I64, I64, I32, I32, I32, I32, P, I64, P],
+    "v1x_score_fp8_ex": [P, P, P, I64, P, P, I64, P, I64, I64, P, I64, I64, I32, I32, I32, I32, I64, P, I64, P],
     "v1x_mqa_logits_fp8": [P, P, P, P, I64, P, P, P, I64, I64, I32, I32, I64, P],
     "v1x_mqa_logits_fp8_grouped": [P, P, P, P, I64, P, P, P, I64, I64, I64, I64, I32, P, P],
     "v1x_score_fp8_grouped": [P, P, P, I64, I64, P, P, I64, I64, P, P, P, P, P, I64, I64, I64, I64, I32, P, P],

@@ -216,7 +216,7 @@ __global__ void __launch_bounds__(kScoreThreads, kHeads == 1 ? 4 : 1)
 int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages, const int32_t* lens,
                  const int32_t* table, int64_t table_stride, float* out, int64_t out_stride, int64_t max_len,
                  float* page_max, int64_t page_stride, int64_t heads, int relu, int clean, int lens_kind,
-                 int64_t batch, int32_t* status, cudaStream_t stream);
+                 int64_t batch, int32_t* status, cudaStream_t stream, int64_t max_ctas);
 int mqa_tc_grouped(const uint8_t* q, const float* w, const uint8_t* k, const float* k_scale, int64_t keys,
                    const int32_t* win_lo, const int32_t* win_hi, float* out, int64_t out_stride, int64_t group_rows,
                    int64_t real_rows, int relu, int64_t vrows, int32_t* status, cudaStream_t stream);
@@ -231,7 +231,7 @@ namespace {
 int score_dispatch(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages, const int32_t* lens,
                    const int32_t* table, int64_t table_stride, float* out, int64_t out_stride, int64_t max_len,
                    float* page_max, int64_t page_stride, int64_t heads, int relu, int clean, int impl,
-                   int lens_kind, int32_t* status, int64_t batch, void* stream) {
+                   int lens_kind, int32_t* status, int64_t batch, void* stream, int64_t max_ctas = 0) {
   clear_error();
   V1X_CHECK_ARG(heads >= 1 && heads <= 256, "score_fp8: heads must be in [1, 256]");
   V1X_CHECK_ARG(batch >= 0 && max_len >= 0 && pool_pages > 0, "score_fp8: bad geometry");
@@ -249,7 +249,7 @@ int score_dispatch(const uint8_t* q, const float* w, const uint8_t* pool, int64_
   const bool tc = impl == 2 || (impl == 0 && tc_shape);
   if (tc)
     return score_fp8_tc(q, w, pool, pool_pages, lens, table, table_stride, out, out_stride, max_len, page_max,
-                        page_stride, heads, relu, clean, lens_kind, batch, status, as_stream(stream));
+                        page_stride, heads, relu, clean, lens_kind, batch, status, as_stream(stream), max_ctas);
   if (heads > kSimtMaxHeads) {
     set_error("score_fp8: the SIMT path takes heads <= %d", kSimtMaxHeads);
     return V1X_ERR_UNSUPPORTED;
@@ -395,9 +395,11 @@ extern "C" int v1x_score_fp8_ex(const uint8_t* q, const float* w, const uint8_t*
                                 const int32_t* lens, const int32_t* table, int64_t table_stride,
                                 float* out, int64_t out_stride, int64_t max_len, float* page_max,
                                 int64_t page_stride, int64_t heads, int relu, int clean, int impl,
-                                int lens_kind, int32_t* status, int64_t batch, void* stream) {
+                                int lens_kind, int64_t max_ctas, int32_t* status, int64_t batch, void* stream) {
+  using namespace v1x;
+  V1X_CHECK_ARG(max_ctas >= 0, "score_fp8: max_ctas must be >= 0");
   return v1x::score_dispatch(q, w, pool, pool_pages, lens, table, table_stride, out, out_stride, max_len, page_max,
-                             page_stride, heads, relu, clean, impl, lens_kind, status, batch, stream);
+                             page_stride, heads, relu, clean, impl, lens_kind, status, batch, stream, max_ctas);
 }
 
 extern "C" int v1x_mqa_logits_fp8(const uint8_t* q, const float* w, const uint8_t* k, const float* k_scale,

@@ -535,7 +535,8 @@ struct GroupedOut {
 int score_tc_launch(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages, const int32_t* lens,
                     const int32_t* table, int64_t table_stride, float* out, int64_t out_stride, int64_t max_len,
                     float* page_max, int64_t page_stride, int64_t heads, int relu, int clean, int lens_kind,
-                    int64_t batch, int32_t* status, cudaStream_t stream, const GroupedOut* grp);
+                    int64_t batch, int32_t* status, cudaStream_t stream, const GroupedOut* grp,
+                    int64_t max_ctas = 0);
 
 }  // namespace
 
@@ -543,9 +544,9 @@ int score_tc_launch(const uint8_t* q, const float* w, const uint8_t* pool, int64
 int score_fp8_tc(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages, const int32_t* lens,
                  const int32_t* table, int64_t table_stride, float* out, int64_t out_stride, int64_t max_len,
                  float* page_max, int64_t page_stride, int64_t heads, int relu, int clean, int lens_kind,
-                 int64_t batch, int32_t* status, cudaStream_t stream) {
+                 int64_t batch, int32_t* status, cudaStream_t stream, int64_t max_ctas) {
   return score_tc_launch(q, w, pool, pool_pages, lens, table, table_stride, out, out_stride, max_len, page_max,
-                         page_stride, heads, relu, clean, lens_kind, batch, status, stream, nullptr);
+                         page_stride, heads, relu, clean, lens_kind, batch, status, stream, nullptr, max_ctas);
 }
 
 // Grouped mode: `vrows` virtual rows of group_rows query rows x 4 heads.
@@ -576,7 +577,8 @@ namespace {
 int score_tc_launch(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages, const int32_t* lens,
                     const int32_t* table, int64_t table_stride, float* out, int64_t out_stride, int64_t max_len,
                     float* page_max, int64_t page_stride, int64_t heads, int relu, int clean, int lens_kind,
-                    int64_t batch, int32_t* status, cudaStream_t stream, const GroupedOut* grp) {
+                    int64_t batch, int32_t* status, cudaStream_t stream, const GroupedOut* grp,
+                    int64_t max_ctas) {
   if ((heads != 1 && heads % 32 != 0) || heads > 128 || batch > kMaxTcRows || pool_pages >= (int64_t(1) << 31)) {
     set_error("score_fp8 (tensor core): heads must be 1 or a multiple of 32 <= 128 and batch <= %d", kMaxTcRows);
     return V1X_ERR_UNSUPPORTED;
@@ -649,6 +651,10 @@ int score_tc_launch(const uint8_t* q, const float* w, const uint8_t* pool, int64
   size_t smem = plan(grid, w_rows);
   if (cols > 256 || smem > 113 * 1024) {  // two CTAs per SM need <= 256 TMEM columns and <= 113 KB each
     grid = std::min<int64_t>(sms, std::max<int64_t>(max_tiles, 1));
+    smem = plan(grid, w_rows);
+  }
+  if (max_ctas > 0 && grid > max_ctas) {  // the caller's cap (small batches of many in flight)
+    grid = max_ctas;
     smem = plan(grid, w_rows);
   }
   if (smem > 227 * 1024) {

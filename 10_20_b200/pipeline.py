@@ -49,13 +49,14 @@ class SelectionStep:
 
     def __init__(self, case, gather: bool = True, gather_v: bool = False, fused_route_pages: bool = True,
                  keep_logits: bool = False, ratio=None, expand: bool = False, budget=None,
-                 fused: bool = True):
+                 fused: bool = True, score_ctas: int = 0):
         """ratio=None: the fixed page budget take = min(pages, budget) (the
         reference's BudgetMetadata; budget an int32 device tensor of one element,
         by default holding case.take, which bounds it); ratio=(num, den): the
         reference's default take rule min(pages, max(ceil(pages*num/den),
         ceil(topk/64))).  expand: also write the x4 expanded logical positions
-        ([B, 4*topk+64], -1 padded)."""
+        ([B, 4*topk+64], -1 padded).  score_ctas > 0 caps the centre scorer's
+        grid (for small batches stepped many at a time)."""
         c = self.case = case
         d = c.lens.device
         B = c.B
@@ -107,6 +108,7 @@ class SelectionStep:
         if self.fused_select and not self.fine_scores_kept:
             self.scores = None
         self.status = torch.zeros(1, dtype=torch.int32, device=d)
+        self.score_ctas = int(score_ctas)
 
     # -- the step ------------------------------------------------------------
     def _centres(self, rs):
@@ -117,10 +119,11 @@ class SelectionStep:
             scoring.fp8_paged_mqa_logits(c.q8[rs], c.centers, c.w[rs], c.lens[rs], c.center_table[rs], None,
                                          c.P * 8, page_max=self.page_scores[rs], logits=self.keep_logits,
                                          out=self.center_logits[rs] if self.keep_logits else None,
-                                         clean_logits=False, lens_kind="centres")
+                                         clean_logits=False, lens_kind="centres", max_ctas=self.score_ctas)
         else:
             scoring.fp8_paged_mqa_logits(c.q8[rs], c.centers, c.w[rs], c.lens[rs], c.center_table[rs], None,
-                                         c.P * 8, out=self.center_logits[rs], lens_kind="centres")
+                                         c.P * 8, out=self.center_logits[rs], lens_kind="centres",
+                                         max_ctas=self.score_ctas)
 
     def _route(self, rs):
         c = self.case

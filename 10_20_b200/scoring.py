@@ -34,7 +34,7 @@ def fp8_paged_mqa_logits(q, kv_cache, weights, context_lens, block_table, schedu
                          max_context_len: int, clean_logits: bool = True, relu: bool = True,
                          out: torch.Tensor | None = None, impl: str = "auto",
                          page_max: torch.Tensor | None = None, logits: bool = True,
-                         lens_kind: str = "tokens"):
+                         lens_kind: str = "tokens", max_ctas: int = 0):
     """Logits [B, max_context_len] (float32); columns >= context_lens[b] are -inf.
 
     q: e4m3 [B, H, 128] or [B, 1, H, 128]; kv_cache: packed uint8 [pages, 8448] or
@@ -49,6 +49,7 @@ def fp8_paged_mqa_logits(q, kv_cache, weights, context_lens, block_table, schedu
     the centre count of a token length n, max(8 * ((n-1)//1024*16), 1) -- the
     center_lens the query metadata derives (DS/kernels.py:589) -- so centre scoring
     can take the raw token lengths and need not wait for the metadata kernel.
+    max_ctas (extension): > 0 caps the tensor-core scorer's persistent grid.
     """
     if q.dim() == 4:
         require(q.shape[1] == 1, "only next_n == 1 is supported")
@@ -81,7 +82,7 @@ def fp8_paged_mqa_logits(q, kv_cache, weights, context_lens, block_table, schedu
     _lib.call("v1x_score_fp8_ex", ptr(q), ptr(weights), ptr(kv_cache), kv_cache.numel() // 8448, ptr(lens),
               ptr(block_table), block_table.stride(0), ptr(out), out.stride(0) if out is not None else 0,
               int(max_context_len), ptr(page_max), page_max.stride(0) if page_max is not None else 0, H,
-              int(bool(relu)), int(bool(clean_logits)), IMPLS[impl], LENS_KINDS[lens_kind],
+              int(bool(relu)), int(bool(clean_logits)), IMPLS[impl], LENS_KINDS[lens_kind], int(max_ctas),
               ptr(status_word(q.device)), B,
               _lib.stream_of(q), device=q.device)
     return out if logits else page_max

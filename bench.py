@@ -1028,14 +1028,14 @@ class Batches:
     overlaps the selection of the next and consecutive steps touch disjoint
     data.  Events on the caller's stream bracket a run."""
 
-    def __init__(self, cfg, lens, seed, inflight, device):
+    def __init__(self, cfg, lens, seed, inflight, device, score_ctas=0):
         synth = importlib.import_module("10_20_b200.synth")
         pipeline = importlib.import_module("10_20_b200.pipeline")
         self.device = device
         self.sets = []
         for i in range(inflight):
             case = make_case(synth, dict(cfg, B=len(lens)), seed + 7919 * i, device, lens=lens)
-            step = pipeline.SelectionStep(case, gather=cfg["latent"] > 0)
+            step = pipeline.SelectionStep(case, gather=cfg["latent"] > 0, score_ctas=score_ctas)
             st = torch.cuda.Stream(device=device)
             st.wait_stream(torch.cuda.current_stream())
             with torch.cuda.stream(st):
@@ -1218,7 +1218,7 @@ def run_decode(args, cfg):
     inflight = max(1, args.inflight)
     lens_all = _request_lens(cfg, world)
     lens = _shard(cfg, lens_all, world, rank, B)
-    bat = Batches(cfg, lens, 1000 + rank, inflight, device)
+    bat = Batches(cfg, lens, 1000 + rank, inflight, device, score_ctas=args.score_ctas)
     case, step = bat.sets[0]["case"], bat.sets[0]["step"]
     acct = step.algorithmic_bytes()
     gather_on = step.gather
@@ -1298,13 +1298,18 @@ def run_decode(args, cfg):
         strong = {"job_requests": B, "requests_per_gpu": bs, "unit": "queries/s"}
         # the headline's depth of batches in flight, then a depth that keeps as
         # many rows in flight per GPU as one GPU holds with the whole job
+        n_sm = torch.cuda.get_device_properties(device).multi_processor_count
         for depth in (inflight, min(inflight * world, 24)):
-            sb = Batches(dict(cfg, B=bs), lens_s, 2000 + rank, depth, device)
+            # the deep pipeline's centre scorer takes about its batch's share of
+            # the SMs (many small batches on separate streams): grid capped at
+            # 2 * SMs / depth, at least 16 CTAs
+            ctas = 0 if depth == inflight else max(16, 2 * n_sm // depth)
+            sb = Batches(dict(cfg, B=bs), lens_s, 2000 + rank, depth, device, score_ctas=ctas)
             for _ in range(max(args.warmup, 3)):
                 sb.run(depth)
             sms, _, _ = _timed(lambda: sb.run(args.steps), dist, device)
             entry = {"batches_in_flight": depth, "value": B * args.steps / (sms / 1e3),
-                     "ms_per_step": sms / args.steps}
+                     "ms_per_step": sms / args.steps, "score_ctas": ctas or None}
             if depth == inflight:
                 strong.update(entry)
                 split = strong["single_batch_stage_us"] = _stage_split(sb.sets[0]["step"])
@@ -1419,6 +1424,8 @@ def main():
     ap.add_argument("--no-parity", action="store_true", help="skip the oracle spot check of sampled rows")
     ap.add_argument("--inflight", type=int, default=3,
                     help="independent batches in flight (the gather of one overlaps the selection of the next)")
+    ap.add_argument("--score-ctas", type=int, default=0,
+                    help="cap of the centre scorer's persistent grid (0: two CTAs per SM)")
     args = ap.parse_args()
     if args.workload in ("sort", "gather", "pages", "build", "shared", "signed"):
         if args.impl == "reference":

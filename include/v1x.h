@@ -557,12 +557,15 @@ V1X_API int v1x_score_fp8(const uint8_t* q, const float* w, const uint8_t* pool,
  * row b derived from lens[b] by lens_kind: 0 = lens[b] (v1x_score_fp8 itself);
  * 1 = the centre count of a token length n, max(8 * ((n-1)/1024*16), 1) -- the
  * center_lens of DS/kernels.py:589 -- so centre scoring can run on the raw token
- * lengths concurrently with the query-metadata kernel. */
+ * lengths concurrently with the query-metadata kernel.  max_ctas > 0 caps the
+ * tensor-core scorer's persistent grid (0: up to two CTAs per SM): small batches
+ * stepped many at a time on separate streams finish sooner together when each
+ * takes a share of the SMs. */
 V1X_API int v1x_score_fp8_ex(const uint8_t* q, const float* w, const uint8_t* pool, int64_t pool_pages,
                   const int32_t* lens, const int32_t* table, int64_t table_stride, float* out,
                   int64_t out_stride, int64_t max_len, float* page_max, int64_t page_stride,
-                  int64_t heads, int relu, int clean, int impl, int lens_kind, int32_t* status,
-                  int64_t batch, void* stream);
+                  int64_t heads, int relu, int clean, int impl, int lens_kind, int64_t max_ctas,
+                  int32_t* status, int64_t batch, void* stream);
 
 /* Extension (no reference counterpart): the signed-score Scorer's paged logits
  * (NA/scoring.py:48-53, DeepGEMM over q padded to 32 heads, four of them live)
