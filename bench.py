@@ -1321,7 +1321,8 @@ def run_decode(args, cfg):
         strong["limiter"] = (
             f"the row latency of select_fused (one CTA per row, {split.get('select', 0):.0f} us for a batch of "
             f"{bs} rows, as for 128): with {inflight} batches in flight only {bs * inflight} rows are selected "
-            f"at once on 148 SMs, so the step is latency-bound; a deeper pipeline restores the rows in flight")
+            f"at once on 148 SMs, so the step is latency-bound; a deeper pipeline restores the rows in flight "
+            f"(its centre scorer's grid capped to the batch's share of the SMs)")
 
     # ---- parity spot check (rank 0): sampled rows of batch 0 against the oracle -----
     parity = None
