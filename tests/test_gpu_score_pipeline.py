@@ -230,6 +230,20 @@ def test_selection_step_graph_replay(cuda_dev):
     assert torch.equal(step.physical, ref)
 
 
+@pytest.mark.parametrize("ctas", [1, 16, 37])
+def test_selection_step_score_ctas_cap(ctas, cuda_dev):
+    """A capped centre-scorer grid (each CTA takes a longer tile range) gives the
+    same selection as the default grid."""
+    case = _small_case(B=8, seed=13, latent=0)
+    ref = pipeline.SelectionStep(case, gather=False, keep_logits=True)
+    ref.run()
+    step = pipeline.SelectionStep(case, gather=False, keep_logits=True, score_ctas=ctas)
+    step.run()
+    torch.cuda.synchronize()
+    assert torch.equal(step.page_scores, ref.page_scores)
+    assert torch.equal(step.physical, ref.physical) and torch.equal(step.logical, ref.logical)
+
+
 @pytest.mark.parametrize("impl,H", [("simt", 1), ("simt", 16), ("tensor_core", 1), ("tensor_core", 64)])
 def test_page_max_and_route_pages(impl, H, cuda_dev):
     """Scoring page maxima + route_pages == route over the centre logits (bit-exact)."""
