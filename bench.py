@@ -46,7 +46,7 @@ METRIC = "indexed queries/sec (route+FP8 score+Top2048+gather); HBM GB/s as % of
 # measured in the run that prints it (the roofline line says so)
 GATHER_DECODE_DRAM_BYTES = 303167744 + 250278400
 GATHER_DECODE_DRAM_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one gather_rows_kernel launch "
-                             "of this workload, captured separately (profiles/gather_rows_decode_dram.md)")
+                             "of this workload, captured separately")
 
 
 def peaks():

@@ -132,7 +132,7 @@ def test_near_tie_flip_is_within_band(small):
             off = col - take * 64
             lg = off if off < sink else tail + off - sink
         s.physical[r, t] = int(nt[lg // 64]) * 64 + lg % 64
-        s.fine_scores_kept = False          # judge the slots by the oracle's scores alone
+        s.fine_scores_kept = False          # check the slots by the oracle's scores alone
         return SC.check_rows(s, case, [r], latent_check=False)
 
     near = out[0]                            # the best unselected slot: just below the threshold
