@@ -1218,7 +1218,11 @@ def run_decode(args, cfg):
     inflight = max(1, args.inflight)
     lens_all = _request_lens(cfg, world)
     lens = _shard(cfg, lens_all, world, rank, B)
-    bat = Batches(cfg, lens, 1000 + rank, inflight, device, score_ctas=args.score_ctas)
+    # with batches in flight the centre scorer takes one CTA per SM (it leaves
+    # room for the other batches' kernels); one batch alone keeps two per SM
+    n_sms = torch.cuda.get_device_properties(device).multi_processor_count
+    score_ctas = args.score_ctas if args.score_ctas >= 0 else (n_sms if inflight > 1 else 0)
+    bat = Batches(cfg, lens, 1000 + rank, inflight, device, score_ctas=score_ctas)
     case, step = bat.sets[0]["case"], bat.sets[0]["step"]
     acct = step.algorithmic_bytes()
     gather_on = step.gather
@@ -1243,6 +1247,9 @@ def run_decode(args, cfg):
         s.synchronize()
         return g
 
+    # one batch alone: the default grid (two CTAs per SM)
+    step.score_ctas = 0
+    one_graph = capture(step.run)
     step.gather = False
     sel_graph = capture(step.run)
     step.gather = gather_on
@@ -1269,7 +1276,7 @@ def run_decode(args, cfg):
         return [a.elapsed_time(b) for a, b in evs]
 
     diag_steps = min(args.steps, 20)
-    one_ms = timed_each(bat.sets[0]["graph"], diag_steps)
+    one_ms = timed_each(one_graph, diag_steps)
     sel_ms = timed_each(sel_graph, diag_steps)
     # the gather kernel alone, replayed back to back: its 604 MB per launch is far
     # larger than L2, and its own write-backs stay in the timing
@@ -1361,6 +1368,7 @@ def run_decode(args, cfg):
                        "parallelism": f"requests sharded by bytes (longest first), {world} ranks x "
                                       f"{B} requests, no data-path collective",
                        "batches_in_flight": inflight,
+                       "centre_scorer_ctas": score_ctas or "two per SM (one batch alone: always)",
                        "l2": "inputs larger than L2: consecutive steps alternate between independent batches "
                              "(separate pools, ~12 GB each); single-batch diagnostics after a 256 MB read",
                        "algorithmic_bytes_per_step": acct["total"]},
@@ -1425,8 +1433,9 @@ def main():
     ap.add_argument("--no-parity", action="store_true", help="skip the oracle spot check of sampled rows")
     ap.add_argument("--inflight", type=int, default=3,
                     help="independent batches in flight (the gather of one overlaps the selection of the next)")
-    ap.add_argument("--score-ctas", type=int, default=0,
-                    help="cap of the centre scorer's persistent grid (0: two CTAs per SM)")
+    ap.add_argument("--score-ctas", type=int, default=-1,
+                    help="cap of the centre scorer's persistent grid with batches in flight (0: two CTAs per SM; "
+                         "-1: one CTA per SM when more than one batch is in flight, else 0)")
     args = ap.parse_args()
     if args.workload in ("sort", "gather", "pages", "build", "shared", "signed"):
         if args.impl == "reference":
