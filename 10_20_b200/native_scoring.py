@@ -3,14 +3,19 @@
 (NA/shared_scoring.py:9-62) and ``quantize`` (NA/grouping.py:41-44), composed
 from libv1x.so's operators:
 
-- q packing (quantise the four query heads, pad to the 32 the scorer takes,
-  fold the softmax scale into the head weights): ``v1x_pack_q``;
-- signed FP8 paged logits (the no-ReLU DeepGEMM fork the reference loads):
-  ``scoring.fp8_paged_mqa_logits(..., relu=False)``; the ``dsa`` mode's flat
-  logits: ``scoring.fp8_mqa_logits(..., relu=False)``;
+- q packing (quantise the four query heads, fold the softmax scale into the
+  head weights; padded to the 32 heads of the reference's scorer, or kept at
+  four for the grouped scorer): ``v1x_pack_q``;
+- signed FP8 logits (the no-ReLU DeepGEMM fork the reference loads): by
+  default the grouped tensor-core scorer (``scoring.paged_logits_grouped``,
+  ``scoring.mqa_logits_grouped`` for the ``dsa`` mode: 32 query rows x 4 heads
+  per MMA operand, with the validity mask and ``mask_scores`` in the same pass);
+  with ``Scorer.impl`` "tensor_core" or "simt" the per-row scorers
+  (``scoring.fp8_paged_mqa_logits`` / ``fp8_mqa_logits``, ``relu=False``) and a
+  separate ``gather.mask_scores``;
 - page route: ``native_route`` (route.py's tie order);
-- ``gather.mask_scores``; the mapped Top-2048: ``topk2048_mapped``; the
-  ``dsa`` mode's plain Top-2048: ``topk2048``.
+- the mapped Top-2048: ``topk2048_mapped``; the ``dsa`` mode's plain
+  Top-2048: ``topk2048``.
 
 The backend's host state (its arenas, ``state`` / ``arena`` objects) is the
 caller's, duck-typed as in the reference: ``state.pages``, ``state.centers``,
