@@ -8,7 +8,7 @@ p = rank / BASE + (rank % BASE) * 128, BASE = n / 128 for the smallest n in
 {128, ..., 4096} holding the pages -- is fused.route's (VQ:26-30) for every
 (threads, pages) it accepts, and writes the first `take` page ids of the
 ranking to table[:, :take] (the columns after them are the caller's).  So the
-ranking here is fused.route's, written through a scratch row block.  The
+ranking here is fused.route's, written through a row block allocated per call.  The
 bitmap of ``route_mask`` marks the selected pages below ``pages``; the
 reference also writes a 1 at row * pages + id for a padding id >= pages (an
 all -inf tail of the ranking), which lands in the next row or past the buffer,
@@ -20,41 +20,16 @@ from functools import lru_cache
 
 import torch
 
-from .query_fused import module as fused_module
-
-
-_SCRATCH = {}
-_SCRATCH_MAX = 32
-
-
-def _buffers(device, rows, pages, take):
-    key = (device, rows, pages, take)
-    buf = _SCRATCH.get(key)
-    if buf is None:
-        if len(_SCRATCH) >= _SCRATCH_MAX:
-            _SCRATCH.clear()
-        g = max(pages, 64)
-        # all pages active: (n - 1) // 1024 * 16 >= pages
-        n = (g + 15) // 16 * 1024 + 1
-        # take == pages ranks every page (the route's identity branch is for
-        # take >= active only)
-        k = take if take < g else g - 1
-        buf = dict(lens=torch.full((rows,), n, dtype=torch.int32, device=device),
-                   takes=torch.full((rows,), k, dtype=torch.int32, device=device),
-                   sel=torch.empty((rows, take), dtype=torch.int32, device=device),
-                   rt=torch.zeros((rows, g), dtype=torch.int32, device=device),
-                   ft=torch.zeros((rows, take), dtype=torch.int32, device=device),
-                   tail=torch.zeros(rows, dtype=torch.int32, device=device), g=g,
-                   marks=torch.empty((rows, pages + 1), dtype=torch.uint8, device=device))
-        _SCRATCH[key] = buf
-    return buf
+from . import _lib
+from ._lib import ptr
 
 
 def rank_pages(s, pages: int, take: int):
     """The first `take` page ids of each row's ranking (route.py's tie order,
-    any 1 <= take <= pages <= 4096): int32 [rows, take], a scratch buffer that
-    the next call with the same shape overwrites.  s: float32 [rows, >= pages*8]
-    of page centre logits, unit inner stride, row stride a multiple of 4."""
+    any 1 <= take <= pages <= 4096): a new int32 [rows, take] tensor.  s:
+    float32 [rows, >= pages*8] of page centre logits, unit inner stride, row
+    stride a multiple of 4.  Every buffer is allocated per call (from a captured
+    graph's pool when captured), so nothing outlives the caller's references."""
     pages, take = int(pages), int(take)
     if not (0 < take <= pages <= 4096):
         raise ValueError("route: bad pages / take")
@@ -62,18 +37,27 @@ def rank_pages(s, pages: int, take: int):
             and s.stride(1) == 1 and s.stride(0) % 4 == 0):
         raise ValueError("route: bad score layout")
     rows = s.shape[0]
-    buf = _buffers(s.device, rows, pages, take)
+    sel = torch.empty((rows, take), dtype=torch.int32, device=s.device)
     if rows == 0:
-        return buf["sel"]
-    g = buf["g"]
+        return sel
+    g = max(pages, 64)
     if g != pages:   # fewer than 64 pages: the route's smallest geometry, padded with -inf
         pad = torch.full((rows, g * 8), float("-inf"), dtype=torch.float32, device=s.device)
         pad[:, :pages * 8] = s[:, :pages * 8]
         s = pad
+        score_cols = g * 8
     else:            # only the first `pages` pages are ranked, whatever the row holds after them
-        s = s[:, :pages * 8]
-    fused_module().route(s, buf["lens"], buf["takes"], buf["sel"], g, buf["rt"], buf["ft"], buf["tail"], 1, False)
-    return buf["sel"]
+        score_cols = pages * 8
+    # every page active ((n - 1) // 1024 * 16 >= pages for this length), and a
+    # take below the page count (the route's identity branch is for take >= active)
+    lens = torch.full((rows,), (g + 15) // 16 * 1024 + 1, dtype=torch.int32, device=s.device)
+    takes = torch.full((rows,), take if take < g else g - 1, dtype=torch.int32, device=s.device)
+    # without the fine-table fill the route reads neither rt nor tail_rows and
+    # writes no ft: one int stands for each
+    dummy = torch.zeros(1, dtype=torch.int32, device=s.device)
+    _lib.call("v1x_route", ptr(s), s.stride(0), score_cols, ptr(lens), ptr(takes), ptr(sel), 0, take, g,
+              ptr(dummy), ptr(dummy), take, ptr(dummy), 1, 0, rows, _lib.stream_of(s), device=s.device)
+    return sel
 
 
 class _Route:
@@ -93,8 +77,7 @@ class _Route:
             return
         # ranks past the row's pages (padding of the blocked layout, reached
         # only through -inf ties) mark the spare column, not the next row
-        marks = _buffers(s.device, s.shape[0], int(pages), int(take))["marks"]
-        marks.zero_()
+        marks = torch.zeros((s.shape[0], int(pages) + 1), dtype=torch.uint8, device=s.device)
         marks.scatter_(1, torch.where(sel < pages, sel, pages).long(), 1)
         b.copy_(marks[:, :pages])
 
