@@ -65,6 +65,41 @@ def test_shims_reject_cpu_tensors(v1x):
                   torch.zeros((2, 2048), dtype=torch.int32), 0)
 
 
+def test_signed_path_shims_reject_cpu_tensors(v1x):
+    """The signed-score operators check their arguments on the host and refuse
+    CPU tensors (there is no CPU path)."""
+    from importlib import import_module
+    NS = import_module("10_20_b200.native_scoring")
+    T = import_module("10_20_b200.topk2048")
+    G = import_module("10_20_b200.gather")
+    R = import_module("10_20_b200.native_route")
+    S = import_module("10_20_b200.scoring")
+    i32 = lambda *s: torch.zeros(s, dtype=torch.int32)
+    with pytest.raises(ValueError):
+        NS.pack_q(torch.zeros((2, 4, 128), dtype=torch.bfloat16), 0.1)
+    with pytest.raises(ValueError):
+        NS.pack_q(torch.zeros((2, 4, 64), dtype=torch.bfloat16), 0.1)          # head dim 128 only
+    with pytest.raises(ValueError):
+        T.transform(torch.zeros((2, 4096)), i32(2), i32(2, 64), i32(2, 2048), 64)
+    with pytest.raises(ValueError):
+        T.transform(torch.zeros((2, 4096)), i32(2), i32(2, 64), i32(2, 2048), 48)  # page size not 2^k
+    with pytest.raises(ValueError):
+        G.mask_scores(torch.zeros((2, 128)), i32(2, 2), i32(4, 64), i32(2))
+    with pytest.raises(ValueError):
+        R.rank_pages(torch.zeros((2, 800)), 100, 10)
+    with pytest.raises(ValueError):
+        R.extension(64, 4).route(torch.zeros((2, 800)), i32(2, 10), 100, 10)
+    with pytest.raises(ValueError):
+        R.extension(96, 4)
+    q8 = torch.zeros((32, 4, 128), dtype=torch.uint8)
+    with pytest.raises(ValueError):
+        S.paged_logits_grouped(q8, torch.zeros((32, 4)), torch.zeros((2, 8448), dtype=torch.uint8), i32(2), 128,
+                               torch.zeros((32, 128)))
+    with pytest.raises(ValueError):
+        S.mqa_logits_grouped(q8, torch.zeros((32, 4)), (torch.zeros((100, 128), dtype=torch.uint8),
+                             torch.zeros(100)), i32(32), i32(32))
+
+
 def test_triton_style_launcher_requires_grid(v1x):
     from importlib import import_module
     K = import_module("10_20_b200.kernels")
