@@ -5,9 +5,10 @@ Run (CPU only, needs the reference checkout):
     python tests/golden/make_golden.py --reference <path to the reference checkout>
 
 The reference's own Triton kernels (DS/kernels.py, NA/kernels.py,
-NA/fused_grouping.py) are loaded by file path, exactly as the reference's
-tests load them, and executed on CPU tensors by the Triton interpreter
-(TRITON_INTERPRET=1).  The fused CUDA route/topk cannot run here, so their
+NA/fused_grouping.py, the shared-tail experiments, qwen_gqa_probe_kernels.py)
+are loaded by file path, exactly as the reference's tests load them, and
+executed on CPU tensors by the Triton interpreter (TRITON_INTERPRET=1); torch
+helpers (NA/grouping.py quantize) run on CPU.  The fused CUDA route/topk cannot run here, so their
 fixture is the torch reference math of DS/example_v1_query_single_head.py
 evaluated on CPU.  Inputs are seeded; outputs are written as .npz next to this
 script.  The test suite never runs this script; it only reads the .npz files.
