@@ -159,3 +159,17 @@ def test_mask_scores_page_outside_mapping_is_masked():
     mapping = np.zeros((2, 64), np.int32)
     got = O.mask_scores(s, np.array([[5, -1]], np.int32), mapping, [10])
     assert np.isinf(got).all()
+
+
+def test_route_extension_layout_equals_fused_route_for_every_accepted_shape():
+    """NA/deps/route.py:71-76 picks n = the smallest of 128..4096 (and >= THREADS)
+    holding the pages, BASE = n / 128; fused.route (VQ:175-177) picks THREADS x
+    ITEMS by the page count alone.  For every (threads, pages) the extension
+    accepts (pages > threads / 2) the two blocked layouts are the same, which
+    is what lets the extension run on fused.route's ranking."""
+    for threads in (64, 128, 256, 512):
+        sizes = [n for n in (128, 256, 512, 1024, 2048, 4096) if n >= threads]
+        for pages in range(threads // 2 + 1, 4097):
+            n_ext = next(n for n in sizes if pages <= n)
+            t, it = O.route_geometry(max(pages, 64))
+            assert n_ext == t * it, (threads, pages)
