@@ -173,3 +173,27 @@ def test_route_extension_layout_equals_fused_route_for_every_accepted_shape():
             n_ext = next(n for n in sizes if pages <= n)
             t, it = O.route_geometry(max(pages, 64))
             assert n_ext == t * it, (threads, pages)
+
+
+def test_mqa_logits_equals_paged_scoring_of_the_same_keys():
+    """The flat-key logits of the dsa mode equal the paged scorer's over the
+    same keys packed into pages (identity table), inside each row's window."""
+    rng = np.random.default_rng(8)
+    N, rows = 200, 3
+    k8 = O.e4m3_from_f32(rng.standard_normal((N, 128)).astype(np.float32))
+    ks = rng.uniform(0.1, 1, N).astype(np.float32)
+    q8 = O.e4m3_from_f32(rng.standard_normal((rows, 4, 128)).astype(np.float32))
+    w = rng.standard_normal((rows, 4)).astype(np.float32)
+    P = (N + 63) // 64
+    pool = np.zeros((P, 8448), np.uint8)
+    kk = np.zeros((P * 64, 128), np.uint8)
+    kk[:N] = k8
+    sc = np.zeros(P * 64, np.float32)
+    sc[:N] = ks
+    pool[:, :8192] = kk.reshape(P, 8192)
+    pool[:, 8192:] = sc.view(np.uint8).reshape(P, 256)
+    paged = O.score_paged(q8, w, pool, np.arange(P)[None].repeat(rows, 0), [N] * rows, N, relu=False)
+    flat = O.mqa_logits(q8, w, k8, ks, [0, 50, 0], [N, 120, 1], relu=False)
+    assert np.array_equal(flat[0], paged[0])
+    assert np.array_equal(flat[1, 50:120], paged[1, 50:120]) and np.isinf(flat[1, :50]).all()
+    assert flat[2, 0] == paged[2, 0] and np.isinf(flat[2, 1:]).all()
